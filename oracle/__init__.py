@@ -1,0 +1,276 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes bindings for the CPU oracle (liboracle.so).
+
+The oracle restates the reference engine's Rust CPU kernels (see
+wohper_oracle.h).  Only tests/, ``__graft_entry__.smoke()`` and bench.py's
+cpu_baseline / ``--impl reference`` arm import this module, as the checker or
+the timed CPU baseline.  The product package ``wohper_b200`` never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+OK = 0
+ERR_EMPTY_SHAPE = 1
+ERR_INVALID_SHAPE = 2
+ERR_PACKED_WEIGHT_TOO_SMALL = 3
+ERR_SCALE_TOO_SMALL = 4
+ERR_INPUT_TOO_SMALL = 5
+ERR_OUTPUT_TOO_SMALL = 6
+ERR_SCRATCH_TOO_SMALL = 7
+ERR_NON_FINITE_OUTPUT = 8
+
+
+class Fp4Spec(C.Structure):
+    _fields_ = [
+        ("packed_weight", C.c_void_p),
+        ("packed_len", C.c_size_t),
+        ("ue8m0_scales", C.c_void_p),
+        ("scales_len", C.c_size_t),
+        ("rows", C.c_size_t),
+        ("cols", C.c_size_t),
+        ("scale_cols", C.c_size_t),
+    ]
+
+
+class Fp4Expert(C.Structure):
+    _fields_ = [("w1", Fp4Spec), ("w3", Fp4Spec), ("w2", Fp4Spec)]
+
+
+class Fp8Matrix(C.Structure):
+    _fields_ = [
+        ("weight", C.c_void_p),
+        ("scale", C.c_void_p),
+        ("rows", C.c_size_t),
+        ("cols", C.c_size_t),
+        ("scale_rows", C.c_size_t),
+        ("scale_cols", C.c_size_t),
+    ]
+
+
+class Fp8Expert(C.Structure):
+    _fields_ = [("w1", Fp8Matrix), ("w3", Fp8Matrix), ("w2", Fp8Matrix)]
+
+
+def build() -> Path:
+    """Compile liboracle.so with oracle/Makefile (g++, no GPU needed)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        sz, vp, f, i = C.c_size_t, C.c_void_p, C.c_float, C.c_int
+        L.orc_set_threads.argtypes = [i]
+        L.orc_get_threads.restype = i
+        L.orc_decode_fp8_e4m3.argtypes = [C.c_uint8, f]
+        L.orc_decode_fp8_e4m3.restype = f
+        L.orc_decode_ue8m0_scale.argtypes = [C.c_uint8]
+        L.orc_decode_ue8m0_scale.restype = f
+        L.orc_decode_fp4_e2m1.argtypes = [C.c_uint8, f]
+        L.orc_decode_fp4_e2m1.restype = f
+        for n in ("orc_fp8_e4m3_base_lut", "orc_ue8m0_scale_lut", "orc_fp4_e2m1_base_lut",
+                  "orc_fp8_e4m3_sorted_lut"):
+            getattr(L, n).argtypes = [vp]
+        L.orc_fp8_dot_row.argtypes = [vp, vp, sz, sz, vp, i]
+        L.orc_fp8_dot_row.restype = f
+        L.orc_fp8_gemv_rows.argtypes = [vp, sz, sz, sz, vp, sz, sz, sz, sz, sz, vp, sz, vp, sz]
+        L.orc_fp8_gemv_rows.restype = i
+        L.orc_fp8_gemv_rows_multi.argtypes = [vp, sz, sz, sz, vp, sz, sz, sz, sz, sz, vp, sz, sz,
+                                              vp, sz]
+        L.orc_fp8_gemv_rows_multi.restype = i
+        L.orc_fp8_act_quant_dequant_in_place.argtypes = [vp, sz, sz]
+        L.orc_bf16_dot_row.argtypes = [vp, vp, sz, i]
+        L.orc_bf16_dot_row.restype = f
+        L.orc_bf16_gemv.argtypes = [vp, sz, sz, vp, vp]
+        L.orc_bf16_gemv.restype = i
+        L.orc_fp4_matvec.argtypes = [C.POINTER(Fp4Spec), vp, sz, vp, sz, i]
+        L.orc_fp4_matvec.restype = i
+        L.orc_fp4_expert_forward.argtypes = [C.POINTER(Fp4Expert), vp, sz, vp, sz, vp, sz]
+        L.orc_fp4_expert_forward.restype = i
+        L.orc_fp4_expert_scratch_len.argtypes = [sz]
+        L.orc_fp4_expert_scratch_len.restype = sz
+        L.orc_fp8_expert_forward.argtypes = [C.POINTER(Fp8Expert), vp, sz, vp]
+        L.orc_fp8_expert_forward.restype = i
+        L.orc_router.argtypes = [vp, sz, sz, vp, sz, i, vp, f, vp, vp, vp, vp]
+        L.orc_router.restype = i
+        L.orc_deepseek_sqrtsoftplus_route.argtypes = [vp, sz, vp, sz, f, vp, vp]
+        L.orc_deepseek_sqrtsoftplus_route.restype = sz
+        L.orc_moe_combine_token.argtypes = [C.POINTER(Fp4Expert), vp, vp, sz,
+                                            C.POINTER(Fp4Expert), C.POINTER(Fp8Expert), vp, sz,
+                                            vp]
+        L.orc_moe_combine_token.restype = i
+        L.orc_moe_batched.argtypes = [C.POINTER(Fp4Expert), sz, vp, vp, sz, sz,
+                                      C.POINTER(Fp4Expert), vp, sz, vp]
+        L.orc_moe_batched.restype = i
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def threads() -> int:
+    return lib().orc_get_threads()
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=dtype))
+
+
+def fp4_spec(packed, scales, rows, cols, scale_cols, keep: list) -> Fp4Spec:
+    packed = _c(packed, np.uint8)
+    scales = _c(scales, np.uint8)
+    keep += [packed, scales]
+    return Fp4Spec(packed.ctypes.data, packed.size, scales.ctypes.data, scales.size, rows, cols,
+                   scale_cols)
+
+
+def fp4_expert(w1: dict, w3: dict, w2: dict, keep: list) -> Fp4Expert:
+    mk = lambda d: fp4_spec(d["packed"], d["scales"], d["rows"], d["cols"], d["scale_cols"], keep)
+    return Fp4Expert(mk(w1), mk(w3), mk(w2))
+
+
+def fp8_matrix(weight, scale, rows, cols, scale_rows, scale_cols, keep: list) -> Fp8Matrix:
+    weight = _c(weight, np.uint8)
+    scale = _c(scale, np.uint8)
+    keep += [weight, scale]
+    return Fp8Matrix(weight.ctypes.data, scale.ctypes.data, rows, cols, scale_rows, scale_cols)
+
+
+def luts() -> dict:
+    L = lib()
+    out = {}
+    for key, n, fn in (("fp8", 256, L.orc_fp8_e4m3_base_lut), ("ue8m0", 256, L.orc_ue8m0_scale_lut),
+                       ("fp4", 16, L.orc_fp4_e2m1_base_lut),
+                       ("sorted", 256, L.orc_fp8_e4m3_sorted_lut)):
+        a = np.zeros(n, np.float32)
+        fn(_p(a))
+        out[key] = a
+    return out
+
+
+def act_quant(x, block: int = 64) -> np.ndarray:
+    v = _c(x, np.float32).copy()
+    lib().orc_fp8_act_quant_dequant_in_place(_p(v), v.size, block)
+    return v
+
+
+def fp8_dot_row(w, s, col_group, x, avx2=True) -> float:
+    w, s, x = _c(w, np.uint8), _c(s, np.uint8), _c(x, np.float32)
+    return lib().orc_fp8_dot_row(_p(w), _p(s), s.size, col_group, _p(x), int(avx2))
+
+
+def fp8_gemv(weight, scale, x, rows, cols, scale_rows, scale_cols, row_start=0, row_end=None):
+    row_end = rows if row_end is None else row_end
+    w, s, x = _c(weight, np.uint8), _c(scale, np.uint8), _c(x, np.float32)
+    y = np.zeros(row_end - row_start, np.float32)
+    st = lib().orc_fp8_gemv_rows(_p(w), w.size, rows, cols, _p(s), s.size, scale_rows,
+                                 scale_cols, row_start, row_end, _p(x), x.size, _p(y), y.size)
+    return st, y
+
+
+def fp8_gemv_multi(weight, scale, xs, rows, cols, scale_rows, scale_cols, row_start=0,
+                   row_end=None):
+    row_end = rows if row_end is None else row_end
+    w, s, xs = _c(weight, np.uint8), _c(scale, np.uint8), _c(xs, np.float32)
+    count = xs.shape[0]
+    n = row_end - row_start
+    y = np.zeros((count, n), np.float32)
+    st = lib().orc_fp8_gemv_rows_multi(_p(w), w.size, rows, cols, _p(s), s.size, scale_rows,
+                                       scale_cols, row_start, row_end, _p(xs), count,
+                                       xs.shape[1], _p(y), n)
+    return st, y
+
+
+def bf16_dot_row(row_u16, x, avx2=True) -> float:
+    r, x = _c(row_u16, np.uint16), _c(x, np.float32)
+    return lib().orc_bf16_dot_row(_p(r), _p(x), x.size, int(avx2))
+
+
+def bf16_gemv(w_u16, x):
+    w, x = _c(w_u16, np.uint16), _c(x, np.float32)
+    y = np.zeros(w.shape[0], np.float32)
+    st = lib().orc_bf16_gemv(_p(w), w.shape[0], w.shape[1], _p(x), _p(y))
+    return st, y
+
+
+def fp4_matvec(packed, scales, rows, cols, scale_cols, x, path=0, out_len=None):
+    keep: list = []
+    spec = fp4_spec(packed, scales, rows, cols, scale_cols, keep)
+    x = _c(x, np.float32)
+    y = np.zeros(rows if out_len is None else out_len, np.float32)
+    st = lib().orc_fp4_matvec(C.byref(spec), _p(x), x.size, _p(y), y.size, path)
+    return st, y
+
+
+def fp4_expert_forward(expert: Fp4Expert, x, out_len=None, scratch_len=None):
+    x = _c(x, np.float32)
+    y = np.zeros(expert.w2.rows if out_len is None else out_len, np.float32)
+    sl = 2 * expert.w1.rows if scratch_len is None else scratch_len
+    scratch = np.zeros(max(sl, 1), np.float32)
+    st = lib().orc_fp4_expert_forward(C.byref(expert), _p(x), x.size, _p(y), y.size, _p(scratch),
+                                      sl)
+    return st, y
+
+
+def router(gate_u16, x, topk, mode=0, bias=None, route_scale=1.0, hash_ids=None):
+    g, x = _c(gate_u16, np.uint16), _c(x, np.float32)
+    E, H = g.shape
+    b = None if bias is None else _c(bias, np.float32)
+    h = None if hash_ids is None else _c(hash_ids, np.int32)
+    ids = np.full(topk, -1, np.int32)
+    w = np.zeros(topk, np.float32)
+    logits = np.zeros(E, np.float32)
+    n = lib().orc_router(_p(g), E, H, _p(x), topk, mode, _p(b), route_scale, _p(h), _p(ids),
+                         _p(w), _p(logits))
+    return n, ids, w, logits
+
+
+def deepseek_sqrtsoftplus_route(logits, topk, route_scale, bias=None):
+    l = _c(logits, np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    ids = np.zeros(topk, np.int32)
+    w = np.zeros(topk, np.float32)
+    n = lib().orc_deepseek_sqrtsoftplus_route(_p(l), l.size, _p(b), topk, route_scale, _p(ids),
+                                              _p(w))
+    return ids[:n], w[:n]
+
+
+def moe_combine_token(experts_arr, ids, weights, shared_fp4, x, shared_fp8=None):
+    ids, weights, x = _c(ids, np.int32), _c(weights, np.float32), _c(x, np.float32)
+    y = np.zeros(x.size, np.float32)
+    sh4 = C.byref(shared_fp4) if shared_fp4 is not None else None
+    sh8 = C.byref(shared_fp8) if shared_fp8 is not None else None
+    st = lib().orc_moe_combine_token(experts_arr, _p(ids), _p(weights), ids.size, sh4, sh8,
+                                     _p(x), x.size, _p(y))
+    return st, y
+
+
+def moe_batched(experts_arr, num_experts, ids, weights, shared_fp4, x):
+    ids, weights, x = _c(ids, np.int32), _c(weights, np.float32), _c(x, np.float32)
+    T, K = ids.shape
+    y = np.zeros_like(x)
+    sh4 = C.byref(shared_fp4) if shared_fp4 is not None else None
+    st = lib().orc_moe_batched(experts_arr, num_experts, _p(ids), _p(weights), T, K, sh4, _p(x),
+                               x.shape[1], _p(y))
+    return st, y
