@@ -1,0 +1,395 @@
+#!/usr/bin/env python3
+"""bench.py -- decode tokens/s of the one-token FP4 MoE FFN.
+
+One step = one token through the MoE FFN layer of DeepSeek-V4-Flash shape:
+router (256 x 4096 bf16 gate, top-6 by raw logit, softmax over the selected),
+6 routed + 1 shared FP4 E2M1 expert (4096 -> 2048 -> 4096, UE8M0 per 32),
+SwiGLU with the reference clamps, act quant before every matvec, combine with
+w_i/sum(w) in route order.  Weights are seeded synthetic (random init, no
+checkpoint), HBM-resident; every step uses a fresh token, and L2 is flushed
+(256 MiB memset) between steps outside the timed events, so each step reads
+its experts from HBM.
+
+N > 1 (torchrun): the path has no exchange at batch 1, so every rank runs a
+full replica on its own token stream (weak scaling, no collective on the data
+path); the timed region is the max over ranks.
+
+--impl reference: the reference's CPU implementation of the same step (the
+C++ restatement of its Rust AVX2 kernels, oracle/), on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+E, HID, INTER, TOPK = 256, 4096, 2048, 6
+PACKED_W13 = INTER * HID // 2            # bytes of w1 (= w3) packed
+SCALES_W13 = INTER * HID // 32
+PACKED_W2 = HID * INTER // 2
+SCALES_W2 = HID * INTER // 32
+EXPERT_BYTES = 2 * (PACKED_W13 + SCALES_W13) + PACKED_W2 + SCALES_W2   # 13,369,344
+ROUTER_BYTES = E * HID * 2
+SLOTS = TOPK + 1
+STEP_BYTES = SLOTS * EXPERT_BYTES + ROUTER_BYTES + 2 * HID * 4
+UP_BYTES = SLOTS * 2 * (PACKED_W13 + SCALES_W13)       # moe_up algorithmic bytes / launch
+DOWN_BYTES = SLOTS * (PACKED_W2 + SCALES_W2)
+METRIC = "decode tokens/s (one-token FP4 MoE FFN, config 2)"
+WORKLOAD = ("config 2: one-token FP4 MoE FFN, 256 experts 4096->2048->4096 E2M1/UE8M0-32, "
+            "bf16 router top-6 softmax-renormalised, 6 routed + 1 shared expert")
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def all_max(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU side (oracle = the reference's CPU kernels restated): cpu_baseline and
+# the --impl reference arm.  Experts are generated per id on first use.
+# ---------------------------------------------------------------------------
+class HostModel:
+    def __init__(self, seed: int):
+        from tests import helpers as H
+
+        self.H = H
+        self.seed = seed
+        self.gate = H.router_gate(seed + 7, E, HID)
+        self.cache: dict = {}
+
+    def expert(self, e: int):
+        import oracle as O
+
+        if e not in self.cache:
+            keep: list = []
+            w1, s1 = self.H.fp4_matrix(self.seed * 1000 + 3 * e, INTER, HID)
+            w3, s3 = self.H.fp4_matrix(self.seed * 1000 + 3 * e + 1, INTER, HID)
+            w2, s2 = self.H.fp4_matrix(self.seed * 1000 + 3 * e + 2, HID, INTER)
+            spec = O.Fp4Expert(O.fp4_spec(w1, s1, INTER, HID, HID // 32, keep),
+                               O.fp4_spec(w3, s3, INTER, HID, HID // 32, keep),
+                               O.fp4_spec(w2, s2, HID, INTER, INTER // 32, keep))
+            self.cache[e] = (spec, keep)
+        return self.cache[e][0]
+
+    def step(self, x):
+        import oracle as O
+
+        n, ids, w, _ = O.router(self.gate, x, TOPK, mode=0)
+        arr = (O.Fp4Expert * (E + 1))()
+        for e in list(ids) + [E]:
+            arr[e] = self.expert(int(e))
+        st, y = O.moe_combine_token(arr, ids, w, arr[E], x)
+        assert st == O.OK
+        return y
+
+
+def cpu_run(steps: int, warmup: int, seed: int = 900, budget_s: float | None = None):
+    import oracle as O
+
+    model = HostModel(seed)
+    xs = model.H.activations(seed + 1, steps + warmup, HID)
+    for i in range(warmup):
+        model.step(xs[i])
+    t0 = time.perf_counter()
+    done = 0
+    for i in range(steps):
+        model.step(xs[warmup + i])
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, O.threads()
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    import wohper_b200 as W
+    from tests import helpers as H
+
+    dev = torch.device("cuda", local)
+    ctx = W.Context(local)
+    stack = H.torch_fp4_experts(1000 + rank, E + 1, HID, INTER, device=dev)
+    gate = torch.from_numpy(H.router_gate(1007, E, HID).view(np.int16)).to(dev)
+
+    def wexp(e):
+        w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+        return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+    layer = W.MoeLayer(ctx, [wexp(e) for e in range(E)], wexp(E), gate, topk=TOPK,
+                       router_mode=W.ROUTER_RAW_LOGITS, max_tokens=1)
+    n_tok = args.warmup + args.steps
+    xs = torch.from_numpy(H.activations(2000 + rank, n_tok, HID)).to(dev)
+    y = torch.empty(1, HID, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+
+    # ---- device-resident timing -------------------------------------------
+    for i in range(args.warmup):
+        flush.zero_()
+        layer.forward(xs[i:i + 1], y)
+    ctx.sync()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            flush.zero_()
+            ev[k][0].record(stream)
+            layer.forward(xs[args.warmup + k:args.warmup + k + 1], y)
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ctx.sync()
+    ms_local = sum(a.elapsed_time(b) for a, b in ev)
+    ms_total = all_max(world, ms_local)
+    ms_step = ms_total / args.steps
+    clocks = clk.summary()
+
+    # ---- per-kernel roofline (profiling: events between kernels, no PDL) ----
+    ctx.set_profiling(True)
+    phases = []
+    for k in range(min(args.steps, 10)):
+        flush.zero_()
+        layer.forward(xs[args.warmup + k:args.warmup + k + 1], y)
+        phases.append(ctx.phase_times())
+    ctx.set_profiling(False)
+    ctx.sync()
+    ph = np.array(phases)  # [router, moe_up, moe_down]
+    up_ms = float(ph[:, 1].mean())
+    down_ms = float(ph[:, 2].mean())
+    router_ms = float(ph[:, 0].mean())
+    peak, peak_kind = peaks()
+    up_gbs = UP_BYTES / (up_ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with host buffers ---------------------
+    xh = torch.from_numpy(H.activations(3000 + rank, n_tok, HID)).pin_memory()
+    yh = torch.empty(args.steps, HID).pin_memory()
+    xd = torch.empty(1, HID, device=dev)
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.warmup):
+        flush.zero_()
+        xd.copy_(xh[i:i + 1], non_blocking=True)
+        layer.forward(xd, y)
+        yh[0:1].copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    for k in range(args.steps):
+        flush.zero_()
+        ev2[k][0].record(stream)
+        xd.copy_(xh[args.warmup + k:args.warmup + k + 1], non_blocking=True)
+        layer.forward(xd, y)
+        yh[k:k + 1].copy_(y, non_blocking=True)
+        ev2[k][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    ctx.sync()
+
+    result = None
+    if rank == 0:
+        value = world / (ms_step * 1e-3)
+        result = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 6),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp4-e2m1 x fp8-e4m3 (act-quant) products, f32 accumulate",
+            "data": "synthetic (seeded random-init weights and N(0,1) tokens)",
+            "config": {
+                "workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID, "inter": INTER,
+                "batch": 1, "shared_expert": "fp4",
+                "l2": "flushed between steps (256 MiB memset outside the timed events)",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "bytes_per_step": STEP_BYTES,
+            },
+            "step_hbm_gbs": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
+            "phases_ms": {"router": round(router_ms, 5), "moe_up": round(up_ms, 5),
+                          "moe_down": round(down_ms, 5)},
+            "roofline": {
+                "kernel": "moe_up_kernel (w1+w3 FP4 matvecs of 7 experts + SwiGLU + act quant)",
+                "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
+                "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
+                "algorithmic_bytes": UP_BYTES, "traffic": None,
+                "down_kernel_gbs": round(DOWN_BYTES / (down_ms * 1e-3) / 1e9, 1),
+            },
+            "e2e": {"value": round(world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 6), "h2d_bytes_per_step": HID * 4,
+                    "d2h_bytes_per_step": HID * 4,
+                    "path": "pinned host x -> H2D -> wh_moe_ffn (C ABI) -> D2H y"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks,
+        }
+    layer.close()
+    ctx.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, n, cores = cpu_run(steps=40, warmup=1, budget_s=20.0)
+        result["cpu_baseline"] = {
+            "value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} tokens of the same workload (router + 6 routed + shared expert), "
+                      "C++ restatement of the reference's AVX2 kernels, reference threading "
+                      "(nproc-2 threads)"}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return result
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import oracle as O
+
+    O.set_threads(os.cpu_count() or 1)
+    v, n, cores = cpu_run(steps=args.steps, warmup=args.warmup)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup,
+        "ms_per_step": round(1e3 / v, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp4-e2m1 x fp8-e4m3 (act-quant) products, f32 accumulate",
+        "data": "synthetic (seeded random-init weights and N(0,1) tokens)",
+        "config": {"workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID,
+                   "inter": INTER, "batch": 1, "shared_expert": "fp4"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} tokens, one per step"},
+        "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,215 @@
+/*
+ * wohper_b200.h -- C ABI of the B200 (sm_100a) dequant-matmul hot path of
+ * Wohper (engine/zc_infer_core).  Every entry point here replaces one Rust
+ * function of the reference's kernel layer; the comment above each cites the
+ * reference interface it stands in for (path:line inside the reference
+ * project).  A Rust FFI crate binds these symbols one to one.
+ *
+ * Conventions
+ *  - All data pointers are DEVICE pointers owned by the caller (weights are
+ *    uploaded once and stay resident in HBM); sizes are element counts unless
+ *    a name says bytes.  Host-side descriptor structs (wh_fp4_matvec_spec,
+ *    wh_fp4_expert, wh_moe_desc) hold device pointers.
+ *  - Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream).  Argument errors are detected on the host before anything is
+ *    launched and returned immediately.  Errors that only the device can see
+ *    (a non-finite output, a timed-out wait) are recorded in the context and
+ *    returned by wh_ctx_sync(), which mirrors the reference's synchronous
+ *    Result<(), Error>: call it after a call to get the reference's behaviour.
+ *  - Status codes 1..8 are DeepSeekV4KernelError
+ *    (engine/zc_infer_core/src/deepseek_v4.rs:398-408) in declaration order.
+ *  - One wh_ctx per device and per calling thread at a time; calls on one ctx
+ *    are not re-entrant (the reference serves one request at a time behind a
+ *    mutex, src/server/api.rs:301).
+ */
+#ifndef WOHPER_B200_H
+#define WOHPER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* wh_stream_t; /* == cudaStream_t */
+
+typedef enum wh_status {
+  WH_OK = 0,
+  WH_ERR_EMPTY_SHAPE = 1,
+  WH_ERR_INVALID_SHAPE = 2,
+  WH_ERR_PACKED_WEIGHT_TOO_SMALL = 3,
+  WH_ERR_SCALE_TOO_SMALL = 4,
+  WH_ERR_INPUT_TOO_SMALL = 5,
+  WH_ERR_OUTPUT_TOO_SMALL = 6,
+  WH_ERR_SCRATCH_TOO_SMALL = 7,
+  WH_ERR_NON_FINITE_OUTPUT = 8,
+  WH_ERR_INVALID_POINTER = 9, /* ComputeError::InvalidPointer (src/compute.rs:337) */
+  WH_ERR_UNSUPPORTED = 10,    /* ComputeError::UnsupportedQuantFormat / InvalidQuantBlock */
+  WH_ERR_CUDA = 20,           /* a CUDA runtime call failed (detail: wh_last_error_detail) */
+  WH_ERR_NCCL = 21,           /* a collective failed (expert parallelism) */
+  WH_ERR_TIMEOUT = 22,        /* a bounded device-side wait expired */
+  WH_ERR_DEVICE_ARG = 23      /* a device-side index check failed (e.g. expert id) */
+} wh_status;
+
+/* ------------------------------------------------------------------------ */
+/* Context                                                                   */
+/* ------------------------------------------------------------------------ */
+typedef struct wh_ctx wh_ctx;
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int wh_version(void);
+
+/* Creates a context on `device` (cudaSetDevice is called).  Allocates the
+ * device status word and uploads the act-quant rounding table, which is
+ * measured from the host's libm log2f so ceil(log2f(.)) matches the
+ * reference bit for bit (src/compute.rs:2516). */
+wh_status wh_ctx_create(int device, wh_ctx** out);
+void wh_ctx_destroy(wh_ctx* ctx);
+
+/* Synchronises `stream` and returns the first device-side error recorded since
+ * the previous wh_ctx_sync (WH_ERR_NON_FINITE_OUTPUT, WH_ERR_TIMEOUT,
+ * WH_ERR_DEVICE_ARG), then clears it. */
+wh_status wh_ctx_sync(wh_ctx* ctx, wh_stream_t stream);
+
+/* Human-readable detail of the last error returned on this thread. */
+const char* wh_last_error_detail(void);
+
+/* Per-phase timing, the counterpart of the reference's ZC_PROF pass timers
+ * (src/server/generation.rs:2344-2351).  While profiling is on, multi-kernel
+ * entry points (wh_moe_ffn, wh_fp4_expert_forward) record a CUDA event before
+ * and after each kernel and launch without programmatic dependent launch;
+ * wh_ctx_phase_times synchronises and writes the last call's per-kernel
+ * milliseconds (in launch order) to ms[0..n), returning the phase count. */
+wh_status wh_ctx_set_profiling(wh_ctx* ctx, int on);
+int wh_ctx_phase_times(wh_ctx* ctx, float* ms, int max_phases);
+
+/* ------------------------------------------------------------------------ */
+/* FP8 E4M3 x UE8M0 block-scaled GEMV                                        */
+/* ------------------------------------------------------------------------ */
+/* Replaces gemv_fp8_e4m3_ue8m0_tensorwise (src/compute.rs:6174-6239),
+ * gemv_fp8_e4m3_ue8m0_rows (src/compute.rs:6244-6321) and
+ * gemv_fp8_e4m3_ue8m0_rows_multi (src/compute.rs:6384-6577).
+ *   weight [rows][cols] E4M3 bytes; scale [scale_rows][scale_cols] UE8M0
+ *   bytes (rows % scale_rows == 0, cols % scale_cols == 0); computes output
+ *   rows [row_start, row_end) for `batch` inputs x[b*ldx + c] into
+ *   y[b*ldy + (r - row_start)].  Every output equals the reference's AVX2 row
+ *   kernel bit for bit, for any batch.  act_quant_block > 0 first applies the
+ *   reference's FP8 activation quant-dequant (block size act_quant_block) to
+ *   a copy of each input, as its call sites do before every FP8 GEMV
+ *   (src/compute.rs:4001). */
+wh_status wh_fp8_gemv(wh_ctx* ctx, const uint8_t* weight, const uint8_t* scale, int rows, int cols,
+                      int scale_rows, int scale_cols, int row_start, int row_end, const float* x,
+                      int batch, int ldx, float* y, int ldy, int act_quant_block,
+                      wh_stream_t stream);
+
+/* Replaces fp8_act_quant_dequant_in_place (src/compute.rs:2504-2545): per
+ * block, power-of-two scale from the block amax, nearest E4M3 value with ties
+ * to the lower entry, in place. */
+wh_status wh_act_quant_fp8(wh_ctx* ctx, float* values, size_t n, int block_size,
+                           wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* FP4 E2M1 x UE8M0(per 32) matvec and expert forward                         */
+/* ------------------------------------------------------------------------ */
+/* Mirrors Fp4Matvec (src/deepseek_v4.rs:410-417); lengths are in bytes. */
+typedef struct wh_fp4_matvec_spec {
+  const uint8_t* packed_weight; /* [rows][(cols+1)/2], low nibble = even column */
+  size_t packed_len;
+  const uint8_t* ue8m0_scales; /* [rows][scale_cols] */
+  size_t scales_len;
+  size_t rows, cols, scale_cols;
+} wh_fp4_matvec_spec;
+
+/* Mirrors DeepSeekV4Fp4Expert (src/deepseek_v4.rs:419-428). */
+typedef struct wh_fp4_expert {
+  wh_fp4_matvec_spec w1, w3, w2;
+} wh_fp4_expert;
+
+/* Replaces fp4_e2m1_ue8m0_matvec_scalar (src/deepseek_v4.rs:464-549);
+ * same validation order and errors as validate_fp4_matvec
+ * (src/deepseek_v4.rs:434-462). */
+wh_status wh_fp4_matvec(wh_ctx* ctx, const wh_fp4_matvec_spec* spec, const float* input,
+                        size_t input_len, float* output, size_t output_len, wh_stream_t stream);
+
+/* Replaces deepseek_v4_fp4_expert_scratch_len (src/deepseek_v4.rs:430-432). */
+size_t wh_fp4_expert_scratch_len(size_t intermediate);
+
+/* Replaces deepseek_v4_fp4_expert_forward_scalar (src/deepseek_v4.rs:561-601):
+ * act quant(x) -> w1, w3 -> SwiGLU with the reference clamps -> act quant ->
+ * w2.  `scratch` is a device buffer of scratch_len floats, at least
+ * wh_fp4_expert_scratch_len(w1.rows). */
+wh_status wh_fp4_expert_forward(wh_ctx* ctx, const wh_fp4_expert* expert, const float* input,
+                                size_t input_len, float* output, size_t output_len,
+                                float* scratch, size_t scratch_len, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Router                                                                    */
+/* ------------------------------------------------------------------------ */
+#define WH_ROUTER_RAW_LOGITS 0     /* RouterMath::RawLogits + legacy softmax */
+#define WH_ROUTER_SQRT_SOFTPLUS 1  /* RouterMath::DeepSeekV4SqrtSoftplus */
+
+/* Replaces route_experts_from_dense_block (src/compute.rs:2129-2236) with
+ * finalize_route_weights (src/compute.rs:2253-2268) and, in raw-logit mode,
+ * normalize_route_weights_legacy (src/server/generation.rs:3152-3180).
+ *   gate [experts][hidden] bf16 (uint16 bits); x [tokens][hidden];
+ *   ids/weights [tokens][topk]; hash_ids (nullable, [tokens][topk]) is the
+ *   tid2eid row of each token for hash layers (sqrt-softplus mode).  Expert
+ *   ids are bit-exact with the reference.  logits (nullable,
+ *   [tokens][experts]) receives the raw gate logits.  experts <= 1024,
+ *   topk <= 32. */
+wh_status wh_router_topk(wh_ctx* ctx, const uint16_t* gate, int experts, int hidden,
+                         const float* x, int tokens, int topk, int mode, const float* bias,
+                         float route_scale, const int32_t* hash_ids, int32_t* ids,
+                         float* weights, float* logits, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* MoE FFN layer (router + routed FP4 experts + shared expert + combine)      */
+/* ------------------------------------------------------------------------ */
+typedef struct wh_moe_desc {
+  int num_experts;              /* routed experts (256 in DeepSeek-V4-Flash) */
+  int hidden;                   /* 4096 */
+  int inter;                    /* 2048 */
+  const wh_fp4_expert* experts; /* host array [num_experts] of device-pointer specs */
+  const wh_fp4_expert* shared;  /* nullable: always-on shared expert */
+  const uint16_t* gate;         /* [num_experts][hidden] bf16 router weight */
+  const float* gate_bias;       /* nullable selection bias (sqrt-softplus mode) */
+  int topk;                     /* 6 */
+  int router_mode;              /* WH_ROUTER_* */
+  float route_scale;            /* 1.5 in DeepSeek-V4-Flash */
+  int max_tokens;               /* largest `tokens` wh_moe_ffn will be given */
+} wh_moe_desc;
+
+typedef struct wh_moe_plan wh_moe_plan;
+
+/* Validates every expert (as validate_fp4_matvec) and builds the device-side
+ * descriptors (TMA tensor maps) once; allocates them on the device. */
+wh_status wh_moe_plan_create(wh_ctx* ctx, const wh_moe_desc* desc, wh_moe_plan** out);
+void wh_moe_plan_destroy(wh_moe_plan* plan);
+
+/* Device scratch bytes wh_moe_ffn needs for `tokens` tokens. */
+size_t wh_moe_scratch_bytes(const wh_moe_plan* plan, int tokens);
+
+/* One MoE FFN step for `tokens` tokens (x, y: [tokens][hidden] f32).
+ * Replaces, per token, routing (see wh_router_topk) followed by
+ * compute_active_and_shared_experts (src/compute.rs:1872-1946):
+ * y = shared(x) + sum_k expert_k(x) * w_k/sum(w), summed in route order.
+ * ids_out/weights_out (nullable, [tokens][topk]) receive the routes. */
+wh_status wh_moe_ffn(wh_ctx* ctx, const wh_moe_plan* plan, const float* x, int tokens,
+                     const int32_t* hash_ids, float* y, int32_t* ids_out, float* weights_out,
+                     void* scratch, size_t scratch_bytes, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Test hooks (host-only, no device work): expose the host-side pieces the   */
+/* kernels rely on so CPU tests can pin them.                                */
+/* ------------------------------------------------------------------------ */
+/* The act-quant ceil(log2f) threshold table: out[E] for biased exponent E. */
+void wh_debug_act_quant_table(uint32_t out[256]);
+/* The E4M3 nearest-with-ties-to-lower rounding the kernels use (|t| <= 448). */
+float wh_debug_e4m3_round(float t);
+void wh_debug_e4m3_round_n(const float* in, float* out, size_t n); /* host arrays */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WOHPER_B200_H */

@@ -1,0 +1,357 @@
+"""wohper_b200 -- B200 (sm_100a) dequant-matmul hot path of Wohper.
+
+This package is the Python host side of the C ABI declared in
+``include/wohper_b200.h`` (library ``wohper_b200/libwohper_b200.so``).  Its
+functions carry the names of the reference engine's Rust functions they stand
+in for (engine/zc_infer_core), take torch CUDA tensors (device memory), run
+asynchronously on the current torch stream, and raise :class:`WohperError`
+with the reference's error kind (``DeepSeekV4KernelError`` order) on failure.
+
+There is no CPU fallback: if the CUDA library is missing or the device is not
+an sm_100 part, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional, Sequence
+
+from . import build as _build
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = _build.LIB
+
+STATUS_NAMES = {
+    0: "Ok",
+    1: "EmptyShape",
+    2: "InvalidShape",
+    3: "PackedWeightTooSmall",
+    4: "ScaleTooSmall",
+    5: "InputTooSmall",
+    6: "OutputTooSmall",
+    7: "ScratchTooSmall",
+    8: "NonFiniteOutput",
+    9: "InvalidPointer",
+    10: "Unsupported",
+    20: "Cuda",
+    21: "Nccl",
+    22: "Timeout",
+    23: "DeviceArg",
+}
+ROUTER_RAW_LOGITS = 0
+ROUTER_SQRT_SOFTPLUS = 1
+
+# Every symbol include/wohper_b200.h declares (checked by tests/test_capi.py).
+EXPORTS = (
+    "wh_version", "wh_ctx_create", "wh_ctx_destroy", "wh_ctx_sync", "wh_last_error_detail",
+    "wh_fp8_gemv", "wh_act_quant_fp8", "wh_fp4_matvec", "wh_fp4_expert_scratch_len",
+    "wh_fp4_expert_forward", "wh_router_topk", "wh_moe_plan_create", "wh_moe_plan_destroy",
+    "wh_moe_scratch_bytes", "wh_moe_ffn", "wh_debug_act_quant_table", "wh_debug_e4m3_round",
+    "wh_ctx_set_profiling", "wh_ctx_phase_times", "wh_debug_e4m3_round_n",
+)
+
+
+class WohperError(RuntimeError):
+    def __init__(self, status: int, detail: str = ""):
+        self.status = status
+        self.kind = STATUS_NAMES.get(status, f"Status{status}")
+        super().__init__(f"{self.kind} ({status}): {detail}")
+
+
+class Fp4MatvecSpec(C.Structure):
+    """wh_fp4_matvec_spec == Fp4Matvec (src/deepseek_v4.rs:410-417)."""
+    _fields_ = [
+        ("packed_weight", C.c_void_p), ("packed_len", C.c_size_t),
+        ("ue8m0_scales", C.c_void_p), ("scales_len", C.c_size_t),
+        ("rows", C.c_size_t), ("cols", C.c_size_t), ("scale_cols", C.c_size_t),
+    ]
+
+
+class Fp4ExpertSpec(C.Structure):
+    """wh_fp4_expert == DeepSeekV4Fp4Expert (src/deepseek_v4.rs:419-428)."""
+    _fields_ = [("w1", Fp4MatvecSpec), ("w3", Fp4MatvecSpec), ("w2", Fp4MatvecSpec)]
+
+
+class MoeDesc(C.Structure):
+    _fields_ = [
+        ("num_experts", C.c_int), ("hidden", C.c_int), ("inter", C.c_int),
+        ("experts", C.POINTER(Fp4ExpertSpec)), ("shared", C.POINTER(Fp4ExpertSpec)),
+        ("gate", C.c_void_p), ("gate_bias", C.c_void_p), ("topk", C.c_int),
+        ("router_mode", C.c_int), ("route_scale", C.c_float), ("max_tokens", C.c_int),
+    ]
+
+
+_lib: Optional[C.CDLL] = None
+
+
+def lib(build_if_missing: bool = True) -> C.CDLL:
+    """Load libwohper_b200.so (building it first if asked and it is stale)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if build_if_missing and not _build.up_to_date():
+        _build.build()
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: run python -m wohper_b200.build")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i, sz, f = C.c_void_p, C.c_int, C.c_size_t, C.c_float
+    st = C.c_int
+    sig = {
+        "wh_version": (i, []),
+        "wh_ctx_create": (st, [i, C.POINTER(vp)]),
+        "wh_ctx_destroy": (None, [vp]),
+        "wh_ctx_sync": (st, [vp, vp]),
+        "wh_last_error_detail": (C.c_char_p, []),
+        "wh_fp8_gemv": (st, [vp, vp, vp, i, i, i, i, i, i, vp, i, i, vp, i, i, vp]),
+        "wh_act_quant_fp8": (st, [vp, vp, sz, i, vp]),
+        "wh_fp4_matvec": (st, [vp, C.POINTER(Fp4MatvecSpec), vp, sz, vp, sz, vp]),
+        "wh_fp4_expert_scratch_len": (sz, [sz]),
+        "wh_fp4_expert_forward": (st, [vp, C.POINTER(Fp4ExpertSpec), vp, sz, vp, sz, vp, sz, vp]),
+        "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
+        "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
+        "wh_moe_plan_destroy": (None, [vp]),
+        "wh_moe_scratch_bytes": (sz, [vp, i]),
+        "wh_moe_ffn": (st, [vp, vp, vp, i, vp, vp, vp, vp, vp, sz, vp]),
+        "wh_debug_act_quant_table": (None, [vp]),
+        "wh_debug_e4m3_round": (f, [f]),
+        "wh_debug_e4m3_round_n": (None, [vp, vp, sz]),
+        "wh_ctx_set_profiling": (st, [vp, i]),
+        "wh_ctx_phase_times": (i, [vp, vp, i]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        detail = lib().wh_last_error_detail()
+        raise WohperError(status, detail.decode() if detail else "")
+
+
+def _ptr(t) -> Optional[int]:
+    if t is None:
+        return None
+    return int(t.data_ptr())
+
+
+def _stream(stream=None) -> Optional[int]:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+class Context:
+    """wh_ctx: one per device; owns the device status word."""
+
+    def __init__(self, device: int = 0):
+        import torch
+
+        if not torch.cuda.is_available():
+            raise RuntimeError("wohper_b200 needs a CUDA device (sm_100a); none is visible")
+        torch.cuda.set_device(device)
+        self.device = device
+        h = C.c_void_p()
+        _check(lib().wh_ctx_create(device, C.byref(h)))
+        self.handle = h
+
+    def sync(self, stream=None) -> None:
+        """Synchronise and raise the first device-side error (NonFiniteOutput...)."""
+        _check(lib().wh_ctx_sync(self.handle, _stream(stream)))
+
+    def set_profiling(self, on: bool) -> None:
+        _check(lib().wh_ctx_set_profiling(self.handle, int(bool(on))))
+
+    def phase_times(self, max_phases: int = 16) -> list:
+        buf = (C.c_float * max_phases)()
+        n = lib().wh_ctx_phase_times(self.handle, C.cast(buf, C.c_void_p), max_phases)
+        return [float(buf[i]) for i in range(n)]
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().wh_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# --------------------------------------------------------------------------
+# FP8 GEMV family (src/compute.rs:6174-6577)
+# --------------------------------------------------------------------------
+def gemv_fp8_e4m3_ue8m0_rows_multi(ctx: Context, weight, scale, inputs, row_start: int,
+                                   row_end: int, outputs=None, act_quant_block: int = 0,
+                                   stream=None):
+    """Batched row-range FP8 GEMV: outputs[b, r-row_start] for rows [row_start,row_end)."""
+    import torch
+
+    rows, cols = weight.shape
+    srows, scols = scale.shape
+    if inputs.dim() == 1:
+        inputs = inputs.view(1, -1)
+    batch = inputs.shape[0]
+    if outputs is None:
+        outputs = torch.empty(batch, row_end - row_start, device=inputs.device, dtype=torch.float32)
+    _check(lib().wh_fp8_gemv(ctx.handle, _ptr(weight), _ptr(scale), rows, cols, srows, scols,
+                             row_start, row_end, _ptr(inputs), batch, inputs.stride(0),
+                             _ptr(outputs), outputs.stride(0) if outputs.dim() > 1 else outputs.numel(),
+                             act_quant_block, _stream(stream)))
+    return outputs
+
+
+def gemv_fp8_e4m3_ue8m0_rows(ctx, weight, scale, input, row_start, row_end, output=None,
+                             act_quant_block=0, stream=None):
+    out = gemv_fp8_e4m3_ue8m0_rows_multi(ctx, weight, scale, input.view(1, -1), row_start,
+                                         row_end, None if output is None else output.view(1, -1),
+                                         act_quant_block, stream)
+    return out.view(-1)
+
+
+def gemv_fp8_e4m3_ue8m0_tensorwise(ctx, weight, scale, input, output=None, act_quant_block=0,
+                                   stream=None):
+    return gemv_fp8_e4m3_ue8m0_rows(ctx, weight, scale, input, 0, weight.shape[0], output,
+                                    act_quant_block, stream)
+
+
+def fp8_act_quant_dequant_in_place(ctx, values, block_size: int = 64, stream=None):
+    _check(lib().wh_act_quant_fp8(ctx.handle, _ptr(values), values.numel(), block_size,
+                                  _stream(stream)))
+    return values
+
+
+# --------------------------------------------------------------------------
+# FP4 (src/deepseek_v4.rs:410-601)
+# --------------------------------------------------------------------------
+@dataclass
+class Fp4Matvec:
+    """Fp4Matvec: packed_weight (uint8 [rows, (cols+1)//2]) and ue8m0_scales
+    (uint8 [rows, scale_cols]) are CUDA tensors."""
+    packed_weight: object
+    ue8m0_scales: object
+    rows: int
+    cols: int
+    scale_cols: int
+
+    def spec(self) -> Fp4MatvecSpec:
+        return Fp4MatvecSpec(_ptr(self.packed_weight), self.packed_weight.numel(),
+                             _ptr(self.ue8m0_scales), self.ue8m0_scales.numel(), self.rows,
+                             self.cols, self.scale_cols)
+
+
+@dataclass
+class DeepSeekV4Fp4Expert:
+    w1: Fp4Matvec
+    w3: Fp4Matvec
+    w2: Fp4Matvec
+
+    def spec(self) -> Fp4ExpertSpec:
+        return Fp4ExpertSpec(self.w1.spec(), self.w3.spec(), self.w2.spec())
+
+
+def fp4_e2m1_ue8m0_matvec(ctx, spec: Fp4Matvec, input, output, stream=None):
+    s = spec.spec()
+    _check(lib().wh_fp4_matvec(ctx.handle, C.byref(s), _ptr(input), input.numel(), _ptr(output),
+                               output.numel(), _stream(stream)))
+    return output
+
+
+def deepseek_v4_fp4_expert_scratch_len(intermediate: int) -> int:
+    return int(lib().wh_fp4_expert_scratch_len(intermediate))
+
+
+def deepseek_v4_fp4_expert_forward(ctx, expert: DeepSeekV4Fp4Expert, input, output, scratch,
+                                   stream=None):
+    s = expert.spec()
+    _check(lib().wh_fp4_expert_forward(ctx.handle, C.byref(s), _ptr(input), input.numel(),
+                                       _ptr(output), output.numel(), _ptr(scratch),
+                                       scratch.numel(), _stream(stream)))
+    return output
+
+
+# --------------------------------------------------------------------------
+# Router (src/compute.rs:2129-2268, src/server/generation.rs:3137-3180)
+# --------------------------------------------------------------------------
+def route_experts(ctx, gate_bf16, x, topk: int, mode: int = ROUTER_RAW_LOGITS, bias=None,
+                  route_scale: float = 1.0, hash_ids=None, logits=None, stream=None):
+    """gate_bf16: int16/uint16 bits or torch.bfloat16 [experts, hidden]; x [tokens, hidden]."""
+    import torch
+
+    if x.dim() == 1:
+        x = x.view(1, -1)
+    E, H = gate_bf16.shape
+    T = x.shape[0]
+    ids = torch.empty(T, topk, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, topk, dtype=torch.float32, device=x.device)
+    _check(lib().wh_router_topk(ctx.handle, _ptr(gate_bf16), E, H, _ptr(x), T, topk, mode,
+                                _ptr(bias), route_scale, _ptr(hash_ids), _ptr(ids), _ptr(w),
+                                _ptr(logits), _stream(stream)))
+    return ids, w
+
+
+# --------------------------------------------------------------------------
+# MoE layer
+# --------------------------------------------------------------------------
+class MoeLayer:
+    """A prepared MoE FFN layer (router + routed FP4 experts + shared expert).
+
+    forward(x) replaces routing + compute_active_and_shared_experts
+    (src/compute.rs:1872-2030) for each token of x [tokens, hidden].
+    """
+
+    def __init__(self, ctx: Context, experts: Sequence[DeepSeekV4Fp4Expert],
+                 shared: Optional[DeepSeekV4Fp4Expert], gate_bf16, topk: int = 6,
+                 router_mode: int = ROUTER_RAW_LOGITS, route_scale: float = 1.0,
+                 gate_bias=None, max_tokens: int = 1):
+        import torch
+
+        self.ctx = ctx
+        self.hidden = experts[0].w1.cols
+        self.inter = experts[0].w1.rows
+        self.topk = topk
+        self._experts = list(experts)
+        self._shared = shared
+        self._gate = gate_bf16
+        self._bias = gate_bias
+        arr = (Fp4ExpertSpec * len(experts))(*[e.spec() for e in experts])
+        sh = shared.spec() if shared is not None else None
+        d = MoeDesc(len(experts), self.hidden, self.inter, arr,
+                    C.pointer(sh) if sh is not None else None, _ptr(gate_bf16), _ptr(gate_bias),
+                    topk, router_mode, route_scale, max_tokens)
+        h = C.c_void_p()
+        _check(lib().wh_moe_plan_create(ctx.handle, C.byref(d), C.byref(h)))
+        self.plan = h
+        self.max_tokens = max_tokens
+        nbytes = lib().wh_moe_scratch_bytes(h, max_tokens)
+        self.scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{ctx.device}")
+
+    def forward(self, x, y=None, ids=None, weights=None, hash_ids=None, stream=None):
+        import torch
+
+        if x.dim() == 1:
+            x = x.view(1, -1)
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty_like(x)
+        _check(lib().wh_moe_ffn(self.ctx.handle, self.plan, _ptr(x), T, _ptr(hash_ids), _ptr(y),
+                                _ptr(ids), _ptr(weights), _ptr(self.scratch), self.scratch.numel(),
+                                _stream(stream)))
+        return y
+
+    def close(self):
+        if getattr(self, "plan", None):
+            lib().wh_moe_plan_destroy(self.plan)
+            self.plan = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,737 @@
+// capi.cu -- the extern "C" boundary (include/wohper_b200.h): argument
+// validation in the reference's error order, tensor-map construction, plan /
+// context management and kernel dispatch.  Host code only.
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/wohper_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace wh {
+cudaError_t launch_router_ex(const RouterArgs& a, __half* xq, float* xq_mult, cudaStream_t s,
+                             bool pdl);
+cudaError_t launch_moe_up_ex(const MoeArgs& a, const __half* xq, const float* xq_mult, __half* hq,
+                             float* hq_mult, cudaStream_t s, bool pdl);
+cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* hq_mult,
+                               cudaStream_t s, bool pdl);
+cudaError_t launch_xq(const float* x, int n, int tokens, __half* xq, float* xq_mult,
+                      cudaStream_t s);
+cudaError_t launch_swiglu(float* gate, const float* up, int n, uint32_t* status, cudaStream_t s);
+}  // namespace wh
+
+using namespace wh;
+
+namespace {
+
+thread_local std::string g_detail;
+
+wh_status fail(wh_status st, const std::string& why) {
+  g_detail = why;
+  return st;
+}
+wh_status cuda_fail(cudaError_t e, const char* where) {
+  g_detail = std::string(where) + ": " + cudaGetErrorString(e);
+  return WH_ERR_CUDA;
+}
+#define WH_CUDA(call)                                   \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---------------------------------------------------------------------------
+// Act-quant threshold table: ceilf(log2f(q)) == k for q = 2^k * (1 + m/2^23)
+// exactly when m == 0 or m < thr[E] (E = k + 127); measured with the host
+// libm log2f, which is what the reference engine calls.
+// ---------------------------------------------------------------------------
+ActQuantTable build_act_quant_table() {
+  ActQuantTable t;
+  for (int E = 0; E < 256; ++E) {
+    t.thr[E] = 0;
+    if (E == 0 || E == 255) continue;
+    const int k = E - 127;
+    auto ceil_is_k = [&](uint32_t m) {
+      float q = u2f((uint32_t(E) << 23) | m);
+      return ceilf(log2f(q)) == (float)k;
+    };
+    // smallest m in [1, 2^23) with ceil(log2f(q)) != k  (log2f is monotonic)
+    uint32_t lo = 1, hi = 1u << 23;
+    if (!ceil_is_k(1)) {
+      t.thr[E] = 1;
+      continue;
+    }
+    while (hi - lo > 1) {
+      uint32_t mid = lo + (hi - lo) / 2;
+      if (ceil_is_k(mid))
+        lo = mid;
+      else
+        hi = mid;
+    }
+    t.thr[E] = hi;
+  }
+  return t;
+}
+const ActQuantTable& act_quant_table_host() {
+  static ActQuantTable t = build_act_quant_table();
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor maps
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// u8 matrix [rows][row_bytes], box [box_rows][128 B], 128-byte swizzle.
+wh_status make_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                      uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(WH_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d) rows=%llu row_bytes=%llu",
+             (int)r, (unsigned long long)rows, (unsigned long long)row_bytes);
+    return fail(WH_ERR_CUDA, buf);
+  }
+  return WH_OK;
+}
+
+// validate_fp4_matvec (src/deepseek_v4.rs:434-462)
+wh_status validate_fp4(const wh_fp4_matvec_spec& s, size_t input_len, size_t output_len) {
+  if (s.rows == 0 || s.cols == 0 || s.scale_cols == 0) return fail(WH_ERR_EMPTY_SHAPE, "empty shape");
+  if (input_len < s.cols) return fail(WH_ERR_INPUT_TOO_SMALL, "input too small");
+  if (output_len < s.rows) return fail(WH_ERR_OUTPUT_TOO_SMALL, "output too small");
+  if (s.cols % s.scale_cols != 0) return fail(WH_ERR_INVALID_SHAPE, "cols % scale_cols != 0");
+  const size_t row_bytes = (s.cols + 1) / 2;
+  if (s.rows > SIZE_MAX / row_bytes) return fail(WH_ERR_INVALID_SHAPE, "weight size overflow");
+  if (s.packed_len < s.rows * row_bytes)
+    return fail(WH_ERR_PACKED_WEIGHT_TOO_SMALL, "packed weight too small");
+  if (s.rows > SIZE_MAX / s.scale_cols) return fail(WH_ERR_INVALID_SHAPE, "scale size overflow");
+  if (s.scales_len < s.rows * s.scale_cols) return fail(WH_ERR_SCALE_TOO_SMALL, "scales too small");
+  if (!s.packed_weight || !s.ue8m0_scales) return fail(WH_ERR_INVALID_POINTER, "null weight");
+  if (s.rows > 0x7fffffff || s.cols > 0x7fffffff) return fail(WH_ERR_UNSUPPORTED, "shape > 2^31");
+  return WH_OK;
+}
+
+// Fast (TMA) path shape rule for an expert: 32-column groups, box-aligned rows.
+bool expert_fast_ok(const wh_fp4_expert& e, size_t hidden, size_t inter) {
+  auto ok = [](const wh_fp4_matvec_spec& s) {
+    return s.cols % 32 == 0 && s.scale_cols == s.cols / 32 && aligned(s.packed_weight, 16) &&
+           aligned(s.ue8m0_scales, 8);
+  };
+  return ok(e.w1) && ok(e.w3) && ok(e.w2) && hidden % 256 == 0 && inter % 256 == 0 &&
+         hidden % 16 == 0 && hidden <= 16384 && inter <= 16384;
+}
+
+struct DevExpertSet {
+  CUtensorMap* maps = nullptr;      // device [n][3]
+  Fp4ExpertDev* experts = nullptr;  // device [n]
+  int n = 0;
+};
+
+wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) {
+  std::vector<CUtensorMap> maps(size_t(n) * 3);
+  std::vector<Fp4ExpertDev> ex(n);
+  for (int i = 0; i < n; ++i) {
+    const wh_fp4_expert& e = list[i];
+    wh_status st;
+    if ((st = make_u8_map(&maps[i * 3 + 0], e.w1.packed_weight, e.w1.rows, e.w1.cols / 2, 64)))
+      return st;
+    if ((st = make_u8_map(&maps[i * 3 + 1], e.w3.packed_weight, e.w3.rows, e.w3.cols / 2, 64)))
+      return st;
+    if ((st = make_u8_map(&maps[i * 3 + 2], e.w2.packed_weight, e.w2.rows, e.w2.cols / 2, 16)))
+      return st;
+    ex[i] = Fp4ExpertDev{e.w1.ue8m0_scales, e.w3.ue8m0_scales, e.w2.ue8m0_scales,
+                         e.w1.packed_weight, e.w3.packed_weight, e.w2.packed_weight};
+  }
+  WH_CUDA(cudaMalloc(&out->maps, maps.size() * sizeof(CUtensorMap)));
+  WH_CUDA(cudaMalloc(&out->experts, ex.size() * sizeof(Fp4ExpertDev)));
+  WH_CUDA(cudaMemcpy(out->maps, maps.data(), maps.size() * sizeof(CUtensorMap),
+                     cudaMemcpyHostToDevice));
+  WH_CUDA(cudaMemcpy(out->experts, ex.data(), ex.size() * sizeof(Fp4ExpertDev),
+                     cudaMemcpyHostToDevice));
+  out->n = n;
+  return WH_OK;
+}
+void free_expert_set(DevExpertSet& s) {
+  if (s.maps) cudaFree(s.maps);
+  if (s.experts) cudaFree(s.experts);
+  s = DevExpertSet{};
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+struct wh_ctx {
+  int device = 0;
+  int num_sms = 148;
+  uint32_t* status = nullptr;    // device word: WH_DEV_* bits
+  uint32_t* counters = nullptr;  // device, router last-CTA counters (zero at rest)
+  int counters_len = 0;
+  void* work = nullptr;  // generic-path workspace
+  size_t work_bytes = 0;
+  std::map<std::tuple<const void*, int, int, int>, CUtensorMap> fp8_maps;
+  std::map<std::tuple<const void*, const void*, const void*, size_t, size_t>, DevExpertSet> experts;
+  bool profile = false;
+  std::vector<cudaEvent_t> ev;  // 2 per phase
+  int phases = 0;
+
+  bool pdl() const { return !profile; }
+  void prof_begin() { phases = 0; }
+  wh_status prof_mark(cudaStream_t s) {  // call before the first and after every kernel
+    if (!profile) return WH_OK;
+    if ((int)ev.size() <= phases) {
+      cudaEvent_t e;
+      WH_CUDA(cudaEventCreate(&e));
+      ev.push_back(e);
+    }
+    WH_CUDA(cudaEventRecord(ev[phases], s));
+    ++phases;
+    return WH_OK;
+  }
+
+  wh_status ensure_work(size_t bytes) {
+    if (bytes <= work_bytes) return WH_OK;
+    if (work) cudaFree(work);
+    work = nullptr;
+    work_bytes = 0;
+    WH_CUDA(cudaMalloc(&work, bytes));
+    work_bytes = bytes;
+    return WH_OK;
+  }
+  wh_status ensure_counters(int n) {
+    if (n <= counters_len) return WH_OK;
+    if (counters) cudaFree(counters);
+    counters = nullptr;
+    counters_len = 0;
+    WH_CUDA(cudaMalloc(&counters, sizeof(uint32_t) * n));
+    WH_CUDA(cudaMemset(counters, 0, sizeof(uint32_t) * n));
+    counters_len = n;
+    return WH_OK;
+  }
+};
+
+struct wh_moe_plan {
+  wh_ctx* ctx = nullptr;
+  wh_moe_desc d{};
+  DevExpertSet set;  // routed experts, then the shared expert
+  uint32_t* counters = nullptr;
+};
+
+extern "C" {
+
+int wh_version(void) { return 100; }
+
+const char* wh_last_error_detail(void) { return g_detail.c_str(); }
+
+wh_status wh_ctx_create(int device, wh_ctx** out) {
+  if (!out) return fail(WH_ERR_INVALID_POINTER, "out is null");
+  *out = nullptr;
+  WH_CUDA(cudaSetDevice(device));
+  int major = 0, minor = 0;
+  WH_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  WH_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+  if (major != 10 || minor != 0)
+    return fail(WH_ERR_UNSUPPORTED, "wohper_b200 kernels are built for sm_100a (B200)");
+  wh_ctx* c = new wh_ctx();
+  c->device = device;
+  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  cudaError_t e = cudaMalloc(&c->status, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) {
+    delete c;
+    return cuda_fail(e, "status word");
+  }
+  set_act_quant_table(act_quant_table_host(), nullptr);
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(c->status);
+    delete c;
+    return cuda_fail(e, "act quant table upload");
+  }
+  *out = c;
+  return WH_OK;
+}
+
+void wh_ctx_destroy(wh_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  for (auto& kv : c->experts) free_expert_set(kv.second);
+  for (auto e : c->ev) cudaEventDestroy(e);
+  if (c->status) cudaFree(c->status);
+  if (c->counters) cudaFree(c->counters);
+  if (c->work) cudaFree(c->work);
+  delete c;
+}
+
+wh_status wh_ctx_sync(wh_ctx* c, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  WH_CUDA(cudaStreamSynchronize(stream));
+  uint32_t st = 0;
+  WH_CUDA(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost));
+  if (st == 0) return WH_OK;
+  WH_CUDA(cudaMemset(c->status, 0, sizeof st));
+  if (st & WH_DEV_TIMEOUT) return fail(WH_ERR_TIMEOUT, "a device-side wait timed out");
+  if (st & WH_DEV_BADARG) return fail(WH_ERR_DEVICE_ARG, "device-side index check failed");
+  return fail(WH_ERR_NON_FINITE_OUTPUT, "non-finite output");
+}
+
+wh_status wh_ctx_set_profiling(wh_ctx* c, int on) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  c->profile = on != 0;
+  c->phases = 0;
+  return WH_OK;
+}
+
+int wh_ctx_phase_times(wh_ctx* c, float* ms, int max_phases) {
+  if (!c || !c->profile || c->phases < 2) return 0;
+  if (cudaEventSynchronize(c->ev[c->phases - 1]) != cudaSuccess) return 0;
+  int n = 0;
+  for (int i = 0; i + 1 < c->phases && n < max_phases; ++i, ++n)
+    cudaEventElapsedTime(&ms[n], c->ev[i], c->ev[i + 1]);
+  return n;
+}
+
+// ---------------------------------------------------------------------------
+wh_status wh_act_quant_fp8(wh_ctx* c, float* v, size_t n, int block, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  if (block <= 0 || n == 0) return WH_OK;  // the reference returns early
+  if (!v) return fail(WH_ERR_INVALID_POINTER, "values is null");
+  WH_CUDA(launch_act_quant(v, (long long)n, block, c->status, c->num_sms, stream));
+  return WH_OK;
+}
+
+wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows, int cols,
+                      int scale_rows, int scale_cols, int row_start, int row_end, const float* x,
+                      int batch, int ldx, float* y, int ldy, int act_quant_block,
+                      wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  // src/compute.rs:6256-6289 validation order
+  if (rows <= 0 || cols <= 0 || scale_rows <= 0 || scale_cols <= 0 || rows % scale_rows != 0 ||
+      cols % scale_cols != 0)
+    return fail(WH_ERR_INVALID_SHAPE, "DeepSeek FP8 scale shape");
+  if (row_start < 0 || row_start >= row_end || row_end > rows)
+    return fail(WH_ERR_INVALID_SHAPE, "DeepSeek FP8 row range");
+  if (batch <= 0) return fail(WH_ERR_INVALID_SHAPE, "FP8 multi GEMV input/output count");
+  if (ldx < cols) return fail(WH_ERR_INVALID_SHAPE, "DeepSeek FP8 GEMV input too small");
+  if (ldy < row_end - row_start) return fail(WH_ERR_OUTPUT_TOO_SMALL, "output too small");
+  if (act_quant_block < 0) return fail(WH_ERR_INVALID_SHAPE, "act_quant_block < 0");
+  if (!weight || !scale || !x || !y) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+
+  Fp8GemvArgs a{};
+  a.weight = weight;
+  a.scale = scale;
+  a.rows = rows;
+  a.cols = cols;
+  a.scale_rows = scale_rows;
+  a.scale_cols = scale_cols;
+  a.row_start = row_start;
+  a.row_end = row_end;
+  a.x = x;
+  a.ldx = ldx;
+  a.y = y;
+  a.ldy = ldy;
+  a.batch = batch;
+  a.act_quant_block = act_quant_block;
+  a.status = c->status;
+
+  const bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
+                    ldx % 4 == 0 && fp8_gemv_smem_bytes(1, cols) <= 200 * 1024;
+  if (fast) {
+    const int nrows = row_end - row_start;
+    int tb = batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8;
+    while (tb > 1 && fp8_gemv_smem_bytes(tb, cols) > 200 * 1024) tb /= 2;
+    const int tiles = (batch + tb - 1) / tb;
+    int per = std::max(1, c->num_sms / tiles);
+    int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
+    a.box_rows = box_rows;
+    auto key = std::make_tuple((const void*)weight, rows, cols, box_rows);
+    auto it = c->fp8_maps.find(key);
+    if (it == c->fp8_maps.end()) {
+      CUtensorMap m;
+      wh_status st = make_u8_map(&m, weight, rows, cols, box_rows);
+      if (st != WH_OK) return st;
+      it = c->fp8_maps.emplace(key, m).first;
+    }
+    // the launcher picks TB from batch; keep it consistent with the smem check
+    if (tb != (batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8)) {
+      // large cols: run the batch in slices the shared memory can hold
+      for (int b0 = 0; b0 < batch; b0 += tb) {
+        Fp8GemvArgs s = a;
+        s.x = x + (size_t)b0 * ldx;
+        s.y = y + (size_t)b0 * ldy;
+        s.batch = std::min(tb, batch - b0);
+        WH_CUDA(launch_fp8_gemv(&it->second, s, c->num_sms, stream, false));
+      }
+      return WH_OK;
+    }
+    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, false));
+    return WH_OK;
+  }
+  // generic path
+  if (act_quant_block > 0) {
+    wh_status st = c->ensure_work(sizeof(float) * (size_t)batch * cols);
+    if (st != WH_OK) return st;
+    float* xw = static_cast<float*>(c->work);
+    WH_CUDA(cudaMemcpy2DAsync(xw, sizeof(float) * cols, x, sizeof(float) * ldx,
+                              sizeof(float) * cols, batch, cudaMemcpyDeviceToDevice, stream));
+    WH_CUDA(launch_act_quant(xw, (long long)batch * cols, act_quant_block, c->status, c->num_sms,
+                             stream));
+    // blocks must not straddle inputs: the reference quantises each input alone
+    if (cols % act_quant_block != 0) {
+      for (int b = 0; b < batch; ++b) {
+        WH_CUDA(cudaMemcpyAsync(xw + (size_t)b * cols, x + (size_t)b * ldx, sizeof(float) * cols,
+                                cudaMemcpyDeviceToDevice, stream));
+        WH_CUDA(launch_act_quant(xw + (size_t)b * cols, cols, act_quant_block, c->status,
+                                 c->num_sms, stream));
+      }
+    }
+    a.x = xw;
+    a.ldx = cols;
+    a.act_quant_block = 0;
+  }
+  WH_CUDA(launch_fp8_gemv(nullptr, a, c->num_sms, stream, false));
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
+wh_status wh_fp4_matvec(wh_ctx* c, const wh_fp4_matvec_spec* s, const float* input,
+                        size_t input_len, float* output, size_t output_len, wh_stream_t stream) {
+  if (!c || !s) return fail(WH_ERR_INVALID_POINTER, "null ctx/spec");
+  wh_status st = validate_fp4(*s, input_len, output_len);
+  if (st != WH_OK) return st;
+  if (!input || !output) return fail(WH_ERR_INVALID_POINTER, "null input/output");
+  Fp4MatvecArgs a{s->packed_weight, s->ue8m0_scales, (int)s->rows, (int)s->cols,
+                  (int)s->scale_cols, input, output, c->status};
+  WH_CUDA(launch_fp4_matvec(a, c->num_sms, stream));
+  return WH_OK;
+}
+
+size_t wh_fp4_expert_scratch_len(size_t intermediate) { return intermediate * 2; }
+
+wh_status wh_fp4_expert_forward(wh_ctx* c, const wh_fp4_expert* e, const float* input,
+                                size_t input_len, float* output, size_t output_len,
+                                float* scratch, size_t scratch_len, wh_stream_t stream) {
+  if (!c || !e) return fail(WH_ERR_INVALID_POINTER, "null ctx/expert");
+  // src/deepseek_v4.rs:567-583
+  if (e->w1.cols != input_len || e->w3.cols != input_len || e->w1.rows != e->w3.rows ||
+      e->w2.cols != e->w1.rows)
+    return fail(WH_ERR_INVALID_SHAPE, "expert shapes");
+  if (output_len < e->w2.rows) return fail(WH_ERR_OUTPUT_TOO_SMALL, "output too small");
+  const size_t inter = e->w1.rows, hidden = input_len;
+  if (scratch_len < wh_fp4_expert_scratch_len(inter))
+    return fail(WH_ERR_SCRATCH_TOO_SMALL, "scratch too small");
+  wh_status st;
+  if ((st = validate_fp4(e->w1, hidden, inter)) != WH_OK) return st;
+  if ((st = validate_fp4(e->w3, hidden, inter)) != WH_OK) return st;
+  if ((st = validate_fp4(e->w2, inter, output_len)) != WH_OK) return st;
+  if (!input || !output || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+
+  if (expert_fast_ok(*e, hidden, inter) && e->w2.rows == hidden) {
+    auto key = std::make_tuple((const void*)e->w1.packed_weight, (const void*)e->w3.packed_weight,
+                               (const void*)e->w2.packed_weight, hidden, inter);
+    auto it = c->experts.find(key);
+    if (it == c->experts.end()) {
+      DevExpertSet set;
+      if ((st = build_expert_set(e, 1, &set)) != WH_OK) return st;
+      it = c->experts.emplace(key, set).first;
+    }
+    // scratch layout: xq f16[hidden] | xq_mult f32[hidden/64] | hq f16[inter] | hq_mult f32[inter/64]
+    const size_t need = align256(hidden * 2) + align256(hidden / 16) + align256(inter * 2) +
+                        align256(inter / 16);
+    uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
+    if (need > scratch_len * sizeof(float) || !aligned(scratch, 256)) {
+      if ((st = c->ensure_work(need)) != WH_OK) return st;
+      base = static_cast<uint8_t*>(c->work);
+    }
+    __half* xq = reinterpret_cast<__half*>(base);
+    float* xqm = reinterpret_cast<float*>(base + align256(hidden * 2));
+    __half* hq = reinterpret_cast<__half*>(base + align256(hidden * 2) + align256(hidden / 16));
+    float* hqm = reinterpret_cast<float*>(base + align256(hidden * 2) + align256(hidden / 16) +
+                                          align256(inter * 2));
+    MoeArgs a{};
+    a.maps = it->second.maps;
+    a.experts = it->second.experts;
+    a.num_experts = 0;
+    a.has_shared = 1;
+    a.hidden = (int)hidden;
+    a.inter = (int)inter;
+    a.x = input;
+    a.tokens = 1;
+    a.topk = 0;
+    a.y = output;
+    a.expert_out = output;
+    a.combine = 0;
+    a.status = c->status;
+    c->prof_begin();
+    if ((st = c->prof_mark(stream)) != WH_OK) return st;
+    WH_CUDA(launch_xq(input, (int)hidden, 1, xq, xqm, stream));
+    if ((st = c->prof_mark(stream)) != WH_OK) return st;
+    WH_CUDA(launch_moe_up_ex(a, xq, xqm, hq, hqm, stream, c->pdl()));
+    if ((st = c->prof_mark(stream)) != WH_OK) return st;
+    WH_CUDA(launch_moe_down_ex(a, hq, hqm, stream, c->pdl()));
+    return c->prof_mark(stream);
+  }
+  // generic exact path: act quant -> w1,w3 -> SwiGLU -> act quant -> w2
+  if ((st = c->ensure_work(sizeof(float) * hidden)) != WH_OK) return st;
+  float* xw = static_cast<float*>(c->work);
+  WH_CUDA(cudaMemcpyAsync(xw, input, sizeof(float) * hidden, cudaMemcpyDeviceToDevice, stream));
+  WH_CUDA(launch_act_quant(xw, (long long)hidden, 64, c->status, c->num_sms, stream));
+  float* gate = scratch;
+  float* up = scratch + inter;
+  Fp4MatvecArgs m1{e->w1.packed_weight, e->w1.ue8m0_scales, (int)inter, (int)hidden,
+                   (int)e->w1.scale_cols, xw, gate, c->status};
+  Fp4MatvecArgs m3{e->w3.packed_weight, e->w3.ue8m0_scales, (int)inter, (int)hidden,
+                   (int)e->w3.scale_cols, xw, up, c->status};
+  WH_CUDA(launch_fp4_matvec(m1, c->num_sms, stream));
+  WH_CUDA(launch_fp4_matvec(m3, c->num_sms, stream));
+  WH_CUDA(launch_swiglu(gate, up, (int)inter, c->status, stream));
+  WH_CUDA(launch_act_quant(gate, (long long)inter, 64, c->status, c->num_sms, stream));
+  Fp4MatvecArgs m2{e->w2.packed_weight, e->w2.ue8m0_scales, (int)e->w2.rows, (int)inter,
+                   (int)e->w2.scale_cols, gate, output, c->status};
+  WH_CUDA(launch_fp4_matvec(m2, c->num_sms, stream));
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
+wh_status wh_router_topk(wh_ctx* c, const uint16_t* gate, int experts, int hidden,
+                         const float* x, int tokens, int topk, int mode, const float* bias,
+                         float route_scale, const int32_t* hash_ids, int32_t* ids,
+                         float* weights, float* logits, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  if (experts <= 0 || hidden <= 0 || tokens <= 0 || topk <= 0)
+    return fail(WH_ERR_INVALID_SHAPE, "router shape");
+  if (experts > 1024 || topk > 32) return fail(WH_ERR_UNSUPPORTED, "experts > 1024 or topk > 32");
+  if (mode != WH_ROUTER_RAW_LOGITS && mode != WH_ROUTER_SQRT_SOFTPLUS)
+    return fail(WH_ERR_INVALID_SHAPE, "router mode");
+  if (!gate || !x || !ids || !weights) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  // the 16-column chunk loop reads bf16 pairs and float2s; below one chunk only
+  // the scalar tail runs
+  if (hidden >= 16 && (hidden % 2 != 0 || !aligned(gate, 4) || !aligned(x, 8)))
+    return fail(WH_ERR_UNSUPPORTED, "router needs an even hidden size and aligned rows");
+  wh_status st = c->ensure_counters(tokens);
+  if (st != WH_OK) return st;
+  float* lg = logits;
+  if (!lg) {
+    if ((st = c->ensure_work(sizeof(float) * (size_t)tokens * experts)) != WH_OK) return st;
+    lg = static_cast<float*>(c->work);
+  }
+  RouterArgs a{};
+  a.gate = gate;
+  a.experts = experts;
+  a.hidden = hidden;
+  a.x = x;
+  a.tokens = tokens;
+  a.topk = topk;
+  a.mode = mode;
+  a.bias = bias;
+  a.route_scale = route_scale;
+  a.hash_ids = hash_ids;
+  a.logits = lg;
+  a.ids = ids;
+  a.weights = weights;
+  a.combine_w = nullptr;
+  a.counters = c->counters;
+  a.status = c->status;
+  WH_CUDA(launch_router_ex(a, nullptr, nullptr, stream, false));
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
+wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out) {
+  if (!c || !d || !out) return fail(WH_ERR_INVALID_POINTER, "null argument");
+  *out = nullptr;
+  if (d->num_experts <= 0 || d->hidden <= 0 || d->inter <= 0 || d->topk <= 0 ||
+      d->max_tokens <= 0)
+    return fail(WH_ERR_EMPTY_SHAPE, "moe shape");
+  if (d->topk > d->num_experts || d->topk > 7 || d->num_experts > 1024)
+    return fail(WH_ERR_UNSUPPORTED, "topk must be <= 7 (8 slots with the shared expert)");
+  if (!d->experts || !d->gate) return fail(WH_ERR_INVALID_POINTER, "experts/gate");
+  if (d->router_mode != WH_ROUTER_RAW_LOGITS && d->router_mode != WH_ROUTER_SQRT_SOFTPLUS)
+    return fail(WH_ERR_INVALID_SHAPE, "router mode");
+  const int n = d->num_experts + (d->shared ? 1 : 0);
+  std::vector<wh_fp4_expert> all(d->experts, d->experts + d->num_experts);
+  if (d->shared) all.push_back(*d->shared);
+  for (const auto& e : all) {
+    if (e.w1.cols != (size_t)d->hidden || e.w3.cols != (size_t)d->hidden ||
+        e.w1.rows != (size_t)d->inter || e.w3.rows != (size_t)d->inter ||
+        e.w2.cols != (size_t)d->inter || e.w2.rows != (size_t)d->hidden)
+      return fail(WH_ERR_INVALID_SHAPE, "expert shape differs from the layer shape");
+    wh_status st;
+    if ((st = validate_fp4(e.w1, d->hidden, d->inter)) != WH_OK) return st;
+    if ((st = validate_fp4(e.w3, d->hidden, d->inter)) != WH_OK) return st;
+    if ((st = validate_fp4(e.w2, d->inter, d->hidden)) != WH_OK) return st;
+    if (!expert_fast_ok(e, d->hidden, d->inter))
+      return fail(WH_ERR_UNSUPPORTED,
+                  "MoE layer needs 32-column scale groups, hidden/inter multiples of 256 and "
+                  "16-byte aligned weights");
+  }
+  wh_moe_plan* p = new wh_moe_plan();
+  p->ctx = c;
+  p->d = *d;
+  p->d.experts = nullptr;
+  p->d.shared = nullptr;
+  wh_status st = build_expert_set(all.data(), n, &p->set);
+  if (st != WH_OK) {
+    free_expert_set(p->set);
+    delete p;
+    return st;
+  }
+  p->d.shared = d->shared ? reinterpret_cast<const wh_fp4_expert*>(1) : nullptr;  // flag only
+  cudaError_t e = cudaMalloc(&p->counters, sizeof(uint32_t) * d->max_tokens);
+  if (e == cudaSuccess) e = cudaMemset(p->counters, 0, sizeof(uint32_t) * d->max_tokens);
+  if (e != cudaSuccess) {
+    free_expert_set(p->set);
+    delete p;
+    return cuda_fail(e, "plan counters");
+  }
+  *out = p;
+  return WH_OK;
+}
+
+void wh_moe_plan_destroy(wh_moe_plan* p) {
+  if (!p) return;
+  free_expert_set(p->set);
+  if (p->counters) cudaFree(p->counters);
+  delete p;
+}
+
+namespace {
+struct MoeScratch {
+  float* logits;
+  float* combine_w;
+  int32_t* ids;
+  float* weights;
+  __half* xq;
+  float* xq_mult;
+  __half* hq;
+  float* hq_mult;
+  size_t bytes;
+};
+MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
+  const auto& d = p->d;
+  const int S = d.topk + (d.shared ? 1 : 0);
+  MoeScratch s{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* q = base ? base + off : nullptr;
+    off += align256(bytes);
+    return q;
+  };
+  s.logits = reinterpret_cast<float*>(take(sizeof(float) * T * d.num_experts));
+  s.combine_w = reinterpret_cast<float*>(take(sizeof(float) * T * d.topk));
+  s.ids = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * T * d.topk));
+  s.weights = reinterpret_cast<float*>(take(sizeof(float) * T * d.topk));
+  s.xq = reinterpret_cast<__half*>(take(2 * (size_t)T * d.hidden));
+  s.xq_mult = reinterpret_cast<float*>(take(sizeof(float) * T * (d.hidden / 64)));
+  s.hq = reinterpret_cast<__half*>(take(2 * (size_t)T * S * d.inter));
+  s.hq_mult = reinterpret_cast<float*>(take(sizeof(float) * T * S * (d.inter / 64)));
+  s.bytes = off;
+  return s;
+}
+}  // namespace
+
+size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
+  if (!p || tokens <= 0) return 0;
+  return moe_scratch_layout(p, tokens, nullptr).bytes;
+}
+
+wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
+                     const int32_t* hash_ids, float* y, int32_t* ids_out, float* weights_out,
+                     void* scratch, size_t scratch_bytes, wh_stream_t stream) {
+  if (!c || !p) return fail(WH_ERR_INVALID_POINTER, "null ctx/plan");
+  if (tokens <= 0) return fail(WH_ERR_EMPTY_SHAPE, "tokens <= 0");
+  if (tokens > p->d.max_tokens) return fail(WH_ERR_INVALID_SHAPE, "tokens > plan max_tokens");
+  if (!x || !y || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  if (!aligned(x, 16) || !aligned(scratch, 256))
+    return fail(WH_ERR_INVALID_POINTER, "x must be 16-byte and scratch 256-byte aligned");
+  MoeScratch s = moe_scratch_layout(p, tokens, static_cast<uint8_t*>(scratch));
+  if (scratch_bytes < s.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "moe scratch too small");
+  const auto& d = p->d;
+  RouterArgs r{};
+  r.gate = d.gate;
+  r.experts = d.num_experts;
+  r.hidden = d.hidden;
+  r.x = x;
+  r.tokens = tokens;
+  r.topk = d.topk;
+  r.mode = d.router_mode;
+  r.bias = d.gate_bias;
+  r.route_scale = d.route_scale;
+  r.hash_ids = hash_ids;
+  r.logits = s.logits;
+  r.ids = ids_out ? ids_out : s.ids;
+  r.weights = weights_out ? weights_out : s.weights;
+  r.combine_w = s.combine_w;
+  r.counters = p->counters;
+  r.status = c->status;
+  c->prof_begin();
+  wh_status pst;
+  if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
+  WH_CUDA(launch_router_ex(r, s.xq, s.xq_mult, stream, c->pdl()));
+  if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
+  MoeArgs a{};
+  a.maps = p->set.maps;
+  a.experts = p->set.experts;
+  a.num_experts = d.num_experts;
+  a.has_shared = d.shared ? 1 : 0;
+  a.hidden = d.hidden;
+  a.inter = d.inter;
+  a.x = x;
+  a.tokens = tokens;
+  a.topk = d.topk;
+  a.ids = r.ids;
+  a.combine_w = s.combine_w;
+  a.h = nullptr;
+  a.y = y;
+  a.expert_out = nullptr;
+  a.combine = 1;
+  a.status = c->status;
+  WH_CUDA(launch_moe_up_ex(a, s.xq, s.xq_mult, s.hq, s.hq_mult, stream, c->pdl()));
+  if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
+  WH_CUDA(launch_moe_down_ex(a, s.hq, s.hq_mult, stream, c->pdl()));
+  return c->prof_mark(stream);
+}
+
+void wh_debug_act_quant_table(uint32_t out[256]) {
+  const ActQuantTable& t = act_quant_table_host();
+  memcpy(out, t.thr, sizeof(t.thr));
+}
+
+float wh_debug_e4m3_round(float t) { return e4m3_nearest_ties_lower(t); }
+
+void wh_debug_e4m3_round_n(const float* in, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = e4m3_nearest_ties_lower(in[i]);
+}
+
+}  // extern "C"

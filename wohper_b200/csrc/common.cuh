@@ -1,0 +1,268 @@
+// common.cuh -- device helpers shared by every wohper_b200 kernel (sm_100a).
+//
+// * bounded mbarrier waits (every spin has a %globaltimer deadline; on expiry
+//   the kernel records WH_DEV_TIMEOUT in the context status word and returns,
+//   it never traps),
+// * TMA (cp.async.bulk.tensor, no multicast) and 1-D bulk copies into shared
+//   memory,
+// * exact decoders for the reference's FP8 E4M3 / UE8M0 / FP4 tables,
+// * the reference's FP8 activation quant-dequant rounding, bit for bit.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#define WH_DEV_NONFINITE 1u  // an output was NaN/Inf (DeepSeekV4KernelError::NonFiniteOutput)
+#define WH_DEV_TIMEOUT 2u    // a bounded wait expired
+#define WH_DEV_BADARG 4u     // a device-side argument check failed (index out of range)
+
+#ifndef WH_WAIT_NS
+#define WH_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait in these kernels
+#endif
+
+namespace wh {
+
+__host__ __device__ __forceinline__ uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+  return __float_as_uint(f);
+#else
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+#endif
+}
+__host__ __device__ __forceinline__ float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float(u);
+#else
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void flag(uint32_t* status, uint32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and flags WH_DEV_TIMEOUT) if the phase did not
+// complete before the deadline.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t* status) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, phase)) {
+    if (globaltimer() - start > WH_WAIT_NS) {
+      flag(status, WH_DEV_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// TMA / bulk copies (no .multicast::cluster anywhere in this project)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// 2-D tiled load; c0 = innermost coordinate (bytes for u8 maps; multiple of 16).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+// 1-D bulk copy: src, dst 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue early / wait for the previous kernel's memory to be visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Packed / mixed-precision FP32 arithmetic (sm_100)
+// ---------------------------------------------------------------------------
+// Two independent IEEE fmas: (a.x*b.x+c.x, a.y*b.y+c.y), each rounded once.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t A = (uint64_t(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+  uint64_t B = (uint64_t(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
+  uint64_t Cc = (uint64_t(__float_as_uint(c.y)) << 32) | __float_as_uint(c.x);
+  uint64_t D;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(Cc));
+  return make_float2(__uint_as_float(uint32_t(D)), __uint_as_float(uint32_t(D >> 32)));
+}
+// fp32 fma whose multiplicands are f16 (exactly widened): round(a*b + c) once.
+__device__ __forceinline__ float fma_f16lo(uint32_t a2, uint32_t b2, float c) {
+  float d;
+  asm("{ .reg .b16 al, ah, bl, bh; mov.b32 {al, ah}, %1; mov.b32 {bl, bh}, %2;"
+      " fma.rn.f32.f16 %0, al, bl, %3; }"
+      : "=f"(d)
+      : "r"(a2), "r"(b2), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_f16hi(uint32_t a2, uint32_t b2, float c) {
+  float d;
+  asm("{ .reg .b16 al, ah, bl, bh; mov.b32 {al, ah}, %1; mov.b32 {bl, bh}, %2;"
+      " fma.rn.f32.f16 %0, ah, bh, %3; }"
+      : "=f"(d)
+      : "r"(a2), "r"(b2), "f"(c));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// Decoders
+// ---------------------------------------------------------------------------
+// Two E4M3 bytes (low 16 bits of v) -> f16x2 via the hardware converter.  Exact
+// for every byte except 0x7F/0xFF, which the hardware maps to NaN and the
+// reference maps to +-480; callers detect a non-finite row and recompute it
+// with decode_fp8_exact().
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
+  uint32_t h;
+  asm("{ .reg .b16 t; cvt.u16.u32 t, %1; cvt.rn.f16x2.e4m3x2 %0, t; }" : "=r"(h) : "r"(v));
+  return h;
+}
+__device__ __forceinline__ float2 h2_to_f2(uint32_t h) {
+  __half2 v = *reinterpret_cast<__half2*>(&h);
+  return __half22float2(v);
+}
+// decode_fp8_e4m3(byte, 1.0) of the reference, exactly (0x7F -> 480, 0x80 -> +0).
+__host__ __device__ __forceinline__ float decode_fp8_exact(uint32_t b) {
+  // e at bits 23..26, m at 20..22 of a float whose value is decode * 2^-120;
+  // the multiply by 2^120 is exact (this library is built without FTZ).
+  if ((b & 0x7Fu) == 0) return 0.0f;
+  const float v = u2f((b & 0x7Fu) << 20) * 1.329227995784916e36f;
+  return (b & 0x80u) ? -v : v;
+}
+// UE8M0 scale byte -> float: 0 -> 0, else 2^(b-127) (b=255 -> +inf).
+__host__ __device__ __forceinline__ float decode_ue8m0(uint32_t b) {
+  if (b == 0) return 0.0f;
+  if (b == 255) return u2f(0x7f800000u);
+  if (b == 1) return u2f(0x00800000u);  // 2^-126
+  return u2f(b << 23);
+}
+
+// One packed FP4 byte (low nibble = even column) -> f16x2 of the reference's
+// FP4_E2M1_BASE_LUT values (nibble 1 = 0.125, not OCP's 0.5).  The hardware
+// e2m1 converter gives OCP values; the only difference is +-0.5 -> +-0.125,
+// i.e. f16 0x3800 -> 0x3000: bit 11 is cleared whenever bit 10 is clear (the
+// only OCP magnitudes with bit 11 set are 0.5, 1.0, 1.5, and 1.0/1.5 have
+// bit 10 set).
+__device__ __forceinline__ uint32_t fp4x2_to_f16x2_ref(uint32_t byte_in_low8) {
+  uint32_t h;
+  asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(h) : "r"(byte_in_low8));
+  // clear bit 11 of each half where bit 10 is 0
+  uint32_t keep = (h << 1) | ~0x08000800u;
+  return h & keep;
+}
+
+// ---------------------------------------------------------------------------
+// FP8 activation quant-dequant (src/compute.rs:2504-2545), exact.
+//   amax = max(max|v|, 1e-4); scale = exp2(ceil(log2(amax/448))) in f32 with
+//   libm log2f; q = nearest E4M3 grid point of clamp(v/scale, +-448), ties to
+//   the lower (more negative) entry; v = q*scale.
+// ceil(log2f(q)) equals the exact ceil(log2 q) except in a narrow band just
+// above each power of two where log2f rounds to the integer itself; the band's
+// upper mantissa limit per exponent is measured once on the host from the
+// platform log2f (the same libm the reference engine calls) and passed in.
+// ---------------------------------------------------------------------------
+struct ActQuantTable {
+  // For biased exponent E of q = amax/448: ceil(log2f(q)) == E-127 iff the
+  // mantissa m satisfies m < thr[E] (m == 0 is always inside).
+  uint32_t thr[256];
+};
+
+__device__ __forceinline__ int ceil_log2f_ref(float q, const ActQuantTable* t) {
+  uint32_t u = __float_as_uint(q);
+  uint32_t E = (u >> 23) & 0xFF;
+  uint32_t m = u & 0x7FFFFF;
+  int k = int(E) - 127;
+  if (m == 0 || m < t->thr[E]) return k;
+  return k + 1;
+}
+
+// scale = 2^k as float for k in the normal range (k >= -126 always holds here:
+// amax >= 1e-4).
+__device__ __forceinline__ float exp2i(int k) {
+  if (k > 127) return __int_as_float(0x7f800000);
+  return __uint_as_float(uint32_t(k + 127) << 23);
+}
+
+// Nearest E4M3 grid value of t (|t| <= 448 or NaN) with ties to the lower
+// entry, as nearest_in_sorted_lut over the reference's sorted LUT.  Returns
+// +0.0 for results that are zero.
+__host__ __device__ __forceinline__ float e4m3_nearest_ties_lower(float t) {
+  if (t != t) return -480.0f;  // NaN: partition_point == 0 -> lut[0]
+  const bool neg = t < 0.0f;
+  const float a = fabsf(t);
+  float r;
+  if (a < 0.015625f) {  // E4M3 subnormal range: grid 2^-9
+    const float q = a * 512.0f;  // exact
+    float n = floorf(q);
+    const float f = q - n;  // exact
+    if (f > 0.5f || (f == 0.5f && neg)) n += 1.0f;
+    r = n * 0.001953125f;
+  } else {
+    const uint32_t u = f2u(a);
+    const uint32_t rem = u & 0xFFFFFu;
+    uint32_t base = u & ~0xFFFFFu;
+    if (rem > 0x80000u || (rem == 0x80000u && neg)) base += 0x100000u;
+    r = u2f(base);
+  }
+  if (r == 0.0f) return 0.0f;
+  return neg ? -r : r;
+}
+
+}  // namespace wh

@@ -1,0 +1,341 @@
+// fp8_gemv.cu -- FP8 E4M3 x UE8M0(128x128) GEMV / batched GEMV for sm_100a.
+//
+// Replaces gemv_fp8_e4m3_ue8m0_{tensorwise,rows,rows_multi}
+// (engine/zc_infer_core/src/compute.rs:6174-6577).  Every output equals the
+// reference's AVX2 row kernel fp8_ue8m0_dot_row_avx2 (src/compute.rs:5977-6018)
+// bit for bit: per 128-column group, 16 FMA chains of 8 steps (g0 lanes j over
+// columns 16c+j, g1 lanes over 16c+8+j), P_j = g0_j + g1_j,
+// acc_j = fma(P_j, scale_g, acc_j) over the groups in order, then the pairwise
+// 8-lane sum.  The batched form keeps the same per-(row,input) arithmetic, so
+// it is batch-invariant like the reference's rows_multi.
+//
+// Layout / data movement (fast path, col_group == 128):
+//   * one CTA per block of <= 32 rows (block size chosen so the grid covers
+//     the SMs once); a producer warp streams [rows x 128 B] boxes of W with TMA
+//     (SWIZZLE_128B) through an 8-stage mbarrier ring; the swizzle makes the
+//     consumers' row-per-lane reads bank-conflict free;
+//   * 4 lanes per row, each owning 4 of the 16 chains (4 bytes per 16-byte
+//     chunk), so a warp covers 8 rows; x sits in shared memory (optionally
+//     act-quantised in the prologue) and is read as broadcast float4s;
+//   * E4M3 -> f16x2 by the hardware converter, f16 -> f32, fma.rn.f32x2.
+//     0x7F/0xFF (the reference's +-480, NaN for the hardware) make the row
+//     non-finite; such rows are recomputed with the exact bit decoder.
+// Shapes the fast path does not cover (col_group != 128, cols % 16 != 0) run
+// fp8_gemv_generic_kernel, one thread per (row, input), same arithmetic.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace wh {
+
+__constant__ ActQuantTable c_aq;
+
+void set_act_quant_table(const ActQuantTable& t, cudaStream_t s) {
+  cudaMemcpyToSymbolAsync(c_aq, &t, sizeof(t), 0, cudaMemcpyHostToDevice, s);
+}
+const ActQuantTable* act_quant_table_device() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, c_aq);
+  return reinterpret_cast<const ActQuantTable*>(p);
+}
+
+// Block-wise act quant-dequant of a shared-memory vector, by one warp per
+// block of `block` values (block <= 64*8).  Exact reference semantics.
+__device__ void act_quant_smem_warp(float* v, int n, int block, int warp, int nwarps, int lane,
+                                    const ActQuantTable* tab) {
+  for (int b0 = warp * block; b0 < n; b0 += nwarps * block) {
+    int b1 = min(n, b0 + block);
+    float amax = 0.0f;
+    for (int i = b0 + lane; i < b1; i += 32) amax = fmaxf(amax, fabsf(v[i]));
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    amax = fmaxf(amax, 1.0e-4f);
+    float q = __fdiv_rn(amax, 448.0f);
+    float scale = exp2i(ceil_log2f_ref(q, tab));
+    for (int i = b0 + lane; i < b1; i += 32) {
+      float t = __fdiv_rn(v[i], scale);
+      t = t < -448.0f ? -448.0f : t;
+      t = t > 448.0f ? 448.0f : t;
+      v[i] = __fmul_rn(e4m3_nearest_ties_lower(t), scale);
+    }
+  }
+}
+
+// Standalone in-place act quant (fp8_act_quant_dequant_in_place).
+__global__ void act_quant_kernel(float* v, long long n, int block, uint32_t* status) {
+  int lane = threadIdx.x & 31;
+  long long warp = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  pdl_wait_prior();
+  for (long long b0 = warp * block; b0 < n; b0 += nw * block) {
+    long long b1 = b0 + block < n ? b0 + block : n;
+    float amax = 0.0f;
+    for (long long i = b0 + lane; i < b1; i += 32) amax = fmaxf(amax, fabsf(v[i]));
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    amax = fmaxf(amax, 1.0e-4f);
+    float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
+    for (long long i = b0 + lane; i < b1; i += 32) {
+      float t = __fdiv_rn(v[i], scale);
+      t = t < -448.0f ? -448.0f : t;
+      t = t > 448.0f ? 448.0f : t;
+      v[i] = __fmul_rn(e4m3_nearest_ties_lower(t), scale);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Exact scalar restatement of fp8_ue8m0_dot_row_avx2 for one (row, input),
+// used by the generic kernel and for the rare non-finite recompute.
+__device__ float fp8_row_dot_exact(const uint8_t* __restrict__ w, const uint8_t* __restrict__ srow,
+                                   int scale_cols, int col_group, const float* __restrict__ x) {
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  float tail = 0.0f;
+  const int chunks = col_group / 16;
+  for (int g = 0; g < scale_cols; ++g) {
+    float scale = decode_ue8m0(srow[g]);
+    const uint8_t* bytes = w + (long long)g * col_group;
+    const float* cols = x + (long long)g * col_group;
+    float g0[8], g1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g0[j] = g1[j] = 0.0f;
+    for (int c = 0; c < chunks; ++c) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        g0[j] = fmaf(decode_fp8_exact(bytes[16 * c + j]), cols[16 * c + j], g0[j]);
+        g1[j] = fmaf(decode_fp8_exact(bytes[16 * c + 8 + j]), cols[16 * c + 8 + j], g1[j]);
+      }
+    }
+    float rem = 0.0f;
+    for (int i = chunks * 16; i < col_group; ++i)
+      rem = __fadd_rn(rem, __fmul_rn(decode_fp8_exact(bytes[i]), cols[i]));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = fmaf(__fadd_rn(g0[j], g1[j]), scale, acc[j]);
+    tail = __fadd_rn(tail, __fmul_rn(rem, scale));
+  }
+  float h = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                      __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+  return __fadd_rn(h, tail);
+}
+
+__global__ void fp8_gemv_generic_kernel(Fp8GemvArgs a) {
+  pdl_wait_prior();
+  long long n = (long long)(a.row_end - a.row_start) * a.batch;
+  const int row_group = a.rows / a.scale_rows;
+  const int col_group = a.cols / a.scale_cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    int b = int(i / (a.row_end - a.row_start));
+    int r = a.row_start + int(i % (a.row_end - a.row_start));
+    const uint8_t* w = a.weight + (long long)r * a.cols;
+    const uint8_t* s = a.scale + (long long)(r / row_group) * a.scale_cols;
+    float acc = fp8_row_dot_exact(w, s, a.scale_cols, col_group, a.x + (long long)b * a.ldx);
+    if (!isfinite(acc)) flag(a.status, WH_DEV_NONFINITE);
+    a.y[(long long)b * a.ldy + (r - a.row_start)] = acc;
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+// Fast path
+// ---------------------------------------------------------------------------
+constexpr int kFp8Stages = 8;
+constexpr int kFp8StageBytes = 32 * 128;  // up to 32 rows x 128 B, 1024-aligned
+
+template <int TB>
+__global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                           Fp8GemvArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;                                         // kFp8Stages * 4 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kFp8Stages * kFp8StageBytes);
+  uint64_t* empty = full + kFp8Stages;
+  float* xs = reinterpret_cast<float*>(empty + kFp8Stages);       // TB x cols
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nconsumer = (blockDim.x >> 5) - 1;  // last warp is the producer
+  const int box_rows = a.box_rows;
+  const int row0 = a.row_start + blockIdx.x * box_rows;
+  const int ngroups = a.scale_cols;  // col_group == 128
+  const int tile = blockIdx.y;       // input tile
+  const int tb = min(TB, a.batch - tile * TB);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFp8Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], nconsumer);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == nconsumer) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      for (int g = 0; g < ngroups; ++g) {
+        const int s = g % kFp8Stages;
+        if (g >= kFp8Stages) {
+          if (!mbar_wait(&empty[s], ((g / kFp8Stages) - 1) & 1, a.status)) break;
+        }
+        mbar_arrive_expect_tx(&full[s], box_rows * 128);
+        tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait_prior();  // x may be produced by the previous kernel in the stream
+  const int nthr = nconsumer * 32;
+  for (int b = 0; b < tb; ++b) {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (long long)(tile * TB + b) * a.ldx);
+    float4* dst = reinterpret_cast<float4*>(xs + b * a.cols);
+    for (int i = threadIdx.x; i < a.cols / 4; i += nthr) dst[i] = src[i];
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+  if (a.act_quant_block > 0) {
+    for (int b = 0; b < tb; ++b)
+      act_quant_smem_warp(xs + b * a.cols, a.cols, a.act_quant_block, warp, nconsumer, lane, &c_aq);
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+  }
+
+  const int rloc = warp * 8 + (lane >> 2);  // row within the box
+  const int q = lane & 3;
+  const int row = row0 + rloc;
+  const bool active = rloc < box_rows && row < a.row_end;
+  const int row_group = a.rows / a.scale_rows;
+  const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
+
+  float acc[TB][4];
+#pragma unroll
+  for (int b = 0; b < TB; ++b)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[b][j] = 0.0f;
+
+  bool ok = true;
+  for (int g = 0; g < ngroups; ++g) {
+    const int s = g % kFp8Stages;
+    if (!mbar_wait(&full[s], (g / kFp8Stages) & 1, a.status)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* base = stages + s * kFp8StageBytes + rloc * 128 + 4 * q;
+    uint32_t wv[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      wv[c] = *reinterpret_cast<const uint32_t*>(base + 16 * (c ^ (rloc & 7)));
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    float2 wf[8][2];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      wf[c][0] = h2_to_f2(e4m3x2_to_f16x2(wv[c]));
+      wf[c][1] = h2_to_f2(e4m3x2_to_f16x2(wv[c] >> 16));
+    }
+    const float scale = decode_ue8m0(__ldg(srow + g));
+#pragma unroll
+    for (int b = 0; b < TB; ++b) {
+      if (b < tb) {
+        const float* xg = xs + b * a.cols + g * 128 + 4 * q;
+        float2 p01 = make_float2(0.0f, 0.0f), p23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float4 xv = *reinterpret_cast<const float4*>(xg + 16 * c);
+          p01 = ffma2(wf[c][0], make_float2(xv.x, xv.y), p01);
+          p23 = ffma2(wf[c][1], make_float2(xv.z, xv.w), p23);
+        }
+        // P_j = g0_j + g1_j: lanes q and q^2 hold g0 / g1 of the same j
+        float o0 = __shfl_xor_sync(0xffffffffu, p01.x, 2);
+        float o1 = __shfl_xor_sync(0xffffffffu, p01.y, 2);
+        float o2 = __shfl_xor_sync(0xffffffffu, p23.x, 2);
+        float o3 = __shfl_xor_sync(0xffffffffu, p23.y, 2);
+        float2 P01 = make_float2(__fadd_rn(p01.x, o0), __fadd_rn(p01.y, o1));
+        float2 P23 = make_float2(__fadd_rn(p23.x, o2), __fadd_rn(p23.y, o3));
+        float2 a01 = ffma2(P01, make_float2(scale, scale), make_float2(acc[b][0], acc[b][1]));
+        float2 a23 = ffma2(P23, make_float2(scale, scale), make_float2(acc[b][2], acc[b][3]));
+        acc[b][0] = a01.x;
+        acc[b][1] = a01.y;
+        acc[b][2] = a23.x;
+        acc[b][3] = a23.y;
+      }
+    }
+  }
+  if (!ok) return;
+  const int row_end_loc = a.row_end;
+#pragma unroll
+  for (int b = 0; b < TB; ++b) {
+    if (b < tb) {
+      float h = __fadd_rn(__fadd_rn(acc[b][0], acc[b][1]), __fadd_rn(acc[b][2], acc[b][3]));
+      float other = __shfl_xor_sync(0xffffffffu, h, 1);
+      if (q == 0 && active) {
+        float tot = __fadd_rn(__fadd_rn(h, other), 0.0f);
+        const int bi = tile * TB + b;
+        if (!isfinite(tot)) {
+          // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
+          const float* xb = xs + b * a.cols;
+          tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xb);
+          if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
+        }
+        a.y[(long long)bi * a.ldy + (row - a.row_start)] = tot;
+      }
+    }
+  }
+  (void)row_end_loc;
+  pdl_launch_dependents();
+}
+
+size_t fp8_gemv_smem_bytes(int tb, int cols) {
+  return 1024 + kFp8Stages * kFp8StageBytes + 2 * kFp8Stages * sizeof(uint64_t) +
+         size_t(tb) * cols * sizeof(float);
+}
+
+cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
+                            cudaStream_t stream, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (wmap == nullptr) {
+    long long n = (long long)(a.row_end - a.row_start) * a.batch;
+    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3((unsigned)std::min<long long>((n + 127) / 128, 4LL * num_sms));
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, fp8_gemv_generic_kernel, a);
+  }
+  const int nrows = a.row_end - a.row_start;
+  const int tb = a.batch < 8 ? (a.batch < 4 ? (a.batch < 2 ? 1 : 2) : 4) : 8;
+  const int nconsumer = (a.box_rows + 7) / 8;
+  cfg.blockDim = dim3(32 * (nconsumer + 1));
+  cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + tb - 1) / tb);
+  cfg.dynamicSmemBytes = fp8_gemv_smem_bytes(tb, a.cols);
+  cudaError_t e;
+#define WH_LAUNCH_TB(T)                                                                     \
+  case T:                                                                                   \
+    e = cudaFuncSetAttribute(fp8_gemv_tma_kernel<T>,                                        \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
+                             (int)cfg.dynamicSmemBytes);                                    \
+    if (e != cudaSuccess) return e;                                                         \
+    return cudaLaunchKernelEx(&cfg, fp8_gemv_tma_kernel<T>, *wmap, a);
+  switch (tb) {
+    WH_LAUNCH_TB(1)
+    WH_LAUNCH_TB(2)
+    WH_LAUNCH_TB(4)
+    WH_LAUNCH_TB(8)
+  }
+#undef WH_LAUNCH_TB
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_act_quant(float* v, long long n, int block, uint32_t* status, int num_sms,
+                             cudaStream_t stream) {
+  long long blocks = (n + block - 1) / block;
+  long long warps = std::min<long long>(blocks, 8LL * num_sms * 4);
+  unsigned grid = (unsigned)std::max<long long>(1, (warps + 3) / 4);
+  act_quant_kernel<<<grid, 128, 0, stream>>>(v, n, block, status);
+  return cudaGetLastError();
+}
+
+}  // namespace wh

@@ -1,0 +1,103 @@
+// kernels.cuh -- argument blocks and launchers of the wohper_b200 kernels
+// (internal to the library; the public surface is include/wohper_b200.h).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace wh {
+
+// ---------------- FP8 GEMV ----------------
+struct Fp8GemvArgs {
+  const uint8_t* weight;  // [rows][cols] E4M3
+  const uint8_t* scale;   // [scale_rows][scale_cols] UE8M0
+  int rows, cols, scale_rows, scale_cols;
+  int row_start, row_end;
+  const float* x;  // [batch][ldx]
+  int ldx;
+  float* y;  // [batch][ldy], y[b*ldy + r - row_start]
+  int ldy;
+  int batch;
+  int act_quant_block;  // 0 or the block size of a fused act quant of x
+  int box_rows;         // rows per CTA (fast path)
+  uint32_t* status;
+};
+
+void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);
+const ActQuantTable* act_quant_table_device();
+size_t fp8_gemv_smem_bytes(int tb, int cols);
+// wmap == nullptr selects the generic kernel.
+cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
+                            cudaStream_t stream, bool pdl);
+cudaError_t launch_act_quant(float* v, long long n, int block, uint32_t* status, int num_sms,
+                             cudaStream_t stream);
+
+// ---------------- FP4 matvec (standalone, f32 input) ----------------
+struct Fp4MatvecArgs {
+  const uint8_t* packed;  // [rows][(cols+1)/2]
+  const uint8_t* scales;  // [rows][scale_cols]
+  int rows, cols, scale_cols;
+  const float* x;
+  float* y;
+  uint32_t* status;
+};
+cudaError_t launch_fp4_matvec(const Fp4MatvecArgs& a, int num_sms, cudaStream_t stream);
+
+// ---------------- router ----------------
+struct RouterArgs {
+  const uint16_t* gate;  // [experts][hidden] bf16 bits
+  int experts, hidden;
+  const float* x;  // [tokens][hidden]
+  int tokens;
+  int topk;
+  int mode;            // 0 = RawLogits (softmax over the selected), 1 = DeepSeek sqrt-softplus
+  const float* bias;   // nullable, mode 1 selection bias
+  float route_scale;   // mode 1
+  const int32_t* hash_ids;  // nullable [tokens][topk] (tid2eid rows), mode 1
+  float* logits;       // [tokens][experts] scratch/output
+  int32_t* ids;        // [tokens][topk]
+  float* weights;      // [tokens][topk] route weights after the mode's normalisation
+  float* combine_w;    // [tokens][topk] w_k / sum(w) as the combine applies them (nullable)
+  uint32_t* counters;  // [tokens] zero-initialised, reset by the kernel
+  uint32_t* status;
+};
+cudaError_t launch_router(const RouterArgs& a, int num_sms, cudaStream_t stream, bool pdl);
+
+// ---------------- MoE (FP4 experts, one token per call or a few) ----------------
+// Tensor maps for every expert's w1/w3 (box [32 rows][128 B]) and w2 (box
+// [16 rows][128 B]) live in device memory (built once per weight set).
+struct Fp4ExpertDev {
+  const uint8_t* w1_scale;  // [inter][hidden/32]
+  const uint8_t* w3_scale;
+  const uint8_t* w2_scale;  // [hidden][inter/32]
+  const uint8_t* w1;        // packed (used by the exact fallback)
+  const uint8_t* w3;
+  const uint8_t* w2;
+};
+struct MoeArgs {
+  const CUtensorMap* maps;     // [num_experts + has_shared][3] (w1, w3, w2)
+  const Fp4ExpertDev* experts; // [num_experts + has_shared]
+  int num_experts;             // routed experts
+  int has_shared;              // slot num_experts is the shared expert
+  int hidden, inter;
+  const float* x;              // [tokens][hidden]
+  int tokens;
+  int topk;
+  const int32_t* ids;          // [tokens][topk]
+  const float* combine_w;      // [tokens][topk]
+  float* h;                    // scratch [tokens][slots][inter]
+  float* y;                    // [tokens][hidden]
+  float* expert_out;           // nullable [tokens][slots][hidden] (per-expert outputs)
+  int combine;                 // 1: routed combine + shared; 0: write expert_out only
+  uint32_t* status;
+};
+cudaError_t launch_moe_up(const MoeArgs& a, int num_sms, cudaStream_t stream, bool pdl);
+cudaError_t launch_moe_down(const MoeArgs& a, int num_sms, cudaStream_t stream, bool pdl);
+size_t moe_up_smem_bytes(int hidden);
+size_t moe_down_smem_bytes(int inter, int slots);
+
+}  // namespace wh

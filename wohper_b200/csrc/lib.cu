@@ -1,0 +1,5 @@
+// lib.cu -- single translation unit of libwohper_b200.so (keeps the one
+// __constant__ act-quant table and every kernel in one module, no -rdc).
+#include "fp8_gemv.cu"
+#include "moe.cu"
+#include "capi.cu"
