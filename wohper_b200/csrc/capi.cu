@@ -164,11 +164,14 @@ wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) 
   for (int i = 0; i < n; ++i) {
     const wh_fp4_expert& e = list[i];
     wh_status st;
-    if ((st = make_u8_map(&maps[i * 3 + 0], e.w1.packed_weight, e.w1.rows, e.w1.cols / 2, 64)))
+    if ((st = make_u8_map(&maps[i * 3 + 0], e.w1.packed_weight, e.w1.rows, e.w1.cols / 2,
+                          kMoeUpRows)))
       return st;
-    if ((st = make_u8_map(&maps[i * 3 + 1], e.w3.packed_weight, e.w3.rows, e.w3.cols / 2, 64)))
+    if ((st = make_u8_map(&maps[i * 3 + 1], e.w3.packed_weight, e.w3.rows, e.w3.cols / 2,
+                          kMoeUpRows)))
       return st;
-    if ((st = make_u8_map(&maps[i * 3 + 2], e.w2.packed_weight, e.w2.rows, e.w2.cols / 2, 16)))
+    if ((st = make_u8_map(&maps[i * 3 + 2], e.w2.packed_weight, e.w2.rows, e.w2.cols / 2,
+                          kMoeDownRows)))
       return st;
     ex[i] = Fp4ExpertDev{e.w1.ue8m0_scales, e.w3.ue8m0_scales, e.w2.ue8m0_scales,
                          e.w1.packed_weight, e.w3.packed_weight, e.w2.packed_weight};
@@ -198,6 +201,8 @@ struct wh_ctx {
   uint32_t* status = nullptr;    // device word: WH_DEV_* bits
   uint32_t* counters = nullptr;  // device, router last-CTA counters (zero at rest)
   int counters_len = 0;
+  uint32_t* blk_counters = nullptr;  // device, moe_up act-quant block counters (zero at rest)
+  int blk_counters_len = 0;
   void* work = nullptr;  // generic-path workspace
   size_t work_bytes = 0;
   std::map<std::tuple<const void*, int, int, int>, CUtensorMap> fp8_maps;
@@ -229,6 +234,16 @@ struct wh_ctx {
     work_bytes = bytes;
     return WH_OK;
   }
+  wh_status ensure_blk_counters(int n) {
+    if (n <= blk_counters_len) return WH_OK;
+    if (blk_counters) cudaFree(blk_counters);
+    blk_counters = nullptr;
+    blk_counters_len = 0;
+    WH_CUDA(cudaMalloc(&blk_counters, sizeof(uint32_t) * n));
+    WH_CUDA(cudaMemset(blk_counters, 0, sizeof(uint32_t) * n));
+    blk_counters_len = n;
+    return WH_OK;
+  }
   wh_status ensure_counters(int n) {
     if (n <= counters_len) return WH_OK;
     if (counters) cudaFree(counters);
@@ -245,7 +260,8 @@ struct wh_moe_plan {
   wh_ctx* ctx = nullptr;
   wh_moe_desc d{};
   DevExpertSet set;  // routed experts, then the shared expert
-  uint32_t* counters = nullptr;
+  uint32_t* counters = nullptr;      // router: [max_tokens]
+  uint32_t* blk_counters = nullptr;  // moe_up: [max_tokens][slots][inter/64]
 };
 
 extern "C" {
@@ -290,6 +306,7 @@ void wh_ctx_destroy(wh_ctx* c) {
   for (auto e : c->ev) cudaEventDestroy(e);
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
+  if (c->blk_counters) cudaFree(c->blk_counters);
   if (c->work) cudaFree(c->work);
   delete c;
 }
@@ -466,19 +483,24 @@ wh_status wh_fp4_expert_forward(wh_ctx* c, const wh_fp4_expert* e, const float* 
       if ((st = build_expert_set(e, 1, &set)) != WH_OK) return st;
       it = c->experts.emplace(key, set).first;
     }
-    // scratch layout: xq f16[hidden] | xq_mult f32[hidden/64] | hq f16[inter] | hq_mult f32[inter/64]
-    const size_t need = align256(hidden * 2) + align256(hidden / 16) + align256(inter * 2) +
-                        align256(inter / 16);
+    // scratch layout: xq f16[hidden] | xq_mult f32[hidden/64] | h f32[inter] |
+    //                 hq f16[inter] | hq_mult f32[inter/64]
+    const size_t o_xqm = align256(hidden * 2);
+    const size_t o_h = o_xqm + align256(hidden / 16);
+    const size_t o_hq = o_h + align256(inter * 4);
+    const size_t o_hqm = o_hq + align256(inter * 2);
+    const size_t need = o_hqm + align256(inter / 16);
     uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
     if (need > scratch_len * sizeof(float) || !aligned(scratch, 256)) {
       if ((st = c->ensure_work(need)) != WH_OK) return st;
       base = static_cast<uint8_t*>(c->work);
     }
+    if ((st = c->ensure_blk_counters((int)(inter / 64))) != WH_OK) return st;
     __half* xq = reinterpret_cast<__half*>(base);
-    float* xqm = reinterpret_cast<float*>(base + align256(hidden * 2));
-    __half* hq = reinterpret_cast<__half*>(base + align256(hidden * 2) + align256(hidden / 16));
-    float* hqm = reinterpret_cast<float*>(base + align256(hidden * 2) + align256(hidden / 16) +
-                                          align256(inter * 2));
+    float* xqm = reinterpret_cast<float*>(base + o_xqm);
+    float* hbuf = reinterpret_cast<float*>(base + o_h);
+    __half* hq = reinterpret_cast<__half*>(base + o_hq);
+    float* hqm = reinterpret_cast<float*>(base + o_hqm);
     MoeArgs a{};
     a.maps = it->second.maps;
     a.experts = it->second.experts;
@@ -489,6 +511,8 @@ wh_status wh_fp4_expert_forward(wh_ctx* c, const wh_fp4_expert* e, const float* 
     a.x = input;
     a.tokens = 1;
     a.topk = 0;
+    a.h = hbuf;
+    a.blk_counters = c->blk_counters;
     a.y = output;
     a.expert_out = output;
     a.combine = 0;
@@ -608,8 +632,11 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
     return st;
   }
   p->d.shared = d->shared ? reinterpret_cast<const wh_fp4_expert*>(1) : nullptr;  // flag only
+  const size_t nblk = (size_t)d->max_tokens * (d->topk + 1) * (d->inter / 64);
   cudaError_t e = cudaMalloc(&p->counters, sizeof(uint32_t) * d->max_tokens);
   if (e == cudaSuccess) e = cudaMemset(p->counters, 0, sizeof(uint32_t) * d->max_tokens);
+  if (e == cudaSuccess) e = cudaMalloc(&p->blk_counters, sizeof(uint32_t) * nblk);
+  if (e == cudaSuccess) e = cudaMemset(p->blk_counters, 0, sizeof(uint32_t) * nblk);
   if (e != cudaSuccess) {
     free_expert_set(p->set);
     delete p;
@@ -623,6 +650,7 @@ void wh_moe_plan_destroy(wh_moe_plan* p) {
   if (!p) return;
   free_expert_set(p->set);
   if (p->counters) cudaFree(p->counters);
+  if (p->blk_counters) cudaFree(p->blk_counters);
   delete p;
 }
 
@@ -634,6 +662,7 @@ struct MoeScratch {
   float* weights;
   __half* xq;
   float* xq_mult;
+  float* h;
   __half* hq;
   float* hq_mult;
   size_t bytes;
@@ -654,6 +683,7 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
   s.weights = reinterpret_cast<float*>(take(sizeof(float) * T * d.topk));
   s.xq = reinterpret_cast<__half*>(take(2 * (size_t)T * d.hidden));
   s.xq_mult = reinterpret_cast<float*>(take(sizeof(float) * T * (d.hidden / 64)));
+  s.h = reinterpret_cast<float*>(take(4 * (size_t)T * S * d.inter));
   s.hq = reinterpret_cast<__half*>(take(2 * (size_t)T * S * d.inter));
   s.hq_mult = reinterpret_cast<float*>(take(sizeof(float) * T * S * (d.inter / 64)));
   s.bytes = off;
@@ -712,7 +742,8 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   a.topk = d.topk;
   a.ids = r.ids;
   a.combine_w = s.combine_w;
-  a.h = nullptr;
+  a.h = s.h;
+  a.blk_counters = p->blk_counters;
   a.y = y;
   a.expert_out = nullptr;
   a.combine = 1;
@@ -722,6 +753,7 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   WH_CUDA(launch_moe_down_ex(a, s.hq, s.hq_mult, stream, c->pdl()));
   return c->prof_mark(stream);
 }
+
 
 void wh_debug_act_quant_table(uint32_t out[256]) {
   const ActQuantTable& t = act_quant_table_host();

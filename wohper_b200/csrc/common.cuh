@@ -57,6 +57,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Round a dynamic shared-memory pointer up to a 1024-byte boundary of the
+// SHARED address space (what TMA's 128-byte swizzle requires).  The extern
+// array is declared with 16-byte alignment only, so the compiler cannot fold
+// this computation away; a CTA's dynamic shared memory is not 1024-aligned in
+// general when several CTAs share an SM.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
@@ -98,6 +108,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
   return true;
 }
 
+// Named barrier `id` over `nthreads` threads (a multiple of 32) that also ANDs
+// a predicate across them; warps that already left the kernel are not counted.
+__device__ __forceinline__ int bar_and(int id, int nthreads, int pred) {
+  int r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.and.pred q, %2, %3, p;"
+      " selp.s32 %0, 1, 0, q; }"
+      : "=r"(r)
+      : "r"(pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // TMA / bulk copies (no .multicast::cluster anywhere in this project)
 // ---------------------------------------------------------------------------
@@ -135,15 +158,11 @@ __device__ __forceinline__ void pdl_wait_prior() {
 // ---------------------------------------------------------------------------
 // Packed / mixed-precision FP32 arithmetic (sm_100)
 // ---------------------------------------------------------------------------
-// Two independent IEEE fmas: (a.x*b.x+c.x, a.y*b.y+c.y), each rounded once.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t A = (uint64_t(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
-  uint64_t B = (uint64_t(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
-  uint64_t Cc = (uint64_t(__float_as_uint(c.y)) << 32) | __float_as_uint(c.x);
-  uint64_t D;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(Cc));
-  return make_float2(__uint_as_float(uint32_t(D)), __uint_as_float(uint32_t(D >> 32)));
-}
+// Two independent IEEE fmas: (a.x*b.x+c.x, a.y*b.y+c.y), each rounded once
+// (fma.rn.f32x2 through the toolkit's sm_100 intrinsic).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 // fp32 fma whose multiplicands are f16 (exactly widened): round(a*b + c) once.
 __device__ __forceinline__ float fma_f16lo(uint32_t a2, uint32_t b2, float c) {
   float d;

@@ -138,18 +138,26 @@ __global__ void fp8_gemv_generic_kernel(Fp8GemvArgs a) {
 // ---------------------------------------------------------------------------
 // Fast path
 // ---------------------------------------------------------------------------
-constexpr int kFp8Stages = 8;
 constexpr int kFp8StageBytes = 32 * 128;  // up to 32 rows x 128 B, 1024-aligned
+constexpr int kFp8MaxStages = 48;
+constexpr size_t kFp8SmemBudget = 200 * 1024;
+
+// stages that fit next to tb x cols floats of input
+static int fp8_stages(int tb, int cols, int ngroups) {
+  long long room = (long long)kFp8SmemBudget - 1024 - (long long)tb * cols * 4 - 2 * kFp8MaxStages * 8;
+  int ns = (int)std::max(0LL, room / kFp8StageBytes);
+  return std::min({ns, kFp8MaxStages, ngroups});
+}
 
 template <int TB>
 __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap,
-                                                           Fp8GemvArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem;                                         // kFp8Stages * 4 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kFp8Stages * kFp8StageBytes);
-  uint64_t* empty = full + kFp8Stages;
-  float* xs = reinterpret_cast<float*>(empty + kFp8Stages);       // TB x cols
+                                                           Fp8GemvArgs a, int nstages) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
+  uint64_t* empty = full + kFp8MaxStages;
+  float* xs = reinterpret_cast<float*>(empty + kFp8MaxStages);  // TB x cols
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nconsumer = (blockDim.x >> 5) - 1;  // last warp is the producer
@@ -160,7 +168,7 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   const int tb = min(TB, a.batch - tile * TB);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFp8Stages; ++s) {
+    for (int s = 0; s < nstages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], nconsumer);
     }
@@ -169,17 +177,19 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   __syncthreads();
 
   if (warp == nconsumer) {
-    // ---------------- producer ----------------
+    // ---------------- producer: weights do not depend on earlier kernels ----
     if (lane == 0) {
       prefetch_tensormap(&wmap);
-      for (int g = 0; g < ngroups; ++g) {
-        const int s = g % kFp8Stages;
-        if (g >= kFp8Stages) {
-          if (!mbar_wait(&empty[s], ((g / kFp8Stages) - 1) & 1, a.status)) break;
-        }
+      int g = 0;
+      for (; g < ngroups; ++g) {
+        const int s = g % nstages;
+        if (g >= nstages && !mbar_wait(&empty[s], ((g / nstages) - 1) & 1, a.status)) break;
         mbar_arrive_expect_tx(&full[s], box_rows * 128);
         tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
       }
+      // no copy may be in flight when this warp leaves
+      for (int i = max(0, g - nstages); i < g; ++i)
+        mbar_wait(&full[i % nstages], (i / nstages) & 1, a.status);
     }
     return;
   }
@@ -206,16 +216,15 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   const int row_group = a.rows / a.scale_rows;
   const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
 
-  float acc[TB][4];
+  float2 acc01[TB], acc23[TB];
 #pragma unroll
-  for (int b = 0; b < TB; ++b)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[b][j] = 0.0f;
+  for (int b = 0; b < TB; ++b) acc01[b] = acc23[b] = make_float2(0.0f, 0.0f);
 
   bool ok = true;
   for (int g = 0; g < ngroups; ++g) {
-    const int s = g % kFp8Stages;
-    if (!mbar_wait(&full[s], (g / kFp8Stages) & 1, a.status)) {
+    const int s = g % nstages;
+    const float scale = decode_ue8m0(__ldg(srow + g));
+    if (!mbar_wait(&full[s], (g / nstages) & 1, a.status)) {
       ok = false;
       break;
     }
@@ -224,48 +233,45 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       wv[c] = *reinterpret_cast<const uint32_t*>(base + 16 * (c ^ (rloc & 7)));
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
     float2 wf[8][2];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       wf[c][0] = h2_to_f2(e4m3x2_to_f16x2(wv[c]));
       wf[c][1] = h2_to_f2(e4m3x2_to_f16x2(wv[c] >> 16));
     }
-    const float scale = decode_ue8m0(__ldg(srow + g));
+    const float2 sc = make_float2(scale, scale);
 #pragma unroll
     for (int b = 0; b < TB; ++b) {
       if (b < tb) {
         const float* xg = xs + b * a.cols + g * 128 + 4 * q;
+        float4 xv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
         float2 p01 = make_float2(0.0f, 0.0f), p23 = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          float4 xv = *reinterpret_cast<const float4*>(xg + 16 * c);
-          p01 = ffma2(wf[c][0], make_float2(xv.x, xv.y), p01);
-          p23 = ffma2(wf[c][1], make_float2(xv.z, xv.w), p23);
+          p01 = ffma2(wf[c][0], make_float2(xv[c].x, xv[c].y), p01);
+          p23 = ffma2(wf[c][1], make_float2(xv[c].z, xv[c].w), p23);
         }
         // P_j = g0_j + g1_j: lanes q and q^2 hold g0 / g1 of the same j
-        float o0 = __shfl_xor_sync(0xffffffffu, p01.x, 2);
-        float o1 = __shfl_xor_sync(0xffffffffu, p01.y, 2);
-        float o2 = __shfl_xor_sync(0xffffffffu, p23.x, 2);
-        float o3 = __shfl_xor_sync(0xffffffffu, p23.y, 2);
-        float2 P01 = make_float2(__fadd_rn(p01.x, o0), __fadd_rn(p01.y, o1));
-        float2 P23 = make_float2(__fadd_rn(p23.x, o2), __fadd_rn(p23.y, o3));
-        float2 a01 = ffma2(P01, make_float2(scale, scale), make_float2(acc[b][0], acc[b][1]));
-        float2 a23 = ffma2(P23, make_float2(scale, scale), make_float2(acc[b][2], acc[b][3]));
-        acc[b][0] = a01.x;
-        acc[b][1] = a01.y;
-        acc[b][2] = a23.x;
-        acc[b][3] = a23.y;
+        float2 o01, o23;
+        o01.x = __shfl_xor_sync(0xffffffffu, p01.x, 2);
+        o01.y = __shfl_xor_sync(0xffffffffu, p01.y, 2);
+        o23.x = __shfl_xor_sync(0xffffffffu, p23.x, 2);
+        o23.y = __shfl_xor_sync(0xffffffffu, p23.y, 2);
+        acc01[b] = ffma2(fadd2(p01, o01), sc, acc01[b]);
+        acc23[b] = ffma2(fadd2(p23, o23), sc, acc23[b]);
       }
     }
+    // release the slot only after the loaded words have been consumed
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
   if (!ok) return;
-  const int row_end_loc = a.row_end;
 #pragma unroll
   for (int b = 0; b < TB; ++b) {
     if (b < tb) {
-      float h = __fadd_rn(__fadd_rn(acc[b][0], acc[b][1]), __fadd_rn(acc[b][2], acc[b][3]));
+      float h = __fadd_rn(__fadd_rn(acc01[b].x, acc01[b].y), __fadd_rn(acc23[b].x, acc23[b].y));
       float other = __shfl_xor_sync(0xffffffffu, h, 1);
       if (q == 0 && active) {
         float tot = __fadd_rn(__fadd_rn(h, other), 0.0f);
@@ -280,12 +286,13 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
       }
     }
   }
-  (void)row_end_loc;
   pdl_launch_dependents();
 }
 
 size_t fp8_gemv_smem_bytes(int tb, int cols) {
-  return 1024 + kFp8Stages * kFp8StageBytes + 2 * kFp8Stages * sizeof(uint64_t) +
+  const int ns = fp8_stages(tb, cols, 1 << 20);
+  if (ns < 4) return size_t(1) << 30;  // does not fit: caller takes the generic path
+  return 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
          size_t(tb) * cols * sizeof(float);
 }
 
@@ -308,9 +315,11 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
   const int nrows = a.row_end - a.row_start;
   const int tb = a.batch < 8 ? (a.batch < 4 ? (a.batch < 2 ? 1 : 2) : 4) : 8;
   const int nconsumer = (a.box_rows + 7) / 8;
+  const int ns = fp8_stages(tb, a.cols, a.scale_cols);
   cfg.blockDim = dim3(32 * (nconsumer + 1));
   cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + tb - 1) / tb);
-  cfg.dynamicSmemBytes = fp8_gemv_smem_bytes(tb, a.cols);
+  cfg.dynamicSmemBytes = 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
+                         size_t(tb) * a.cols * sizeof(float);
   cudaError_t e;
 #define WH_LAUNCH_TB(T)                                                                     \
   case T:                                                                                   \
@@ -318,7 +327,7 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
                              cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
                              (int)cfg.dynamicSmemBytes);                                    \
     if (e != cudaSuccess) return e;                                                         \
-    return cudaLaunchKernelEx(&cfg, fp8_gemv_tma_kernel<T>, *wmap, a);
+    return cudaLaunchKernelEx(&cfg, fp8_gemv_tma_kernel<T>, *wmap, a, ns);
   switch (tb) {
     WH_LAUNCH_TB(1)
     WH_LAUNCH_TB(2)

@@ -68,8 +68,12 @@ struct RouterArgs {
 cudaError_t launch_router(const RouterArgs& a, int num_sms, cudaStream_t stream, bool pdl);
 
 // ---------------- MoE (FP4 experts, one token per call or a few) ----------------
-// Tensor maps for every expert's w1/w3 (box [32 rows][128 B]) and w2 (box
-// [16 rows][128 B]) live in device memory (built once per weight set).
+// Tensor maps for every expert's w1/w3 (box [kMoeUpRows rows][128 B]) and w2
+// (box [kMoeDownRows rows][128 B]) live in device memory (built once per
+// weight set).  The host builds the maps with these box heights and the
+// kernels size their shared-memory stages and transaction counts from them.
+constexpr int kMoeUpRows = 32;
+constexpr int kMoeDownRows = 16;
 struct Fp4ExpertDev {
   const uint8_t* w1_scale;  // [inter][hidden/32]
   const uint8_t* w3_scale;
@@ -89,7 +93,8 @@ struct MoeArgs {
   int topk;
   const int32_t* ids;          // [tokens][topk]
   const float* combine_w;      // [tokens][topk]
-  float* h;                    // scratch [tokens][slots][inter]
+  float* h;                    // scratch [tokens][slots][inter] (SwiGLU hidden, f32)
+  uint32_t* blk_counters;      // zeroed [tokens][slots][inter/64] arrival counters
   float* y;                    // [tokens][hidden]
   float* expert_out;           // nullable [tokens][slots][hidden] (per-expert outputs)
   int combine;                 // 1: routed combine + shared; 0: write expert_out only

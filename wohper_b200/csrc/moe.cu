@@ -70,218 +70,288 @@ __device__ __forceinline__ int32_t total_key(float f) {
 }
 
 // ---------------------------------------------------------------------------
-// Router
+// Router: one warp per 4 expert rows.  The rows and the token's x are bulk
+// copied into shared memory first (rows padded by 32 B so the 4 rows of a warp
+// hit different banks); every lane then walks its two FMA chains over smem.
 // ---------------------------------------------------------------------------
-constexpr int kRouterWarps = 8;
-constexpr int kRouterRowsPerCta = kRouterWarps * 4;
+constexpr int kRouterRowsPerCta = 4;
 
-__global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a, __half* xq,
-                                                                  float* xq_mult) {
+struct RouterSmemPlan {
+  int row_stride;  // bytes
+  size_t bytes;
+};
+__host__ __device__ inline RouterSmemPlan router_smem_plan(int hidden) {
+  RouterSmemPlan p;
+  p.row_stride = hidden * 2 + 32;
+  p.bytes = 64 + size_t(kRouterRowsPerCta) * p.row_stride + size_t(hidden) * 4;
+  return p;
+}
+
+__device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane) {
+  const float* L = a.logits + (long long)t * a.experts;
+  constexpr int kMaxPerLane = 32;  // experts <= 1024
+  const int ne = (a.experts + 31) / 32;
+  float sc[kMaxPerLane];
+  int32_t key[kMaxPerLane];
+  for (int i = 0; i < ne; ++i) {
+    const int ex = i * 32 + lane;
+    float v = ex < a.experts ? __ldcg(L + ex) : 0.0f;
+    if (a.mode == 1 && ex < a.experts) v = sqrt_softplus_ref(v);
+    sc[i] = v;
+    float sel = v;
+    if (a.mode == 1 && a.bias != nullptr && ex < a.experts) sel = __fadd_rn(v, a.bias[ex]);
+    key[i] = ex < a.experts ? total_key(sel) : INT32_MIN;
+  }
+  int32_t ids[32];
+  float score[32];
+  int n = 0;
+  uint32_t taken = 0;  // bit i: entry i*32+lane already selected
+  auto score_of = [&](int ex) {
+    float mine = 0.0f;
+    for (int i = 0; i < ne; ++i)
+      if (i * 32 + lane == ex) mine = sc[i];
+    return __shfl_sync(0xffffffffu, mine, ex & 31);
+  };
+  if (a.mode == 1 && a.hash_ids != nullptr) {
+    // tid2eid hash routing (src/compute.rs:2190-2206)
+    for (int k = 0; k < a.topk; ++k) {
+      const int ex = a.hash_ids[(long long)t * a.topk + k];
+      if (ex >= 0 && ex < a.experts) {
+        const float got = score_of(ex);
+        ids[n] = ex;
+        score[n] = got;
+        ++n;
+      }
+    }
+  } else {
+    // stable descending sort by total_cmp, truncated: max key, lowest id on ties
+    const int kk = min(a.topk, a.experts);
+    for (int k = 0; k < kk; ++k) {
+      int32_t bk = INT32_MIN;
+      int bi = 0x7fffffff;
+      for (int i = 0; i < ne; ++i) {
+        const int ex = i * 32 + lane;
+        if (ex < a.experts && !((taken >> i) & 1u) && (key[i] > bk || (key[i] == bk && ex < bi))) {
+          bk = key[i];
+          bi = ex;
+        }
+      }
+      for (int o = 16; o; o >>= 1) {
+        const int32_t ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ok2 > bk || (ok2 == bk && oi < bi)) {
+          bk = ok2;
+          bi = oi;
+        }
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      ids[k] = bi;
+      score[k] = score_of(bi);
+      n = k + 1;
+    }
+  }
+  if (lane != 0) return;
+  float w[32];
+  for (int k = 0; k < n; ++k) w[k] = score[k];
+  if (a.mode == 1) {
+    // finalize_route_weights (src/compute.rs:2253-2268)
+    float sum = 0.0f;
+    for (int k = 0; k < n; ++k) sum = __fadd_rn(sum, w[k]);
+    if (n > 0) {
+      if (sum > 0.0f && isfinite(sum)) {
+        for (int k = 0; k < n; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], sum), a.route_scale);
+      } else {
+        const float u = __fdiv_rn(a.route_scale, (float)n);
+        for (int k = 0; k < n; ++k) w[k] = u;
+      }
+    }
+  } else if (n > 0) {
+    // normalize_route_weights_legacy (src/server/generation.rs:3152-3180)
+    bool uniform = false;
+    for (int k = 0; k < n; ++k) uniform = uniform || !isfinite(w[k]);
+    if (!uniform) {
+      float mx = -INFINITY;
+      for (int k = 0; k < n; ++k) mx = fmaxf(mx, w[k]);
+      float sum = 0.0f;
+      for (int k = 0; k < n; ++k) {
+        w[k] = glibc_like_expf(__fsub_rn(w[k], mx));
+        sum = __fadd_rn(sum, w[k]);
+      }
+      if (!isfinite(sum) || sum <= 1.1920929e-07f)
+        uniform = true;
+      else
+        for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(w[k], sum);
+    }
+    if (uniform)
+      for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(1.0f, (float)n);
+  }
+  // combine weights w_k / sum(w) (valid_route_weight_sum, src/compute.rs:2015-2030)
+  bool valid = true;
+  float sum = 0.0f;
+  for (int k = 0; k < n; ++k) {
+    if (isfinite(w[k]) && w[k] >= 0.0f)
+      sum = __fadd_rn(sum, w[k]);
+    else {
+      valid = false;
+      break;
+    }
+  }
+  if (valid && sum <= 1.1920929e-07f) valid = false;
+  for (int k = 0; k < a.topk; ++k) {
+    a.ids[(long long)t * a.topk + k] = k < n ? ids[k] : -1;
+    a.weights[(long long)t * a.topk + k] = k < n ? w[k] : 0.0f;
+    if (a.combine_w)
+      a.combine_w[(long long)t * a.topk + k] =
+          k < n ? (valid ? __fdiv_rn(w[k], sum) : __fdiv_rn(1.0f, (float)n)) : 0.0f;
+  }
+  a.counters[t] = 0;  // ready for the next call
+}
+
+// kSmem: rows and x staged in shared memory (hidden % 8 == 0, 16-byte aligned
+// rows); otherwise read straight from global memory.
+template <bool kSmem>
+__global__ void __launch_bounds__(32) router_kernel(RouterArgs a, __half* xq, float* xq_mult) {
+  extern __shared__ __align__(16) uint8_t rsmem[];
   const int t = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x;
+  const int e0 = blockIdx.x * kRouterRowsPerCta;
+  const int nrows = min(kRouterRowsPerCta, a.experts - e0);
+  const RouterSmemPlan plan = router_smem_plan(a.hidden);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(rsmem);
+  uint8_t* rows_s = rsmem + 64;
+  float* x_s = reinterpret_cast<float*>(rows_s + kRouterRowsPerCta * plan.row_stride);
+
+  if (kSmem && lane == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (kSmem && lane == 0) {
+    // gate rows do not depend on earlier kernels: start them before the PDL wait
+    mbar_arrive_expect_tx(bar, nrows * a.hidden * 2 + a.hidden * 4);
+    for (int r = 0; r < nrows; ++r)
+      bulk_load(rows_s + r * plan.row_stride, a.gate + (long long)(e0 + r) * a.hidden,
+                a.hidden * 2, bar);
+  }
   pdl_wait_prior();
   const float* x = a.x + (long long)t * a.hidden;
+  if (kSmem && lane == 0) bulk_load(x_s, x, a.hidden * 4, bar);
 
-  // (1) act-quantised copy of x for the expert kernels (one warp per 64-block)
+  // (1) act-quantised copy of x for the expert kernels: 64-blocks over the CTAs
   if (xq != nullptr) {
     const int nblk = a.hidden / 64;
-    for (int blk = blockIdx.x * kRouterWarps + warp; blk < nblk; blk += gridDim.x * kRouterWarps) {
-      float v0 = x[blk * 64 + lane], v1 = x[blk * 64 + 32 + lane];
+    for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+      const float v0 = x[blk * 64 + lane], v1 = x[blk * 64 + 32 + lane];
       float amax = fmaxf(fabsf(v0), fabsf(v1));
       for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       amax = fmaxf(amax, 1.0e-4f);
-      float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
+      const float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
       xq[(long long)t * a.hidden + blk * 64 + lane] = __float2half_rn(aq_grid(v0, scale));
       xq[(long long)t * a.hidden + blk * 64 + 32 + lane] = __float2half_rn(aq_grid(v1, scale));
       if (lane == 0) xq_mult[(long long)t * nblk + blk] = __fmul_rn(scale, 8.0f);
     }
   }
 
-  // (2) logits: 8 lanes per expert row, lane p owns chains 2p,2p+1 of acc0
-  // (p<4) or of acc1 (p>=4); dot_bf16_row_avx2 (src/compute.rs:6115-6136)
+  // (2) logits: 8 lanes per expert row; lane p owns chains 2p,2p+1 of acc0
+  // (p<4) or of acc1 (p>=4) -- dot_bf16_row_avx2 (src/compute.rs:6115-6136)
   const int p = lane & 7;
-  const int e = blockIdx.x * kRouterRowsPerCta + warp * 4 + (lane >> 3);
-  const int ee = e < a.experts ? e : a.experts - 1;  // every lane joins the shuffles
+  const int r = lane >> 3;
+  const int rr = r < nrows ? r : nrows - 1;  // every lane joins the shuffles
   const int chunks = a.hidden / 16;
-  {
-    const uint16_t* row = a.gate + (long long)ee * a.hidden;
-    const uint32_t* w32 = reinterpret_cast<const uint32_t*>(row) + p;  // 2 bf16 at 16c+2p
-    const float2* x2 = reinterpret_cast<const float2*>(x) + p;
-    float2 acc = make_float2(0.0f, 0.0f);
-#pragma unroll 8
-    for (int c = 0; c < chunks; ++c) {
-      uint32_t wv = __ldg(w32 + c * 8);
-      float2 wf = make_float2(__uint_as_float(wv << 16), __uint_as_float(wv & 0xffff0000u));
-      acc = ffma2(wf, __ldg(x2 + c * 8), acc);
-    }
-    // v_j = acc0_j + acc1_j (lanes p and p^4)
-    float o0 = __shfl_xor_sync(0xffffffffu, acc.x, 4);
-    float o1 = __shfl_xor_sync(0xffffffffu, acc.y, 4);
-    float s = __fadd_rn(__fadd_rn(acc.x, o0), __fadd_rn(acc.y, o1));  // lane p: v_{2p}+v_{2p+1}
-    float s1 = __shfl_xor_sync(0xffffffffu, s, 1);
-    float s2 = __fadd_rn(s, s1);  // p=0: (v0+v1)+(v2+v3); p=2: (v4+v5)+(v6+v7)
-    float s3 = __shfl_xor_sync(0xffffffffu, s2, 2);
-    float hs = __fadd_rn(s2, s3);
-    if (p == 0 && e < a.experts) {
-      float tail = 0.0f;
-      for (int i = chunks * 16; i < a.hidden; ++i)
-        tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(row[i]) << 16), x[i]));
-      a.logits[(long long)t * a.experts + e] = __fadd_rn(hs, tail);
-    }
+  const uint16_t* grow = a.gate + (long long)(e0 + rr) * a.hidden;
+  const uint32_t* w32;
+  const float2* x2;
+  if (kSmem) {
+    if (!mbar_wait(bar, 0, a.status)) return;
+    w32 = reinterpret_cast<const uint32_t*>(rows_s + rr * plan.row_stride) + p;
+    x2 = reinterpret_cast<const float2*>(x_s) + p;
+  } else {
+    w32 = reinterpret_cast<const uint32_t*>(grow) + p;
+    x2 = reinterpret_cast<const float2*>(x) + p;
+  }
+  float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll 16
+  for (int c = 0; c < chunks; ++c) {
+    const uint32_t wv = w32[c * 8];
+    const float2 wf = make_float2(__uint_as_float(wv << 16), __uint_as_float(wv & 0xffff0000u));
+    acc = ffma2(wf, x2[c * 8], acc);
+  }
+  // v_j = acc0_j + acc1_j (lanes p and p^4)
+  const float o0 = __shfl_xor_sync(0xffffffffu, acc.x, 4);
+  const float o1 = __shfl_xor_sync(0xffffffffu, acc.y, 4);
+  const float sv = __fadd_rn(__fadd_rn(acc.x, o0), __fadd_rn(acc.y, o1));  // v_{2p}+v_{2p+1}
+  const float s2 = __fadd_rn(sv, __shfl_xor_sync(0xffffffffu, sv, 1));
+  const float hs = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
+  if (p == 0 && r < nrows) {
+    float tail = 0.0f;
+    for (int i = chunks * 16; i < a.hidden; ++i)
+      tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(grow[i]) << 16), x[i]));
+    a.logits[(long long)t * a.experts + e0 + r] = __fadd_rn(hs, tail);
   }
 
-  // (3) last CTA of this token: top-k + weights
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    uint32_t prev = atomicAdd(&a.counters[t], 1u);
-    last = (prev == gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!last) {
-    pdl_launch_dependents();
-    return;
-  }
+  // (3) the last CTA of this token does top-k + weights
   __threadfence();
-  if (warp == 0) {
-    const float* L = a.logits + (long long)t * a.experts;
-    constexpr int kMaxPerLane = 32;  // experts <= 1024
-    float sc[kMaxPerLane];
-    int32_t key[kMaxPerLane];
-    for (int i = 0; i < kMaxPerLane; ++i) {
-      int ex = i * 32 + lane;
-      float v = ex < a.experts ? __ldcg(L + ex) : 0.0f;
-      if (a.mode == 1 && ex < a.experts) v = sqrt_softplus_ref(v);
-      sc[i] = v;
-      float sel = v;
-      if (a.mode == 1 && a.bias != nullptr && ex < a.experts) sel = __fadd_rn(v, a.bias[ex]);
-      key[i] = ex < a.experts ? total_key(sel) : INT32_MIN;
-    }
-    int32_t ids[32];
-    float score[32];
-    int n = 0;
-    uint32_t taken = 0;  // bit i: entry i*32+lane already selected
-    auto score_of = [&](int ex) {
-      float mine = 0.0f;
-      for (int i = 0; i < kMaxPerLane; ++i)
-        if (i * 32 + lane == ex) mine = sc[i];
-      return __shfl_sync(0xffffffffu, mine, ex & 31);
-    };
-    if (a.mode == 1 && a.hash_ids != nullptr) {
-      // tid2eid hash routing (src/compute.rs:2190-2206)
-      for (int k = 0; k < a.topk; ++k) {
-        const int ex = a.hash_ids[(long long)t * a.topk + k];
-        if (ex >= 0 && ex < a.experts) {
-          const float got = score_of(ex);
-          ids[n] = ex;
-          score[n] = got;
-          ++n;
-        }
-      }
-    } else {
-      // stable descending sort by total_cmp, truncated: max key, lowest id on ties
-      const int kk = min(a.topk, a.experts);
-      for (int k = 0; k < kk; ++k) {
-        int32_t bk = INT32_MIN;
-        int bi = 0x7fffffff;
-        for (int i = 0; i < kMaxPerLane; ++i) {
-          const int ex = i * 32 + lane;
-          if (ex < a.experts && !((taken >> i) & 1u) && (key[i] > bk || (key[i] == bk && ex < bi))) {
-            bk = key[i];
-            bi = ex;
-          }
-        }
-        for (int o = 16; o; o >>= 1) {
-          const int32_t ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (ok2 > bk || (ok2 == bk && oi < bi)) {
-            bk = ok2;
-            bi = oi;
-          }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        ids[k] = bi;
-        score[k] = score_of(bi);
-        n = k + 1;
-      }
-    }
-    if (lane == 0) {
-      float w[32];
-      for (int k = 0; k < n; ++k) w[k] = score[k];
-      if (a.mode == 1) {
-        float sum = 0.0f;
-        for (int k = 0; k < n; ++k) sum = __fadd_rn(sum, w[k]);
-        if (n > 0) {
-          if (sum > 0.0f && isfinite(sum)) {
-            for (int k = 0; k < n; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], sum), a.route_scale);
-          } else {
-            float u = __fdiv_rn(a.route_scale, (float)n);
-            for (int k = 0; k < n; ++k) w[k] = u;
-          }
-        }
-      } else if (n > 0) {
-        bool uniform = false;
-        for (int k = 0; k < n; ++k) uniform = uniform || !isfinite(w[k]);
-        if (!uniform) {
-          float mx = -INFINITY;
-          for (int k = 0; k < n; ++k) mx = fmaxf(mx, w[k]);
-          float sum = 0.0f;
-          for (int k = 0; k < n; ++k) {
-            w[k] = glibc_like_expf(__fsub_rn(w[k], mx));
-            sum = __fadd_rn(sum, w[k]);
-          }
-          if (!isfinite(sum) || sum <= 1.1920929e-07f)
-            uniform = true;
-          else
-            for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(w[k], sum);
-        }
-        if (uniform)
-          for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(1.0f, (float)n);
-      }
-      // combine weights w_k / sum(w) (valid_route_weight_sum, src/compute.rs:2015-2030)
-      bool valid = true;
-      float sum = 0.0f;
-      for (int k = 0; k < n; ++k) {
-        if (isfinite(w[k]) && w[k] >= 0.0f)
-          sum = __fadd_rn(sum, w[k]);
-        else {
-          valid = false;
-          break;
-        }
-      }
-      if (valid && sum <= 1.1920929e-07f) valid = false;
-      for (int k = 0; k < a.topk; ++k) {
-        a.ids[(long long)t * a.topk + k] = k < n ? ids[k] : -1;
-        a.weights[(long long)t * a.topk + k] = k < n ? w[k] : 0.0f;
-        if (a.combine_w)
-          a.combine_w[(long long)t * a.topk + k] =
-              k < n ? (valid ? __fdiv_rn(w[k], sum) : __fdiv_rn(1.0f, (float)n)) : 0.0f;
-      }
-      a.counters[t] = 0;  // ready for the next call
-    }
-  }
+  __syncwarp();
+  uint32_t prev = 0;
+  if (lane == 0) prev = atomicAdd(&a.counters[t], 1u);
+  prev = __shfl_sync(0xffffffffu, prev, 0);
   pdl_launch_dependents();
+  if (prev != gridDim.x - 1) return;
+  __threadfence();
+  router_topk_and_weights(a, t, lane);
 }
 
 // ---------------------------------------------------------------------------
 // Shared FP4 group kernel: one lane = one row; 16 packed bytes = one group of
-// 32 columns; x given as 16 f16x2 words of E4M3 grid values.
+// 32 columns; x given as 4 uint4 (16 f16x2 words) of E4M3 grid values.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void fp4_group_chains(const uint4 wb, const uint4* xq4, float gacc[8]) {
+__device__ __forceinline__ void fp4_group_chains(const uint4 wb, const uint4 (&xv)[4],
+                                                 float gacc[8]) {
   const uint32_t ws[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
   for (int j = 0; j < 8; ++j) gacc[j] = 0.0f;
   // c-th fma of every lane chain: columns 8c + j  (word c, nibble j)
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint4 xv = xq4[c];  // f16 pairs for columns 8c..8c+7
-    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    const uint32_t xs[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint32_t wh2 = fp4x2_to_f16x2_ref(ws[c] >> (8 * i));
+      const uint32_t wh2 = fp4x2_to_f16x2_ref(ws[c] >> (8 * i));
       gacc[2 * i] = fma_f16lo(wh2, xs[i], gacc[2 * i]);
       gacc[2 * i + 1] = fma_f16hi(wh2, xs[i], gacc[2 * i + 1]);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_x4(const __half* base, int G, uint4 (&xv)[4]) {
+  const uint4* p = reinterpret_cast<const uint4*>(base + G * 32);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) xv[c] = p[c];
+}
+
+// 8 groups (one 128-byte box column) of one row: wb[g] = the row's 16 bytes of
+// group g, xs = the input's f16 grid values, xm = the 64-block multipliers.
+__device__ __forceinline__ void fp4_box_accumulate(const uint4 (&wb)[8], const __half* xs,
+                                                   const float* xm, int box, uint2 sb,
+                                                   float acc[8]) {
+  const uint32_t sbw[2] = {sb.x, sb.y};
+  uint4 xv[2][4];
+  load_x4(xs, box * 8, xv[0]);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const int G = box * 8 + g;
+    if (g + 1 < 8) load_x4(xs, G + 1, xv[(g + 1) & 1]);
+    float gacc[8];
+    fp4_group_chains(wb[g], xv[g & 1], gacc);
+    const float m = xm[G >> 1];
+    const float s8 = __fmul_rn(decode_ue8m0((sbw[g >> 2] >> (8 * (g & 3))) & 0xff), 0.125f);
+    const float2 mm = make_float2(m, m), ss = make_float2(s8, s8);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const float2 r = ffma2(fmul2(make_float2(gacc[j], gacc[j + 1]), mm), ss,
+                             make_float2(acc[j], acc[j + 1]));
+      acc[j] = r.x;
+      acc[j + 1] = r.y;
     }
   }
 }
@@ -292,48 +362,60 @@ __device__ __forceinline__ float hsum8(const float a[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// moe_up: grid (inter/64, slots, tokens); 2 consumer warps (64 rows) + 1 producer
+// moe_up: grid (inter/32, slots, tokens).  Warp 0 computes w1 (gate) rows,
+// warp 1 the same w3 (up) rows, warp 2 streams both with TMA.  The SwiGLU
+// hidden of the 32 rows goes to global memory; the second CTA of each 64-row
+// act-quant block to finish quantises the block (atomic arrival counter, no
+// waiting).
 // ---------------------------------------------------------------------------
-constexpr int kUpStages = 6;
-constexpr int kUpRows = 64;
-constexpr int kUpStageBytes = kUpRows * 128;  // 8 KB
+#ifndef WH_UP_STAGES
+#define WH_UP_STAGES 5
+#endif
+constexpr int kUpStages = WH_UP_STAGES;
+constexpr int kUpRows = kMoeUpRows;
+constexpr int kUpBox = kUpRows * 128;         // 4 KB
+constexpr int kUpStageBytes = 2 * kUpBox;     // w1 box + w3 box
 
+#ifndef WH_UP_EXTRA_SMEM
+#define WH_UP_EXTRA_SMEM 0
+#endif
 size_t moe_up_smem_bytes(int hidden) {
-  return 1024 + kUpStages * kUpStageBytes + 2 * kUpStages * 8 + hidden * 2 + (hidden / 64) * 4 +
-         64;
+  return 1024 + kUpStages * kUpStageBytes + 2 * kUpStages * 8 + 16 + hidden * 2 +
+         (hidden / 64) * 4 + 256 + WH_UP_EXTRA_SMEM;
 }
 
 __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __restrict__ xq,
                                                     const float* __restrict__ xq_mult,
                                                     __half* hq, float* hq_mult) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kUpStages * kUpStageBytes);
   uint64_t* empty = full + kUpStages;
-  __half* xs = reinterpret_cast<__half*>(empty + kUpStages);
+  uint64_t* xbar = empty + kUpStages;
+  __half* xs = reinterpret_cast<__half*>(xbar + 2);
   float* xm = reinterpret_cast<float*>(xs + a.hidden);
-  float* red = xm + a.hidden / 64;  // [2] block amax exchange
+  float* gsh = xm + a.hidden / 64;  // [32] gate values handed to the up warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.z, slot = blockIdx.y;
   const int row0 = blockIdx.x * kUpRows;
   const int nslots = a.topk + a.has_shared;
   const int nbox = a.hidden / 256;  // 128 B = 256 columns per box
-  const int nstage = 2 * nbox;      // w1, w3 interleaved
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUpStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);
     }
+    mbar_init(xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
   int expert;
   if (slot >= a.topk) {
-    expert = a.num_experts;  // shared expert slot
+    expert = a.num_experts;  // shared expert slot: no dependency on the router
   } else {
     pdl_wait_prior();  // ids come from the router
     expert = a.ids[(long long)t * a.topk + slot];
@@ -346,121 +428,135 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
       const CUtensorMap* m3 = a.maps + expert * 3 + 1;
       prefetch_tensormap(m1);
       prefetch_tensormap(m3);
-      for (int i = 0; i < nstage; ++i) {
+      auto issue = [&](int i) {
         const int s = i % kUpStages;
-        if (i >= kUpStages && !mbar_wait(&empty[s], ((i / kUpStages) - 1) & 1, a.status)) break;
         mbar_arrive_expect_tx(&full[s], kUpStageBytes);
-        tma_load_2d(stages + s * kUpStageBytes, (i & 1) ? m3 : m1, &full[s], (i >> 1) * 128, row0);
+        tma_load_2d(stages + s * kUpStageBytes, m1, &full[s], i * 128, row0);
+        tma_load_2d(stages + s * kUpStageBytes + kUpBox, m3, &full[s], i * 128, row0);
+      };
+      // first pass of the ring needs no free slot
+      int i = 0;
+      for (; i < nbox && i < kUpStages; ++i) issue(i);
+      // staged input (produced by the router / act-quant kernel); the
+      // consumers wait for it before freeing any stage
+      if (slot >= a.topk) pdl_wait_prior();
+      mbar_arrive_expect_tx(xbar, a.hidden * 2 + (a.hidden / 64) * 4);
+      bulk_load(xs, xq + (long long)t * a.hidden, a.hidden * 2, xbar);
+      bulk_load(xm, xq_mult + (long long)t * (a.hidden / 64), (a.hidden / 64) * 4, xbar);
+      for (; i < nbox; ++i) {
+        if (!mbar_wait(&empty[i % kUpStages], ((i / kUpStages) - 1) & 1, a.status)) break;
+        issue(i);
       }
       // leave no copy in flight if the consumers stopped early
-      for (int i = max(0, nstage - kUpStages); i < nstage; ++i)
-        mbar_wait(&full[i % kUpStages], (i / kUpStages) & 1, a.status);
+      for (int k = max(0, i - kUpStages); k < i; ++k)
+        mbar_wait(&full[k % kUpStages], (k / kUpStages) & 1, a.status);
+      mbar_wait(xbar, 0, a.status);
     }
     return;
   }
-  if (slot >= a.topk) pdl_wait_prior();
   if (!valid_expert) {
     if (threadIdx.x == 0) flag(a.status, WH_DEV_BADARG);
     return;
   }
+  // the next kernel reads the router's ids before its own wait: only release it
+  // once the router has completed (shared-slot CTAs have not waited yet)
+  if (slot >= a.topk) pdl_wait_prior();
   pdl_launch_dependents();
+  // a failed (timed-out) wait skips the work but still reaches the named
+  // barrier below, so the partner warp is never stranded
+  bool ok = mbar_wait(xbar, 0, a.status);
 
-  // stage the token's quantised input
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(xq + (long long)t * a.hidden);
-    uint4* dst = reinterpret_cast<uint4*>(xs);
-    for (int i = threadIdx.x; i < a.hidden / 8; i += 64) dst[i] = src[i];
-    for (int i = threadIdx.x; i < a.hidden / 64; i += 64) xm[i] = xq_mult[(long long)t * (a.hidden / 64) + i];
-    asm volatile("bar.sync 1, 64;");
-  }
-
-  const int r = warp * 32 + lane;  // row within the 64-row block
-  const int row = row0 + r;
+  const int row = row0 + lane;
   const Fp4ExpertDev ed = a.experts[expert];
   const int scols = a.hidden / 32;
-  const uint8_t* s1 = ed.w1_scale + (long long)row * scols;
-  const uint8_t* s3 = ed.w3_scale + (long long)row * scols;
-  float acc1[8], acc3[8];
+  const uint8_t* srow = (warp == 0 ? ed.w1_scale : ed.w3_scale) + (long long)row * scols;
+  float acc[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc1[j] = acc3[j] = 0.0f;
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
 
-  bool ok = true;
-  for (int i = 0; i < nstage; ++i) {
+  for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kUpStages;
+    const uint2 sb = __ldg(reinterpret_cast<const uint2*>(srow + i * 8));
     if (!mbar_wait(&full[s], (i / kUpStages) & 1, a.status)) {
       ok = false;
       break;
     }
-    const int box = i >> 1;
-    const uint8_t* base = stages + s * kUpStageBytes + r * 128;
+    const uint8_t* base = stages + s * kUpStageBytes + warp * kUpBox + lane * 128;
     uint4 wb[8];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (r & 7)));
+    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (lane & 7)));
+    fp4_box_accumulate(wb, xs, xm, i, sb, acc);
+    // release the slot only after every lane has consumed its loads: an
+    // arrive issued while shared-memory loads are still outstanding lets the
+    // next TMA overwrite the slot under them (seen with several CTAs per SM)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const uint2 sb = __ldg(reinterpret_cast<const uint2*>(((i & 1) ? s3 : s1) + box * 8));
-    const uint32_t sbw[2] = {sb.x, sb.y};
-    float* acc = (i & 1) ? acc3 : acc1;
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      const int G = box * 8 + g;  // 32-column group index
-      float gacc[8];
-      fp4_group_chains(wb[g], reinterpret_cast<const uint4*>(xs + G * 32), gacc);
-      const float m = xm[G >> 1];
-      const float s8 = __fmul_rn(decode_ue8m0((sbw[g >> 2] >> (8 * (g & 3))) & 0xff), 0.125f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = fmaf(__fmul_rn(gacc[j], m), s8, acc[j]);
-    }
   }
-  if (!ok) return;
+  const float v = __fadd_rn(hsum8(acc), 0.0f);
+  if (!isfinite(v)) flag(a.status, WH_DEV_NONFINITE);
+  if (warp == 0) gsh[lane] = v;
+  const int ok_both = bar_and(1, 64, ok);
+  if (warp == 0 || !ok_both) return;
 
-  const float gate = __fadd_rn(hsum8(acc1), 0.0f);
-  const float up = __fadd_rn(hsum8(acc3), 0.0f);
-  if (!isfinite(gate) || !isfinite(up)) flag(a.status, WH_DEV_NONFINITE);
   // SwiGLU with the reference clamps (src/deepseek_v4.rs:556-596)
-  const float gated = fminf(gate, 10.0f);
-  float upped = up;
+  const float gated = fminf(gsh[lane], 10.0f);
+  float upped = v;
   upped = upped < -10.0f ? -10.0f : upped;
   upped = upped > 10.0f ? 10.0f : upped;
   const float h = __fmul_rn(silu_ref(gated), upped);
-  // act quant over this 64-row block (src/deepseek_v4.rs:595)
-  float amax = fabsf(h);
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if (lane == 0) red[warp] = amax;
-  asm volatile("bar.sync 1, 64;");
-  amax = fmaxf(fmaxf(red[0], red[1]), 1.0e-4f);
-  const float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
   const long long hb = ((long long)t * nslots + slot) * a.inter;
-  hq[hb + row] = __float2half_rn(aq_grid(h, scale));
-  if (r == 0) hq_mult[hb / 64 + row / 64] = __fmul_rn(scale, 8.0f);
-  if (a.h) a.h[hb + row] = h;
+  a.h[hb + row] = h;
+  // act quant over the 64-row block (src/deepseek_v4.rs:595): the later of the
+  // two 32-row CTAs quantises the whole block.  Every lane fences its store
+  // before lane 0 publishes the arrival.
+  __threadfence();
+  __syncwarp();
+  uint32_t prev = 0;
+  const long long blk = hb / 64 + row0 / 64;
+  if (lane == 0) prev = atomicAdd(&a.blk_counters[blk], 1u);
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev == 0) return;
+  __threadfence();
+  const int b0 = (row0 / 64) * 64;
+  const float h0 = __ldcg(a.h + hb + b0 + lane), h1 = __ldcg(a.h + hb + b0 + 32 + lane);
+  float amax = fmaxf(fabsf(h0), fabsf(h1));
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1.0e-4f);
+  const float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
+  hq[hb + b0 + lane] = __float2half_rn(aq_grid(h0, scale));
+  hq[hb + b0 + 32 + lane] = __float2half_rn(aq_grid(h1, scale));
+  if (lane == 0) {
+    hq_mult[blk] = __fmul_rn(scale, 8.0f);
+    a.blk_counters[blk] = 0;  // ready for the next call
+  }
 }
 
 // ---------------------------------------------------------------------------
 // moe_down: grid (hidden/16, tokens); 4 consumer warps (8 slots x 16 rows) + producer
 // ---------------------------------------------------------------------------
 constexpr int kDownStages = 4;
-constexpr int kDownRows = 16;
+constexpr int kDownRows = kMoeDownRows;
 constexpr int kDownSlots = 8;
 constexpr int kDownBox = kDownRows * 128;              // 2 KB
 constexpr int kDownStageBytes = kDownSlots * kDownBox;  // 16 KB
 
 size_t moe_down_smem_bytes(int inter, int slots) {
   (void)slots;
-  return 1024 + kDownStages * kDownStageBytes + 2 * kDownStages * 8 +
+  return 1024 + kDownStages * kDownStageBytes + 2 * kDownStages * 8 + 16 +
          kDownSlots * (inter * 2 + 16) + kDownSlots * (inter / 64) * 4 +
          kDownSlots * kDownRows * 4 + 64;
 }
 
 __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* __restrict__ hq,
                                                        const float* __restrict__ hq_mult) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kDownStages * kDownStageBytes);
   uint64_t* empty = full + kDownStages;
+  uint64_t* xbar = empty + kDownStages;
   const int hstride = a.inter * 2 + 16;  // bytes per slot (padded: slots of a warp hit other banks)
-  uint8_t* hs = reinterpret_cast<uint8_t*>(empty + kDownStages);
+  uint8_t* hs = reinterpret_cast<uint8_t*>(xbar + 2);
   float* hm = reinterpret_cast<float*>(hs + kDownSlots * hstride);
   float* ys = hm + kDownSlots * (a.inter / 64);
   __shared__ int slot_expert[kDownSlots];
@@ -485,6 +581,7 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
     }
+    mbar_init(xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -512,15 +609,16 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
 
   pdl_wait_prior();  // hq from moe_up
   pdl_launch_dependents();
-  // stage hq of every slot
-  for (int k = 0; k < nslots; ++k) {
-    const uint4* src = reinterpret_cast<const uint4*>(hq + ((long long)t * nslots + k) * a.inter);
-    uint4* dst = reinterpret_cast<uint4*>(hs + k * hstride);
-    for (int i = threadIdx.x; i < a.inter / 8; i += 128) dst[i] = src[i];
-    for (int i = threadIdx.x; i < a.inter / 64; i += 128)
-      hm[k * (a.inter / 64) + i] = hq_mult[((long long)t * nslots + k) * (a.inter / 64) + i];
+  // stage hq of every slot (bulk copies, one barrier)
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4));
+    for (int k = 0; k < nslots; ++k) {
+      bulk_load(hs + k * hstride, hq + ((long long)t * nslots + k) * a.inter, a.inter * 2, xbar);
+      bulk_load(hm + k * (a.inter / 64), hq_mult + ((long long)t * nslots + k) * (a.inter / 64),
+                (a.inter / 64) * 4, xbar);
+    }
   }
-  asm volatile("bar.sync 1, 128;");
+  bool ok = mbar_wait(xbar, 0, a.status);
 
   const int slot = warp * 2 + (lane >> 4);
   const int r = lane & 15;
@@ -534,9 +632,10 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  bool ok = true;
-  for (int i = 0; i < nbox; ++i) {
+  for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kDownStages;
+    uint2 sb = make_uint2(0, 0);
+    if (active) sb = __ldg(reinterpret_cast<const uint2*>(srow + i * 8));
     if (!mbar_wait(&full[s], (i / kDownStages) & 1, a.status)) {
       ok = false;
       break;
@@ -547,33 +646,19 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
 #pragma unroll
       for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (r & 7)));
     }
-    __syncwarp();
+    if (active) fp4_box_accumulate(wb, hslot, hmul, i, sb, acc);
+    __syncwarp();  // slot released after its data has been consumed
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (active) {
-      const uint2 sb = __ldg(reinterpret_cast<const uint2*>(srow + i * 8));
-      const uint32_t sbw[2] = {sb.x, sb.y};
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        const int G = i * 8 + g;
-        float gacc[8];
-        fp4_group_chains(wb[g], reinterpret_cast<const uint4*>(hslot + G * 32), gacc);
-        const float m = hmul[G >> 1];
-        const float s8 = __fmul_rn(decode_ue8m0((sbw[g >> 2] >> (8 * (g & 3))) & 0xff), 0.125f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = fmaf(__fmul_rn(gacc[j], m), s8, acc[j]);
-      }
-    }
   }
-  if (!ok) return;
-  if (active) {
+  if (ok && active) {
     const float yv = __fadd_rn(hsum8(acc), 0.0f);
     if (!isfinite(yv)) flag(a.status, WH_DEV_NONFINITE);
     ys[slot * kDownRows + r] = yv;
     if (a.expert_out)
       a.expert_out[((long long)t * nslots + slot) * a.hidden + row] = yv;
   }
-  asm volatile("bar.sync 1, 128;");
-  if (a.combine && threadIdx.x < kDownRows) {
+  const int ok_all = bar_and(1, 128, ok);
+  if (ok_all && a.combine && threadIdx.x < kDownRows) {
     const int rr = threadIdx.x;
     const float* cw = a.combine_w + (long long)t * a.topk;
     float routed = 0.0f;
@@ -698,8 +783,19 @@ cudaError_t launch_router_ex(const RouterArgs& a, __half* xq, float* xq_mult, cu
                              bool pdl) {
   cudaLaunchAttribute attr[1];
   dim3 grid((a.experts + kRouterRowsPerCta - 1) / kRouterRowsPerCta, a.tokens);
-  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kRouterWarps * 32), 0, s, attr, pdl);
-  return cudaLaunchKernelEx(&cfg, router_kernel, a, xq, xq_mult);
+  const bool smem_ok = a.hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(a.gate) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.x) % 16) == 0 &&
+                       router_smem_plan(a.hidden).bytes <= 200 * 1024;
+  if (smem_ok) {
+    const size_t smem = router_smem_plan(a.hidden).bytes;
+    cudaError_t e = cudaFuncSetAttribute(router_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(32), smem, s, attr, pdl);
+    return cudaLaunchKernelEx(&cfg, router_kernel<true>, a, xq, xq_mult);
+  }
+  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(32), 64, s, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, router_kernel<false>, a, xq, xq_mult);
 }
 
 cudaError_t launch_moe_up_ex(const MoeArgs& a, const __half* xq, const float* xq_mult, __half* hq,
