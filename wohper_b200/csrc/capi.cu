@@ -146,7 +146,7 @@ wh_status validate_fp4(const wh_fp4_matvec_spec& s, size_t input_len, size_t out
 bool expert_fast_ok(const wh_fp4_expert& e, size_t hidden, size_t inter) {
   auto ok = [](const wh_fp4_matvec_spec& s) {
     return s.cols % 32 == 0 && s.scale_cols == s.cols / 32 && aligned(s.packed_weight, 16) &&
-           aligned(s.ue8m0_scales, 8);
+           aligned(s.ue8m0_scales, 16);
   };
   return ok(e.w1) && ok(e.w3) && ok(e.w2) && hidden % 256 == 0 && inter % 256 == 0 &&
          hidden % 16 == 0 && hidden <= 16384 && inter <= 16384;

@@ -205,13 +205,10 @@ __host__ __device__ __forceinline__ float decode_fp8_exact(uint32_t b) {
   const float v = u2f((b & 0x7Fu) << 20) * 1.329227995784916e36f;
   return (b & 0x80u) ? -v : v;
 }
-// UE8M0 scale byte -> float: 0 -> 0, else 2^(b-127) (b=255 -> +inf).
-__host__ __device__ __forceinline__ float decode_ue8m0(uint32_t b) {
-  if (b == 0) return 0.0f;
-  if (b == 255) return u2f(0x7f800000u);
-  if (b == 1) return u2f(0x00800000u);  // 2^-126
-  return u2f(b << 23);
-}
+// UE8M0 scale byte -> float: 0 -> 0, else 2^(b-127) (b=255 -> +inf), exactly
+// decode_ue8m0_scale of the reference: the byte placed in the f32 exponent
+// field gives all three cases (0 -> +0.0, 1 -> 2^-126, 255 -> +inf).
+__host__ __device__ __forceinline__ float decode_ue8m0(uint32_t b) { return u2f((b & 0xffu) << 23); }
 
 // One packed FP4 byte (low nibble = even column) -> f16x2 of the reference's
 // FP4_E2M1_BASE_LUT values (nibble 1 = 0.125, not OCP's 0.5).  The hardware

@@ -22,12 +22,30 @@
 //     non-finite; such rows are recomputed with the exact bit decoder.
 // Shapes the fast path does not cover (col_group != 128, cols % 16 != 0) run
 // fp8_gemv_generic_kernel, one thread per (row, input), same arithmetic.
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace wh {
 
 __constant__ ActQuantTable c_aq;
+
+cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_pair(dev, kernel);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
 
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s) {
   cudaMemcpyToSymbolAsync(c_aq, &t, sizeof(t), 0, cudaMemcpyHostToDevice, s);
@@ -144,7 +162,8 @@ constexpr size_t kFp8SmemBudget = 200 * 1024;
 
 // stages that fit next to tb x cols floats of input
 static int fp8_stages(int tb, int cols, int ngroups) {
-  long long room = (long long)kFp8SmemBudget - 1024 - (long long)tb * cols * 4 - 2 * kFp8MaxStages * 8;
+  long long room = (long long)kFp8SmemBudget - 1024 - (long long)tb * cols * 4 -
+                   2 * kFp8MaxStages * 8 - (32LL * (cols / 128) + 16);
   int ns = (int)std::max(0LL, room / kFp8StageBytes);
   return std::min({ns, kFp8MaxStages, ngroups});
 }
@@ -158,6 +177,7 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
   uint64_t* empty = full + kFp8MaxStages;
   float* xs = reinterpret_cast<float*>(empty + kFp8MaxStages);  // TB x cols
+  uint8_t* scale_s = reinterpret_cast<uint8_t*>(xs + TB * a.cols);  // CTA's scale rows
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nconsumer = (blockDim.x >> 5) - 1;  // last warp is the producer
@@ -180,12 +200,16 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
     // ---------------- producer: weights do not depend on earlier kernels ----
     if (lane == 0) {
       prefetch_tensormap(&wmap);
-      int g = 0;
+      int g = 0, s = 0;
+      uint32_t phase = 0;  // phase of the empty barrier the next refill waits for
       for (; g < ngroups; ++g) {
-        const int s = g % nstages;
-        if (g >= nstages && !mbar_wait(&empty[s], ((g / nstages) - 1) & 1, a.status)) break;
+        if (g >= nstages && !mbar_wait(&empty[s], phase, a.status)) break;
         mbar_arrive_expect_tx(&full[s], box_rows * 128);
         tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
+        if (++s == nstages) {
+          s = 0;
+          if (g >= nstages) phase ^= 1u;
+        }
       }
       // no copy may be in flight when this warp leaves
       for (int i = max(0, g - nstages); i < g; ++i)
@@ -202,6 +226,14 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
     float4* dst = reinterpret_cast<float4*>(xs + b * a.cols);
     for (int i = threadIdx.x; i < a.cols / 4; i += nthr) dst[i] = src[i];
   }
+  // the UE8M0 scale rows this CTA's rows use (<= 32), so the group loop never
+  // waits on a global load
+  const int row_group = a.rows / a.scale_rows;
+  const int last_row = min(row0 + box_rows, a.row_end) - 1;
+  const int srow0 = row0 / row_group;
+  const int nsrows = last_row / row_group - srow0 + 1;
+  for (int i = threadIdx.x; i < nsrows * a.scale_cols; i += nthr)
+    scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
   asm volatile("bar.sync 1, %0;" ::"r"(nthr));
   if (a.act_quant_block > 0) {
     for (int b = 0; b < tb; ++b)
@@ -213,18 +245,19 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   const int q = lane & 3;
   const int row = row0 + rloc;
   const bool active = rloc < box_rows && row < a.row_end;
-  const int row_group = a.rows / a.scale_rows;
   const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
+  const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
 
   float2 acc01[TB], acc23[TB];
 #pragma unroll
   for (int b = 0; b < TB; ++b) acc01[b] = acc23[b] = make_float2(0.0f, 0.0f);
 
   bool ok = true;
+  int s = 0;
+  uint32_t phase = 0;
   for (int g = 0; g < ngroups; ++g) {
-    const int s = g % nstages;
-    const float scale = decode_ue8m0(__ldg(srow + g));
-    if (!mbar_wait(&full[s], (g / nstages) & 1, a.status)) {
+    const float scale = decode_ue8m0(srow_s[g]);
+    if (!mbar_wait(&full[s], phase, a.status)) {
       ok = false;
       break;
     }
@@ -266,6 +299,10 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
     // release the slot only after the loaded words have been consumed
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == nstages) {
+      s = 0;
+      phase ^= 1u;
+    }
   }
   if (!ok) return;
 #pragma unroll
@@ -289,11 +326,13 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   pdl_launch_dependents();
 }
 
+static size_t fp8_scale_smem(int cols) { return size_t(32) * (cols / 128) + 16; }
+
 size_t fp8_gemv_smem_bytes(int tb, int cols) {
   const int ns = fp8_stages(tb, cols, 1 << 20);
   if (ns < 4) return size_t(1) << 30;  // does not fit: caller takes the generic path
   return 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
-         size_t(tb) * cols * sizeof(float);
+         size_t(tb) * cols * sizeof(float) + fp8_scale_smem(cols);
 }
 
 cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
@@ -319,13 +358,11 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
   cfg.blockDim = dim3(32 * (nconsumer + 1));
   cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + tb - 1) / tb);
   cfg.dynamicSmemBytes = 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
-                         size_t(tb) * a.cols * sizeof(float);
+                         size_t(tb) * a.cols * sizeof(float) + fp8_scale_smem(a.cols);
   cudaError_t e;
 #define WH_LAUNCH_TB(T)                                                                     \
   case T:                                                                                   \
-    e = cudaFuncSetAttribute(fp8_gemv_tma_kernel<T>,                                        \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
-                             (int)cfg.dynamicSmemBytes);                                    \
+    e = ensure_smem(fp8_gemv_tma_kernel<T>, cfg.dynamicSmemBytes);                          \
     if (e != cudaSuccess) return e;                                                         \
     return cudaLaunchKernelEx(&cfg, fp8_gemv_tma_kernel<T>, *wmap, a, ns);
   switch (tb) {

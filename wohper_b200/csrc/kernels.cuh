@@ -11,6 +11,14 @@
 
 namespace wh {
 
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel); the
+// attribute call is not repeated on the launch path.
+cudaError_t ensure_smem_attr(const void* kernel, size_t bytes);
+template <class K>
+inline cudaError_t ensure_smem(K* kernel, size_t bytes) {
+  return ensure_smem_attr(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // ---------------- FP8 GEMV ----------------
 struct Fp8GemvArgs {
   const uint8_t* weight;  // [rows][cols] E4M3

@@ -87,13 +87,17 @@ __host__ __device__ inline RouterSmemPlan router_smem_plan(int hidden) {
   return p;
 }
 
+// Top-k selection and route weights for token t by one warp, all in
+// registers.  PER = logits held per lane (experts <= 32*PER).  Lane k ends up
+// owning route k; ordered sums (the reference accumulates left to right) are
+// gathered to lane 0 with shuffles.
+template <int PER>
 __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane) {
   const float* L = a.logits + (long long)t * a.experts;
-  constexpr int kMaxPerLane = 32;  // experts <= 1024
-  const int ne = (a.experts + 31) / 32;
-  float sc[kMaxPerLane];
-  int32_t key[kMaxPerLane];
-  for (int i = 0; i < ne; ++i) {
+  float sc[PER];
+  int32_t key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
     const int ex = i * 32 + lane;
     float v = ex < a.experts ? __ldcg(L + ex) : 0.0f;
     if (a.mode == 1 && ex < a.experts) v = sqrt_softplus_ref(v);
@@ -102,40 +106,45 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
     if (a.mode == 1 && a.bias != nullptr && ex < a.experts) sel = __fadd_rn(v, a.bias[ex]);
     key[i] = ex < a.experts ? total_key(sel) : INT32_MIN;
   }
-  int32_t ids[32];
-  float score[32];
-  int n = 0;
-  uint32_t taken = 0;  // bit i: entry i*32+lane already selected
-  auto score_of = [&](int ex) {
+  auto score_of = [&](int ex) {  // warp-uniform ex
     float mine = 0.0f;
-    for (int i = 0; i < ne; ++i)
-      if (i * 32 + lane == ex) mine = sc[i];
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (i == (ex >> 5)) mine = sc[i];
     return __shfl_sync(0xffffffffu, mine, ex & 31);
   };
+  int my_id = -1;
+  float my_score = 0.0f;
+  int n = 0;
   if (a.mode == 1 && a.hash_ids != nullptr) {
-    // tid2eid hash routing (src/compute.rs:2190-2206)
+    // tid2eid hash routing (src/compute.rs:2190-2206): keep valid ids in order
     for (int k = 0; k < a.topk; ++k) {
       const int ex = a.hash_ids[(long long)t * a.topk + k];
       if (ex >= 0 && ex < a.experts) {
         const float got = score_of(ex);
-        ids[n] = ex;
-        score[n] = got;
+        if (lane == n) {
+          my_id = ex;
+          my_score = got;
+        }
         ++n;
       }
     }
   } else {
     // stable descending sort by total_cmp, truncated: max key, lowest id on ties
+    uint32_t taken = 0;
     const int kk = min(a.topk, a.experts);
     for (int k = 0; k < kk; ++k) {
       int32_t bk = INT32_MIN;
       int bi = 0x7fffffff;
-      for (int i = 0; i < ne; ++i) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
         const int ex = i * 32 + lane;
         if (ex < a.experts && !((taken >> i) & 1u) && (key[i] > bk || (key[i] == bk && ex < bi))) {
           bk = key[i];
           bi = ex;
         }
       }
+#pragma unroll
       for (int o = 16; o; o >>= 1) {
         const int32_t ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
@@ -145,66 +154,59 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
         }
       }
       if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      ids[k] = bi;
-      score[k] = score_of(bi);
+      const float got = score_of(bi);
+      if (lane == k) {
+        my_id = bi;
+        my_score = got;
+      }
       n = k + 1;
     }
   }
-  if (lane != 0) return;
-  float w[32];
-  for (int k = 0; k < n; ++k) w[k] = score[k];
+  const bool mine = lane < n;
+  // ordered left-to-right sum of v over lanes 0..n-1 (reference summation order)
+  auto ordered_sum = [&](float v) {
+    float acc = 0.0f;
+    for (int k = 0; k < n; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, k));
+    return acc;  // uniform
+  };
+  float w = my_score;
   if (a.mode == 1) {
     // finalize_route_weights (src/compute.rs:2253-2268)
-    float sum = 0.0f;
-    for (int k = 0; k < n; ++k) sum = __fadd_rn(sum, w[k]);
+    const float sum = ordered_sum(mine ? w : 0.0f);
     if (n > 0) {
-      if (sum > 0.0f && isfinite(sum)) {
-        for (int k = 0; k < n; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], sum), a.route_scale);
-      } else {
-        const float u = __fdiv_rn(a.route_scale, (float)n);
-        for (int k = 0; k < n; ++k) w[k] = u;
-      }
+      if (sum > 0.0f && isfinite(sum))
+        w = __fmul_rn(__fdiv_rn(w, sum), a.route_scale);
+      else
+        w = __fdiv_rn(a.route_scale, (float)n);
     }
   } else if (n > 0) {
     // normalize_route_weights_legacy (src/server/generation.rs:3152-3180)
-    bool uniform = false;
-    for (int k = 0; k < n; ++k) uniform = uniform || !isfinite(w[k]);
+    bool uniform = __any_sync(0xffffffffu, mine && !isfinite(w));
     if (!uniform) {
-      float mx = -INFINITY;
-      for (int k = 0; k < n; ++k) mx = fmaxf(mx, w[k]);
-      float sum = 0.0f;
-      for (int k = 0; k < n; ++k) {
-        w[k] = glibc_like_expf(__fsub_rn(w[k], mx));
-        sum = __fadd_rn(sum, w[k]);
-      }
+      float mx = mine ? w : -INFINITY;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float e = mine ? glibc_like_expf(__fsub_rn(w, mx)) : 0.0f;
+      const float sum = ordered_sum(e);
       if (!isfinite(sum) || sum <= 1.1920929e-07f)
         uniform = true;
       else
-        for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(w[k], sum);
+        w = __fdiv_rn(e, sum);
     }
-    if (uniform)
-      for (int k = 0; k < n; ++k) w[k] = __fdiv_rn(1.0f, (float)n);
+    if (uniform) w = __fdiv_rn(1.0f, (float)n);
   }
   // combine weights w_k / sum(w) (valid_route_weight_sum, src/compute.rs:2015-2030)
-  bool valid = true;
-  float sum = 0.0f;
-  for (int k = 0; k < n; ++k) {
-    if (isfinite(w[k]) && w[k] >= 0.0f)
-      sum = __fadd_rn(sum, w[k]);
-    else {
-      valid = false;
-      break;
-    }
-  }
-  if (valid && sum <= 1.1920929e-07f) valid = false;
-  for (int k = 0; k < a.topk; ++k) {
-    a.ids[(long long)t * a.topk + k] = k < n ? ids[k] : -1;
-    a.weights[(long long)t * a.topk + k] = k < n ? w[k] : 0.0f;
+  const bool bad = __any_sync(0xffffffffu, mine && !(isfinite(w) && w >= 0.0f));
+  const float wsum = ordered_sum(mine ? w : 0.0f);
+  const bool valid = !bad && wsum > 1.1920929e-07f;
+  if (lane < a.topk) {
+    const long long o = (long long)t * a.topk + lane;
+    a.ids[o] = mine ? my_id : -1;
+    a.weights[o] = mine ? w : 0.0f;
     if (a.combine_w)
-      a.combine_w[(long long)t * a.topk + k] =
-          k < n ? (valid ? __fdiv_rn(w[k], sum) : __fdiv_rn(1.0f, (float)n)) : 0.0f;
+      a.combine_w[o] = mine ? (valid ? __fdiv_rn(w, wsum) : __fdiv_rn(1.0f, (float)n)) : 0.0f;
   }
-  a.counters[t] = 0;  // ready for the next call
+  if (lane == 0) a.counters[t] = 0;  // ready for the next call
 }
 
 // kSmem: rows and x staged in shared memory (hidden % 8 == 0, 16-byte aligned
@@ -282,23 +284,35 @@ __global__ void __launch_bounds__(32) router_kernel(RouterArgs a, __half* xq, fl
   const float sv = __fadd_rn(__fadd_rn(acc.x, o0), __fadd_rn(acc.y, o1));  // v_{2p}+v_{2p+1}
   const float s2 = __fadd_rn(sv, __shfl_xor_sync(0xffffffffu, sv, 1));
   const float hs = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
-  if (p == 0 && r < nrows) {
+  float lg = hs;
+  if (p == 0) {
     float tail = 0.0f;
     for (int i = chunks * 16; i < a.hidden; ++i)
       tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(grow[i]) << 16), x[i]));
-    a.logits[(long long)t * a.experts + e0 + r] = __fadd_rn(hs, tail);
+    lg = __fadd_rn(hs, tail);
   }
-
-  // (3) the last CTA of this token does top-k + weights
-  __threadfence();
-  __syncwarp();
+  // lane 0 writes the CTA's logits itself, then publishes them (one writer,
+  // one fence, one arrival)
+  float lrow[kRouterRowsPerCta];
+#pragma unroll
+  for (int k = 0; k < kRouterRowsPerCta; ++k) lrow[k] = __shfl_sync(0xffffffffu, lg, 8 * k);
   uint32_t prev = 0;
-  if (lane == 0) prev = atomicAdd(&a.counters[t], 1u);
+  if (lane == 0) {
+    for (int k = 0; k < nrows; ++k) a.logits[(long long)t * a.experts + e0 + k] = lrow[k];
+    __threadfence();
+    prev = atomicAdd(&a.counters[t], 1u);
+  }
   prev = __shfl_sync(0xffffffffu, prev, 0);
   pdl_launch_dependents();
+  // (3) the last CTA of this token does top-k + weights
   if (prev != gridDim.x - 1) return;
   __threadfence();
-  router_topk_and_weights(a, t, lane);
+  if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane);
+  else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane);
+  else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane);
+  else if (a.experts <= 256) router_topk_and_weights<8>(a, t, lane);
+  else if (a.experts <= 512) router_topk_and_weights<16>(a, t, lane);
+  else router_topk_and_weights<32>(a, t, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -368,20 +382,14 @@ __device__ __forceinline__ float hsum8(const float a[8]) {
 // act-quant block to finish quantises the block (atomic arrival counter, no
 // waiting).
 // ---------------------------------------------------------------------------
-#ifndef WH_UP_STAGES
-#define WH_UP_STAGES 5
-#endif
-constexpr int kUpStages = WH_UP_STAGES;
+constexpr int kUpStages = 4;
 constexpr int kUpRows = kMoeUpRows;
 constexpr int kUpBox = kUpRows * 128;         // 4 KB
 constexpr int kUpStageBytes = 2 * kUpBox;     // w1 box + w3 box
 
-#ifndef WH_UP_EXTRA_SMEM
-#define WH_UP_EXTRA_SMEM 0
-#endif
 size_t moe_up_smem_bytes(int hidden) {
   return 1024 + kUpStages * kUpStageBytes + 2 * kUpStages * 8 + 16 + hidden * 2 +
-         (hidden / 64) * 4 + 256 + WH_UP_EXTRA_SMEM;
+         (hidden / 64) * 4 + 128 + 2 * kUpRows * (hidden / 32) + 64;
 }
 
 __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __restrict__ xq,
@@ -396,6 +404,7 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
   __half* xs = reinterpret_cast<__half*>(xbar + 2);
   float* xm = reinterpret_cast<float*>(xs + a.hidden);
   float* gsh = xm + a.hidden / 64;  // [32] gate values handed to the up warp
+  uint8_t* ssm = reinterpret_cast<uint8_t*>(gsh + 32);  // [2][32 rows][hidden/32] scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.z, slot = blockIdx.y;
@@ -440,9 +449,14 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
       // staged input (produced by the router / act-quant kernel); the
       // consumers wait for it before freeing any stage
       if (slot >= a.topk) pdl_wait_prior();
-      mbar_arrive_expect_tx(xbar, a.hidden * 2 + (a.hidden / 64) * 4);
+      const int scols = a.hidden / 32;
+      const Fp4ExpertDev& ex = a.experts[expert];
+      mbar_arrive_expect_tx(xbar, a.hidden * 2 + (a.hidden / 64) * 4 + 2 * kUpRows * scols);
       bulk_load(xs, xq + (long long)t * a.hidden, a.hidden * 2, xbar);
       bulk_load(xm, xq_mult + (long long)t * (a.hidden / 64), (a.hidden / 64) * 4, xbar);
+      // this CTA's scale rows are contiguous: [32 rows][hidden/32] per matrix
+      bulk_load(ssm, ex.w1_scale + (long long)row0 * scols, kUpRows * scols, xbar);
+      bulk_load(ssm + kUpRows * scols, ex.w3_scale + (long long)row0 * scols, kUpRows * scols, xbar);
       for (; i < nbox; ++i) {
         if (!mbar_wait(&empty[i % kUpStages], ((i / kUpStages) - 1) & 1, a.status)) break;
         issue(i);
@@ -467,16 +481,15 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
   bool ok = mbar_wait(xbar, 0, a.status);
 
   const int row = row0 + lane;
-  const Fp4ExpertDev ed = a.experts[expert];
   const int scols = a.hidden / 32;
-  const uint8_t* srow = (warp == 0 ? ed.w1_scale : ed.w3_scale) + (long long)row * scols;
+  const uint8_t* srow = ssm + (warp * kUpRows + lane) * scols;
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
 
   for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kUpStages;
-    const uint2 sb = __ldg(reinterpret_cast<const uint2*>(srow + i * 8));
+    const uint2 sb = *reinterpret_cast<const uint2*>(srow + i * 8);
     if (!mbar_wait(&full[s], (i / kUpStages) & 1, a.status)) {
       ok = false;
       break;
@@ -544,7 +557,7 @@ size_t moe_down_smem_bytes(int inter, int slots) {
   (void)slots;
   return 1024 + kDownStages * kDownStageBytes + 2 * kDownStages * 8 + 16 +
          kDownSlots * (inter * 2 + 16) + kDownSlots * (inter / 64) * 4 +
-         kDownSlots * kDownRows * 4 + 64;
+         kDownSlots * kDownRows * 4 + kDownSlots * kDownRows * (inter / 32) + 64;
 }
 
 __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* __restrict__ hq,
@@ -559,6 +572,7 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
   uint8_t* hs = reinterpret_cast<uint8_t*>(xbar + 2);
   float* hm = reinterpret_cast<float*>(hs + kDownSlots * hstride);
   float* ys = hm + kDownSlots * (a.inter / 64);
+  uint8_t* ssm = reinterpret_cast<uint8_t*>(ys + kDownSlots * kDownRows);  // [slot][16][inter/32]
   __shared__ int slot_expert[kDownSlots];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -610,12 +624,20 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
   pdl_wait_prior();  // hq from moe_up
   pdl_launch_dependents();
   // stage hq of every slot (bulk copies, one barrier)
+  const int scols = a.inter / 32;
   if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4));
+    int nvalid = 0;
+    for (int k = 0; k < nslots; ++k) nvalid += slot_expert[k] >= 0;
+    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4) +
+                                    nvalid * kDownRows * scols);
     for (int k = 0; k < nslots; ++k) {
       bulk_load(hs + k * hstride, hq + ((long long)t * nslots + k) * a.inter, a.inter * 2, xbar);
       bulk_load(hm + k * (a.inter / 64), hq_mult + ((long long)t * nslots + k) * (a.inter / 64),
                 (a.inter / 64) * 4, xbar);
+      const int e = slot_expert[k];
+      if (e >= 0)  // this CTA's 16 scale rows of the slot's w2 are contiguous
+        bulk_load(ssm + k * kDownRows * scols, a.experts[e].w2_scale + (long long)row0 * scols,
+                  kDownRows * scols, xbar);
     }
   }
   bool ok = mbar_wait(xbar, 0, a.status);
@@ -625,8 +647,7 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
   const int row = row0 + r;
   const int e = slot < nslots ? slot_expert[slot] : -1;
   const bool active = e >= 0;
-  const int scols = a.inter / 32;
-  const uint8_t* srow = active ? a.experts[e].w2_scale + (long long)row * scols : nullptr;
+  const uint8_t* srow = ssm + ((active ? slot : 0) * kDownRows + r) * scols;
   const __half* hslot = reinterpret_cast<const __half*>(hs + (active ? slot : 0) * hstride);
   const float* hmul = hm + (active ? slot : 0) * (a.inter / 64);
   float acc[8];
@@ -635,7 +656,7 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
   for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kDownStages;
     uint2 sb = make_uint2(0, 0);
-    if (active) sb = __ldg(reinterpret_cast<const uint2*>(srow + i * 8));
+    if (active) sb = *reinterpret_cast<const uint2*>(srow + i * 8);
     if (!mbar_wait(&full[s], (i / kDownStages) & 1, a.status)) {
       ok = false;
       break;
@@ -788,8 +809,7 @@ cudaError_t launch_router_ex(const RouterArgs& a, __half* xq, float* xq_mult, cu
                        router_smem_plan(a.hidden).bytes <= 200 * 1024;
   if (smem_ok) {
     const size_t smem = router_smem_plan(a.hidden).bytes;
-    cudaError_t e = cudaFuncSetAttribute(router_kernel<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem(router_kernel<true>, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(32), smem, s, attr, pdl);
     return cudaLaunchKernelEx(&cfg, router_kernel<true>, a, xq, xq_mult);
@@ -802,8 +822,7 @@ cudaError_t launch_moe_up_ex(const MoeArgs& a, const __half* xq, const float* xq
                              float* hq_mult, cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
   const size_t smem = moe_up_smem_bytes(a.hidden);
-  cudaError_t e = cudaFuncSetAttribute(moe_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = ensure_smem(moe_up_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.inter / kUpRows, a.topk + a.has_shared, a.tokens);
   cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(96), smem, s, attr, pdl);
@@ -814,8 +833,7 @@ cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* 
                                cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
   const size_t smem = moe_down_smem_bytes(a.inter, a.topk + a.has_shared);
-  cudaError_t e = cudaFuncSetAttribute(moe_down_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(moe_down_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.hidden / kDownRows, a.tokens);
   cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(160), smem, s, attr, pdl);
