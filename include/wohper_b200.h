@@ -143,6 +143,23 @@ wh_status wh_fp4_expert_forward(wh_ctx* ctx, const wh_fp4_expert* expert, const 
                                 size_t input_len, float* output, size_t output_len,
                                 float* scratch, size_t scratch_len, wh_stream_t stream);
 
+/* wh_fp4_expert_forward without caller scratch and without any device
+ * allocation: no reference counterpart (the reference's callers always pass
+ * scratch).  For callers that cannot allocate device memory on the call path
+ * -- a server whose arena owns all of HBM, or a decode loop that must not take
+ * cudaMalloc/cudaFree's implicit synchronisation -- and cannot lend scratch.
+ * Scratch is a fixed 65536-float device array inside the library; experts
+ * with hidden + 2 * intermediate > 65536 return WH_ERR_SCRATCH_TOO_SMALL.
+ * Nothing in it needs to start at zero.  The first call on each device looks
+ * the array up (cudaGetSymbolAddress) and should happen before any stream
+ * capture.  The array is shared by every caller on a device: calls that
+ * overlap in time there (other streams, threads or contexts) race; calls in
+ * order on one stream are safe.  Computes the reference-order exact path;
+ * device-side errors are reported by wh_ctx_sync like every other call. */
+wh_status wh_fp4_expert_forward_noalloc(wh_ctx* ctx, const wh_fp4_expert* expert,
+                                        const float* input, size_t input_len, float* output,
+                                        size_t output_len, wh_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Router                                                                    */
 /* ------------------------------------------------------------------------ */

@@ -49,6 +49,7 @@ EXPORTS = (
     "wh_fp4_expert_forward", "wh_router_topk", "wh_moe_plan_create", "wh_moe_plan_destroy",
     "wh_moe_scratch_bytes", "wh_moe_ffn", "wh_debug_act_quant_table", "wh_debug_e4m3_round",
     "wh_ctx_set_profiling", "wh_ctx_phase_times", "wh_debug_e4m3_round_n",
+    "wh_fp4_expert_forward_noalloc",
 )
 
 
@@ -108,6 +109,7 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_fp4_matvec": (st, [vp, C.POINTER(Fp4MatvecSpec), vp, sz, vp, sz, vp]),
         "wh_fp4_expert_scratch_len": (sz, [sz]),
         "wh_fp4_expert_forward": (st, [vp, C.POINTER(Fp4ExpertSpec), vp, sz, vp, sz, vp, sz, vp]),
+        "wh_fp4_expert_forward_noalloc": (st, [vp, C.POINTER(Fp4ExpertSpec), vp, sz, vp, sz, vp]),
         "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
         "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
         "wh_moe_plan_destroy": (None, [vp]),
@@ -273,6 +275,16 @@ def deepseek_v4_fp4_expert_forward(ctx, expert: DeepSeekV4Fp4Expert, input, outp
     _check(lib().wh_fp4_expert_forward(ctx.handle, C.byref(s), _ptr(input), input.numel(),
                                        _ptr(output), output.numel(), _ptr(scratch),
                                        scratch.numel(), _stream(stream)))
+    return output
+
+
+def deepseek_v4_fp4_expert_forward_noalloc(ctx, expert: DeepSeekV4Fp4Expert, input, output,
+                                           stream=None):
+    """The expert forward with library-owned static scratch (no allocation)."""
+    s = expert.spec()
+    _check(lib().wh_fp4_expert_forward_noalloc(ctx.handle, C.byref(s), _ptr(input),
+                                               input.numel(), _ptr(output), output.numel(),
+                                               _stream(stream)))
     return output
 
 

@@ -3,3 +3,4 @@
 #include "fp8_gemv.cu"
 #include "moe.cu"
 #include "capi.cu"
+#include "noalloc.cu"
