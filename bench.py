@@ -45,6 +45,9 @@ SLOTS = TOPK + 1
 STEP_BYTES = SLOTS * EXPERT_BYTES + ROUTER_BYTES + 2 * HID * 4
 UP_BYTES = SLOTS * 2 * (PACKED_W13 + SCALES_W13)       # moe_up algorithmic bytes / launch
 DOWN_BYTES = SLOTS * (PACKED_W2 + SCALES_W2)
+# DRAM bytes (read + write) of one moe_up launch from an ncu capture of the
+# --ncu-case moe16 workload, which processes the same units per launch
+UP_TRAFFIC = 63_292_672
 METRIC = "decode tokens/s (one-token FP4 MoE FFN, config 2)"
 WORKLOAD = ("config 2: one-token FP4 MoE FFN, 256 experts 4096->2048->4096 E2M1/UE8M0-32, "
             "bf16 router top-6 softmax-renormalised, 6 routed + 1 shared expert")
@@ -371,7 +374,9 @@ def run_ours(args):
                 "kernel": "moe_up_kernel (w1+w3 FP4 matvecs of 7 experts + SwiGLU + act quant)",
                 "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
-                "algorithmic_bytes": UP_BYTES, "traffic": None,
+                "algorithmic_bytes": UP_BYTES, "traffic": UP_TRAFFIC,
+                "traffic_source": "ncu dram__bytes_read+write of one moe_up launch "
+                                  "(bench.py --ncu-case moe16: same 7 experts' w1/w3 per launch)",
                 "down_kernel_gbs": round(DOWN_BYTES / (down_ms * 1e-3) / 1e9, 1),
             },
             "e2e": {"value": round(world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
@@ -423,6 +428,53 @@ def run_reference(args):
     }
 
 
+def run_ncu_case(args):
+    """Small single-GPU workloads for ncu captures (no JSON bench line).
+
+    fp8:   config-1 FP8 GEMV (4096 x 4096, one token), one launch per step.
+    moe16: the config-2 MoE FFN step with 16 routed experts instead of 256
+           (220 MB of weights; the kernels read the same 7 experts' bytes per
+           token as at 256), router + moe_up + moe_down per step.
+    L2 is flushed (256 MiB memset) before every step."""
+    import torch
+
+    import wohper_b200 as W
+    from tests import helpers as H
+
+    ctx = W.Context(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    n = args.warmup + args.steps
+    if args.ncu_case == "fp8":
+        w, s = H.fp8_weight(1, HID, HID)
+        wd, sd = torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda()
+        x = torch.from_numpy(H.activations(2, 1, HID).reshape(-1)).cuda()
+        for _ in range(n):
+            flush.zero_()
+            W.gemv_fp8_e4m3_ue8m0_tensorwise(ctx, wd, sd, x)
+    else:
+        ne = 16
+        stack = H.torch_fp4_experts(5, ne + 1, HID, INTER)
+        gate = torch.from_numpy(H.router_gate(6, ne, HID).view(np.int16)).cuda()
+
+        def wexp(e):
+            w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+            return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+        layer = W.MoeLayer(ctx, [wexp(e) for e in range(ne)], wexp(ne), gate, topk=TOPK,
+                           max_tokens=1)
+        xs = torch.from_numpy(H.activations(7, n, HID)).cuda()
+        y = torch.empty(1, HID, device="cuda")
+        for i in range(n):
+            flush.zero_()
+            layer.forward(xs[i:i + 1], y)
+        layer.close()
+    ctx.sync()
+    ctx.close()
+    print(json.dumps({"ncu_case": args.ncu_case, "steps": n}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -430,7 +482,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16"],
+                    help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case(args)
+        return
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:

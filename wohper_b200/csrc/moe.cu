@@ -70,11 +70,15 @@ __device__ __forceinline__ int32_t total_key(float f) {
 }
 
 // ---------------------------------------------------------------------------
-// Router: one warp per 4 expert rows.  The rows and the token's x are bulk
-// copied into shared memory first (rows padded by 32 B so the 4 rows of a warp
-// hit different banks); every lane then walks its two FMA chains over smem.
+// Router: a CTA of two warps covers 4 expert rows.  Each half-warp owns one
+// row and each of its 16 lanes one of the 16 FMA chains of dot_bf16_row_avx2
+// (lanes 0-7: acc0 lane j, columns 16c+j; lanes 8-15: acc1 lane j, columns
+// 16c+8+j).  The rows and the token's x are bulk copied into shared memory
+// first (rows padded by 32 B so the two rows of a warp hit different banks).
+// The CTA that arrives last selects the top-k and computes the route weights.
 // ---------------------------------------------------------------------------
 constexpr int kRouterRowsPerCta = 4;
+constexpr int kRouterThreads = 64;
 
 struct RouterSmemPlan {
   int row_stride;  // bytes
@@ -87,31 +91,61 @@ __host__ __device__ inline RouterSmemPlan router_smem_plan(int hidden) {
   return p;
 }
 
+__device__ __forceinline__ float key_to_float(int32_t k) {  // inverse of total_key
+  return __int_as_float(k ^ int32_t(uint32_t(k >> 31) >> 1));
+}
+
+// Arrival counter with release (this CTA's logits) and acquire (everyone
+// else's, for the last arriver) at GPU scope.
+__device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // Top-k selection and route weights for token t by one warp, all in
-// registers.  PER = logits held per lane (experts <= 32*PER).  Lane k ends up
-// owning route k; ordered sums (the reference accumulates left to right) are
-// gathered to lane 0 with shuffles.
+// registers.  PER = logits held per lane (candidate i of lane l is expert
+// i*32+l; experts <= 32*PER).  Lane k ends up owning route k.  Each step of the
+// selection is a warp-wide arg-max (redux max of the total_cmp key, then redux
+// min of the expert id among the lanes holding it), which is the order of the
+// reference's stable descending sort.  Ordered sums (the reference adds left
+// to right) gather their terms with independent shuffles first.
 template <int PER>
 __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane) {
+  constexpr unsigned kFull = 0xffffffffu;
   const float* L = a.logits + (long long)t * a.experts;
+  const bool biased = a.mode == 1 && a.bias != nullptr;
   float sc[PER];
   int32_t key[PER];
+  uint32_t avail = 0;  // bit i: candidate i exists and is not selected yet
+  // every load first, so that they are in flight together
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int ex = i * 32 + lane;
-    float v = ex < a.experts ? __ldcg(L + ex) : 0.0f;
-    if (a.mode == 1 && ex < a.experts) v = sqrt_softplus_ref(v);
-    sc[i] = v;
-    float sel = v;
-    if (a.mode == 1 && a.bias != nullptr && ex < a.experts) sel = __fadd_rn(v, a.bias[ex]);
-    key[i] = ex < a.experts ? total_key(sel) : INT32_MIN;
+    const bool in = ex < a.experts;
+    sc[i] = in ? __ldcg(L + ex) : 0.0f;
+    avail |= uint32_t(in) << i;
   }
+  if (a.mode == 1) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if ((avail >> i) & 1u) sc[i] = sqrt_softplus_ref(sc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int ex = i * 32 + lane;
+    key[i] = total_key((biased && ex < a.experts) ? __fadd_rn(sc[i], __ldg(a.bias + ex)) : sc[i]);
+  }
+
   auto score_of = [&](int ex) {  // warp-uniform ex
     float mine = 0.0f;
 #pragma unroll
     for (int i = 0; i < PER; ++i)
       if (i == (ex >> 5)) mine = sc[i];
-    return __shfl_sync(0xffffffffu, mine, ex & 31);
+    return __shfl_sync(kFull, mine, ex & 31);
   };
   int my_id = -1;
   float my_score = 0.0f;
@@ -131,42 +165,40 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
     }
   } else {
     // stable descending sort by total_cmp, truncated: max key, lowest id on ties
-    uint32_t taken = 0;
     const int kk = min(a.topk, a.experts);
     for (int k = 0; k < kk; ++k) {
       int32_t bk = INT32_MIN;
       int bi = 0x7fffffff;
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
-        const int ex = i * 32 + lane;
-        if (ex < a.experts && !((taken >> i) & 1u) && (key[i] > bk || (key[i] == bk && ex < bi))) {
+        // ids grow with i on a lane: a strict '>' keeps the lowest id on ties
+        if (((avail >> i) & 1u) && (bi == 0x7fffffff || key[i] > bk)) {
           bk = key[i];
-          bi = ex;
+          bi = i * 32 + lane;
         }
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const int32_t ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ok2 > bk || (ok2 == bk && oi < bi)) {
-          bk = ok2;
-          bi = oi;
-        }
-      }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      const float got = score_of(bi);
+      const int32_t m = __reduce_max_sync(kFull, bk);
+      const int win = int(__reduce_min_sync(
+          kFull, (bi != 0x7fffffff && bk == m) ? uint32_t(bi) : 0xffffffffu));
+      if ((win & 31) == lane) avail &= ~(1u << (win >> 5));
+      const float got = score_of(win);
       if (lane == k) {
-        my_id = bi;
+        my_id = win;
         my_score = got;
       }
       n = k + 1;
     }
   }
   const bool mine = lane < n;
-  // ordered left-to-right sum of v over lanes 0..n-1 (reference summation order)
-  auto ordered_sum = [&](float v) {
+  auto ordered_sum = [&](float v) {  // v_0 + v_1 + ... + v_{n-1}, left to right
+    float g[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] = __shfl_sync(kFull, v, k);
     float acc = 0.0f;
-    for (int k = 0; k < n; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, k));
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < n) acc = __fadd_rn(acc, g[k]);
+    for (int k = 8; k < n; ++k) acc = __fadd_rn(acc, __shfl_sync(kFull, v, k));
     return acc;  // uniform
   };
   float w = my_score;
@@ -181,11 +213,11 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
     }
   } else if (n > 0) {
     // normalize_route_weights_legacy (src/server/generation.rs:3152-3180)
-    bool uniform = __any_sync(0xffffffffu, mine && !isfinite(w));
+    bool uniform = __any_sync(kFull, mine && !isfinite(w));
     if (!uniform) {
-      float mx = mine ? w : -INFINITY;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      // every selected w is finite here, where total_cmp order is numeric
+      // order (a -0/+0 tie gives the same exp(w - max) either way)
+      const float mx = key_to_float(__reduce_max_sync(kFull, mine ? total_key(w) : INT32_MIN));
       const float e = mine ? glibc_like_expf(__fsub_rn(w, mx)) : 0.0f;
       const float sum = ordered_sum(e);
       if (!isfinite(sum) || sum <= 1.1920929e-07f)
@@ -196,7 +228,7 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
     if (uniform) w = __fdiv_rn(1.0f, (float)n);
   }
   // combine weights w_k / sum(w) (valid_route_weight_sum, src/compute.rs:2015-2030)
-  const bool bad = __any_sync(0xffffffffu, mine && !(isfinite(w) && w >= 0.0f));
+  const bool bad = __any_sync(kFull, mine && !(isfinite(w) && w >= 0.0f));
   const float wsum = ordered_sum(mine ? w : 0.0f);
   const bool valid = !bad && wsum > 1.1920929e-07f;
   if (lane < a.topk) {
@@ -212,23 +244,27 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
 // kSmem: rows and x staged in shared memory (hidden % 8 == 0, 16-byte aligned
 // rows); otherwise read straight from global memory.
 template <bool kSmem>
-__global__ void __launch_bounds__(32) router_kernel(RouterArgs a, __half* xq, float* xq_mult) {
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, __half* xq,
+                                                                float* xq_mult) {
   extern __shared__ __align__(16) uint8_t rsmem[];
   const int t = blockIdx.y;
-  const int lane = threadIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int e0 = blockIdx.x * kRouterRowsPerCta;
   const int nrows = min(kRouterRowsPerCta, a.experts - e0);
   const RouterSmemPlan plan = router_smem_plan(a.hidden);
   uint64_t* bar = reinterpret_cast<uint64_t*>(rsmem);
+  uint32_t* last_s = reinterpret_cast<uint32_t*>(rsmem + 8);
   uint8_t* rows_s = rsmem + 64;
   float* x_s = reinterpret_cast<float*>(rows_s + kRouterRowsPerCta * plan.row_stride);
 
-  if (kSmem && lane == 0) {
+  if (kSmem && tid == 0) {
     mbar_init(bar, 1);
     fence_barrier_init();
   }
-  __syncwarp();
-  if (kSmem && lane == 0) {
+  __syncthreads();
+  if (kSmem && tid == 0) {
     // gate rows do not depend on earlier kernels: start them before the PDL wait
     mbar_arrive_expect_tx(bar, nrows * a.hidden * 2 + a.hidden * 4);
     for (int r = 0; r < nrows; ++r)
@@ -237,12 +273,12 @@ __global__ void __launch_bounds__(32) router_kernel(RouterArgs a, __half* xq, fl
   }
   pdl_wait_prior();
   const float* x = a.x + (long long)t * a.hidden;
-  if (kSmem && lane == 0) bulk_load(x_s, x, a.hidden * 4, bar);
+  if (kSmem && tid == 0) bulk_load(x_s, x, a.hidden * 4, bar);
 
-  // (1) act-quantised copy of x for the expert kernels: 64-blocks over the CTAs
+  // (1) act-quantised copy of x for the expert kernels: 64-blocks over the warps
   if (xq != nullptr) {
     const int nblk = a.hidden / 64;
-    for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    for (int blk = blockIdx.x * 2 + warp; blk < nblk; blk += gridDim.x * 2) {
       const float v0 = x[blk * 64 + lane], v1 = x[blk * 64 + 32 + lane];
       float amax = fmaxf(fabsf(v0), fabsf(v1));
       for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -254,59 +290,43 @@ __global__ void __launch_bounds__(32) router_kernel(RouterArgs a, __half* xq, fl
     }
   }
 
-  // (2) logits: 8 lanes per expert row; lane p owns chains 2p,2p+1 of acc0
-  // (p<4) or of acc1 (p>=4) -- dot_bf16_row_avx2 (src/compute.rs:6115-6136)
-  const int p = lane & 7;
-  const int r = lane >> 3;
+  // (2) logits -- dot_bf16_row_avx2 (src/compute.rs:6115-6136)
+  const int p = lane & 15;
+  const int r = warp * 2 + (lane >> 4);
   const int rr = r < nrows ? r : nrows - 1;  // every lane joins the shuffles
   const int chunks = a.hidden / 16;
   const uint16_t* grow = a.gate + (long long)(e0 + rr) * a.hidden;
-  const uint32_t* w32;
-  const float2* x2;
+  const uint16_t* wv;
+  const float* xv;
   if (kSmem) {
-    if (!mbar_wait(bar, 0, a.status)) return;
-    w32 = reinterpret_cast<const uint32_t*>(rows_s + rr * plan.row_stride) + p;
-    x2 = reinterpret_cast<const float2*>(x_s) + p;
+    mbar_wait(bar, 0, a.status);  // a timeout is flagged; the CTA still finishes
+    wv = reinterpret_cast<const uint16_t*>(rows_s + rr * plan.row_stride) + p;
+    xv = x_s + p;
   } else {
-    w32 = reinterpret_cast<const uint32_t*>(grow) + p;
-    x2 = reinterpret_cast<const float2*>(x) + p;
+    wv = grow + p;
+    xv = x + p;
   }
-  float2 acc = make_float2(0.0f, 0.0f);
+  float acc = 0.0f;
 #pragma unroll 16
-  for (int c = 0; c < chunks; ++c) {
-    const uint32_t wv = w32[c * 8];
-    const float2 wf = make_float2(__uint_as_float(wv << 16), __uint_as_float(wv & 0xffff0000u));
-    acc = ffma2(wf, x2[c * 8], acc);
-  }
-  // v_j = acc0_j + acc1_j (lanes p and p^4)
-  const float o0 = __shfl_xor_sync(0xffffffffu, acc.x, 4);
-  const float o1 = __shfl_xor_sync(0xffffffffu, acc.y, 4);
-  const float sv = __fadd_rn(__fadd_rn(acc.x, o0), __fadd_rn(acc.y, o1));  // v_{2p}+v_{2p+1}
-  const float s2 = __fadd_rn(sv, __shfl_xor_sync(0xffffffffu, sv, 1));
-  const float hs = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
-  float lg = hs;
-  if (p == 0) {
+  for (int c = 0; c < chunks; ++c)
+    acc = __fmaf_rn(__uint_as_float(uint32_t(wv[c * 16]) << 16), xv[c * 16], acc);
+  // v_j = acc0_j + acc1_j, then the pairwise horizontal sum of v_0..v_7
+  const float v = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+  const float h1 = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  const float h2 = __fadd_rn(h1, __shfl_xor_sync(0xffffffffu, h1, 2));
+  const float h3 = __fadd_rn(h2, __shfl_xor_sync(0xffffffffu, h2, 4));
+  if (p == 0 && r < nrows) {
     float tail = 0.0f;
     for (int i = chunks * 16; i < a.hidden; ++i)
       tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(grow[i]) << 16), x[i]));
-    lg = __fadd_rn(hs, tail);
+    a.logits[(long long)t * a.experts + e0 + r] = __fadd_rn(h3, tail);
   }
-  // lane 0 writes the CTA's logits itself, then publishes them (one writer,
-  // one fence, one arrival)
-  float lrow[kRouterRowsPerCta];
-#pragma unroll
-  for (int k = 0; k < kRouterRowsPerCta; ++k) lrow[k] = __shfl_sync(0xffffffffu, lg, 8 * k);
-  uint32_t prev = 0;
-  if (lane == 0) {
-    for (int k = 0; k < nrows; ++k) a.logits[(long long)t * a.experts + e0 + k] = lrow[k];
-    __threadfence();
-    prev = atomicAdd(&a.counters[t], 1u);
-  }
-  prev = __shfl_sync(0xffffffffu, prev, 0);
+  __syncthreads();
+  if (tid == 0) *last_s = atomic_add_acq_rel(&a.counters[t], 1u) == gridDim.x - 1;
+  __syncthreads();
   pdl_launch_dependents();
   // (3) the last CTA of this token does top-k + weights
-  if (prev != gridDim.x - 1) return;
-  __threadfence();
+  if (!*last_s || warp != 0) return;
   if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane);
   else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane);
   else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane);
@@ -811,10 +831,10 @@ cudaError_t launch_router_ex(const RouterArgs& a, __half* xq, float* xq_mult, cu
     const size_t smem = router_smem_plan(a.hidden).bytes;
     cudaError_t e = ensure_smem(router_kernel<true>, smem);
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(32), smem, s, attr, pdl);
+    cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kRouterThreads), smem, s, attr, pdl);
     return cudaLaunchKernelEx(&cfg, router_kernel<true>, a, xq, xq_mult);
   }
-  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(32), 64, s, attr, pdl);
+  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kRouterThreads), 64, s, attr, pdl);
   return cudaLaunchKernelEx(&cfg, router_kernel<false>, a, xq, xq_mult);
 }
 
