@@ -82,3 +82,21 @@ def expert_views(stack: dict, e: int):
 
 def max_rel_err(got: np.ndarray, ref: np.ndarray, floor: float = 1e-6) -> float:
     return float(np.max(np.abs(got - ref) / np.maximum(np.abs(ref), floor)))
+
+
+def zipf_routing(seed: int, gate_bits: np.ndarray, x: np.ndarray, s: float = 1.1,
+                 strength: float = 1.4):
+    """Zipf-skewed routing for raw-logit top-k: hidden column 0 of every token
+    is set to 1.0 and gate column 0 to the prior -strength * s * ln(rank) over a
+    seeded permutation of the experts, so logit_e = gate_e . x + prior_e and the
+    per-expert token counts become uneven (popular experts, empty ones).
+    Returns (gate_bits, x) copies."""
+    g = gate_bits.copy()
+    x = x.copy()
+    E = g.shape[0]
+    ranks = np.empty(E, np.int64)
+    ranks[rng(seed).permutation(E)] = np.arange(1, E + 1)
+    prior = (-strength * s * np.log(ranks)).astype(np.float32)
+    g[:, 0] = bf16_bits(prior)
+    x[:, 0] = 1.0
+    return g, x

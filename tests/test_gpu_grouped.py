@@ -1,0 +1,137 @@
+"""Batched MoE FFN on the tensor cores (wh_moe_ffn with tokens >= 32): router
+ids bit-exact with the reference router, outputs within tolerance of the
+reference's expert-major batched path (src/compute.rs:1779-1810, union in
+ascending expert id, src/server/generation.rs:2487-2569), restated by the
+oracle's moe_batched.
+
+Tolerance: the grouped GEMMs multiply exactly (FP4 weights converted to E4M3,
+act-quantised E4M3 tokens, UE8M0 scales) but accumulate in the tensor core's
+order and use expf in SiLU, so the SwiGLU hidden can differ from the
+reference's by a few ulp and its act quant can then land on the neighbouring
+E4M3 grid point (a grid flip, up to 1/8 of that hidden value).  One flip
+moves a whole output row by that h times a w2 column, which no
+element-wise relative gate survives on small outputs, so the gate is on the
+layer: max |y - ref| <= 2e-3 * max|ref| and RMS(y - ref) <= 1e-4 * RMS(ref).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from tests import helpers as H
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def W():
+    import wohper_b200
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return wohper_b200
+
+
+@pytest.fixture(scope="module")
+def ctx(W):
+    c = W.Context(0)
+    yield c
+    c.close()
+
+
+def _layer(W, ctx, stack, gate_bits, E, Hd, I, max_tokens, topk=6):
+    def wexp(e):
+        w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+        return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, I, Hd, Hd // 32),
+                                     W.Fp4Matvec(w3, s3, I, Hd, Hd // 32),
+                                     W.Fp4Matvec(w2, s2, Hd, I, I // 32))
+
+    return W.MoeLayer(ctx, [wexp(e) for e in range(E)], wexp(E),
+                      torch.from_numpy(gate_bits.view(np.int16)).cuda(), topk=topk,
+                      max_tokens=max_tokens)
+
+
+def _oracle_experts(stack, E, Hd, I):
+    keep = []
+    arr = (O.Fp4Expert * (E + 1))()
+    for e in range(E + 1):
+        w1, s1, w3, s3, w2, s2 = [t.cpu().numpy() for t in H.expert_views(stack, e)]
+        arr[e] = O.Fp4Expert(O.fp4_spec(w1, s1, I, Hd, Hd // 32, keep),
+                             O.fp4_spec(w3, s3, I, Hd, Hd // 32, keep),
+                             O.fp4_spec(w2, s2, Hd, I, I // 32, keep))
+    return arr, keep
+
+
+def _check(ctx, layer, stack, gate, x, E, Hd, I, topk=6):
+    T = x.shape[0]
+    ids = torch.zeros(T, topk, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(T, topk, device="cuda")
+    y = layer.forward(torch.from_numpy(x).cuda(), ids=ids, weights=wts)
+    ctx.sync()
+    y, ids, wts = y.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy()
+    oids = np.zeros((T, topk), np.int32)
+    ows = np.zeros((T, topk), np.float32)
+    for t in range(T):
+        _, oids[t], ows[t], _ = O.router(gate, x[t], topk, mode=0)
+    np.testing.assert_array_equal(ids, oids)
+    np.testing.assert_allclose(wts, ows, rtol=2e-6, atol=0)
+    arr, keep = _oracle_experts(stack, E, Hd, I)
+    st, want = O.moe_batched(arr, E, oids, ows, arr[E], x)
+    assert st == O.OK
+    assert np.isfinite(y).all()
+    err = y - want
+    assert np.abs(err).max() <= 2e-3 * np.abs(want).max()
+    assert np.sqrt((err ** 2).mean()) <= 1e-4 * np.sqrt((want ** 2).mean())
+    return np.bincount(oids.reshape(-1), minlength=E)
+
+
+def test_grouped_small_layer(ctx, W):
+    E, Hd, I, T = 16, 1024, 512, 64
+    stack = H.torch_fp4_experts(71, E + 1, Hd, I)
+    gate = H.router_gate(72, E, Hd)
+    x = H.activations(73, T, Hd)
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
+    try:
+        _check(ctx, layer, stack, gate, x, E, Hd, I)
+    finally:
+        layer.close()
+
+
+def test_grouped_uneven_groups_multi_tile_and_empty(ctx, W):
+    # Zipf-skewed routing: some experts get > 128 rows (several N tiles),
+    # some get none
+    E, Hd, I, T = 48, 1024, 512, 320
+    stack = H.torch_fp4_experts(74, E + 1, Hd, I)
+    gate, x = H.zipf_routing(75, H.router_gate(76, E, Hd), H.activations(77, T, Hd))
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
+    try:
+        counts = _check(ctx, layer, stack, gate, x, E, Hd, I)
+    finally:
+        layer.close()
+    assert counts.max() > 128 and (counts == 0).sum() > 0, counts
+
+
+def test_grouped_token_counts_not_multiple_of_tile(ctx, W):
+    # 33 tokens (just above the grouped threshold), an odd tail in every tile
+    E, Hd, I, T = 8, 512, 512, 33
+    stack = H.torch_fp4_experts(78, E + 1, Hd, I)
+    gate = H.router_gate(79, E, Hd)
+    x = H.activations(80, T, Hd)
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, 64)
+    try:
+        _check(ctx, layer, stack, gate, x, E, Hd, I)
+    finally:
+        layer.close()
+
+
+def test_grouped_v4_shape(ctx, W):
+    # DeepSeek-V4-Flash expert shape (4096 -> 2048 -> 4096), 64 experts
+    E, Hd, I, T = 64, 4096, 2048, 96
+    stack = H.torch_fp4_experts(81, E + 1, Hd, I)
+    gate, x = H.zipf_routing(82, H.router_gate(83, E, Hd), H.activations(84, T, Hd))
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
+    try:
+        _check(ctx, layer, stack, gate, x, E, Hd, I)
+    finally:
+        layer.close()

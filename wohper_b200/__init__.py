@@ -341,7 +341,9 @@ class MoeLayer:
         _check(lib().wh_moe_plan_create(ctx.handle, C.byref(d), C.byref(h)))
         self.plan = h
         self.max_tokens = max_tokens
-        nbytes = lib().wh_moe_scratch_bytes(h, max_tokens)
+        # the per-token path (fewer than 32 tokens) and the grouped path lay
+        # scratch out differently: size for the larger of the two
+        nbytes = max(lib().wh_moe_scratch_bytes(h, t) for t in {max_tokens, min(max_tokens, 31)})
         self.scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{ctx.device}")
 
     def forward(self, x, y=None, ids=None, weights=None, hash_ids=None, stream=None):

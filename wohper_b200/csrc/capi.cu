@@ -104,17 +104,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// u8 matrix [rows][row_bytes], box [box_rows][128 B], 128-byte swizzle.
+// u8 matrix [rows][row_bytes], box [box_rows][box_bytes]: 128-byte swizzle
+// for 128-byte boxes (the layout the kernels read back), none otherwise.
 wh_status make_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
-                      uint32_t box_rows) {
+                      uint32_t box_rows, uint32_t box_bytes = 128) {
   auto fn = encode_fn();
   if (!fn) return fail(WH_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {row_bytes, rows};
   cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t box[2] = {box_bytes, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];
@@ -155,6 +157,7 @@ bool expert_fast_ok(const wh_fp4_expert& e, size_t hidden, size_t inter) {
 struct DevExpertSet {
   CUtensorMap* maps = nullptr;      // device [n][3]
   Fp4ExpertDev* experts = nullptr;  // device [n]
+  CUtensorMap* gmaps = nullptr;     // device [n][3], grouped-GEMM boxes (nullable)
   int n = 0;
 };
 
@@ -188,7 +191,39 @@ wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) 
 void free_expert_set(DevExpertSet& s) {
   if (s.maps) cudaFree(s.maps);
   if (s.experts) cudaFree(s.experts);
+  if (s.gmaps) cudaFree(s.gmaps);
   s = DevExpertSet{};
+}
+
+// Whether any expert scale byte is 0 or 255 (device scan of every matrix).
+wh_status scan_scale_bytes(const Fp4ExpertDev* ex, int n, int hidden, int inter, int* bad) {
+  uint32_t* flag = nullptr;
+  WH_CUDA(cudaMalloc(&flag, sizeof(uint32_t)));
+  uint32_t h = 1;
+  cudaError_t e = cudaMemset(flag, 0, sizeof(uint32_t));
+  if (e == cudaSuccess) e = launch_scale_check(ex, n, hidden, inter, flag, nullptr);
+  if (e == cudaSuccess) e = cudaMemcpy(&h, flag, sizeof h, cudaMemcpyDeviceToHost);
+  cudaFree(flag);
+  if (e != cudaSuccess) return cuda_fail(e, "scale scan");
+  *bad = h != 0;
+  return WH_OK;
+}
+
+// Grouped-GEMM tensor maps: FP4 tiles of 128 rows x 128 K (64 B), unswizzled.
+wh_status build_grouped_maps(const wh_fp4_expert* list, int n, DevExpertSet* out) {
+  std::vector<CUtensorMap> maps(size_t(n) * 3);
+  for (int i = 0; i < n; ++i) {
+    const wh_fp4_matvec_spec* m[3] = {&list[i].w1, &list[i].w3, &list[i].w2};
+    for (int j = 0; j < 3; ++j) {
+      wh_status st = make_u8_map(&maps[i * 3 + j], m[j]->packed_weight, m[j]->rows,
+                                 m[j]->cols / 2, 128, 64);
+      if (st != WH_OK) return st;
+    }
+  }
+  WH_CUDA(cudaMalloc(&out->gmaps, maps.size() * sizeof(CUtensorMap)));
+  WH_CUDA(cudaMemcpy(out->gmaps, maps.data(), maps.size() * sizeof(CUtensorMap),
+                     cudaMemcpyHostToDevice));
+  return WH_OK;
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -262,6 +297,7 @@ struct wh_moe_plan {
   DevExpertSet set;  // routed experts, then the shared expert
   uint32_t* counters = nullptr;      // router: [max_tokens]
   uint32_t* blk_counters = nullptr;  // moe_up: [max_tokens][slots][inter/64]
+  bool grouped = false;              // tensor-core path available (tokens >= kGroupedMinTokens)
 };
 
 extern "C" {
@@ -632,6 +668,19 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
     return st;
   }
   p->d.shared = d->shared ? reinterpret_cast<const wh_fp4_expert*>(1) : nullptr;  // flag only
+  if (d->max_tokens >= kGroupedMinTokens && d->hidden % 512 == 0 && d->inter % 512 == 0) {
+    // UE8M0 bytes 0 and 255 mean 0 and +inf in the reference but 2^-127 and NaN
+    // to the tensor core: layers holding either stay on the per-token path
+    int bad = 1;
+    st = build_grouped_maps(all.data(), n, &p->set);
+    if (st == WH_OK) st = scan_scale_bytes(p->set.experts, n, d->hidden, d->inter, &bad);
+    if (st != WH_OK) {
+      free_expert_set(p->set);
+      delete p;
+      return st;
+    }
+    p->grouped = bad == 0;
+  }
   const size_t nblk = (size_t)d->max_tokens * (d->topk + 1) * (d->inter / 64);
   cudaError_t e = cudaMalloc(&p->counters, sizeof(uint32_t) * d->max_tokens);
   if (e == cudaSuccess) e = cudaMemset(p->counters, 0, sizeof(uint32_t) * d->max_tokens);
@@ -691,9 +740,146 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
 }
 }  // namespace
 
+struct GroupedScratch {
+  float* logits;
+  float* combine_w;
+  int32_t* ids;
+  float* weights;
+  int* slot;
+  int* counts;
+  int* offsets;
+  int4* units_up;
+  int4* units_down;
+  int* n_units;
+  uint8_t* xq;   // [rows][hidden] E4M3
+  uint8_t* xsf;  // [rows][hidden/32]
+  uint8_t* hq;   // [rows][inter] E4M3
+  uint8_t* hsf;  // [rows][inter/32]
+  float* yrows;  // [rows][hidden]
+  int rows;
+  size_t bytes;
+};
+GroupedScratch grouped_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
+  const auto& d = p->d;
+  const int ne = d.num_experts + (d.shared ? 1 : 0);
+  const int R = T * d.topk + (d.shared ? T : 0);
+  const size_t tiles = size_t(R) / 128 + 1 + ne;  // >= sum over experts of ceil(rows/128)
+  GroupedScratch s{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* q = base ? base + off : nullptr;
+    off += align256(bytes);
+    return q;
+  };
+  s.logits = reinterpret_cast<float*>(take(sizeof(float) * T * d.num_experts));
+  s.combine_w = reinterpret_cast<float*>(take(sizeof(float) * T * d.topk));
+  s.ids = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * T * d.topk));
+  s.weights = reinterpret_cast<float*>(take(sizeof(float) * T * d.topk));
+  s.slot = reinterpret_cast<int*>(take(sizeof(int) * T * d.topk));
+  s.counts = reinterpret_cast<int*>(take(sizeof(int) * (ne + 1)));
+  s.offsets = reinterpret_cast<int*>(take(sizeof(int) * (ne + 2)));
+  s.units_up = reinterpret_cast<int4*>(take(sizeof(int4) * tiles * (d.inter / 128)));
+  s.units_down = reinterpret_cast<int4*>(take(sizeof(int4) * tiles * (d.hidden / 128)));
+  s.n_units = reinterpret_cast<int*>(take(sizeof(int) * 2));
+  s.xq = take((size_t)R * d.hidden);
+  s.xsf = take((size_t)R * (d.hidden / 32));
+  s.hq = take((size_t)R * d.inter);
+  s.hsf = take((size_t)R * (d.inter / 32));
+  s.yrows = reinterpret_cast<float*>(take(sizeof(float) * (size_t)R * d.hidden));
+  s.rows = R;
+  s.bytes = off;
+  return s;
+}
+bool use_grouped(const wh_moe_plan* p, int tokens) {
+  return p->grouped && tokens >= kGroupedMinTokens;
+}
+
 size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
   if (!p || tokens <= 0) return 0;
+  if (use_grouped(p, tokens)) return grouped_scratch_layout(p, tokens, nullptr).bytes;
   return moe_scratch_layout(p, tokens, nullptr).bytes;
+}
+
+// Batched path (tokens >= kGroupedMinTokens): router, routing bookkeeping and
+// dispatch, grouped up/down GEMMs on the tensor cores, combine.
+wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
+                          const int32_t* hash_ids, float* y, int32_t* ids_out,
+                          float* weights_out, void* scratch, size_t scratch_bytes,
+                          wh_stream_t stream) {
+  const auto& d = p->d;
+  GroupedScratch g = grouped_scratch_layout(p, tokens, static_cast<uint8_t*>(scratch));
+  if (scratch_bytes < g.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "moe scratch too small");
+  const int has_shared = d.shared ? 1 : 0;
+  RouterArgs r{};
+  r.gate = d.gate;
+  r.experts = d.num_experts;
+  r.hidden = d.hidden;
+  r.x = x;
+  r.tokens = tokens;
+  r.topk = d.topk;
+  r.mode = d.router_mode;
+  r.bias = d.gate_bias;
+  r.route_scale = d.route_scale;
+  r.hash_ids = hash_ids;
+  r.logits = g.logits;
+  r.ids = ids_out ? ids_out : g.ids;
+  r.weights = weights_out ? weights_out : g.weights;
+  r.combine_w = g.combine_w;
+  r.counters = p->counters;
+  r.status = c->status;
+  GroupedPlanArgs pa{};
+  pa.ids = r.ids;
+  pa.tokens = tokens;
+  pa.topk = d.topk;
+  pa.num_experts = d.num_experts;
+  pa.has_shared = has_shared;
+  pa.counts = g.counts;
+  pa.slot = g.slot;
+  pa.offsets = g.offsets;
+  pa.units_up = g.units_up;
+  pa.units_down = g.units_down;
+  pa.n_units = g.n_units;
+  pa.mt_up = d.inter / 128;
+  pa.mt_down = d.hidden / 128;
+  pa.status = c->status;
+  CUtensorMap bup, bdown;
+  wh_status st;
+  if ((st = make_u8_map(&bup, g.xq, g.rows, d.hidden, 128, 128)) != WH_OK) return st;
+  if ((st = make_u8_map(&bdown, g.hq, g.rows, d.inter, 128, 128)) != WH_OK) return st;
+  GroupedArgs up{};
+  up.amaps = p->set.gmaps;
+  up.experts = p->set.experts;
+  up.K = d.hidden;
+  up.M = d.inter;
+  up.bsf = g.xsf;
+  up.rows_total = g.rows;
+  up.units = g.units_up;
+  up.n_units = g.n_units;
+  up.hq = g.hq;
+  up.hsf = g.hsf;
+  up.status = c->status;
+  GroupedArgs down = up;
+  down.K = d.inter;
+  down.M = d.hidden;
+  down.bsf = g.hsf;
+  down.units = g.units_down;
+  down.n_units = g.n_units + 1;
+  down.hq = nullptr;
+  down.hsf = nullptr;
+  down.y = g.yrows;
+  c->prof_begin();
+  if ((st = c->prof_mark(stream)) != WH_OK) return st;
+  WH_CUDA(cudaMemsetAsync(g.counts, 0, sizeof(int) * (d.num_experts + 1), stream));
+  WH_CUDA(launch_router_ex(r, nullptr, nullptr, stream, false));
+  if ((st = c->prof_mark(stream)) != WH_OK) return st;
+  WH_CUDA(launch_grouped_route(pa, x, d.hidden, g.xq, g.xsf, stream));
+  if ((st = c->prof_mark(stream)) != WH_OK) return st;
+  WH_CUDA(launch_grouped_gemm(true, bup, up, c->num_sms, stream));
+  if ((st = c->prof_mark(stream)) != WH_OK) return st;
+  WH_CUDA(launch_grouped_gemm(false, bdown, down, c->num_sms, stream));
+  if ((st = c->prof_mark(stream)) != WH_OK) return st;
+  WH_CUDA(launch_grouped_combine(pa, g.yrows, g.combine_w, x, y, d.hidden, stream));
+  return c->prof_mark(stream);
 }
 
 wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
@@ -705,6 +891,9 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   if (!x || !y || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
   if (!aligned(x, 16) || !aligned(scratch, 256))
     return fail(WH_ERR_INVALID_POINTER, "x must be 16-byte and scratch 256-byte aligned");
+  if (use_grouped(p, tokens))
+    return moe_ffn_grouped(c, p, x, tokens, hash_ids, y, ids_out, weights_out, scratch,
+                           scratch_bytes, stream);
   MoeScratch s = moe_scratch_layout(p, tokens, static_cast<uint8_t*>(scratch));
   if (scratch_bytes < s.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "moe scratch too small");
   const auto& d = p->d;

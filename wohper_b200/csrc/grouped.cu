@@ -1,0 +1,563 @@
+// grouped.cu -- batched MoE FFN (many tokens) on the 5th-generation tensor
+// cores: expert-major grouped GEMMs with block-scaled FP8 MMA.
+//
+// The reference processes a batch expert by expert, one matvec per
+// (token, expert) row (accumulate_expert_for_positions, src/compute.rs:1779-1810;
+// union in ascending expert id, src/server/generation.rs:2487-2569).  Here the
+// rows of each expert are gathered into one contiguous block and every
+// expert's w1/w3 and w2 run as GEMMs:
+//
+//   route (router_kernel) -> count + units -> dispatch (act quant of each token,
+//   scattered to its 7 expert rows) -> grouped up GEMM (w1, w3, SwiGLU, act
+//   quant of h) -> grouped down GEMM (w2) -> combine in ascending expert id.
+//
+// FP4 weights: the reference's E2M1 table has 0.125 at code 1, which the
+// hardware's OCP E2M1 decode (0.5) does not match, but every value of it is
+// exact in E4M3.  Converter warps therefore turn each FP4 tile into E4M3 in
+// shared memory and the MMA is kind::mxf8f6f4 with UE8M0 scales: the weight's
+// per-32 scale bytes as SFA, the activation's act-quant exponent as SFB.
+// Products are exact; the accumulation order is the tensor core's, so results
+// match the reference within floating-point tolerance (not bit for bit).
+#include <cuda_fp8.h>
+
+#include "tc.cuh"
+
+namespace wh {
+
+constexpr int kGroupedMinTokens = 32;  // wh_moe_ffn uses the grouped path from here on
+// K (hidden and inter) must be a multiple of 512: scale bytes are read 16 at a
+// time (4 K tiles of 128)
+constexpr int kGN = 128;        // tokens per tile (MMA N)
+constexpr int kGStages = 4;     // TMA ring depth (raw FP4 A + E4M3 B per K tile)
+constexpr int kGConv = 2;       // converted-A ring depth
+constexpr int kGThreads = 192;  // warps 0-3: convert + epilogue, 4: TMA, 5: MMA
+constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
+constexpr int kGConvA = 128 * 128;  // E4M3 A tile
+constexpr int kGB = kGN * 128;      // E4M3 B tile
+constexpr uint32_t kGTmemCols = 512;
+
+struct GroupedArgs {
+  const CUtensorMap* amaps;  // [experts][3] FP4 maps, box {64 B, 128 rows}
+  const Fp4ExpertDev* experts;
+  int K, M;                  // reduction length; rows of each weight matrix
+  const uint8_t* bsf;        // [rows][K/32] UE8M0 of the B rows
+  int rows_total;
+  const int4* units;         // (expert, m tile, first row, valid rows)
+  const int* n_units;
+  uint8_t* hq;               // up: [rows][M] E4M3 of act-quantised h
+  uint8_t* hsf;              // up: [rows][M/32] UE8M0
+  float* y;                  // down: [rows][M]
+  uint32_t* status;
+};
+
+template <bool kUp>
+struct GroupedSmem {
+  static constexpr int kRawStage = kGB + (kUp ? 2 : 1) * kGRawA;
+  static constexpr int kConvStage = (kUp ? 2 : 1) * kGConvA;
+  static constexpr int kSfStage = (kUp ? 3 : 2) * 512;
+  static constexpr size_t kBytes = 1024 + size_t(kGStages) * kRawStage +
+                                   size_t(kGConv) * kConvStage + size_t(kGConv) * kSfStage +
+                                   (2 * kGStages + 2 * kGConv + 5) * 8 + 16 + 2 * 4 * 16 * 4;
+};
+
+// 8 FP4 codes (one 32-bit word, code i in bits 4i..4i+3) -> 8 E4M3 bytes of
+// the reference values {0, 0.125, 1, 1.5, 2, 3, 4, 6} with the code's sign.
+__device__ __forceinline__ uint2 fp4x8_to_e4m3x8(uint32_t w) {
+  const uint32_t mag = w & 0x77777777u;
+  const uint32_t lo = __byte_perm(0x3C382000u, 0x4C484440u, mag);
+  const uint32_t hi = __byte_perm(0x3C382000u, 0x4C484440u, mag >> 16);
+  const uint32_t w4 = w << 4;
+  const uint32_t slo = __byte_perm(w4, w, 0x5140);  // sign of code i at bit 7 of byte i
+  const uint32_t shi = __byte_perm(w4, w, 0x7362);
+  return make_uint2(lo | (slo & 0x80808080u), hi | (shi & 0x80808080u));
+}
+
+// One FP4 tile [128 rows][64 B] -> E4M3 [128 rows][128 B], 128-byte swizzle.
+__device__ __forceinline__ void convert_tile(const uint8_t* raw, uint8_t* dst, int tid) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = tid + 128 * j;
+    const int r = i >> 2, ch = i & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 64 + ch * 16);
+    const uint2 a = fp4x8_to_e4m3x8(v.x), b = fp4x8_to_e4m3x8(v.y);
+    const uint2 c = fp4x8_to_e4m3x8(v.z), d = fp4x8_to_e4m3x8(v.w);
+    uint8_t* row = dst + r * 128;
+    *reinterpret_cast<uint4*>(row + (((2 * ch) ^ (r & 7)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+    *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ (r & 7)) << 4)) =
+        make_uint4(c.x, c.y, d.x, d.y);
+  }
+}
+
+// ceil(log2f(q)) through the act-quant threshold table (shared-memory copy)
+__device__ __forceinline__ int ceil_log2f_thr(float q, const uint32_t* thr) {
+  const uint32_t u = __float_as_uint(q);
+  const uint32_t E = (u >> 23) & 0xFF, m = u & 0x7FFFFF;
+  const int k = int(E) - 127;
+  return (m == 0 || m < thr[E]) ? k : k + 1;
+}
+// byte k of a 16-byte group (k warp-uniform or not, no local memory)
+__device__ __forceinline__ uint32_t pick4(const uint4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ uint8_t e4m3_byte(float q) {
+  return (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
+}
+
+template <bool kUp>
+__global__ void __launch_bounds__(kGThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap bmap, GroupedArgs a) {
+  using L = GroupedSmem<kUp>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint8_t* raw = smem;                                        // [stages][B | A1 | A3]
+  uint8_t* conv = raw + kGStages * L::kRawStage;              // [conv][A1 | A3]
+  uint8_t* sfs = conv + kGConv * L::kConvStage;               // [conv][SFA1 | SFA3 | SFB]
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sfs + kGConv * L::kSfStage);
+  uint64_t* raw_empty = raw_full + kGStages;
+  uint64_t* conv_full = raw_empty + kGStages;
+  uint64_t* conv_empty = conv_full + kGConv;
+  uint64_t* acc_full = conv_empty + kGConv;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint64_t* pair_bar = mma_done + 1;  // [2]: warps 0+1, warps 2+3 (act-quant amax exchange)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + 2);
+  float* amax_s = reinterpret_cast<float*>(tmem_base_s + 4);  // [2 parity][4 warps][16]
+
+  __shared__ uint32_t aq_thr[256];  // act-quant ceil(log2f) thresholds
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ktiles = a.K / 128;
+  constexpr int kMats = kUp ? 2 : 1;
+  for (int i = tid; i < 256; i += kGThreads) aq_thr[i] = c_aq.thr[i];
+
+  if (tid == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 5);
+    }
+    for (int c = 0; c < kGConv; ++c) {
+      mbar_init(&conv_full[c], 4);
+      mbar_init(&conv_empty[c], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(mma_done, 1);
+    mbar_init(&pair_bar[0], 64);
+    mbar_init(&pair_bar[1], 64);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_s, kGTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+  const int n_units = *a.n_units;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t g = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const int4 un = a.units[u];
+        const CUtensorMap* m1 = a.amaps + un.x * 3 + (kUp ? 0 : 2);
+        const CUtensorMap* m3 = a.amaps + un.x * 3 + 1;
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          const int s = g % kGStages;
+          if (g >= kGStages && !mbar_wait(&raw_empty[s], ((g / kGStages) - 1) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = raw + s * L::kRawStage;
+          mbar_arrive_expect_tx(&raw_full[s], kGB + kMats * kGRawA);
+          tma_load_2d(st, &bmap, &raw_full[s], kt * 128, un.z);
+          tma_load_2d(st + kGB, m1, &raw_full[s], kt * 64, un.y * 128);
+          if (kUp) tma_load_2d(st + kGB + kGRawA, m3, &raw_full[s], kt * 64, un.y * 128);
+        }
+      }
+      // no copy may be in flight when the CTA exits
+      for (uint32_t i = g > kGStages ? g - kGStages : 0; i < g; ++i)
+        mbar_wait(&raw_full[i % kGStages], (i / kGStages) & 1, a.status);
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t g = 0, gc = 0, nu = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
+        if (nu > 0 && !mbar_wait(acc_empty, (nu - 1) & 1, a.status)) break;
+        tc::fence_after_sync();
+        for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
+          const int s = g % kGStages, c = gc % kGConv;
+          if (!mbar_wait(&conv_full[c], (gc / kGConv) & 1, a.status) ||
+              !mbar_wait(&raw_full[s], (g / kGStages) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t tsf = tmem + 2 * kGN + 16 * c;
+          const uint8_t* sf = sfs + c * L::kSfStage;
+          tc::cp_sf_block(tsf, tc::desc_sf_block(smem_u32(sf)));
+          if (kUp) tc::cp_sf_block(tsf + 4, tc::desc_sf_block(smem_u32(sf + 512)));
+          const uint32_t tsfb = tsf + 8;
+          tc::cp_sf_block(tsfb, tc::desc_sf_block(smem_u32(sf + (kUp ? 1024 : 512))));
+          const uint8_t* bt = raw + s * L::kRawStage;
+          const uint8_t* ct = conv + c * L::kConvStage;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (kt | k) != 0;
+            const uint32_t id = tc::idesc_mxf8(kGN, k, k);
+            const uint64_t db = tc::desc_sw128(smem_u32(bt + 32 * k));
+            tc::mma_mxf8(tmem, tc::desc_sw128(smem_u32(ct + 32 * k)), db, id,
+                         tsf | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
+            if (kUp)
+              tc::mma_mxf8(tmem + kGN, tc::desc_sw128(smem_u32(ct + kGConvA + 32 * k)), db, id,
+                           (tsf + 4) | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
+          }
+          tc::commit(&conv_empty[c]);
+          tc::commit(&raw_empty[s]);
+        }
+        if (ok) tc::commit(acc_full);
+      }
+      // every MMA and scale copy has finished before TMEM is released
+      tc::commit(mma_done);
+      mbar_wait(mma_done, 0, a.status);
+    }
+  } else {
+    // ---------------- converters + epilogue (warps 0-3, TMEM lanes 32w..) ----
+    bool ok = true;
+    uint32_t g = 0, gc = 0, nu = 0, chunk = 0;
+    const int r = tid;  // A row / B row this thread stages scale factors for
+    const int sfk = a.K / 32;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
+      const int4 un = a.units[u];
+      const Fp4ExpertDev& ex = a.experts[un.x];
+      const uint8_t* sfa1 = (kUp ? ex.w1_scale : ex.w2_scale) + (long long)(un.y * 128 + r) * sfk;
+      const uint8_t* sfa3 = ex.w3_scale + (long long)(un.y * 128 + r) * sfk;
+      const bool brow_ok = un.z + r < a.rows_total;
+      const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * sfk;
+      // scale bytes of 4 K tiles per 16-byte load, one group ahead
+      auto sf_group = [&](int kt0, uint4& qa1, uint4& qa3, uint4& qb) {
+        qa1 = __ldg(reinterpret_cast<const uint4*>(sfa1 + kt0 * 4));
+        qa3 = kUp ? __ldg(reinterpret_cast<const uint4*>(sfa3 + kt0 * 4)) : make_uint4(0, 0, 0, 0);
+        qb = brow_ok ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
+                     : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+      };
+      uint4 ca1, ca3, cb, na1, na3, nb;
+      sf_group(0, na1, na3, nb);
+      for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
+        const int s = g % kGStages, c = gc % kGConv;
+        if ((kt & 3) == 0) {
+          ca1 = na1;
+          ca3 = na3;
+          cb = nb;
+          if (kt + 4 < ktiles) sf_group(kt + 4, na1, na3, nb);
+        }
+        const uint32_t va1 = pick4(ca1, kt & 3);
+        const uint32_t va3 = pick4(ca3, kt & 3);
+        const uint32_t vb = pick4(cb, kt & 3);
+        if (!mbar_wait(&raw_full[s], (g / kGStages) & 1, a.status) ||
+            (gc >= kGConv && !mbar_wait(&conv_empty[c], ((gc / kGConv) - 1) & 1, a.status))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* st = raw + s * L::kRawStage;
+        uint8_t* ct = conv + c * L::kConvStage;
+        convert_tile(st + kGB, ct, tid);
+        if (kUp) convert_tile(st + kGB + kGRawA, ct + kGConvA, tid);
+        uint8_t* sf = sfs + c * L::kSfStage;
+        const int atom = (r & 31) * 16 + (r >> 5) * 4;
+        *reinterpret_cast<uint32_t*>(sf + atom) = va1;
+        if (kUp) *reinterpret_cast<uint32_t*>(sf + 512 + atom) = va3;
+        *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = vb;
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&conv_full[c]);
+          mbar_arrive(&raw_empty[s]);
+        }
+      }
+      // ---------------- epilogue ----------------
+      if (ok) ok = mbar_wait(acc_full, nu & 1, a.status);
+      if (!ok) break;
+      tc::fence_after_sync();
+      const int feat = un.y * 128 + warp * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+      for (int n0 = 0; n0 < kGN; n0 += 16) {
+        uint32_t v1[16];
+        tc::ld_32x32b_x16(trow + n0, v1);
+        if (kUp) {
+          uint32_t v3[16];
+          tc::ld_32x32b_x16(trow + kGN + n0, v3);
+          tc::wait_ld();
+          float h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            // SwiGLU with the reference clamps (src/deepseek_v4.rs:589-593)
+            const float gte = fminf(__uint_as_float(v1[j]), 10.0f);
+            const float upv = fminf(fmaxf(__uint_as_float(v3[j]), -10.0f), 10.0f);
+            h[j] = gte / (1.0f + expf(-gte)) * upv;
+          }
+          // act quant of h over 64 features (two warps) per token
+          float am[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float m = fabsf(h[j]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            am[j] = m;
+          }
+          float* xs_amax = amax_s + (chunk & 1) * 64;
+          if (lane < 16) {
+            float mine = am[0];
+#pragma unroll
+            for (int j = 1; j < 16; ++j)
+              if (lane == j) mine = am[j];
+            xs_amax[warp * 16 + lane] = mine;
+          }
+          mbar_arrive(&pair_bar[warp >> 1]);
+          if (!mbar_wait(&pair_bar[warp >> 1], chunk & 1, a.status)) ok = false;
+          ++chunk;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float m = fmaxf(fmaxf(am[j], xs_amax[(warp ^ 1) * 16 + j]), 1.0e-4f);
+            const int k = ceil_log2f_thr(__fdiv_rn(m, 448.0f), aq_thr);
+            // h / 2^k == h * 2^-k exactly; clamp and round as aq_grid does
+            float t = __fmul_rn(h[j], exp2i(-k));
+            t = t < -448.0f ? -448.0f : t;
+            t = t > 448.0f ? 448.0f : t;
+            const float q = e4m3_nearest_ties_lower(t);
+            const int row = un.z + n0 + j;
+            if (n0 + j < un.w) {
+              a.hq[(long long)row * a.M + feat] = e4m3_byte(q);
+              if ((warp & 1) == 0 && lane < 2)
+                a.hsf[(long long)row * (a.M / 32) + (un.y * 128 + warp * 32) / 32 + lane] =
+                    (uint8_t)(k + 127);
+            }
+          }
+        } else {
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n0 + j < un.w) a.y[(long long)(un.z + n0 + j) * a.M + feat] = __uint_as_float(v1[j]);
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, kGTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// routing bookkeeping
+// ---------------------------------------------------------------------------
+struct GroupedPlanArgs {
+  const int32_t* ids;  // [T][topk]
+  int tokens, topk, num_experts, has_shared;
+  int* counts;         // [experts + 1], zeroed before the count kernel
+  int* slot;           // [T][topk] row of (t, k) within its expert
+  int* offsets;        // [experts + 2] first row of each expert (shared = experts)
+  int4* units_up;      // (expert, m tile, first row, valid rows)
+  int4* units_down;
+  int* n_units;        // [2]
+  int mt_up, mt_down;  // 128-row tiles of inter / hidden
+  uint32_t* status;
+};
+
+__global__ void grouped_count_kernel(GroupedPlanArgs a) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.tokens * a.topk) return;
+  const int e = a.ids[i];
+  if (e < 0 || e >= a.num_experts) {
+    flag(a.status, WH_DEV_BADARG);
+    a.slot[i] = -1;
+    return;
+  }
+  a.slot[i] = atomicAdd(&a.counts[e], 1);
+}
+
+// One CTA: exclusive scans of rows and tiles over the experts, then the unit
+// lists (expert-major so that CTAs running together share B rows).
+__global__ void __launch_bounds__(1024) grouped_units_kernel(GroupedPlanArgs a) {
+  __shared__ int tiles_s[1025];
+  __shared__ int rows_s[1025];
+  const int ne = a.num_experts + a.has_shared;
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    const int n = e < a.num_experts ? a.counts[e] : a.tokens;
+    rows_s[e] = n;
+    tiles_s[e] = (n + kGN - 1) / kGN;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int row = 0, tile = 0;
+    for (int e = 0; e < ne; ++e) {
+      const int n = rows_s[e], t = tiles_s[e];
+      rows_s[e] = row;
+      tiles_s[e] = tile;
+      a.offsets[e] = row;
+      row += n;
+      tile += t;
+    }
+    a.offsets[ne] = row;
+    a.n_units[0] = tile * a.mt_up;
+    a.n_units[1] = tile * a.mt_down;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    const int n = a.offsets[e + 1] - a.offsets[e];
+    const int nt = (n + kGN - 1) / kGN;
+    for (int t = 0; t < nt; ++t) {
+      const int row0 = a.offsets[e] + t * kGN;
+      const int nv = min(kGN, n - t * kGN);
+      const int u = tiles_s[e] + t;
+      for (int m = 0; m < a.mt_up; ++m) a.units_up[u * a.mt_up + m] = make_int4(e, m, row0, nv);
+      for (int m = 0; m < a.mt_down; ++m)
+        a.units_down[u * a.mt_down + m] = make_int4(e, m, row0, nv);
+    }
+  }
+}
+
+// Act quant of each token (src/compute.rs:2504-2545, block 64) written as E4M3
+// bytes + UE8M0 exponents to the token's rows of every expert it routes to.
+__global__ void __launch_bounds__(128) grouped_dispatch_kernel(GroupedPlanArgs a, const float* x,
+                                                               int hidden, uint8_t* xq,
+                                                               uint8_t* xsf) {
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int rows[33];
+  if (threadIdx.x < a.topk) {
+    const int i = t * a.topk + threadIdx.x;
+    const int e = a.ids[i];
+    rows[threadIdx.x] = (e >= 0 && e < a.num_experts && a.slot[i] >= 0) ? a.offsets[e] + a.slot[i]
+                                                                         : -1;
+  }
+  if (threadIdx.x == 0) rows[a.topk] = a.has_shared ? a.offsets[a.num_experts] + t : -1;
+  __syncthreads();
+  const int nrows = a.topk + 1;
+  const float* xt = x + (long long)t * hidden;
+  for (int blk = warp; blk < hidden / 64; blk += 4) {
+    const float v0 = xt[blk * 64 + 2 * lane], v1 = xt[blk * 64 + 2 * lane + 1];
+    float amax = fmaxf(fabsf(v0), fabsf(v1));
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    amax = fmaxf(amax, 1.0e-4f);
+    const int k = ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq);
+    const float sc = exp2i(k);
+    const uint32_t b2 = uint32_t(e4m3_byte(aq_grid(v0, sc))) | uint32_t(e4m3_byte(aq_grid(v1, sc))) << 8;
+    for (int j = 0; j < nrows; ++j) {
+      const int row = rows[j];
+      if (row < 0) continue;
+      reinterpret_cast<uint16_t*>(xq + (long long)row * hidden + blk * 64)[lane] = (uint16_t)b2;
+      if (lane < 2) xsf[(long long)row * (hidden / 32) + blk * 2 + lane] = (uint8_t)(k + 127);
+    }
+  }
+}
+
+// y[t] = shared(x_t) + sum over t's experts in ascending id of y_e * w/sum(w)
+// (finish of the batched path, src/compute.rs:1817-1870 with the union order of
+// src/server/generation.rs:2487-2569).
+__global__ void __launch_bounds__(256) grouped_combine_kernel(GroupedPlanArgs a, const float* yrows,
+                                                              const float* combine_w, const float* x,
+                                                              float* y, int hidden) {
+  const int t = blockIdx.x;
+  __shared__ int rows[33];
+  __shared__ float ws[33];
+  if (threadIdx.x == 0) {
+    int n = 0;
+    // insertion order by expert id ascending
+    int ids[32];
+    for (int k = 0; k < a.topk; ++k) {
+      const int i = t * a.topk + k;
+      const int e = a.ids[i];
+      if (e < 0 || e >= a.num_experts || a.slot[i] < 0) continue;
+      int p = n++;
+      while (p > 0 && ids[p - 1] > e) {
+        ids[p] = ids[p - 1];
+        rows[p] = rows[p - 1];
+        ws[p] = ws[p - 1];
+        --p;
+      }
+      ids[p] = e;
+      rows[p] = a.offsets[e] + a.slot[i];
+      ws[p] = combine_w[i];
+    }
+    rows[32] = n;
+  }
+  __syncthreads();
+  const int n = rows[32];
+  const long long sh = a.has_shared ? (long long)(a.offsets[a.num_experts] + t) * hidden : -1;
+  for (int h = threadIdx.x; h < hidden; h += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < n; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(yrows[(long long)rows[j] * hidden + h], ws[j]));
+    float out;
+    if (n > 0)
+      out = sh >= 0 ? __fadd_rn(yrows[sh + h], acc) : acc;
+    else
+      out = sh >= 0 ? yrows[sh + h] : x[(long long)t * hidden + h];
+    y[(long long)t * hidden + h] = out;
+  }
+}
+
+// Any UE8M0 scale byte equal to 0 or 255 in any expert matrix -> *flag = 1.
+__global__ void grouped_scale_check_kernel(const Fp4ExpertDev* ex, int hidden, int inter,
+                                           uint32_t* flag) {
+  const Fp4ExpertDev& e = ex[blockIdx.y];
+  const uint8_t* p = blockIdx.z == 0 ? e.w1_scale : blockIdx.z == 1 ? e.w3_scale : e.w2_scale;
+  const long long n4 = (long long)hidden * inter / 32 / 4;
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+  bool bad = false;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t v = q[i];
+    bad |= (((v - 0x01010101u) & ~v & 0x80808080u) | ((~v - 0x01010101u) & v & 0x80808080u)) != 0;
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u);
+}
+
+cudaError_t launch_scale_check(const Fp4ExpertDev* ex, int n, int hidden, int inter,
+                               uint32_t* flag, cudaStream_t s) {
+  grouped_scale_check_kernel<<<dim3(16, n, 3), 256, 0, s>>>(ex, hidden, inter, flag);
+  return cudaGetLastError();
+}
+
+size_t grouped_smem_bytes(bool up) {
+  return up ? GroupedSmem<true>::kBytes : GroupedSmem<false>::kBytes;
+}
+
+cudaError_t launch_grouped_gemm(bool up, const CUtensorMap& bmap, const GroupedArgs& a, int num_sms,
+                                cudaStream_t s) {
+  const size_t smem = grouped_smem_bytes(up);
+  cudaError_t e = up ? ensure_smem(grouped_gemm_kernel<true>, smem)
+                     : ensure_smem(grouped_gemm_kernel<false>, smem);
+  if (e != cudaSuccess) return e;
+  if (up)
+    grouped_gemm_kernel<true><<<num_sms, kGThreads, smem, s>>>(bmap, a);
+  else
+    grouped_gemm_kernel<false><<<num_sms, kGThreads, smem, s>>>(bmap, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grouped_route(const GroupedPlanArgs& p, const float* x, int hidden,
+                                 uint8_t* xq, uint8_t* xsf, cudaStream_t s) {
+  const int n = p.tokens * p.topk;
+  grouped_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+  grouped_units_kernel<<<1, 1024, 0, s>>>(p);
+  grouped_dispatch_kernel<<<p.tokens, 128, 0, s>>>(p, x, hidden, xq, xsf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grouped_combine(const GroupedPlanArgs& p, const float* yrows,
+                                   const float* combine_w, const float* x, float* y, int hidden,
+                                   cudaStream_t s) {
+  grouped_combine_kernel<<<p.tokens, 256, 0, s>>>(p, yrows, combine_w, x, y, hidden);
+  return cudaGetLastError();
+}
+
+}  // namespace wh

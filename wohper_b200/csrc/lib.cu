@@ -2,5 +2,6 @@
 // __constant__ act-quant table and every kernel in one module, no -rdc).
 #include "fp8_gemv.cu"
 #include "moe.cu"
+#include "grouped.cu"
 #include "capi.cu"
 #include "noalloc.cu"
