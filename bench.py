@@ -428,6 +428,174 @@ def run_reference(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# config 3: batched (prefill) MoE FFN on the tensor cores
+# ---------------------------------------------------------------------------
+T3 = 2048
+METRIC3 = "prefill tokens/s (batched FP4 MoE FFN, config 3)"
+WORKLOAD3 = ("config 3: 2048 tokens through the FP4 MoE FFN, 256 experts + shared, "
+             "4096->2048->4096, Zipf(1.1)-skewed top-6 routing, grouped block-scaled GEMMs")
+W13_BYTES = 2 * (PACKED_W13 + SCALES_W13)   # w1 + w3 of one expert
+W2_BYTES = PACKED_W2 + SCALES_W2
+
+
+def config3_inputs(H, seed):
+    gate, x = H.zipf_routing(seed + 9, H.router_gate(seed + 6, E, HID),
+                             H.activations(seed + 7, T3, HID))
+    return gate, x
+
+
+def config3_cpu(T_sample: int, seed: int, threads_all: bool):
+    """Oracle (the reference's CPU kernels restated) on T_sample tokens of the
+    config-3 workload: exact router per token, then the expert-major batched
+    path.  Returns (tokens/s, threads)."""
+    import oracle as O
+    from tests import helpers as H
+
+    if threads_all:
+        O.set_threads(os.cpu_count() or 1)
+    gate, x = config3_inputs(H, seed)
+    x = x[:T_sample]
+    model = HostModel(seed)
+    model.gate = gate
+    t0 = time.perf_counter()
+    ids = np.zeros((T_sample, TOPK), np.int32)
+    ws = np.zeros((T_sample, TOPK), np.float32)
+    for t in range(T_sample):
+        _, ids[t], ws[t], _ = O.router(gate, x[t], TOPK, mode=0)
+    t_route = time.perf_counter() - t0
+    arr = (O.Fp4Expert * (E + 1))()
+    for e in set(ids.reshape(-1).tolist()) | {E}:
+        arr[e] = model.expert(int(e))  # generated untimed
+    t1 = time.perf_counter()
+    st, _ = O.moe_batched(arr, E, ids, ws, arr[E], x)
+    dt = t_route + time.perf_counter() - t1
+    assert st == O.OK
+    return T_sample / dt, O.threads()
+
+
+def run_config3(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    import wohper_b200 as W
+    from tests import helpers as H
+
+    dev = torch.device("cuda", local)
+    ctx = W.Context(local)
+    stack = H.torch_fp4_experts(1000 + rank, E + 1, HID, INTER, device=dev)
+    gate_np, x_np = config3_inputs(H, 1000 + rank)
+
+    def wexp(e):
+        w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+        return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+    layer = W.MoeLayer(ctx, [wexp(e) for e in range(E)], wexp(E),
+                       torch.from_numpy(gate_np.view(np.int16)).to(dev), topk=TOPK,
+                       max_tokens=T3)
+    x = torch.from_numpy(x_np).to(dev)
+    y = torch.empty_like(x)
+    ids = torch.zeros(T3, TOPK, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        flush.zero_()
+        layer.forward(x, y, ids=ids)
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            flush.zero_()
+            ev[k][0].record(stream)
+            layer.forward(x, y, ids=ids)
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ctx.sync()
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    counts = np.bincount(ids.cpu().numpy().reshape(-1), minlength=E)
+    used = int((counts > 0).sum()) + 1  # + shared
+    R = T3 * TOPK + T3
+    # per-kernel times (events between kernels)
+    ctx.set_profiling(True)
+    phases = []
+    for _ in range(3):
+        flush.zero_()
+        layer.forward(x, y, ids=ids)
+        phases.append(ctx.phase_times())
+    ctx.set_profiling(False)
+    ctx.sync()
+    ph = np.array(phases).mean(0)  # router, route+dispatch, up, down, combine
+    up_ms, down_ms = float(ph[2]), float(ph[3])
+    up_bytes = used * W13_BYTES + R * HID + R * INTER + R * (HID + INTER) // 32
+    up_flops = 2.0 * R * 2 * INTER * HID
+    peak, peak_kind = peaks()
+    up_gbs = up_bytes / (up_ms * 1e-3) / 1e9
+    step_flops = 2.0 * R * 3 * INTER * HID
+    # end to end: pinned host tokens -> H2D -> wh_moe_ffn -> D2H
+    xh = torch.from_numpy(x_np).pin_memory()
+    yh = torch.empty(T3, HID).pin_memory()
+    xd = torch.empty_like(x)
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for k in range(args.steps):
+        flush.zero_()
+        ev2[k][0].record(stream)
+        xd.copy_(xh, non_blocking=True)
+        layer.forward(xd, y)
+        yh.copy_(y, non_blocking=True)
+        ev2[k][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC3, "value": round(world * T3 / (ms_step * 1e-3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp4-e2m1 (as e4m3) x fp8-e4m3, ue8m0 block scales, f32 accumulate",
+            "data": "synthetic (seeded random-init weights, N(0,1) tokens, Zipf prior on routing)",
+            "config": {"workload": WORKLOAD3, "experts": E, "topk": TOPK, "hidden": HID,
+                       "inter": INTER, "tokens": T3, "experts_used": used,
+                       "max_expert_rows": int(counts.max()), "rows": R,
+                       "l2": "flushed between steps (256 MiB memset outside the timed events)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "phases_ms": {"router": round(float(ph[0]), 4), "route_dispatch": round(float(ph[1]), 4),
+                          "up": round(up_ms, 4), "down": round(down_ms, 4),
+                          "combine": round(float(ph[4]), 4)},
+            "roofline": {"kernel": "grouped_gemm_kernel<up> (w1+w3 of the used experts, SwiGLU, act quant)",
+                         "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
+                         "algorithmic_bytes": int(up_bytes), "traffic": None,
+                         "tensor_tflops": round(up_flops / (up_ms * 1e-3) / 1e12, 1)},
+            "step_tflops": round(step_flops / (ms_step * 1e-3) / 1e12, 1),
+            "e2e": {"value": round(world * T3 / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": T3 * HID * 4,
+                    "d2h_bytes_per_step": T3 * HID * 4,
+                    "path": "pinned host x -> H2D -> wh_moe_ffn (C ABI) -> D2H y"},
+            "gpu_launches": 7 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            v, th = config3_cpu(16, 1000, threads_all=False)
+            res["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": th,
+                                   "kind": "port",
+                                   "sample": "16 tokens of the same workload: exact router + "
+                                             "expert-major batched path of the C++ restatement"}
+    layer.close()
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res
+
+
 def run_ncu_case(args):
     """Small single-GPU workloads for ncu captures (no JSON bench line).
 
@@ -435,6 +603,9 @@ def run_ncu_case(args):
     moe16: the config-2 MoE FFN step with 16 routed experts instead of 256
            (220 MB of weights; the kernels read the same 7 experts' bytes per
            token as at 256), router + moe_up + moe_down per step.
+    grouped16: the config-3 batched path at 256 tokens and 16 experts (plus
+           the shared one) of the config shape: router, dispatch, grouped up
+           and down GEMMs, combine per step.
     L2 is flushed (256 MiB memset) before every step."""
     import torch
 
@@ -451,6 +622,25 @@ def run_ncu_case(args):
         for _ in range(n):
             flush.zero_()
             W.gemv_fp8_e4m3_ue8m0_tensorwise(ctx, wd, sd, x)
+    elif args.ncu_case == "grouped16":
+        ne, T = 16, 256
+        stack = H.torch_fp4_experts(5, ne + 1, HID, INTER)
+        gate, xs = H.zipf_routing(9, H.router_gate(6, ne, HID), H.activations(7, T, HID))
+
+        def wexp(e):
+            w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+            return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+        layer = W.MoeLayer(ctx, [wexp(e) for e in range(ne)], wexp(ne),
+                           torch.from_numpy(gate.view(np.int16)).cuda(), topk=TOPK, max_tokens=T)
+        x = torch.from_numpy(xs).cuda()
+        y = torch.empty_like(x)
+        for i in range(n):
+            flush.zero_()
+            layer.forward(x, y)
+        layer.close()
     else:
         ne = 16
         stack = H.torch_fp4_experts(5, ne + 1, HID, INTER)
@@ -482,14 +672,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ncu-case", choices=["fp8", "moe16"],
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3],
+                    help="2: one-token decode FFN (default); 3: 2048-token batched FFN")
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case(args)
         return
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
-    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.config == 3 and args.impl == "ours":
+        res = run_config3(args)
+    else:
+        res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
         print(json.dumps(res), flush=True)
 

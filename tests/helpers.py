@@ -85,11 +85,14 @@ def max_rel_err(got: np.ndarray, ref: np.ndarray, floor: float = 1e-6) -> float:
 
 
 def zipf_routing(seed: int, gate_bits: np.ndarray, x: np.ndarray, s: float = 1.1,
-                 strength: float = 1.4):
+                 strength: float = 0.7):
     """Zipf-skewed routing for raw-logit top-k: hidden column 0 of every token
     is set to 1.0 and gate column 0 to the prior -strength * s * ln(rank) over a
     seeded permutation of the experts, so logit_e = gate_e . x + prior_e and the
-    per-expert token counts become uneven (popular experts, empty ones).
+    per-expert token counts become uneven (popular experts, empty ones).  With
+    the N(0, 0.02) gate (logit std 1.28 at hidden 4096), strength 0.7 gives
+    counts close to Zipf(1.1) for 2048 tokens x top-6 over 256 experts
+    (largest ~1300, 10th ~280, 100th ~15, a few experts with none).
     Returns (gate_bits, x) copies."""
     g = gate_bits.copy()
     x = x.copy()

@@ -103,7 +103,8 @@ def test_grouped_uneven_groups_multi_tile_and_empty(ctx, W):
     # some get none
     E, Hd, I, T = 48, 1024, 512, 320
     stack = H.torch_fp4_experts(74, E + 1, Hd, I)
-    gate, x = H.zipf_routing(75, H.router_gate(76, E, Hd), H.activations(77, T, Hd))
+    gate, x = H.zipf_routing(75, H.router_gate(76, E, Hd), H.activations(77, T, Hd),
+                            strength=1.4)
     layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
     try:
         counts = _check(ctx, layer, stack, gate, x, E, Hd, I)
@@ -129,7 +130,8 @@ def test_grouped_v4_shape(ctx, W):
     # DeepSeek-V4-Flash expert shape (4096 -> 2048 -> 4096), 64 experts
     E, Hd, I, T = 64, 4096, 2048, 96
     stack = H.torch_fp4_experts(81, E + 1, Hd, I)
-    gate, x = H.zipf_routing(82, H.router_gate(83, E, Hd), H.activations(84, T, Hd))
+    gate, x = H.zipf_routing(82, H.router_gate(83, E, Hd), H.activations(84, T, Hd),
+                            strength=1.4)
     layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
     try:
         _check(ctx, layer, stack, gate, x, E, Hd, I)

@@ -30,7 +30,8 @@ constexpr int kGroupedMinTokens = 32;  // wh_moe_ffn uses the grouped path from 
 constexpr int kGN = 128;        // tokens per tile (MMA N)
 constexpr int kGStages = 4;     // TMA ring depth (raw FP4 A + E4M3 B per K tile)
 constexpr int kGConv = 2;       // converted-A ring depth
-constexpr int kGThreads = 192;  // warps 0-3: convert + epilogue, 4: TMA, 5: MMA
+constexpr int kGWork = 8;       // converter + epilogue warps
+constexpr int kGThreads = (kGWork + 2) * 32;  // + TMA producer warp + MMA warp
 constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
 constexpr int kGConvA = 128 * 128;  // E4M3 A tile
 constexpr int kGB = kGN * 128;      // E4M3 B tile
@@ -57,7 +58,7 @@ struct GroupedSmem {
   static constexpr int kSfStage = (kUp ? 3 : 2) * 512;
   static constexpr size_t kBytes = 1024 + size_t(kGStages) * kRawStage +
                                    size_t(kGConv) * kConvStage + size_t(kGConv) * kSfStage +
-                                   (2 * kGStages + 2 * kGConv + 5) * 8 + 16 + 2 * 4 * 16 * 4;
+                                   (2 * kGStages + 2 * kGConv + 7) * 8 + 16 + 2 * kGWork * 16 * 4;
 };
 
 // 8 FP4 codes (one 32-bit word, code i in bits 4i..4i+3) -> 8 E4M3 bytes of
@@ -72,11 +73,12 @@ __device__ __forceinline__ uint2 fp4x8_to_e4m3x8(uint32_t w) {
   return make_uint2(lo | (slo & 0x80808080u), hi | (shi & 0x80808080u));
 }
 
-// One FP4 tile [128 rows][64 B] -> E4M3 [128 rows][128 B], 128-byte swizzle.
+// Two of the 512 16-byte chunks of an FP4 tile [128 rows][64 B] -> E4M3
+// [128 rows][128 B] with 128-byte swizzle (256 threads cover the tile).
 __device__ __forceinline__ void convert_tile(const uint8_t* raw, uint8_t* dst, int tid) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int i = tid + 128 * j;
+  for (int j = 0; j < 2; ++j) {
+    const int i = tid + 256 * j;
     const int r = i >> 2, ch = i & 3;
     const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 64 + ch * 16);
     const uint2 a = fp4x8_to_e4m3x8(v.x), b = fp4x8_to_e4m3x8(v.y);
@@ -95,13 +97,19 @@ __device__ __forceinline__ int ceil_log2f_thr(float q, const uint32_t* thr) {
   const int k = int(E) - 127;
   return (m == 0 || m < thr[E]) ? k : k + 1;
 }
-// byte k of a 16-byte group (k warp-uniform or not, no local memory)
+// word k of a 16-byte group without local memory
 __device__ __forceinline__ uint32_t pick4(const uint4& v, int k) {
   return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
 }
 
 __device__ __forceinline__ uint8_t e4m3_byte(float q) {
   return (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
+}
+// two values -> E4M3 bytes, round to nearest even, saturated to +-448
+__device__ __forceinline__ uint32_t e4m3x2_rn(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 template <bool kUp>
@@ -120,11 +128,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint64_t* acc_full = conv_empty + kGConv;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
-  uint64_t* pair_bar = mma_done + 1;  // [2]: warps 0+1, warps 2+3 (act-quant amax exchange)
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + 2);
-  float* amax_s = reinterpret_cast<float*>(tmem_base_s + 4);  // [2 parity][4 warps][16]
-
+  uint64_t* pair_bar = mma_done + 1;  // [4]: warps 2p and 2p+1 (act-quant amax exchange)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + 4);
+  float* amax_s = reinterpret_cast<float*>(tmem_base_s + 4);  // [2 parity][8 warps][16]
   __shared__ uint32_t aq_thr[256];  // act-quant ceil(log2f) thresholds
+
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ktiles = a.K / 128;
   constexpr int kMats = kUp ? 2 : 1;
@@ -133,17 +141,16 @@ __global__ void __launch_bounds__(kGThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kGStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 5);
+      mbar_init(&raw_empty[s], kGWork + 1);
     }
     for (int c = 0; c < kGConv; ++c) {
-      mbar_init(&conv_full[c], 4);
+      mbar_init(&conv_full[c], kGWork);
       mbar_init(&conv_empty[c], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, kGWork);
     mbar_init(mma_done, 1);
-    mbar_init(&pair_bar[0], 64);
-    mbar_init(&pair_bar[1], 64);
+    for (int p = 0; p < 4; ++p) mbar_init(&pair_bar[p], 64);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -156,7 +163,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const uint32_t tmem = *tmem_base_s;
   const int n_units = *a.n_units;
 
-  if (warp == 4) {
+  if (warp == kGWork) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       bool ok = true;
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       for (uint32_t i = g > kGStages ? g - kGStages : 0; i < g; ++i)
         mbar_wait(&raw_full[i % kGStages], (i / kGStages) & 1, a.status);
     }
-  } else if (warp == 5) {
+  } else if (warp == kGWork + 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
@@ -227,38 +234,38 @@ __global__ void __launch_bounds__(kGThreads, 1)
       mbar_wait(mma_done, 0, a.status);
     }
   } else {
-    // ---------------- converters + epilogue (warps 0-3, TMEM lanes 32w..) ----
+    // ------- converters + epilogue: warp w reads TMEM lanes 32*(w%4).., -------
+    // ------- columns [64*(w/4), +64) of the accumulators                  -------
     bool ok = true;
     uint32_t g = 0, gc = 0, nu = 0, chunk = 0;
-    const int r = tid;  // A row / B row this thread stages scale factors for
+    // scale factors: threads 0-127 stage SFA1 (+ SFB) of row tid, threads
+    // 128-255 stage SFA3 of row tid-128
+    const int r = tid & 127;
+    const bool second = tid >= 128;
     const int sfk = a.K / 32;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
       const int4 un = a.units[u];
       const Fp4ExpertDev& ex = a.experts[un.x];
-      const uint8_t* sfa1 = (kUp ? ex.w1_scale : ex.w2_scale) + (long long)(un.y * 128 + r) * sfk;
-      const uint8_t* sfa3 = ex.w3_scale + (long long)(un.y * 128 + r) * sfk;
+      const uint8_t* sfa = (second ? ex.w3_scale : (kUp ? ex.w1_scale : ex.w2_scale)) +
+                           (long long)(un.y * 128 + r) * sfk;
+      const bool need_a = !second || kUp;
       const bool brow_ok = un.z + r < a.rows_total;
       const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * sfk;
       // scale bytes of 4 K tiles per 16-byte load, one group ahead
-      auto sf_group = [&](int kt0, uint4& qa1, uint4& qa3, uint4& qb) {
-        qa1 = __ldg(reinterpret_cast<const uint4*>(sfa1 + kt0 * 4));
-        qa3 = kUp ? __ldg(reinterpret_cast<const uint4*>(sfa3 + kt0 * 4)) : make_uint4(0, 0, 0, 0);
-        qb = brow_ok ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
-                     : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+      auto sf_group = [&](int kt0, uint4& qa, uint4& qb) {
+        qa = need_a ? __ldg(reinterpret_cast<const uint4*>(sfa + kt0 * 4)) : make_uint4(0, 0, 0, 0);
+        qb = (!second && brow_ok) ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
+                                  : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
       };
-      uint4 ca1, ca3, cb, na1, na3, nb;
-      sf_group(0, na1, na3, nb);
+      uint4 ca, cb, na, nb;
+      sf_group(0, na, nb);
       for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
         const int s = g % kGStages, c = gc % kGConv;
         if ((kt & 3) == 0) {
-          ca1 = na1;
-          ca3 = na3;
+          ca = na;
           cb = nb;
-          if (kt + 4 < ktiles) sf_group(kt + 4, na1, na3, nb);
+          if (kt + 4 < ktiles) sf_group(kt + 4, na, nb);
         }
-        const uint32_t va1 = pick4(ca1, kt & 3);
-        const uint32_t va3 = pick4(ca3, kt & 3);
-        const uint32_t vb = pick4(cb, kt & 3);
         if (!mbar_wait(&raw_full[s], (g / kGStages) & 1, a.status) ||
             (gc >= kGConv && !mbar_wait(&conv_empty[c], ((gc / kGConv) - 1) & 1, a.status))) {
           ok = false;
@@ -270,9 +277,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (kUp) convert_tile(st + kGB + kGRawA, ct + kGConvA, tid);
         uint8_t* sf = sfs + c * L::kSfStage;
         const int atom = (r & 31) * 16 + (r >> 5) * 4;
-        *reinterpret_cast<uint32_t*>(sf + atom) = va1;
-        if (kUp) *reinterpret_cast<uint32_t*>(sf + 512 + atom) = va3;
-        *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = vb;
+        if (!second) {
+          *reinterpret_cast<uint32_t*>(sf + atom) = pick4(ca, kt & 3);
+          *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = pick4(cb, kt & 3);
+        } else if (kUp) {
+          *reinterpret_cast<uint32_t*>(sf + 512 + atom) = pick4(ca, kt & 3);
+        }
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -284,9 +294,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
       if (ok) ok = mbar_wait(acc_full, nu & 1, a.status);
       if (!ok) break;
       tc::fence_after_sync();
-      const int feat = un.y * 128 + warp * 32 + lane;
-      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-      for (int n0 = 0; n0 < kGN; n0 += 16) {
+      const int q4 = warp & 3;
+      const int feat = un.y * 128 + q4 * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+      const int col0 = (warp >> 2) * 64;
+      for (int n0 = col0; n0 < col0 + 64; n0 += 16) {
+        if (n0 >= un.w) break;  // every remaining column is past the expert's rows
         uint32_t v1[16];
         tc::ld_32x32b_x16(trow + n0, v1);
         if (kUp) {
@@ -299,44 +312,42 @@ __global__ void __launch_bounds__(kGThreads, 1)
             // SwiGLU with the reference clamps (src/deepseek_v4.rs:589-593)
             const float gte = fminf(__uint_as_float(v1[j]), 10.0f);
             const float upv = fminf(fmaxf(__uint_as_float(v3[j]), -10.0f), 10.0f);
-            h[j] = gte / (1.0f + expf(-gte)) * upv;
+            h[j] = __fdividef(gte, 1.0f + __expf(-gte)) * upv;
           }
-          // act quant of h over 64 features (two warps) per token
-          float am[16];
+          // act quant of h per token over the 64 features of warps 2p, 2p+1
+          float mine = 0.0f;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float m = fabsf(h[j]);
 #pragma unroll
             for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            am[j] = m;
+            if (lane == j) mine = m;
           }
-          float* xs_amax = amax_s + (chunk & 1) * 64;
-          if (lane < 16) {
-            float mine = am[0];
-#pragma unroll
-            for (int j = 1; j < 16; ++j)
-              if (lane == j) mine = am[j];
-            xs_amax[warp * 16 + lane] = mine;
-          }
+          float* xs_amax = amax_s + (chunk & 1) * (kGWork * 16);
+          if (lane < 16) xs_amax[warp * 16 + lane] = mine;
           mbar_arrive(&pair_bar[warp >> 1]);
           if (!mbar_wait(&pair_bar[warp >> 1], chunk & 1, a.status)) ok = false;
           ++chunk;
+          // lane j < 16: exponent of token n0 + j
+          int kj = 0;
+          if (lane < 16) {
+            const float m = fmaxf(fmaxf(mine, xs_amax[(warp ^ 1) * 16 + lane]), 1.0e-4f);
+            kj = ceil_log2f_thr(__fdiv_rn(m, 448.0f), aq_thr);
+            const int row = un.z + n0 + lane;
+            if ((warp & 1) == 0 && n0 + lane < un.w)
+              *reinterpret_cast<uint16_t*>(a.hsf + (long long)row * (a.M / 32) +
+                                           (un.y * 128 + q4 * 32) / 32) =
+                  (uint16_t)((kj + 127) * 0x0101);
+          }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float m = fmaxf(fmaxf(am[j], xs_amax[(warp ^ 1) * 16 + j]), 1.0e-4f);
-            const int k = ceil_log2f_thr(__fdiv_rn(m, 448.0f), aq_thr);
-            // h / 2^k == h * 2^-k exactly; clamp and round as aq_grid does
-            float t = __fmul_rn(h[j], exp2i(-k));
-            t = t < -448.0f ? -448.0f : t;
-            t = t > 448.0f ? 448.0f : t;
-            const float q = e4m3_nearest_ties_lower(t);
-            const int row = un.z + n0 + j;
-            if (n0 + j < un.w) {
-              a.hq[(long long)row * a.M + feat] = e4m3_byte(q);
-              if ((warp & 1) == 0 && lane < 2)
-                a.hsf[(long long)row * (a.M / 32) + (un.y * 128 + warp * 32) / 32 + lane] =
-                    (uint8_t)(k + 127);
-            }
+          for (int j = 0; j < 16; j += 2) {
+            const int k0 = __shfl_sync(0xffffffffu, kj, j);
+            const int k1 = __shfl_sync(0xffffffffu, kj, j + 1);
+            // h / 2^k == h * 2^-k exactly
+            const uint32_t b2 = e4m3x2_rn(__fmul_rn(h[j], exp2i(-k0)), __fmul_rn(h[j + 1], exp2i(-k1)));
+            const long long row = un.z + n0 + j;
+            if (n0 + j < un.w) a.hq[row * a.M + feat] = (uint8_t)(b2 & 0xff);
+            if (n0 + j + 1 < un.w) a.hq[(row + 1) * a.M + feat] = (uint8_t)(b2 >> 8);
           }
         } else {
           tc::wait_ld();
