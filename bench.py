@@ -578,7 +578,7 @@ def run_config3(args):
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": T3 * HID * 4,
                     "d2h_bytes_per_step": T3 * HID * 4,
                     "path": "pinned host x -> H2D -> wh_moe_ffn (C ABI) -> D2H y"},
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 8 * args.steps,
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:

@@ -324,8 +324,9 @@ def test_fp4_expert_forward_fast_path_bit_exact(ctx, W, hidden, inter):
 
 # ---------------------------------------------------------------- router
 @pytest.mark.parametrize("mode", [0, 1])
-def test_router_ids_bit_exact(ctx, W, mode):
-    E, Hd, T, K = 256, 4096, 16, 6
+@pytest.mark.parametrize("E,T", [(256, 16), (256, 80), (200, 45)])  # T >= 32: batched router
+def test_router_ids_bit_exact(ctx, W, mode, E, T):
+    Hd, K = 4096, 6
     gate = H.router_gate(31, E, Hd)
     x = H.activations(32, T, Hd)
     bias = (np.random.default_rng(33).standard_normal(E) * 0.01).astype(np.float32) if mode else None

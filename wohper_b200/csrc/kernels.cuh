@@ -73,7 +73,6 @@ struct RouterArgs {
   uint32_t* counters;  // [tokens] zero-initialised, reset by the kernel
   uint32_t* status;
 };
-cudaError_t launch_router(const RouterArgs& a, int num_sms, cudaStream_t stream, bool pdl);
 
 // ---------------- MoE (FP4 experts, one token per call or a few) ----------------
 // Tensor maps for every expert's w1/w3 (box [kMoeUpRows rows][128 B]) and w2

@@ -820,8 +820,133 @@ static cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, size_t smem, cudaStream
   return cfg;
 }
 
+// ---------------------------------------------------------------------------
+// Batched router (many tokens, no act-quantised copy needed): the logits as a
+// tiled CUDA-core GEMM and then one warp per token for the top-k.  A thread
+// owns one expert x 4 tokens and keeps, for each of them, the 16 FMA chains
+// of dot_bf16_row_avx2 (src/compute.rs:6115-6136: chain p accumulates
+// columns 16c + p; logit = pairwise hsum of chain p + chain p+8, p < 8), so
+// every logit -- and therefore every selected id -- is the reference's bit
+// for bit.  Tiles: 32 experts x 32 tokens x 64 columns, double-buffered in
+// shared memory with a register prefetch of the next tile.
+// ---------------------------------------------------------------------------
+constexpr int kRbTile = 32, kRbK = 64, kRbStride = kRbK + 4;  // floats per padded smem row
+
+__global__ void __launch_bounds__(256) router_logits_batched_kernel(RouterArgs a) {
+  __shared__ __align__(16) float ws[2][kRbTile * kRbStride];
+  __shared__ __align__(16) float xs[2][kRbTile * kRbStride];
+  const int e0 = blockIdx.x * kRbTile, t0 = blockIdx.y * kRbTile;
+  const int tid = threadIdx.x, lane = tid & 31, tg = tid >> 5;  // expert e0+lane, tokens 4tg..
+  // loaders: gate row gr, 8 bf16 at column 8*gc; x rows xr[j], 4 floats at 4*xc[j]
+  const int gr = tid >> 3, gc = tid & 7;
+  const uint4* gsrc = reinterpret_cast<const uint4*>(
+      a.gate + (long long)min(e0 + gr, a.experts - 1) * a.hidden + gc * 8);
+  const float4* xsrc[2];
+  int xoff[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = tid + 256 * j, r = i >> 4, c = i & 15;
+    xsrc[j] = reinterpret_cast<const float4*>(a.x + (long long)min(t0 + r, a.tokens - 1) * a.hidden +
+                                              c * 4);
+    xoff[j] = r * kRbStride + c * 4;
+  }
+  uint4 gv;
+  float4 xv[2];
+  auto fetch = [&](int k0) {
+    gv = __ldg(gsrc + k0 / 8);
+    xv[0] = __ldg(xsrc[0] + k0 / 4);
+    xv[1] = __ldg(xsrc[1] + k0 / 4);
+  };
+  auto stash = [&](int st) {
+    float* w = &ws[st][gr * kRbStride + gc * 8];
+    *reinterpret_cast<float4*>(w) =
+        make_float4(__uint_as_float(gv.x << 16), __uint_as_float(gv.x & 0xffff0000u),
+                    __uint_as_float(gv.y << 16), __uint_as_float(gv.y & 0xffff0000u));
+    *reinterpret_cast<float4*>(w + 4) =
+        make_float4(__uint_as_float(gv.z << 16), __uint_as_float(gv.z & 0xffff0000u),
+                    __uint_as_float(gv.w << 16), __uint_as_float(gv.w & 0xffff0000u));
+    *reinterpret_cast<float4*>(&xs[st][xoff[0]]) = xv[0];
+    *reinterpret_cast<float4*>(&xs[st][xoff[1]]) = xv[1];
+  };
+  float acc[4][16];
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int p = 0; p < 16; ++p) acc[t][p] = 0.0f;
+  const int nk = a.hidden / kRbK;
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  for (int kc = 0; kc < nk; ++kc) {
+    if (kc + 1 < nk) fetch((kc + 1) * kRbK);
+    const float* wr = &ws[kc & 1][lane * kRbStride];
+    const float* xr = &xs[kc & 1][(tg * 4) * kRbStride];
+#pragma unroll
+    for (int c = 0; c < kRbK / 16; ++c) {
+      float w[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(wr + c * 16 + 4 * q);
+        w[4 * q] = v.x;
+        w[4 * q + 1] = v.y;
+        w[4 * q + 2] = v.z;
+        w[4 * q + 3] = v.w;
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + t * kRbStride + c * 16 + 4 * q);
+          acc[t][4 * q] = __fmaf_rn(w[4 * q], v.x, acc[t][4 * q]);
+          acc[t][4 * q + 1] = __fmaf_rn(w[4 * q + 1], v.y, acc[t][4 * q + 1]);
+          acc[t][4 * q + 2] = __fmaf_rn(w[4 * q + 2], v.z, acc[t][4 * q + 2]);
+          acc[t][4 * q + 3] = __fmaf_rn(w[4 * q + 3], v.w, acc[t][4 * q + 3]);
+        }
+      }
+    }
+    if (kc + 1 < nk) stash((kc + 1) & 1);
+    __syncthreads();
+  }
+  const int e = e0 + lane;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int tok = t0 + tg * 4 + t;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(acc[t][j], acc[t][8 + j]);
+    const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                              __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+    // + the (empty) column tail, as the reference adds it: -0 becomes +0
+    if (e < a.experts && tok < a.tokens) a.logits[(long long)tok * a.experts + e] = __fadd_rn(h, 0.0f);
+  }
+}
+
+template <int PER>
+__global__ void __launch_bounds__(128) router_topk_kernel(RouterArgs a) {
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= a.tokens) return;  // warp-uniform
+  router_topk_and_weights<PER>(a, t, threadIdx.x & 31);
+}
+
+cudaError_t launch_router_batched(const RouterArgs& a, cudaStream_t s) {
+  dim3 grid((a.experts + kRbTile - 1) / kRbTile, (a.tokens + kRbTile - 1) / kRbTile);
+  router_logits_batched_kernel<<<grid, 256, 0, s>>>(a);
+  const int blocks = (a.tokens + 3) / 4;
+  if (a.experts <= 32) router_topk_kernel<1><<<blocks, 128, 0, s>>>(a);
+  else if (a.experts <= 64) router_topk_kernel<2><<<blocks, 128, 0, s>>>(a);
+  else if (a.experts <= 128) router_topk_kernel<4><<<blocks, 128, 0, s>>>(a);
+  else if (a.experts <= 256) router_topk_kernel<8><<<blocks, 128, 0, s>>>(a);
+  else if (a.experts <= 512) router_topk_kernel<16><<<blocks, 128, 0, s>>>(a);
+  else router_topk_kernel<32><<<blocks, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_router_ex(const RouterArgs& a, __half* xq, float* xq_mult, cudaStream_t s,
                              bool pdl) {
+  if (xq == nullptr && a.tokens >= 32 && a.hidden % kRbK == 0 &&
+      (reinterpret_cast<uintptr_t>(a.gate) % 16) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.x) % 16) == 0)
+    return launch_router_batched(a, s);
   cudaLaunchAttribute attr[1];
   dim3 grid((a.experts + kRouterRowsPerCta - 1) / kRouterRowsPerCta, a.tokens);
   const bool smem_ok = a.hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(a.gate) % 16) == 0 &&
