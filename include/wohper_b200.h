@@ -195,6 +195,13 @@ typedef struct wh_moe_desc {
   int router_mode;              /* WH_ROUTER_* */
   float route_scale;            /* 1.5 in DeepSeek-V4-Flash */
   int max_tokens;               /* largest `tokens` wh_moe_ffn will be given */
+  int exact;                    /* 1: the bit-exact CUDA-core kernels for every call.
+                                   0: calls of 32 or more tokens run on the tensor cores
+                                   (grouped GEMMs, results within tolerance), smaller
+                                   ones on the bit-exact kernels.  2: the tensor cores
+                                   for every call.  The tensor-core path needs hidden
+                                   and inter multiples of 512 and no UE8M0 scale byte 0
+                                   or 255; otherwise the bit-exact kernels run. */
 } wh_moe_desc;
 
 typedef struct wh_moe_plan wh_moe_plan;

@@ -381,13 +381,16 @@ def moe_layer(ctx, W):
     experts = [_w_expert(W, stack, e) for e in range(E)]
     shared = _w_expert(W, stack, E)
     layer = W.MoeLayer(ctx, experts, shared, dev(gate.view(np.int16)), topk=6,
-                       router_mode=W.ROUTER_RAW_LOGITS, max_tokens=4)
-    yield stack, gate, layer
+                       router_mode=W.ROUTER_RAW_LOGITS, max_tokens=4, exact=1)
+    fast = W.MoeLayer(ctx, experts, shared, dev(gate.view(np.int16)), topk=6,
+                      router_mode=W.ROUTER_RAW_LOGITS, max_tokens=4, exact=2)
+    yield stack, gate, layer, fast
     layer.close()
+    fast.close()
 
 
 def test_moe_ffn_config2_vs_oracle(ctx, W, moe_layer):
-    stack, gate, layer = moe_layer
+    stack, gate, layer, _ = moe_layer
     E, Hd = 256, 4096
     T = 3
     x = H.activations(43, T, Hd)
@@ -414,9 +417,36 @@ def test_moe_ffn_config2_vs_oracle(ctx, W, moe_layer):
 
 
 def test_moe_ffn_batch_equals_single_token(ctx, W, moe_layer):
-    _, _, layer = moe_layer
+    _, _, layer, _ = moe_layer
     x = dev(H.activations(44, 4, 4096))
     yb = layer.forward(x)
     ys = torch.stack([layer.forward(x[t:t + 1].contiguous()).view(-1) for t in range(4)])
     ctx.sync()
     np.testing.assert_array_equal(bits(yb.cpu().numpy()), bits(ys.cpu().numpy()))
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_moe_ffn_config2_tensor_core_path_vs_oracle(ctx, W, moe_layer, T):
+    """Decode-sized calls on the tensor-core path (desc.exact = 0): router ids
+    bit-exact; outputs within the grouped-path tolerance (tests/test_gpu_grouped.py:
+    exact products, tensor-core accumulation order, act-quant grid flips of the
+    SwiGLU hidden): max |y - ref| <= 2e-3 max|ref|, RMS <= 1e-4 RMS(ref)."""
+    stack, gate, _, fast = moe_layer
+    E, Hd = 256, 4096
+    x = H.activations(44 + T, T, Hd)
+    ids = torch.zeros(T, 6, dtype=torch.int32, device="cuda")
+    y = fast.forward(dev(x), ids=ids)
+    ctx.sync()
+    y, ids = y.cpu().numpy(), ids.cpu().numpy()
+    for t in range(T):
+        n, oid, ow, _ = O.router(gate, x[t], 6, mode=0)
+        np.testing.assert_array_equal(ids[t], oid)
+        keep = []
+        arr = (O.Fp4Expert * (E + 1))()
+        for e in list(oid) + [E]:
+            arr[e] = _oracle_expert(stack, e, keep)
+        st, want = O.moe_combine_token(arr, oid, ow, arr[E], x[t])
+        assert st == O.OK
+        err = y[t] - want
+        assert np.abs(err).max() <= 2e-3 * np.abs(want).max()
+        assert np.sqrt((err ** 2).mean()) <= 1e-4 * np.sqrt((want ** 2).mean())

@@ -80,6 +80,7 @@ class MoeDesc(C.Structure):
         ("experts", C.POINTER(Fp4ExpertSpec)), ("shared", C.POINTER(Fp4ExpertSpec)),
         ("gate", C.c_void_p), ("gate_bias", C.c_void_p), ("topk", C.c_int),
         ("router_mode", C.c_int), ("route_scale", C.c_float), ("max_tokens", C.c_int),
+        ("exact", C.c_int),
     ]
 
 
@@ -321,7 +322,7 @@ class MoeLayer:
     def __init__(self, ctx: Context, experts: Sequence[DeepSeekV4Fp4Expert],
                  shared: Optional[DeepSeekV4Fp4Expert], gate_bf16, topk: int = 6,
                  router_mode: int = ROUTER_RAW_LOGITS, route_scale: float = 1.0,
-                 gate_bias=None, max_tokens: int = 1):
+                 gate_bias=None, max_tokens: int = 1, exact: int = 0):
         import torch
 
         self.ctx = ctx
@@ -336,7 +337,7 @@ class MoeLayer:
         sh = shared.spec() if shared is not None else None
         d = MoeDesc(len(experts), self.hidden, self.inter, arr,
                     C.pointer(sh) if sh is not None else None, _ptr(gate_bf16), _ptr(gate_bias),
-                    topk, router_mode, route_scale, max_tokens)
+                    topk, router_mode, route_scale, max_tokens, int(exact))
         h = C.c_void_p()
         _check(lib().wh_moe_plan_create(ctx.handle, C.byref(d), C.byref(h)))
         self.plan = h

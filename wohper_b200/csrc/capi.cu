@@ -297,7 +297,7 @@ struct wh_moe_plan {
   DevExpertSet set;  // routed experts, then the shared expert
   uint32_t* counters = nullptr;      // router: [max_tokens]
   uint32_t* blk_counters = nullptr;  // moe_up: [max_tokens][slots][inter/64]
-  bool grouped = false;              // tensor-core path available (tokens >= kGroupedMinTokens)
+  bool grouped = false;              // tensor-core path available (desc.exact == 0)
 };
 
 extern "C" {
@@ -668,7 +668,7 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
     return st;
   }
   p->d.shared = d->shared ? reinterpret_cast<const wh_fp4_expert*>(1) : nullptr;  // flag only
-  if (d->max_tokens >= kGroupedMinTokens && d->hidden % 512 == 0 && d->inter % 512 == 0) {
+  if (d->exact != 1 && d->hidden % 512 == 0 && d->inter % 512 == 0) {
     // UE8M0 bytes 0 and 255 mean 0 and +inf in the reference but 2^-127 and NaN
     // to the tensor core: layers holding either stay on the per-token path
     int bad = 1;
@@ -740,6 +740,9 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
 }
 }  // namespace
 
+// decode-sized calls: 16-token tiles and the single-token (route-order) combine
+int grouped_tile_n(int tokens) { return tokens < kGroupedMinTokens ? kGNSmall : kGN; }
+
 struct GroupedScratch {
   float* logits;
   float* combine_w;
@@ -763,7 +766,7 @@ GroupedScratch grouped_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base
   const auto& d = p->d;
   const int ne = d.num_experts + (d.shared ? 1 : 0);
   const int R = T * d.topk + (d.shared ? T : 0);
-  const size_t tiles = size_t(R) / 128 + 1 + ne;  // >= sum over experts of ceil(rows/128)
+  const size_t tiles = size_t(R) / grouped_tile_n(T) + 1 + ne;  // >= sum of ceil(rows/tile)
   GroupedScratch s{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -790,8 +793,12 @@ GroupedScratch grouped_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base
   s.bytes = off;
   return s;
 }
+// exact 0 (auto): tensor cores from kGroupedMinTokens tokens on, the exact
+// kernels below (they are faster for decode-sized calls); 2: tensor cores for
+// every call; 1: never.
 bool use_grouped(const wh_moe_plan* p, int tokens) {
-  return p->grouped && tokens >= kGroupedMinTokens;
+  if (!p->grouped) return false;
+  return p->d.exact == 2 ? tokens >= 1 : tokens >= kGroupedMinTokens;
 }
 
 size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
@@ -841,11 +848,13 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   pa.n_units = g.n_units;
   pa.mt_up = d.inter / 128;
   pa.mt_down = d.hidden / 128;
+  pa.tile_n = grouped_tile_n(tokens);
+  pa.route_order = tokens < kGroupedMinTokens;
   pa.status = c->status;
   CUtensorMap bup, bdown;
   wh_status st;
-  if ((st = make_u8_map(&bup, g.xq, g.rows, d.hidden, 128, 128)) != WH_OK) return st;
-  if ((st = make_u8_map(&bdown, g.hq, g.rows, d.inter, 128, 128)) != WH_OK) return st;
+  if ((st = make_u8_map(&bup, g.xq, g.rows, d.hidden, pa.tile_n, 128)) != WH_OK) return st;
+  if ((st = make_u8_map(&bdown, g.hq, g.rows, d.inter, pa.tile_n, 128)) != WH_OK) return st;
   GroupedArgs up{};
   up.amaps = p->set.gmaps;
   up.experts = p->set.experts;
@@ -874,9 +883,9 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   if ((st = c->prof_mark(stream)) != WH_OK) return st;
   WH_CUDA(launch_grouped_route(pa, x, d.hidden, g.xq, g.xsf, stream));
   if ((st = c->prof_mark(stream)) != WH_OK) return st;
-  WH_CUDA(launch_grouped_gemm(true, bup, up, c->num_sms, stream));
+  WH_CUDA(launch_grouped_gemm(true, pa.tile_n, bup, up, c->num_sms, stream));
   if ((st = c->prof_mark(stream)) != WH_OK) return st;
-  WH_CUDA(launch_grouped_gemm(false, bdown, down, c->num_sms, stream));
+  WH_CUDA(launch_grouped_gemm(false, pa.tile_n, bdown, down, c->num_sms, stream));
   if ((st = c->prof_mark(stream)) != WH_OK) return st;
   WH_CUDA(launch_grouped_combine(pa, g.yrows, g.combine_w, x, y, d.hidden, stream));
   return c->prof_mark(stream);

@@ -24,17 +24,21 @@
 
 namespace wh {
 
-constexpr int kGroupedMinTokens = 32;  // wh_moe_ffn uses the grouped path from here on
+// Below this many tokens a call is decode-sized: 16-token tiles and the
+// single-token (route-order) combine; from here on 128-token tiles and the
+// batched (ascending expert id) combine.
+constexpr int kGroupedMinTokens = 32;
 // K (hidden and inter) must be a multiple of 512: scale bytes are read 16 at a
 // time (4 K tiles of 128)
-constexpr int kGN = 128;        // tokens per tile (MMA N)
+constexpr int kGN = 128;        // tokens per tile (MMA N) of batches
+constexpr int kGNSmall = 16;    // tokens per tile for decode-sized batches
 constexpr int kGStages = 4;     // TMA ring depth (raw FP4 A + E4M3 B per K tile)
 constexpr int kGConv = 2;       // converted-A ring depth
 constexpr int kGWork = 8;       // converter + epilogue warps
 constexpr int kGThreads = (kGWork + 2) * 32;  // + TMA producer warp + MMA warp
 constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
 constexpr int kGConvA = 128 * 128;  // E4M3 A tile
-constexpr int kGB = kGN * 128;      // E4M3 B tile
+
 constexpr uint32_t kGTmemCols = 512;
 
 struct GroupedArgs {
@@ -51,8 +55,9 @@ struct GroupedArgs {
   uint32_t* status;
 };
 
-template <bool kUp>
+template <bool kUp, int kN>
 struct GroupedSmem {
+  static constexpr int kGB = kN * 128;  // E4M3 B tile (1024-byte multiple)
   static constexpr int kRawStage = kGB + (kUp ? 2 : 1) * kGRawA;
   static constexpr int kConvStage = (kUp ? 2 : 1) * kGConvA;
   static constexpr int kSfStage = (kUp ? 3 : 2) * 512;
@@ -112,10 +117,11 @@ __device__ __forceinline__ uint32_t e4m3x2_rn(float lo, float hi) {
   return r;
 }
 
-template <bool kUp>
+template <bool kUp, int kN>
 __global__ void __launch_bounds__(kGThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap bmap, GroupedArgs a) {
-  using L = GroupedSmem<kUp>;
+  using L = GroupedSmem<kUp, kN>;
+  constexpr int kGB = L::kGB;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* raw = smem;                                        // [stages][B | A1 | A3]
@@ -205,7 +211,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             break;
           }
           tc::fence_after_sync();
-          const uint32_t tsf = tmem + 2 * kGN + 16 * c;
+          const uint32_t tsf = tmem + 2 * kN + 16 * c;
           const uint8_t* sf = sfs + c * L::kSfStage;
           tc::cp_sf_block(tsf, tc::desc_sf_block(smem_u32(sf)));
           if (kUp) tc::cp_sf_block(tsf + 4, tc::desc_sf_block(smem_u32(sf + 512)));
@@ -216,12 +222,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint32_t acc = (kt | k) != 0;
-            const uint32_t id = tc::idesc_mxf8(kGN, k, k);
+            const uint32_t id = tc::idesc_mxf8(kN, k, k);
             const uint64_t db = tc::desc_sw128(smem_u32(bt + 32 * k));
             tc::mma_mxf8(tmem, tc::desc_sw128(smem_u32(ct + 32 * k)), db, id,
                          tsf | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
             if (kUp)
-              tc::mma_mxf8(tmem + kGN, tc::desc_sw128(smem_u32(ct + kGConvA + 32 * k)), db, id,
+              tc::mma_mxf8(tmem + kN, tc::desc_sw128(smem_u32(ct + kGConvA + 32 * k)), db, id,
                            (tsf + 4) | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
           }
           tc::commit(&conv_empty[c]);
@@ -297,14 +303,17 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const int q4 = warp & 3;
       const int feat = un.y * 128 + q4 * 32 + lane;
       const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-      const int col0 = (warp >> 2) * 64;
-      for (int n0 = col0; n0 < col0 + 64; n0 += 16) {
+      // columns of this warp: halves of the tile (a single 16-column chunk for
+      // the small tile, taken by warps 0-3)
+      constexpr int kCols = kN >= 32 ? kN / 2 : kN;
+      const int col0 = kN >= 32 ? (warp >> 2) * kCols : (warp < 4 ? 0 : kN);
+      for (int n0 = col0; n0 < col0 + kCols && n0 < kN; n0 += 16) {
         if (n0 >= un.w) break;  // every remaining column is past the expert's rows
         uint32_t v1[16];
         tc::ld_32x32b_x16(trow + n0, v1);
         if (kUp) {
           uint32_t v3[16];
-          tc::ld_32x32b_x16(trow + kGN + n0, v3);
+          tc::ld_32x32b_x16(trow + kN + n0, v3);
           tc::wait_ld();
           float h[16];
 #pragma unroll
@@ -379,6 +388,8 @@ struct GroupedPlanArgs {
   int4* units_down;
   int* n_units;        // [2]
   int mt_up, mt_down;  // 128-row tiles of inter / hidden
+  int tile_n;          // tokens per tile of the grouped GEMMs
+  int route_order;     // combine in route order (single-token semantics) instead of id order
   uint32_t* status;
 };
 
@@ -397,36 +408,53 @@ __global__ void grouped_count_kernel(GroupedPlanArgs a) {
 // One CTA: exclusive scans of rows and tiles over the experts, then the unit
 // lists (expert-major so that CTAs running together share B rows).
 __global__ void __launch_bounds__(1024) grouped_units_kernel(GroupedPlanArgs a) {
-  __shared__ int tiles_s[1025];
-  __shared__ int rows_s[1025];
+  __shared__ int tiles_s[1056];
+  __shared__ int rows_s[1056];
   const int ne = a.num_experts + a.has_shared;
+  const int tn = a.tile_n;
   for (int e = threadIdx.x; e < ne; e += blockDim.x) {
     const int n = e < a.num_experts ? a.counts[e] : a.tokens;
     rows_s[e] = n;
-    tiles_s[e] = (n + kGN - 1) / kGN;
+    tiles_s[e] = (n + tn - 1) / tn;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    // exclusive scans of rows and tiles, 32 experts per step
+    const int lane = threadIdx.x;
     int row = 0, tile = 0;
-    for (int e = 0; e < ne; ++e) {
-      const int n = rows_s[e], t = tiles_s[e];
-      rows_s[e] = row;
-      tiles_s[e] = tile;
-      a.offsets[e] = row;
-      row += n;
-      tile += t;
+    for (int base = 0; base < ne; base += 32) {
+      const int e = base + lane;
+      const int n = e < ne ? rows_s[e] : 0, t = e < ne ? tiles_s[e] : 0;
+      int sn = n, st = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int pn = __shfl_up_sync(0xffffffffu, sn, o), pt = __shfl_up_sync(0xffffffffu, st, o);
+        if (lane >= o) {
+          sn += pn;
+          st += pt;
+        }
+      }
+      if (e < ne) {
+        rows_s[e] = row + sn - n;
+        tiles_s[e] = tile + st - t;
+        a.offsets[e] = row + sn - n;
+      }
+      row += __shfl_sync(0xffffffffu, sn, 31);
+      tile += __shfl_sync(0xffffffffu, st, 31);
     }
-    a.offsets[ne] = row;
-    a.n_units[0] = tile * a.mt_up;
-    a.n_units[1] = tile * a.mt_down;
+    if (lane == 0) {
+      a.offsets[ne] = row;
+      a.n_units[0] = tile * a.mt_up;
+      a.n_units[1] = tile * a.mt_down;
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < ne; e += blockDim.x) {
     const int n = a.offsets[e + 1] - a.offsets[e];
-    const int nt = (n + kGN - 1) / kGN;
+    const int nt = (n + tn - 1) / tn;
     for (int t = 0; t < nt; ++t) {
-      const int row0 = a.offsets[e] + t * kGN;
-      const int nv = min(kGN, n - t * kGN);
+      const int row0 = a.offsets[e] + t * tn;
+      const int nv = min(tn, n - t * tn);
       const int u = tiles_s[e] + t;
       for (int m = 0; m < a.mt_up; ++m) a.units_up[u * a.mt_up + m] = make_int4(e, m, row0, nv);
       for (int m = 0; m < a.mt_down; ++m)
@@ -488,7 +516,7 @@ __global__ void __launch_bounds__(256) grouped_combine_kernel(GroupedPlanArgs a,
       const int e = a.ids[i];
       if (e < 0 || e >= a.num_experts || a.slot[i] < 0) continue;
       int p = n++;
-      while (p > 0 && ids[p - 1] > e) {
+      while (!a.route_order && p > 0 && ids[p - 1] > e) {
         ids[p] = ids[p - 1];
         rows[p] = rows[p - 1];
         ws[p] = ws[p - 1];
@@ -505,8 +533,11 @@ __global__ void __launch_bounds__(256) grouped_combine_kernel(GroupedPlanArgs a,
   const long long sh = a.has_shared ? (long long)(a.offsets[a.num_experts] + t) * hidden : -1;
   for (int h = threadIdx.x; h < hidden; h += blockDim.x) {
     float acc = 0.0f;
-    for (int j = 0; j < n; ++j)
-      acc = __fadd_rn(acc, __fmul_rn(yrows[(long long)rows[j] * hidden + h], ws[j]));
+    if (a.route_order && n == 1)  // one expert: unweighted (src/compute.rs:1960-1966)
+      acc = yrows[(long long)rows[0] * hidden + h];
+    else
+      for (int j = 0; j < n; ++j)
+        acc = __fadd_rn(acc, __fmul_rn(yrows[(long long)rows[j] * hidden + h], ws[j]));
     float out;
     if (n > 0)
       out = sh >= 0 ? __fadd_rn(yrows[sh + h], acc) : acc;
@@ -538,21 +569,24 @@ cudaError_t launch_scale_check(const Fp4ExpertDev* ex, int n, int hidden, int in
   return cudaGetLastError();
 }
 
-size_t grouped_smem_bytes(bool up) {
-  return up ? GroupedSmem<true>::kBytes : GroupedSmem<false>::kBytes;
+template <bool kUp, int kN>
+cudaError_t launch_grouped_t(const CUtensorMap& bmap, const GroupedArgs& a, int num_sms,
+                             cudaStream_t s) {
+  const size_t smem = GroupedSmem<kUp, kN>::kBytes;
+  cudaError_t e = ensure_smem(grouped_gemm_kernel<kUp, kN>, smem);
+  if (e != cudaSuccess) return e;
+  grouped_gemm_kernel<kUp, kN><<<num_sms, kGThreads, smem, s>>>(bmap, a);
+  return cudaGetLastError();
 }
 
-cudaError_t launch_grouped_gemm(bool up, const CUtensorMap& bmap, const GroupedArgs& a, int num_sms,
-                                cudaStream_t s) {
-  const size_t smem = grouped_smem_bytes(up);
-  cudaError_t e = up ? ensure_smem(grouped_gemm_kernel<true>, smem)
-                     : ensure_smem(grouped_gemm_kernel<false>, smem);
-  if (e != cudaSuccess) return e;
-  if (up)
-    grouped_gemm_kernel<true><<<num_sms, kGThreads, smem, s>>>(bmap, a);
-  else
-    grouped_gemm_kernel<false><<<num_sms, kGThreads, smem, s>>>(bmap, a);
-  return cudaGetLastError();
+// tile_n: kGN (batches) or kGNSmall (decode-sized)
+cudaError_t launch_grouped_gemm(bool up, int tile_n, const CUtensorMap& bmap, const GroupedArgs& a,
+                                int num_sms, cudaStream_t s) {
+  if (tile_n == kGNSmall)
+    return up ? launch_grouped_t<true, kGNSmall>(bmap, a, num_sms, s)
+              : launch_grouped_t<false, kGNSmall>(bmap, a, num_sms, s);
+  return up ? launch_grouped_t<true, kGN>(bmap, a, num_sms, s)
+            : launch_grouped_t<false, kGN>(bmap, a, num_sms, s);
 }
 
 cudaError_t launch_grouped_route(const GroupedPlanArgs& p, const float* x, int hidden,
