@@ -224,6 +224,48 @@ wh_status wh_moe_ffn(wh_ctx* ctx, const wh_moe_plan* plan, const float* x, int t
                      void* scratch, size_t scratch_bytes, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Expert parallelism: the routed experts sharded contiguously over `world`   */
+/* ranks (rank r owns [r*E_l, (r+1)*E_l), E_l = plan's num_experts), the      */
+/* shared expert replicated.  The reference runs on one host and has no       */
+/* counterpart; these calls split its batched MoE (accumulate_expert_for_     */
+/* positions + finish, src/compute.rs:1779-1870) across ranks.  The caller     */
+/* moves data between them with its collectives (NCCL all-to-all):            */
+/*   wh_ep_dispatch -> all-to-all(send_counts), all-to-all(send rows) ->        */
+/*   wh_ep_expert_ffn -> all-to-all(result rows back) -> wh_ep_combine.         */
+/* The plan's gate may be NULL; ids and weights come from the caller's router. */
+/* ------------------------------------------------------------------------ */
+/* Bytes of one dispatched row: hidden E4M3 bytes + hidden/32 UE8M0 bytes,
+ * rounded up to 16. */
+size_t wh_ep_row_bytes(int hidden);
+/* Scratch for wh_ep_dispatch / wh_ep_expert_ffn with `tokens` own tokens and at
+ * most `max_recv_rows` received rows. */
+size_t wh_ep_scratch_bytes(const wh_moe_plan* plan, int world, int tokens, int max_recv_rows);
+/* Act quant of the rank's tokens x [tokens][hidden] and one row per route in
+ * send [tokens*topk][row_bytes], ordered by global expert id (so by destination
+ * rank).  send_counts [world*E_l] (device) receives the routes per (rank, local
+ * expert); pos [tokens*topk] the send row of each route (-1 for an invalid id,
+ * which also sets WH_ERR_DEVICE_ARG). */
+wh_status wh_ep_dispatch(wh_ctx* ctx, const wh_moe_plan* plan, int world, const float* x,
+                         int tokens, const int32_t* ids, uint8_t* send, int32_t* send_counts,
+                         int32_t* pos, void* scratch, size_t scratch_bytes, wh_stream_t stream);
+/* The local experts over the received rows recv [recv_rows][row_bytes]
+ * (source-major, counts recv_counts [world][E_l] on the device) and the shared
+ * expert over the own tokens x_local.  y_rows [recv_rows + tokens][hidden]:
+ * row i < recv_rows is the result of received row i, row recv_rows + t the
+ * shared expert's output for own token t. */
+wh_status wh_ep_expert_ffn(wh_ctx* ctx, const wh_moe_plan* plan, int world, const uint8_t* recv,
+                           const int32_t* recv_counts, int recv_rows, const float* x_local,
+                           int tokens, float* y_rows, void* scratch, size_t scratch_bytes,
+                           wh_stream_t stream);
+/* y[t] = y_shared[t] + sum over t's routes in ascending expert id of
+ * y_back[pos] * w/sum(w) (uniform when the weights are not finite and
+ * positive): y_back [tokens*topk][hidden] holds the result rows returned in
+ * send order. */
+wh_status wh_ep_combine(wh_ctx* ctx, const wh_moe_plan* plan, const int32_t* ids,
+                        const float* weights, const int32_t* pos, int tokens, const float* y_back,
+                        const float* y_shared, float* y, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Test hooks (host-only, no device work): expose the host-side pieces the   */
 /* kernels rely on so CPU tests can pin them.                                */
 /* ------------------------------------------------------------------------ */

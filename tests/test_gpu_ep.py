@@ -1,0 +1,79 @@
+"""Expert parallelism on the GPU: the expert-parallel layer at world size 1
+reproduces the single-GPU batched layer given the same routes, and (when two
+or more GPUs are visible) a 2-rank NCCL run reproduces it too
+(tests/ep_worker.py)."""
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from tests import helpers as H
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_ep_world1_matches_batched_layer():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import torch.distributed as dist
+
+    import wohper_b200 as W
+    from wohper_b200.ep import EpMoeLayer
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ["MASTER_PORT"] = str(_port())
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        E, Hd, I, T = 16, 1024, 512, 64
+        ctx = W.Context(0)
+        stack = H.torch_fp4_experts(95, E + 1, Hd, I)
+        gate = H.router_gate(96, E, Hd)
+
+        def wexp(e):
+            w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+            return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, I, Hd, Hd // 32),
+                                         W.Fp4Matvec(w3, s3, I, Hd, Hd // 32),
+                                         W.Fp4Matvec(w2, s2, Hd, I, I // 32))
+
+        experts = [wexp(e) for e in range(E)]
+        layer = W.MoeLayer(ctx, experts, wexp(E), torch.from_numpy(gate.view(np.int16)).cuda(),
+                           topk=6, max_tokens=T)
+        x = torch.from_numpy(H.activations(97, T, Hd)).cuda()
+        ids = torch.zeros(T, 6, dtype=torch.int32, device="cuda")
+        w = torch.zeros(T, 6, device="cuda")
+        want = layer.forward(x, ids=ids, weights=w)
+        ep = EpMoeLayer(ctx, experts, wexp(E), 1)
+        got = ep.forward(x, ids, w)
+        ctx.sync()
+        diff = float((got - want).abs().max())
+        assert diff <= 1e-6 * float(want.abs().max()), diff
+        ep.close()
+        layer.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_two_ranks_nccl():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node=2", "--master-addr=127.0.0.1",
+                        f"--master-port={_port()}", str(ROOT / "tests" / "ep_worker.py")],
+                       env=env, cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    assert "ep world=2" in r.stdout

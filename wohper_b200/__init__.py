@@ -49,7 +49,8 @@ EXPORTS = (
     "wh_fp4_expert_forward", "wh_router_topk", "wh_moe_plan_create", "wh_moe_plan_destroy",
     "wh_moe_scratch_bytes", "wh_moe_ffn", "wh_debug_act_quant_table", "wh_debug_e4m3_round",
     "wh_ctx_set_profiling", "wh_ctx_phase_times", "wh_debug_e4m3_round_n",
-    "wh_fp4_expert_forward_noalloc",
+    "wh_fp4_expert_forward_noalloc", "wh_ep_row_bytes", "wh_ep_scratch_bytes", "wh_ep_dispatch",
+    "wh_ep_expert_ffn", "wh_ep_combine",
 )
 
 
@@ -111,6 +112,11 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_fp4_expert_scratch_len": (sz, [sz]),
         "wh_fp4_expert_forward": (st, [vp, C.POINTER(Fp4ExpertSpec), vp, sz, vp, sz, vp, sz, vp]),
         "wh_fp4_expert_forward_noalloc": (st, [vp, C.POINTER(Fp4ExpertSpec), vp, sz, vp, sz, vp]),
+        "wh_ep_row_bytes": (sz, [i]),
+        "wh_ep_scratch_bytes": (sz, [vp, i, i, i]),
+        "wh_ep_dispatch": (st, [vp, vp, i, vp, i, vp, vp, vp, vp, vp, sz, vp]),
+        "wh_ep_expert_ffn": (st, [vp, vp, i, vp, vp, i, vp, i, vp, vp, sz, vp]),
+        "wh_ep_combine": (st, [vp, vp, vp, vp, vp, i, vp, vp, vp, vp]),
         "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
         "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
         "wh_moe_plan_destroy": (None, [vp]),

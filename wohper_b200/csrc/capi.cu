@@ -195,6 +195,23 @@ void free_expert_set(DevExpertSet& s) {
   s = DevExpertSet{};
 }
 
+// u8 matrix whose rows are `row_bytes` long but only the first `cols` bytes
+// are loaded: box [box_rows][128 B], 128-byte swizzle.
+wh_status make_u8_map_strided(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                              uint64_t row_bytes, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(WH_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WH_ERR_CUDA, "cuTensorMapEncodeTiled (strided) failed");
+  return WH_OK;
+}
+
 // Whether any expert scale byte is 0 or 255 (device scan of every matrix).
 wh_status scan_scale_bytes(const Fp4ExpertDev* ex, int n, int hidden, int inter, int* bad) {
   uint32_t* flag = nullptr;
@@ -636,7 +653,7 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
     return fail(WH_ERR_EMPTY_SHAPE, "moe shape");
   if (d->topk > d->num_experts || d->topk > 7 || d->num_experts > 1024)
     return fail(WH_ERR_UNSUPPORTED, "topk must be <= 7 (8 slots with the shared expert)");
-  if (!d->experts || !d->gate) return fail(WH_ERR_INVALID_POINTER, "experts/gate");
+  if (!d->experts) return fail(WH_ERR_INVALID_POINTER, "experts");
   if (d->router_mode != WH_ROUTER_RAW_LOGITS && d->router_mode != WH_ROUTER_SQRT_SOFTPLUS)
     return fail(WH_ERR_INVALID_SHAPE, "router mode");
   const int n = d->num_experts + (d->shared ? 1 : 0);
@@ -861,6 +878,7 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   up.K = d.hidden;
   up.M = d.inter;
   up.bsf = g.xsf;
+  up.bsf_stride = d.hidden / 32;
   up.rows_total = g.rows;
   up.units = g.units_up;
   up.n_units = g.n_units;
@@ -871,6 +889,7 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   down.K = d.inter;
   down.M = d.hidden;
   down.bsf = g.hsf;
+  down.bsf_stride = d.inter / 32;
   down.units = g.units_down;
   down.n_units = g.n_units + 1;
   down.hq = nullptr;
@@ -898,6 +917,7 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   if (tokens <= 0) return fail(WH_ERR_EMPTY_SHAPE, "tokens <= 0");
   if (tokens > p->d.max_tokens) return fail(WH_ERR_INVALID_SHAPE, "tokens > plan max_tokens");
   if (!x || !y || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  if (!p->d.gate) return fail(WH_ERR_INVALID_POINTER, "plan has no router gate");
   if (!aligned(x, 16) || !aligned(scratch, 256))
     return fail(WH_ERR_INVALID_POINTER, "x must be 16-byte and scratch 256-byte aligned");
   if (use_grouped(p, tokens))
@@ -962,6 +982,204 @@ float wh_debug_e4m3_round(float t) { return e4m3_nearest_ties_lower(t); }
 
 void wh_debug_e4m3_round_n(const float* in, float* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = e4m3_nearest_ties_lower(in[i]);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Expert parallelism (routed experts sharded over ranks, collectives between
+// the calls).  The plan holds the rank's local experts (and the shared one).
+// ---------------------------------------------------------------------------
+namespace {
+struct EpScratch {
+  int* slot;
+  int* off;
+  int* totals;
+  int* seg_off;
+  int* src_off;
+  int* exp_off;
+  int* row_map;
+  int4* units_up;
+  int4* units_down;
+  int* n_units;
+  uint8_t* sorted;
+  uint8_t* hq;
+  uint8_t* hsf;
+  size_t bytes;
+};
+EpScratch ep_scratch_layout(const wh_moe_plan* p, int world, int tokens, int max_recv_rows,
+                            uint8_t* base) {
+  const auto& d = p->d;
+  const int El = d.num_experts, nseg = world * El;
+  const size_t rows = (size_t)max_recv_rows + tokens;
+  const size_t tiles = rows / kGN + El + 2;
+  const size_t rb = wh_ep_row_bytes(d.hidden);
+  EpScratch s{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* q = base ? base + off : nullptr;
+    off += align256(bytes);
+    return q;
+  };
+  s.slot = reinterpret_cast<int*>(take(sizeof(int) * (size_t)tokens * d.topk));
+  s.off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
+  s.totals = reinterpret_cast<int*>(take(sizeof(int) * (El + 1)));
+  s.seg_off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
+  s.src_off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
+  s.exp_off = reinterpret_cast<int*>(take(sizeof(int) * (El + 2)));
+  s.row_map = reinterpret_cast<int*>(take(sizeof(int) * rows));
+  s.units_up = reinterpret_cast<int4*>(take(sizeof(int4) * tiles * (d.inter / 128)));
+  s.units_down = reinterpret_cast<int4*>(take(sizeof(int4) * tiles * (d.hidden / 128)));
+  s.n_units = reinterpret_cast<int*>(take(sizeof(int) * 2));
+  s.sorted = take(rows * rb);
+  s.hq = take(rows * d.inter);
+  s.hsf = take(rows * (d.inter / 32));
+  s.bytes = off;
+  return s;
+}
+wh_status ep_check(const wh_moe_plan* p, int world) {
+  if (!p) return fail(WH_ERR_INVALID_POINTER, "null plan");
+  if (world < 1 || world * p->d.num_experts > 1024)
+    return fail(WH_ERR_UNSUPPORTED, "world * local experts must be in [1, 1024]");
+  if (!p->grouped)
+    return fail(WH_ERR_UNSUPPORTED,
+                "expert parallelism runs on the tensor-core path: hidden and inter multiples "
+                "of 512, desc.exact != 1, no UE8M0 scale byte 0 or 255");
+  return WH_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t wh_ep_row_bytes(int hidden) {
+  return ((size_t)hidden + (size_t)hidden / 32 + 15) & ~size_t(15);
+}
+
+size_t wh_ep_scratch_bytes(const wh_moe_plan* p, int world, int tokens, int max_recv_rows) {
+  if (!p || world < 1 || tokens < 0 || max_recv_rows < 0) return 0;
+  return ep_scratch_layout(p, world, tokens, max_recv_rows, nullptr).bytes;
+}
+
+wh_status wh_ep_dispatch(wh_ctx* c, const wh_moe_plan* p, int world, const float* x, int tokens,
+                         const int32_t* ids, uint8_t* send, int32_t* send_counts, int32_t* pos,
+                         void* scratch, size_t scratch_bytes, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "null ctx");
+  wh_status st;
+  if ((st = ep_check(p, world)) != WH_OK) return st;
+  if (tokens < 0) return fail(WH_ERR_INVALID_SHAPE, "tokens < 0");
+  if (!send_counts || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  const auto& d = p->d;
+  EpScratch s = ep_scratch_layout(p, world, tokens, 0, static_cast<uint8_t*>(scratch));
+  if (scratch_bytes < s.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "ep scratch too small");
+  if (tokens == 0) {
+    WH_CUDA(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world * d.num_experts, stream));
+    return WH_OK;
+  }
+  if (!x || !ids || !send || !pos) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  if (!aligned(x, 16) || !aligned(send, 16)) return fail(WH_ERR_INVALID_POINTER, "alignment");
+  EpArgs a{};
+  a.world = world;
+  a.local_experts = d.num_experts;
+  a.topk = d.topk;
+  a.hidden = d.hidden;
+  a.row_bytes = (int)wh_ep_row_bytes(d.hidden);
+  a.ids = ids;
+  a.tokens = tokens;
+  a.cnt = send_counts;
+  a.slot = s.slot;
+  a.off = s.off;
+  a.pos = pos;
+  a.status = c->status;
+  WH_CUDA(launch_ep_dispatch(a, x, send, stream));
+  return WH_OK;
+}
+
+wh_status wh_ep_expert_ffn(wh_ctx* c, const wh_moe_plan* p, int world, const uint8_t* recv,
+                           const int32_t* recv_counts, int recv_rows, const float* x_local,
+                           int tokens, float* y_rows, void* scratch, size_t scratch_bytes,
+                           wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "null ctx");
+  wh_status st;
+  if ((st = ep_check(p, world)) != WH_OK) return st;
+  if (recv_rows < 0 || tokens < 0) return fail(WH_ERR_INVALID_SHAPE, "negative rows");
+  if (!recv_counts || !y_rows || !scratch || (recv_rows > 0 && !recv) || (tokens > 0 && !x_local))
+    return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  const auto& d = p->d;
+  const int has_shared = d.shared ? 1 : 0;
+  const int rows = recv_rows + (has_shared ? tokens : 0);
+  EpScratch s = ep_scratch_layout(p, world, tokens, recv_rows, static_cast<uint8_t*>(scratch));
+  if (scratch_bytes < s.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "ep scratch too small");
+  if (rows == 0) return WH_OK;
+  const int rb = (int)wh_ep_row_bytes(d.hidden);
+  EpSortArgs so{};
+  so.recv_counts = recv_counts;
+  so.world = world;
+  so.local_experts = d.num_experts;
+  so.totals = s.totals;
+  so.seg_off = s.seg_off;
+  so.src_off = s.src_off;
+  so.exp_off = s.exp_off;
+  so.recv = recv;
+  so.sorted = s.sorted;
+  so.row_map = s.row_map;
+  so.row_bytes = rb;
+  GroupedPlanArgs g{};
+  g.tokens = has_shared ? tokens : 0;
+  g.num_experts = d.num_experts;
+  g.has_shared = has_shared;
+  g.counts = s.totals;
+  g.offsets = s.exp_off;
+  g.units_up = s.units_up;
+  g.units_down = s.units_down;
+  g.n_units = s.n_units;
+  g.mt_up = d.inter / 128;
+  g.mt_down = d.hidden / 128;
+  g.tile_n = kGN;
+  g.status = c->status;
+  WH_CUDA(launch_ep_prepare(so, g, x_local, d.hidden, recv_rows, stream));
+  // B operand: the sorted rows (E4M3 hidden bytes, then the exponents)
+  CUtensorMap bup, bdown;
+  if ((st = make_u8_map_strided(&bup, s.sorted, rows, d.hidden, rb, kGN)) != WH_OK) return st;
+  if ((st = make_u8_map(&bdown, s.hq, rows, d.inter, kGN, 128)) != WH_OK) return st;
+  GroupedArgs up{};
+  up.amaps = p->set.gmaps;
+  up.experts = p->set.experts;
+  up.K = d.hidden;
+  up.M = d.inter;
+  up.bsf = s.sorted + d.hidden;
+  up.bsf_stride = rb;
+  up.rows_total = rows;
+  up.units = s.units_up;
+  up.n_units = s.n_units;
+  up.hq = s.hq;
+  up.hsf = s.hsf;
+  up.status = c->status;
+  GroupedArgs dn = up;
+  dn.K = d.inter;
+  dn.M = d.hidden;
+  dn.bsf = s.hsf;
+  dn.bsf_stride = d.inter / 32;
+  dn.units = s.units_down;
+  dn.n_units = s.n_units + 1;
+  dn.hq = nullptr;
+  dn.hsf = nullptr;
+  dn.y = y_rows;
+  dn.y_row_map = s.row_map;
+  WH_CUDA(launch_grouped_gemm(true, kGN, bup, up, c->num_sms, stream));
+  WH_CUDA(launch_grouped_gemm(false, kGN, bdown, dn, c->num_sms, stream));
+  return WH_OK;
+}
+
+wh_status wh_ep_combine(wh_ctx* c, const wh_moe_plan* p, const int32_t* ids, const float* weights,
+                        const int32_t* pos, int tokens, const float* y_back, const float* y_shared,
+                        float* y, wh_stream_t stream) {
+  if (!c || !p) return fail(WH_ERR_INVALID_POINTER, "null ctx/plan");
+  if (tokens <= 0) return WH_OK;
+  if (!ids || !weights || !pos || !y || (!y_back && p->d.topk > 0) || (p->d.shared && !y_shared))
+    return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  WH_CUDA(launch_ep_combine(ids, weights, pos, tokens, p->d.topk, y_back, y_shared,
+                            p->d.shared ? 1 : 0, y, p->d.hidden, stream));
+  return WH_OK;
 }
 
 }  // extern "C"

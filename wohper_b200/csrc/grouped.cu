@@ -45,13 +45,15 @@ struct GroupedArgs {
   const CUtensorMap* amaps;  // [experts][3] FP4 maps, box {64 B, 128 rows}
   const Fp4ExpertDev* experts;
   int K, M;                  // reduction length; rows of each weight matrix
-  const uint8_t* bsf;        // [rows][K/32] UE8M0 of the B rows
+  const uint8_t* bsf;        // UE8M0 of the B rows, row r at bsf + r * bsf_stride
+  int bsf_stride;            // bytes (K/32 for a dense [rows][K/32] array)
   int rows_total;
   const int4* units;         // (expert, m tile, first row, valid rows)
   const int* n_units;
   uint8_t* hq;               // up: [rows][M] E4M3 of act-quantised h
   uint8_t* hsf;              // up: [rows][M/32] UE8M0
   float* y;                  // down: [rows][M]
+  const int* y_row_map;      // down, nullable: output row of each B row
   uint32_t* status;
 };
 
@@ -256,7 +258,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
                            (long long)(un.y * 128 + r) * sfk;
       const bool need_a = !second || kUp;
       const bool brow_ok = un.z + r < a.rows_total;
-      const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * sfk;
+      const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * a.bsf_stride;
       // scale bytes of 4 K tiles per 16-byte load, one group ahead
       auto sf_group = [&](int kt0, uint4& qa, uint4& qb) {
         qa = need_a ? __ldg(reinterpret_cast<const uint4*>(sfa + kt0 * 4)) : make_uint4(0, 0, 0, 0);
@@ -362,7 +364,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
           tc::wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (n0 + j < un.w) a.y[(long long)(un.z + n0 + j) * a.M + feat] = __uint_as_float(v1[j]);
+            if (n0 + j < un.w) {
+              const int row = un.z + n0 + j;
+              a.y[(long long)(a.y_row_map ? a.y_row_map[row] : row) * a.M + feat] =
+                  __uint_as_float(v1[j]);
+            }
         }
       }
       tc::fence_before_sync();

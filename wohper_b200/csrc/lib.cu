@@ -3,5 +3,6 @@
 #include "fp8_gemv.cu"
 #include "moe.cu"
 #include "grouped.cu"
+#include "ep.cu"
 #include "capi.cu"
 #include "noalloc.cu"
