@@ -596,6 +596,157 @@ def run_config3(args):
     return res
 
 
+# ---------------------------------------------------------------------------
+# config 4: expert-parallel MoE layer over the ranks (NCCL all-to-all)
+# ---------------------------------------------------------------------------
+T4 = 8192
+METRIC4 = "expert-parallel MoE layer tokens/s (config 4)"
+WORKLOAD4 = ("config 4: 8192 tokens per step through the FP4 MoE FFN, 256 experts sharded "
+             "contiguously over the ranks + replicated shared expert, seeded uniform-random "
+             "top-6 routes, NCCL all-to-all dispatch/combine")
+
+
+def config4_routes(seed: int):
+    g = np.random.default_rng(seed)
+    ids = np.array([g.choice(E, TOPK, replace=False) for _ in range(T4)], np.int32)
+    w = g.uniform(0.1, 1.0, (T4, TOPK)).astype(np.float32)
+    return ids, w
+
+
+def config4_cpu(T_sample: int):
+    """The reference's batched MoE (oracle restatement) on T_sample tokens of
+    the config-4 workload (uniform routes): tokens/s on this host."""
+    import oracle as O
+    from tests import helpers as H
+
+    ids, w = config4_routes(4000)
+    ids, w = ids[:T_sample], w[:T_sample]
+    x = H.activations(4001, T_sample, HID)
+    model = HostModel(4002)
+    arr = (O.Fp4Expert * (E + 1))()
+    for e in set(ids.reshape(-1).tolist()) | {E}:
+        arr[e] = model.expert(int(e))
+    t0 = time.perf_counter()
+    st, _ = O.moe_batched(arr, E, ids, w, arr[E], x)
+    dt = time.perf_counter() - t0
+    assert st == O.OK
+    return T_sample / dt, O.threads()
+
+
+def run_config4(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup(args.gpus)
+    import wohper_b200 as W
+    from tests import helpers as H
+    from wohper_b200.ep import DeviceOps, EpMoeLayer
+
+    if world == 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29631")
+        dist.init_process_group("nccl", rank=0, world_size=1,
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    ctx = W.Context(local)
+    El = E // world
+    stack = H.torch_fp4_experts(4100 + rank, El + 1, HID, INTER, device=dev)
+
+    def wexp(e):
+        w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+        return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                     W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+    layer = EpMoeLayer(ctx, [wexp(e) for e in range(El)], wexp(El), world)
+    ids_all, w_all = config4_routes(4000)
+    Tl = T4 // world
+    lo = rank * Tl
+    x = torch.from_numpy(H.activations(4200 + rank, Tl, HID)).to(dev)
+    ids = torch.from_numpy(ids_all[lo:lo + Tl]).to(dev)
+    wts = torch.from_numpy(w_all[lo:lo + Tl]).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        flush.zero_()
+        layer.forward(x, ids, wts)
+    torch.cuda.synchronize()
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            flush.zero_()
+            ev[k][0].record(stream)
+            layer.forward(x, ids, wts)
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    # phase split of one step (events between the calls and collectives)
+    ops = DeviceOps(layer)
+    pe = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    flush.zero_()
+    pe[0].record(stream)
+    send, cnt, pos = ops.dispatch(x, ids)
+    rc = torch.empty_like(cnt)
+    dist.all_to_all_single(rc, cnt)
+    per_dest = ops.to_list(cnt.view(world, El).sum(1))
+    per_src = ops.to_list(rc.view(world, El).sum(1))
+    R = sum(per_src)
+    recv = ops.empty_rows(R)
+    pe[1].record(stream)
+    dist.all_to_all_single(recv, send, output_split_sizes=per_src, input_split_sizes=per_dest)
+    pe[2].record(stream)
+    y_rows = ops.expert_ffn(recv, rc, R, x)
+    pe[3].record(stream)
+    y_back = ops.empty_results(send.shape[0])
+    dist.all_to_all_single(y_back, y_rows[:R], output_split_sizes=per_dest,
+                           input_split_sizes=per_src)
+    pe[4].record(stream)
+    ops.combine(ids, wts, pos, y_back, y_rows[R:])
+    pe[5].record(stream)
+    torch.cuda.synchronize()
+    ctx.sync()
+    ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(5)]
+    rb = layer.row_bytes
+    sent_remote = sum(n for d, n in enumerate(per_dest) if d != rank)
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC4, "value": round(T4 / (ms_step * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "fp4-e2m1 (as e4m3) x fp8-e4m3, ue8m0 block scales, f32 accumulate",
+            "data": "synthetic (seeded random-init weights, N(0,1) tokens, uniform routes)",
+            "config": {"workload": WORKLOAD4, "experts": E, "topk": TOPK, "hidden": HID,
+                       "inter": INTER, "tokens": T4, "tokens_per_rank": Tl,
+                       "experts_per_rank": El, "dispatch_row_bytes": int(rb),
+                       "l2": "flushed between steps (256 MiB memset outside the timed events)",
+                       "parallelism": f"expert parallel x{world}"},
+            "phases_ms_max_over_ranks": {
+                "dispatch": round(ph[0], 4), "all_to_all_rows": round(ph[1], 4),
+                "expert_ffn": round(ph[2], 4), "all_to_all_results": round(ph[3], 4),
+                "combine": round(ph[4], 4)},
+            "rank0_remote_rows_sent": sent_remote,
+            "gpu_launches": 16 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            v, th = config4_cpu(16)
+            res["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": th,
+                                   "kind": "port",
+                                   "sample": "16 tokens of the workload through the C++ "
+                                             "restatement's batched path, one host"}
+    layer.close()
+    ctx.close()
+    dist.destroy_process_group()
+    return res
+
+
 def run_ncu_case(args):
     """Small single-GPU workloads for ncu captures (no JSON bench line).
 
@@ -672,8 +823,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3],
-                    help="2: one-token decode FFN (default); 3: 2048-token batched FFN")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: one-token decode FFN (default); 3: 2048-token batched FFN; "
+                         "4: expert-parallel layer over the ranks")
     ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
@@ -683,6 +835,8 @@ def main():
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.config == 3 and args.impl == "ours":
         res = run_config3(args)
+    elif args.config == 4 and args.impl == "ours":
+        res = run_config4(args)
     else:
         res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
