@@ -32,9 +32,12 @@ constexpr int kGroupedMinTokens = 32;
 // time (4 K tiles of 128)
 constexpr int kGN = 128;        // tokens per tile (MMA N) of batches
 constexpr int kGNSmall = 16;    // tokens per tile for decode-sized batches
-constexpr int kGStages = 4;     // TMA ring depth (raw FP4 A + E4M3 B per K tile)
+// TMA ring depth (raw FP4 A + E4M3 B per K tile): deeper for the small tile,
+// whose stages are smaller
+template <int kN>
+struct GStages { static constexpr int value = kN <= 16 ? 8 : 4; };
 constexpr int kGConv = 2;       // converted-A ring depth
-constexpr int kGWork = 8;       // converter + epilogue warps
+constexpr int kGWork = 16;      // converter + epilogue warps
 constexpr int kGThreads = (kGWork + 2) * 32;  // + TMA producer warp + MMA warp
 constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
 constexpr int kGConvA = 128 * 128;  // E4M3 A tile
@@ -59,13 +62,15 @@ struct GroupedArgs {
 
 template <bool kUp, int kN>
 struct GroupedSmem {
+  static constexpr int kGStages = GStages<kN>::value;
   static constexpr int kGB = kN * 128;  // E4M3 B tile (1024-byte multiple)
   static constexpr int kRawStage = kGB + (kUp ? 2 : 1) * kGRawA;
   static constexpr int kConvStage = (kUp ? 2 : 1) * kGConvA;
   static constexpr int kSfStage = (kUp ? 3 : 2) * 512;
   static constexpr size_t kBytes = 1024 + size_t(kGStages) * kRawStage +
                                    size_t(kGConv) * kConvStage + size_t(kGConv) * kSfStage +
-                                   (2 * kGStages + 2 * kGConv + 7) * 8 + 16 + 2 * kGWork * 16 * 4;
+                                   (2 * kGStages + 2 * kGConv + 3 + kGWork / 2) * 8 + 16 +
+                                   2 * kGWork * 16 * 4;
 };
 
 // 8 FP4 codes (one 32-bit word, code i in bits 4i..4i+3) -> 8 E4M3 bytes of
@@ -80,21 +85,35 @@ __device__ __forceinline__ uint2 fp4x8_to_e4m3x8(uint32_t w) {
   return make_uint2(lo | (slo & 0x80808080u), hi | (shi & 0x80808080u));
 }
 
-// Two of the 512 16-byte chunks of an FP4 tile [128 rows][64 B] -> E4M3
-// [128 rows][128 B] with 128-byte swizzle (256 threads cover the tile).
-__device__ __forceinline__ void convert_tile(const uint8_t* raw, uint8_t* dst, int tid) {
+// FP4 tiles [128 rows][64 B] -> E4M3 [128 rows][128 B] with 128-byte
+// swizzle; 32 * kGWork threads, 512 / (32 * kGWork) 16-byte chunks of each
+// of the kMats tiles per thread.  Every load is issued before the first
+// conversion.
+template <int kMats>
+__device__ __forceinline__ void convert_tiles(const uint8_t* raw, int raw_stride, uint8_t* dst,
+                                              int dst_stride, int tid) {
+  constexpr int kPer = 512 / (32 * kGWork);
+  uint4 v[kMats][kPer];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int i = tid + 256 * j;
-    const int r = i >> 2, ch = i & 3;
-    const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 64 + ch * 16);
-    const uint2 a = fp4x8_to_e4m3x8(v.x), b = fp4x8_to_e4m3x8(v.y);
-    const uint2 c = fp4x8_to_e4m3x8(v.z), d = fp4x8_to_e4m3x8(v.w);
-    uint8_t* row = dst + r * 128;
-    *reinterpret_cast<uint4*>(row + (((2 * ch) ^ (r & 7)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
-    *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ (r & 7)) << 4)) =
-        make_uint4(c.x, c.y, d.x, d.y);
-  }
+  for (int m = 0; m < kMats; ++m)
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + 32 * kGWork * j;
+      v[m][j] = *reinterpret_cast<const uint4*>(raw + m * raw_stride + (i >> 2) * 64 + (i & 3) * 16);
+    }
+#pragma unroll
+  for (int m = 0; m < kMats; ++m)
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + 32 * kGWork * j;
+      const int r = i >> 2, ch = i & 3;
+      const uint2 a = fp4x8_to_e4m3x8(v[m][j].x), b = fp4x8_to_e4m3x8(v[m][j].y);
+      const uint2 c = fp4x8_to_e4m3x8(v[m][j].z), d = fp4x8_to_e4m3x8(v[m][j].w);
+      uint8_t* row = dst + m * dst_stride + r * 128;
+      *reinterpret_cast<uint4*>(row + (((2 * ch) ^ (r & 7)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+      *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ (r & 7)) << 4)) =
+          make_uint4(c.x, c.y, d.x, d.y);
+    }
 }
 
 // ceil(log2f(q)) through the act-quant threshold table (shared-memory copy)
@@ -124,6 +143,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap bmap, GroupedArgs a) {
   using L = GroupedSmem<kUp, kN>;
   constexpr int kGB = L::kGB;
+  constexpr int kGStages = L::kGStages;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* raw = smem;                                        // [stages][B | A1 | A3]
@@ -136,8 +156,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint64_t* acc_full = conv_empty + kGConv;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
-  uint64_t* pair_bar = mma_done + 1;  // [4]: warps 2p and 2p+1 (act-quant amax exchange)
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + 4);
+  uint64_t* pair_bar = mma_done + 1;  // [kGWork/2]: warps 2p, 2p+1 (act-quant amax exchange)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + kGWork / 2);
   float* amax_s = reinterpret_cast<float*>(tmem_base_s + 4);  // [2 parity][8 warps][16]
   __shared__ uint32_t aq_thr[256];  // act-quant ceil(log2f) thresholds
 
@@ -158,7 +178,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, kGWork);
     mbar_init(mma_done, 1);
-    for (int p = 0; p < 4; ++p) mbar_init(&pair_bar[p], 64);
+    for (int p = 0; p < kGWork / 2; ++p) mbar_init(&pair_bar[p], 64);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -176,10 +196,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       bool ok = true;
       uint32_t g = 0;
+      prefetch_tensormap(&bmap);
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const int4 un = a.units[u];
         const CUtensorMap* m1 = a.amaps + un.x * 3 + (kUp ? 0 : 2);
         const CUtensorMap* m3 = a.amaps + un.x * 3 + 1;
+        prefetch_tensormap(m1);
+        if (kUp) prefetch_tensormap(m3);
         for (int kt = 0; kt < ktiles; ++kt, ++g) {
           const int s = g % kGStages;
           if (g >= kGStages && !mbar_wait(&raw_empty[s], ((g / kGStages) - 1) & 1, a.status)) {
@@ -247,22 +270,23 @@ __global__ void __launch_bounds__(kGThreads, 1)
     bool ok = true;
     uint32_t g = 0, gc = 0, nu = 0, chunk = 0;
     // scale factors: threads 0-127 stage SFA1 (+ SFB) of row tid, threads
-    // 128-255 stage SFA3 of row tid-128
+    // 128-255 stage SFA3 of row tid-128, the others none
     const int r = tid & 127;
     const bool second = tid >= 128;
+    const bool stages_sf = tid < 256;
     const int sfk = a.K / 32;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
       const int4 un = a.units[u];
       const Fp4ExpertDev& ex = a.experts[un.x];
       const uint8_t* sfa = (second ? ex.w3_scale : (kUp ? ex.w1_scale : ex.w2_scale)) +
                            (long long)(un.y * 128 + r) * sfk;
-      const bool need_a = !second || kUp;
+      const bool need_a = stages_sf && (!second || kUp);
       const bool brow_ok = un.z + r < a.rows_total;
       const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * a.bsf_stride;
       // scale bytes of 4 K tiles per 16-byte load, one group ahead
       auto sf_group = [&](int kt0, uint4& qa, uint4& qb) {
         qa = need_a ? __ldg(reinterpret_cast<const uint4*>(sfa + kt0 * 4)) : make_uint4(0, 0, 0, 0);
-        qb = (!second && brow_ok) ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
+        qb = (!second && stages_sf && brow_ok) ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
                                   : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
       };
       uint4 ca, cb, na, nb;
@@ -281,11 +305,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
         const uint8_t* st = raw + s * L::kRawStage;
         uint8_t* ct = conv + c * L::kConvStage;
-        convert_tile(st + kGB, ct, tid);
-        if (kUp) convert_tile(st + kGB + kGRawA, ct + kGConvA, tid);
+        convert_tiles<kMats>(st + kGB, kGRawA, ct, kGConvA, tid);
         uint8_t* sf = sfs + c * L::kSfStage;
         const int atom = (r & 31) * 16 + (r >> 5) * 4;
-        if (!second) {
+        if (!stages_sf) {
+        } else if (!second) {
           *reinterpret_cast<uint32_t*>(sf + atom) = pick4(ca, kt & 3);
           *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = pick4(cb, kt & 3);
         } else if (kUp) {
@@ -305,10 +329,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const int q4 = warp & 3;
       const int feat = un.y * 128 + q4 * 32 + lane;
       const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-      // columns of this warp: halves of the tile (a single 16-column chunk for
-      // the small tile, taken by warps 0-3)
-      constexpr int kCols = kN >= 32 ? kN / 2 : kN;
-      const int col0 = kN >= 32 ? (warp >> 2) * kCols : (warp < 4 ? 0 : kN);
+      // columns of this warp: the tile split over the kGWork/4 groups of 4
+      // warps in 16-column chunks (the small tile's single chunk goes to warps 0-3)
+      constexpr int kGroups = kGWork / 4;
+      constexpr int kCols = kN / kGroups >= 16 ? kN / kGroups : 16;
+      const int col0 = (warp >> 2) * kCols;
       for (int n0 = col0; n0 < col0 + kCols && n0 < kN; n0 += 16) {
         if (n0 >= un.w) break;  // every remaining column is past the expert's rows
         uint32_t v1[16];
@@ -474,7 +499,7 @@ __global__ void __launch_bounds__(1024) grouped_units_kernel(GroupedPlanArgs a) 
 __global__ void __launch_bounds__(128) grouped_dispatch_kernel(GroupedPlanArgs a, const float* x,
                                                                int hidden, uint8_t* xq,
                                                                uint8_t* xsf) {
-  const int t = blockIdx.x;
+  const int t = blockIdx.x;  // blockIdx.y: 4 of the token's 64-blocks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int rows[33];
   if (threadIdx.x < a.topk) {
@@ -487,7 +512,7 @@ __global__ void __launch_bounds__(128) grouped_dispatch_kernel(GroupedPlanArgs a
   __syncthreads();
   const int nrows = a.topk + 1;
   const float* xt = x + (long long)t * hidden;
-  for (int blk = warp; blk < hidden / 64; blk += 4) {
+  for (int blk = blockIdx.y * 4 + warp; blk < hidden / 64; blk += 4 * gridDim.y) {
     const float v0 = xt[blk * 64 + 2 * lane], v1 = xt[blk * 64 + 2 * lane + 1];
     float amax = fmaxf(fabsf(v0), fabsf(v1));
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -537,7 +562,7 @@ __global__ void __launch_bounds__(256) grouped_combine_kernel(GroupedPlanArgs a,
   __syncthreads();
   const int n = rows[32];
   const long long sh = a.has_shared ? (long long)(a.offsets[a.num_experts] + t) * hidden : -1;
-  for (int h = threadIdx.x; h < hidden; h += blockDim.x) {
+  for (int h = blockIdx.y * blockDim.x + threadIdx.x; h < hidden; h += blockDim.x * gridDim.y) {
     float acc = 0.0f;
     if (a.route_order && n == 1)  // one expert: unweighted (src/compute.rs:1960-1966)
       acc = yrows[(long long)rows[0] * hidden + h];
@@ -600,14 +625,15 @@ cudaError_t launch_grouped_route(const GroupedPlanArgs& p, const float* x, int h
   const int n = p.tokens * p.topk;
   grouped_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
   grouped_units_kernel<<<1, 1024, 0, s>>>(p);
-  grouped_dispatch_kernel<<<p.tokens, 128, 0, s>>>(p, x, hidden, xq, xsf);
+  grouped_dispatch_kernel<<<dim3(p.tokens, hidden / 256), 128, 0, s>>>(p, x, hidden, xq, xsf);
   return cudaGetLastError();
 }
 
 cudaError_t launch_grouped_combine(const GroupedPlanArgs& p, const float* yrows,
                                    const float* combine_w, const float* x, float* y, int hidden,
                                    cudaStream_t s) {
-  grouped_combine_kernel<<<p.tokens, 256, 0, s>>>(p, yrows, combine_w, x, y, hidden);
+  grouped_combine_kernel<<<dim3(p.tokens, (hidden + 1023) / 1024), 256, 0, s>>>(p, yrows, combine_w,
+                                                                              x, y, hidden);
   return cudaGetLastError();
 }
 
