@@ -221,10 +221,21 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
   // ---------------- consumers ----------------
   pdl_wait_prior();  // x may be produced by the previous kernel in the stream
   const int nthr = nconsumer * 32;
+  // x and the scale rows: every load in flight before the first store (one
+  // memory latency instead of one per pass)
   for (int b = 0; b < tb; ++b) {
     const float4* src = reinterpret_cast<const float4*>(a.x + (long long)(tile * TB + b) * a.ldx);
     float4* dst = reinterpret_cast<float4*>(xs + b * a.cols);
-    for (int i = threadIdx.x; i < a.cols / 4; i += nthr) dst[i] = src[i];
+    const int n4 = a.cols / 4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * nthr) {
+      float4 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (i0 + k * nthr < n4) v[k] = __ldg(src + i0 + k * nthr);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (i0 + k * nthr < n4) dst[i0 + k * nthr] = v[k];
+    }
   }
   // the UE8M0 scale rows this CTA's rows use (<= 32), so the group loop never
   // waits on a global load
@@ -252,20 +263,43 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
 #pragma unroll
   for (int b = 0; b < TB; ++b) acc01[b] = acc23[b] = make_float2(0.0f, 0.0f);
 
+  // Software pipeline: the weights (and, for one input, x) of group g + 1
+  // are loaded from shared memory while group g is decoded and accumulated.
   bool ok = true;
-  int s = 0;
-  uint32_t phase = 0;
-  for (int g = 0; g < ngroups; ++g) {
-    const float scale = decode_ue8m0(srow_s[g]);
-    if (!mbar_wait(&full[s], phase, a.status)) {
-      ok = false;
-      break;
-    }
-    const uint8_t* base = stages + s * kFp8StageBytes + rloc * 128 + 4 * q;
-    uint32_t wv[8];
+  uint32_t wv[8], wn[8];
+  float4 xc[8], xn[8];  // x of the current / next group (TB == 1 only)
+  auto load_group = [&](int slot, int g, uint32_t (&w)[8], float4 (&x)[8]) {
+    const uint8_t* base = stages + slot * kFp8StageBytes + rloc * 128 + 4 * q;
 #pragma unroll
     for (int c = 0; c < 8; ++c)
-      wv[c] = *reinterpret_cast<const uint32_t*>(base + 16 * (c ^ (rloc & 7)));
+      w[c] = *reinterpret_cast<const uint32_t*>(base + 16 * (c ^ (rloc & 7)));
+    if (TB == 1) {
+      const float* xg = xs + g * 128 + 4 * q;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
+    }
+  };
+  int s = 0;
+  uint32_t phase = 0;
+  if (ngroups > 0) {
+    ok = mbar_wait(&full[0], 0, a.status);
+    if (ok) load_group(0, 0, wv, xc);
+  }
+  for (int g = 0; ok && g < ngroups; ++g) {
+    int sn = s + 1;
+    uint32_t pn = phase;
+    if (sn == nstages) {
+      sn = 0;
+      pn ^= 1u;
+    }
+    if (g + 1 < ngroups) {
+      if (!mbar_wait(&full[sn], pn, a.status)) {
+        ok = false;
+        break;
+      }
+      load_group(sn, g + 1, wn, xn);
+    }
+    const float scale = decode_ue8m0(srow_s[g]);
     float2 wf[8][2];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -276,10 +310,15 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
 #pragma unroll
     for (int b = 0; b < TB; ++b) {
       if (b < tb) {
-        const float* xg = xs + b * a.cols + g * 128 + 4 * q;
         float4 xv[8];
+        if (TB == 1) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
+          for (int c = 0; c < 8; ++c) xv[c] = xc[c];
+        } else {
+          const float* xg = xs + b * a.cols + g * 128 + 4 * q;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
+        }
         float2 p01 = make_float2(0.0f, 0.0f), p23 = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -299,9 +338,12 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
     // release the slot only after the loaded words have been consumed
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (++s == nstages) {
-      s = 0;
-      phase ^= 1u;
+    s = sn;
+    phase = pn;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      wv[c] = wn[c];
+      xc[c] = xn[c];
     }
   }
   if (!ok) return;
