@@ -603,7 +603,9 @@ T4 = 8192
 METRIC4 = "expert-parallel MoE layer tokens/s (config 4)"
 WORKLOAD4 = ("config 4: 8192 tokens per step through the FP4 MoE FFN, 256 experts sharded "
              "contiguously over the ranks + replicated shared expert, seeded uniform-random "
-             "top-6 routes, NCCL all-to-all dispatch/combine")
+             "top-6 routes; rows and results cross NVLink as peer-memory stores from the "
+             "dispatch kernel and the down GEMM's epilogue (--ep-transport nccl: NCCL "
+             "all-to-all)")
 
 
 def config4_routes(seed: int):
@@ -658,9 +660,10 @@ def run_config4(args):
                                      W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
                                      W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
 
-    layer = EpMoeLayer(ctx, [wexp(e) for e in range(El)], wexp(El), world)
-    ids_all, w_all = config4_routes(4000)
     Tl = T4 // world
+    layer = EpMoeLayer(ctx, [wexp(e) for e in range(El)], wexp(El), world,
+                       transport=args.ep_transport, max_tokens=Tl)
+    ids_all, w_all = config4_routes(4000)
     lo = rank * Tl
     x = torch.from_numpy(H.activations(4200 + rank, Tl, HID)).to(dev)
     ids = torch.from_numpy(ids_all[lo:lo + Tl]).to(dev)
@@ -686,31 +689,47 @@ def run_config4(args):
     barrier(world)
     ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
     # phase split of one step (events between the calls and collectives)
-    ops = DeviceOps(layer)
-    pe = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-    flush.zero_()
-    pe[0].record(stream)
-    send, cnt, pos = ops.dispatch(x, ids)
-    rc = torch.empty_like(cnt)
-    dist.all_to_all_single(rc, cnt)
-    per_dest = ops.to_list(cnt.view(world, El).sum(1))
-    per_src = ops.to_list(rc.view(world, El).sum(1))
-    R = sum(per_src)
-    recv = ops.empty_rows(R)
-    pe[1].record(stream)
-    dist.all_to_all_single(recv, send, output_split_sizes=per_src, input_split_sizes=per_dest)
-    pe[2].record(stream)
-    y_rows = ops.expert_ffn(recv, rc, R, x)
-    pe[3].record(stream)
-    y_back = ops.empty_results(send.shape[0])
-    dist.all_to_all_single(y_back, y_rows[:R], output_split_sizes=per_dest,
-                           input_split_sizes=per_src)
-    pe[4].record(stream)
-    ops.combine(ids, wts, pos, y_back, y_rows[R:])
-    pe[5].record(stream)
-    torch.cuda.synchronize()
-    ctx.sync()
-    ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(5)]
+    flat = ids.reshape(-1).to(torch.int64) // El
+    per_dest = torch.bincount(flat, minlength=world).tolist()
+    if args.ep_transport == "p2p":
+        pe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        flush.zero_()
+        layer.forward_p2p(x, ids, wts, marks=lambda i: pe[i].record(stream))
+        torch.cuda.synchronize()
+        ctx.sync()
+        ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(3)]
+        phases = {"dispatch_and_row_stores": round(ph[0], 4),
+                  "expert_ffn_and_result_stores": round(ph[1], 4),
+                  "wait_and_combine": round(ph[2], 4)}
+    else:
+        ops = DeviceOps(layer)
+        pe = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        flush.zero_()
+        pe[0].record(stream)
+        send, cnt, pos = ops.dispatch(x, ids)
+        rc = torch.empty_like(cnt)
+        dist.all_to_all_single(rc, cnt)
+        both = ops.to_list(ops.cat([cnt.view(world, El).sum(1), rc.view(world, El).sum(1)]))
+        per_dest, per_src = both[:world], both[world:]
+        R = sum(per_src)
+        recv = ops.empty_rows(R)
+        pe[1].record(stream)
+        dist.all_to_all_single(recv, send, output_split_sizes=per_src, input_split_sizes=per_dest)
+        pe[2].record(stream)
+        y_rows = ops.expert_ffn(recv, rc, R, x)
+        pe[3].record(stream)
+        y_back = ops.empty_results(send.shape[0])
+        dist.all_to_all_single(y_back, y_rows[:R], output_split_sizes=per_dest,
+                               input_split_sizes=per_src)
+        pe[4].record(stream)
+        ops.combine(ids, wts, pos, y_back, y_rows[R:])
+        pe[5].record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(5)]
+        phases = {"dispatch": round(ph[0], 4), "all_to_all_rows": round(ph[1], 4),
+                  "expert_ffn": round(ph[2], 4), "all_to_all_results": round(ph[3], 4),
+                  "combine": round(ph[4], 4)}
     rb = layer.row_bytes
     sent_remote = sum(n for d, n in enumerate(per_dest) if d != rank)
     res = None
@@ -727,12 +746,12 @@ def run_config4(args):
                        "experts_per_rank": El, "dispatch_row_bytes": int(rb),
                        "l2": "flushed between steps (256 MiB memset outside the timed events)",
                        "parallelism": f"expert parallel x{world}"},
-            "phases_ms_max_over_ranks": {
-                "dispatch": round(ph[0], 4), "all_to_all_rows": round(ph[1], 4),
-                "expert_ffn": round(ph[2], 4), "all_to_all_results": round(ph[3], 4),
-                "combine": round(ph[4], 4)},
+            "transport": args.ep_transport,
+            "phases_ms_max_over_ranks": phases,
             "rank0_remote_rows_sent": sent_remote,
-            "gpu_launches": 16 * args.steps,
+            # count, scan, pack | totals, units, permute, pack_local, map_tail, up,
+            # down | combine (the NCCL transport adds the collectives' kernels)
+            "gpu_launches": 11 * args.steps,
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:
@@ -826,6 +845,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
                     help="2: one-token decode FFN (default); 3: 2048-token batched FFN; "
                          "4: expert-parallel layer over the ranks")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="config 4: rows over NVLink peer stores (p2p) or NCCL all-to-all")
     ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()

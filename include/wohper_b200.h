@@ -265,6 +265,44 @@ wh_status wh_ep_combine(wh_ctx* ctx, const wh_moe_plan* plan, const int32_t* ids
                         const float* weights, const int32_t* pos, int tokens, const float* y_back,
                         const float* y_shared, float* y, wh_stream_t stream);
 
+/* Expert parallelism over peer memory: the same step without NCCL and without */
+/* a host synchronisation.  Each rank creates a window (device memory the      */
+/* other ranks store into over NVLink), exports its CUDA IPC handle, and       */
+/* connects to every rank's handle (the caller moves the handles, e.g. with an */
+/* all-gather).  Per step, on every rank and in this order:                    */
+/*   wh_ep_p2p_dispatch -> wh_ep_p2p_expert_ffn -> wh_ep_p2p_combine          */
+/* The kernels wait on the other ranks' arrival flags with a bounded wait     */
+/* (WH_ERR_TIMEOUT at the next wh_ctx_sync when a rank never arrives).  All    */
+/* ranks run the same number of steps; before wh_ep_window_destroy every rank  */
+/* finishes its last step (device synchronised, then a host barrier), so that  */
+/* no rank still stores into a window being freed.                             */
+/* ------------------------------------------------------------------------ */
+#define WH_EP_IPC_HANDLE_BYTES 64
+typedef struct wh_ep_window wh_ep_window;
+/* Bytes of one rank's exported window for at most max_tokens tokens per rank
+ * (rows are laid out with room for max_tokens * topk rows from every source). */
+size_t wh_ep_window_bytes(const wh_moe_plan* plan, int world, int max_tokens);
+/* Allocates the window of `rank` and writes its IPC handle (64 bytes). */
+wh_status wh_ep_window_create(wh_ctx* ctx, const wh_moe_plan* plan, int world, int rank,
+                              int max_tokens, wh_ep_window** out, uint8_t* ipc_handle);
+/* handles: [world][64], rank r's handle at r * 64 (this rank's own is ignored). */
+wh_status wh_ep_window_connect(wh_ep_window* window, const uint8_t* handles);
+void wh_ep_window_destroy(wh_ep_window* window);
+/* Act quant of x [tokens][hidden] and one row per route stored into the
+ * destination rank's window; pos [tokens*topk] receives the row of each route's
+ * result in this rank's window (-1 for an invalid id, WH_ERR_DEVICE_ARG). */
+wh_status wh_ep_p2p_dispatch(wh_ctx* ctx, wh_ep_window* window, const float* x, int tokens,
+                             const int32_t* ids, int32_t* pos, wh_stream_t stream);
+/* Waits for every source's rows, runs the local experts over them and the
+ * shared expert over x_local (y_shared [tokens][hidden]); each result row is
+ * stored into the window of the rank that owns its token. */
+wh_status wh_ep_p2p_expert_ffn(wh_ctx* ctx, wh_ep_window* window, const float* x_local,
+                               int tokens, float* y_shared, wh_stream_t stream);
+/* Waits for every destination's results, then y as wh_ep_combine. */
+wh_status wh_ep_p2p_combine(wh_ctx* ctx, wh_ep_window* window, const int32_t* ids,
+                            const float* weights, const int32_t* pos, int tokens,
+                            const float* y_shared, float* y, wh_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Test hooks (host-only, no device work): expose the host-side pieces the   */
 /* kernels rely on so CPU tests can pin them.                                */

@@ -25,6 +25,9 @@ class NumpyOps:
     def to_list(self, t):
         return [int(v) for v in t.tolist()]
 
+    def cat(self, ts):
+        return torch.cat(ts)
+
     def empty_rows(self, n):
         return torch.empty(n, self.hidden, dtype=torch.float32)
 

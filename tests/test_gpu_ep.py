@@ -1,7 +1,7 @@
 """Expert parallelism on the GPU: the expert-parallel layer at world size 1
-reproduces the single-GPU batched layer given the same routes, and (when two
-or more GPUs are visible) a 2-rank NCCL run reproduces it too
-(tests/ep_worker.py)."""
+(both transports, several steps through the same window) reproduces the
+single-GPU batched layer given the same routes, and (when two or more GPUs are
+visible) 2-rank runs of both transports reproduce it too (tests/ep_worker.py)."""
 import os
 import socket
 import subprocess
@@ -55,19 +55,22 @@ def test_ep_world1_matches_batched_layer():
         ids = torch.zeros(T, 6, dtype=torch.int32, device="cuda")
         w = torch.zeros(T, 6, device="cuda")
         want = layer.forward(x, ids=ids, weights=w)
-        ep = EpMoeLayer(ctx, experts, wexp(E), 1)
-        got = ep.forward(x, ids, w)
-        ctx.sync()
-        diff = float((got - want).abs().max())
-        assert diff <= 1e-6 * float(want.abs().max()), diff
-        ep.close()
+        for transport in ("nccl", "p2p"):
+            ep = EpMoeLayer(ctx, experts, wexp(E), 1, transport=transport, max_tokens=T)
+            for step in range(3):  # the peer transport reuses its window (epochs)
+                n = (T, T // 2, 0)[step]
+                got = ep.forward(x[:n].contiguous(), ids[:n].contiguous(), w[:n].contiguous())
+                ctx.sync()
+                diff = float((got - want[:n]).abs().max()) if n else 0.0
+                assert diff <= 1e-6 * float(want.abs().max()), (transport, step, diff)
+            ep.close()
         layer.close()
         ctx.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_two_ranks_nccl():
+def test_ep_two_ranks():
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")

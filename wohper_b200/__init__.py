@@ -50,7 +50,9 @@ EXPORTS = (
     "wh_moe_scratch_bytes", "wh_moe_ffn", "wh_debug_act_quant_table", "wh_debug_e4m3_round",
     "wh_ctx_set_profiling", "wh_ctx_phase_times", "wh_debug_e4m3_round_n",
     "wh_fp4_expert_forward_noalloc", "wh_ep_row_bytes", "wh_ep_scratch_bytes", "wh_ep_dispatch",
-    "wh_ep_expert_ffn", "wh_ep_combine",
+    "wh_ep_expert_ffn", "wh_ep_combine", "wh_ep_window_bytes", "wh_ep_window_create",
+    "wh_ep_window_connect", "wh_ep_window_destroy", "wh_ep_p2p_dispatch",
+    "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine",
 )
 
 
@@ -117,6 +119,13 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_ep_dispatch": (st, [vp, vp, i, vp, i, vp, vp, vp, vp, vp, sz, vp]),
         "wh_ep_expert_ffn": (st, [vp, vp, i, vp, vp, i, vp, i, vp, vp, sz, vp]),
         "wh_ep_combine": (st, [vp, vp, vp, vp, vp, i, vp, vp, vp, vp]),
+        "wh_ep_window_bytes": (sz, [vp, i, i]),
+        "wh_ep_window_create": (st, [vp, vp, i, i, i, C.POINTER(vp), vp]),
+        "wh_ep_window_connect": (st, [vp, vp]),
+        "wh_ep_window_destroy": (None, [vp]),
+        "wh_ep_p2p_dispatch": (st, [vp, vp, vp, i, vp, vp, vp]),
+        "wh_ep_p2p_expert_ffn": (st, [vp, vp, vp, i, vp, vp]),
+        "wh_ep_p2p_combine": (st, [vp, vp, vp, vp, vp, i, vp, vp, vp]),
         "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
         "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
         "wh_moe_plan_destroy": (None, [vp]),

@@ -994,6 +994,7 @@ namespace {
 struct EpScratch {
   int* slot;
   int* off;
+  int* seg_cnt;
   int* totals;
   int* seg_off;
   int* src_off;
@@ -1023,6 +1024,7 @@ EpScratch ep_scratch_layout(const wh_moe_plan* p, int world, int tokens, int max
   };
   s.slot = reinterpret_cast<int*>(take(sizeof(int) * (size_t)tokens * d.topk));
   s.off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
+  s.seg_cnt = reinterpret_cast<int*>(take(sizeof(int) * nseg));
   s.totals = reinterpret_cast<int*>(take(sizeof(int) * (El + 1)));
   s.seg_off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
   s.src_off = reinterpret_cast<int*>(take(sizeof(int) * nseg));
@@ -1102,19 +1104,23 @@ wh_status wh_ep_expert_ffn(wh_ctx* c, const wh_moe_plan* p, int world, const uin
   wh_status st;
   if ((st = ep_check(p, world)) != WH_OK) return st;
   if (recv_rows < 0 || tokens < 0) return fail(WH_ERR_INVALID_SHAPE, "negative rows");
-  if (!recv_counts || !y_rows || !scratch || (recv_rows > 0 && !recv) || (tokens > 0 && !x_local))
-    return fail(WH_ERR_INVALID_POINTER, "null buffer");
   const auto& d = p->d;
   const int has_shared = d.shared ? 1 : 0;
   const int rows = recv_rows + (has_shared ? tokens : 0);
+  if (rows == 0) return WH_OK;
+  if (!recv_counts || !y_rows || !scratch || (recv_rows > 0 && !recv) || (tokens > 0 && !x_local))
+    return fail(WH_ERR_INVALID_POINTER, "null buffer");
   EpScratch s = ep_scratch_layout(p, world, tokens, recv_rows, static_cast<uint8_t*>(scratch));
   if (scratch_bytes < s.bytes) return fail(WH_ERR_SCRATCH_TOO_SMALL, "ep scratch too small");
-  if (rows == 0) return WH_OK;
   const int rb = (int)wh_ep_row_bytes(d.hidden);
   EpSortArgs so{};
   so.recv_counts = recv_counts;
   so.world = world;
   so.local_experts = d.num_experts;
+  so.seg_stride = 0;
+  so.max_rows = recv_rows;
+  so.status = c->status;
+  so.seg_cnt = s.seg_cnt;
   so.totals = s.totals;
   so.seg_off = s.seg_off;
   so.src_off = s.src_off;
@@ -1179,6 +1185,331 @@ wh_status wh_ep_combine(wh_ctx* c, const wh_moe_plan* p, const int32_t* ids, con
     return fail(WH_ERR_INVALID_POINTER, "null buffer");
   WH_CUDA(launch_ep_combine(ids, weights, pos, tokens, p->d.topk, y_back, y_shared,
                             p->d.shared ? 1 : 0, y, p->d.hidden, stream));
+  return WH_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Expert parallelism over peer memory (CUDA IPC windows, NVLink stores).
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == WH_EP_IPC_HANDLE_BYTES, "IPC handle size");
+
+struct wh_ep_window {
+  wh_ctx* ctx = nullptr;
+  const wh_moe_plan* plan = nullptr;
+  int world = 0, rank = 0, max_tokens = 0, cap = 0, row_bytes = 0;
+  // the exported window: [recv rows | counts | row flags, result flags | result rows]
+  uint8_t* base = nullptr;
+  size_t bytes = 0, o_recv = 0, o_counts = 0, o_flags = 0, o_yback = 0;
+  // rank-private state
+  uint8_t* local = nullptr;
+  EpScratch sc{};
+  int* cnt = nullptr;
+  int* off = nullptr;
+  uint32_t* done = nullptr;  // [2] arrival counters: dispatch, down GEMM
+  EpPeer* peers = nullptr;   // [world]
+  float** yback_peers = nullptr;        // [world] peer d's result rows
+  uint64_t** res_flag_peers = nullptr;  // [world] &peer d's res_flag[rank]
+  CUtensorMap bup{}, bdown{};
+  std::vector<void*> opened;
+  uint64_t epoch = 0;
+  int stage = 0;  // 0 idle / after combine, 1 dispatched, 2 expert FFN issued
+  bool connected = false;
+};
+
+namespace {
+struct EpWindowLayout {
+  size_t recv, counts, flags, yback, bytes;
+};
+EpWindowLayout ep_window_layout(const wh_moe_plan* p, int world, int cap) {
+  const auto& d = p->d;
+  EpWindowLayout w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  w.recv = take((size_t)world * cap * wh_ep_row_bytes(d.hidden));
+  w.counts = take(sizeof(int) * (size_t)world * d.num_experts);
+  w.flags = take(sizeof(uint64_t) * 2 * (size_t)world);
+  w.yback = take(sizeof(float) * (size_t)world * cap * d.hidden);
+  w.bytes = off;
+  return w;
+}
+wh_status ep_window_args(const wh_moe_plan* p, int world, int rank, int max_tokens) {
+  wh_status st;
+  if ((st = ep_check(p, world)) != WH_OK) return st;
+  if (rank < 0 || rank >= world) return fail(WH_ERR_INVALID_SHAPE, "rank out of [0, world)");
+  if (max_tokens < 1) return fail(WH_ERR_INVALID_SHAPE, "max_tokens < 1");
+  if ((long long)world * max_tokens * p->d.topk + max_tokens > (1LL << 30))
+    return fail(WH_ERR_INVALID_SHAPE, "world * max_tokens * topk too large");
+  return WH_OK;
+}
+void ep_window_free(wh_ep_window* w) {
+  for (void* q : w->opened) cudaIpcCloseMemHandle(q);
+  if (w->base) cudaFree(w->base);
+  if (w->local) cudaFree(w->local);
+  delete w;
+}
+}  // namespace
+
+extern "C" {
+
+size_t wh_ep_window_bytes(const wh_moe_plan* p, int world, int max_tokens) {
+  if (ep_window_args(p, world, 0, max_tokens) != WH_OK) return 0;
+  return ep_window_layout(p, world, max_tokens * p->d.topk).bytes;
+}
+
+wh_status wh_ep_window_create(wh_ctx* c, const wh_moe_plan* p, int world, int rank,
+                              int max_tokens, wh_ep_window** out, uint8_t* ipc_handle) {
+  if (!c || !out || !ipc_handle) return fail(WH_ERR_INVALID_POINTER, "null ctx/out/handle");
+  *out = nullptr;
+  wh_status st;
+  if ((st = ep_window_args(p, world, rank, max_tokens)) != WH_OK) return st;
+  const auto& d = p->d;
+  wh_ep_window* w = new wh_ep_window();
+  w->ctx = c;
+  w->plan = p;
+  w->world = world;
+  w->rank = rank;
+  w->max_tokens = max_tokens;
+  w->cap = max_tokens * d.topk;
+  w->row_bytes = (int)wh_ep_row_bytes(d.hidden);
+  const EpWindowLayout L = ep_window_layout(p, world, w->cap);
+  w->bytes = L.bytes;
+  w->o_recv = L.recv;
+  w->o_counts = L.counts;
+  w->o_flags = L.flags;
+  w->o_yback = L.yback;
+  const int nseg = world * d.num_experts;
+  const size_t sc_bytes =
+      ep_scratch_layout(p, world, max_tokens, world * w->cap, nullptr).bytes;
+  const size_t tab = align256(sc_bytes) + 2 * align256(sizeof(int) * nseg) + 256 +
+                     align256(sizeof(EpPeer) * world) + 2 * align256(sizeof(void*) * world);
+  cudaError_t e = cudaMalloc(&w->base, w->bytes);
+  if (e == cudaSuccess) e = cudaMemset(w->base, 0, w->bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->local, tab);
+  if (e == cudaSuccess) e = cudaMemset(w->local, 0, tab);
+  cudaIpcMemHandle_t h{};
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, w->base);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    ep_window_free(w);
+    return cuda_fail(e, "expert-parallel window");
+  }
+  size_t o = 0;
+  w->sc = ep_scratch_layout(p, world, max_tokens, world * w->cap, w->local);
+  o += align256(sc_bytes);
+  w->cnt = reinterpret_cast<int*>(w->local + o);
+  o += align256(sizeof(int) * nseg);
+  w->off = reinterpret_cast<int*>(w->local + o);
+  o += align256(sizeof(int) * nseg);
+  w->done = reinterpret_cast<uint32_t*>(w->local + o);
+  o += 256;
+  w->peers = reinterpret_cast<EpPeer*>(w->local + o);
+  o += align256(sizeof(EpPeer) * world);
+  w->yback_peers = reinterpret_cast<float**>(w->local + o);
+  o += align256(sizeof(void*) * world);
+  w->res_flag_peers = reinterpret_cast<uint64_t**>(w->local + o);
+  // B operand maps over the fixed sorted-row and h buffers
+  const int rows = world * w->cap + max_tokens;
+  if ((st = make_u8_map_strided(&w->bup, w->sc.sorted, rows, d.hidden, w->row_bytes, kGN)) !=
+          WH_OK ||
+      (st = make_u8_map(&w->bdown, w->sc.hq, rows, d.inter, kGN, 128)) != WH_OK) {
+    ep_window_free(w);
+    return st;
+  }
+  memcpy(ipc_handle, &h, WH_EP_IPC_HANDLE_BYTES);
+  *out = w;
+  return WH_OK;
+}
+
+wh_status wh_ep_window_connect(wh_ep_window* w, const uint8_t* handles) {
+  if (!w || !handles) return fail(WH_ERR_INVALID_POINTER, "null window/handles");
+  if (w->connected) return fail(WH_ERR_UNSUPPORTED, "window already connected");
+  std::vector<EpPeer> peers(w->world);
+  std::vector<float*> yb(w->world);
+  std::vector<uint64_t*> rf(w->world);
+  for (int d = 0; d < w->world; ++d) {
+    uint8_t* b = w->base;
+    if (d != w->rank) {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, handles + (size_t)d * WH_EP_IPC_HANDLE_BYTES, WH_EP_IPC_HANDLE_BYTES);
+      void* q = nullptr;
+      WH_CUDA(cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess));
+      w->opened.push_back(q);
+      b = static_cast<uint8_t*>(q);
+    }
+    peers[d].recv = b + w->o_recv;
+    peers[d].counts = reinterpret_cast<int*>(b + w->o_counts);
+    peers[d].row_flag = reinterpret_cast<uint64_t*>(b + w->o_flags);
+    peers[d].res_flag = peers[d].row_flag + w->world;
+    peers[d].yback = reinterpret_cast<float*>(b + w->o_yback);
+    yb[d] = peers[d].yback;
+    rf[d] = peers[d].res_flag + w->rank;
+  }
+  WH_CUDA(cudaMemcpy(w->peers, peers.data(), sizeof(EpPeer) * w->world, cudaMemcpyHostToDevice));
+  WH_CUDA(cudaMemcpy(w->yback_peers, yb.data(), sizeof(void*) * w->world,
+                     cudaMemcpyHostToDevice));
+  WH_CUDA(cudaMemcpy(w->res_flag_peers, rf.data(), sizeof(void*) * w->world,
+                     cudaMemcpyHostToDevice));
+  w->connected = true;
+  return WH_OK;
+}
+
+void wh_ep_window_destroy(wh_ep_window* w) {
+  if (!w) return;
+  cudaDeviceSynchronize();
+  ep_window_free(w);
+}
+
+wh_status wh_ep_p2p_dispatch(wh_ctx* c, wh_ep_window* w, const float* x, int tokens,
+                             const int32_t* ids, int32_t* pos, wh_stream_t stream) {
+  if (!c || !w) return fail(WH_ERR_INVALID_POINTER, "null ctx/window");
+  if (!w->connected) return fail(WH_ERR_UNSUPPORTED, "window not connected");
+  if (w->stage != 0) return fail(WH_ERR_UNSUPPORTED, "dispatch before the previous combine");
+  if (tokens < 0 || tokens > w->max_tokens)
+    return fail(WH_ERR_INVALID_SHAPE, "tokens outside [0, max_tokens]");
+  if (tokens > 0 && (!x || !ids || !pos)) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  if (tokens > 0 && !aligned(x, 16)) return fail(WH_ERR_INVALID_POINTER, "alignment");
+  const auto& d = w->plan->d;
+  EpArgs a{};
+  a.world = w->world;
+  a.local_experts = d.num_experts;
+  a.topk = d.topk;
+  a.hidden = d.hidden;
+  a.row_bytes = w->row_bytes;
+  a.ids = ids;
+  a.tokens = tokens;
+  a.cnt = w->cnt;
+  a.slot = w->sc.slot;
+  a.status = c->status;
+  EpP2pArgs q{};
+  q.world = w->world;
+  q.rank = w->rank;
+  q.local_experts = d.num_experts;
+  q.topk = d.topk;
+  q.hidden = d.hidden;
+  q.row_bytes = w->row_bytes;
+  q.cap = w->cap;
+  q.ids = ids;
+  q.tokens = tokens;
+  q.cnt = w->cnt;
+  q.slot = w->sc.slot;
+  q.off = w->off;
+  q.pos = pos;
+  q.peers = w->peers;
+  q.done = w->done;
+  q.epoch = w->epoch + 1;
+  q.status = c->status;
+  WH_CUDA(launch_ep_p2p_dispatch(q, a, x, stream));
+  ++w->epoch;
+  w->stage = 1;
+  return WH_OK;
+}
+
+wh_status wh_ep_p2p_expert_ffn(wh_ctx* c, wh_ep_window* w, const float* x_local, int tokens,
+                               float* y_shared, wh_stream_t stream) {
+  if (!c || !w) return fail(WH_ERR_INVALID_POINTER, "null ctx/window");
+  if (w->stage != 1) return fail(WH_ERR_UNSUPPORTED, "expert FFN without a dispatch");
+  if (tokens < 0 || tokens > w->max_tokens)
+    return fail(WH_ERR_INVALID_SHAPE, "tokens outside [0, max_tokens]");
+  const auto& d = w->plan->d;
+  const int has_shared = d.shared ? 1 : 0;
+  if (has_shared && tokens > 0 && (!x_local || !y_shared))
+    return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  if (has_shared && tokens > 0 && !aligned(x_local, 16))
+    return fail(WH_ERR_INVALID_POINTER, "alignment");
+  const int peer_rows = w->world * w->cap;
+  const EpScratch& s = w->sc;
+  EpSortArgs so{};
+  so.recv_counts = reinterpret_cast<const int*>(w->base + w->o_counts);
+  so.world = w->world;
+  so.local_experts = d.num_experts;
+  so.seg_stride = w->cap;
+  so.max_rows = peer_rows;
+  so.wait = reinterpret_cast<const uint64_t*>(w->base + w->o_flags);
+  so.epoch = w->epoch;
+  so.status = c->status;
+  so.seg_cnt = s.seg_cnt;
+  so.totals = s.totals;
+  so.seg_off = s.seg_off;
+  so.src_off = s.src_off;
+  so.exp_off = s.exp_off;
+  so.recv = w->base + w->o_recv;
+  so.sorted = s.sorted;
+  so.row_map = s.row_map;
+  so.row_bytes = w->row_bytes;
+  GroupedPlanArgs g{};
+  g.tokens = has_shared ? tokens : 0;
+  g.num_experts = d.num_experts;
+  g.has_shared = has_shared;
+  g.counts = s.totals;
+  g.offsets = s.exp_off;
+  g.units_up = s.units_up;
+  g.units_down = s.units_down;
+  g.n_units = s.n_units;
+  g.mt_up = d.inter / 128;
+  g.mt_down = d.hidden / 128;
+  g.tile_n = kGN;
+  g.status = c->status;
+  WH_CUDA(launch_ep_prepare(so, g, x_local, d.hidden, peer_rows, stream));
+  GroupedArgs up{};
+  up.amaps = w->plan->set.gmaps;
+  up.experts = w->plan->set.experts;
+  up.K = d.hidden;
+  up.M = d.inter;
+  up.bsf = s.sorted + d.hidden;
+  up.bsf_stride = w->row_bytes;
+  up.rows_total = peer_rows + w->max_tokens;
+  up.units = s.units_up;
+  up.n_units = s.n_units;
+  up.hq = s.hq;
+  up.hsf = s.hsf;
+  up.status = c->status;
+  GroupedArgs dn = up;
+  dn.K = d.inter;
+  dn.M = d.hidden;
+  dn.bsf = s.hsf;
+  dn.bsf_stride = d.inter / 32;
+  dn.units = s.units_down;
+  dn.n_units = s.n_units + 1;
+  dn.hq = nullptr;
+  dn.hsf = nullptr;
+  dn.y = y_shared;
+  dn.y_row_map = s.row_map;
+  dn.y_peers = w->yback_peers;
+  dn.y_peer_rows = peer_rows;
+  dn.y_cap = w->cap;
+  dn.y_self_off = w->rank * w->cap;
+  dn.sig_flags = w->res_flag_peers;
+  dn.sig_done = w->done + 1;
+  dn.sig_n = w->world;
+  dn.sig_epoch = w->epoch;
+  WH_CUDA(launch_grouped_gemm(true, kGN, w->bup, up, c->num_sms, stream));
+  WH_CUDA(launch_grouped_gemm(false, kGN, w->bdown, dn, c->num_sms, stream));
+  w->stage = 2;
+  return WH_OK;
+}
+
+wh_status wh_ep_p2p_combine(wh_ctx* c, wh_ep_window* w, const int32_t* ids, const float* weights,
+                            const int32_t* pos, int tokens, const float* y_shared, float* y,
+                            wh_stream_t stream) {
+  if (!c || !w) return fail(WH_ERR_INVALID_POINTER, "null ctx/window");
+  if (w->stage != 2) return fail(WH_ERR_UNSUPPORTED, "combine without an expert FFN");
+  if (tokens < 0 || tokens > w->max_tokens)
+    return fail(WH_ERR_INVALID_SHAPE, "tokens outside [0, max_tokens]");
+  const auto& d = w->plan->d;
+  if (tokens > 0 && (!ids || !weights || !pos || !y || (d.shared && !y_shared)))
+    return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  WH_CUDA(launch_ep_p2p_combine(
+      ids, weights, pos, tokens, d.topk, reinterpret_cast<const float*>(w->base + w->o_yback),
+      y_shared, d.shared ? 1 : 0, y, d.hidden,
+      reinterpret_cast<const uint64_t*>(w->base + w->o_flags) + w->world, w->world, w->epoch,
+      c->status, stream));
+  w->stage = 0;
   return WH_OK;
 }
 

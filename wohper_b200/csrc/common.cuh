@@ -108,6 +108,52 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// system-scope flags between ranks (bounded waits, never a trap)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Wait until *p >= epoch; false (and WH_DEV_TIMEOUT) after the deadline or when
+// another wait of this launch sequence already timed out.
+__device__ __forceinline__ bool wait_epoch(const uint64_t* p, uint64_t epoch, uint32_t* status) {
+  if (ld_acquire_sys(p) >= epoch) return true;
+  const uint64_t start = globaltimer();
+  for (uint32_t it = 0; ld_acquire_sys(p) < epoch; ++it) {
+    if ((status && (*(volatile uint32_t*)status & WH_DEV_TIMEOUT)) ||
+        globaltimer() - start > WH_WAIT_NS || it > (1u << 26)) {
+      flag(status, WH_DEV_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// every thread of the CTA calls this after its last global store; returns
+// true in the (one) CTA that arrived last, after which all its threads may
+// read what the other CTAs stored
+__device__ __forceinline__ bool last_cta_arrival(uint32_t* done) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(done, 1u);
+    last = prev == gridDim.x - 1;
+    if (last) {
+      __threadfence_system();
+      *done = 0;
+    }
+  }
+  __syncthreads();
+  return last;
+}
+
 // Named barrier `id` over `nthreads` threads (a multiple of 32) that also ANDs
 // a predicate across them; warps that already left the kernel are not counted.
 __device__ __forceinline__ int bar_and(int id, int nthreads, int pred) {

@@ -57,6 +57,17 @@ struct GroupedArgs {
   uint8_t* hsf;              // up: [rows][M/32] UE8M0
   float* y;                  // down: [rows][M]
   const int* y_row_map;      // down, nullable: output row of each B row
+  // down, peer transport: output rows m < y_peer_rows belong to source rank
+  // m / y_cap and go to row y_self_off + m % y_cap of y_peers[m / y_cap] (that
+  // rank's window); rows m >= y_peer_rows go to row m - y_peer_rows of y
+  float* const* y_peers;
+  int y_peer_rows, y_cap, y_self_off;
+  // nullable: after its last store, the kernel's last CTA releases
+  // *sig_flags[i] = sig_epoch for i < sig_n (arrival counter sig_done)
+  uint64_t* const* sig_flags;
+  uint32_t* sig_done;
+  int sig_n;
+  uint64_t sig_epoch;
   uint32_t* status;
 };
 
@@ -391,8 +402,15 @@ __global__ void __launch_bounds__(kGThreads, 1)
           for (int j = 0; j < 16; ++j)
             if (n0 + j < un.w) {
               const int row = un.z + n0 + j;
-              a.y[(long long)(a.y_row_map ? a.y_row_map[row] : row) * a.M + feat] =
-                  __uint_as_float(v1[j]);
+              const int m = a.y_row_map ? a.y_row_map[row] : row;
+              float* dst;
+              if (m < a.y_peer_rows) {
+                const int src = m / a.y_cap;
+                dst = a.y_peers[src] + (long long)(a.y_self_off + m - src * a.y_cap) * a.M;
+              } else {
+                dst = a.y + (long long)(m - a.y_peer_rows) * a.M;
+              }
+              dst[feat] = __uint_as_float(v1[j]);
             }
         }
       }
@@ -404,6 +422,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, kGTmemCols);
+  if (a.sig_flags && last_cta_arrival(a.sig_done) && tid < a.sig_n)
+    st_release_sys(a.sig_flags[tid], a.sig_epoch);
 }
 
 // ---------------------------------------------------------------------------

@@ -10,10 +10,19 @@ forward on every rank:
     all-to-all of the f32 result rows back to their token's rank
     combine (ascending expert id, w / sum(w)) + shared
 
-The collective sequence (`ep_step`) is written once against a small device-ops
-interface: `DeviceOps` runs the library's kernels through the C ABI (NCCL
-process group on the GPU); the CPU tests drive the same sequence over gloo with
-a numpy stand-in for the kernels.
+Two transports move the rows:
+
+* "p2p" (default): no collective and no host synchronisation per step.  Every
+  rank exports a window of device memory over CUDA IPC (handles exchanged once
+  with the process group); the dispatch kernel stores each route's row into its
+  destination's window over NVLink, the down GEMM's epilogue stores each result
+  row into the window of the token's rank, and arrival flags with bounded
+  device-side waits order the three calls (wh_ep_p2p_*).
+* "nccl": the collective sequence `ep_step` (all-to-all of counts, rows and
+  results over the process group), written once against a small device-ops
+  interface: `DeviceOps` runs the library's kernels through the C ABI; the CPU
+  tests drive the same sequence over gloo with a numpy stand-in for the
+  kernels.
 """
 from __future__ import annotations
 
@@ -33,8 +42,10 @@ def ep_step(ops, x, ids, weights, world: int, local_experts: int, group=None):
     send, send_counts, pos = ops.dispatch(x, ids)
     recv_counts = ops.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
-    per_dest = ops.to_list(send_counts.view(world, local_experts).sum(1))
-    per_src = ops.to_list(recv_counts.view(world, local_experts).sum(1))
+    # one host synchronisation for both split lists
+    both = ops.to_list(ops.cat([send_counts.view(world, local_experts).sum(1),
+                                recv_counts.view(world, local_experts).sum(1)]))
+    per_dest, per_src = both[:world], both[world:]
     R = sum(per_src)
     recv = ops.empty_rows(R)
     dist.all_to_all_single(recv, send, output_split_sizes=per_src, input_split_sizes=per_dest,
@@ -59,6 +70,11 @@ class DeviceOps:
 
     def to_list(self, t):
         return [int(v) for v in t.tolist()]
+
+    def cat(self, ts):
+        import torch
+
+        return torch.cat(ts)
 
     def empty_rows(self, n):
         import torch
@@ -118,10 +134,15 @@ class EpMoeLayer:
 
     def __init__(self, ctx: Context, local_experts: Sequence[DeepSeekV4Fp4Expert],
                  shared: Optional[DeepSeekV4Fp4Expert], world: int, topk: int = 6,
-                 group=None):
+                 group=None, transport: str = "p2p", max_tokens: int = 1024):
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"transport must be 'p2p' or 'nccl', not {transport!r}")
         self.ctx = ctx
         self.world = world
         self.group = group
+        self.transport = transport
+        self.max_tokens = max_tokens
+        self.window = None
         self.topk = topk
         self.local_experts = len(local_experts)
         self.hidden = local_experts[0].w1.cols
@@ -137,6 +158,27 @@ class EpMoeLayer:
         self.plan = h
         self.row_bytes = lib().wh_ep_row_bytes(self.hidden)
         self.scratch = None
+        if transport == "p2p":
+            self._connect()
+
+    def _connect(self):
+        """Create this rank's window and connect to every rank's (collective)."""
+        import torch.distributed as dist
+
+        rank = dist.get_rank(self.group) if self.world > 1 else 0
+        handle = (C.c_uint8 * 64)()
+        win = C.c_void_p()
+        _check(lib().wh_ep_window_create(self.ctx.handle, self.plan, self.world, rank,
+                                         self.max_tokens, C.byref(win), handle))
+        self.window = win
+        mine = bytes(handle)
+        if self.world > 1:
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=self.group)
+        else:
+            allh = [mine]
+        buf = (C.c_uint8 * (64 * self.world)).from_buffer_copy(b"".join(allh))
+        _check(lib().wh_ep_window_connect(self.window, buf))
 
     def _ensure_scratch(self, tokens: int, recv_rows: int):
         import torch
@@ -147,10 +189,49 @@ class EpMoeLayer:
                                        device=self.device)
 
     def forward(self, x, ids, weights):
-        return ep_step(DeviceOps(self), x, ids, weights, self.world, self.local_experts,
-                       self.group)
+        if self.transport == "nccl":
+            return ep_step(DeviceOps(self), x, ids, weights, self.world, self.local_experts,
+                           self.group)
+        return self.forward_p2p(x, ids, weights)
+
+    def forward_p2p(self, x, ids, weights, marks=None):
+        """The peer-transport step; `marks(i)` (optional) is called before the
+        first call and after each of the three (event records for phase times)."""
+        import torch
+
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
+        L, s, h = lib(), _stream(None), self.ctx.handle
+        pos = torch.empty(T * self.topk, dtype=torch.int32, device=self.device)
+        ysh = torch.empty(T, self.hidden, dtype=torch.float32, device=self.device)
+        y = torch.empty(T, self.hidden, dtype=torch.float32, device=self.device)
+        if marks:
+            marks(0)
+        _check(L.wh_ep_p2p_dispatch(h, self.window, _ptr(x), T, _ptr(ids), _ptr(pos), s))
+        if marks:
+            marks(1)
+        _check(L.wh_ep_p2p_expert_ffn(h, self.window, _ptr(x), T, _ptr(ysh), s))
+        if marks:
+            marks(2)
+        _check(L.wh_ep_p2p_combine(h, self.window, _ptr(ids), _ptr(weights), _ptr(pos), T,
+                                   _ptr(ysh), _ptr(y), s))
+        if marks:
+            marks(3)
+        return y
 
     def close(self):
+        """Collective for the peer transport: no rank may still store into a
+        window that is being freed."""
+        if self.window is not None:
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            lib().wh_ep_window_destroy(self.window)
+            self.window = None
         if getattr(self, "plan", None):
             lib().wh_moe_plan_destroy(self.plan)
             self.plan = None
