@@ -48,6 +48,10 @@ DOWN_BYTES = SLOTS * (PACKED_W2 + SCALES_W2)
 # DRAM bytes (read + write) of one moe_up launch from an ncu capture of the
 # --ncu-case moe16 workload, which processes the same units per launch
 UP_TRAFFIC = 63_292_672
+# grouped up GEMM: DRAM bytes read per algorithmic byte read in the ncu capture of the
+# grouped16 case (161,668,608 / 159,088,640; profiles/grouped_gemm_grouped16.md); the
+# config-3 launch is too large to capture, its traffic is scaled by the units processed
+GROUPED_UP_TRAFFIC_RATIO = 161_668_608 / 159_088_640
 METRIC = "decode tokens/s (one-token FP4 MoE FFN, config 2)"
 WORKLOAD = ("config 2: one-token FP4 MoE FFN, 256 experts 4096->2048->4096 E2M1/UE8M0-32, "
             "bf16 router top-6 softmax-renormalised, 6 routed + 1 shared expert")
@@ -571,7 +575,9 @@ def run_config3(args):
             "roofline": {"kernel": "grouped_gemm_kernel<up> (w1+w3 of the used experts, SwiGLU, act quant)",
                          "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
-                         "algorithmic_bytes": int(up_bytes), "traffic": None,
+                         "algorithmic_bytes": int(up_bytes),
+                         "traffic": int(up_bytes * GROUPED_UP_TRAFFIC_RATIO),
+                         "traffic_note": "scaled from the ncu capture of the grouped16 case",
                          "tensor_tflops": round(up_flops / (up_ms * 1e-3) / 1e12, 1)},
             "step_tflops": round(step_flops / (ms_step * 1e-3) / 1e12, 1),
             "e2e": {"value": round(world * T3 / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
