@@ -78,7 +78,8 @@ __device__ __forceinline__ int32_t total_key(float f) {
 // The CTA that arrives last selects the top-k and computes the route weights.
 // ---------------------------------------------------------------------------
 constexpr int kRouterRowsPerCta = 4;
-constexpr int kRouterThreads = 64;
+constexpr int kRouterWorkers = 64;                  // warps 0-1: logits, act quant, top-k
+constexpr int kRouterThreads = kRouterWorkers + 32;  // warp 2: the dry top-k pass
 
 struct RouterSmemPlan {
   int row_stride;  // bytes
@@ -114,7 +115,8 @@ __device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* p, uint32_t v) 
 // reference's stable descending sort.  Ordered sums (the reference adds left
 // to right) gather their terms with independent shuffles first.
 template <int PER>
-__device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane) {
+__device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane,
+                                                        bool dry = false) {
   constexpr unsigned kFull = 0xffffffffu;
   const float* L = a.logits + (long long)t * a.experts;
   const bool biased = a.mode == 1 && a.bias != nullptr;
@@ -231,6 +233,7 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
   const bool bad = __any_sync(kFull, mine && !(isfinite(w) && w >= 0.0f));
   const float wsum = ordered_sum(mine ? w : 0.0f);
   const bool valid = !bad && wsum > 1.1920929e-07f;
+  if (dry) return;
   if (lane < a.topk) {
     const long long o = (long long)t * a.topk + lane;
     a.ids[o] = mine ? my_id : -1;
@@ -239,6 +242,21 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
       a.combine_w[o] = mine ? (valid ? __fdiv_rn(w, wsum) : __fdiv_rn(1.0f, (float)n)) : 0.0f;
   }
   if (lane == 0) a.counters[t] = 0;  // ready for the next call
+}
+
+// The top-k runs once per token, in one warp of the last CTA, usually on code
+// that is in no cache (the weights streamed since the last call evict it).
+// A third warp of every CTA runs it once "dry" (no stores; logits of an
+// earlier call or of this one, whichever are there) while the other two
+// compute the logits, so that the last CTA's real pass fetches its
+// instructions on chip (not inlined: both passes run the same code).
+__device__ __noinline__ void router_topk_any(const RouterArgs& a, int t, int lane, bool dry) {
+  if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane, dry);
+  else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane, dry);
+  else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane, dry);
+  else if (a.experts <= 256) router_topk_and_weights<8>(a, t, lane, dry);
+  else if (a.experts <= 512) router_topk_and_weights<16>(a, t, lane, dry);
+  else router_topk_and_weights<32>(a, t, lane, dry);
 }
 
 // kSmem: rows and x staged in shared memory (hidden % 8 == 0, 16-byte aligned
@@ -270,6 +288,10 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, __
     for (int r = 0; r < nrows; ++r)
       bulk_load(rows_s + r * plan.row_stride, a.gate + (long long)(e0 + r) * a.hidden,
                 a.hidden * 2, bar);
+  }
+  if (warp == 2) {
+    router_topk_any(a, t, lane, true);
+    return;  // the barriers below count warps 0-1 only
   }
   pdl_wait_prior();
   const float* x = a.x + (long long)t * a.hidden;
@@ -321,18 +343,13 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterArgs a, __
       tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(grow[i]) << 16), x[i]));
     a.logits[(long long)t * a.experts + e0 + r] = __fadd_rn(h3, tail);
   }
-  __syncthreads();
+  bar_and(1, kRouterWorkers, 1);
   if (tid == 0) *last_s = atomic_add_acq_rel(&a.counters[t], 1u) == gridDim.x - 1;
-  __syncthreads();
+  bar_and(1, kRouterWorkers, 1);
   pdl_launch_dependents();
   // (3) the last CTA of this token does top-k + weights
   if (!*last_s || warp != 0) return;
-  if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane);
-  else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane);
-  else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane);
-  else if (a.experts <= 256) router_topk_and_weights<8>(a, t, lane);
-  else if (a.experts <= 512) router_topk_and_weights<16>(a, t, lane);
-  else router_topk_and_weights<32>(a, t, lane);
+  router_topk_any(a, t, lane, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -390,18 +407,77 @@ __device__ __forceinline__ void fp4_box_accumulate(const uint4 (&wb)[8], const _
   }
 }
 
+// The same over half of a row's chains: lane half hf = 0 runs chains 0-3 (bytes
+// 0 and 1 of every word, columns 8c + 0..3), hf = 1 chains 4-7 (bytes 2 and 3,
+// columns 8c + 4..7); acc[j] is chain 4 hf + j.  Each chain sees the same FMAs
+// in the same order as in fp4_box_accumulate.
+__device__ __forceinline__ void fp4_box_accumulate_half(const uint4 (&wb)[8], const __half* xs,
+                                                        const float* xm, int box, uint2 sb,
+                                                        int hf, float acc[4]) {
+  const uint32_t sbw[2] = {sb.x, sb.y};
+  const int sh = 16 * hf;
+  // x pair words of columns 8c + 4hf + {0,1} and {2,3}: uint2 index 8G + 2c + hf
+  const uint2* xp = reinterpret_cast<const uint2*>(xs) + hf;
+  uint2 xv[2][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) xv[0][c] = xp[8 * (box * 8) + 2 * c];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const int G = box * 8 + g;
+    if (g + 1 < 8) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xv[(g + 1) & 1][c] = xp[8 * (G + 1) + 2 * c];
+    }
+    const uint32_t ws[4] = {wb[g].x, wb[g].y, wb[g].z, wb[g].w};
+    float gacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t hw = ws[c] >> sh;
+      const uint32_t w0 = fp4x2_to_f16x2_ref(hw);
+      const uint32_t w1 = fp4x2_to_f16x2_ref(hw >> 8);
+      const uint2 xc = xv[g & 1][c];
+      gacc[0] = fma_f16lo(w0, xc.x, gacc[0]);
+      gacc[1] = fma_f16hi(w0, xc.x, gacc[1]);
+      gacc[2] = fma_f16lo(w1, xc.y, gacc[2]);
+      gacc[3] = fma_f16hi(w1, xc.y, gacc[3]);
+    }
+    const float m = xm[G >> 1];
+    const float s8 = __fmul_rn(decode_ue8m0((sbw[g >> 2] >> (8 * (g & 3))) & 0xff), 0.125f);
+    const float2 mm = make_float2(m, m), ss = make_float2(s8, s8);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const float2 r = ffma2(fmul2(make_float2(gacc[j], gacc[j + 1]), mm), ss,
+                             make_float2(acc[j], acc[j + 1]));
+      acc[j] = r.x;
+      acc[j + 1] = r.y;
+    }
+  }
+}
+
+// hsum8 of a row whose chains are split over lanes 2r (chains 0-3) and 2r+1
+// (chains 4-7): the same association, ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)).
+__device__ __forceinline__ float hsum8_pair(const float a[4]) {
+  const float q = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+  const float o = __shfl_xor_sync(0xffffffffu, q, 1);
+  return __fadd_rn(q, o);
+}
+
 __device__ __forceinline__ float hsum8(const float a[8]) {
   return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
                    __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
 }
 
 // ---------------------------------------------------------------------------
-// moe_up: grid (inter/32, slots, tokens).  Warp 0 computes w1 (gate) rows,
-// warp 1 the same w3 (up) rows, warp 2 streams both with TMA.  The SwiGLU
-// hidden of the 32 rows goes to global memory; the second CTA of each 64-row
-// act-quant block to finish quantises the block (atomic arrival counter, no
-// waiting).
+// moe_up: grid (inter/32, slots, tokens).  Warps 0-1 compute the 32 w1 (gate)
+// rows, warps 2-3 the same w3 (up) rows, two lanes per row (each lane four of
+// the row's eight FMA chains); warp 4 streams both with TMA.  Four consumer
+// warps per CTA spread the FMA work evenly over an SM's four schedulers.  The
+// SwiGLU hidden of the 32 rows goes to global memory; the second CTA of each
+// 64-row act-quant block to finish quantises the block (atomic arrival
+// counter, no waiting).
 // ---------------------------------------------------------------------------
+constexpr int kUpConsumers = 4;
+constexpr int kUpThreads = (kUpConsumers + 1) * 32;
 constexpr int kUpStages = 4;
 constexpr int kUpRows = kMoeUpRows;
 constexpr int kUpBox = kUpRows * 128;         // 4 KB
@@ -412,7 +488,7 @@ size_t moe_up_smem_bytes(int hidden) {
          (hidden / 64) * 4 + 128 + 2 * kUpRows * (hidden / 32) + 64;
 }
 
-__global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __restrict__ xq,
+__global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __half* __restrict__ xq,
                                                     const float* __restrict__ xq_mult,
                                                     __half* hq, float* hq_mult) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -435,7 +511,7 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUpStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 2);
+      mbar_init(&empty[s], kUpConsumers);
     }
     mbar_init(xbar, 1);
     fence_barrier_init();
@@ -451,7 +527,7 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
   }
   const bool valid_expert = expert >= 0 && expert < a.num_experts + a.has_shared;
 
-  if (warp == 2) {
+  if (warp == kUpConsumers) {
     if (lane == 0 && valid_expert) {
       const CUtensorMap* m1 = a.maps + expert * 3 + 0;
       const CUtensorMap* m3 = a.maps + expert * 3 + 1;
@@ -463,20 +539,35 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
         tma_load_2d(stages + s * kUpStageBytes, m1, &full[s], i * 128, row0);
         tma_load_2d(stages + s * kUpStageBytes + kUpBox, m3, &full[s], i * 128, row0);
       };
-      // first pass of the ring needs no free slot
-      int i = 0;
-      for (; i < nbox && i < kUpStages; ++i) issue(i);
-      // staged input (produced by the router / act-quant kernel); the
-      // consumers wait for it before freeing any stage
-      if (slot >= a.topk) pdl_wait_prior();
       const int scols = a.hidden / 32;
       const Fp4ExpertDev& ex = a.experts[expert];
+      // x and its multipliers (produced by the router) and this CTA's scale
+      // rows ([32 rows][hidden/32] per matrix, contiguous) on one barrier
       mbar_arrive_expect_tx(xbar, a.hidden * 2 + (a.hidden / 64) * 4 + 2 * kUpRows * scols);
-      bulk_load(xs, xq + (long long)t * a.hidden, a.hidden * 2, xbar);
-      bulk_load(xm, xq_mult + (long long)t * (a.hidden / 64), (a.hidden / 64) * 4, xbar);
-      // this CTA's scale rows are contiguous: [32 rows][hidden/32] per matrix
-      bulk_load(ssm, ex.w1_scale + (long long)row0 * scols, kUpRows * scols, xbar);
-      bulk_load(ssm + kUpRows * scols, ex.w3_scale + (long long)row0 * scols, kUpRows * scols, xbar);
+      auto load_scales = [&]() {
+        bulk_load(ssm, ex.w1_scale + (long long)row0 * scols, kUpRows * scols, xbar);
+        bulk_load(ssm + kUpRows * scols, ex.w3_scale + (long long)row0 * scols, kUpRows * scols,
+                  xbar);
+      };
+      auto load_x = [&]() {
+        bulk_load(xs, xq + (long long)t * a.hidden, a.hidden * 2, xbar);
+        bulk_load(xm, xq_mult + (long long)t * (a.hidden / 64), (a.hidden / 64) * 4, xbar);
+      };
+      int i = 0;
+      if (slot >= a.topk) {
+        // shared expert: weights and scales do not depend on the router, so
+        // they stream while it runs; x once it has completed
+        load_scales();
+        for (; i < nbox && i < kUpStages; ++i) issue(i);  // first pass needs no free slot
+        pdl_wait_prior();
+        load_x();
+      } else {
+        // routed (the router has completed): the small inputs go ahead of the
+        // ring so that they do not queue behind 32 KB of weights
+        load_x();
+        load_scales();
+        for (; i < nbox && i < kUpStages; ++i) issue(i);
+      }
       for (; i < nbox; ++i) {
         if (!mbar_wait(&empty[i % kUpStages], ((i / kUpStages) - 1) & 1, a.status)) break;
         issue(i);
@@ -498,52 +589,57 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
   pdl_launch_dependents();
   // a failed (timed-out) wait skips the work but still reaches the named
   // barrier below, so the partner warp is never stranded
-  bool ok = mbar_wait(xbar, 0, a.status);
+  bool ok = __all_sync(0xffffffffu, mbar_wait(xbar, 0, a.status));
 
-  const int row = row0 + lane;
+  const int mat = warp >> 1;                      // 0: w1, 1: w3
+  const int rl = (warp & 1) * 16 + (lane >> 1);   // row within the CTA's 32
+  const int hf = lane & 1;                        // chain half
+  const int row = row0 + rl;
   const int scols = a.hidden / 32;
-  const uint8_t* srow = ssm + (warp * kUpRows + lane) * scols;
-  float acc[8];
+  const uint8_t* srow = ssm + (mat * kUpRows + rl) * scols;
+  float acc[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
 
   for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kUpStages;
     const uint2 sb = *reinterpret_cast<const uint2*>(srow + i * 8);
-    if (!mbar_wait(&full[s], (i / kUpStages) & 1, a.status)) {
+    // warp-uniform: the lane pairs exchange partial sums with shuffles
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kUpStages) & 1, a.status))) {
       ok = false;
       break;
     }
-    const uint8_t* base = stages + s * kUpStageBytes + warp * kUpBox + lane * 128;
+    const uint8_t* base = stages + s * kUpStageBytes + mat * kUpBox + rl * 128;
     uint4 wb[8];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (lane & 7)));
-    fp4_box_accumulate(wb, xs, xm, i, sb, acc);
+    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (rl & 7)));
+    fp4_box_accumulate_half(wb, xs, xm, i, sb, hf, acc);
     // release the slot only after every lane has consumed its loads: an
     // arrive issued while shared-memory loads are still outstanding lets the
     // next TMA overwrite the slot under them (seen with several CTAs per SM)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  const float v = __fadd_rn(hsum8(acc), 0.0f);
+  const float v = __fadd_rn(hsum8_pair(acc), 0.0f);
   if (!isfinite(v)) flag(a.status, WH_DEV_NONFINITE);
-  if (warp == 0) gsh[lane] = v;
-  const int ok_both = bar_and(1, 64, ok);
-  if (warp == 0 || !ok_both) return;
+  if (mat == 0 && hf == 0) gsh[rl] = v;
+  const int ok_all = bar_and(1, kUpConsumers * 32, ok);
+  if (mat == 0 || !ok_all) return;
 
   // SwiGLU with the reference clamps (src/deepseek_v4.rs:556-596)
-  const float gated = fminf(gsh[lane], 10.0f);
+  const float gated = fminf(gsh[rl], 10.0f);
   float upped = v;
   upped = upped < -10.0f ? -10.0f : upped;
   upped = upped > 10.0f ? 10.0f : upped;
-  const float h = __fmul_rn(silu_ref(gated), upped);
+  const float hv = __fmul_rn(silu_ref(gated), upped);
   const long long hb = ((long long)t * nslots + slot) * a.inter;
-  a.h[hb + row] = h;
+  if (hf == 0) a.h[hb + row] = hv;
   // act quant over the 64-row block (src/deepseek_v4.rs:595): the later of the
-  // two 32-row CTAs quantises the whole block.  Every lane fences its store
-  // before lane 0 publishes the arrival.
+  // two 32-row CTAs quantises the whole block.  Every thread fences its store
+  // before warp 2's lane 0 publishes the arrival.
   __threadfence();
-  __syncwarp();
+  bar_and(2, 64, 1);
+  if (warp != 2) return;
   uint32_t prev = 0;
   const long long blk = hb / 64 + row0 / 64;
   if (lane == 0) prev = atomicAdd(&a.blk_counters[blk], 1u);
@@ -565,8 +661,11 @@ __global__ void __launch_bounds__(96) moe_up_kernel(MoeArgs a, const __half* __r
 }
 
 // ---------------------------------------------------------------------------
-// moe_down: grid (hidden/16, tokens); 4 consumer warps (8 slots x 16 rows) + producer
+// moe_down: grid (hidden/16, tokens); 8 consumer warps (warp k = slot k, 16 rows,
+// two lanes per row) + a TMA producer warp
 // ---------------------------------------------------------------------------
+constexpr int kDownConsumers = 8;
+constexpr int kDownThreads = (kDownConsumers + 1) * 32;
 constexpr int kDownStages = 4;
 constexpr int kDownRows = kMoeDownRows;
 constexpr int kDownSlots = 8;
@@ -580,7 +679,7 @@ size_t moe_down_smem_bytes(int inter, int slots) {
          kDownSlots * kDownRows * 4 + kDownSlots * kDownRows * (inter / 32) + 64;
 }
 
-__global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* __restrict__ hq,
+__global__ void __launch_bounds__(kDownThreads) moe_down_kernel(MoeArgs a, const __half* __restrict__ hq,
                                                        const float* __restrict__ hq_mult) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -610,17 +709,19 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
     if (e < -1 || e >= a.num_experts + a.has_shared) e = -1;
     slot_expert[threadIdx.x] = e;
   }
+  uint64_t* sbar = xbar + 1;  // the slots' w2 scale rows
   if (threadIdx.x == 0) {
     for (int s = 0; s < kDownStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);
+      mbar_init(&empty[s], kDownConsumers);
     }
     mbar_init(xbar, 1);
+    mbar_init(sbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == 4) {
+  if (warp == kDownConsumers) {
     if (lane == 0) {
       int nvalid = 0;
       for (int k = 0; k < nslots; ++k) nvalid += slot_expert[k] >= 0;
@@ -641,43 +742,50 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
     return;
   }
 
-  pdl_wait_prior();  // hq from moe_up
-  pdl_launch_dependents();
-  // stage hq of every slot (bulk copies, one barrier)
+  // the w2 scale rows depend only on the router's ids: stage them before the
+  // wait for moe_up (this CTA's 16 rows of each slot's w2 scales are contiguous)
   const int scols = a.inter / 32;
   if (threadIdx.x == 0) {
     int nvalid = 0;
     for (int k = 0; k < nslots; ++k) nvalid += slot_expert[k] >= 0;
-    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4) +
-                                    nvalid * kDownRows * scols);
+    mbar_arrive_expect_tx(sbar, nvalid * kDownRows * scols);
+    for (int k = 0; k < nslots; ++k) {
+      const int e = slot_expert[k];
+      if (e >= 0)
+        bulk_load(ssm + k * kDownRows * scols, a.experts[e].w2_scale + (long long)row0 * scols,
+                  kDownRows * scols, sbar);
+    }
+  }
+  pdl_wait_prior();  // hq from moe_up
+  pdl_launch_dependents();
+  // stage hq of every slot (bulk copies, one barrier)
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4));
     for (int k = 0; k < nslots; ++k) {
       bulk_load(hs + k * hstride, hq + ((long long)t * nslots + k) * a.inter, a.inter * 2, xbar);
       bulk_load(hm + k * (a.inter / 64), hq_mult + ((long long)t * nslots + k) * (a.inter / 64),
                 (a.inter / 64) * 4, xbar);
-      const int e = slot_expert[k];
-      if (e >= 0)  // this CTA's 16 scale rows of the slot's w2 are contiguous
-        bulk_load(ssm + k * kDownRows * scols, a.experts[e].w2_scale + (long long)row0 * scols,
-                  kDownRows * scols, xbar);
     }
   }
-  bool ok = mbar_wait(xbar, 0, a.status);
+  bool ok = __all_sync(0xffffffffu, mbar_wait(sbar, 0, a.status) && mbar_wait(xbar, 0, a.status));
 
-  const int slot = warp * 2 + (lane >> 4);
-  const int r = lane & 15;
+  const int slot = warp;
+  const int r = lane >> 1;
+  const int hf = lane & 1;
   const int row = row0 + r;
   const int e = slot < nslots ? slot_expert[slot] : -1;
   const bool active = e >= 0;
   const uint8_t* srow = ssm + ((active ? slot : 0) * kDownRows + r) * scols;
   const __half* hslot = reinterpret_cast<const __half*>(hs + (active ? slot : 0) * hstride);
   const float* hmul = hm + (active ? slot : 0) * (a.inter / 64);
-  float acc[8];
+  float acc[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
   for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kDownStages;
     uint2 sb = make_uint2(0, 0);
     if (active) sb = *reinterpret_cast<const uint2*>(srow + i * 8);
-    if (!mbar_wait(&full[s], (i / kDownStages) & 1, a.status)) {
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kDownStages) & 1, a.status))) {
       ok = false;
       break;
     }
@@ -687,18 +795,20 @@ __global__ void __launch_bounds__(160) moe_down_kernel(MoeArgs a, const __half* 
 #pragma unroll
       for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (r & 7)));
     }
-    if (active) fp4_box_accumulate(wb, hslot, hmul, i, sb, acc);
+    if (active) fp4_box_accumulate_half(wb, hslot, hmul, i, sb, hf, acc);
     __syncwarp();  // slot released after its data has been consumed
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (ok && active) {
-    const float yv = __fadd_rn(hsum8(acc), 0.0f);
+  if (ok && active) {  // warp-uniform
+    const float yv = __fadd_rn(hsum8_pair(acc), 0.0f);
     if (!isfinite(yv)) flag(a.status, WH_DEV_NONFINITE);
-    ys[slot * kDownRows + r] = yv;
-    if (a.expert_out)
-      a.expert_out[((long long)t * nslots + slot) * a.hidden + row] = yv;
+    if (hf == 0) {
+      ys[slot * kDownRows + r] = yv;
+      if (a.expert_out)
+        a.expert_out[((long long)t * nslots + slot) * a.hidden + row] = yv;
+    }
   }
-  const int ok_all = bar_and(1, 128, ok);
+  const int ok_all = bar_and(1, kDownConsumers * 32, ok);
   if (ok_all && a.combine && threadIdx.x < kDownRows) {
     const int rr = threadIdx.x;
     const float* cw = a.combine_w + (long long)t * a.topk;
@@ -970,7 +1080,7 @@ cudaError_t launch_moe_up_ex(const MoeArgs& a, const __half* xq, const float* xq
   cudaError_t e = ensure_smem(moe_up_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.inter / kUpRows, a.topk + a.has_shared, a.tokens);
-  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(96), smem, s, attr, pdl);
+  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kUpThreads), smem, s, attr, pdl);
   return cudaLaunchKernelEx(&cfg, moe_up_kernel, a, xq, xq_mult, hq, hq_mult);
 }
 
@@ -981,7 +1091,7 @@ cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* 
   cudaError_t e = ensure_smem(moe_down_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.hidden / kDownRows, a.tokens);
-  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(160), smem, s, attr, pdl);
+  cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kDownThreads), smem, s, attr, pdl);
   return cudaLaunchKernelEx(&cfg, moe_down_kernel, a, hq, hq_mult);
 }
 
