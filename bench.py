@@ -47,7 +47,7 @@ UP_BYTES = SLOTS * 2 * (PACKED_W13 + SCALES_W13)       # moe_up algorithmic byte
 DOWN_BYTES = SLOTS * (PACKED_W2 + SCALES_W2)
 # DRAM bytes (read + write) of one moe_up launch from an ncu capture of the
 # --ncu-case moe16 workload, which processes the same units per launch
-UP_TRAFFIC = 63_292_672
+UP_TRAFFIC = 63_314_688
 # grouped up GEMM: DRAM bytes read per algorithmic byte read in the ncu capture of the
 # grouped16 case (161,668,608 / 159,088,640; profiles/grouped_gemm_grouped16.md); the
 # config-3 launch is too large to capture, its traffic is scaled by the units processed
