@@ -48,6 +48,10 @@ DOWN_BYTES = SLOTS * (PACKED_W2 + SCALES_W2)
 # DRAM bytes (read + write) of one moe_up launch from an ncu capture of the
 # --ncu-case moe16 workload, which processes the same units per launch
 UP_TRAFFIC = 63_314_688
+# DRAM bytes of one moe_decode_kernel launch (the whole config-2 step); None until
+# captured with ncu
+STEP_TRAFFIC = None
+STEP_TRAFFIC_SOURCE = "not captured yet"
 # grouped up GEMM: DRAM bytes read per algorithmic byte read in the ncu capture of the
 # grouped16 case (161,668,608 / 159,088,640; profiles/grouped_gemm_grouped16.md); the
 # config-3 launch is too large to capture, its traffic is scaled by the units processed
@@ -307,19 +311,31 @@ def run_ours(args):
     graph_matches_direct = bool(torch.equal(y_direct, y))
     del graph
 
-    # ---- per-kernel roofline (profiling: events between kernels, no PDL) ----
-    ctx.set_profiling(True)
-    phases = []
-    for k in range(min(args.steps, 10)):
-        flush.zero_()
-        layer.forward(xs[args.warmup + k:args.warmup + k + 1], y)
-        phases.append(ctx.phase_times())
-    ctx.set_profiling(False)
-    ctx.sync()
-    ph = np.array(phases)  # [router, moe_up, moe_down]
-    up_ms = float(ph[:, 1].mean())
-    down_ms = float(ph[:, 2].mean())
-    router_ms = float(ph[:, 0].mean())
+    # ---- roofline of the timed kernel (profiling: CUDA events around it) -----
+    def profile_phases():
+        ctx.set_profiling(True)
+        phases = []
+        for k in range(min(args.steps, 10)):
+            flush.zero_()
+            layer.forward(xs[args.warmup + k:args.warmup + k + 1], y)
+            phases.append(ctx.phase_times())
+        ctx.set_profiling(False)
+        ctx.sync()
+        return np.array(phases)
+
+    ph3 = profile_phases()
+    fused = ph3.shape[1] == 1  # the timed step ran as the persistent decode kernel
+    step_kernel_ms = float(ph3[:, 0].mean()) if fused else None
+    # the other schedule of the same step, for comparison (A/B)
+    layer.set_fused_decode(not fused)
+    ph_ab = profile_phases()
+    layer.set_fused_decode(fused)
+    if fused:
+        ph3, ph_ab = ph_ab, ph3
+    fused_ab_ms = float(ph_ab[:, 0].mean()) if ph_ab.shape[1] == 1 else None
+    up_ms = float(ph3[:, 1].mean())
+    down_ms = float(ph3[:, 2].mean())
+    router_ms = float(ph3[:, 0].mean())
     peak, peak_kind = peaks()
     up_gbs = UP_BYTES / (up_ms * 1e-3) / 1e9
 
@@ -374,7 +390,18 @@ def run_ours(args):
             "step_hbm_gbs": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
             "phases_ms": {"router": round(router_ms, 5), "moe_up": round(up_ms, 5),
                           "moe_down": round(down_ms, 5)},
-            "roofline": {
+            "persistent_decode_kernel_ms": (round(fused_ab_ms, 5) if fused_ab_ms is not None
+                                            else None),
+            "roofline": ({
+                "kernel": "moe_decode_kernel (router + w1/w3 + SwiGLU + act quant + w2 + combine, "
+                          "one persistent kernel)",
+                "bound": "hbm", "achieved": round(STEP_BYTES / (step_kernel_ms * 1e-3) / 1e9, 1),
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round(STEP_BYTES / (step_kernel_ms * 1e-3) / 1e9 / peak, 4),
+                "algorithmic_bytes": STEP_BYTES, "kernel_ms": round(step_kernel_ms, 5),
+                "traffic": STEP_TRAFFIC,
+                "traffic_source": STEP_TRAFFIC_SOURCE,
+            } if fused else {
                 "kernel": "moe_up_kernel (w1+w3 FP4 matvecs of 7 experts + SwiGLU + act quant)",
                 "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
@@ -382,12 +409,12 @@ def run_ours(args):
                 "traffic_source": "ncu dram__bytes_read+write of one moe_up launch "
                                   "(bench.py --ncu-case moe16: same 7 experts' w1/w3 per launch)",
                 "down_kernel_gbs": round(DOWN_BYTES / (down_ms * 1e-3) / 1e9, 1),
-            },
+            }),
             "e2e": {"value": round(world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                     "ms_per_step": round(e2e_ms, 6), "h2d_bytes_per_step": HID * 4,
                     "d2h_bytes_per_step": HID * 4,
                     "path": "pinned host x -> H2D -> wh_moe_ffn (C ABI) -> D2H y"},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (1 if fused else 3) * args.steps,
             "timing": timing,
             "graph_output_matches_direct_call": graph_matches_direct,
             "clocks": clocks,

@@ -222,6 +222,13 @@ size_t wh_moe_scratch_bytes(const wh_moe_plan* plan, int tokens);
 wh_status wh_moe_ffn(wh_ctx* ctx, const wh_moe_plan* plan, const float* x, int tokens,
                      const int32_t* hash_ids, float* y, int32_t* ids_out, float* weights_out,
                      void* scratch, size_t scratch_bytes, wh_stream_t stream);
+/* on = 1: one-token calls of wh_moe_ffn run as one persistent kernel (router,
+ * w1/w3, w2 and the combine; one cooperative CTA per SM) when the shapes allow
+ * it: experts <= 2 x SM count, hidden % 512 == 0, inter % 256 == 0, hidden and
+ * inter <= 4096, topk + shared <= 8.  The arithmetic is the same bit for bit.
+ * The default (0) runs the router, moe_up and moe_down kernels, which are
+ * faster on B200 today. */
+wh_status wh_moe_plan_set_fused_decode(wh_moe_plan* plan, int on);
 
 /* ------------------------------------------------------------------------ */
 /* Expert parallelism: the routed experts sharded contiguously over `world`   */

@@ -425,6 +425,74 @@ def test_moe_ffn_batch_equals_single_token(ctx, W, moe_layer):
     np.testing.assert_array_equal(bits(yb.cpu().numpy()), bits(ys.cpu().numpy()))
 
 
+def test_moe_ffn_decode_kernel_vs_oracle_and_three_kernels(ctx, W, moe_layer):
+    """One-token calls run as the persistent decode kernel (decode.cu): the
+    same outputs and routes bit for bit as the three-kernel path, over several
+    tokens in a row (its grid counters and act-quant counters reset between
+    calls), and within the exact path's oracle tolerance."""
+    stack, gate, layer, _ = moe_layer
+    E, Hd = 256, 4096
+    x = H.activations(47, 6, Hd)
+    outs = {}
+    for fused in (True, False):
+        layer.set_fused_decode(fused)
+        ys, idss, wss = [], [], []
+        for t in range(6):
+            ids = torch.zeros(1, 6, dtype=torch.int32, device="cuda")
+            wts = torch.zeros(1, 6, device="cuda")
+            ys.append(layer.forward(dev(x[t:t + 1]), ids=ids, weights=wts).cpu().numpy()[0])
+            idss.append(ids.cpu().numpy()[0])
+            wss.append(wts.cpu().numpy()[0])
+        ctx.sync()
+        outs[fused] = (np.array(ys), np.array(idss), np.array(wss))
+    layer.set_fused_decode(False)
+    np.testing.assert_array_equal(bits(outs[True][0]), bits(outs[False][0]))
+    np.testing.assert_array_equal(outs[True][1], outs[False][1])
+    np.testing.assert_array_equal(bits(outs[True][2]), bits(outs[False][2]))
+    y, ids = outs[True][0], outs[True][1]
+    for t in range(2):
+        n, oid, ow, _ = O.router(gate, x[t], 6, mode=0)
+        np.testing.assert_array_equal(ids[t], oid)
+        keep = []
+        arr = (O.Fp4Expert * (E + 1))()
+        for e in list(oid) + [E]:
+            arr[e] = _oracle_expert(stack, e, keep)
+        st, want = O.moe_combine_token(arr, oid, ow, arr[E], x[t])
+        assert st == O.OK
+        assert np.max(np.abs(y[t] - want)) <= 1e-4 * float(np.abs(want).max())
+
+
+@pytest.mark.parametrize("hashed", [False, True])
+def test_moe_ffn_decode_kernel_deepseek_router(ctx, W, moe_layer, hashed):
+    """The decode kernel with the sqrt-softplus router (selection bias, route
+    scale, optional tid2eid hash rows) equals the three-kernel path bit for bit."""
+    stack, gate, _, _ = moe_layer
+    E, Hd = 256, 4096
+    experts = [_w_expert(W, stack, e) for e in range(E)]
+    bias = dev(np.random.default_rng(48).normal(0, 0.01, E).astype(np.float32))
+    layer = W.MoeLayer(ctx, experts, _w_expert(W, stack, E), dev(gate.view(np.int16)), topk=6,
+                       router_mode=W.ROUTER_SQRT_SOFTPLUS, gate_bias=bias, route_scale=2.5,
+                       max_tokens=1, exact=1)
+    x = H.activations(49, 3, Hd)
+    g = np.random.default_rng(50)
+    hrows = dev(np.array([g.choice(E, 6, replace=False) for _ in range(3)], np.int32))
+    outs = {}
+    for fused in (True, False):
+        layer.set_fused_decode(fused)
+        res = []
+        for t in range(3):
+            ids = torch.zeros(1, 6, dtype=torch.int32, device="cuda")
+            hid = hrows[t:t + 1].contiguous() if hashed else None
+            y = layer.forward(dev(x[t:t + 1]), ids=ids, hash_ids=hid)
+            res.append((y.cpu().numpy()[0], ids.cpu().numpy()[0]))
+        ctx.sync()
+        outs[fused] = res
+    layer.close()
+    for (ya, ia), (yb, ib) in zip(outs[True], outs[False]):
+        np.testing.assert_array_equal(ia, ib)
+        np.testing.assert_array_equal(bits(ya), bits(yb))
+
+
 @pytest.mark.parametrize("T", [1, 3])
 def test_moe_ffn_config2_tensor_core_path_vs_oracle(ctx, W, moe_layer, T):
     """Decode-sized calls on the tensor-core path (desc.exact = 0): router ids

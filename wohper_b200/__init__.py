@@ -52,7 +52,7 @@ EXPORTS = (
     "wh_fp4_expert_forward_noalloc", "wh_ep_row_bytes", "wh_ep_scratch_bytes", "wh_ep_dispatch",
     "wh_ep_expert_ffn", "wh_ep_combine", "wh_ep_window_bytes", "wh_ep_window_create",
     "wh_ep_window_connect", "wh_ep_window_destroy", "wh_ep_p2p_dispatch",
-    "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine",
+    "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine", "wh_moe_plan_set_fused_decode",
 )
 
 
@@ -129,6 +129,7 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
         "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
         "wh_moe_plan_destroy": (None, [vp]),
+        "wh_moe_plan_set_fused_decode": (st, [vp, i]),
         "wh_moe_scratch_bytes": (sz, [vp, i]),
         "wh_moe_ffn": (st, [vp, vp, vp, i, vp, vp, vp, vp, vp, sz, vp]),
         "wh_debug_act_quant_table": (None, [vp]),
@@ -374,6 +375,10 @@ class MoeLayer:
                                 _ptr(ids), _ptr(weights), _ptr(self.scratch), self.scratch.numel(),
                                 _stream(stream)))
         return y
+
+    def set_fused_decode(self, on: bool = True) -> None:
+        """One-token calls as one persistent kernel (on) or as three kernels (default)."""
+        _check(lib().wh_moe_plan_set_fused_decode(self.plan, 1 if on else 0))
 
     def close(self):
         if getattr(self, "plan", None):

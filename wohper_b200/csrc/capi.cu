@@ -158,15 +158,19 @@ struct DevExpertSet {
   CUtensorMap* maps = nullptr;      // device [n][3]
   Fp4ExpertDev* experts = nullptr;  // device [n]
   CUtensorMap* gmaps = nullptr;     // device [n][3], grouped-GEMM boxes (nullable)
+  CUtensorMap* dmaps = nullptr;     // device [n], w2 boxes [8 rows][128 B] (decode kernel)
   int n = 0;
 };
 
 wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) {
-  std::vector<CUtensorMap> maps(size_t(n) * 3);
+  std::vector<CUtensorMap> maps(size_t(n) * 3), dmaps(n);
   std::vector<Fp4ExpertDev> ex(n);
   for (int i = 0; i < n; ++i) {
     const wh_fp4_expert& e = list[i];
     wh_status st;
+    if ((st = make_u8_map(&dmaps[i], e.w2.packed_weight, e.w2.rows, e.w2.cols / 2,
+                          kDecDownRows)))
+      return st;
     if ((st = make_u8_map(&maps[i * 3 + 0], e.w1.packed_weight, e.w1.rows, e.w1.cols / 2,
                           kMoeUpRows)))
       return st;
@@ -180,8 +184,11 @@ wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) 
                          e.w1.packed_weight, e.w3.packed_weight, e.w2.packed_weight};
   }
   WH_CUDA(cudaMalloc(&out->maps, maps.size() * sizeof(CUtensorMap)));
+  WH_CUDA(cudaMalloc(&out->dmaps, dmaps.size() * sizeof(CUtensorMap)));
   WH_CUDA(cudaMalloc(&out->experts, ex.size() * sizeof(Fp4ExpertDev)));
   WH_CUDA(cudaMemcpy(out->maps, maps.data(), maps.size() * sizeof(CUtensorMap),
+                     cudaMemcpyHostToDevice));
+  WH_CUDA(cudaMemcpy(out->dmaps, dmaps.data(), dmaps.size() * sizeof(CUtensorMap),
                      cudaMemcpyHostToDevice));
   WH_CUDA(cudaMemcpy(out->experts, ex.data(), ex.size() * sizeof(Fp4ExpertDev),
                      cudaMemcpyHostToDevice));
@@ -192,6 +199,7 @@ void free_expert_set(DevExpertSet& s) {
   if (s.maps) cudaFree(s.maps);
   if (s.experts) cudaFree(s.experts);
   if (s.gmaps) cudaFree(s.gmaps);
+  if (s.dmaps) cudaFree(s.dmaps);
   s = DevExpertSet{};
 }
 
@@ -315,6 +323,9 @@ struct wh_moe_plan {
   uint32_t* counters = nullptr;      // router: [max_tokens]
   uint32_t* blk_counters = nullptr;  // moe_up: [max_tokens][slots][inter/64]
   bool grouped = false;              // tensor-core path available (desc.exact == 0)
+  uint32_t* dec_sync = nullptr;      // decode kernel's grid counters [4] (zero at rest)
+  int decode_ok = -1;                // one-token persistent kernel: -1 not checked yet
+  bool decode_on = false;            // wh_moe_plan_set_fused_decode (opt-in)
 };
 
 extern "C" {
@@ -703,6 +714,8 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
   if (e == cudaSuccess) e = cudaMemset(p->counters, 0, sizeof(uint32_t) * d->max_tokens);
   if (e == cudaSuccess) e = cudaMalloc(&p->blk_counters, sizeof(uint32_t) * nblk);
   if (e == cudaSuccess) e = cudaMemset(p->blk_counters, 0, sizeof(uint32_t) * nblk);
+  if (e == cudaSuccess) e = cudaMalloc(&p->dec_sync, sizeof(uint32_t) * 4);
+  if (e == cudaSuccess) e = cudaMemset(p->dec_sync, 0, sizeof(uint32_t) * 4);
   if (e != cudaSuccess) {
     free_expert_set(p->set);
     delete p;
@@ -717,7 +730,14 @@ void wh_moe_plan_destroy(wh_moe_plan* p) {
   free_expert_set(p->set);
   if (p->counters) cudaFree(p->counters);
   if (p->blk_counters) cudaFree(p->blk_counters);
+  if (p->dec_sync) cudaFree(p->dec_sync);
   delete p;
+}
+
+wh_status wh_moe_plan_set_fused_decode(wh_moe_plan* p, int on) {
+  if (!p) return fail(WH_ERR_INVALID_POINTER, "null plan");
+  p->decode_on = on != 0;
+  return WH_OK;
 }
 
 namespace {
@@ -946,8 +966,6 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   c->prof_begin();
   wh_status pst;
   if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
-  WH_CUDA(launch_router_ex(r, s.xq, s.xq_mult, stream, c->pdl()));
-  if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
   MoeArgs a{};
   a.maps = p->set.maps;
   a.experts = p->set.experts;
@@ -966,6 +984,28 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   a.expert_out = nullptr;
   a.combine = 1;
   a.status = c->status;
+  wh_moe_plan* mp = const_cast<wh_moe_plan*>(p);
+  if (tokens == 1 && p->decode_on) {
+    if (mp->decode_ok < 0)
+      mp->decode_ok = decode_supported(d.num_experts, d.hidden, d.inter, d.topk,
+                                       d.shared ? 1 : 0, c->num_sms) ? 1 : 0;
+    if (mp->decode_ok) {
+      // the whole step as one persistent kernel (decode.cu)
+      DecodeArgs da{};
+      da.r = r;
+      da.m = a;
+      da.dmaps = p->set.dmaps;
+      da.xq = s.xq;
+      da.xq_mult = s.xq_mult;
+      da.hq = s.hq;
+      da.hq_mult = s.hq_mult;
+      da.sync = p->dec_sync;
+      WH_CUDA(launch_moe_decode(da, c->num_sms, stream));
+      return c->prof_mark(stream);
+    }
+  }
+  WH_CUDA(launch_router_ex(r, s.xq, s.xq_mult, stream, c->pdl()));
+  if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
   WH_CUDA(launch_moe_up_ex(a, s.xq, s.xq_mult, s.hq, s.hq_mult, stream, c->pdl()));
   if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
   WH_CUDA(launch_moe_down_ex(a, s.hq, s.hq_mult, stream, c->pdl()));

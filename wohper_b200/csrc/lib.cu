@@ -2,6 +2,7 @@
 // __constant__ act-quant table and every kernel in one module, no -rdc).
 #include "fp8_gemv.cu"
 #include "moe.cu"
+#include "decode.cu"
 #include "grouped.cu"
 #include "ep.cu"
 #include "capi.cu"
