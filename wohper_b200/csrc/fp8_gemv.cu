@@ -169,7 +169,7 @@ static int fp8_stages(int tb, int cols, int ngroups) {
 }
 
 template <int TB>
-__global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap,
                                                            Fp8GemvArgs a, int nstages) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -252,31 +252,35 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
     asm volatile("bar.sync 1, %0;" ::"r"(nthr));
   }
 
-  const int rloc = warp * 8 + (lane >> 2);  // row within the box
-  const int q = lane & 3;
+  // 8 lanes per row; lane q holds the reference's chains j = 2(q & 3) and
+  // 2(q & 3) + 1 of g0 (q < 4: columns 16c + 2q, +1) or of g1 (q >= 4: columns
+  // 16c + 8 + 2(q - 4), +1), c = 0..7 in order.  Lanes q and q ^ 4 add g0_j and
+  // g1_j; acc_j = fma(g0_j + g1_j, scale, acc_j) as the reference.
+  const int rloc = warp * 4 + (lane >> 3);  // row within the box
+  const int q = lane & 7;
   const int row = row0 + rloc;
   const bool active = rloc < box_rows && row < a.row_end;
   const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
   const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
 
-  float2 acc01[TB], acc23[TB];
+  float2 acc[TB];
 #pragma unroll
-  for (int b = 0; b < TB; ++b) acc01[b] = acc23[b] = make_float2(0.0f, 0.0f);
+  for (int b = 0; b < TB; ++b) acc[b] = make_float2(0.0f, 0.0f);
 
   // Software pipeline: the weights (and, for one input, x) of group g + 1
   // are loaded from shared memory while group g is decoded and accumulated.
   bool ok = true;
   uint32_t wv[8], wn[8];
-  float4 xc[8], xn[8];  // x of the current / next group (TB == 1 only)
-  auto load_group = [&](int slot, int g, uint32_t (&w)[8], float4 (&x)[8]) {
-    const uint8_t* base = stages + slot * kFp8StageBytes + rloc * 128 + 4 * q;
+  float2 xc[8], xn[8];  // x of the current / next group (TB == 1 only)
+  auto load_group = [&](int slot, int g, uint32_t (&w)[8], float2 (&x)[8]) {
+    const uint8_t* base = stages + slot * kFp8StageBytes + rloc * 128 + 2 * q;
 #pragma unroll
     for (int c = 0; c < 8; ++c)
-      w[c] = *reinterpret_cast<const uint32_t*>(base + 16 * (c ^ (rloc & 7)));
+      w[c] = *reinterpret_cast<const uint16_t*>(base + 16 * (c ^ (rloc & 7)));
     if (TB == 1) {
-      const float* xg = xs + g * 128 + 4 * q;
+      const float* xg = xs + g * 128 + 2 * q;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
+      for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const float2*>(xg + 16 * c);
     }
   };
   int s = 0;
@@ -300,39 +304,30 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
       load_group(sn, g + 1, wn, xn);
     }
     const float scale = decode_ue8m0(srow_s[g]);
-    float2 wf[8][2];
+    float2 wf[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      wf[c][0] = h2_to_f2(e4m3x2_to_f16x2(wv[c]));
-      wf[c][1] = h2_to_f2(e4m3x2_to_f16x2(wv[c] >> 16));
-    }
+    for (int c = 0; c < 8; ++c) wf[c] = h2_to_f2(e4m3x2_to_f16x2(wv[c]));
     const float2 sc = make_float2(scale, scale);
 #pragma unroll
     for (int b = 0; b < TB; ++b) {
       if (b < tb) {
-        float4 xv[8];
+        float2 xv[8];
         if (TB == 1) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) xv[c] = xc[c];
         } else {
-          const float* xg = xs + b * a.cols + g * 128 + 4 * q;
+          const float* xg = xs + b * a.cols + g * 128 + 2 * q;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float4*>(xg + 16 * c);
+          for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float2*>(xg + 16 * c);
         }
-        float2 p01 = make_float2(0.0f, 0.0f), p23 = make_float2(0.0f, 0.0f);
+        float2 pj = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          p01 = ffma2(wf[c][0], make_float2(xv[c].x, xv[c].y), p01);
-          p23 = ffma2(wf[c][1], make_float2(xv[c].z, xv[c].w), p23);
-        }
-        // P_j = g0_j + g1_j: lanes q and q^2 hold g0 / g1 of the same j
-        float2 o01, o23;
-        o01.x = __shfl_xor_sync(0xffffffffu, p01.x, 2);
-        o01.y = __shfl_xor_sync(0xffffffffu, p01.y, 2);
-        o23.x = __shfl_xor_sync(0xffffffffu, p23.x, 2);
-        o23.y = __shfl_xor_sync(0xffffffffu, p23.y, 2);
-        acc01[b] = ffma2(fadd2(p01, o01), sc, acc01[b]);
-        acc23[b] = ffma2(fadd2(p23, o23), sc, acc23[b]);
+        for (int c = 0; c < 8; ++c) pj = ffma2(wf[c], xv[c], pj);
+        // P_j = g0_j + g1_j: lanes q and q ^ 4 hold g0 / g1 of the same j
+        float2 o;
+        o.x = __shfl_xor_sync(0xffffffffu, pj.x, 4);
+        o.y = __shfl_xor_sync(0xffffffffu, pj.y, 4);
+        acc[b] = ffma2(fadd2(pj, o), sc, acc[b]);
       }
     }
     // release the slot only after the loaded words have been consumed
@@ -350,10 +345,12 @@ __global__ void __launch_bounds__(160) fp8_gemv_tma_kernel(const __grid_constant
 #pragma unroll
   for (int b = 0; b < TB; ++b) {
     if (b < tb) {
-      float h = __fadd_rn(__fadd_rn(acc01[b].x, acc01[b].y), __fadd_rn(acc23[b].x, acc23[b].y));
-      float other = __shfl_xor_sync(0xffffffffu, h, 1);
+      // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
+      const float s2 = __fadd_rn(acc[b].x, acc[b].y);
+      const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
+      const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 2));
       if (q == 0 && active) {
-        float tot = __fadd_rn(__fadd_rn(h, other), 0.0f);
+        float tot = __fadd_rn(s8, 0.0f);
         const int bi = tile * TB + b;
         if (!isfinite(tot)) {
           // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
@@ -395,7 +392,7 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
   }
   const int nrows = a.row_end - a.row_start;
   const int tb = a.batch < 8 ? (a.batch < 4 ? (a.batch < 2 ? 1 : 2) : 4) : 8;
-  const int nconsumer = (a.box_rows + 7) / 8;
+  const int nconsumer = (a.box_rows + 3) / 4;  // 4 rows per consumer warp
   const int ns = fp8_stages(tb, a.cols, a.scale_cols);
   cfg.blockDim = dim3(32 * (nconsumer + 1));
   cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + tb - 1) / tb);
