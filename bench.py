@@ -340,28 +340,31 @@ def run_ours(args):
     up_gbs = UP_BYTES / (up_ms * 1e-3) / 1e9
 
     # ---- end to end through the C ABI with host buffers ---------------------
+    # wh_moe_ffn takes the token and the output as pinned host memory (the
+    # reference's interface is host slices): a kernel pulls x over the bus into
+    # device scratch and moe_down writes y straight into host memory, so each
+    # step moves hidden*4 bytes in each direction with no copy-engine transfer
     xh = torch.from_numpy(H.activations(3000 + rank, n_tok, HID)).pin_memory()
     yh = torch.empty(args.steps, HID).pin_memory()
-    xd = torch.empty(1, HID, device=dev)
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     for i in range(args.warmup):
         flush.zero_()
-        xd.copy_(xh[i:i + 1], non_blocking=True)
-        layer.forward(xd, y)
-        yh[0:1].copy_(y, non_blocking=True)
+        layer.forward(xh[i:i + 1], yh[0:1])
     torch.cuda.synchronize()
     barrier(world)
     for k in range(args.steps):
         flush.zero_()
         ev2[k][0].record(stream)
-        xd.copy_(xh[args.warmup + k:args.warmup + k + 1], non_blocking=True)
-        layer.forward(xd, y)
-        yh[k:k + 1].copy_(y, non_blocking=True)
+        layer.forward(xh[args.warmup + k:args.warmup + k + 1], yh[k:k + 1])
         ev2[k][1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    # the host copy holds the device results of the same tokens, bit for bit
+    e2e_check = layer.forward(xh[args.warmup:args.warmup + 1].to(dev))
+    torch.cuda.synchronize()
+    e2e_matches_device = bool(torch.equal(e2e_check.cpu(), yh[0:1]))
     ctx.sync()
 
     result = None
@@ -413,7 +416,9 @@ def run_ours(args):
             "e2e": {"value": round(world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                     "ms_per_step": round(e2e_ms, 6), "h2d_bytes_per_step": HID * 4,
                     "d2h_bytes_per_step": HID * 4,
-                    "path": "pinned host x -> H2D -> wh_moe_ffn (C ABI) -> D2H y"},
+                    "path": "pinned host x -> wh_moe_ffn (C ABI; the device reads x and "
+                            "writes y through the mapped host buffers)",
+                    "matches_device_pointer_call": e2e_matches_device},
             "gpu_launches": (1 if fused else 3) * args.steps,
             "timing": timing,
             "graph_output_matches_direct_call": graph_matches_direct,

@@ -218,7 +218,12 @@ size_t wh_moe_scratch_bytes(const wh_moe_plan* plan, int tokens);
  * Replaces, per token, routing (see wh_router_topk) followed by
  * compute_active_and_shared_experts (src/compute.rs:1872-1946):
  * y = shared(x) + sum_k expert_k(x) * w_k/sum(w), summed in route order.
- * ids_out/weights_out (nullable, [tokens][topk]) receive the routes. */
+ * ids_out/weights_out (nullable, [tokens][topk]) receive the routes.
+ * x and y may be device memory or pinned host memory that the device maps at
+ * the same address (cudaHostAlloc / cudaHostRegister): the kernels then read x
+ * and write y over the bus, with no copy-engine transfer; pageable host memory
+ * returns WH_ERR_INVALID_POINTER.  The host-memory result is complete once the
+ * stream has been synchronised. */
 wh_status wh_moe_ffn(wh_ctx* ctx, const wh_moe_plan* plan, const float* x, int tokens,
                      const int32_t* hash_ids, float* y, int32_t* ids_out, float* weights_out,
                      void* scratch, size_t scratch_bytes, wh_stream_t stream);

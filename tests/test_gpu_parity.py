@@ -462,6 +462,25 @@ def test_moe_ffn_decode_kernel_vs_oracle_and_three_kernels(ctx, W, moe_layer):
         assert np.max(np.abs(y[t] - want)) <= 1e-4 * float(np.abs(want).max())
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_moe_ffn_host_buffers(ctx, W, moe_layer, T):
+    """x and y may be pinned host memory (the device pulls x over the bus and
+    writes y back): the same bits as device buffers, on the exact and the
+    tensor-core paths.  Pageable host memory is refused before any kernel runs."""
+    _, _, layer, fast = moe_layer
+    x = H.activations(51 + T, T, 4096)
+    for lay in (layer, fast):
+        want = lay.forward(dev(x))
+        xh = torch.from_numpy(x).pin_memory()
+        yh = torch.empty(T, 4096).pin_memory()
+        lay.forward(xh, yh)
+        ctx.sync()
+        np.testing.assert_array_equal(bits(yh.numpy()), bits(want.cpu().numpy()))
+    with pytest.raises(W.WohperError) as err:
+        layer.forward(torch.from_numpy(x.copy()), torch.empty(T, 4096))
+    assert err.value.kind == "InvalidPointer"
+
+
 @pytest.mark.parametrize("hashed", [False, True])
 def test_moe_ffn_decode_kernel_deepseek_router(ctx, W, moe_layer, hashed):
     """The decode kernel with the sqrt-softplus router (selection bias, route

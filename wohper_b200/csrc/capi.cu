@@ -26,6 +26,7 @@ cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* 
 cudaError_t launch_xq(const float* x, int n, int tokens, __half* xq, float* xq_mult,
                       cudaStream_t s);
 cudaError_t launch_swiglu(float* gate, const float* up, int n, uint32_t* status, cudaStream_t s);
+cudaError_t launch_stage_rows(const float* src, float* dst, size_t n, cudaStream_t s);
 }  // namespace wh
 
 using namespace wh;
@@ -49,6 +50,19 @@ wh_status cuda_fail(cudaError_t e, const char* where) {
   } while (0)
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// 0: device (or managed) memory; 1: pinned host memory the device reaches at
+// the same address; -1: neither (pageable host memory, or not a valid pointer)
+int device_reach(const void* p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) return 0;
+  if (at.type == cudaMemoryTypeHost) return at.devicePointer == p ? 1 : -1;
+  return -1;
+}
 
 // ---------------------------------------------------------------------------
 // Act-quant threshold table: ceilf(log2f(q)) == k for q = 2^k * (1 + m/2^23)
@@ -838,10 +852,17 @@ bool use_grouped(const wh_moe_plan* p, int tokens) {
   return p->d.exact == 2 ? tokens >= 1 : tokens >= kGroupedMinTokens;
 }
 
+// the path's scratch, then room to stage x when the caller passes it in host
+// memory
+size_t moe_path_scratch_bytes(const wh_moe_plan* p, int tokens) {
+  return use_grouped(p, tokens) ? grouped_scratch_layout(p, tokens, nullptr).bytes
+                                : moe_scratch_layout(p, tokens, nullptr).bytes;
+}
+
 size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
   if (!p || tokens <= 0) return 0;
-  if (use_grouped(p, tokens)) return grouped_scratch_layout(p, tokens, nullptr).bytes;
-  return moe_scratch_layout(p, tokens, nullptr).bytes;
+  return align256(moe_path_scratch_bytes(p, tokens)) +
+         align256(sizeof(float) * (size_t)tokens * p->d.hidden);
 }
 
 // Batched path (tokens >= kGroupedMinTokens): router, routing bookkeeping and
@@ -940,6 +961,22 @@ wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens
   if (!p->d.gate) return fail(WH_ERR_INVALID_POINTER, "plan has no router gate");
   if (!aligned(x, 16) || !aligned(scratch, 256))
     return fail(WH_ERR_INVALID_POINTER, "x must be 16-byte and scratch 256-byte aligned");
+  if (scratch_bytes < wh_moe_scratch_bytes(p, tokens))
+    return fail(WH_ERR_SCRATCH_TOO_SMALL, "moe scratch too small");
+  // x and y may be device memory or pinned host memory the device can address
+  // (the reference passes host slices): x is then pulled into the scratch by a
+  // kernel and y is written straight to host memory by the last kernel, with no
+  // copy-engine transfer on either side
+  const int xk = device_reach(x), yk = device_reach(y);
+  if (xk < 0 || yk < 0)
+    return fail(WH_ERR_INVALID_POINTER,
+                "x and y must be device memory or pinned, device-mapped host memory");
+  if (xk == 1) {
+    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) +
+                                         align256(moe_path_scratch_bytes(p, tokens)));
+    WH_CUDA(launch_stage_rows(x, xs, (size_t)tokens * p->d.hidden, stream));
+    x = xs;
+  }
   if (use_grouped(p, tokens))
     return moe_ffn_grouped(c, p, x, tokens, hash_ids, y, ids_out, weights_out, scratch,
                            scratch_bytes, stream);

@@ -1096,6 +1096,23 @@ cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* 
 }
 
 // Stand-alone act quant to f16 grid values + block multipliers (x = q*mult/8)
+// x from pinned host memory into device memory (n floats, 16-byte aligned):
+// one pass over the bus, no copy engine
+__global__ void __launch_bounds__(256) stage_rows_kernel(const float4* __restrict__ src,
+                                                         float4* __restrict__ dst, size_t n4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+cudaError_t launch_stage_rows(const float* src, float* dst, size_t n, cudaStream_t s) {
+  const size_t n4 = n / 4;
+  const unsigned grid = (unsigned)std::min<size_t>((n4 + 255) / 256, 1024);
+  stage_rows_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(src),
+                                         reinterpret_cast<float4*>(dst), n4);
+  return cudaGetLastError();
+}
+
 __global__ void xq_kernel(const float* x, int n, int tokens, __half* xq, float* xq_mult) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   pdl_wait_prior();
