@@ -49,7 +49,25 @@ typedef enum wh_status {
   WH_ERR_CUDA = 20,           /* a CUDA runtime call failed (detail: wh_last_error_detail) */
   WH_ERR_NCCL = 21,           /* a collective failed (expert parallelism) */
   WH_ERR_TIMEOUT = 22,        /* a bounded device-side wait expired */
-  WH_ERR_DEVICE_ARG = 23      /* a device-side index check failed (e.g. expert id) */
+  WH_ERR_DEVICE_ARG = 23,     /* a device-side index check failed (e.g. expert id) */
+  /* ZCBLK01 blocks: ComputeError variants (src/compute.rs:329-343); the detail
+   * string (wh_last_error_detail) is the variant's &'static str. */
+  WH_ERR_BLOCK_MAGIC = 30,     /* InvalidQuantBlockMagic */
+  WH_ERR_BLOCK_VERSION = 31,   /* UnsupportedQuantBlockVersion */
+  WH_ERR_BLOCK_TRUNCATED = 32, /* TruncatedQuantBlock(field) */
+  WH_ERR_BLOCK_INVALID = 33,   /* InvalidQuantBlock(reason) */
+  WH_ERR_TENSOR_INDEX = 34,    /* TensorIndexOutOfRange */
+  /* ZCINF01 model files: ModelFormatError variants (src/model_format.rs:31-55)
+   * and SchedulerError::InvalidExpert (src/scheduler.rs:14). */
+  WH_ERR_IO = 40,              /* Io */
+  WH_ERR_MODEL_MAGIC = 41,     /* InvalidMagic */
+  WH_ERR_MODEL_VERSION = 42,   /* UnsupportedVersion */
+  WH_ERR_UNALIGNED = 43,       /* Unaligned { field } (detail = the field name) */
+  WH_ERR_TRUNCATED_MANIFEST = 44, /* TruncatedManifest */
+  WH_ERR_LAYER_COUNT = 45,     /* LayerCountMismatch */
+  WH_ERR_EXPERT_TABLE = 46,    /* InvalidExpertTable */
+  WH_ERR_SHARD_MAP = 47,       /* ShardMap (shard map or experts pack index) */
+  WH_ERR_INVALID_EXPERT = 48   /* the layer has no expert with that id */
 } wh_status;
 
 /* ------------------------------------------------------------------------ */
@@ -314,6 +332,150 @@ wh_status wh_ep_p2p_expert_ffn(wh_ctx* ctx, wh_ep_window* window, const float* x
 wh_status wh_ep_p2p_combine(wh_ctx* ctx, wh_ep_window* window, const int32_t* ids,
                             const float* weights, const int32_t* pos, int tokens,
                             const float* y_shared, float* y, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* ZCBLK01 tensor blocks (host memory; no device work)                        */
+/* ------------------------------------------------------------------------ */
+/* A block is [header 40 B][records 52 B each][names][data][shapes]; all
+ * positions below are byte offsets from the start of the block. */
+typedef struct wh_zcblk_header {
+  uint32_t tensor_count, quant_format, flags, reserved;
+  uint64_t record_table_offset, names_offset;
+} wh_zcblk_header;
+
+typedef struct wh_zcblk_tensor {
+  uint16_t dtype_original, quant_format;
+  uint32_t rank, flags; /* role = flags & 0xffff (TensorRole, src/compute.rs:455-499) */
+  uint64_t name_pos, name_len;
+  uint64_t shape_pos;   /* the [rank:u32][dims:u64 x rank] blob */
+  uint64_t data_pos, data_len;
+  float scale, zero_point;
+  uint32_t reserved;
+} wh_zcblk_tensor;
+
+/* Replaces parse_quant_block (src/compute.rs:1099-1147). */
+wh_status wh_zcblk_parse(const uint8_t* block, size_t len, wh_zcblk_header* out);
+/* Replaces QuantBlockLayout::tensor (src/compute.rs:545-595). */
+wh_status wh_zcblk_tensor_at(const uint8_t* block, size_t len, uint32_t index,
+                             wh_zcblk_tensor* out);
+/* Replaces ShapeLayout::dim (src/compute.rs:514-520). */
+wh_status wh_zcblk_tensor_dim(const uint8_t* block, size_t len, const wh_zcblk_tensor* tensor,
+                              uint32_t index, uint64_t* out);
+/* Replaces find_tensor_by_suffix (src/compute.rs:1149-1169): the one tensor
+ * whose name ends with `suffix` (NUL-terminated). */
+wh_status wh_zcblk_find_suffix(const uint8_t* block, size_t len, const char* suffix,
+                               wh_zcblk_tensor* out);
+
+typedef struct wh_zcblk_fp4_view {
+  uint64_t weight_pos, weight_len, scale_pos, scale_len;
+  uint64_t rows, cols, scale_cols;
+} wh_zcblk_fp4_view;
+typedef struct wh_zcblk_fp4_expert_view {
+  wh_zcblk_fp4_view w1, w3, w2;
+} wh_zcblk_fp4_expert_view;
+/* Replaces parse_quant_block + deepseek_v4_fp4_expert_from_quant_block
+ * (src/compute.rs:1199-1267): w1/w3/w2 found by the .wN.weight / .wN.scale
+ * name suffixes, checked as FP4 E2M1 packed + UE8M0, shapes cross-checked. */
+wh_status wh_zcblk_fp4_expert(const uint8_t* block, size_t len, wh_zcblk_fp4_expert_view* out);
+
+/* Device bytes one expert block of `payload_bytes` needs once its six tensors
+ * are placed at 256-byte boundaries (w1 weight, w1 scale, w3 weight, w3 scale,
+ * w2 weight, w2 scale). */
+size_t wh_fp4_expert_device_bytes(uint64_t payload_bytes);
+/* Parses one FP4 expert block held in host memory and copies its six tensors
+ * to `dst` (device, 256-byte aligned, at least wh_fp4_expert_device_bytes);
+ * `out` receives device specs for wh_fp4_expert_forward / wh_moe_desc.  The
+ * copies are asynchronous on `stream`; keep `block` alive until they finish. */
+wh_status wh_fp4_expert_upload(wh_ctx* ctx, const uint8_t* block, size_t len, void* dst,
+                               size_t dst_bytes, wh_fp4_expert* out, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* ZCINF01 model manifest, shard map and experts pack                        */
+/* ------------------------------------------------------------------------ */
+/* EngineHeader (src/model_format.rs:57-81), 128 bytes. */
+typedef struct wh_engine_header {
+  uint8_t magic[8];
+  uint32_t version, endian;
+  uint64_t file_size, manifest_offset, manifest_size, tokenizer_offset, tokenizer_size;
+  uint64_t router_metadata_offset, router_metadata_size;
+  uint32_t model_family, architecture, num_layers, hidden_size, num_attention_heads;
+  uint32_t num_kv_heads, experts_per_layer, active_experts_per_token, block_alignment;
+  uint32_t disk_quant_format;
+  uint64_t manifest_checksum, file_checksum;
+} wh_engine_header;
+
+/* MoELayerBlockDesc (src/model_format.rs:141-150); block type = flags & 0xff
+ * (0 compute, 1 global auxiliary). */
+typedef struct wh_model_layer {
+  uint32_t layer_id, flags;
+  uint64_t dense_offset, dense_disk_bytes, dense_payload_bytes, dense_dequant_bytes;
+  uint32_t num_experts, reserved;
+} wh_model_layer;
+
+/* ExpertBlockDescDisk (src/model_format.rs:113-125), 56 bytes. */
+typedef struct wh_model_expert {
+  uint32_t layer_id, expert_id;
+  uint64_t disk_offset, disk_bytes, payload_bytes, dequant_bytes;
+  uint32_t quant_format, route_rank_hint;
+  uint64_t checksum;
+} wh_model_expert;
+
+#define WH_SOURCE_MODEL 0 /* the model file at the manifest's disk_offset */
+#define WH_SOURCE_SHARD 1 /* an expert shard file named by MODEL.shards.json */
+#define WH_SOURCE_PACK 2  /* the experts pack named by MODEL.experts_pack.index.json */
+typedef struct wh_expert_source {
+  const char* path; /* owned by the model handle */
+  uint64_t offset, disk_bytes, payload_bytes;
+  int kind;         /* WH_SOURCE_* */
+  int reserved;
+} wh_expert_source;
+
+typedef struct wh_model wh_model;
+/* Replaces ModelManifest::load (src/model_format.rs:193-263): header,
+ * manifest, layer and expert tables with their validation, then the optional
+ * MODEL.shards.json (load_optional_shard_map, :339-436; merge_sidecar_experts
+ * = the reference's ZC_SIDECAR_EXPERTS=all) and the optional
+ * MODEL.experts_pack.index.json (load_optional_expert_pack, :463-505). */
+wh_status wh_model_open(const char* path, int merge_sidecar_experts, wh_model** out);
+void wh_model_close(wh_model* model);
+wh_status wh_model_get_header(const wh_model* model, wh_engine_header* out);
+int wh_model_layer_count(const wh_model* model);
+/* `layer_index` is the position in the manifest's layer table (a global
+ * auxiliary block may share layer_id 0 with the first compute layer). */
+wh_status wh_model_get_layer(const wh_model* model, int layer_index, wh_model_layer* out);
+wh_status wh_model_get_expert(const wh_model* model, int layer_index, int expert_index,
+                              wh_model_expert* out);
+/* Where an expert's block is read from, as MoEIoScheduler::enqueue_expert_read
+ * (src/scheduler.rs:148-193): the experts pack when it has the expert, else
+ * the manifest's block in its shard file (if the shard map names one) or in
+ * the model file. */
+wh_status wh_model_expert_source(const wh_model* model, int layer_index, uint32_t expert_id,
+                                 wh_expert_source* out);
+
+/* ------------------------------------------------------------------------ */
+/* Expert loader: FP4 expert blocks from disk into HBM                        */
+/* ------------------------------------------------------------------------ */
+/* Reader threads pread each expert's block into pinned staging buffers (two
+ * per thread) and the copy engines move its six tensors into a caller-owned
+ * device arena at 256-byte boundaries while the next block is read.  No
+ * reference counterpart: the reference reads blocks into host RAM
+ * (src/direct_io.rs) and computes from there; here the experts live in HBM.
+ * threads <= 0 picks 8; direct_io != 0 opens files with O_DIRECT where the
+ * file system allows it. */
+typedef struct wh_expert_loader wh_expert_loader;
+wh_status wh_expert_loader_create(wh_ctx* ctx, const wh_model* model, int threads, int direct_io,
+                                  wh_expert_loader** out);
+void wh_expert_loader_destroy(wh_expert_loader* loader);
+/* Arena bytes wh_expert_loader_load needs for these experts of a layer. */
+wh_status wh_expert_arena_bytes(const wh_model* model, int layer_index,
+                                const uint32_t* expert_ids, int n, size_t* out);
+/* Loads experts expert_ids[0..n) of the layer into `arena` (device memory,
+ * 256-byte aligned, at least wh_expert_arena_bytes); out[i] receives the
+ * device specs of expert_ids[i].  Returns once every block has been read and
+ * its copies queued; work queued on `stream` afterwards sees the weights. */
+wh_status wh_expert_loader_load(wh_expert_loader* loader, int layer_index,
+                                const uint32_t* expert_ids, int n, void* arena,
+                                size_t arena_bytes, wh_fp4_expert* out, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Test hooks (host-only, no device work): expose the host-side pieces the   */

@@ -38,6 +38,20 @@ STATUS_NAMES = {
     21: "Nccl",
     22: "Timeout",
     23: "DeviceArg",
+    30: "InvalidQuantBlockMagic",
+    31: "UnsupportedQuantBlockVersion",
+    32: "TruncatedQuantBlock",
+    33: "InvalidQuantBlock",
+    34: "TensorIndexOutOfRange",
+    40: "Io",
+    41: "InvalidMagic",
+    42: "UnsupportedVersion",
+    43: "Unaligned",
+    44: "TruncatedManifest",
+    45: "LayerCountMismatch",
+    46: "InvalidExpertTable",
+    47: "ShardMap",
+    48: "InvalidExpert",
 }
 ROUTER_RAW_LOGITS = 0
 ROUTER_SQRT_SOFTPLUS = 1
@@ -53,6 +67,12 @@ EXPORTS = (
     "wh_ep_expert_ffn", "wh_ep_combine", "wh_ep_window_bytes", "wh_ep_window_create",
     "wh_ep_window_connect", "wh_ep_window_destroy", "wh_ep_p2p_dispatch",
     "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine", "wh_moe_plan_set_fused_decode",
+    "wh_zcblk_parse", "wh_zcblk_tensor_at", "wh_zcblk_tensor_dim", "wh_zcblk_find_suffix",
+    "wh_zcblk_fp4_expert", "wh_fp4_expert_device_bytes", "wh_fp4_expert_upload",
+    "wh_model_open", "wh_model_close", "wh_model_get_header", "wh_model_layer_count",
+    "wh_model_get_layer", "wh_model_get_expert", "wh_model_expert_source",
+    "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
+    "wh_expert_loader_load",
 )
 
 
@@ -137,6 +157,24 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_debug_e4m3_round_n": (None, [vp, vp, sz]),
         "wh_ctx_set_profiling": (st, [vp, i]),
         "wh_ctx_phase_times": (i, [vp, vp, i]),
+        "wh_zcblk_parse": (st, [vp, sz, vp]),
+        "wh_zcblk_tensor_at": (st, [vp, sz, C.c_uint32, vp]),
+        "wh_zcblk_tensor_dim": (st, [vp, sz, vp, C.c_uint32, vp]),
+        "wh_zcblk_find_suffix": (st, [vp, sz, C.c_char_p, vp]),
+        "wh_zcblk_fp4_expert": (st, [vp, sz, vp]),
+        "wh_fp4_expert_device_bytes": (sz, [C.c_uint64]),
+        "wh_fp4_expert_upload": (st, [vp, vp, sz, vp, sz, C.POINTER(Fp4ExpertSpec), vp]),
+        "wh_model_open": (st, [C.c_char_p, i, C.POINTER(vp)]),
+        "wh_model_close": (None, [vp]),
+        "wh_model_get_header": (st, [vp, vp]),
+        "wh_model_layer_count": (i, [vp]),
+        "wh_model_get_layer": (st, [vp, i, vp]),
+        "wh_model_get_expert": (st, [vp, i, i, vp]),
+        "wh_model_expert_source": (st, [vp, i, C.c_uint32, vp]),
+        "wh_expert_loader_create": (st, [vp, vp, i, i, C.POINTER(vp)]),
+        "wh_expert_loader_destroy": (None, [vp]),
+        "wh_expert_arena_bytes": (st, [vp, i, vp, i, C.POINTER(sz)]),
+        "wh_expert_loader_load": (st, [vp, i, vp, i, vp, sz, C.POINTER(Fp4ExpertSpec), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

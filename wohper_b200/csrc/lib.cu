@@ -6,4 +6,5 @@
 #include "grouped.cu"
 #include "ep.cu"
 #include "capi.cu"
+#include "zcblk.cu"
 #include "noalloc.cu"
