@@ -365,6 +365,226 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
   pdl_launch_dependents();
 }
 
+// ---------------------------------------------------------------------------
+// One-input fast path: lane = row, warp = column group.
+//
+// The reference's g0/g1 chains restart at every 128-column group, so a
+// (row, group) pair is an independent unit of 16 chains x 8 FMAs; only
+// acc_j = fma(P_j, scale_g, acc_j) runs across the groups.  Phase 1 gives each
+// lane one row of the tile and each warp a column group: the lane runs all 16
+// chains of its (row, group) with the group's x read as shared-memory
+// broadcasts and its weight row read as 16-byte words (bank-conflict free
+// under the 128-byte swizzle), and stores P_j = g0_j + g1_j.  Eight chain
+// warps give each (row, j) a thread that runs the acc_j chain over the groups
+// in order, each group as soon as its P_j are stored (one mbarrier per group),
+// so the chain runs under the weight stream; then the pairwise 8-lane sum.
+// Same arithmetic as fp8_gemv_tma_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kRgConsumers = 16;  // phase-1 warps
+constexpr int kRgChain = 8;       // chain warps: 32 rows x 8 chains
+constexpr int kRgMaxGroups = 64;  // cols <= 8192
+constexpr int kRgThreads = 32 * (kRgConsumers + kRgChain + 1);
+
+static int fp8_rg_stages(int cols) {
+  const int ngroups = cols / 128;
+  if (ngroups > kRgMaxGroups) return 0;
+  long long room = (long long)kFp8SmemBudget - 1024 - (long long)cols * 4 -
+                   (long long)ngroups * 32 * 8 * 4 - (2 * kFp8MaxStages + kRgMaxGroups) * 8 -
+                   (32LL * ngroups + 16);
+  int ns = (int)std::max(0LL, room / kFp8StageBytes);
+  return std::min({ns, kFp8MaxStages, ngroups});
+}
+
+size_t fp8_gemv_rg_smem_bytes(int cols) {
+  const int ns = fp8_rg_stages(cols);
+  if (ns < 4) return size_t(1) << 30;
+  const int ngroups = cols / 128;
+  return 1024 + size_t(ns) * kFp8StageBytes +
+         (2 * kFp8MaxStages + kRgMaxGroups) * sizeof(uint64_t) + size_t(cols) * sizeof(float) +
+         size_t(ngroups) * 32 * 8 * sizeof(float) + size_t(32) * ngroups + 16;
+}
+
+__global__ void __launch_bounds__(kRgThreads)
+    fp8_gemv_rowgroup_kernel(const __grid_constant__ CUtensorMap wmap, Fp8GemvArgs a,
+                             int nstages) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
+  uint64_t* empty = full + kFp8MaxStages;
+  uint64_t* pready = empty + kFp8MaxStages;                       // [kRgMaxGroups]
+  float* xs = reinterpret_cast<float*>(pready + kRgMaxGroups);    // cols
+  const int ngroups = a.scale_cols;                               // col_group == 128
+  float* ps = xs + a.cols;                                        // [ngroups][32][8]
+  uint8_t* scale_s = reinterpret_cast<uint8_t*>(ps + ngroups * 32 * 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int box_rows = a.box_rows;
+  const int row0 = a.row_start + blockIdx.x * box_rows;
+
+  // one barrier per thread: a single thread initialising them one after the
+  // other delays the first TMA issue by about a microsecond
+  {
+    const int t = threadIdx.x;
+    const bool ring = ngroups > nstages;  // empty barriers only when slots are reused
+    if (t < nstages) mbar_init(&full[t], 1);
+    else if (t < 2 * kFp8MaxStages && t - kFp8MaxStages < nstages && ring)
+      mbar_init(&empty[t - kFp8MaxStages], 1);  // one warp consumes each group
+    else if (t >= 2 * kFp8MaxStages && t - 2 * kFp8MaxStages < ngroups)
+      mbar_init(&pready[t - 2 * kFp8MaxStages], 1);
+    if (t < 2 * kFp8MaxStages + kRgMaxGroups) fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kRgConsumers + kRgChain) {
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      int g = 0, s = 0;
+      uint32_t phase = 0;
+      for (; g < ngroups; ++g) {
+        if (g >= nstages && !mbar_wait(&empty[s], phase, a.status)) break;
+        mbar_arrive_expect_tx(&full[s], box_rows * 128);
+        tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
+        if (++s == nstages) {
+          s = 0;
+          if (g >= nstages) phase ^= 1u;
+        }
+      }
+      for (int i = max(0, g - nstages); i < g; ++i)
+        mbar_wait(&full[i % nstages], (i / nstages) & 1, a.status);
+    }
+    return;
+  }
+
+  constexpr int nthr = kRgConsumers * 32;
+  const int row_group = a.rows / a.scale_rows;
+  const int last_row = min(row0 + box_rows, a.row_end) - 1;
+  const int srow0 = row0 / row_group;
+  const int nsrows = last_row / row_group - srow0 + 1;
+  if (warp >= kRgConsumers) {
+    // ---- chain warps: acc_j over the groups as their P_j land ----
+    const int t = threadIdx.x - nthr;  // 0 .. 255
+    for (int i = t; i < nsrows * a.scale_cols; i += 32 * kRgChain)
+      scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
+    asm volatile("bar.sync 2, %0;" ::"r"(32 * kRgChain));
+    const int rr = t >> 3, j = t & 7;
+    const int row = row0 + rr;
+    const bool active = rr < box_rows && row < a.row_end;
+    const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
+    const float* pj = ps + rr * 8 + j;
+    float acc = 0.0f;
+    bool ok = true;
+    for (int g = 0; g < ngroups; ++g) {
+      if (!mbar_wait(&pready[g], 0, a.status)) {
+        ok = false;
+        break;
+      }
+      acc = fmaf(pj[g * 256], decode_ue8m0(srow_s[g]), acc);
+    }
+    // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
+    const float s2 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+    const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
+    const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));
+    if (j == 0 && active && ok) {
+      float tot = __fadd_rn(s8, 0.0f);
+      if (!isfinite(tot)) {
+        // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
+        const uint8_t* srow = a.scale + (long long)(row / row_group) * a.scale_cols;
+        tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs);
+        if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
+      }
+      a.y[row - a.row_start] = tot;
+    }
+    pdl_launch_dependents();
+    return;
+  }
+  pdl_wait_prior();
+  // x: when no act-quant block straddles a 128-column group, each warp stages
+  // (and act-quantises) only the groups it computes, so phase 1 starts without
+  // a CTA-wide barrier and the x loads overlap the weight stream
+  const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  float4* xs4 = reinterpret_cast<float4*>(xs);
+  const bool own_x = a.act_quant_block == 0 || 128 % a.act_quant_block == 0;
+  if (own_x) {
+    for (int g0 = warp; g0 < ngroups; g0 += 4 * kRgConsumers) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (g0 + k * kRgConsumers < ngroups) v[k] = __ldg(x4 + (g0 + k * kRgConsumers) * 32 + lane);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (g0 + k * kRgConsumers < ngroups) xs4[(g0 + k * kRgConsumers) * 32 + lane] = v[k];
+    }
+  } else {
+    const int n4 = a.cols / 4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * nthr) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (i0 + k * nthr < n4) v[k] = __ldg(x4 + i0 + k * nthr);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (i0 + k * nthr < n4) xs4[i0 + k * nthr] = v[k];
+    }
+  }
+  if (own_x) {
+    __syncwarp();
+    if (a.act_quant_block > 0) {
+      for (int g = warp; g < ngroups; g += kRgConsumers)
+        act_quant_smem_warp(xs + g * 128, 128, a.act_quant_block, 0, 1, lane, &c_aq);
+      __syncwarp();
+    }
+  } else {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+    act_quant_smem_warp(xs, a.cols, a.act_quant_block, warp, kRgConsumers, lane, &c_aq);
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+  }
+
+  // ---- phase 1: P_j of (row = lane, group) ----
+  bool ok = true;
+  const int r = lane;
+  const bool has_row = r < box_rows;
+  for (int g = warp; g < ngroups; g += kRgConsumers) {
+    const int s = g % nstages;
+    ok = ok && mbar_wait(&full[s], (uint32_t)((g / nstages) & 1), a.status);
+    if (ok && has_row) {
+      const uint8_t* wrow = stages + s * kFp8StageBytes + r * 128;
+      const float4* xg = reinterpret_cast<const float4*>(xs + g * 128);
+      float2 g0[4], g1[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) g0[k] = g1[k] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(wrow + 16 * (c ^ (r & 7)));
+        const float4 x0 = xg[4 * c], x1 = xg[4 * c + 1], x2 = xg[4 * c + 2], x3 = xg[4 * c + 3];
+        // bytes 0..7 (w.x, w.y): g0 chains j = 0..7; bytes 8..15: g1 chains
+        g0[0] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.x)), make_float2(x0.x, x0.y), g0[0]);
+        g0[1] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.x >> 16)), make_float2(x0.z, x0.w), g0[1]);
+        g0[2] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.y)), make_float2(x1.x, x1.y), g0[2]);
+        g0[3] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.y >> 16)), make_float2(x1.z, x1.w), g0[3]);
+        g1[0] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.z)), make_float2(x2.x, x2.y), g1[0]);
+        g1[1] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.z >> 16)), make_float2(x2.z, x2.w), g1[1]);
+        g1[2] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.w)), make_float2(x3.x, x3.y), g1[2]);
+        g1[3] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.w >> 16)), make_float2(x3.z, x3.w), g1[3]);
+      }
+      float4* pd = reinterpret_cast<float4*>(ps + (g * 32 + r) * 8);
+      const float2 p0 = fadd2(g0[0], g1[0]), p1 = fadd2(g0[1], g1[1]);
+      const float2 p2 = fadd2(g0[2], g1[2]), p3 = fadd2(g0[3], g1[3]);
+      pd[0] = make_float4(p0.x, p0.y, p1.x, p1.y);
+      pd[1] = make_float4(p2.x, p2.y, p3.x, p3.y);
+    }
+    // the P_j stores of the warp before the arrival (which releases them to
+    // the chain warps); after a timed-out wait the arrivals still come, so no
+    // chain thread waits on a group that will never be computed
+    __syncwarp();
+    if (lane == 0) {
+      if (ngroups > nstages) mbar_arrive(&empty[s]);
+      mbar_arrive(&pready[g]);
+    }
+  }
+  pdl_launch_dependents();
+}
+
 static size_t fp8_scale_smem(int cols) { return size_t(32) * (cols / 128) + 16; }
 
 size_t fp8_gemv_smem_bytes(int tb, int cols) {
@@ -391,6 +611,15 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
     return cudaLaunchKernelEx(&cfg, fp8_gemv_generic_kernel, a);
   }
   const int nrows = a.row_end - a.row_start;
+  if (a.batch == 1 && a.ldx >= a.cols && fp8_gemv_rg_smem_bytes(a.cols) <= kFp8SmemBudget + 1024) {
+    const int ns = fp8_rg_stages(a.cols);
+    cfg.blockDim = dim3(kRgThreads);
+    cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows);
+    cfg.dynamicSmemBytes = fp8_gemv_rg_smem_bytes(a.cols);
+    cudaError_t e = ensure_smem(fp8_gemv_rowgroup_kernel, cfg.dynamicSmemBytes);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, fp8_gemv_rowgroup_kernel, *wmap, a, ns);
+  }
   const int tb = a.batch < 8 ? (a.batch < 4 ? (a.batch < 2 ? 1 : 2) : 4) : 8;
   const int nconsumer = (a.box_rows + 3) / 4;  // 4 rows per consumer warp
   const int ns = fp8_stages(tb, a.cols, a.scale_cols);
