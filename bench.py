@@ -1052,6 +1052,151 @@ def run_expert_load(args):
     return res
 
 
+# ---------------------------------------------------------------------------
+# BF16 lm_head top-k over the DeepSeek vocabulary
+# ---------------------------------------------------------------------------
+VOCAB = 129280
+METRIC_LM = "lm_head top-k tokens/s (BF16 129280 x 4096 logits + top-k)"
+WORKLOAD_LM = ("lm_head top-k: every logit of the BF16 lm_head of DeepSeek-V3/V4 shape "
+               "(129280 x 4096, 1.06 GB) in the reference's dot_bf16_row order, then the "
+               "top-k push_topk_candidate keeps, sorted; one hidden vector per step")
+LM_TRAFFIC_RATIO = None  # DRAM bytes / algorithmic bytes of lm_logits_kernel (ncu, lmhead case)
+
+
+def lm_head_cpu(w_np, xs, k, steps):
+    """The oracle's restatement on all host threads: seconds per step."""
+    import oracle as O
+
+    O.lm_head_topk(w_np[:4096], xs[0], k)  # warm the library
+    t0 = time.perf_counter()
+    for i in range(steps):
+        O.lm_head_topk(w_np, xs[i % len(xs)], k)
+    return (time.perf_counter() - t0) / steps
+
+
+def run_lm_head(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    k = max(args.lm_top_k, 1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(700 + rank)
+    w = (torch.randn(VOCAB, HID, device=dev, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16)
+    xs = [torch.randn(HID, device=dev, generator=g) for _ in range(8)]
+    if args.impl == "reference":
+        res = None
+        if rank == 0:
+            w_np = w.cpu().numpy().view(np.uint16)
+            xs_np = [x.cpu().numpy() for x in xs]
+            sec = lm_head_cpu(w_np, xs_np, k, max(args.steps, 1))
+            v = 1.0 / sec
+            res = {"metric": METRIC_LM, "value": round(v, 2), "unit": "tokens/s",
+                   "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                   "higher_is_better": True, "impl": "reference", "scaling": "weak",
+                   "vs_baseline": None, "dtype": "bf16 x f32, f32 accumulate",
+                   "data": "synthetic (N(0, 0.02) bf16 weights, N(0, 1) hidden vectors)",
+                   "config": {"workload": WORKLOAD_LM, "rows": VOCAB, "cols": HID, "top_k": k},
+                   "cpu_baseline": {"value": round(v, 2), "unit": "tokens/s",
+                                    "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"{max(args.steps, 1)} full steps"},
+                   "e2e": {"value": round(v, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}}
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return res
+
+    import wohper_b200 as W
+
+    ctx = W.Context(local)
+    scratch = torch.empty(W.lib().wh_lm_head_scratch_bytes(VOCAB, k), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        W.lm_head_topk_score(ctx, w, xs[i % 8], k, scratch=scratch)
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            W.lm_head_topk_score(ctx, w, xs[i % 8], k, scratch=scratch)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ctx.sync()
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    ctx.set_profiling(True)
+    phases = []
+    for i in range(5):
+        W.lm_head_topk_score(ctx, w, xs[i % 8], k, scratch=scratch)
+        phases.append(ctx.phase_times())
+    ctx.set_profiling(False)
+    ctx.sync()
+    ph = np.median(np.array(phases), axis=0)  # logits, collect, select
+    # end to end: x from pinned host memory, tokens + logits back to it
+    xh = [x.cpu().pin_memory() for x in xs]
+    xd = torch.empty(HID, device=dev)
+    th = torch.empty(k, dtype=torch.int32).pin_memory()
+    vh = torch.empty(k).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        ev2[i][0].record(stream)
+        xd.copy_(xh[i % 8], non_blocking=True)
+        t, v = W.lm_head_topk_score(ctx, w, xd, k, scratch=scratch)
+        th[:t.numel()].copy_(t, non_blocking=True)
+        vh[:v.numel()].copy_(v, non_blocking=True)
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    peak, peak_kind = peaks()
+    alg = VOCAB * HID * 2 + HID * 4 + VOCAB * 4
+    logits_ms = float(ph[0])
+    achieved = alg / (logits_ms * 1e-3) / 1e9
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC_LM, "value": round(world * 1e3 / ms_step, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 x f32, f32 accumulate (reference dot order)",
+            "data": "synthetic (N(0, 0.02) bf16 weights, N(0, 1) hidden vectors)",
+            "config": {"workload": WORKLOAD_LM, "rows": VOCAB, "cols": HID, "top_k": k,
+                       "l2": "inputs larger than L2 (1.06 GB of weights per step)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "phases_ms": {"logits": round(logits_ms, 4), "collect": round(float(ph[1]), 4),
+                          "select": round(float(ph[2]), 4)},
+            "roofline": {"kernel": "lm_logits_kernel", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "algorithmic_bytes": alg,
+                         "traffic": int(alg * LM_TRAFFIC_RATIO) if LM_TRAFFIC_RATIO else None},
+            "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": HID * 4,
+                    "d2h_bytes_per_step": k * 8,
+                    "path": "pinned host x -> H2D -> wh_lm_head_topk (C ABI) -> D2H tokens + logits"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            w_np = w.cpu().numpy().view(np.uint16)
+            sec = lm_head_cpu(w_np, [x.cpu().numpy() for x in xs], k, 3)
+            res["cpu_baseline"] = {"value": round(1.0 / sec, 2), "unit": "tokens/s",
+                                   "cores": os.cpu_count(), "kind": "port",
+                                   "sample": "3 full steps (all 129280 rows, top-k) of the "
+                                             "oracle's restatement on all host threads"}
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res
+
+
 def run_ncu_case(args):
     """Small single-GPU workloads for ncu captures (no JSON bench line).
 
@@ -1062,6 +1207,8 @@ def run_ncu_case(args):
     grouped16: the config-3 batched path at 256 tokens and 16 experts (plus
            the shared one) of the config shape: router, dispatch, grouped up
            and down GEMMs, combine per step.
+    lmhead: the BF16 lm_head top-50 on 32768 x 4096 (268 MB of weights),
+           logits + candidates + selection per step.
     L2 is flushed (256 MiB memset) before every step."""
     import torch
 
@@ -1071,7 +1218,16 @@ def run_ncu_case(args):
     ctx = W.Context(0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     n = args.warmup + args.steps
-    if args.ncu_case == "fp8":
+    if args.ncu_case == "lmhead":
+        g = torch.Generator(device="cuda")
+        g.manual_seed(3)
+        wl = (torch.randn(32768, HID, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        wl = wl.view(torch.int16)
+        x = torch.randn(HID, device="cuda", generator=g)
+        for _ in range(n):
+            flush.zero_()
+            W.lm_head_topk_score(ctx, wl, x, 50)
+    elif args.ncu_case == "fp8":
         w, s = H.fp8_weight(1, HID, HID)
         wd, sd = torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda()
         x = torch.from_numpy(H.activations(2, 1, HID).reshape(-1)).cuda()
@@ -1133,14 +1289,16 @@ def main():
                          "4: expert-parallel layer over the ranks")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="config 4: rows over NVLink peer stores (p2p) or NCCL all-to-all")
-    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head"],
                     help="moe: the MoE FFN step of --config (default); expert-load: one "
-                         "layer's FP4 experts from an experts pack on disk into HBM")
+                         "layer's FP4 experts from an experts pack on disk into HBM; lm-head: "
+                         "the BF16 lm_head top-k over the DeepSeek vocabulary")
     ap.add_argument("--load-threads", type=int, default=8,
                     help="expert-load: reader threads of the expert loader")
     ap.add_argument("--direct-io", action="store_true",
                     help="expert-load: O_DIRECT reads (bypass the page cache)")
-    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16"],
+    ap.add_argument("--lm-top-k", type=int, default=50, help="lm-head: top_k")
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
     if args.ncu_case:
@@ -1149,6 +1307,8 @@ def main():
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.workload == "expert-load":
         res = run_expert_load(args)
+    elif args.workload == "lm-head":
+        res = run_lm_head(args)
     elif args.config == 3 and args.impl == "ours":
         res = run_config3(args)
     elif args.config == 4 and args.impl == "ours":

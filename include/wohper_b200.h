@@ -334,6 +334,25 @@ wh_status wh_ep_p2p_combine(wh_ctx* ctx, wh_ep_window* window, const int32_t* id
                             const float* y_shared, float* y, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* BF16 lm_head top-k                                                         */
+/* ------------------------------------------------------------------------ */
+/* Device scratch bytes wh_lm_head_topk needs. */
+size_t wh_lm_head_scratch_bytes(long long rows, int top_k);
+/* Replaces score_bf16_lm_head_topk (src/compute.rs:2867-2913) and
+ * RowIndex::topk_bf16_lm_head (src/row_index.rs:208-300): every row's logit is
+ * dot_bf16_row (src/compute.rs:6116-6136) of weight [rows][cols] (bf16 bits)
+ * with x, bit-exact; the rows kept are those push_topk_candidate keeps
+ * (src/compute.rs:2948-2962), ties and NaNs included, written sorted
+ * descending by total_cmp: out_tokens / out_logits [min(top_k, rows)]
+ * (device), token = row_base + row.  top_k < 1 means 1 (top_k.max(1)).
+ * logits (nullable, [rows], device) also receives every row's logit.  Needs
+ * cols % 8 == 0 and a 16-byte aligned weight; top_k <= 511; cols <= 16384. */
+wh_status wh_lm_head_topk(wh_ctx* ctx, const uint16_t* weight, long long rows, int cols,
+                          uint32_t row_base, const float* x, size_t x_len, int top_k,
+                          uint32_t* out_tokens, float* out_logits, float* logits, void* scratch,
+                          size_t scratch_bytes, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* ZCBLK01 tensor blocks (host memory; no device work)                        */
 /* ------------------------------------------------------------------------ */
 /* A block is [header 40 B][records 52 B each][names][data][shapes]; all

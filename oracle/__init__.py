@@ -98,6 +98,8 @@ def lib() -> C.CDLL:
         L.orc_bf16_dot_row.restype = f
         L.orc_bf16_gemv.argtypes = [vp, sz, sz, vp, vp]
         L.orc_bf16_gemv.restype = i
+        L.orc_lm_head_topk.argtypes = [vp, sz, sz, vp, sz, C.c_uint32, vp, vp, vp]
+        L.orc_lm_head_topk.restype = i
         L.orc_fp4_matvec.argtypes = [C.POINTER(Fp4Spec), vp, sz, vp, sz, i]
         L.orc_fp4_matvec.restype = i
         L.orc_fp4_expert_forward.argtypes = [C.POINTER(Fp4Expert), vp, sz, vp, sz, vp, sz]
@@ -212,6 +214,20 @@ def bf16_gemv(w_u16, x):
     y = np.zeros(w.shape[0], np.float32)
     st = lib().orc_bf16_gemv(_p(w), w.shape[0], w.shape[1], _p(x), _p(y))
     return st, y
+
+
+def lm_head_topk(w_u16, x, top_k, row_base=0):
+    """score_bf16_lm_head_topk + push_topk_candidate + the final sort: returns
+    (count, tokens, logits of the top-k, all logits)."""
+    w, x = _c(w_u16, np.uint16), _c(x, np.float32)
+    rows, cols = w.shape
+    k = max(int(top_k), 1)
+    tok = np.zeros(k, np.uint32)
+    val = np.zeros(k, np.float32)
+    logits = np.zeros(rows, np.float32)
+    n = lib().orc_lm_head_topk(_p(w), rows, cols, _p(x), k, row_base, _p(tok), _p(val),
+                               _p(logits))
+    return n, tok[:max(n, 0)], val[:max(n, 0)], logits
 
 
 def fp4_matvec(packed, scales, rows, cols, scale_cols, x, path=0, out_len=None):

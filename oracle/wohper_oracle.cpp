@@ -828,6 +828,48 @@ size_t orc_deepseek_sqrtsoftplus_route(const float* logits, size_t n, const floa
   return k;
 }
 
+// score_bf16_lm_head_topk + push_topk_candidate + the final sort
+// (src/compute.rs:2838-2962)
+int orc_lm_head_topk(const uint16_t* weight, size_t rows, size_t cols, const float* x,
+                     size_t top_k, uint32_t row_base, uint32_t* tokens_out, float* logits_topk,
+                     float* logits_out) {
+  if (rows == 0) return -1;
+  top_k = std::max<size_t>(top_k, 1);
+  std::vector<float> logits(rows);
+  orc_bf16_gemv(weight, rows, cols, x, logits.data());
+  if (logits_out) std::copy(logits.begin(), logits.end(), logits_out);
+  auto key = [](float f) {  // f32::total_cmp key
+    int32_t b;
+    std::memcpy(&b, &f, 4);
+    return b ^ (int32_t)(((uint32_t)(b >> 31)) >> 1);
+  };
+  std::vector<std::pair<uint32_t, float>> best;
+  best.reserve(std::min<size_t>(top_k, 64));
+  for (size_t r = 0; r < rows; ++r) {
+    const uint32_t token = row_base + (uint32_t)r;
+    const float logit = logits[r];
+    if (best.size() < top_k) {
+      best.push_back({token, logit});
+      continue;
+    }
+    // min_by(total_cmp): the first of equal minima
+    size_t worst = 0;
+    for (size_t i = 1; i < best.size(); ++i)
+      if (key(best[i].second) < key(best[worst].second)) worst = i;
+    if (logit > best[worst].second) best[worst] = {token, logit};
+  }
+  // sort_by(|l, r| r.total_cmp(l)): stable, descending
+  std::stable_sort(best.begin(), best.end(),
+                   [&](const std::pair<uint32_t, float>& l, const std::pair<uint32_t, float>& r) {
+                     return key(l.second) > key(r.second);
+                   });
+  for (size_t i = 0; i < best.size(); ++i) {
+    tokens_out[i] = best[i].first;
+    logits_topk[i] = best[i].second;
+  }
+  return (int)best.size();
+}
+
 // compute_active_and_shared_experts (src/compute.rs:1872-1946)
 int orc_moe_combine_token(const orc_fp4_expert* experts, const int32_t* ids, const float* weights,
                           size_t topk, const orc_fp4_expert* shared_fp4,

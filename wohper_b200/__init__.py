@@ -72,7 +72,7 @@ EXPORTS = (
     "wh_model_open", "wh_model_close", "wh_model_get_header", "wh_model_layer_count",
     "wh_model_get_layer", "wh_model_get_expert", "wh_model_expert_source",
     "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
-    "wh_expert_loader_load",
+    "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
 )
 
 
@@ -157,6 +157,9 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_debug_e4m3_round_n": (None, [vp, vp, sz]),
         "wh_ctx_set_profiling": (st, [vp, i]),
         "wh_ctx_phase_times": (i, [vp, vp, i]),
+        "wh_lm_head_scratch_bytes": (sz, [C.c_longlong, i]),
+        "wh_lm_head_topk": (st, [vp, vp, C.c_longlong, i, C.c_uint32, vp, sz, i, vp, vp, vp, vp,
+                                 sz, vp]),
         "wh_zcblk_parse": (st, [vp, sz, vp]),
         "wh_zcblk_tensor_at": (st, [vp, sz, C.c_uint32, vp]),
         "wh_zcblk_tensor_dim": (st, [vp, sz, vp, C.c_uint32, vp]),
@@ -366,6 +369,29 @@ def route_experts(ctx, gate_bf16, x, topk: int, mode: int = ROUTER_RAW_LOGITS, b
 # --------------------------------------------------------------------------
 # MoE layer
 # --------------------------------------------------------------------------
+def lm_head_topk_score(ctx: Context, weight_bf16, x, top_k: int, row_base: int = 0,
+                       logits=None, scratch=None, stream=None):
+    """score_bf16_lm_head_topk + push_topk_candidate + the final sort
+    (src/compute.rs:2838-2962) on the device: weight_bf16 [rows, cols] (bf16 bits as
+    int16/uint16, or a bfloat16 tensor), x [cols] f32.  Returns (tokens int32,
+    logits f32) of min(top_k, rows) entries, sorted descending."""
+    import torch
+
+    rows, cols = weight_bf16.shape
+    k = max(int(top_k), 1)
+    n = min(k, rows)
+    dev = weight_bf16.device
+    toks = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
+    vals = torch.empty(max(k, 1), dtype=torch.float32, device=dev)
+    if scratch is None:
+        scratch = torch.empty(lib().wh_lm_head_scratch_bytes(rows, k), dtype=torch.uint8,
+                              device=dev)
+    _check(lib().wh_lm_head_topk(ctx.handle, _ptr(weight_bf16), rows, cols, row_base, _ptr(x),
+                                 x.numel(), k, _ptr(toks), _ptr(vals), _ptr(logits),
+                                 _ptr(scratch), scratch.numel(), _stream(stream)))
+    return toks[:n], vals[:n]
+
+
 class MoeLayer:
     """A prepared MoE FFN layer (router + routed FP4 experts + shared expert).
 

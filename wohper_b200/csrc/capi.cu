@@ -670,6 +670,64 @@ wh_status wh_router_topk(wh_ctx* c, const uint16_t* gate, int experts, int hidde
 }
 
 // ---------------------------------------------------------------------------
+size_t wh_lm_head_scratch_bytes(long long rows, int top_k) {
+  return lm_head_scratch_bytes(rows < 1 ? 1 : rows, top_k < 1 ? 1 : top_k);
+}
+
+wh_status wh_lm_head_topk(wh_ctx* c, const uint16_t* weight, long long rows, int cols,
+                          uint32_t row_base, const float* x, size_t x_len, int top_k,
+                          uint32_t* out_tokens, float* out_logits, float* logits, void* scratch,
+                          size_t scratch_bytes, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  top_k = top_k < 1 ? 1 : top_k;  // top_k.max(1) (src/compute.rs:2777)
+  // src/compute.rs:2769-2797 and score_bf16_lm_head_topk's checks, in order
+  if (!scratch || scratch_bytes == 0) return fail(WH_ERR_SCRATCH_TOO_SMALL, "scratch is empty");
+  if (cols <= 0 || rows < 0) return fail(WH_ERR_INVALID_SHAPE, "LM-head shape");
+  if (x_len < (size_t)cols) return fail(WH_ERR_INVALID_SHAPE, "LM-head input too small");
+  if (rows == 0) return fail(WH_ERR_INVALID_SHAPE, "LM-head has no rows");
+  if (!weight || !x || !out_tokens || !out_logits) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  if (!lm_head_supported(rows, cols, top_k) || cols % 8 != 0 || !aligned(weight, 16))
+    return fail(WH_ERR_UNSUPPORTED,
+                "lm_head top-k needs cols % 8 == 0, cols <= 16384, a 16-byte aligned weight "
+                "and top_k <= 511");
+  if (scratch_bytes < lm_head_scratch_bytes(rows, top_k))
+    return fail(WH_ERR_SCRATCH_TOO_SMALL, "lm_head scratch too small");
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  auto carve = [&](size_t bytes) {
+    uint8_t* q = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+    p = q + bytes;
+    return q;
+  };
+  LmHeadArgs a{};
+  a.weight = weight;
+  a.x = x;
+  a.rows = rows;
+  a.cols = cols;
+  a.top_k = top_k;
+  a.row_base = row_base;
+  float* lg = reinterpret_cast<float*>(carve(size_t(rows) * 4));
+  a.logits = logits ? logits : lg;
+  // flags, counter, candidate count and the histogram are zeroed by one memset
+  a.flags = reinterpret_cast<uint32_t*>(carve(16 + 4096 * 4));
+  a.counter = a.flags + 1;
+  a.cand_count = a.flags + 2;
+  a.hist = reinterpret_cast<int*>(a.flags + 4);
+  a.cand = reinterpret_cast<uint64_t*>(carve(8192 * 8));
+  a.out_tokens = out_tokens;
+  a.out_logits = out_logits;
+  cudaStream_t s = (cudaStream_t)stream;
+  WH_CUDA(cudaMemsetAsync(a.flags, 0, 16 + 4096 * 4, s));
+  wh_status st;
+  c->prof_begin();
+  if ((st = c->prof_mark(s)) != WH_OK) return st;
+  for (int stage = 0; stage < 3; ++stage) {
+    WH_CUDA(launch_lm_head_stage(a, stage, c->pdl(), s));
+    if ((st = c->prof_mark(s)) != WH_OK) return st;
+  }
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
 wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out) {
   if (!c || !d || !out) return fail(WH_ERR_INVALID_POINTER, "null argument");
   *out = nullptr;

@@ -19,6 +19,27 @@ inline cudaError_t ensure_smem(K* kernel, size_t bytes) {
   return ensure_smem_attr(reinterpret_cast<const void*>(kernel), bytes);
 }
 
+// ---------------- BF16 lm_head top-k ----------------
+struct LmHeadArgs {
+  const uint16_t* weight;  // [rows][cols] bf16 bits
+  const float* x;          // [cols]
+  long long rows;
+  int cols;
+  int top_k;
+  uint32_t row_base;
+  float* logits;      // [rows]
+  uint32_t* flags;    // bit 0: a NaN logit (zeroed before the launch)
+  uint32_t* counter;  // passes handed out (zeroed before the launch)
+  uint32_t* cand_count;  // candidates collected (zeroed before the launch)
+  int* hist;             // [4096] histogram (zeroed before the launch)
+  uint64_t* cand;        // [8192] candidate keys
+  uint32_t* out_tokens;
+  float* out_logits;
+};
+size_t lm_head_scratch_bytes(long long rows, int top_k);
+bool lm_head_supported(long long rows, int cols, int top_k);
+cudaError_t launch_lm_head_stage(const LmHeadArgs& a, int stage, bool pdl, cudaStream_t s);
+
 // ---------------- FP8 GEMV ----------------
 struct Fp8GemvArgs {
   const uint8_t* weight;  // [rows][cols] E4M3

@@ -5,6 +5,7 @@
 #include "decode.cu"
 #include "grouped.cu"
 #include "ep.cu"
+#include "lmhead.cu"
 #include "capi.cu"
 #include "zcblk.cu"
 #include "noalloc.cu"
