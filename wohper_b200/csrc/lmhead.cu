@@ -217,13 +217,24 @@ constexpr int kLmCollectRows = 8 * 1024;  // rows per collect CTA
 
 __global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
   __shared__ int s_bin;
+  __shared__ int hist[kLmBins];
   const int tid = threadIdx.x, lane = tid & 31;
   pdl_wait_prior();
+  // the logits this CTA examines, loaded before the histogram work
+  const long long r0 = (long long)blockIdx.x * kLmCollectRows;
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const long long r = r0 + k * 1024 + tid;
+    v[k] = r < a.rows ? a.logits[r] : 0.0f;
+  }
+  for (int i = tid; i < kLmBins; i += blockDim.x) hist[i] = a.hist[i];
+  __syncthreads();
   const long long want = a.rows < a.top_k + 1 ? a.rows : (long long)a.top_k + 1;
   if (tid < 32) {
     // lane l sums 128 bins from the top: [4095 - 128 l - 127, 4095 - 128 l]
     int sum = 0;
-    for (int i = 0; i < 128; ++i) sum += a.hist[kLmBins - 1 - 128 * lane - i];
+    for (int i = 0; i < 128; ++i) sum += hist[kLmBins - 1 - 128 * lane - i];
     int incl = sum;
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -235,7 +246,7 @@ __global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
     if (lane == src) {
       int acc = excl, b = kLmBins - 1 - 128 * lane;
       for (int i = 0; i < 128; ++i, --b) {
-        acc += a.hist[b];
+        acc += hist[b];
         if (acc >= want) break;
       }
       s_bin = b < 0 ? 0 : b;
@@ -243,13 +254,6 @@ __global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
   }
   __syncthreads();
   const int bmin = s_bin;
-  const long long r0 = (long long)blockIdx.x * kLmCollectRows;
-  float v[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const long long r = r0 + k * 1024 + tid;
-    v[k] = r < a.rows ? a.logits[r] : 0.0f;
-  }
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const long long r = r0 + k * 1024 + tid;
@@ -265,9 +269,9 @@ __global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
 // the (k+1)-th (IEEE comparison) and no logit is NaN, the reference's result
 // is exactly the sorted top k; ties, NaNs or more candidates than fit take the
 // exact replay of push_topk_candidate.
-__global__ void __launch_bounds__(1024) lm_select_kernel(LmHeadArgs a) {
+__global__ void __launch_bounds__(256) lm_select_kernel(LmHeadArgs a) {
   extern __shared__ __align__(16) uint64_t lm_sel[];  // cand[kLmSelCap] | replay state
-  __shared__ int s_fallback, s_n;
+  __shared__ int s_n;
   uint64_t* cand = lm_sel;
   uint32_t* best_row = reinterpret_cast<uint32_t*>(cand + kLmSelCap);
   float* best_val = reinterpret_cast<float*>(best_row + kLmMaxK + 1);
@@ -280,17 +284,15 @@ __global__ void __launch_bounds__(1024) lm_select_kernel(LmHeadArgs a) {
     while (n2 < int(n)) n2 <<= 1;
     for (int i = tid; i < n2; i += blockDim.x) cand[i] = i < int(n) ? a.cand[i] : ~0ull;
     bitonic_sort(cand, n2);
-    if (tid == 0) {
-      bool fb = false;
-      if (a.rows > a.top_k) {
-        fb = (*a.flags & 1u) != 0;
-        for (int i = 0; i < a.top_k && !fb; ++i)
-          if (lm_key_value(cand[i]) == lm_key_value(cand[i + 1])) fb = true;  // IEEE tie
-      }
-      s_fallback = fb;
+    // rows <= k: nothing was ever replaced and the key order is the answer;
+    // otherwise an IEEE tie among the first k + 1 (or a NaN) needs the replay
+    bool fb = false;
+    if (a.rows > a.top_k) {
+      for (int i = tid; i < a.top_k; i += blockDim.x)
+        fb |= lm_key_value(cand[i]) == lm_key_value(cand[i + 1]);
+      if (tid == 0) fb |= (*a.flags & 1u) != 0;
     }
-    __syncthreads();
-    replay = s_fallback;
+    replay = __syncthreads_or(fb) != 0;
     if (!replay) {
       const int count = int(a.rows < a.top_k ? a.rows : (long long)a.top_k);
       for (int i = tid; i < count; i += blockDim.x) {
@@ -361,7 +363,7 @@ cudaError_t launch_lm_head_stage(const LmHeadArgs& a, int stage, bool pdl, cudaS
       cfg.gridDim = dim3(unsigned((a.rows + kLmCollectRows - 1) / kLmCollectRows));
       return cudaLaunchKernelEx(&cfg, lm_collect_kernel, a);
     default:
-      cfg.blockDim = dim3(1024);
+      cfg.blockDim = dim3(256);
       cfg.gridDim = dim3(1);
       cfg.dynamicSmemBytes = size_t(kLmSelCap) * 8 + 2 * (kLmMaxK + 1) * 4;
       e = ensure_smem(lm_select_kernel, cfg.dynamicSmemBytes);
