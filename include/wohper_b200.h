@@ -179,6 +179,28 @@ wh_status wh_fp4_expert_forward_noalloc(wh_ctx* ctx, const wh_fp4_expert* expert
                                         size_t output_len, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* FP8 E4M3 x UE8M0(128x128) expert (DeepSeek-V4's shared expert)             */
+/* ------------------------------------------------------------------------ */
+typedef struct wh_fp8_matrix {
+  const uint8_t* weight; /* [rows][cols] E4M3 */
+  const uint8_t* scale;  /* [scale_rows][scale_cols] UE8M0 */
+  int rows, cols, scale_rows, scale_cols;
+} wh_fp8_matrix;
+typedef struct wh_fp8_expert {
+  wh_fp8_matrix w1, w3, w2;
+} wh_fp8_expert;
+
+/* Floats of scratch wh_fp8_expert_forward needs (hidden + 2 * intermediate). */
+size_t wh_fp8_expert_scratch_len(size_t hidden, size_t intermediate);
+/* Replaces compute_deepseek_fp8_shared_expert_into_hidden
+ * (src/compute.rs:5545-5614): act quant (block 64) of the input -> w1, w3 (FP8
+ * GEMV, bit-exact) -> SwiGLU with the reference clamps -> act quant (64) -> w2,
+ * written to output[0..w2.rows).  Shape errors in the reference's order. */
+wh_status wh_fp8_expert_forward(wh_ctx* ctx, const wh_fp8_expert* expert, const float* input,
+                                size_t input_len, float* output, size_t output_len,
+                                float* scratch, size_t scratch_len, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Router                                                                    */
 /* ------------------------------------------------------------------------ */
 #define WH_ROUTER_RAW_LOGITS 0     /* RouterMath::RawLogits + legacy softmax */
@@ -220,6 +242,9 @@ typedef struct wh_moe_desc {
                                    for every call.  The tensor-core path needs hidden
                                    and inter multiples of 512 and no UE8M0 scale byte 0
                                    or 255; otherwise the bit-exact kernels run. */
+  const wh_fp8_expert* shared_fp8; /* nullable: an FP8 shared expert instead of `shared`
+                                      (DeepSeek-V4's layout); y = shared(x) + routed, as
+                                      compute_active_and_shared_experts adds them */
 } wh_moe_desc;
 
 typedef struct wh_moe_plan wh_moe_plan;

@@ -159,6 +159,14 @@ def fp8_matrix(weight, scale, rows, cols, scale_rows, scale_cols, keep: list) ->
     return Fp8Matrix(weight.ctypes.data, scale.ctypes.data, rows, cols, scale_rows, scale_cols)
 
 
+def fp8_expert_forward(expert: Fp8Expert, x):
+    """compute_deepseek_fp8_shared_expert_into_hidden: (status, output[w2.rows])."""
+    x = _c(x, np.float32)
+    y = np.zeros(expert.w2.rows, np.float32)
+    st = lib().orc_fp8_expert_forward(C.byref(expert), _p(x), x.size, _p(y))
+    return st, y
+
+
 def luts() -> dict:
     L = lib()
     out = {}

@@ -73,6 +73,7 @@ EXPORTS = (
     "wh_model_get_layer", "wh_model_get_expert", "wh_model_expert_source",
     "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
     "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
+    "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward",
 )
 
 
@@ -97,13 +98,24 @@ class Fp4ExpertSpec(C.Structure):
     _fields_ = [("w1", Fp4MatvecSpec), ("w3", Fp4MatvecSpec), ("w2", Fp4MatvecSpec)]
 
 
+class Fp8MatrixSpec(C.Structure):
+    """wh_fp8_matrix: E4M3 weight [rows][cols] + UE8M0 scales [scale_rows][scale_cols]."""
+    _fields_ = [("weight", C.c_void_p), ("scale", C.c_void_p), ("rows", C.c_int),
+                ("cols", C.c_int), ("scale_rows", C.c_int), ("scale_cols", C.c_int)]
+
+
+class Fp8ExpertSpec(C.Structure):
+    """wh_fp8_expert: DeepSeek-V4's FP8 shared expert (w1, w3, w2)."""
+    _fields_ = [("w1", Fp8MatrixSpec), ("w3", Fp8MatrixSpec), ("w2", Fp8MatrixSpec)]
+
+
 class MoeDesc(C.Structure):
     _fields_ = [
         ("num_experts", C.c_int), ("hidden", C.c_int), ("inter", C.c_int),
         ("experts", C.POINTER(Fp4ExpertSpec)), ("shared", C.POINTER(Fp4ExpertSpec)),
         ("gate", C.c_void_p), ("gate_bias", C.c_void_p), ("topk", C.c_int),
         ("router_mode", C.c_int), ("route_scale", C.c_float), ("max_tokens", C.c_int),
-        ("exact", C.c_int),
+        ("exact", C.c_int), ("shared_fp8", C.POINTER(Fp8ExpertSpec)),
     ]
 
 
@@ -158,6 +170,9 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_ctx_set_profiling": (st, [vp, i]),
         "wh_ctx_phase_times": (i, [vp, vp, i]),
         "wh_lm_head_scratch_bytes": (sz, [C.c_longlong, i]),
+        "wh_fp8_expert_scratch_len": (sz, [sz, sz]),
+        "wh_fp8_expert_forward": (st, [vp, C.POINTER(Fp8ExpertSpec), vp, sz, vp, sz, vp, sz,
+                                       vp]),
         "wh_lm_head_topk": (st, [vp, vp, C.c_longlong, i, C.c_uint32, vp, sz, i, vp, vp, vp, vp,
                                  sz, vp]),
         "wh_zcblk_parse": (st, [vp, sz, vp]),
@@ -369,6 +384,40 @@ def route_experts(ctx, gate_bf16, x, topk: int, mode: int = ROUTER_RAW_LOGITS, b
 # --------------------------------------------------------------------------
 # MoE layer
 # --------------------------------------------------------------------------
+@dataclass
+class Fp8Matrix:
+    """An FP8 E4M3 matrix with UE8M0 block scales: weight uint8 [rows, cols] and
+    scale uint8 [scale_rows, scale_cols] CUDA tensors."""
+    weight: object
+    scale: object
+
+    def spec(self) -> Fp8MatrixSpec:
+        r, c = self.weight.shape
+        sr, sc = self.scale.shape
+        return Fp8MatrixSpec(_ptr(self.weight), _ptr(self.scale), r, c, sr, sc)
+
+
+@dataclass
+class DeepSeekV4Fp8Expert:
+    """DeepSeek-V4's FP8 shared expert (w1, w3 [inter, hidden], w2 [hidden, inter])."""
+    w1: Fp8Matrix
+    w3: Fp8Matrix
+    w2: Fp8Matrix
+
+    def spec(self) -> Fp8ExpertSpec:
+        return Fp8ExpertSpec(self.w1.spec(), self.w3.spec(), self.w2.spec())
+
+
+def deepseek_v4_fp8_expert_forward(ctx, expert: DeepSeekV4Fp8Expert, input, output, scratch,
+                                   stream=None):
+    """compute_deepseek_fp8_shared_expert_into_hidden (src/compute.rs:5545-5614)."""
+    s = expert.spec()
+    _check(lib().wh_fp8_expert_forward(ctx.handle, C.byref(s), _ptr(input), input.numel(),
+                                       _ptr(output), output.numel(), _ptr(scratch),
+                                       scratch.numel(), _stream(stream)))
+    return output
+
+
 def lm_head_topk_score(ctx: Context, weight_bf16, x, top_k: int, row_base: int = 0,
                        logits=None, scratch=None, stream=None):
     """score_bf16_lm_head_topk + push_topk_candidate + the final sort
@@ -400,9 +449,11 @@ class MoeLayer:
     """
 
     def __init__(self, ctx: Context, experts: Sequence[DeepSeekV4Fp4Expert],
-                 shared: Optional[DeepSeekV4Fp4Expert], gate_bf16, topk: int = 6,
+                 shared, gate_bf16, topk: int = 6,
                  router_mode: int = ROUTER_RAW_LOGITS, route_scale: float = 1.0,
                  gate_bias=None, max_tokens: int = 1, exact: int = 0):
+        """shared: a DeepSeekV4Fp4Expert, a DeepSeekV4Fp8Expert (DeepSeek-V4's
+        layout) or None."""
         import torch
 
         self.ctx = ctx
@@ -414,10 +465,12 @@ class MoeLayer:
         self._gate = gate_bf16
         self._bias = gate_bias
         arr = (Fp4ExpertSpec * len(experts))(*[e.spec() for e in experts])
+        fp8 = isinstance(shared, DeepSeekV4Fp8Expert)
         sh = shared.spec() if shared is not None else None
         d = MoeDesc(len(experts), self.hidden, self.inter, arr,
-                    C.pointer(sh) if sh is not None else None, _ptr(gate_bf16), _ptr(gate_bias),
-                    topk, router_mode, route_scale, max_tokens, int(exact))
+                    C.pointer(sh) if sh is not None and not fp8 else None, _ptr(gate_bf16),
+                    _ptr(gate_bias), topk, router_mode, route_scale, max_tokens, int(exact),
+                    C.pointer(sh) if fp8 else None)
         h = C.c_void_p()
         _check(lib().wh_moe_plan_create(ctx.handle, C.byref(d), C.byref(h)))
         self.plan = h

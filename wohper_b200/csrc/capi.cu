@@ -340,6 +340,8 @@ struct wh_moe_plan {
   uint32_t* dec_sync = nullptr;      // decode kernel's grid counters [4] (zero at rest)
   int decode_ok = -1;                // one-token persistent kernel: -1 not checked yet
   bool decode_on = false;            // wh_moe_plan_set_fused_decode (opt-in)
+  bool has_sfp8 = false;             // an FP8 shared expert (run after the routed path)
+  wh_fp8_expert sfp8{};
 };
 
 extern "C" {
@@ -426,10 +428,14 @@ wh_status wh_act_quant_fp8(wh_ctx* c, float* v, size_t n, int block, wh_stream_t
   return WH_OK;
 }
 
-wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows, int cols,
-                      int scale_rows, int scale_cols, int row_start, int row_end, const float* x,
-                      int batch, int ldx, float* y, int ldy, int act_quant_block,
-                      wh_stream_t stream) {
+}  // extern "C"
+
+namespace {
+// wh_fp8_gemv with an optional addend (laid out like y): y = gemv + addend
+wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows,
+                        int cols, int scale_rows, int scale_cols, int row_start, int row_end,
+                        const float* x, int batch, int ldx, float* y, int ldy,
+                        int act_quant_block, const float* addend, wh_stream_t stream) {
   if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
   // src/compute.rs:6256-6289 validation order
   if (rows <= 0 || cols <= 0 || scale_rows <= 0 || scale_cols <= 0 || rows % scale_rows != 0 ||
@@ -459,6 +465,7 @@ wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, in
   a.batch = batch;
   a.act_quant_block = act_quant_block;
   a.status = c->status;
+  a.addend = addend;
 
   const bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
                     ldx % 4 == 0 && fp8_gemv_smem_bytes(1, cols) <= 200 * 1024;
@@ -485,6 +492,7 @@ wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, in
         Fp8GemvArgs s = a;
         s.x = x + (size_t)b0 * ldx;
         s.y = y + (size_t)b0 * ldy;
+        s.addend = addend ? addend + (size_t)b0 * ldy : nullptr;
         s.batch = std::min(tb, batch - b0);
         WH_CUDA(launch_fp8_gemv(&it->second, s, c->num_sms, stream, false));
       }
@@ -517,6 +525,70 @@ wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, in
   }
   WH_CUDA(launch_fp8_gemv(nullptr, a, c->num_sms, stream, false));
   return WH_OK;
+}
+
+// compute_deepseek_fp8_shared_expert_into_hidden (src/compute.rs:5545-5614) for
+// `tokens` inputs: act quant (64) -> w1, w3 -> SwiGLU with the reference clamps
+// -> act quant (64) -> w2, written to y (+ addend).  h1 / h3: [tokens][inter].
+wh_status fp8_expert_run(wh_ctx* c, const wh_fp8_expert& e, const float* x, int tokens, int ldx,
+                         float* y, int ldy, const float* addend, float* h1, float* h3,
+                         wh_stream_t stream) {
+  const int inter = e.w1.rows;
+  wh_status st;
+  if ((st = fp8_gemv_impl(c, e.w1.weight, e.w1.scale, e.w1.rows, e.w1.cols, e.w1.scale_rows,
+                          e.w1.scale_cols, 0, e.w1.rows, x, tokens, ldx, h1, inter, 64, nullptr,
+                          stream)) != WH_OK)
+    return st;
+  if ((st = fp8_gemv_impl(c, e.w3.weight, e.w3.scale, e.w3.rows, e.w3.cols, e.w3.scale_rows,
+                          e.w3.scale_cols, 0, e.w3.rows, x, tokens, ldx, h3, inter, 64, nullptr,
+                          stream)) != WH_OK)
+    return st;
+  WH_CUDA(launch_swiglu(h1, h3, tokens * inter, c->status, (cudaStream_t)stream));
+  return fp8_gemv_impl(c, e.w2.weight, e.w2.scale, e.w2.rows, e.w2.cols, e.w2.scale_rows,
+                       e.w2.scale_cols, 0, e.w2.rows, h1, tokens, inter, y, ldy, 64, addend,
+                       stream);
+}
+
+// the shape checks of compute_deepseek_fp8_shared_expert_into_hidden
+wh_status fp8_expert_check(const wh_fp8_expert& e, size_t hidden) {
+  if ((size_t)e.w1.cols != hidden || (size_t)e.w3.cols != hidden)
+    return fail(WH_ERR_INVALID_SHAPE, "DeepSeek shared expert input dim");
+  if (e.w1.rows != e.w3.rows || e.w2.cols != e.w1.rows)
+    return fail(WH_ERR_INVALID_SHAPE, "DeepSeek shared expert projection shape");
+  return WH_OK;
+}
+}  // namespace
+
+extern "C" {
+
+wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows, int cols,
+                      int scale_rows, int scale_cols, int row_start, int row_end, const float* x,
+                      int batch, int ldx, float* y, int ldy, int act_quant_block,
+                      wh_stream_t stream) {
+  return fp8_gemv_impl(c, weight, scale, rows, cols, scale_rows, scale_cols, row_start, row_end,
+                       x, batch, ldx, y, ldy, act_quant_block, nullptr, stream);
+}
+
+size_t wh_fp8_expert_scratch_len(size_t hidden, size_t intermediate) {
+  return hidden + 2 * intermediate;
+}
+
+wh_status wh_fp8_expert_forward(wh_ctx* c, const wh_fp8_expert* e, const float* input,
+                                size_t input_len, float* output, size_t output_len,
+                                float* scratch, size_t scratch_len, wh_stream_t stream) {
+  if (!c || !e) return fail(WH_ERR_INVALID_POINTER, "null ctx/expert");
+  wh_status st;
+  if ((st = fp8_expert_check(*e, input_len)) != WH_OK) return st;
+  if ((size_t)e->w2.rows > output_len)
+    return fail(WH_ERR_OUTPUT_TOO_SMALL, "output too small: required=" +
+                                             std::to_string(e->w2.rows) +
+                                             ", actual=" + std::to_string(output_len));
+  const size_t inter = (size_t)e->w1.rows;
+  if (scratch_len < wh_fp8_expert_scratch_len(input_len, inter))
+    return fail(WH_ERR_SCRATCH_TOO_SMALL, "scratch too small");
+  if (!input || !output || !scratch) return fail(WH_ERR_INVALID_POINTER, "null buffer");
+  return fp8_expert_run(c, *e, input, 1, (int)input_len, output, (int)output_len, nullptr,
+                        scratch, scratch + inter, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -737,6 +809,17 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
   if (d->topk > d->num_experts || d->topk > 7 || d->num_experts > 1024)
     return fail(WH_ERR_UNSUPPORTED, "topk must be <= 7 (8 slots with the shared expert)");
   if (!d->experts) return fail(WH_ERR_INVALID_POINTER, "experts");
+  if (d->shared && d->shared_fp8)
+    return fail(WH_ERR_INVALID_SHAPE, "at most one shared expert (FP4 or FP8)");
+  if (d->shared_fp8) {
+    wh_status sst = fp8_expert_check(*d->shared_fp8, (size_t)d->hidden);
+    if (sst != WH_OK) return sst;
+    if (d->shared_fp8->w2.rows != d->hidden)
+      return fail(WH_ERR_INVALID_SHAPE, "FP8 shared expert output rows != hidden");
+    if (!d->shared_fp8->w1.weight || !d->shared_fp8->w3.weight || !d->shared_fp8->w2.weight ||
+        !d->shared_fp8->w1.scale || !d->shared_fp8->w3.scale || !d->shared_fp8->w2.scale)
+      return fail(WH_ERR_INVALID_POINTER, "FP8 shared expert weights");
+  }
   if (d->router_mode != WH_ROUTER_RAW_LOGITS && d->router_mode != WH_ROUTER_SQRT_SOFTPLUS)
     return fail(WH_ERR_INVALID_SHAPE, "router mode");
   const int n = d->num_experts + (d->shared ? 1 : 0);
@@ -761,6 +844,11 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
   p->d = *d;
   p->d.experts = nullptr;
   p->d.shared = nullptr;
+  p->d.shared_fp8 = nullptr;
+  if (d->shared_fp8) {
+    p->has_sfp8 = true;
+    p->sfp8 = *d->shared_fp8;
+  }
   wh_status st = build_expert_set(all.data(), n, &p->set);
   if (st != WH_OK) {
     free_expert_set(p->set);
@@ -919,8 +1007,10 @@ size_t moe_path_scratch_bytes(const wh_moe_plan* p, int tokens) {
 
 size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
   if (!p || tokens <= 0) return 0;
-  return align256(moe_path_scratch_bytes(p, tokens)) +
-         align256(sizeof(float) * (size_t)tokens * p->d.hidden);
+  size_t n = align256(moe_path_scratch_bytes(p, tokens)) +
+             align256(sizeof(float) * (size_t)tokens * p->d.hidden);
+  if (p->has_sfp8) n += 2 * align256(sizeof(float) * (size_t)tokens * p->d.inter);
+  return n;
 }
 
 // Batched path (tokens >= kGroupedMinTokens): router, routing bookkeeping and
@@ -1009,9 +1099,31 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   return c->prof_mark(stream);
 }
 
+static wh_status moe_ffn_routed(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
+                                const int32_t* hash_ids, float* y, int32_t* ids_out,
+                                float* weights_out, void* scratch, size_t scratch_bytes,
+                                wh_stream_t stream);
+
 wh_status wh_moe_ffn(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
                      const int32_t* hash_ids, float* y, int32_t* ids_out, float* weights_out,
                      void* scratch, size_t scratch_bytes, wh_stream_t stream) {
+  wh_status st = moe_ffn_routed(c, p, x, tokens, hash_ids, y, ids_out, weights_out, scratch,
+                                scratch_bytes, stream);
+  if (st != WH_OK || !p->has_sfp8) return st;
+  // y = shared(x) + routed (src/compute.rs:1940-1944): the FP8 shared expert's
+  // w2 GEMV adds the routed result in its epilogue
+  uint8_t* base = static_cast<uint8_t*>(scratch) + align256(moe_path_scratch_bytes(p, tokens));
+  const float* xd = device_reach(x) == 1 ? reinterpret_cast<const float*>(base) : x;
+  base += align256(sizeof(float) * (size_t)tokens * p->d.hidden);
+  float* h1 = reinterpret_cast<float*>(base);
+  float* h3 = reinterpret_cast<float*>(base + align256(sizeof(float) * (size_t)tokens * p->d.inter));
+  return fp8_expert_run(c, p->sfp8, xd, tokens, p->d.hidden, y, p->d.hidden, y, h1, h3, stream);
+}
+
+static wh_status moe_ffn_routed(wh_ctx* c, const wh_moe_plan* p, const float* x, int tokens,
+                                const int32_t* hash_ids, float* y, int32_t* ids_out,
+                                float* weights_out, void* scratch, size_t scratch_bytes,
+                                wh_stream_t stream) {
   if (!c || !p) return fail(WH_ERR_INVALID_POINTER, "null ctx/plan");
   if (tokens <= 0) return fail(WH_ERR_EMPTY_SHAPE, "tokens <= 0");
   if (tokens > p->d.max_tokens) return fail(WH_ERR_INVALID_SHAPE, "tokens > plan max_tokens");
@@ -1176,6 +1288,8 @@ EpScratch ep_scratch_layout(const wh_moe_plan* p, int world, int tokens, int max
 }
 wh_status ep_check(const wh_moe_plan* p, int world) {
   if (!p) return fail(WH_ERR_INVALID_POINTER, "null plan");
+  if (p->has_sfp8)
+    return fail(WH_ERR_UNSUPPORTED, "expert parallelism takes an FP4 shared expert");
   if (world < 1 || world * p->d.num_experts > 1024)
     return fail(WH_ERR_UNSUPPORTED, "world * local experts must be in [1, 1024]");
   if (!p->grouped)

@@ -148,7 +148,8 @@ __global__ void fp8_gemv_generic_kernel(Fp8GemvArgs a) {
     const uint8_t* s = a.scale + (long long)(r / row_group) * a.scale_cols;
     float acc = fp8_row_dot_exact(w, s, a.scale_cols, col_group, a.x + (long long)b * a.ldx);
     if (!isfinite(acc)) flag(a.status, WH_DEV_NONFINITE);
-    a.y[(long long)b * a.ldy + (r - a.row_start)] = acc;
+    const long long o = (long long)b * a.ldy + (r - a.row_start);
+    a.y[o] = a.addend ? __fadd_rn(acc, a.addend[o]) : acc;
   }
   pdl_launch_dependents();
 }
@@ -358,7 +359,8 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
           tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xb);
           if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
         }
-        a.y[(long long)bi * a.ldy + (row - a.row_start)] = tot;
+        const long long o = (long long)bi * a.ldy + (row - a.row_start);
+        a.y[o] = a.addend ? __fadd_rn(tot, a.addend[o]) : tot;
       }
     }
   }
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(kRgThreads)
         tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs);
         if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
       }
-      a.y[row - a.row_start] = tot;
+      a.y[row - a.row_start] = a.addend ? __fadd_rn(tot, a.addend[row - a.row_start]) : tot;
     }
     pdl_launch_dependents();
     return;

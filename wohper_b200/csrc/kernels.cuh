@@ -54,6 +54,7 @@ struct Fp8GemvArgs {
   int act_quant_block;  // 0 or the block size of a fused act quant of x
   int box_rows;         // rows per CTA (fast path)
   uint32_t* status;
+  const float* addend;  // nullable, laid out like y: y = gemv + addend (after the finite check)
 };
 
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);
