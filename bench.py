@@ -242,7 +242,27 @@ def run_ours(args):
                                      W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
                                      W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
 
-    layer = W.MoeLayer(ctx, [wexp(e) for e in range(E)], wexp(E), gate, topk=TOPK,
+    # --shared fp8: DeepSeek-V4's layout, an FP8 E4M3 shared expert (UE8M0 per
+    # 128x128) run on the FP8 GEMV after the routed experts
+    fp8_shared = args.shared == "fp8"
+    if fp8_shared:
+        def f8(seed, r, c):
+            w, sc = H.fp8_weight(seed, r, c)
+            return W.Fp8Matrix(torch.from_numpy(w).to(dev), torch.from_numpy(sc).to(dev))
+
+        shared = W.DeepSeekV4Fp8Expert(f8(4001, INTER, HID), f8(4002, INTER, HID),
+                                       f8(4003, HID, INTER))
+        slots = TOPK
+        shared_bytes = 3 * INTER * HID + 3 * (INTER // 128) * (HID // 128)
+    else:
+        shared = wexp(E)
+        slots = SLOTS
+        shared_bytes = EXPERT_BYTES
+    up_bytes = slots * 2 * (PACKED_W13 + SCALES_W13)
+    down_bytes = slots * (PACKED_W2 + SCALES_W2)
+    step_bytes = TOPK * EXPERT_BYTES + shared_bytes + ROUTER_BYTES + 2 * HID * 4
+    up_traffic = UP_TRAFFIC if not fp8_shared else int(UP_TRAFFIC * slots / SLOTS)
+    layer = W.MoeLayer(ctx, [wexp(e) for e in range(E)], shared, gate, topk=TOPK,
                        router_mode=W.ROUTER_RAW_LOGITS, max_tokens=1)
     n_tok = args.warmup + args.steps
     xs = torch.from_numpy(H.activations(2000 + rank, n_tok, HID)).to(dev)
@@ -338,7 +358,7 @@ def run_ours(args):
     down_ms = float(ph3[:, 2].mean())
     router_ms = float(ph3[:, 0].mean())
     peak, peak_kind = peaks()
-    up_gbs = UP_BYTES / (up_ms * 1e-3) / 1e9
+    up_gbs = up_bytes / (up_ms * 1e-3) / 1e9
 
     # ---- end to end through the C ABI with host buffers ---------------------
     # wh_moe_ffn takes the token and the output as pinned host memory (the
@@ -386,12 +406,14 @@ def run_ours(args):
             "data": "synthetic (seeded random-init weights and N(0,1) tokens)",
             "config": {
                 "workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID, "inter": INTER,
-                "batch": 1, "shared_expert": "fp4",
+                "batch": 1,
+                "shared_expert": ("fp8 e4m3 x ue8m0-128x128 (DeepSeek-V4's layout), on the FP8 "
+                                  "GEMV after the routed experts" if fp8_shared else "fp4"),
                 "l2": "flushed between steps (256 MiB memset outside the timed events)",
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                "bytes_per_step": STEP_BYTES,
+                "bytes_per_step": step_bytes,
             },
-            "step_hbm_gbs": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
+            "step_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
             "phases_ms": {"router": round(router_ms, 5), "moe_up": round(up_ms, 5),
                           "moe_down": round(down_ms, 5)},
             "persistent_decode_kernel_ms": (round(fused_ab_ms, 5) if fused_ab_ms is not None
@@ -399,20 +421,22 @@ def run_ours(args):
             "roofline": ({
                 "kernel": "moe_decode_kernel (router + w1/w3 + SwiGLU + act quant + w2 + combine, "
                           "one persistent kernel)",
-                "bound": "hbm", "achieved": round(STEP_BYTES / (step_kernel_ms * 1e-3) / 1e9, 1),
+                "bound": "hbm", "achieved": round(step_bytes / (step_kernel_ms * 1e-3) / 1e9, 1),
                 "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": round(STEP_BYTES / (step_kernel_ms * 1e-3) / 1e9 / peak, 4),
-                "algorithmic_bytes": STEP_BYTES, "kernel_ms": round(step_kernel_ms, 5),
+                "frac": round(step_bytes / (step_kernel_ms * 1e-3) / 1e9 / peak, 4),
+                "algorithmic_bytes": step_bytes, "kernel_ms": round(step_kernel_ms, 5),
                 "traffic": STEP_TRAFFIC,
                 "traffic_source": STEP_TRAFFIC_SOURCE,
             } if fused else {
-                "kernel": "moe_up_kernel (w1+w3 FP4 matvecs of 7 experts + SwiGLU + act quant)",
+                "kernel": f"moe_up_kernel (w1+w3 FP4 matvecs of {slots} experts + SwiGLU + "
+                          "act quant)",
                 "bound": "hbm", "achieved": round(up_gbs, 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / peak, 4),
-                "algorithmic_bytes": UP_BYTES, "traffic": UP_TRAFFIC,
+                "algorithmic_bytes": up_bytes, "traffic": up_traffic,
                 "traffic_source": "ncu dram__bytes_read+write of one moe_up launch "
-                                  "(bench.py --ncu-case moe16: same 7 experts' w1/w3 per launch)",
-                "down_kernel_gbs": round(DOWN_BYTES / (down_ms * 1e-3) / 1e9, 1),
+                                  "(bench.py --ncu-case moe16: same 7 experts' w1/w3 per launch)"
+                                  + (", scaled by 6/7 slots" if fp8_shared else ""),
+                "down_kernel_gbs": round(down_bytes / (down_ms * 1e-3) / 1e9, 1),
             }),
             "e2e": {"value": round(world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                     "ms_per_step": round(e2e_ms, 6), "h2d_bytes_per_step": HID * 4,
@@ -420,7 +444,7 @@ def run_ours(args):
                     "path": "pinned host x -> wh_moe_ffn (C ABI; the device reads x and "
                             "writes y through the mapped host buffers)",
                     "matches_device_pointer_call": e2e_matches_device},
-            "gpu_launches": (1 if fused else 3) * args.steps,
+            "gpu_launches": ((1 if fused else 3) + (4 if fp8_shared else 0)) * args.steps,
             "timing": timing,
             "graph_output_matches_direct_call": graph_matches_direct,
             "clocks": clocks,
@@ -431,7 +455,8 @@ def run_ours(args):
         v, n, cores = cpu_run(steps=24, warmup=1, budget_s=20.0)
         result["cpu_baseline"] = {
             "value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{n} tokens of the same workload (router + 6 routed + shared expert), "
+            "sample": f"{n} tokens of the same workload (router + 6 routed + shared expert"
+                      + (", the shared expert in FP4" if fp8_shared else "") + "), "
                       "C++ restatement of the reference's AVX2 kernels, reference threading "
                       "(nproc-2 threads)"}
     if world > 1:
@@ -1060,7 +1085,10 @@ METRIC_LM = "lm_head top-k tokens/s (BF16 129280 x 4096 logits + top-k)"
 WORKLOAD_LM = ("lm_head top-k: every logit of the BF16 lm_head of DeepSeek-V3/V4 shape "
                "(129280 x 4096, 1.06 GB) in the reference's dot_bf16_row order, then the "
                "top-k push_topk_candidate keeps, sorted; one hidden vector per step")
-LM_TRAFFIC_RATIO = None  # DRAM bytes / algorithmic bytes of lm_logits_kernel (ncu, lmhead case)
+# DRAM bytes / algorithmic bytes of lm_logits_kernel from the ncu capture of the lmhead case
+# (32768 rows: 268,467,200 read + 3,915,264 written / 268,582,912; profiles/lm_logits_lmhead.md),
+# scaled to the full launch by rows
+LM_TRAFFIC_RATIO = 272_382_464 / 268_582_912
 
 
 def lm_head_cpu(w_np, xs, k, steps):
@@ -1298,6 +1326,9 @@ def main():
     ap.add_argument("--direct-io", action="store_true",
                     help="expert-load: O_DIRECT reads (bypass the page cache)")
     ap.add_argument("--lm-top-k", type=int, default=50, help="lm-head: top_k")
+    ap.add_argument("--shared", default="fp4", choices=["fp4", "fp8"],
+                    help="config 2: the shared expert's format (fp4, as BASELINE's config 2; "
+                         "fp8: DeepSeek-V4's FP8 shared expert)")
     ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
