@@ -1225,6 +1225,153 @@ def run_lm_head(args):
     return res
 
 
+# dram bytes per launch from an ncu capture of --ncu-case mla (None until measured)
+MLA_TRAFFIC = None
+METRIC_MLA = "MLA attention-core calls/s (one decode token, one DeepSeek-V4 layer, 64 heads)"
+MLA_HEADS, MLA_HD, MLA_NOPE, MLA_POS, MLA_COMP = 64, 512, 448, 4095, 1024
+WORKLOAD_MLA = ("MLA attention core of DeepSeek-V4-Flash (64 heads x 512 = 448 nope + 64 rope), "
+                "ratio-4 layer at token 4095: 128-row sliding window + 1024 compressed rows, "
+                "attention sink, YaRN inverse RoPE")
+
+
+def mla_inputs(dev, seed):
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    q = torch.randn(MLA_HEADS, MLA_HD, device=dev, generator=g) * 0.05
+    keys = torch.randn(MLA_POS + 1, MLA_HD, device=dev, generator=g)
+    comp = torch.randn(MLA_COMP, MLA_HD, device=dev, generator=g)
+    sink = torch.randn(MLA_HEADS, device=dev, generator=g)
+    return q, keys, comp, sink
+
+
+def mla_cpu(q, keys, comp, sink, fr, steps):
+    """The oracle's scalar restatement on one host thread: seconds per call."""
+    import oracle as O
+
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.mla_attention(q, keys, MLA_POS, 128, comp, sink, fr, MLA_NOPE)
+    return (time.perf_counter() - t0) / steps
+
+
+def run_mla(args):
+    import torch
+
+    import wohper_b200 as W
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    q, keys, comp, sink = mla_inputs(dev, 800 + rank)
+    theta, yarn = W.deepseek_rope_for_layer(2)
+    fr = W.rope_inv_freqs(MLA_HD - MLA_NOPE, theta, yarn)
+    cfg = {"workload": WORKLOAD_MLA, "heads": MLA_HEADS, "head_dim": MLA_HD,
+           "token_pos": MLA_POS, "window": 128, "compressed_rows": MLA_COMP,
+           "l2": "flushed between calls (256 MiB memset outside the timed events)",
+           "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+    if args.impl == "reference":
+        res = None
+        if rank == 0:
+            host = [t.cpu().numpy() for t in (q, keys, comp, sink)]
+            sec = mla_cpu(*host, fr, max(args.steps, 1))
+            v = 1.0 / sec
+            res = {"metric": METRIC_MLA, "value": round(v, 2), "unit": "calls/s",
+                   "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                   "higher_is_better": True, "impl": "reference", "scaling": "weak",
+                   "vs_baseline": None, "dtype": "f32", "data": "synthetic (N(0, 1) cache rows)",
+                   "config": cfg,
+                   "cpu_baseline": {"value": round(v, 2), "unit": "calls/s", "cores": 1,
+                                    "kind": "port", "sample": f"{max(args.steps, 1)} full calls"},
+                   "e2e": {"value": round(v, 2), "unit": "calls/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}}
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return res
+
+    ctx = W.Context(local)
+    out = torch.empty(MLA_HEADS, MLA_HD, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def call(qd):
+        W.mla_attention(ctx, qd, keys, MLA_POS, fr, MLA_NOPE, compressed=comp, sink=sink,
+                        out=out)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(q)
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            call(q)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    # end to end: the query from pinned host memory, the output back to it
+    qh = q.cpu().pin_memory()
+    qd = torch.empty_like(q)
+    oh = torch.empty(MLA_HEADS, MLA_HD).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        ev2[i][0].record(stream)
+        qd.copy_(qh, non_blocking=True)
+        call(qd)
+        oh.copy_(out, non_blocking=True)
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    peak, peak_kind = peaks()
+    rows = 128 + MLA_COMP
+    alg = rows * MLA_HD * 4 + 2 * MLA_HEADS * MLA_HD * 4 + MLA_HEADS * 4
+    achieved = alg / (ms_step * 1e-3) / 1e9
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC_MLA, "value": round(world * 1e3 / ms_step, 2), "unit": "calls/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (reference operation order, no FMA)",
+            "data": "synthetic (N(0, 1) cache rows, N(0, 0.05) queries)", "config": cfg,
+            "roofline": {"kernel": "mla_scores_kernel + mla_output_kernel", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "algorithmic_bytes": alg, "traffic": MLA_TRAFFIC,
+                         "note": "latency-bound: the reference's in-order sums are "
+                                 f"dependent chains of {MLA_HD} (scores) and {rows} "
+                                 "(weighted sum) additions"},
+            "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "calls/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
+                    "d2h_bytes_per_step": out.numel() * 4,
+                    "path": "pinned host q -> H2D -> wh_mla_attention (C ABI) -> D2H output"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            host = [t.cpu().numpy() for t in (q, keys, comp, sink)]
+            sec = mla_cpu(*host, fr, 3)
+            res["cpu_baseline"] = {"value": round(1.0 / sec, 2), "unit": "calls/s", "cores": 1,
+                                   "kind": "port",
+                                   "sample": "3 full calls of the oracle's scalar restatement"}
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res
+
+
 def run_ncu_case(args):
     """Small single-GPU workloads for ncu captures (no JSON bench line).
 
@@ -1237,6 +1384,7 @@ def run_ncu_case(args):
            and down GEMMs, combine per step.
     lmhead: the BF16 lm_head top-50 on 32768 x 4096 (268 MB of weights),
            logits + candidates + selection per step.
+    mla:   the MLA attention core at the bench's shape (10 MB of cache rows).
     L2 is flushed (256 MiB memset) before every step."""
     import torch
 
@@ -1246,7 +1394,14 @@ def run_ncu_case(args):
     ctx = W.Context(0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     n = args.warmup + args.steps
-    if args.ncu_case == "lmhead":
+    if args.ncu_case == "mla":
+        q, keys, comp, sink = mla_inputs(torch.device("cuda", 0), 5)
+        theta, yarn = W.deepseek_rope_for_layer(2)
+        fr = W.rope_inv_freqs(MLA_HD - MLA_NOPE, theta, yarn)
+        for _ in range(n):
+            flush.zero_()
+            W.mla_attention(ctx, q, keys, MLA_POS, fr, MLA_NOPE, compressed=comp, sink=sink)
+    elif args.ncu_case == "lmhead":
         g = torch.Generator(device="cuda")
         g.manual_seed(3)
         wl = (torch.randn(32768, HID, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
@@ -1317,10 +1472,11 @@ def main():
                          "4: expert-parallel layer over the ranks")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="config 4: rows over NVLink peer stores (p2p) or NCCL all-to-all")
-    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head", "mla"],
                     help="moe: the MoE FFN step of --config (default); expert-load: one "
                          "layer's FP4 experts from an experts pack on disk into HBM; lm-head: "
-                         "the BF16 lm_head top-k over the DeepSeek vocabulary")
+                         "the BF16 lm_head top-k over the DeepSeek vocabulary; mla: the MLA "
+                         "attention core of one DeepSeek-V4 layer at token 4095")
     ap.add_argument("--load-threads", type=int, default=8,
                     help="expert-load: reader threads of the expert loader")
     ap.add_argument("--direct-io", action="store_true",
@@ -1329,7 +1485,7 @@ def main():
     ap.add_argument("--shared", default="fp4", choices=["fp4", "fp8"],
                     help="config 2: the shared expert's format (fp4, as BASELINE's config 2; "
                          "fp8: DeepSeek-V4's FP8 shared expert)")
-    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead"],
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead", "mla"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
     if args.ncu_case:
@@ -1340,6 +1496,8 @@ def main():
         res = run_expert_load(args)
     elif args.workload == "lm-head":
         res = run_lm_head(args)
+    elif args.workload == "mla":
+        res = run_mla(args)
     elif args.config == 3 and args.impl == "ours":
         res = run_config3(args)
     elif args.config == 4 and args.impl == "ours":

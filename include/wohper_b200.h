@@ -359,6 +359,36 @@ wh_status wh_ep_p2p_combine(wh_ctx* ctx, wh_ep_window* window, const int32_t* id
                             const float* y_shared, float* y, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* MLA attention (DeepSeek-V4 decode)                                          */
+/* ------------------------------------------------------------------------ */
+/* Replaces rope_inv_freqs (src/compute.rs:2591-2621) on the host: inv_freqs
+ * [rope_dim/2].  yarn_factor <= 0 or original_seq_len == 0: plain RoPE. */
+void wh_rope_inv_freqs(int rope_dim, float theta, float yarn_factor, float yarn_beta_fast,
+                       float yarn_beta_slow, uint64_t yarn_original_seq_len, float* inv_freqs);
+/* The attention core of compute_deepseek_v4_mla_attention (src/compute.rs:4080-4185),
+ * bit-exact: scores q.k * head_dim^-0.5 over the sliding window
+ * [max(0, token_pos + 1 - window), token_pos] of the layer's key cache and over
+ * the compressed rows, softmax with the optional sink, the in-order weighted
+ * sum of the keys (the values are the keys), division by the denominator and
+ * the inverse RoPE of the rope part [nope_dim, head_dim).
+ *   q [heads][head_dim]; keys: cache rows 0..token_pos, row stride key_stride;
+ *   compressed [compressed_count][head_dim] (nullable when 0); sink [heads]
+ *   (nullable); inv_freqs: HOST array [(head_dim - nope_dim)/2], the layer's
+ *   rope_inv_freqs; out [heads][head_dim].  Device pointers otherwise.
+ * The cos/sin of token_pos * inv_freq are computed on the host with the C
+ * library, like the reference's f32::sin_cos; exp is the host C library's expf,
+ * reproduced on the device through a table measured at first use (about 3 s of
+ * host time once per process).  The scores live in a context-owned workspace:
+ * calls on one context are serialised by the caller (one stream at a time).
+ * Errors: InvalidShape (nope_dim > head_dim, odd rope part, key_stride <
+ * head_dim, window < 1), Unsupported (rope part > 128, odd nope_dim, more than
+ * 512 heads, or heads/head_dim/visible rows beyond shared memory). */
+wh_status wh_mla_attention(wh_ctx* ctx, const float* q, int heads, int head_dim, int nope_dim,
+                           const float* keys, int key_stride, int token_pos, int window,
+                           const float* compressed, int compressed_count, const float* sink,
+                           const float* inv_freqs, float* out, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* BF16 lm_head top-k                                                         */
 /* ------------------------------------------------------------------------ */
 /* Device scratch bytes wh_lm_head_topk needs. */
@@ -530,6 +560,13 @@ void wh_debug_act_quant_table(uint32_t out[256]);
 /* The E4M3 nearest-with-ties-to-lower rounding the kernels use (|t| <= 448). */
 float wh_debug_e4m3_round(float t);
 void wh_debug_e4m3_round_n(const float* in, float* out, size_t n); /* host arrays */
+/* The table that makes the device's exp equal the host C library's expf (built
+ * on first use by scanning expf over (-104, 89)): the number of entries, negated
+ * if some difference fell outside the device's midpoint gate. */
+int wh_debug_expf_table(const uint32_t** keys, const float** vals);
+/* y[i] = the host libm's expf(x[i]), evaluated on the device (device arrays). */
+wh_status wh_debug_ref_expf(wh_ctx* ctx, const float* x, float* y, size_t n,
+                            wh_stream_t stream);
 
 #ifdef __cplusplus
 }

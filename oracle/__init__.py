@@ -100,6 +100,12 @@ def lib() -> C.CDLL:
         L.orc_bf16_gemv.restype = i
         L.orc_lm_head_topk.argtypes = [vp, sz, sz, vp, sz, C.c_uint32, vp, vp, vp]
         L.orc_lm_head_topk.restype = i
+        L.orc_expf_n.argtypes = [vp, vp, sz]
+        L.orc_expf_n.restype = None
+        L.orc_rope_inv_freqs.argtypes = [sz, f, f, f, f, sz, vp]
+        L.orc_rope_inv_freqs.restype = None
+        L.orc_mla_attention.argtypes = [vp, sz, sz, sz, vp, sz, sz, sz, vp, sz, vp, vp, vp]
+        L.orc_mla_attention.restype = None
         L.orc_fp4_matvec.argtypes = [C.POINTER(Fp4Spec), vp, sz, vp, sz, i]
         L.orc_fp4_matvec.restype = i
         L.orc_fp4_expert_forward.argtypes = [C.POINTER(Fp4Expert), vp, sz, vp, sz, vp, sz]
@@ -222,6 +228,40 @@ def bf16_gemv(w_u16, x):
     y = np.zeros(w.shape[0], np.float32)
     st = lib().orc_bf16_gemv(_p(w), w.shape[0], w.shape[1], _p(x), _p(y))
     return st, y
+
+
+def expf(x):
+    """The host C library's expf, elementwise (Rust's f32::exp)."""
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_expf_n(_p(x), _p(y), x.size)
+    return y
+
+
+def rope_inv_freqs(rope_dim, theta, yarn=None):
+    """rope_inv_freqs (src/compute.rs:2591-2621); yarn = (factor, beta_fast,
+    beta_slow, original_seq_len) or None."""
+    out = np.zeros(rope_dim // 2, np.float32)
+    fa, bf, bs, osl = yarn if yarn else (0.0, 0.0, 0.0, 0)
+    lib().orc_rope_inv_freqs(rope_dim, theta, fa, bf, bs, osl, _p(out))
+    return out
+
+
+def mla_attention(q, keys, token_pos, window, compressed, sink, inv_freqs, nope_dim):
+    """The attention core of compute_deepseek_v4_mla_attention: q [heads, head_dim],
+    keys [positions, stride], compressed [count, head_dim] or None, sink [heads] or
+    None -> out [heads, head_dim]."""
+    q = _c(q, np.float32)
+    keys = _c(keys, np.float32)
+    heads, hd = q.shape
+    comp = None if compressed is None else _c(compressed, np.float32)
+    sk = None if sink is None else _c(sink, np.float32)
+    fr = _c(inv_freqs, np.float32)
+    out = np.zeros((heads, hd), np.float32)
+    lib().orc_mla_attention(_p(q), heads, hd, nope_dim, _p(keys), keys.shape[1], token_pos,
+                            window, _p(comp), 0 if comp is None else comp.shape[0], _p(sk),
+                            _p(fr), _p(out))
+    return out
 
 
 def lm_head_topk(w_u16, x, top_k, row_base=0):

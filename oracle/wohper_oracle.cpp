@@ -828,6 +828,98 @@ size_t orc_deepseek_sqrtsoftplus_route(const float* logits, size_t n, const floa
   return k;
 }
 
+void orc_expf_n(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
+}
+
+// rope_inv_freqs (src/compute.rs:2591-2621)
+void orc_rope_inv_freqs(size_t rope_dim, float theta, float yarn_factor, float beta_fast,
+                        float beta_slow, size_t original_seq_len, float* out) {
+  size_t pairs = rope_dim / 2;
+  for (size_t pair = 0; pair < pairs; ++pair)
+    out[pair] = powf(theta, -((float)(2 * pair)) / (float)rope_dim);
+  if (yarn_factor <= 0.0f || original_seq_len == 0) return;
+  float dim = (float)rope_dim;
+  float base_ln = logf(theta);
+  const float PI = 3.14159265358979323846f;  // std::f32::consts::PI
+  auto find_correction_dim = [&](float num_rotations) {
+    return dim * logf((float)original_seq_len / (num_rotations * 2.0f * PI)) / (2.0f * base_ln);
+  };
+  float low = std::fmax(floorf(find_correction_dim(beta_fast)), 0.0f);
+  float high = std::fmin(ceilf(find_correction_dim(beta_slow)), dim - 1.0f);
+  if (std::fabs(low - high) < 1.1920929e-07f) high = low + 0.001f;
+  for (size_t pair = 0; pair < pairs; ++pair) {
+    float ramp = (((float)pair) - low) / (high - low);
+    ramp = ramp < 0.0f ? 0.0f : (ramp > 1.0f ? 1.0f : ramp);  // clamp(0.0, 1.0): NaN stays
+    float smooth = 1.0f - ramp;
+    out[pair] = out[pair] / yarn_factor * (1.0f - smooth) + out[pair] * smooth;
+  }
+}
+
+// apply_rope_interleaved_with_freqs (src/compute.rs:2623-2651)
+static void rope_pairs(float* values, size_t position, const float* inv_freqs, size_t pairs,
+                       bool inverse) {
+  float pos = (float)position;
+  for (size_t pair = 0; pair < pairs; ++pair) {
+    float angle = pos * inv_freqs[pair];
+    float s = sinf(angle), c = cosf(angle);
+    if (inverse) s = -s;
+    float even = values[2 * pair], odd = values[2 * pair + 1];
+    values[2 * pair] = even * c - odd * s;
+    values[2 * pair + 1] = even * s + odd * c;
+  }
+}
+
+// the attention core of compute_deepseek_v4_mla_attention (src/compute.rs:4080-4185)
+void orc_mla_attention(const float* q, size_t heads, size_t head_dim, size_t nope_dim,
+                       const float* keys, size_t key_stride, size_t token_pos, size_t window,
+                       const float* compressed, size_t compressed_count, const float* sink,
+                       const float* inv_freqs, float* out) {
+  const float scale = powf((float)head_dim, -0.5f);
+  size_t context = token_pos + 1;
+  size_t window_start = context > window ? context - window : 0;
+  for (size_t i = 0; i < heads * head_dim; ++i) out[i] = 0.0f;
+  auto dot = [&](const float* a, const float* b) {
+    float score = 0.0f;
+    for (size_t d = 0; d < head_dim; ++d) score += a[d] * b[d];
+    return score;
+  };
+  for (size_t head = 0; head < heads; ++head) {
+    const float* qh = q + head * head_dim;
+    float max_score = -INFINITY;
+    for (size_t pos = window_start; pos < context; ++pos) {
+      float score = dot(qh, keys + pos * key_stride) * scale;
+      if (score > max_score) max_score = score;
+    }
+    for (size_t b = 0; b < compressed_count; ++b) {
+      float score = dot(qh, compressed + b * head_dim) * scale;
+      if (score > max_score) max_score = score;
+    }
+    float denom = 0.0f;
+    if (sink) denom += expf(sink[head] - max_score);
+    float* oh = out + head * head_dim;
+    float weights_sum = 0.0f;
+    for (size_t pos = window_start; pos < context; ++pos) {
+      const float* key = keys + pos * key_stride;
+      float score = dot(qh, key);
+      float weight = expf((score * scale) - max_score);
+      weights_sum += weight;
+      for (size_t d = 0; d < head_dim; ++d) oh[d] += weight * key[d];
+    }
+    for (size_t b = 0; b < compressed_count; ++b) {
+      const float* key = compressed + b * head_dim;
+      float score = dot(qh, key);
+      float weight = expf((score * scale) - max_score);
+      weights_sum += weight;
+      for (size_t d = 0; d < head_dim; ++d) oh[d] += weight * key[d];
+    }
+    denom += weights_sum;
+    if (denom > 0.0f)
+      for (size_t d = 0; d < head_dim; ++d) oh[d] /= denom;
+    rope_pairs(oh + nope_dim, token_pos, inv_freqs, (head_dim - nope_dim) / 2, true);
+  }
+}
+
 // score_bf16_lm_head_topk + push_topk_candidate + the final sort
 // (src/compute.rs:2838-2962)
 int orc_lm_head_topk(const uint16_t* weight, size_t rows, size_t cols, const float* x,

@@ -73,7 +73,8 @@ EXPORTS = (
     "wh_model_get_layer", "wh_model_get_expert", "wh_model_expert_source",
     "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
     "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
-    "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward",
+    "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward", "wh_rope_inv_freqs",
+    "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf",
 )
 
 
@@ -170,6 +171,10 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_ctx_set_profiling": (st, [vp, i]),
         "wh_ctx_phase_times": (i, [vp, vp, i]),
         "wh_lm_head_scratch_bytes": (sz, [C.c_longlong, i]),
+        "wh_rope_inv_freqs": (None, [i, f, f, f, f, C.c_uint64, vp]),
+        "wh_debug_expf_table": (i, [C.POINTER(vp), C.POINTER(vp)]),
+        "wh_debug_ref_expf": (st, [vp, vp, vp, sz, vp]),
+        "wh_mla_attention": (st, [vp, vp, i, i, i, vp, i, i, i, vp, i, vp, vp, vp, vp]),
         "wh_fp8_expert_scratch_len": (sz, [sz, sz]),
         "wh_fp8_expert_forward": (st, [vp, C.POINTER(Fp8ExpertSpec), vp, sz, vp, sz, vp, sz,
                                        vp]),
@@ -439,6 +444,59 @@ def lm_head_topk_score(ctx: Context, weight_bf16, x, top_k: int, row_base: int =
                                  x.numel(), k, _ptr(toks), _ptr(vals), _ptr(logits),
                                  _ptr(scratch), scratch.numel(), _stream(stream)))
     return toks[:n], vals[:n]
+
+
+# DeepSeek-V4's attention constants (src/compute.rs DEEPSEEK_V4_YARN,
+# DEEPSEEK_V4_COMPRESS_ROPE_THETA, DEEPSEEK_V4_SLIDING_WINDOW_SIZE)
+DEEPSEEK_V4_YARN = (16.0, 32.0, 1.0, 65536)
+DEEPSEEK_V4_COMPRESS_ROPE_THETA = 160000.0
+DEEPSEEK_V4_ROPE_THETA = 10000.0
+DEEPSEEK_V4_SLIDING_WINDOW = 128
+# DEEPSEEK_V4_COMPRESS_RATIOS (src/compute.rs:2551-2554): per physical layer
+DEEPSEEK_V4_COMPRESS_RATIOS = (0, 0) + (4, 128) * 20 + (4, 0)
+
+
+def deepseek_rope_for_layer(layer: int):
+    """deepseek_rope_for_layer (src/compute.rs:2575-2585): (theta, yarn or None)."""
+    ratio = DEEPSEEK_V4_COMPRESS_RATIOS[layer] if 0 <= layer < len(DEEPSEEK_V4_COMPRESS_RATIOS) else 0
+    if ratio > 0:
+        return DEEPSEEK_V4_COMPRESS_ROPE_THETA, DEEPSEEK_V4_YARN
+    return DEEPSEEK_V4_ROPE_THETA, None
+
+
+def rope_inv_freqs(rope_dim: int, theta: float, yarn=None):
+    """rope_inv_freqs (src/compute.rs:2591-2621): per-pair inverse frequencies,
+    YaRN-blended when yarn = (factor, beta_fast, beta_slow, original_seq_len)."""
+    import numpy as np
+
+    out = np.zeros(rope_dim // 2, np.float32)
+    fa, bf, bs, osl = yarn if yarn else (0.0, 0.0, 0.0, 0)
+    lib().wh_rope_inv_freqs(rope_dim, theta, fa, bf, bs, osl, out.ctypes.data)
+    return out
+
+
+def mla_attention(ctx: Context, q, keys, token_pos: int, inv_freqs, nope_dim: int,
+                  window: int = DEEPSEEK_V4_SLIDING_WINDOW, compressed=None, sink=None,
+                  out=None, stream=None):
+    """The attention core of compute_deepseek_v4_mla_attention
+    (src/compute.rs:4080-4185) on the device, bit-exact: q [heads, head_dim] f32,
+    keys [positions > token_pos, key_stride] f32 (the layer's latent KV cache rows;
+    key and value are the same row), compressed [count, head_dim] f32 or None,
+    sink [heads] f32 or None, inv_freqs: the layer's rope_inv_freqs (host array).
+    Returns out [heads, head_dim]."""
+    import numpy as np
+    import torch
+
+    heads, head_dim = q.shape
+    if out is None:
+        out = torch.empty(heads, head_dim, dtype=torch.float32, device=q.device)
+    fr = np.ascontiguousarray(inv_freqs, dtype=np.float32)
+    cc = 0 if compressed is None else compressed.shape[0]
+    _check(lib().wh_mla_attention(ctx.handle, _ptr(q), heads, head_dim, nope_dim, _ptr(keys),
+                                  keys.stride(0), token_pos, window, _ptr(compressed), cc,
+                                  _ptr(sink), fr.ctypes.data if fr.size else None, _ptr(out),
+                                  _stream(stream)))
+    return out
 
 
 class MoeLayer:

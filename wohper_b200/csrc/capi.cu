@@ -299,6 +299,34 @@ struct wh_ctx {
     return WH_OK;
   }
 
+  void* mla_work = nullptr;  // MLA scores and tile maxima
+  size_t mla_work_bytes = 0;
+  wh_status ensure_mla_work(size_t bytes) {
+    if (bytes <= mla_work_bytes) return WH_OK;
+    if (mla_work) cudaFree(mla_work);
+    mla_work = nullptr;
+    mla_work_bytes = 0;
+    WH_CUDA(cudaMalloc(&mla_work, bytes));
+    mla_work_bytes = bytes;
+    return WH_OK;
+  }
+  ExpfTable expf{nullptr, nullptr, 0};  // device copy of the host expf table
+  void* expf_mem = nullptr;
+  wh_status ensure_expf_table() {
+    if (expf_mem) return WH_OK;
+    const uint32_t* keys;
+    const float* vals;
+    int n;
+    if (!expf_table_host(&keys, &vals, &n))
+      return fail(WH_ERR_UNSUPPORTED, "host expf differs outside the device's midpoint gate");
+    const size_t kb = sizeof(uint32_t) * (size_t)n, vb = sizeof(float) * (size_t)n;
+    WH_CUDA(cudaMalloc(&expf_mem, kb + vb + 16));
+    WH_CUDA(cudaMemcpy(expf_mem, keys, kb, cudaMemcpyHostToDevice));
+    WH_CUDA(cudaMemcpy((char*)expf_mem + kb, vals, vb, cudaMemcpyHostToDevice));
+    expf = ExpfTable{(const uint32_t*)expf_mem, (const float*)((char*)expf_mem + kb), n};
+    return WH_OK;
+  }
+
   wh_status ensure_work(size_t bytes) {
     if (bytes <= work_bytes) return WH_OK;
     if (work) cudaFree(work);
@@ -388,6 +416,8 @@ void wh_ctx_destroy(wh_ctx* c) {
   if (c->counters) cudaFree(c->counters);
   if (c->blk_counters) cudaFree(c->blk_counters);
   if (c->work) cudaFree(c->work);
+  if (c->expf_mem) cudaFree(c->expf_mem);
+  if (c->mla_work) cudaFree(c->mla_work);
   delete c;
 }
 
@@ -738,6 +768,87 @@ wh_status wh_router_topk(wh_ctx* c, const uint16_t* gate, int experts, int hidde
   a.counters = c->counters;
   a.status = c->status;
   WH_CUDA(launch_router_ex(a, nullptr, nullptr, stream, false));
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// rope_inv_freqs (src/compute.rs:2591-2621), operation for operation in f32
+void wh_rope_inv_freqs(int rope_dim, float theta, float yarn_factor, float yarn_beta_fast,
+                       float yarn_beta_slow, uint64_t yarn_original_seq_len, float* inv_freqs) {
+  if (!inv_freqs || rope_dim < 2) return;
+  const int pairs = rope_dim / 2;
+  for (int p = 0; p < pairs; ++p)
+    inv_freqs[p] = powf(theta, -(float)(2 * p) / (float)rope_dim);
+  if (yarn_factor <= 0.0f || yarn_original_seq_len == 0) return;
+  const float dim = (float)rope_dim;
+  const float base_ln = logf(theta);
+  const float pi = 3.14159265358979323846f;
+  auto correction_dim = [&](float rotations) {
+    return dim * logf((float)yarn_original_seq_len / (rotations * 2.0f * pi)) /
+           (2.0f * base_ln);
+  };
+  const float low = fmaxf(floorf(correction_dim(yarn_beta_fast)), 0.0f);
+  float high = fminf(ceilf(correction_dim(yarn_beta_slow)), dim - 1.0f);
+  if (fabsf(low - high) < 1.1920929e-07f) high = low + 0.001f;
+  for (int p = 0; p < pairs; ++p) {
+    float ramp = ((float)p - low) / (high - low);
+    ramp = ramp < 0.0f ? 0.0f : (ramp > 1.0f ? 1.0f : ramp);
+    const float smooth = 1.0f - ramp;
+    inv_freqs[p] = inv_freqs[p] / yarn_factor * (1.0f - smooth) + inv_freqs[p] * smooth;
+  }
+}
+
+wh_status wh_mla_attention(wh_ctx* c, const float* q, int heads, int head_dim, int nope_dim,
+                           const float* keys, int key_stride, int token_pos, int window,
+                           const float* compressed, int compressed_count, const float* sink,
+                           const float* inv_freqs, float* out, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  if (heads < 1 || head_dim < 1 || nope_dim < 0 || nope_dim > head_dim ||
+      (head_dim - nope_dim) % 2 != 0 || key_stride < head_dim || token_pos < 0 || window < 1 ||
+      compressed_count < 0)
+    return fail(WH_ERR_INVALID_SHAPE, "MLA attention shape");
+  const int pairs = (head_dim - nope_dim) / 2;
+  if (pairs > 64) return fail(WH_ERR_UNSUPPORTED, "rope dim > 128");
+  if (pairs > 0 && nope_dim % 2 != 0) return fail(WH_ERR_UNSUPPORTED, "odd nope_dim");
+  if (!q || !keys || !out || (compressed_count > 0 && !compressed) || (pairs > 0 && !inv_freqs))
+    return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  MlaArgs a{};
+  a.q = q;
+  a.keys = keys;
+  a.compressed = compressed;
+  a.sink = sink;
+  a.out = out;
+  a.heads = heads;
+  a.head_dim = head_dim;
+  a.nope_dim = nope_dim;
+  a.key_stride = key_stride;
+  const int context = token_pos + 1;
+  a.window_start = context > window ? context - window : 0;  // saturating_sub
+  a.window_len = context - a.window_start;
+  a.compressed_count = compressed_count;
+  size_t smem_scores = 0, smem_output = 0;
+  if (!mla_plan(a, &smem_scores, &smem_output))
+    return fail(WH_ERR_UNSUPPORTED, "heads, head_dim or visible rows do not fit shared memory");
+  auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  a.vec4 = head_dim % 4 == 0 && key_stride % 4 == 0 && al16(q) && al16(keys) &&
+           (compressed_count == 0 || al16(compressed));
+  a.scale = powf((float)head_dim, -0.5f);  // (head_dim as f32).powf(-0.5)
+  cudaSetDevice(c->device);
+  if (wh_status st = c->ensure_expf_table()) return st;
+  a.expf = c->expf;
+  const int positions = a.window_len + compressed_count;
+  if (wh_status st = c->ensure_mla_work(mla_scratch_bytes(heads, positions, a.tile_pos))) return st;
+  a.scores = (float*)c->mla_work;
+  a.weights = a.scores + (size_t)positions * heads;
+  a.tile_max = a.weights + (size_t)positions * heads;
+  a.head_max = a.tile_max + (size_t)((positions + a.tile_pos - 1) / a.tile_pos) * heads;
+  const float pos = (float)token_pos;
+  for (int i = 0; i < pairs; ++i) {
+    const float angle = pos * inv_freqs[i];
+    a.rope_sin[i] = sinf(angle);
+    a.rope_cos[i] = cosf(angle);
+  }
+  WH_CUDA(launch_mla_attention(a, smem_scores, smem_output, (cudaStream_t)stream));
   return WH_OK;
 }
 
@@ -1229,6 +1340,21 @@ float wh_debug_e4m3_round(float t) { return e4m3_nearest_ties_lower(t); }
 
 void wh_debug_e4m3_round_n(const float* in, float* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = e4m3_nearest_ties_lower(in[i]);
+}
+
+int wh_debug_expf_table(const uint32_t** keys, const float** vals) {
+  int n = 0;
+  const bool ok = expf_table_host(keys, vals, &n);
+  return ok ? n : -n;
+}
+
+wh_status wh_debug_ref_expf(wh_ctx* c, const float* x, float* y, size_t n, wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  if (n > 0 && (!x || !y)) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  cudaSetDevice(c->device);
+  if (wh_status st = c->ensure_expf_table()) return st;
+  WH_CUDA(launch_ref_expf(x, y, (long long)n, c->expf, (cudaStream_t)stream));
+  return WH_OK;
 }
 
 }  // extern "C"

@@ -19,6 +19,59 @@ inline cudaError_t ensure_smem(K* kernel, size_t bytes) {
   return ensure_smem_attr(reinterpret_cast<const void*>(kernel), bytes);
 }
 
+// ---------------- the host libm's expf on the device ----------------
+// Inputs where the host's expf differs from exp((double)x) rounded once, or
+// lies too close to a rounding midpoint to trust the device's double exp:
+// keys ascending (float bits as uint32), vals the host expf.
+struct ExpfTable {
+  const uint32_t* keys;
+  const float* vals;
+  int n;
+};
+bool expf_table_host(const uint32_t** keys, const float** vals, int* n);
+
+__device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
+  const double yd = exp((double)x);
+  const float c = __double2float_rn(yd);
+  const uint32_t cb = __float_as_uint(c);
+  const double dc = (double)c;
+  const double other = (double)__uint_as_float(yd > dc ? cb + 1u : cb - 1u);
+  if (fabs(yd - 0.5 * (dc + other)) <= yd * 0x1p-30) {
+    const uint32_t xb = __float_as_uint(x);
+    int lo = 0, hi = t.n;  // first key >= xb
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(t.keys + mid) < xb) lo = mid + 1; else hi = mid;
+    }
+    if (lo < t.n && __ldg(t.keys + lo) == xb) return __ldg(t.vals + lo);
+  }
+  return c;
+}
+cudaError_t launch_ref_expf(const float* x, float* y, long long n, ExpfTable t, cudaStream_t s);
+
+// ---------------- MLA attention core ----------------
+struct MlaArgs {
+  const float* q;           // [heads][head_dim]
+  const float* keys;        // layer cache rows [positions][key_stride]
+  const float* compressed;  // [compressed_count][head_dim]
+  const float* sink;        // [heads] or nullptr
+  float* out;               // [heads][head_dim]
+  float* scores;            // scratch [window_len + compressed_count][heads]
+  float* tile_max;          // scratch [tiles][heads]
+  float* weights;           // scratch [heads][window_len + compressed_count]
+  float* head_max;          // scratch [heads]
+  int heads, head_dim, nope_dim, key_stride;
+  int window_start, window_len, compressed_count;
+  int tile_pos, smem_ld, head_group, vec4;  // launch plan (mla_plan)
+  float scale;
+  ExpfTable expf;
+  float rope_cos[64], rope_sin[64];  // per rope pair at the token's position
+};
+bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output);
+size_t mla_scratch_bytes(int heads, int positions, int tile_pos);
+cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t smem_output,
+                                 cudaStream_t s);
+
 // ---------------- BF16 lm_head top-k ----------------
 struct LmHeadArgs {
   const uint16_t* weight;  // [rows][cols] bf16 bits

@@ -3,6 +3,8 @@
 #include "fp8_gemv.cu"
 #include "moe.cu"
 #include "decode.cu"
+#include "libm_exact.cu"
+#include "mla.cu"
 #include "grouped.cu"
 #include "ep.cu"
 #include "lmhead.cu"
