@@ -1344,7 +1344,8 @@ def run_mla(args):
             "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (reference operation order, no FMA)",
             "data": "synthetic (N(0, 1) cache rows, N(0, 0.05) queries)", "config": cfg,
-            "roofline": {"kernel": "mla_scores_kernel + mla_output_kernel", "bound": "hbm",
+            "roofline": {"kernel": "mla_scores_kernel + mla_weights_kernel + mla_output_kernel",
+                         "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algorithmic_bytes": alg, "traffic": MLA_TRAFFIC,
@@ -1355,7 +1356,7 @@ def run_mla(args):
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
                     "d2h_bytes_per_step": out.numel() * 4,
                     "path": "pinned host q -> H2D -> wh_mla_attention (C ABI) -> D2H output"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:

@@ -81,7 +81,11 @@ int wh_version(void);
 /* Creates a context on `device` (cudaSetDevice is called).  Allocates the
  * device status word and uploads the act-quant rounding table, which is
  * measured from the host's libm log2f so ceil(log2f(.)) matches the
- * reference bit for bit (src/compute.rs:2516). */
+ * reference bit for bit (src/compute.rs:2516).  The first context of a process
+ * also measures the host libm's expf table (about 3 s of host time; every exp
+ * of the kernels -- SiLU, the router, the MLA softmax -- then equals the
+ * reference's f32::exp bit for bit), and each device gets its copy once (5.5 MB,
+ * held until exit). */
 wh_status wh_ctx_create(int device, wh_ctx** out);
 void wh_ctx_destroy(wh_ctx* ctx);
 
@@ -377,12 +381,12 @@ void wh_rope_inv_freqs(int rope_dim, float theta, float yarn_factor, float yarn_
  *   rope_inv_freqs; out [heads][head_dim].  Device pointers otherwise.
  * The cos/sin of token_pos * inv_freq are computed on the host with the C
  * library, like the reference's f32::sin_cos; exp is the host C library's expf,
- * reproduced on the device through a table measured at first use (about 3 s of
- * host time once per process).  The scores live in a context-owned workspace:
- * calls on one context are serialised by the caller (one stream at a time).
+ * reproduced on the device through the table that wh_ctx_create installs.  The
+ * scores live in a context-owned workspace: calls on one context are serialised
+ * by the caller (one stream at a time).
  * Errors: InvalidShape (nope_dim > head_dim, odd rope part, key_stride <
- * head_dim, window < 1), Unsupported (rope part > 128, odd nope_dim, more than
- * 512 heads, or heads/head_dim/visible rows beyond shared memory). */
+ * head_dim, window < 1), Unsupported (rope part > 128, odd nope_dim, or
+ * head_dim / visible rows beyond shared memory). */
 wh_status wh_mla_attention(wh_ctx* ctx, const float* q, int heads, int head_dim, int nope_dim,
                            const float* keys, int key_stride, int token_pos, int window,
                            const float* compressed, int compressed_count, const float* sink,
@@ -560,9 +564,11 @@ void wh_debug_act_quant_table(uint32_t out[256]);
 /* The E4M3 nearest-with-ties-to-lower rounding the kernels use (|t| <= 448). */
 float wh_debug_e4m3_round(float t);
 void wh_debug_e4m3_round_n(const float* in, float* out, size_t n); /* host arrays */
-/* The table that makes the device's exp equal the host C library's expf (built
- * on first use by scanning expf over (-104, 89)): the number of entries, negated
- * if some difference fell outside the device's midpoint gate. */
+/* The table that makes the device's exp equal the host C library's expf: the
+ * first wh_ctx_create of a process builds it by scanning expf over (-104, 89)
+ * (about 3 s of host time on 8 threads) and installs it on each device.
+ * Returns the number of entries, negated if some difference fell outside the
+ * device's midpoint gate (wh_ctx_create then fails with Unsupported). */
 int wh_debug_expf_table(const uint32_t** keys, const float** vals);
 /* y[i] = the host libm's expf(x[i]), evaluated on the device (device arrays). */
 wh_status wh_debug_ref_expf(wh_ctx* ctx, const float* x, float* y, size_t n,

@@ -310,23 +310,6 @@ struct wh_ctx {
     mla_work_bytes = bytes;
     return WH_OK;
   }
-  ExpfTable expf{nullptr, nullptr, 0};  // device copy of the host expf table
-  void* expf_mem = nullptr;
-  wh_status ensure_expf_table() {
-    if (expf_mem) return WH_OK;
-    const uint32_t* keys;
-    const float* vals;
-    int n;
-    if (!expf_table_host(&keys, &vals, &n))
-      return fail(WH_ERR_UNSUPPORTED, "host expf differs outside the device's midpoint gate");
-    const size_t kb = sizeof(uint32_t) * (size_t)n, vb = sizeof(float) * (size_t)n;
-    WH_CUDA(cudaMalloc(&expf_mem, kb + vb + 16));
-    WH_CUDA(cudaMemcpy(expf_mem, keys, kb, cudaMemcpyHostToDevice));
-    WH_CUDA(cudaMemcpy((char*)expf_mem + kb, vals, vb, cudaMemcpyHostToDevice));
-    expf = ExpfTable{(const uint32_t*)expf_mem, (const float*)((char*)expf_mem + kb), n};
-    return WH_OK;
-  }
-
   wh_status ensure_work(size_t bytes) {
     if (bytes <= work_bytes) return WH_OK;
     if (work) cudaFree(work);
@@ -397,7 +380,13 @@ wh_status wh_ctx_create(int device, wh_ctx** out) {
     return cuda_fail(e, "status word");
   }
   set_act_quant_table(act_quant_table_host(), nullptr);
-  e = cudaDeviceSynchronize();
+  cudaError_t te = cudaSuccess;
+  if (!install_expf_table(&te)) {
+    cudaFree(c->status);
+    delete c;
+    return fail(WH_ERR_UNSUPPORTED, "host expf differs outside the device's midpoint gate");
+  }
+  e = te != cudaSuccess ? te : cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(c->status);
     delete c;
@@ -416,7 +405,6 @@ void wh_ctx_destroy(wh_ctx* c) {
   if (c->counters) cudaFree(c->counters);
   if (c->blk_counters) cudaFree(c->blk_counters);
   if (c->work) cudaFree(c->work);
-  if (c->expf_mem) cudaFree(c->expf_mem);
   if (c->mla_work) cudaFree(c->mla_work);
   delete c;
 }
@@ -834,14 +822,12 @@ wh_status wh_mla_attention(wh_ctx* c, const float* q, int heads, int head_dim, i
            (compressed_count == 0 || al16(compressed));
   a.scale = powf((float)head_dim, -0.5f);  // (head_dim as f32).powf(-0.5)
   cudaSetDevice(c->device);
-  if (wh_status st = c->ensure_expf_table()) return st;
-  a.expf = c->expf;
   const int positions = a.window_len + compressed_count;
-  if (wh_status st = c->ensure_mla_work(mla_scratch_bytes(heads, positions, a.tile_pos))) return st;
+  if (wh_status st = c->ensure_mla_work(mla_scratch_bytes(heads, positions))) return st;
   a.scores = (float*)c->mla_work;
   a.weights = a.scores + (size_t)positions * heads;
   a.tile_max = a.weights + (size_t)positions * heads;
-  a.head_max = a.tile_max + (size_t)((positions + a.tile_pos - 1) / a.tile_pos) * heads;
+  a.head_max = a.tile_max + mla_tile_count(positions) * heads;
   const float pos = (float)token_pos;
   for (int i = 0; i < pairs; ++i) {
     const float angle = pos * inv_freqs[i];
@@ -1352,8 +1338,7 @@ wh_status wh_debug_ref_expf(wh_ctx* c, const float* x, float* y, size_t n, wh_st
   if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
   if (n > 0 && (!x || !y)) return fail(WH_ERR_INVALID_POINTER, "null pointer");
   cudaSetDevice(c->device);
-  if (wh_status st = c->ensure_expf_table()) return st;
-  WH_CUDA(launch_ref_expf(x, y, (long long)n, c->expf, (cudaStream_t)stream));
+  WH_CUDA(launch_ref_expf(x, y, (long long)n, (cudaStream_t)stream));
   return WH_OK;
 }
 

@@ -26,9 +26,13 @@ inline cudaError_t ensure_smem(K* kernel, size_t bytes) {
 struct ExpfTable {
   const uint32_t* keys;
   const float* vals;
+  const uint32_t* bucket;  // [2^20 + 1]: first key index of each (bits >> 12) bucket
   int n;
 };
+constexpr int kExpfBucketShift = 12;
+constexpr uint32_t kExpfBuckets = 1u << (32 - kExpfBucketShift);
 bool expf_table_host(const uint32_t** keys, const float** vals, int* n);
+bool expf_bucket_host(const uint32_t** bucket);
 
 __device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
   const double yd = exp((double)x);
@@ -37,8 +41,11 @@ __device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
   const double dc = (double)c;
   const double other = (double)__uint_as_float(yd > dc ? cb + 1u : cb - 1u);
   if (fabs(yd - 0.5 * (dc + other)) <= yd * 0x1p-30) {
+    // near a rounding midpoint (about 0.6 % of inputs): x's bucket bounds, then
+    // a binary search over the bucket's few keys
     const uint32_t xb = __float_as_uint(x);
-    int lo = 0, hi = t.n;  // first key >= xb
+    const uint32_t b = xb >> kExpfBucketShift;
+    int lo = (int)__ldg(t.bucket + b), hi = (int)__ldg(t.bucket + b + 1);
     while (lo < hi) {
       const int mid = (lo + hi) >> 1;
       if (__ldg(t.keys + mid) < xb) lo = mid + 1; else hi = mid;
@@ -47,7 +54,13 @@ __device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
   }
   return c;
 }
-cudaError_t launch_ref_expf(const float* x, float* y, long long n, ExpfTable t, cudaStream_t s);
+// The table of the current device, installed by install_expf_table (wh_ctx_create).
+__constant__ ExpfTable c_expf;
+__device__ __forceinline__ float libm_expf(float x) { return ref_expf(x, c_expf); }
+// Builds the host table once per process and installs it on the current device
+// (once per device).  Returns false when the table cannot reproduce the host expf.
+bool install_expf_table(cudaError_t* err);
+cudaError_t launch_ref_expf(const float* x, float* y, long long n, cudaStream_t s);
 
 // ---------------- MLA attention core ----------------
 struct MlaArgs {
@@ -62,13 +75,13 @@ struct MlaArgs {
   float* head_max;          // scratch [heads]
   int heads, head_dim, nope_dim, key_stride;
   int window_start, window_len, compressed_count;
-  int tile_pos, smem_ld, head_group, vec4;  // launch plan (mla_plan)
+  int smem_ld, head_group, stages, vec4;  // launch plan (mla_plan)
   float scale;
-  ExpfTable expf;
   float rope_cos[64], rope_sin[64];  // per rope pair at the token's position
 };
 bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output);
-size_t mla_scratch_bytes(int heads, int positions, int tile_pos);
+size_t mla_scratch_bytes(int heads, int positions);
+size_t mla_tile_count(int positions);
 cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t smem_output,
                                  cudaStream_t s);
 

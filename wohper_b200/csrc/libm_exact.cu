@@ -8,14 +8,20 @@
 // glibc 2.39.  Those inputs all lie where exp(x) is within 2^-30 (relative) of
 // a float rounding midpoint.
 //
-// The table is measured, not derived: at first use the library calls the
-// running process's expf on every float in (-104, 89) (all host threads) and
-// records each x whose expf differs from the once-rounded double exp, plus
-// every x whose exp lies within 2^-44 of a midpoint (there a one-ulp
-// difference between the host's and the device's double exp could flip the
-// rounding).  On the device, ref_expf rounds exp((double)x) once and looks x up
-// in the sorted table only when the result is within 2^-30 of a midpoint,
-// about 0.6 % of inputs.  Outside (-104, 89) both sides saturate to 0 or inf.
+// The table is measured, not derived: at the first wh_ctx_create the library
+// calls the running process's expf on every float in (-104, 89) (all host
+// threads, about 3 s of host time once per process) and records each x whose
+// expf differs from the once-rounded double exp, plus every x whose exp lies
+// within 2^-44 of a midpoint (there a one-ulp difference between the host's and
+// the device's double exp could flip the rounding).  The table is installed
+// once per device in constant memory (c_expf).  On the device, ref_expf rounds
+// exp((double)x) once and looks x up only when the result is within 2^-30 of a
+// midpoint, about 0.6 % of inputs: one load of x's bucket bounds (2^20 buckets
+// by the top 20 bits of x), then a binary search over that bucket's keys (65
+// at most for glibc 2.39, a few cache lines).  Outside (-104, 89) both sides
+// saturate to 0 or inf.  Every exp of the reference's arithmetic on this path
+// (SiLU, the router's softplus and softmax, the MLA softmax) goes through
+// libm_expf.
 #include <algorithm>
 #include <atomic>
 #include <mutex>
@@ -32,7 +38,8 @@ namespace {
 struct ExpfHostTable {
   std::vector<uint32_t> keys;  // float bits of x, ascending as uint32
   std::vector<float> vals;     // the host expf(x)
-  bool model_ok = true;        // every difference lies inside the device gate
+  std::vector<uint32_t> bucket;  // first key index per (bits >> 12) bucket, plus n
+  bool model_ok = true;          // every difference lies inside the device gate
 };
 
 inline float bits_to_float(uint32_t u) {
@@ -99,6 +106,13 @@ const ExpfHostTable& expf_host_table() {
       table.vals.insert(table.vals.end(), cv[i].begin(), cv[i].end());
       if (!cok[i]) table.model_ok = false;
     }
+    table.bucket.resize((size_t)kExpfBuckets + 1);
+    size_t k = 0;
+    for (uint64_t b = 0; b <= kExpfBuckets; ++b) {
+      const uint64_t lo = b << kExpfBucketShift;
+      while (k < table.keys.size() && table.keys[k] < lo) ++k;
+      table.bucket[b] = (uint32_t)k;
+    }
   });
   return table;
 }
@@ -114,16 +128,54 @@ bool expf_table_host(const uint32_t** keys, const float** vals, int* n) {
   return t.model_ok;
 }
 
-__global__ void ref_expf_kernel(const float* x, float* y, long long n, ExpfTable t) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    y[i] = ref_expf(x[i], t);
+bool expf_bucket_host(const uint32_t** bucket) {
+  *bucket = expf_host_table().bucket.data();
+  return expf_host_table().model_ok;
 }
 
-cudaError_t launch_ref_expf(const float* x, float* y, long long n, ExpfTable t, cudaStream_t s) {
+bool install_expf_table(cudaError_t* err) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* dev_mem[kMaxDevices] = {};
+  *err = cudaSuccess;
+  const uint32_t* keys;
+  const float* vals;
+  const uint32_t* bucket;
+  int n;
+  if (!expf_table_host(&keys, &vals, &n) || !expf_bucket_host(&bucket)) return false;
+  int device = 0;
+  if ((*err = cudaGetDevice(&device)) != cudaSuccess) return true;
+  if (device < 0 || device >= kMaxDevices) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev_mem[device]) return true;  // installed for the process's lifetime
+  const size_t kb = sizeof(uint32_t) * (size_t)n, vb = sizeof(float) * (size_t)n;
+  const size_t bb = sizeof(uint32_t) * ((size_t)kExpfBuckets + 1);
+  void* mem = nullptr;
+  if ((*err = cudaMalloc(&mem, kb + vb + bb)) != cudaSuccess) return true;
+  const ExpfTable t{(const uint32_t*)mem, (const float*)((char*)mem + kb),
+                    (const uint32_t*)((char*)mem + kb + vb), n};
+  if ((*err = cudaMemcpy(mem, keys, kb, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (*err = cudaMemcpy((char*)mem + kb, vals, vb, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (*err = cudaMemcpy((char*)mem + kb + vb, bucket, bb, cudaMemcpyHostToDevice)) !=
+          cudaSuccess ||
+      (*err = cudaMemcpyToSymbol(c_expf, &t, sizeof(t))) != cudaSuccess) {
+    cudaFree(mem);
+    return true;
+  }
+  dev_mem[device] = mem;
+  return true;
+}
+
+__global__ void ref_expf_kernel(const float* x, float* y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = libm_expf(x[i]);
+}
+
+cudaError_t launch_ref_expf(const float* x, float* y, long long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   const long long blocks = std::min<long long>((n + 255) / 256, 148 * 16);
-  ref_expf_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, y, n, t);
+  ref_expf_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, y, n);
   return cudaGetLastError();
 }
 

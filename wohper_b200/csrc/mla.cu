@@ -9,7 +9,7 @@
 //           order (no fused multiply-add, as the reference's scalar loop)
 //   softmax max over all s_p; denom = exp(sink - max) (when the layer has a
 //           sink) + the in-order sum of w_p = exp(s_p - max), exp being the
-//           host libm's expf reproduced bit for bit (ref_expf)
+//           host libm's expf reproduced bit for bit (libm_expf)
 //   output  o_d = in-order sum over p of w_p * k_p,d (the keys are the values),
 //           divided by denom when it is positive, then inverse RoPE on the
 //           rope pairs (cos and sin of pos * inv_freq computed on the host with
@@ -17,10 +17,11 @@
 //
 // Every sum above is a dependent chain in the reference's order, so the work
 // is spread over chains, never inside one:
-//   mla_scores_kernel  one CTA per tile of positions, all heads: one thread per
-//                      (head, position) chain over d; q and the tile's key rows
-//                      copied into shared memory (rows padded by 16 B so that a
-//                      warp's 16-byte reads of 32 heads hit distinct banks).
+//   mla_scores_kernel  one CTA per (16 positions, 32 heads): lane = head, and
+//                      each thread runs the chains over d of four positions, so
+//                      one 16-byte q read from shared memory serves four chains
+//                      and the key reads are warp broadcasts (rows padded by
+//                      16 B so that the 32 lanes' q reads hit distinct banks).
 //                      Writes the scaled scores [P][heads] and the tile's
 //                      per-head max.
 //   mla_weights_kernel one CTA per (head, 256 positions): the head's max over
@@ -28,10 +29,11 @@
 //   mla_output_kernel  one CTA per (64-feature slice, group of heads): the
 //                      group's weight rows into shared memory, one thread per
 //                      (head, feature) chain over the positions, the slice's
-//                      key rows streamed through a 4-stage cp.async ring of 64
-//                      rows, a denominator warp running the in-order weight
-//                      sums in the same stages, then division, inverse RoPE
-//                      (pair partner by shuffle) and the store.
+//                      key rows streamed through a cp.async ring of 12 (8, 4)
+//                      stages of 64 rows by the feature warps alone (on a named
+//                      barrier), a denominator warp running the in-order weight
+//                      sums beside them, then division, inverse RoPE (pair
+//                      partner by shuffle) and the store.
 // Each kernel is launched as a programmatic dependent of the one before; the
 // staging copies are cp.async, so all of a CTA's loads are in flight at once.
 #include "common.cuh"
@@ -39,10 +41,13 @@
 
 namespace wh {
 
-constexpr int kMlaScoreThreads = 512;
-constexpr int kMlaSlice = 64;  // features per output CTA (two warps per head)
-constexpr int kMlaRingRows = 64;  // key rows per ring stage of the output kernel
-constexpr int kMlaStages = 4;
+constexpr int kMlaScoreHeads = 32;  // heads per scores CTA (one per lane)
+constexpr int kMlaScoreChains = 4;  // positions per thread
+constexpr int kMlaScoreTile = 16;   // positions per scores CTA
+constexpr int kMlaScoreThreads = kMlaScoreHeads * kMlaScoreTile / kMlaScoreChains;
+constexpr int kMlaSlice = 64;       // features per output CTA (two warps per head)
+constexpr int kMlaRingRows = 64;    // key rows per ring stage of the output kernel
+constexpr size_t kMlaStageBytes = sizeof(float) * kMlaRingRows * kMlaSlice;
 constexpr int kMlaWeightThreads = 256;
 
 __device__ __forceinline__ const float* mla_key_row(const MlaArgs& a, int p) {
@@ -67,21 +72,21 @@ __device__ __forceinline__ void cp_async_wait() {
 
 __global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a) {
   extern __shared__ __align__(16) float mla_s[];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = a.heads, D = a.head_dim, ld = a.smem_ld;
   const int P = a.window_len + a.compressed_count;
-  const int p0 = blockIdx.x * a.tile_pos;
-  const int np = min(a.tile_pos, P - p0);
-  float* q_s = mla_s;                           // [H][ld]
-  float* k_s = q_s + (size_t)H * ld;            // [tile_pos][ld]
-  float* sc_s = k_s + (size_t)a.tile_pos * ld;  // [tile_pos][H]
+  const int p0 = blockIdx.x * kMlaScoreTile, np = min(kMlaScoreTile, P - p0);
+  const int hb = blockIdx.y * kMlaScoreHeads, nh = min(kMlaScoreHeads, H - hb);
+  float* q_s = mla_s;                              // [kMlaScoreHeads][ld]
+  float* k_s = q_s + (size_t)kMlaScoreHeads * ld;  // [kMlaScoreTile][ld]
+  float* sc_s = k_s + (size_t)kMlaScoreTile * ld;  // [kMlaScoreTile][kMlaScoreHeads]
   pdl_wait_prior();
-  // stage q and the tile's key rows; every copy in flight at once
+  // the block's q rows and the tile's key rows; every copy in flight at once
   const int cw = a.vec4 ? 4 : 1;
   const int per_row = D / cw;
-  for (int i = tid; i < H * per_row; i += blockDim.x) {
+  for (int i = tid; i < nh * per_row; i += blockDim.x) {
     const int h = i / per_row, c = (i - h * per_row) * cw;
-    cp_async(q_s + h * ld + c, a.q + (long long)h * D + c, a.vec4);
+    cp_async(q_s + h * ld + c, a.q + (long long)(hb + h) * D + c, a.vec4);
   }
   for (int i = tid; i < np * per_row; i += blockDim.x) {
     const int r = i / per_row, c = (i - r * per_row) * cw;
@@ -90,37 +95,57 @@ __global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a)
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
-  // one chain per (head, position): lanes are consecutive heads at one position
-  for (int c = tid; c < H * a.tile_pos; c += blockDim.x) {
-    const int h = c % H, r = c / H;
-    if (r >= np) continue;
-    const float* qh = q_s + h * ld;
-    const float* kr = k_s + r * ld;
-    float s = 0.0f;
+  // lane = head, four positions per thread (rows beyond np are computed on
+  // whatever the buffer holds and never stored)
+  const int r0 = warp * kMlaScoreChains;
+  if (lane < nh && r0 < np) {
+    const float* qh = q_s + lane * ld;
+    const float* kr = k_s + r0 * ld;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
     int d = 0;
-#pragma unroll 4
+#pragma unroll 2
     for (; d + 4 <= D; d += 4) {
       const float4 qv = *reinterpret_cast<const float4*>(qh + d);
-      const float4 kv = *reinterpret_cast<const float4*>(kr + d);
-      s = __fadd_rn(s, __fmul_rn(qv.x, kv.x));
-      s = __fadd_rn(s, __fmul_rn(qv.y, kv.y));
-      s = __fadd_rn(s, __fmul_rn(qv.z, kv.z));
-      s = __fadd_rn(s, __fmul_rn(qv.w, kv.w));
+      const float4 k0 = *reinterpret_cast<const float4*>(kr + d);
+      const float4 k1 = *reinterpret_cast<const float4*>(kr + ld + d);
+      const float4 k2 = *reinterpret_cast<const float4*>(kr + 2 * ld + d);
+      const float4 k3 = *reinterpret_cast<const float4*>(kr + 3 * ld + d);
+#define WH_MLA_STEP(S, K)                 \
+  S = __fadd_rn(S, __fmul_rn(qv.x, K.x)); \
+  S = __fadd_rn(S, __fmul_rn(qv.y, K.y)); \
+  S = __fadd_rn(S, __fmul_rn(qv.z, K.z)); \
+  S = __fadd_rn(S, __fmul_rn(qv.w, K.w));
+      WH_MLA_STEP(s0, k0)
+      WH_MLA_STEP(s1, k1)
+      WH_MLA_STEP(s2, k2)
+      WH_MLA_STEP(s3, k3)
+#undef WH_MLA_STEP
     }
-    for (; d < D; ++d) s = __fadd_rn(s, __fmul_rn(qh[d], kr[d]));
-    s = __fmul_rn(s, a.scale);
-    a.scores[(long long)(p0 + r) * H + h] = s;
-    sc_s[r * H + h] = s;
+    for (; d < D; ++d) {
+      const float qd = qh[d];
+      s0 = __fadd_rn(s0, __fmul_rn(qd, kr[d]));
+      s1 = __fadd_rn(s1, __fmul_rn(qd, kr[ld + d]));
+      s2 = __fadd_rn(s2, __fmul_rn(qd, kr[2 * ld + d]));
+      s3 = __fadd_rn(s3, __fmul_rn(qd, kr[3 * ld + d]));
+    }
+    const float sv[4] = {__fmul_rn(s0, a.scale), __fmul_rn(s1, a.scale),
+                         __fmul_rn(s2, a.scale), __fmul_rn(s3, a.scale)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (r0 + j < np) {
+        a.scores[(long long)(p0 + r0 + j) * H + hb + lane] = sv[j];
+        sc_s[(r0 + j) * kMlaScoreHeads + lane] = sv[j];
+      }
   }
   __syncthreads();
   // the tile's max per head (a NaN score never becomes the max)
-  for (int h = tid; h < H; h += blockDim.x) {
+  if (tid < nh) {
     float m = -INFINITY;
     for (int r = 0; r < np; ++r) {
-      const float v = sc_s[r * H + h];
+      const float v = sc_s[r * kMlaScoreHeads + tid];
       m = v > m ? v : m;
     }
-    a.tile_max[(long long)blockIdx.x * H + h] = m;
+    a.tile_max[(long long)blockIdx.x * H + hb + tid] = m;
   }
   pdl_launch_dependents();
 }
@@ -132,7 +157,7 @@ __global__ void __launch_bounds__(kMlaWeightThreads) mla_weights_kernel(MlaArgs 
   const int tid = threadIdx.x, h = blockIdx.y;
   const int H = a.heads;
   const int P = a.window_len + a.compressed_count;
-  const int ntiles = (P + a.tile_pos - 1) / a.tile_pos;
+  const int ntiles = (P + kMlaScoreTile - 1) / kMlaScoreTile;
   pdl_wait_prior();
   float m = -INFINITY;
   for (int t = tid; t < ntiles; t += blockDim.x) {
@@ -149,24 +174,33 @@ __global__ void __launch_bounds__(kMlaWeightThreads) mla_weights_kernel(MlaArgs 
   for (int w = 0; w < kMlaWeightThreads / 32; ++w) m = s_red[w] > m ? s_red[w] : m;
   const int p = blockIdx.x * kMlaWeightThreads + tid;
   if (p < P)
-    a.weights[(long long)h * P + p] =
-        ref_expf(__fsub_rn(a.scores[(long long)p * H + h], m), a.expf);
+    a.weights[(long long)h * P + p] = libm_expf(__fsub_rn(a.scores[(long long)p * H + h], m));
   if (blockIdx.x == 0 && tid == 0) a.head_max[h] = m;
   pdl_launch_dependents();
 }
 
-// Copies rows [r0, r0 + kMlaRingRows) of the CTA's feature slice into a ring slot.
+// Copies rows [r0, r0 + kMlaRingRows) of the CTA's feature slice into a ring
+// slot; threads [0, nthreads) take part.
 __device__ __forceinline__ void mla_issue_rows(const MlaArgs& a, float* slot, int r0, int P,
-                                               int f0, int nf) {
+                                               int f0, int nf, int nthreads) {
+  const int rows = min(kMlaRingRows, P - r0);
+  if (a.vec4 && nf == kMlaSlice) {
+    constexpr int kPerRow = kMlaSlice / 4;
+    for (int i = threadIdx.x; i < rows * kPerRow; i += nthreads) {
+      const int r = i / kPerRow, c = (i % kPerRow) * 4;
+      cp_async(slot + r * kMlaSlice + c, mla_key_row(a, r0 + r) + f0 + c, true);
+    }
+    return;
+  }
   const int cw = a.vec4 ? 4 : 1;  // floats per copy
   const int per_row = (nf + cw - 1) / cw;
-  const int rows = min(kMlaRingRows, P - r0);
-  for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
+  for (int i = threadIdx.x; i < rows * per_row; i += nthreads) {
     const int r = i / per_row, c = (i - r * per_row) * cw;
     cp_async(slot + r * kMlaSlice + c, mla_key_row(a, r0 + r) + f0 + c, a.vec4);
   }
 }
 
+template <int kStages>
 __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs a) {
   extern __shared__ __align__(16) float mla_w[];  // [group][P] weights | key ring
   __shared__ float s_den[4];
@@ -174,53 +208,67 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   const int D = a.head_dim, G = a.head_group;
   const int P = a.window_len + a.compressed_count;
   const int h0 = blockIdx.y * G;
-  const int fw = 2 * G;  // feature warps; warp fw is the denominator warp
+  const int fw = 2 * G;       // feature warps; warp fw is the denominator warp
+  const int nfeat = fw * 32;  // threads of the feature warps
   const int f0 = blockIdx.x * kMlaSlice, nf = min(kMlaSlice, D - f0);
-  float* ring = mla_w + ((G * P + 3) & ~3);  // [kMlaStages][kMlaRingRows][kMlaSlice]
+  float* ring = mla_w + ((G * P + 3) & ~3);  // [kStages][kMlaRingRows][kMlaSlice]
   const int nst = (P + kMlaRingRows - 1) / kMlaRingRows;
-  pdl_wait_prior();
-  // the key rows do not depend on the scores: start the ring first
-#pragma unroll
-  for (int st = 0; st < kMlaStages - 1; ++st) {
-    if (st < nst)
-      mla_issue_rows(a, ring + st * kMlaRingRows * kMlaSlice, st * kMlaRingRows, P, f0, nf);
-    cp_async_commit();
-  }
-  // the group's weight rows (contiguous [h][P]) behind the ring's first stages
-  for (int i = tid; i < G * P; i += blockDim.x)
-    cp_async(mla_w + i, a.weights + (long long)h0 * P + i, false);
-  cp_async_commit();
-  cp_async_wait<0>();
   const int g = warp >> 1;
   const int fl = (warp & 1) * 32 + lane;  // feature within the slice
   const bool feature = warp < fw && fl < nf;
   const bool dwarp = warp == fw && lane < G;
-  const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * P;
-  float acc = 0.0f;  // feature chain, or the denominator warp's weight sum
-  for (int st = 0; st < nst; ++st) {
-    cp_async_wait<kMlaStages - 2>();
-    __syncthreads();  // stage st (and the weights) landed for every thread; slot st - 1 is free
-    const int nx = st + kMlaStages - 1;
-    if (nx < nst)
-      mla_issue_rows(a, ring + (nx % kMlaStages) * kMlaRingRows * kMlaSlice, nx * kMlaRingRows,
-                     P, f0, nf);
-    cp_async_commit();
-    const float* slot = ring + (st % kMlaStages) * kMlaRingRows * kMlaSlice;
-    const int r0 = st * kMlaRingRows, rows = min(kMlaRingRows, P - r0);
-    if (feature) {
-#pragma unroll 8
-      for (int r = 0; r < rows; ++r)
-        acc = __fadd_rn(acc, __fmul_rn(w[r0 + r], slot[r * kMlaSlice + fl]));
-    } else if (dwarp) {
-      // the in-order sum of the weights, stage by stage
-      for (int r = 0; r < rows; ++r) acc = __fadd_rn(acc, w[r0 + r]);
-    }
+  pdl_wait_prior();
+  // copy group 0, by every thread: the group's weight rows (contiguous [h][P])
+  if ((P & 3) == 0) {
+    for (int i = tid; i < G * P / 4; i += blockDim.x)
+      cp_async(mla_w + 4 * i, a.weights + (long long)h0 * P + 4 * i, true);
+  } else {
+    for (int i = tid; i < G * P; i += blockDim.x)
+      cp_async(mla_w + i, a.weights + (long long)h0 * P + i, false);
   }
-  cp_async_wait<0>();
-  if (dwarp) {
+  cp_async_commit();
+  // the feature warps own the key ring; its first stages are groups 1 .. S-1
+  if (warp < fw) {
+#pragma unroll
+    for (int st = 0; st < kStages - 1; ++st) {
+      if (st < nst)
+        mla_issue_rows(a, ring + st * kMlaRingRows * kMlaSlice, st * kMlaRingRows, P, f0, nf,
+                       nfeat);
+      cp_async_commit();
+    }
+    cp_async_wait<kStages - 1>();  // group 0: the weights
+  } else {
+    cp_async_wait<0>();
+  }
+  __syncthreads();  // the weights are visible to every thread
+  const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * P;
+  float acc = 0.0f;  // a feature chain, or a denominator's weight sum
+  if (warp < fw) {
+    for (int st = 0; st < nst; ++st) {
+      cp_async_wait<kStages - 2>();
+      // stage st landed for every feature thread, and slot st - 1 is free
+      asm volatile("bar.sync 1, %0;" ::"r"(nfeat) : "memory");
+      const int nx = st + kStages - 1;
+      if (nx < nst)
+        mla_issue_rows(a, ring + (nx % kStages) * kMlaRingRows * kMlaSlice, nx * kMlaRingRows,
+                       P, f0, nf, nfeat);
+      cp_async_commit();
+      const float* slot = ring + (st % kStages) * kMlaRingRows * kMlaSlice;
+      const int r0 = st * kMlaRingRows, rows = min(kMlaRingRows, P - r0);
+      if (feature) {
+#pragma unroll 8
+        for (int r = 0; r < rows; ++r)
+          acc = __fadd_rn(acc, __fmul_rn(w[r0 + r], slot[r * kMlaSlice + fl]));
+      }
+    }
+    cp_async_wait<0>();
+  } else if (dwarp) {
+    // the in-order sum of the weights, beside the ring
+#pragma unroll 8
+    for (int p = 0; p < P; ++p) acc = __fadd_rn(acc, w[p]);
     float denom = 0.0f;
     if (a.sink)
-      denom = __fadd_rn(denom, ref_expf(__fsub_rn(a.sink[h0 + lane], a.head_max[h0 + lane]), a.expf));
+      denom = __fadd_rn(denom, libm_expf(__fsub_rn(a.sink[h0 + lane], a.head_max[h0 + lane])));
     s_den[lane] = __fadd_rn(denom, acc);
   }
   __syncthreads();
@@ -246,40 +294,52 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   pdl_launch_dependents();
 }
 
-// Plans the two launches: tile_pos, smem_ld and head_group.  Returns false
-// when the shape does not fit shared memory.
+// Plans the launches: smem_ld, head_group and the output ring's depth (12, 8
+// or 4 stages of 64 rows).  Returns false when the shape does not fit shared
+// memory.
 bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output) {
+  constexpr size_t kBudget = 220 * 1024;
   const int H = a.heads, D = a.head_dim;
   const int P = a.window_len + a.compressed_count;
-  constexpr size_t kBudget = 220 * 1024;
-  if (H > kMlaScoreThreads) return false;
   a.smem_ld = ((D + 3) & ~3) + 4;
-  // as many positions as threads allow, fewer when the key rows would not fit
-  const size_t q_bytes = sizeof(float) * (size_t)H * a.smem_ld;
-  const size_t per_pos = sizeof(float) * (size_t)(a.smem_ld + H);
-  const size_t fit = q_bytes < kBudget ? (kBudget - q_bytes) / per_pos : 0;
-  a.tile_pos = (int)std::min<size_t>(kMlaScoreThreads / H, fit);
-  if (a.tile_pos < 1) return false;
-  *smem_scores = q_bytes + per_pos * a.tile_pos;
-  const size_t ring = sizeof(float) * kMlaStages * kMlaRingRows * kMlaSlice;
-  const size_t wbytes = sizeof(float) * (size_t)P, wbudget = kBudget - ring - 16;
-  a.head_group = (H % 4 == 0 && 4 * wbytes <= wbudget) ? 4
-               : (H % 2 == 0 && 2 * wbytes <= wbudget) ? 2 : 1;
-  *smem_output = sizeof(float) * (((size_t)a.head_group * P + 3) & ~(size_t)3) + ring;
-  return *smem_scores <= kBudget && *smem_output <= kBudget;
+  *smem_scores = sizeof(float) * ((size_t)(kMlaScoreHeads + kMlaScoreTile) * a.smem_ld +
+                                  (size_t)kMlaScoreTile * kMlaScoreHeads);
+  if (*smem_scores > kBudget) return false;
+  for (int stages : {12, 8, 4})
+    for (int g : {4, 2, 1}) {
+      if (H % g) continue;
+      const size_t bytes =
+          sizeof(float) * (((size_t)g * P + 3) & ~(size_t)3) + stages * kMlaStageBytes;
+      if (bytes <= kBudget) {
+        a.head_group = g;
+        a.stages = stages;
+        *smem_output = bytes;
+        return true;
+      }
+    }
+  return false;
 }
 
-size_t mla_scratch_bytes(int heads, int positions, int tile_pos) {
-  const int ntiles = (positions + tile_pos - 1) / tile_pos;
+size_t mla_scratch_bytes(int heads, int positions) {
+  const int ntiles = (positions + kMlaScoreTile - 1) / kMlaScoreTile;
   return sizeof(float) * (2 * (size_t)positions * heads + (size_t)ntiles * heads + heads);
+}
+
+size_t mla_tile_count(int positions) {
+  return (size_t)(positions + kMlaScoreTile - 1) / kMlaScoreTile;
+}
+
+template <int S>
+static cudaError_t launch_mla_output(const cudaLaunchConfig_t& cfg, const MlaArgs& a) {
+  cudaError_t e = ensure_smem(mla_output_kernel<S>, cfg.dynamicSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, mla_output_kernel<S>, a);
 }
 
 cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t smem_output,
                                  cudaStream_t s) {
   const int P = a.window_len + a.compressed_count;
   cudaError_t e = ensure_smem(mla_scores_kernel, smem_scores);
-  if (e != cudaSuccess) return e;
-  e = ensure_smem(mla_output_kernel, smem_output);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -288,7 +348,8 @@ cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t sm
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3((P + a.tile_pos - 1) / a.tile_pos);
+  cfg.gridDim = dim3((P + kMlaScoreTile - 1) / kMlaScoreTile,
+                     (a.heads + kMlaScoreHeads - 1) / kMlaScoreHeads);
   cfg.blockDim = dim3(kMlaScoreThreads);
   cfg.dynamicSmemBytes = smem_scores;
   e = cudaLaunchKernelEx(&cfg, mla_scores_kernel, a);
@@ -301,7 +362,11 @@ cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t sm
   cfg.gridDim = dim3((a.head_dim + kMlaSlice - 1) / kMlaSlice, a.heads / a.head_group);
   cfg.blockDim = dim3(2 * 32 * a.head_group + 32);
   cfg.dynamicSmemBytes = smem_output;
-  return cudaLaunchKernelEx(&cfg, mla_output_kernel, a);
+  switch (a.stages) {
+    case 12: return launch_mla_output<12>(cfg, a);
+    case 8: return launch_mla_output<8>(cfg, a);
+    default: return launch_mla_output<4>(cfg, a);
+  }
 }
 
 }  // namespace wh

@@ -42,14 +42,8 @@ __device__ __forceinline__ float aq_grid(float v, float scale) {
   return e4m3_nearest_ties_lower(t);
 }
 
-__device__ __forceinline__ float glibc_like_expf(float x) {
-  // exp in double then one rounding to float: agrees with glibc expf except
-  // when exp(x) lies within ~1e-16 relative of a float rounding boundary.
-  return (float)exp((double)x);
-}
-
 __device__ __forceinline__ float silu_ref(float x) {  // src/deepseek_v4.rs:551-554
-  return __fdiv_rn(x, __fadd_rn(1.0f, glibc_like_expf(-x)));
+  return __fdiv_rn(x, __fadd_rn(1.0f, libm_expf(-x)));
 }
 
 __device__ __forceinline__ float sqrt_softplus_ref(float v) {  // src/compute.rs:2238-2248
@@ -57,9 +51,9 @@ __device__ __forceinline__ float sqrt_softplus_ref(float v) {  // src/compute.rs
   if (v > 20.0f)
     sp = v;
   else if (v < -20.0f)
-    sp = glibc_like_expf(v);
+    sp = libm_expf(v);
   else
-    sp = (float)log1p((double)glibc_like_expf(v));
+    sp = (float)log1p((double)libm_expf(v));
   return __fsqrt_rn(fmaxf(sp, 0.0f));
 }
 
@@ -220,7 +214,7 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
       // every selected w is finite here, where total_cmp order is numeric
       // order (a -0/+0 tie gives the same exp(w - max) either way)
       const float mx = key_to_float(__reduce_max_sync(kFull, mine ? total_key(w) : INT32_MIN));
-      const float e = mine ? glibc_like_expf(__fsub_rn(w, mx)) : 0.0f;
+      const float e = mine ? libm_expf(__fsub_rn(w, mx)) : 0.0f;
       const float sum = ordered_sum(e);
       if (!isfinite(sum) || sum <= 1.1920929e-07f)
         uniform = true;
