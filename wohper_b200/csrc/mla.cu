@@ -110,15 +110,21 @@ __global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a)
       const float4 k1 = *reinterpret_cast<const float4*>(kr + ld + d);
       const float4 k2 = *reinterpret_cast<const float4*>(kr + 2 * ld + d);
       const float4 k3 = *reinterpret_cast<const float4*>(kr + 3 * ld + d);
-#define WH_MLA_STEP(S, K)                 \
-  S = __fadd_rn(S, __fmul_rn(qv.x, K.x)); \
-  S = __fadd_rn(S, __fmul_rn(qv.y, K.y)); \
-  S = __fadd_rn(S, __fmul_rn(qv.z, K.z)); \
-  S = __fadd_rn(S, __fmul_rn(qv.w, K.w));
-      WH_MLA_STEP(s0, k0)
-      WH_MLA_STEP(s1, k1)
-      WH_MLA_STEP(s2, k2)
-      WH_MLA_STEP(s3, k3)
+      // the four chains interleaved, so that each addition waits on its own
+      // chain only
+#define WH_MLA_STEP(C)                                                            \
+  {                                                                               \
+    const float m0 = __fmul_rn(qv.C, k0.C), m1 = __fmul_rn(qv.C, k1.C);           \
+    const float m2 = __fmul_rn(qv.C, k2.C), m3 = __fmul_rn(qv.C, k3.C);           \
+    s0 = __fadd_rn(s0, m0);                                                       \
+    s1 = __fadd_rn(s1, m1);                                                       \
+    s2 = __fadd_rn(s2, m2);                                                       \
+    s3 = __fadd_rn(s3, m3);                                                       \
+  }
+      WH_MLA_STEP(x)
+      WH_MLA_STEP(y)
+      WH_MLA_STEP(z)
+      WH_MLA_STEP(w)
 #undef WH_MLA_STEP
     }
     for (; d < D; ++d) {
@@ -242,6 +248,7 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   }
   __syncthreads();  // the weights are visible to every thread
   const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * P;
+  const bool w4 = (P & 3) == 0;  // weight rows 16-byte aligned
   float acc = 0.0f;  // a feature chain, or a denominator's weight sum
   if (warp < fw) {
     for (int st = 0; st < nst; ++st) {
@@ -256,9 +263,28 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
       const float* slot = ring + (st % kStages) * kMlaRingRows * kMlaSlice;
       const int r0 = st * kMlaRingRows, rows = min(kMlaRingRows, P - r0);
       if (feature) {
+        if (rows == kMlaRingRows && w4) {
+          // a full stage: the loads of eight rows ahead of their multiplies,
+          // the weights four rows per 16-byte read
+          const float4* wq = reinterpret_cast<const float4*>(w + r0);
+#pragma unroll
+          for (int r = 0; r < kMlaRingRows; r += 8) {
+            const float4 wa = wq[r / 4], wb = wq[r / 4 + 1];
+            float kv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kv[j] = slot[(r + j) * kMlaSlice + fl];
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            float pr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pr[j] = __fmul_rn(wv[j], kv[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, pr[j]);
+          }
+        } else {
 #pragma unroll 8
-        for (int r = 0; r < rows; ++r)
-          acc = __fadd_rn(acc, __fmul_rn(w[r0 + r], slot[r * kMlaSlice + fl]));
+          for (int r = 0; r < rows; ++r)
+            acc = __fadd_rn(acc, __fmul_rn(w[r0 + r], slot[r * kMlaSlice + fl]));
+        }
       }
     }
     cp_async_wait<0>();
