@@ -18,8 +18,8 @@
 // Every sum above is a dependent chain in the reference's order, so the work
 // is spread over chains, never inside one:
 //   mla_scores_kernel  one CTA per (16 positions, 32 heads): lane = head, and
-//                      each thread runs the chains over d of four positions, so
-//                      one 16-byte q read from shared memory serves four chains
+//                      each thread runs the chains over d of two positions, so
+//                      one 16-byte q read from shared memory serves two chains
 //                      and the key reads are warp broadcasts (rows padded by
 //                      16 B so that the 32 lanes' q reads hit distinct banks).
 //                      Writes the scaled scores [P][heads] and the tile's
@@ -42,7 +42,7 @@
 namespace wh {
 
 constexpr int kMlaScoreHeads = 32;  // heads per scores CTA (one per lane)
-constexpr int kMlaScoreChains = 4;  // positions per thread
+constexpr int kMlaScoreChains = 2;  // positions per thread
 constexpr int kMlaScoreTile = 16;   // positions per scores CTA
 constexpr int kMlaScoreThreads = kMlaScoreHeads * kMlaScoreTile / kMlaScoreChains;
 constexpr int kMlaSlice = 64;       // features per output CTA (two warps per head)
@@ -95,49 +95,42 @@ __global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a)
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
-  // lane = head, four positions per thread (rows beyond np are computed on
+  // lane = head, two positions per thread (a row beyond np is computed on
   // whatever the buffer holds and never stored)
   const int r0 = warp * kMlaScoreChains;
   if (lane < nh && r0 < np) {
     const float* qh = q_s + lane * ld;
     const float* kr = k_s + r0 * ld;
-    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    float s0 = 0.0f, s1 = 0.0f;
     int d = 0;
-#pragma unroll 2
+#pragma unroll 4
     for (; d + 4 <= D; d += 4) {
       const float4 qv = *reinterpret_cast<const float4*>(qh + d);
       const float4 k0 = *reinterpret_cast<const float4*>(kr + d);
       const float4 k1 = *reinterpret_cast<const float4*>(kr + ld + d);
-      const float4 k2 = *reinterpret_cast<const float4*>(kr + 2 * ld + d);
-      const float4 k3 = *reinterpret_cast<const float4*>(kr + 3 * ld + d);
-      // the four chains interleaved, so that each addition waits on its own
+      // the two chains interleaved, so that each addition waits on its own
       // chain only
-#define WH_MLA_STEP(C)                                                            \
-  {                                                                               \
-    const float m0 = __fmul_rn(qv.C, k0.C), m1 = __fmul_rn(qv.C, k1.C);           \
-    const float m2 = __fmul_rn(qv.C, k2.C), m3 = __fmul_rn(qv.C, k3.C);           \
-    s0 = __fadd_rn(s0, m0);                                                       \
-    s1 = __fadd_rn(s1, m1);                                                       \
-    s2 = __fadd_rn(s2, m2);                                                       \
-    s3 = __fadd_rn(s3, m3);                                                       \
-  }
-      WH_MLA_STEP(x)
-      WH_MLA_STEP(y)
-      WH_MLA_STEP(z)
-      WH_MLA_STEP(w)
-#undef WH_MLA_STEP
+      const float m0x = __fmul_rn(qv.x, k0.x), m1x = __fmul_rn(qv.x, k1.x);
+      const float m0y = __fmul_rn(qv.y, k0.y), m1y = __fmul_rn(qv.y, k1.y);
+      const float m0z = __fmul_rn(qv.z, k0.z), m1z = __fmul_rn(qv.z, k1.z);
+      const float m0w = __fmul_rn(qv.w, k0.w), m1w = __fmul_rn(qv.w, k1.w);
+      s0 = __fadd_rn(s0, m0x);
+      s1 = __fadd_rn(s1, m1x);
+      s0 = __fadd_rn(s0, m0y);
+      s1 = __fadd_rn(s1, m1y);
+      s0 = __fadd_rn(s0, m0z);
+      s1 = __fadd_rn(s1, m1z);
+      s0 = __fadd_rn(s0, m0w);
+      s1 = __fadd_rn(s1, m1w);
     }
     for (; d < D; ++d) {
       const float qd = qh[d];
       s0 = __fadd_rn(s0, __fmul_rn(qd, kr[d]));
       s1 = __fadd_rn(s1, __fmul_rn(qd, kr[ld + d]));
-      s2 = __fadd_rn(s2, __fmul_rn(qd, kr[2 * ld + d]));
-      s3 = __fadd_rn(s3, __fmul_rn(qd, kr[3 * ld + d]));
     }
-    const float sv[4] = {__fmul_rn(s0, a.scale), __fmul_rn(s1, a.scale),
-                         __fmul_rn(s2, a.scale), __fmul_rn(s3, a.scale)};
+    const float sv[2] = {__fmul_rn(s0, a.scale), __fmul_rn(s1, a.scale)};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
       if (r0 + j < np) {
         a.scores[(long long)(p0 + r0 + j) * H + hb + lane] = sv[j];
         sc_s[(r0 + j) * kMlaScoreHeads + lane] = sv[j];
@@ -217,7 +210,10 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   const int fw = 2 * G;       // feature warps; warp fw is the denominator warp
   const int nfeat = fw * 32;  // threads of the feature warps
   const int f0 = blockIdx.x * kMlaSlice, nf = min(kMlaSlice, D - f0);
-  float* ring = mla_w + ((G * P + 3) & ~3);  // [kStages][kMlaRingRows][kMlaSlice]
+  // weight rows padded to wld = P rounded up to 4, plus 4: the denominator
+  // lanes read distinct banks
+  const int wld = ((P + 3) & ~3) + 4;
+  float* ring = mla_w + G * wld;  // [kStages][kMlaRingRows][kMlaSlice]
   const int nst = (P + kMlaRingRows - 1) / kMlaRingRows;
   const int g = warp >> 1;
   const int fl = (warp & 1) * 32 + lane;  // feature within the slice
@@ -226,11 +222,16 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   pdl_wait_prior();
   // copy group 0, by every thread: the group's weight rows (contiguous [h][P])
   if ((P & 3) == 0) {
-    for (int i = tid; i < G * P / 4; i += blockDim.x)
-      cp_async(mla_w + 4 * i, a.weights + (long long)h0 * P + 4 * i, true);
+    const int q4 = P / 4;
+    for (int i = tid; i < G * q4; i += blockDim.x) {
+      const int gg = i / q4, c = (i - gg * q4) * 4;
+      cp_async(mla_w + gg * wld + c, a.weights + (long long)(h0 + gg) * P + c, true);
+    }
   } else {
-    for (int i = tid; i < G * P; i += blockDim.x)
-      cp_async(mla_w + i, a.weights + (long long)h0 * P + i, false);
+    for (int i = tid; i < G * P; i += blockDim.x) {
+      const int gg = i / P, c = i - gg * P;
+      cp_async(mla_w + gg * wld + c, a.weights + (long long)(h0 + gg) * P + c, false);
+    }
   }
   cp_async_commit();
   // the feature warps own the key ring; its first stages are groups 1 .. S-1
@@ -247,8 +248,7 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
     cp_async_wait<0>();
   }
   __syncthreads();  // the weights are visible to every thread
-  const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * P;
-  const bool w4 = (P & 3) == 0;  // weight rows 16-byte aligned
+  const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * wld;
   float acc = 0.0f;  // a feature chain, or a denominator's weight sum
   if (warp < fw) {
     for (int st = 0; st < nst; ++st) {
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
       const float* slot = ring + (st % kStages) * kMlaRingRows * kMlaSlice;
       const int r0 = st * kMlaRingRows, rows = min(kMlaRingRows, P - r0);
       if (feature) {
-        if (rows == kMlaRingRows && w4) {
+        if (rows == kMlaRingRows) {
           // a full stage: the loads of eight rows ahead of their multiplies,
           // the weights four rows per 16-byte read
           const float4* wq = reinterpret_cast<const float4*>(w + r0);
@@ -335,7 +335,7 @@ bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output) {
     for (int g : {4, 2, 1}) {
       if (H % g) continue;
       const size_t bytes =
-          sizeof(float) * (((size_t)g * P + 3) & ~(size_t)3) + stages * kMlaStageBytes;
+          sizeof(float) * (size_t)g * ((((size_t)P + 3) & ~(size_t)3) + 4) + stages * kMlaStageBytes;
       if (bytes <= kBudget) {
         a.head_group = g;
         a.stages = stages;
