@@ -3,12 +3,13 @@
 
 Integer/index work (router ids) must be identical; fp32 outputs are compared
 bit for bit where the kernel reproduces the reference's association order
-(FP8 GEMV, FP4 matvec, act quant, router logits).  Transcendentals (expf in
-silu and the softmax) are glibc on the reference side and double-precision
-exp rounded to float on the GPU: these agree except when exp(x) sits within
-~1e-16 of a float rounding boundary, so outputs that depend on them are
-checked with the spike gate max_rel < 1e-3 (src/bin/gpu_gemv_spike.rs:201)
-and a normalised-error bound, and the number of bit differences is reported.
+(FP8 GEMV, FP4 matvec, act quant, router logits, the exact expert and MoE
+paths).  The exp in SiLU and in the router's softmax is the host C library's
+expf reproduced on the device (a table measured at context creation), so
+those outputs are bit-exact as well; the spike gate max_rel < 1e-3
+(src/bin/gpu_gemv_spike.rs:201) is checked besides.  The sqrt-softplus
+router's log1p is the device's correctly rounded one where the reference
+calls glibc's log1pf, so its route weights are compared within 2e-6.
 """
 import json
 from pathlib import Path
@@ -319,7 +320,7 @@ def test_fp4_expert_forward_fast_path_bit_exact(ctx, W, hidden, inter):
         got = out.cpu().numpy()
         assert H.max_rel_err(got, want, floor=1e-3 * np.abs(want).max()) < 1e-3
         nd = int(np.sum(bits(got) != bits(want)))
-        assert nd <= hidden // 512, f"{nd} outputs differ from the oracle"
+        assert nd == 0, f"{nd} outputs differ from the oracle"
 
 
 # ---------------------------------------------------------------- router
@@ -340,7 +341,10 @@ def test_router_ids_bit_exact(ctx, W, mode, E, T):
         n, oid, ow, olg = O.router(gate, x[t], K, mode=mode, bias=bias, route_scale=1.5)
         np.testing.assert_array_equal(bits(lg[t]), bits(olg))
         np.testing.assert_array_equal(ids[t], oid)
-        np.testing.assert_allclose(w[t], ow, rtol=2e-6, atol=0)
+        if mode == 0:
+            np.testing.assert_array_equal(bits(w[t]), bits(ow))
+        else:  # log1p of the softplus is the device's, not glibc's log1pf
+            np.testing.assert_allclose(w[t], ow, rtol=2e-6, atol=0)
 
 
 def test_router_kats(ctx, W):
@@ -403,7 +407,7 @@ def test_moe_ffn_config2_vs_oracle(ctx, W, moe_layer):
     for t in range(T):
         n, oid, ow, _ = O.router(gate, x[t], 6, mode=0)
         np.testing.assert_array_equal(ids[t], oid)
-        np.testing.assert_allclose(wts[t], ow, rtol=2e-6, atol=0)
+        np.testing.assert_array_equal(bits(wts[t]), bits(ow))
         keep = []
         arr = (O.Fp4Expert * (E + 1))()
         for e in list(oid) + [E]:
@@ -413,7 +417,7 @@ def test_moe_ffn_config2_vs_oracle(ctx, W, moe_layer):
         scale = float(np.abs(want).max())
         assert np.max(np.abs(y[t] - want)) <= 1e-4 * scale
         total_diff += int(np.sum(bits(y[t]) != bits(want)))
-    assert total_diff <= T * Hd // 256, f"{total_diff} outputs differ from the oracle"
+    assert total_diff == 0, f"{total_diff} outputs differ from the oracle"
 
 
 def test_moe_ffn_batch_equals_single_token(ctx, W, moe_layer):

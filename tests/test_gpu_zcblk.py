@@ -132,7 +132,7 @@ def test_loader_pack_bytes_and_moe_parity(ctx, W, ZB, tmp_path):
         assert st == O.OK
         assert np.max(np.abs(y1[t] - want)) <= 1e-4 * float(np.abs(want).max())
         diff += int(np.sum(y1[t].view(np.uint32) != want.view(np.uint32)))
-    assert diff <= 3 * HID // 256
+    assert diff == 0
     loaded.close()
     direct.close()
     loader.close()
