@@ -1208,7 +1208,7 @@ def run_lm_head(args):
                     "d2h_bytes_per_step": k * 8,
                     "path": "pinned host x -> H2D -> wh_lm_head_topk (C ABI) -> D2H tokens + logits"},
             "gpu_launches": 3 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
         if not args.no_cpu_baseline:
             w_np = w.cpu().numpy().view(np.uint16)
@@ -1225,8 +1225,11 @@ def run_lm_head(args):
     return res
 
 
-# dram bytes per launch from an ncu capture of --ncu-case mla (None until measured)
-MLA_TRAFFIC = None
+# DRAM bytes of one call (the three kernels) from the ncu capture of --ncu-case
+# mla: 2,502,656 + 407,040 + 2,702,592 read, 0 written.  ncu empties the caches
+# before each kernel, so the output kernel's key rows count as DRAM there; in
+# the timed pipeline they are L2 hits.
+MLA_TRAFFIC = 5_612_288
 METRIC_MLA = "MLA attention-core calls/s (one decode token, one DeepSeek-V4 layer, 64 heads)"
 MLA_HEADS, MLA_HD, MLA_NOPE, MLA_POS, MLA_COMP = 64, 512, 448, 4095, 1024
 WORKLOAD_MLA = ("MLA attention core of DeepSeek-V4-Flash (64 heads x 512 = 448 nope + 64 rope), "
@@ -1336,6 +1339,9 @@ def run_mla(args):
     rows = 128 + MLA_COMP
     alg = rows * MLA_HD * 4 + 2 * MLA_HEADS * MLA_HD * 4 + MLA_HEADS * 4
     achieved = alg / (ms_step * 1e-3) / 1e9
+    clocks = clk.summary()
+    sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    chain_us = (MLA_HD + rows) * 4 / sm_mhz
     res = None
     if rank == 0:
         res = {
@@ -1349,15 +1355,18 @@ def run_mla(args):
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algorithmic_bytes": alg, "traffic": MLA_TRAFFIC,
+                         "chain_floor_us": round(chain_us, 3),
+                         "frac_of_chain_floor": round(chain_us / (ms_step * 1e3), 4),
                          "note": "latency-bound: the reference's in-order sums are "
                                  f"dependent chains of {MLA_HD} (scores) and {rows} "
-                                 "(weighted sum) additions"},
+                                 "(weighted sum) additions; chain_floor_us = those "
+                                 "additions at 4 cycles each and the sampled SM clock"},
             "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "calls/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
                     "d2h_bytes_per_step": out.numel() * 4,
                     "path": "pinned host q -> H2D -> wh_mla_attention (C ABI) -> D2H output"},
             "gpu_launches": 3 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
         if not args.no_cpu_baseline:
             host = [t.cpu().numpy() for t in (q, keys, comp, sink)]
