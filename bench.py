@@ -1382,6 +1382,167 @@ def run_mla(args):
     return res
 
 
+METRIC_MHC = "mHC hc_pre + hc_post token-calls/s (DeepSeek-V4 hyper-connections, one sub-block)"
+MHC_HC, MHC_HIDDEN = 4, 4096
+WORKLOAD_MHC = ("mHC of DeepSeek-V4 (hc_mult 4 x hidden 4096, 24 fn rows, 20 Sinkhorn rounds): "
+                "hc_pre (RMS, fn mixes, Sinkhorn split, pooled input) then hc_post "
+                "(redistribution over the 4 residual copies)")
+
+
+def mhc_inputs(dev, seed, T):
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    rows, hc_dim = (2 + MHC_HC) * MHC_HC, MHC_HC * MHC_HIDDEN
+    fn = torch.randn(rows, hc_dim, device=dev, generator=g) * 0.01
+    scale = torch.tensor([0.3, 0.2, 0.5], device=dev)
+    base = torch.randn(rows, device=dev, generator=g) * 0.1
+    x = torch.randn(T, hc_dim, device=dev, generator=g)
+    res = torch.randn(T, hc_dim, device=dev, generator=g)
+    return fn, scale, base, x, res
+
+
+def mhc_cpu(fn, scale, base, x, res, steps):
+    """The oracle's scalar restatement on one host thread: seconds per token-call."""
+    import oracle as O
+
+    t0 = time.perf_counter()
+    n = 0
+    for _ in range(steps):
+        for t in range(x.shape[0]):
+            st, y, post, comb = O.hc_pre(fn, scale, base, x[t], MHC_HC, MHC_HIDDEN)
+            O.hc_post(y, res[t], post, comb, MHC_HC, MHC_HIDDEN)
+            n += 1
+    return (time.perf_counter() - t0) / n
+
+
+def run_mhc(args):
+    import torch
+
+    import wohper_b200 as W
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    T = max(args.mhc_tokens, 1)
+    fn, scale, base, x, res = mhc_inputs(dev, 900 + rank, T)
+    hc_dim = MHC_HC * MHC_HIDDEN
+    cfg = {"workload": WORKLOAD_MHC, "hc_mult": MHC_HC, "hidden": MHC_HIDDEN, "tokens": T,
+           "l2": "flushed between calls (256 MiB memset outside the timed events)",
+           "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+    if args.impl == "reference":
+        res_line = None
+        if rank == 0:
+            host = [t.cpu().numpy() for t in (fn, scale, base, x, res)]
+            sec = mhc_cpu(*host, max(args.steps, 1))
+            v = 1.0 / sec
+            res_line = {"metric": METRIC_MHC, "value": round(v, 2), "unit": "token-calls/s",
+                        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                        "higher_is_better": True, "impl": "reference", "scaling": "weak",
+                        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                        "cpu_baseline": {"value": round(v, 2), "unit": "token-calls/s",
+                                         "cores": 1, "kind": "port",
+                                         "sample": f"{max(args.steps, 1) * T} token-calls"},
+                        "e2e": {"value": round(v, 2), "unit": "token-calls/s",
+                                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return res_line
+
+    ctx = W.Context(local)
+    bufs = (torch.empty(T, MHC_HIDDEN, device=dev), torch.empty(T, MHC_HC, device=dev),
+            torch.empty(T, MHC_HC, MHC_HC, device=dev))
+    out = torch.empty(T, hc_dim, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def call(xd):
+        y, post, comb = W.hc_pre(ctx, fn, scale, base, xd, MHC_HC, MHC_HIDDEN, out=bufs)
+        W.hc_post(ctx, y, res, post, comb, MHC_HC, MHC_HIDDEN, out=out)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(x)
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            call(x)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    xh = x.cpu().pin_memory()
+    xd = torch.empty_like(x)
+    oh = torch.empty(T, hc_dim).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        ev2[i][0].record(stream)
+        xd.copy_(xh, non_blocking=True)
+        call(xd)
+        oh.copy_(out, non_blocking=True)
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = all_max(world, sum(a.elapsed_time(b) for a, b in ev2)) / args.steps
+    peak, peak_kind = peaks()
+    rows = (2 + MHC_HC) * MHC_HC
+    alg = (rows * hc_dim * 4 + rows * 4 + 12 +
+           T * (hc_dim * 4 + MHC_HIDDEN * 4 + (MHC_HC + MHC_HC * MHC_HC) * 4) +
+           T * (MHC_HIDDEN * 4 + 2 * hc_dim * 4 + (MHC_HC + MHC_HC * MHC_HC) * 4))
+    achieved = alg / (ms_step * 1e-3) / 1e9
+    clocks = clk.summary()
+    sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    chain_us = hc_dim * 4 / sm_mhz
+    res_line = None
+    if rank == 0:
+        res_line = {
+            "metric": METRIC_MHC, "value": round(world * T * 1e3 / ms_step, 2),
+            "unit": "token-calls/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (reference operation order, no FMA)",
+            "data": "synthetic (N(0, 0.01) fn rows, N(0, 1) residual copies)", "config": cfg,
+            "roofline": {"kernel": "hc_mix_kernel + hc_post_kernel", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "algorithmic_bytes": alg, "traffic": None,
+                         "chain_floor_us": round(chain_us, 3),
+                         "frac_of_chain_floor": round(chain_us / (ms_step * 1e3), 4),
+                         "note": "latency-bound: the sum of squares and each fn-row dot are "
+                                 f"chains of {hc_dim} dependent additions in the "
+                                 "reference's order; chain_floor_us = one such chain at "
+                                 "4 cycles an addition and the sampled SM clock"},
+            "e2e": {"value": round(world * T * 1e3 / e2e_ms, 2), "unit": "token-calls/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": x.numel() * 4,
+                    "d2h_bytes_per_step": out.numel() * 4,
+                    "path": "pinned host x -> H2D -> wh_hc_pre + wh_hc_post (C ABI) -> D2H"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline:
+            host = [t.cpu().numpy() for t in (fn, scale, base, x, res)]
+            sec = mhc_cpu(*host, 3)
+            res_line["cpu_baseline"] = {"value": round(1.0 / sec, 2), "unit": "token-calls/s",
+                                        "cores": 1, "kind": "port",
+                                        "sample": f"{3 * T} token-calls of the oracle's scalar "
+                                                  "restatement"}
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res_line
+
+
 def run_ncu_case(args):
     """Small single-GPU workloads for ncu captures (no JSON bench line).
 
@@ -1395,6 +1556,7 @@ def run_ncu_case(args):
     lmhead: the BF16 lm_head top-50 on 32768 x 4096 (268 MB of weights),
            logits + candidates + selection per step.
     mla:   the MLA attention core at the bench's shape (10 MB of cache rows).
+    mhc:   hc_pre + hc_post of one token at the bench's shape.
     L2 is flushed (256 MiB memset) before every step."""
     import torch
 
@@ -1404,7 +1566,13 @@ def run_ncu_case(args):
     ctx = W.Context(0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     n = args.warmup + args.steps
-    if args.ncu_case == "mla":
+    if args.ncu_case == "mhc":
+        fn, scale, base, x, res = mhc_inputs(torch.device("cuda", 0), 6, 1)
+        for _ in range(n):
+            flush.zero_()
+            y, post, comb = W.hc_pre(ctx, fn, scale, base, x, MHC_HC, MHC_HIDDEN)
+            W.hc_post(ctx, y, res, post, comb, MHC_HC, MHC_HIDDEN)
+    elif args.ncu_case == "mla":
         q, keys, comp, sink = mla_inputs(torch.device("cuda", 0), 5)
         theta, yarn = W.deepseek_rope_for_layer(2)
         fr = W.rope_inv_freqs(MLA_HD - MLA_NOPE, theta, yarn)
@@ -1482,20 +1650,22 @@ def main():
                          "4: expert-parallel layer over the ranks")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="config 4: rows over NVLink peer stores (p2p) or NCCL all-to-all")
-    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head", "mla"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head", "mla", "mhc"],
                     help="moe: the MoE FFN step of --config (default); expert-load: one "
                          "layer's FP4 experts from an experts pack on disk into HBM; lm-head: "
                          "the BF16 lm_head top-k over the DeepSeek vocabulary; mla: the MLA "
-                         "attention core of one DeepSeek-V4 layer at token 4095")
+                         "attention core of one DeepSeek-V4 layer at token 4095; mhc: hc_pre + "
+                         "hc_post of one DeepSeek-V4 sub-block")
     ap.add_argument("--load-threads", type=int, default=8,
                     help="expert-load: reader threads of the expert loader")
     ap.add_argument("--direct-io", action="store_true",
                     help="expert-load: O_DIRECT reads (bypass the page cache)")
     ap.add_argument("--lm-top-k", type=int, default=50, help="lm-head: top_k")
+    ap.add_argument("--mhc-tokens", type=int, default=1, help="mhc: tokens per call")
     ap.add_argument("--shared", default="fp4", choices=["fp4", "fp8"],
                     help="config 2: the shared expert's format (fp4, as BASELINE's config 2; "
                          "fp8: DeepSeek-V4's FP8 shared expert)")
-    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead", "mla"],
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead", "mla", "mhc"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
     if args.ncu_case:
@@ -1508,6 +1678,8 @@ def main():
         res = run_lm_head(args)
     elif args.workload == "mla":
         res = run_mla(args)
+    elif args.workload == "mhc":
+        res = run_mhc(args)
     elif args.config == 3 and args.impl == "ours":
         res = run_config3(args)
     elif args.config == 4 and args.impl == "ours":

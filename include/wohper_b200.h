@@ -393,6 +393,34 @@ wh_status wh_mla_attention(wh_ctx* ctx, const float* q, int heads, int head_dim,
                            const float* inv_freqs, float* out, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* mHC hyper-connections (DeepSeek-V4)                                         */
+/* ------------------------------------------------------------------------ */
+/* The residual stream of a layer is hc copies of the hidden vector: x is
+ * [tokens][hc][hidden] f32 (hc_dim = hc * hidden per token).  All pointers are
+ * device pointers; every result is bit-exact to the reference (sums in index
+ * order without fused multiply-adds, exp = the host C library's expf).
+ * Errors: InvalidShape (tokens, hc or hidden < 1, negative sinkhorn_iters),
+ * Unsupported (hc > 8), InvalidPointer. */
+
+/* Replaces hc_pre_into + hc_split_sinkhorn_scalar (src/compute.rs:4945-5053)
+ * for each token: fn [(2 + hc) * hc][hc_dim], scale [3], base [(2 + hc) * hc];
+ * outputs y [tokens][hidden] (the sub-block input), post [tokens][hc] and
+ * comb [tokens][hc][hc] for the matching wh_hc_post. */
+wh_status wh_hc_pre(wh_ctx* ctx, const float* fn, const float* scale, const float* base,
+                    const float* x, int tokens, int hc, int hidden, int sinkhorn_iters,
+                    float eps, float* y, float* post, float* comb, wh_stream_t stream);
+/* Replaces hc_post_into (src/compute.rs:5055-5089): out[t][k] = post[t][k] y[t] +
+ * sum_i comb[t][k][i] residual[t][i]; out [tokens][hc][hidden]. */
+wh_status wh_hc_post(wh_ctx* ctx, const float* y, const float* residual, const float* post,
+                     const float* comb, int tokens, int hc, int hidden, float* out,
+                     wh_stream_t stream);
+/* Replaces hc_head_pool (src/compute.rs:5091-5132): fn [hc][hc_dim], base [hc],
+ * the scalar scale; pooled [tokens][hidden]. */
+wh_status wh_hc_head(wh_ctx* ctx, const float* fn, float scale, const float* base, const float* x,
+                     int tokens, int hc, int hidden, float eps, float* pooled,
+                     wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* BF16 lm_head top-k                                                         */
 /* ------------------------------------------------------------------------ */
 /* Device scratch bytes wh_lm_head_topk needs. */

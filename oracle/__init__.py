@@ -106,6 +106,14 @@ def lib() -> C.CDLL:
         L.orc_rope_inv_freqs.restype = None
         L.orc_mla_attention.argtypes = [vp, sz, sz, sz, vp, sz, sz, sz, vp, sz, vp, vp, vp]
         L.orc_mla_attention.restype = None
+        L.orc_hc_split_sinkhorn.argtypes = [vp, sz, vp, sz, vp, sz, sz, sz, f, vp, vp, vp]
+        L.orc_hc_split_sinkhorn.restype = i
+        L.orc_hc_pre.argtypes = [vp, sz, sz, vp, sz, vp, vp, sz, sz, sz, f, vp, vp, vp]
+        L.orc_hc_pre.restype = i
+        L.orc_hc_post.argtypes = [vp, vp, vp, vp, vp, sz, sz]
+        L.orc_hc_post.restype = None
+        L.orc_hc_head.argtypes = [vp, f, vp, vp, sz, sz, f, vp]
+        L.orc_hc_head.restype = None
         L.orc_fp4_matvec.argtypes = [C.POINTER(Fp4Spec), vp, sz, vp, sz, i]
         L.orc_fp4_matvec.restype = i
         L.orc_fp4_expert_forward.argtypes = [C.POINTER(Fp4Expert), vp, sz, vp, sz, vp, sz]
@@ -245,6 +253,45 @@ def rope_inv_freqs(rope_dim, theta, yarn=None):
     fa, bf, bs, osl = yarn if yarn else (0.0, 0.0, 0.0, 0)
     lib().orc_rope_inv_freqs(rope_dim, theta, fa, bf, bs, osl, _p(out))
     return out
+
+
+def hc_split_sinkhorn(mixes, scale, base, hc, iters=20, eps=1e-6):
+    """hc_split_sinkhorn_scalar (src/compute.rs:4945-4991) -> (status, pre, post, comb)."""
+    m, sc, b = _c(mixes, np.float32), _c(scale, np.float32), _c(base, np.float32)
+    pre, post = np.zeros(hc, np.float32), np.zeros(hc, np.float32)
+    comb = np.zeros(hc * hc, np.float32)
+    st = lib().orc_hc_split_sinkhorn(_p(m), m.size, _p(sc), sc.size, _p(b), b.size, hc, iters,
+                                     eps, _p(pre), _p(post), _p(comb))
+    return st, pre, post, comb
+
+
+def hc_pre(fn, scale, base, x, hc, hidden, iters=20, eps=1e-6):
+    """hc_pre_into (src/compute.rs:5016-5053) for one token: fn [mix_hc, hc*hidden],
+    x [hc*hidden] -> (status, y [hidden], post [hc], comb [hc*hc])."""
+    fn, sc, b, x = (_c(fn, np.float32), _c(scale, np.float32), _c(base, np.float32),
+                    _c(x, np.float32))
+    y = np.zeros(hidden, np.float32)
+    post, comb = np.zeros(hc, np.float32), np.zeros(hc * hc, np.float32)
+    st = lib().orc_hc_pre(_p(fn), fn.shape[0], fn.shape[1], _p(sc), sc.size, _p(b), _p(x), hc,
+                          hidden, iters, eps, _p(y), _p(post), _p(comb))
+    return st, y, post, comb
+
+
+def hc_post(y, residual, post, comb, hc, hidden):
+    """hc_post_into (src/compute.rs:5055-5089) for one token -> out [hc*hidden]."""
+    y, r, p, c = (_c(y, np.float32), _c(residual, np.float32), _c(post, np.float32),
+                  _c(comb, np.float32))
+    out = np.zeros(hc * hidden, np.float32)
+    lib().orc_hc_post(_p(y), _p(r), _p(p), _p(c), _p(out), hc, hidden)
+    return out
+
+
+def hc_head(fn, scale, base, x, hc, hidden, eps=1e-6):
+    """hc_head_pool (src/compute.rs:5091-5132) for one token -> pooled [hidden]."""
+    fn, b, x = _c(fn, np.float32), _c(base, np.float32), _c(x, np.float32)
+    pooled = np.zeros(hidden, np.float32)
+    lib().orc_hc_head(_p(fn), float(scale), _p(b), _p(x), hc, hidden, eps, _p(pooled))
+    return pooled
 
 
 def mla_attention(q, keys, token_pos, window, compressed, sink, inv_freqs, nope_dim):

@@ -828,6 +828,122 @@ size_t orc_deepseek_sqrtsoftplus_route(const float* logits, size_t n, const floa
   return k;
 }
 
+// ---------------------------------------------------------------------------
+// mHC hyper-connections (src/compute.rs:4945-5132)
+
+static inline float hc_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// normalize_comb_rows / normalize_comb_cols (src/compute.rs:4993-5013)
+static void hc_norm_rows(float* comb, size_t hc, float eps) {
+  for (size_t j = 0; j < hc; ++j) {
+    float sum = 0.0f;  // row.iter().sum(): in order
+    for (size_t k = 0; k < hc; ++k) sum += comb[j * hc + k];
+    for (size_t k = 0; k < hc; ++k) comb[j * hc + k] /= sum + eps;
+  }
+}
+static void hc_norm_cols(float* comb, size_t hc, float eps) {
+  for (size_t k = 0; k < hc; ++k) {
+    float sum = 0.0f;
+    for (size_t j = 0; j < hc; ++j) sum += comb[j * hc + k];
+    for (size_t j = 0; j < hc; ++j) comb[j * hc + k] /= sum + eps;
+  }
+}
+
+// hc_split_sinkhorn_scalar (src/compute.rs:4945-4991)
+int orc_hc_split_sinkhorn(const float* mixes, size_t mixes_len, const float* scale,
+                          size_t scale_len, const float* base, size_t base_len, size_t hc,
+                          size_t iters, float eps, float* pre, float* post, float* comb) {
+  size_t mix_hc = (2 + hc) * hc;
+  if (mixes_len < mix_hc || base_len < mix_hc || scale_len < 3) return ORC_ERR_INVALID_SHAPE;
+  for (size_t j = 0; j < hc; ++j) {
+    pre[j] = hc_sigmoid(mixes[j] * scale[0] + base[j]) + eps;
+    post[j] = 2.0f * hc_sigmoid(mixes[j + hc] * scale[1] + base[j + hc]);
+  }
+  for (size_t j = 0; j < hc; ++j)
+    for (size_t k = 0; k < hc; ++k)
+      comb[j * hc + k] = mixes[2 * hc + j * hc + k] * scale[2] + base[2 * hc + j * hc + k];
+  for (size_t j = 0; j < hc; ++j) {
+    float* row = comb + j * hc;
+    float mx = -INFINITY;  // fold(NEG_INFINITY, f32::max): NaN-ignoring
+    for (size_t k = 0; k < hc; ++k) mx = std::fmax(mx, row[k]);
+    float sum = 0.0f;
+    for (size_t k = 0; k < hc; ++k) {
+      row[k] = expf(row[k] - mx);
+      sum += row[k];
+    }
+    for (size_t k = 0; k < hc; ++k) row[k] = row[k] / sum + eps;
+  }
+  hc_norm_cols(comb, hc, eps);
+  for (size_t it = 1; it < iters; ++it) {
+    hc_norm_rows(comb, hc, eps);
+    hc_norm_cols(comb, hc, eps);
+  }
+  return ORC_OK;
+}
+
+// sum of squares / hc_dim, then 1 / sqrt(. + eps) (src/compute.rs:5028-5034)
+static float hc_inv_rms(const float* x, size_t hc_dim, float eps) {
+  float sum = 0.0f;
+  for (size_t i = 0; i < hc_dim; ++i) sum += x[i] * x[i];
+  float mean_square = sum / (float)hc_dim;
+  return 1.0f / std::sqrt(mean_square + eps);
+}
+
+// dot_f32_row (src/compute.rs:4875-4884)
+static float hc_dot(const float* row, const float* x, size_t n) {
+  float acc = 0.0f;
+  for (size_t i = 0; i < n; ++i) acc += row[i] * x[i];
+  return acc;
+}
+
+// hc_pre_into (src/compute.rs:5016-5053)
+int orc_hc_pre(const float* fn, size_t mix_hc, size_t fn_hc_dim, const float* scale,
+               size_t scale_len, const float* base, const float* x, size_t hc, size_t hidden,
+               size_t iters, float eps, float* y, float* post, float* comb) {
+  size_t hc_dim = hc * hidden;
+  if (fn_hc_dim != hc_dim) return ORC_ERR_INVALID_SHAPE;
+  float inv_rms = hc_inv_rms(x, hc_dim, eps);
+  std::vector<float> mixes(mix_hc), pre(hc);
+  for (size_t j = 0; j < mix_hc; ++j) mixes[j] = hc_dot(fn + j * hc_dim, x, hc_dim) * inv_rms;
+  int st = orc_hc_split_sinkhorn(mixes.data(), mix_hc, scale, scale_len, base, mix_hc, hc, iters,
+                                 eps, pre.data(), post, comb);
+  if (st != ORC_OK) return st;
+  for (size_t d = 0; d < hidden; ++d) {
+    float acc = 0.0f;
+    for (size_t i = 0; i < hc; ++i) acc += pre[i] * x[i * hidden + d];
+    y[d] = acc;
+  }
+  return ORC_OK;
+}
+
+// hc_post_into (src/compute.rs:5055-5089): out[k] = post[k] y + sum_i comb[k][i] res[i]
+void orc_hc_post(const float* y, const float* residual, const float* post, const float* comb,
+                 float* out, size_t hc, size_t hidden) {
+  for (size_t k = 0; k < hc; ++k)
+    for (size_t d = 0; d < hidden; ++d) {
+      float acc = post[k] * y[d];
+      for (size_t i = 0; i < hc; ++i) acc += comb[k * hc + i] * residual[i * hidden + d];
+      out[k * hidden + d] = acc;
+    }
+}
+
+// hc_head_pool (src/compute.rs:5091-5132)
+void orc_hc_head(const float* fn, float scale, const float* base, const float* x, size_t hc,
+                 size_t hidden, float eps, float* pooled) {
+  size_t hc_dim = hc * hidden;
+  float inv_rms = hc_inv_rms(x, hc_dim, eps);
+  std::vector<float> pre(hc);
+  for (size_t j = 0; j < hc; ++j) {
+    float mix = hc_dot(fn + j * hc_dim, x, hc_dim) * inv_rms;
+    pre[j] = hc_sigmoid(mix * scale + base[j]) + eps;
+  }
+  for (size_t d = 0; d < hidden; ++d) {
+    float acc = 0.0f;
+    for (size_t i = 0; i < hc; ++i) acc += pre[i] * x[i * hidden + d];
+    pooled[d] = acc;
+  }
+}
+
 void orc_expf_n(const float* x, float* y, size_t n) {
   for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
 }

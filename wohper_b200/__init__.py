@@ -74,7 +74,8 @@ EXPORTS = (
     "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
     "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
     "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward", "wh_rope_inv_freqs",
-    "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf",
+    "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf", "wh_hc_pre",
+    "wh_hc_post", "wh_hc_head",
 )
 
 
@@ -174,6 +175,9 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_rope_inv_freqs": (None, [i, f, f, f, f, C.c_uint64, vp]),
         "wh_debug_expf_table": (i, [C.POINTER(vp), C.POINTER(vp)]),
         "wh_debug_ref_expf": (st, [vp, vp, vp, sz, vp]),
+        "wh_hc_pre": (st, [vp, vp, vp, vp, vp, i, i, i, i, f, vp, vp, vp, vp]),
+        "wh_hc_post": (st, [vp, vp, vp, vp, vp, i, i, i, vp, vp]),
+        "wh_hc_head": (st, [vp, vp, f, vp, vp, i, i, i, f, vp, vp]),
         "wh_mla_attention": (st, [vp, vp, i, i, i, vp, i, i, i, vp, i, vp, vp, vp, vp]),
         "wh_fp8_expert_scratch_len": (sz, [sz, sz]),
         "wh_fp8_expert_forward": (st, [vp, C.POINTER(Fp8ExpertSpec), vp, sz, vp, sz, vp, sz,
@@ -496,6 +500,59 @@ def mla_attention(ctx: Context, q, keys, token_pos: int, inv_freqs, nope_dim: in
                                   keys.stride(0), token_pos, window, _ptr(compressed), cc,
                                   _ptr(sink), fr.ctypes.data if fr.size else None, _ptr(out),
                                   _stream(stream)))
+    return out
+
+
+# DeepSeek-V4's hyper-connection settings (src/compute.rs ComputeConfig)
+DEEPSEEK_V4_HC_MULT = 4
+DEEPSEEK_V4_HC_SINKHORN_ITERS = 20
+DEEPSEEK_V4_HC_EPS = 1.0e-6
+
+
+def hc_pre(ctx: Context, fn, scale, base, x, hc: int, hidden: int,
+           sinkhorn_iters: int = DEEPSEEK_V4_HC_SINKHORN_ITERS,
+           eps: float = DEEPSEEK_V4_HC_EPS, out=None, stream=None):
+    """hc_pre_into + hc_split_sinkhorn_scalar (src/compute.rs:4945-5053) on the
+    device for x [tokens, hc * hidden] f32: returns (y [tokens, hidden],
+    post [tokens, hc], comb [tokens, hc, hc]).  fn [(2 + hc) * hc, hc * hidden],
+    scale [3] and base [(2 + hc) * hc] are f32 device tensors."""
+    import torch
+
+    tokens = x.shape[0]
+    dev = x.device
+    if out is None:
+        out = (torch.empty(tokens, hidden, device=dev), torch.empty(tokens, hc, device=dev),
+               torch.empty(tokens, hc, hc, device=dev))
+    y, post, comb = out
+    _check(lib().wh_hc_pre(ctx.handle, _ptr(fn), _ptr(scale), _ptr(base), _ptr(x), tokens, hc,
+                           hidden, sinkhorn_iters, eps, _ptr(y), _ptr(post), _ptr(comb),
+                           _stream(stream)))
+    return y, post, comb
+
+
+def hc_post(ctx: Context, y, residual, post, comb, hc: int, hidden: int, out=None,
+            stream=None):
+    """hc_post_into (src/compute.rs:5055-5089): out [tokens, hc * hidden]."""
+    import torch
+
+    tokens = y.shape[0]
+    if out is None:
+        out = torch.empty(tokens, hc * hidden, device=y.device)
+    _check(lib().wh_hc_post(ctx.handle, _ptr(y), _ptr(residual), _ptr(post), _ptr(comb),
+                            tokens, hc, hidden, _ptr(out), _stream(stream)))
+    return out
+
+
+def hc_head(ctx: Context, fn, scale: float, base, x, hc: int, hidden: int,
+            eps: float = DEEPSEEK_V4_HC_EPS, out=None, stream=None):
+    """hc_head_pool (src/compute.rs:5091-5132): pooled [tokens, hidden]."""
+    import torch
+
+    tokens = x.shape[0]
+    if out is None:
+        out = torch.empty(tokens, hidden, device=x.device)
+    _check(lib().wh_hc_head(ctx.handle, _ptr(fn), float(scale), _ptr(base), _ptr(x), tokens,
+                            hc, hidden, eps, _ptr(out), _stream(stream)))
     return out
 
 

@@ -839,6 +839,79 @@ wh_status wh_mla_attention(wh_ctx* c, const float* q, int heads, int head_dim, i
 }
 
 // ---------------------------------------------------------------------------
+// mHC hyper-connections (src/compute.rs:4945-5132)
+static wh_status hc_common_check(wh_ctx* c, int tokens, int hc, int hidden) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  if (tokens < 1 || hc < 1 || hidden < 1) return fail(WH_ERR_INVALID_SHAPE, "hc sizes");
+  if (hc > kHcMaxHc) return fail(WH_ERR_UNSUPPORTED, "hc_mult > 8");
+  if ((long long)hc * hidden > (1LL << 30)) return fail(WH_ERR_INVALID_SHAPE, "hc_dim too large");
+  return WH_OK;
+}
+
+static bool hc_al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+wh_status wh_hc_pre(wh_ctx* c, const float* fn, const float* scale, const float* base,
+                    const float* x, int tokens, int hc, int hidden, int sinkhorn_iters,
+                    float eps, float* y, float* post, float* comb, wh_stream_t stream) {
+  if (wh_status st = hc_common_check(c, tokens, hc, hidden)) return st;
+  if (sinkhorn_iters < 0) return fail(WH_ERR_INVALID_SHAPE, "sinkhorn_iters < 0");
+  if (!fn || !scale || !base || !x || !y || !post || !comb)
+    return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  HcArgs a{};
+  a.fn = fn;
+  a.scale = scale;
+  a.base = base;
+  a.x = x;
+  a.y = y;
+  a.post = post;
+  a.comb = comb;
+  a.tokens = tokens;
+  a.hc = hc;
+  a.hidden = hidden;
+  a.iters = sinkhorn_iters;
+  a.eps = eps;
+  a.head = 0;
+  a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
+  cudaSetDevice(c->device);
+  WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
+  return WH_OK;
+}
+
+wh_status wh_hc_post(wh_ctx* c, const float* y, const float* residual, const float* post,
+                     const float* comb, int tokens, int hc, int hidden, float* out,
+                     wh_stream_t stream) {
+  if (wh_status st = hc_common_check(c, tokens, hc, hidden)) return st;
+  if (!y || !residual || !post || !comb || !out)
+    return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  HcPostArgs a{y, residual, post, comb, out, tokens, hc, hidden};
+  cudaSetDevice(c->device);
+  WH_CUDA(launch_hc_post(a, c->num_sms, (cudaStream_t)stream));
+  return WH_OK;
+}
+
+wh_status wh_hc_head(wh_ctx* c, const float* fn, float scale, const float* base, const float* x,
+                     int tokens, int hc, int hidden, float eps, float* pooled,
+                     wh_stream_t stream) {
+  if (wh_status st = hc_common_check(c, tokens, hc, hidden)) return st;
+  if (!fn || !base || !x || !pooled) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  HcArgs a{};
+  a.fn = fn;
+  a.base = base;
+  a.x = x;
+  a.y = pooled;
+  a.tokens = tokens;
+  a.hc = hc;
+  a.hidden = hidden;
+  a.eps = eps;
+  a.head = 1;
+  a.head_scale = scale;
+  a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
+  cudaSetDevice(c->device);
+  WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
+  return WH_OK;
+}
+
+// ---------------------------------------------------------------------------
 size_t wh_lm_head_scratch_bytes(long long rows, int top_k) {
   return lm_head_scratch_bytes(rows < 1 ? 1 : rows, top_k < 1 ? 1 : top_k);
 }

@@ -62,6 +62,31 @@ __device__ __forceinline__ float libm_expf(float x) { return ref_expf(x, c_expf)
 bool install_expf_table(cudaError_t* err);
 cudaError_t launch_ref_expf(const float* x, float* y, long long n, cudaStream_t s);
 
+// ---------------- mHC hyper-connections ----------------
+constexpr int kHcMaxHc = 8;
+constexpr int kHcMaxMix = (2 + kHcMaxHc) * kHcMaxHc;
+struct HcArgs {
+  const float* fn;     // [rows][hc * hidden]: (2 + hc) * hc rows (hc_pre) or hc (hc_head)
+  const float* scale;  // [3] (hc_pre)
+  const float* base;   // [rows]
+  const float* x;      // [tokens][hc * hidden]
+  float* y;            // [tokens][hidden]
+  float* post;         // [tokens][hc] (hc_pre)
+  float* comb;         // [tokens][hc][hc] (hc_pre)
+  int tokens, hc, hidden, iters, head, vec4;
+  float eps, head_scale;
+};
+struct HcPostArgs {
+  const float* y;         // [tokens][hidden]
+  const float* residual;  // [tokens][hc * hidden]
+  const float* post;      // [tokens][hc]
+  const float* comb;      // [tokens][hc][hc]
+  float* out;             // [tokens][hc * hidden]
+  int tokens, hc, hidden;
+};
+cudaError_t launch_hc_mix(const HcArgs& a, cudaStream_t s);
+cudaError_t launch_hc_post(const HcPostArgs& a, int num_sms, cudaStream_t s);
+
 // ---------------- MLA attention core ----------------
 struct MlaArgs {
   const float* q;           // [heads][head_dim]

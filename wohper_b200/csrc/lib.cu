@@ -5,6 +5,7 @@
 #include "decode.cu"
 #include "libm_exact.cu"
 #include "mla.cu"
+#include "mhc.cu"
 #include "grouped.cu"
 #include "ep.cu"
 #include "lmhead.cu"
