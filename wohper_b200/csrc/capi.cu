@@ -872,6 +872,7 @@ wh_status wh_hc_pre(wh_ctx* c, const float* fn, const float* scale, const float*
   a.eps = eps;
   a.head = 0;
   a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
+  a.chunk = hc_chunk((2 + hc) * hc);
   cudaSetDevice(c->device);
   WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
   return WH_OK;
@@ -906,6 +907,7 @@ wh_status wh_hc_head(wh_ctx* c, const float* fn, float scale, const float* base,
   a.head = 1;
   a.head_scale = scale;
   a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
+  a.chunk = hc_chunk(hc);
   cudaSetDevice(c->device);
   WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
   return WH_OK;

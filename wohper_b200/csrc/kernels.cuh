@@ -73,9 +73,10 @@ struct HcArgs {
   float* y;            // [tokens][hidden]
   float* post;         // [tokens][hc] (hc_pre)
   float* comb;         // [tokens][hc][hc] (hc_pre)
-  int tokens, hc, hidden, iters, head, vec4;
+  int tokens, hc, hidden, iters, head, vec4, chunk;
   float eps, head_scale;
 };
+int hc_chunk(int rows);
 struct HcPostArgs {
   const float* y;         // [tokens][hidden]
   const float* residual;  // [tokens][hc * hidden]
