@@ -399,6 +399,8 @@ wh_status wh_mla_attention(wh_ctx* ctx, const float* q, int heads, int head_dim,
  * [tokens][hc][hidden] f32 (hc_dim = hc * hidden per token).  All pointers are
  * device pointers; every result is bit-exact to the reference (sums in index
  * order without fused multiply-adds, exp = the host C library's expf).
+ * wh_hc_pre and wh_hc_head keep their chain results in a context-owned
+ * workspace: calls on one context are serialised by the caller.
  * Errors: InvalidShape (tokens, hc or hidden < 1, negative sinkhorn_iters),
  * Unsupported (hc > 8), InvalidPointer. */
 

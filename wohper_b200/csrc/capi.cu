@@ -299,6 +299,17 @@ struct wh_ctx {
     return WH_OK;
   }
 
+  void* hc_work = nullptr;  // mHC chain results
+  size_t hc_work_bytes = 0;
+  wh_status ensure_hc_work(size_t bytes) {
+    if (bytes <= hc_work_bytes) return WH_OK;
+    if (hc_work) cudaFree(hc_work);
+    hc_work = nullptr;
+    hc_work_bytes = 0;
+    WH_CUDA(cudaMalloc(&hc_work, bytes));
+    hc_work_bytes = bytes;
+    return WH_OK;
+  }
   void* mla_work = nullptr;  // MLA scores and tile maxima
   size_t mla_work_bytes = 0;
   wh_status ensure_mla_work(size_t bytes) {
@@ -406,6 +417,7 @@ void wh_ctx_destroy(wh_ctx* c) {
   if (c->blk_counters) cudaFree(c->blk_counters);
   if (c->work) cudaFree(c->work);
   if (c->mla_work) cudaFree(c->mla_work);
+  if (c->hc_work) cudaFree(c->hc_work);
   delete c;
 }
 
@@ -872,8 +884,9 @@ wh_status wh_hc_pre(wh_ctx* c, const float* fn, const float* scale, const float*
   a.eps = eps;
   a.head = 0;
   a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
-  a.chunk = hc_chunk((2 + hc) * hc);
   cudaSetDevice(c->device);
+  if (wh_status st = c->ensure_hc_work(hc_dots_bytes(tokens, (2 + hc) * hc))) return st;
+  a.dots = (float*)c->hc_work;
   WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
   return WH_OK;
 }
@@ -907,8 +920,9 @@ wh_status wh_hc_head(wh_ctx* c, const float* fn, float scale, const float* base,
   a.head = 1;
   a.head_scale = scale;
   a.vec4 = (hc * hidden) % 4 == 0 && hc_al16(fn) && hc_al16(x);
-  a.chunk = hc_chunk(hc);
   cudaSetDevice(c->device);
+  if (wh_status st = c->ensure_hc_work(hc_dots_bytes(tokens, hc))) return st;
+  a.dots = (float*)c->hc_work;
   WH_CUDA(launch_hc_mix(a, (cudaStream_t)stream));
   return WH_OK;
 }

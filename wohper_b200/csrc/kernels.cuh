@@ -73,10 +73,11 @@ struct HcArgs {
   float* y;            // [tokens][hidden]
   float* post;         // [tokens][hc] (hc_pre)
   float* comb;         // [tokens][hc][hc] (hc_pre)
-  int tokens, hc, hidden, iters, head, vec4, chunk;
+  float* dots;         // scratch [tokens][rows + 1]: x . x, then fn_j . x
+  int tokens, hc, hidden, iters, head, vec4;
   float eps, head_scale;
 };
-int hc_chunk(int rows);
+size_t hc_dots_bytes(int tokens, int rows);
 struct HcPostArgs {
   const float* y;         // [tokens][hidden]
   const float* residual;  // [tokens][hc * hidden]

@@ -13,21 +13,18 @@
 // (no fused multiply-add), and its exp is the host libm's expf (libm_expf).
 //
 // The sum of squares and the fn-row dots are dependent chains of hc_dim
-// additions (16384 for V4: about 33 us at 4 cycles an add), so one CTA per
-// token runs them side by side, one thread per chain (chain 0 is x . x, so
-// every chain lane runs the same instruction stream).  The chains consume
-// 25 rows x 4 B per 4 cycles, about 50 GB/s for one SM: the columns of x and
-// of the fn rows stream through a 3-stage cp.async ring of 512-column chunks
-// that all 256 threads fill, so about 100 KB are in flight.  The Sinkhorn
-// split runs on one thread; the pooled output, and hc_post, are elementwise
-// over all threads.
+// additions (16384 for V4: about 33 us at 4 cycles an add).  hc_dots_kernel
+// runs each chain in a CTA of its own (25 CTAs per token for V4); the split
+// kernel then runs the Sinkhorn (or the head gates) on one thread and the
+// pooled output over all threads; hc_post is elementwise.
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace wh {
 
 constexpr int kHcThreads = 256;
-constexpr int kHcStages = 3;
+constexpr int kHcChunk = 512;  // columns per ring stage
+constexpr int kHcRing = 8;     // ring stages (32 KB of shared memory)
 
 __device__ __forceinline__ float hc_sigmoid(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, libm_expf(-x)));
@@ -46,53 +43,53 @@ __device__ __forceinline__ void hc_cp_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Stage st of the ring: columns [st * chunk, +chunk) of x (row 0) and of the
-// fn rows (rows 1 .. rows), copied by every thread of the CTA.
-__device__ __forceinline__ void hc_issue_stage(const HcArgs& a, const float* x, float* slot,
-                                               int st, int rows, int hc_dim) {
-  const int chunk = a.chunk, ld = chunk + 4;
-  const int c0 = st * chunk, ncol = min(chunk, hc_dim - c0);
-  const int cw = a.vec4 ? 4 : 1;
-  const int per_row = (ncol + cw - 1) / cw;
-  for (int i = threadIdx.x; i < (rows + 1) * per_row; i += blockDim.x) {
-    const int r = i / per_row, c = (i - r * per_row) * cw;
-    const float* src = r == 0 ? x + c0 + c : a.fn + (long long)(r - 1) * hc_dim + c0 + c;
-    hc_cp_async(slot + r * ld + c, src, a.vec4);
-  }
-}
-
-// hc_pre (head == 0) or hc_head (head == 1) for token blockIdx.x
-__global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(HcArgs a) {
-  extern __shared__ __align__(16) float hc_ring[];  // [kHcStages][rows + 1][chunk + 4]
-  __shared__ float s_dot[1 + kHcMaxMix];
-  __shared__ float s_pre[kHcMaxHc], s_post[kHcMaxHc], s_comb[kHcMaxHc * kHcMaxHc];
-  const int t = blockIdx.x, tid = threadIdx.x;
-  const int hc = a.hc, hidden = a.hidden, hc_dim = hc * hidden;
-  const int rows = a.head ? hc : (2 + hc) * hc;
+// One chain per CTA: CTA (c, t) computes chain c of token t -- c = 0 is x . x,
+// c = 1 + j is fn_j . x -- with the columns of its row and of x streamed
+// through a cp.async ring that the whole CTA fills (one 16-byte copy per
+// thread per stage); thread 0 runs the chain.  One SM alone cannot keep enough
+// plain loads in flight to feed 25 chains from HBM, so the chains are spread
+// over 25 SMs, each needing about 4 GB/s.
+__global__ void __launch_bounds__(kHcThreads) hc_dots_kernel(HcArgs a) {
+  __shared__ __align__(16) float ring[kHcRing][2][kHcChunk];
+  const int c = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+  const int hc_dim = a.hc * a.hidden;
+  const int rows = a.head ? a.hc : (2 + a.hc) * a.hc;
   const float* x = a.x + (long long)t * hc_dim;
-  const int ld = a.chunk + 4, slot_floats = (rows + 1) * ld;
-  const int nst = (hc_dim + a.chunk - 1) / a.chunk;
+  const float* w = c == 0 ? x : a.fn + (long long)(c - 1) * hc_dim;
+  const int nst = (hc_dim + kHcChunk - 1) / kHcChunk;
   pdl_wait_prior();
-  // chain 0: sum of squares (x . x); chain 1 + j: fn_j . x; the columns stream
-  // through a cp.async ring that every thread fills
-#pragma unroll
-  for (int st = 0; st < kHcStages - 1; ++st) {
-    if (st < nst) hc_issue_stage(a, x, hc_ring + st * slot_floats, st, rows, hc_dim);
+  auto issue = [&](int st) {
+    const int c0 = st * kHcChunk, ncol = min(kHcChunk, hc_dim - c0);
+    float* slot = &ring[st % kHcRing][0][0];
+    if (a.vec4) {
+      const int per_row = ncol / 4;
+      for (int i = tid; i < 2 * per_row; i += blockDim.x) {
+        const int r = i / per_row, col = (i - r * per_row) * 4;
+        hc_cp_async(slot + r * kHcChunk + col, (r ? x : w) + c0 + col, true);
+      }
+    } else {
+      for (int i = tid; i < 2 * ncol; i += blockDim.x) {
+        const int r = i / ncol, col = i - r * ncol;
+        hc_cp_async(slot + r * kHcChunk + col, (r ? x : w) + c0 + col, false);
+      }
+    }
+  };
+#pragma unroll 1
+  for (int st = 0; st < kHcRing - 1; ++st) {
+    if (st < nst) issue(st);
     hc_cp_commit();
   }
-  const bool chain = tid <= rows;
   float acc = 0.0f;
+#pragma unroll 1
   for (int st = 0; st < nst; ++st) {
-    hc_cp_wait<kHcStages - 2>();
+    hc_cp_wait<kHcRing - 2>();
     __syncthreads();  // stage st landed for every thread; slot st - 1 is free
-    const int nx = st + kHcStages - 1;
-    if (nx < nst) hc_issue_stage(a, x, hc_ring + (nx % kHcStages) * slot_floats, nx, rows, hc_dim);
+    if (st + kHcRing - 1 < nst) issue(st + kHcRing - 1);
     hc_cp_commit();
-    if (chain) {
-      const float* slot = hc_ring + (st % kHcStages) * slot_floats;
-      const float* xr = slot;             // row 0: x
-      const float* wr = slot + tid * ld;  // this chain's row (x itself for chain 0)
-      const int ncol = min(a.chunk, hc_dim - st * a.chunk);
+    if (tid == 0) {
+      const float* wr = &ring[st % kHcRing][0][0];
+      const float* xr = &ring[st % kHcRing][1][0];
+      const int ncol = min(kHcChunk, hc_dim - st * kHcChunk);
       int i = 0;
 #pragma unroll 4
       for (; i + 4 <= ncol; i += 4) {
@@ -107,7 +104,21 @@ __global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(HcArgs a) {
     }
   }
   hc_cp_wait<0>();
-  if (chain) s_dot[tid] = acc;
+  if (tid == 0) a.dots[(long long)t * (rows + 1) + c] = acc;
+  pdl_launch_dependents();
+}
+
+// The split (hc_pre: Sinkhorn; hc_head: sigmoid gates) and the pooled output
+// of token blockIdx.x from its chain results.
+__global__ void __launch_bounds__(kHcThreads) hc_split_kernel(HcArgs a) {
+  __shared__ float s_dot[1 + kHcMaxMix];
+  __shared__ float s_pre[kHcMaxHc], s_post[kHcMaxHc], s_comb[kHcMaxHc * kHcMaxHc];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int hc = a.hc, hidden = a.hidden, hc_dim = hc * hidden;
+  const int rows = a.head ? hc : (2 + hc) * hc;
+  const float* x = a.x + (long long)t * hc_dim;
+  pdl_wait_prior();
+  for (int i = tid; i <= rows; i += blockDim.x) s_dot[i] = a.dots[(long long)t * (rows + 1) + i];
   __syncthreads();
   if (tid == 0) {
     const float eps = a.eps;
@@ -190,24 +201,8 @@ __global__ void __launch_bounds__(kHcThreads) hc_post_kernel(HcPostArgs a) {
   pdl_launch_dependents();
 }
 
-// Columns per ring stage: the largest power of two up to 512 whose three
-// stages of (rows + 1) padded rows fit 200 KB.
-int hc_chunk(int rows) {
-  int chunk = 512;
-  while (chunk > 16 && (size_t)kHcStages * (rows + 1) * (chunk + 4) * sizeof(float) > 200 * 1024)
-    chunk >>= 1;
-  return chunk;
-}
-
-size_t hc_mix_smem(int rows, int chunk) {
-  return (size_t)kHcStages * (rows + 1) * (chunk + 4) * sizeof(float);
-}
-
 cudaError_t launch_hc_mix(const HcArgs& a, cudaStream_t s) {
   const int rows = a.head ? a.hc : (2 + a.hc) * a.hc;
-  const size_t smem = hc_mix_smem(rows, a.chunk);
-  cudaError_t e = ensure_smem(hc_mix_kernel, smem);
-  if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -215,10 +210,16 @@ cudaError_t launch_hc_mix(const HcArgs& a, cudaStream_t s) {
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(a.tokens);
+  cfg.gridDim = dim3(rows + 1, a.tokens);
   cfg.blockDim = dim3(kHcThreads);
-  cfg.dynamicSmemBytes = smem;
-  return cudaLaunchKernelEx(&cfg, hc_mix_kernel, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, hc_dots_kernel, a);
+  if (e != cudaSuccess) return e;
+  cfg.gridDim = dim3(a.tokens);
+  return cudaLaunchKernelEx(&cfg, hc_split_kernel, a);
+}
+
+size_t hc_dots_bytes(int tokens, int rows) {
+  return sizeof(float) * (size_t)tokens * (rows + 1);
 }
 
 cudaError_t launch_hc_post(const HcPostArgs& a, int num_sms, cudaStream_t s) {
