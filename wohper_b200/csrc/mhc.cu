@@ -91,14 +91,23 @@ __global__ void __launch_bounds__(kHcThreads) hc_dots_kernel(HcArgs a) {
       const float* xr = &ring[st % kHcRing][1][0];
       const int ncol = min(kHcChunk, hc_dim - st * kHcChunk);
       int i = 0;
-#pragma unroll 4
-      for (; i + 4 <= ncol; i += 4) {
-        const float4 wv = *reinterpret_cast<const float4*>(wr + i);
-        const float4 xv = *reinterpret_cast<const float4*>(xr + i);
-        acc = __fadd_rn(acc, __fmul_rn(wv.x, xv.x));
-        acc = __fadd_rn(acc, __fmul_rn(wv.y, xv.y));
-        acc = __fadd_rn(acc, __fmul_rn(wv.z, xv.z));
-        acc = __fadd_rn(acc, __fmul_rn(wv.w, xv.w));
+      if (ncol == kHcChunk) {
+        // the products of 16 columns formed ahead of their additions
+#pragma unroll 2
+        for (; i < kHcChunk; i += 16) {
+          float pr[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 wv = *reinterpret_cast<const float4*>(wr + i + 4 * q);
+            const float4 xv = *reinterpret_cast<const float4*>(xr + i + 4 * q);
+            pr[4 * q] = __fmul_rn(wv.x, xv.x);
+            pr[4 * q + 1] = __fmul_rn(wv.y, xv.y);
+            pr[4 * q + 2] = __fmul_rn(wv.z, xv.z);
+            pr[4 * q + 3] = __fmul_rn(wv.w, xv.w);
+          }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) acc = __fadd_rn(acc, pr[q]);
+        }
       }
       for (; i < ncol; ++i) acc = __fadd_rn(acc, __fmul_rn(wr[i], xr[i]));
     }
@@ -109,70 +118,88 @@ __global__ void __launch_bounds__(kHcThreads) hc_dots_kernel(HcArgs a) {
 }
 
 // The split (hc_pre: Sinkhorn; hc_head: sigmoid gates) and the pooled output
-// of token blockIdx.x from its chain results.
+// of token blockIdx.x from its chain results.  Elementwise steps run one thread
+// per element; every sum (a softmax row, a Sinkhorn row or column) runs in the
+// reference's order on one thread, with block barriers between the steps.
 __global__ void __launch_bounds__(kHcThreads) hc_split_kernel(HcArgs a) {
-  __shared__ float s_dot[1 + kHcMaxMix];
-  __shared__ float s_pre[kHcMaxHc], s_post[kHcMaxHc], s_comb[kHcMaxHc * kHcMaxHc];
+  __shared__ float s_dot[1 + kHcMaxMix], s_base[kHcMaxMix];
+  __shared__ float s_pre[kHcMaxHc], s_comb[kHcMaxHc * kHcMaxHc], s_sum[kHcMaxHc];
+  __shared__ float s_scale[3], s_inv;
   const int t = blockIdx.x, tid = threadIdx.x;
-  const int hc = a.hc, hidden = a.hidden, hc_dim = hc * hidden;
+  const int hc = a.hc, hidden = a.hidden, hc_dim = hc * hidden, hh = hc * hc;
   const int rows = a.head ? hc : (2 + hc) * hc;
   const float* x = a.x + (long long)t * hc_dim;
+  const float eps = a.eps;
   pdl_wait_prior();
   for (int i = tid; i <= rows; i += blockDim.x) s_dot[i] = a.dots[(long long)t * (rows + 1) + i];
+  for (int i = tid; i < rows; i += blockDim.x) s_base[i] = a.base[i];
+  if (!a.head && tid < 3) s_scale[tid] = a.scale[tid];
   __syncthreads();
   if (tid == 0) {
-    const float eps = a.eps;
     const float mean_square = __fdiv_rn(s_dot[0], (float)hc_dim);
-    const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_square, eps)));
-    if (a.head) {
-      for (int j = 0; j < hc; ++j) {
-        const float mix = __fmul_rn(s_dot[1 + j], inv_rms);
-        s_pre[j] =
-            __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(mix, a.head_scale), a.base[j])), eps);
-      }
-    } else {
-      float* mix = s_dot + 1;
-      for (int j = 0; j < rows; ++j) mix[j] = __fmul_rn(mix[j], inv_rms);
-      const float s0 = a.scale[0], s1 = a.scale[1], s2 = a.scale[2];
-      for (int j = 0; j < hc; ++j) {
-        s_pre[j] = __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(mix[j], s0), a.base[j])), eps);
-        s_post[j] = __fmul_rn(
-            2.0f, hc_sigmoid(__fadd_rn(__fmul_rn(mix[j + hc], s1), a.base[j + hc])));
-      }
-      float* comb = s_comb;
-      for (int j = 0; j < hc * hc; ++j)
-        comb[j] = __fadd_rn(__fmul_rn(mix[2 * hc + j], s2), a.base[2 * hc + j]);
-      // comb = softmax(comb, rows) + eps
-      for (int j = 0; j < hc; ++j) {
-        float* row = comb + j * hc;
-        float mx = -INFINITY;
-        for (int k = 0; k < hc; ++k) mx = fmaxf(mx, row[k]);
-        float sum = 0.0f;
-        for (int k = 0; k < hc; ++k) {
-          row[k] = libm_expf(__fsub_rn(row[k], mx));
-          sum = __fadd_rn(sum, row[k]);
-        }
-        for (int k = 0; k < hc; ++k) row[k] = __fadd_rn(__fdiv_rn(row[k], sum), eps);
-      }
-      // the column normalisation, then (iters - 1) row/column rounds
-      for (int it = 0; it < (a.iters > 1 ? a.iters : 1); ++it) {
-        if (it > 0)
-          for (int j = 0; j < hc; ++j) {
-            float sum = 0.0f;
-            for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, comb[j * hc + k]);
-            const float den = __fadd_rn(sum, eps);
-            for (int k = 0; k < hc; ++k) comb[j * hc + k] = __fdiv_rn(comb[j * hc + k], den);
-          }
-        for (int k = 0; k < hc; ++k) {
-          float sum = 0.0f;
-          for (int j = 0; j < hc; ++j) sum = __fadd_rn(sum, comb[j * hc + k]);
-          const float den = __fadd_rn(sum, eps);
-          for (int j = 0; j < hc; ++j) comb[j * hc + k] = __fdiv_rn(comb[j * hc + k], den);
-        }
-      }
-      for (int j = 0; j < hc; ++j) a.post[(long long)t * hc + j] = s_post[j];
-      for (int j = 0; j < hc * hc; ++j) a.comb[(long long)t * hc * hc + j] = comb[j];
+    s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_square, eps)));
+  }
+  __syncthreads();
+  const float inv_rms = s_inv;
+  if (a.head) {
+    if (tid < hc) {
+      const float mix = __fmul_rn(s_dot[1 + tid], inv_rms);
+      s_pre[tid] =
+          __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(mix, a.head_scale), s_base[tid])), eps);
     }
+  } else {
+    const float* mix = s_dot + 1;  // scaled by inv_rms where used
+    if (tid < hc) {
+      const int j = tid;
+      s_pre[j] = __fadd_rn(
+          hc_sigmoid(__fadd_rn(__fmul_rn(__fmul_rn(mix[j], inv_rms), s_scale[0]), s_base[j])),
+          eps);
+      a.post[(long long)t * hc + j] = __fmul_rn(
+          2.0f, hc_sigmoid(__fadd_rn(__fmul_rn(__fmul_rn(mix[j + hc], inv_rms), s_scale[1]),
+                                     s_base[j + hc])));
+    }
+    if (tid < hh)
+      s_comb[tid] = __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * hc + tid], inv_rms), s_scale[2]),
+                              s_base[2 * hc + tid]);
+    __syncthreads();
+    // comb = softmax(comb, rows) + eps: the row max on the row's thread
+    if (tid < hc) {
+      float mx = -INFINITY;
+      for (int k = 0; k < hc; ++k) mx = fmaxf(mx, s_comb[tid * hc + k]);
+      s_sum[tid] = mx;
+    }
+    __syncthreads();
+    if (tid < hh) s_comb[tid] = libm_expf(__fsub_rn(s_comb[tid], s_sum[tid / hc]));
+    __syncthreads();
+    if (tid < hc) {
+      float sum = 0.0f;
+      for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
+      s_sum[tid] = sum;
+    }
+    __syncthreads();
+    if (tid < hh) s_comb[tid] = __fadd_rn(__fdiv_rn(s_comb[tid], s_sum[tid / hc]), eps);
+    // the column normalisation, then (iters - 1) row/column rounds
+    for (int it = 0; it < (a.iters > 1 ? a.iters : 1); ++it) {
+      if (it > 0) {
+        __syncthreads();
+        if (tid < hc) {
+          float sum = 0.0f;
+          for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
+          s_sum[tid] = __fadd_rn(sum, eps);
+        }
+        __syncthreads();
+        if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid / hc]);
+      }
+      __syncthreads();
+      if (tid < hc) {
+        float sum = 0.0f;
+        for (int j = 0; j < hc; ++j) sum = __fadd_rn(sum, s_comb[j * hc + tid]);
+        s_sum[tid] = __fadd_rn(sum, eps);
+      }
+      __syncthreads();
+      if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid % hc]);
+    }
+    if (tid < hh) a.comb[(long long)t * hh + tid] = s_comb[tid];
   }
   __syncthreads();
   for (int d = tid; d < hidden; d += blockDim.x) {
