@@ -1511,7 +1511,8 @@ def run_mhc(args):
             "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (reference operation order, no FMA)",
             "data": "synthetic (N(0, 0.01) fn rows, N(0, 1) residual copies)", "config": cfg,
-            "roofline": {"kernel": "hc_mix_kernel + hc_post_kernel", "bound": "hbm",
+            "roofline": {"kernel": "hc_dots_kernel + hc_split_kernel + hc_post_kernel",
+                         "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algorithmic_bytes": alg, "traffic": None,
@@ -1525,7 +1526,7 @@ def run_mhc(args):
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": x.numel() * 4,
                     "d2h_bytes_per_step": out.numel() * 4,
                     "path": "pinned host x -> H2D -> wh_hc_pre + wh_hc_post (C ABI) -> D2H"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline:
