@@ -15,8 +15,8 @@
 // The sum of squares and the fn-row dots are dependent chains of hc_dim
 // additions (16384 for V4: about 33 us at 4 cycles an add).  hc_dots_kernel
 // runs each chain in a CTA of its own (25 CTAs per token for V4); the split
-// kernel then runs the Sinkhorn (or the head gates) on one thread and the
-// pooled output over all threads; hc_post is elementwise.
+// kernel then runs the Sinkhorn (or the head gates) and the pooled output;
+// hc_post is elementwise.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -120,7 +120,9 @@ __global__ void __launch_bounds__(kHcThreads) hc_dots_kernel(HcArgs a) {
 // The split (hc_pre: Sinkhorn; hc_head: sigmoid gates) and the pooled output
 // of token blockIdx.x from its chain results.  Elementwise steps run one thread
 // per element; every sum (a softmax row, a Sinkhorn row or column) runs in the
-// reference's order on one thread, with block barriers between the steps.
+// reference's order on one thread.  With hc * hc <= 32 the Sinkhorn runs in one
+// warp, each lane gathering its row and column by shuffles; larger hc takes
+// block barriers between the steps.
 __global__ void __launch_bounds__(kHcThreads) hc_split_kernel(HcArgs a) {
   __shared__ float s_dot[1 + kHcMaxMix], s_base[kHcMaxMix];
   __shared__ float s_pre[kHcMaxHc], s_comb[kHcMaxHc * kHcMaxHc], s_sum[kHcMaxHc];
@@ -158,46 +160,80 @@ __global__ void __launch_bounds__(kHcThreads) hc_split_kernel(HcArgs a) {
           2.0f, hc_sigmoid(__fadd_rn(__fmul_rn(__fmul_rn(mix[j + hc], inv_rms), s_scale[1]),
                                      s_base[j + hc])));
     }
-    if (tid < hh)
-      s_comb[tid] = __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * hc + tid], inv_rms), s_scale[2]),
-                              s_base[2 * hc + tid]);
-    __syncthreads();
-    // comb = softmax(comb, rows) + eps: the row max on the row's thread
-    if (tid < hc) {
-      float mx = -INFINITY;
-      for (int k = 0; k < hc; ++k) mx = fmaxf(mx, s_comb[tid * hc + k]);
-      s_sum[tid] = mx;
-    }
-    __syncthreads();
-    if (tid < hh) s_comb[tid] = libm_expf(__fsub_rn(s_comb[tid], s_sum[tid / hc]));
-    __syncthreads();
-    if (tid < hc) {
-      float sum = 0.0f;
-      for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
-      s_sum[tid] = sum;
-    }
-    __syncthreads();
-    if (tid < hh) s_comb[tid] = __fadd_rn(__fdiv_rn(s_comb[tid], s_sum[tid / hc]), eps);
-    // the column normalisation, then (iters - 1) row/column rounds
-    for (int it = 0; it < (a.iters > 1 ? a.iters : 1); ++it) {
-      if (it > 0) {
-        __syncthreads();
-        if (tid < hc) {
-          float sum = 0.0f;
-          for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
-          s_sum[tid] = __fadd_rn(sum, eps);
+    if (hh <= 32) {
+      // one warp: lane = comb element (j, k); each lane forms its row's and its
+      // column's sums itself, in the reference's order, from shuffles
+      if (tid < 32) {
+        const int lane = tid, j = lane / hc, k = lane % hc;
+        const bool on = lane < hh;
+        float v = on ? __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * hc + lane], inv_rms), s_scale[2]),
+                                 s_base[2 * hc + lane])
+                     : 0.0f;
+        float mx = -INFINITY;
+        for (int kk = 0; kk < hc; ++kk)
+          mx = fmaxf(mx, __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31));
+        v = on ? libm_expf(__fsub_rn(v, mx)) : 0.0f;
+        float sum = 0.0f;
+        for (int kk = 0; kk < hc; ++kk)
+          sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31));
+        v = __fadd_rn(__fdiv_rn(v, sum), eps);
+        for (int it = 0; it < (a.iters > 1 ? a.iters : 1); ++it) {
+          if (it > 0) {
+            float rs = 0.0f;
+            for (int kk = 0; kk < hc; ++kk)
+              rs = __fadd_rn(rs, __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31));
+            v = __fdiv_rn(v, __fadd_rn(rs, eps));
+          }
+          float cs = 0.0f;
+          for (int jj = 0; jj < hc; ++jj)
+            cs = __fadd_rn(cs, __shfl_sync(0xffffffffu, v, (jj * hc + k) & 31));
+          v = __fdiv_rn(v, __fadd_rn(cs, eps));
         }
-        __syncthreads();
-        if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid / hc]);
+        if (on) s_comb[lane] = v;
       }
+      __syncthreads();
+    } else {
+      if (tid < hh)
+        s_comb[tid] = __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * hc + tid], inv_rms), s_scale[2]),
+                                s_base[2 * hc + tid]);
+      __syncthreads();
+      // comb = softmax(comb, rows) + eps: the row max on the row's thread
+      if (tid < hc) {
+        float mx = -INFINITY;
+        for (int k = 0; k < hc; ++k) mx = fmaxf(mx, s_comb[tid * hc + k]);
+        s_sum[tid] = mx;
+      }
+      __syncthreads();
+      if (tid < hh) s_comb[tid] = libm_expf(__fsub_rn(s_comb[tid], s_sum[tid / hc]));
       __syncthreads();
       if (tid < hc) {
         float sum = 0.0f;
-        for (int j = 0; j < hc; ++j) sum = __fadd_rn(sum, s_comb[j * hc + tid]);
-        s_sum[tid] = __fadd_rn(sum, eps);
+        for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
+        s_sum[tid] = sum;
       }
       __syncthreads();
-      if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid % hc]);
+      if (tid < hh) s_comb[tid] = __fadd_rn(__fdiv_rn(s_comb[tid], s_sum[tid / hc]), eps);
+      // the column normalisation, then (iters - 1) row/column rounds
+      for (int it = 0; it < (a.iters > 1 ? a.iters : 1); ++it) {
+        if (it > 0) {
+          __syncthreads();
+          if (tid < hc) {
+            float sum = 0.0f;
+            for (int k = 0; k < hc; ++k) sum = __fadd_rn(sum, s_comb[tid * hc + k]);
+            s_sum[tid] = __fadd_rn(sum, eps);
+          }
+          __syncthreads();
+          if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid / hc]);
+        }
+        __syncthreads();
+        if (tid < hc) {
+          float sum = 0.0f;
+          for (int j = 0; j < hc; ++j) sum = __fadd_rn(sum, s_comb[j * hc + tid]);
+          s_sum[tid] = __fadd_rn(sum, eps);
+        }
+        __syncthreads();
+        if (tid < hh) s_comb[tid] = __fdiv_rn(s_comb[tid], s_sum[tid % hc]);
+      }
     }
     if (tid < hh) a.comb[(long long)t * hh + tid] = s_comb[tid];
   }
