@@ -26,9 +26,13 @@
 //                      per-head max.
 //   mla_weights_kernel one CTA per (head, 256 positions): the head's max over
 //                      the tile maxima and w = exp(s - max), each weight once.
-//   mla_output_kernel  one CTA per (64-feature slice, group of heads): the
-//                      group's weight rows into shared memory, one thread per
-//                      (head, feature) chain over the positions, the slice's
+//   mla_output_kernel  one CTA per (16-feature slice, group of up to 16 heads):
+//                      the group's weight rows into shared memory, one thread
+//                      per (head, feature) chain over the positions (a warp is
+//                      two heads x 16 features, so each key value read from
+//                      shared memory serves 16 heads' chains, and the 16 head
+//                      groups of 64 heads re-read the keys 4 times from L2,
+//                      not 16), the slice's
 //                      key rows streamed through a cp.async ring of 12 (8, 4)
 //                      stages of 64 rows by the feature warps alone (on a named
 //                      barrier), a denominator warp running the in-order weight
@@ -45,7 +49,8 @@ constexpr int kMlaScoreHeads = 32;  // heads per scores CTA (one per lane)
 constexpr int kMlaScoreChains = 2;  // positions per thread
 constexpr int kMlaScoreTile = 16;   // positions per scores CTA
 constexpr int kMlaScoreThreads = kMlaScoreHeads * kMlaScoreTile / kMlaScoreChains;
-constexpr int kMlaSlice = 64;       // features per output CTA (two warps per head)
+constexpr int kMlaSlice = 16;       // features per output CTA (half a warp per head)
+constexpr int kMlaMaxGroup = 16;    // heads per output CTA at most
 constexpr int kMlaRingRows = 64;    // key rows per ring stage of the output kernel
 constexpr size_t kMlaStageBytes = sizeof(float) * kMlaRingRows * kMlaSlice;
 constexpr int kMlaWeightThreads = 256;
@@ -200,14 +205,14 @@ __device__ __forceinline__ void mla_issue_rows(const MlaArgs& a, float* slot, in
 }
 
 template <int kStages>
-__global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs a) {
+__global__ void __launch_bounds__(kMlaMaxGroup * kMlaSlice + 32) mla_output_kernel(MlaArgs a) {
   extern __shared__ __align__(16) float mla_w[];  // [group][P] weights | key ring
-  __shared__ float s_den[4];
+  __shared__ float s_den[kMlaMaxGroup];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int D = a.head_dim, G = a.head_group;
   const int P = a.window_len + a.compressed_count;
   const int h0 = blockIdx.y * G;
-  const int fw = 2 * G;       // feature warps; warp fw is the denominator warp
+  const int fw = (G + 1) / 2;  // feature warps (two heads each); warp fw: denominators
   const int nfeat = fw * 32;  // threads of the feature warps
   const int f0 = blockIdx.x * kMlaSlice, nf = min(kMlaSlice, D - f0);
   // weight rows padded to wld = P rounded up to 4, plus 4: the denominator
@@ -215,9 +220,9 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   const int wld = ((P + 3) & ~3) + 4;
   float* ring = mla_w + G * wld;  // [kStages][kMlaRingRows][kMlaSlice]
   const int nst = (P + kMlaRingRows - 1) / kMlaRingRows;
-  const int g = warp >> 1;
-  const int fl = (warp & 1) * 32 + lane;  // feature within the slice
-  const bool feature = warp < fw && fl < nf;
+  const int g = 2 * warp + (lane >> 4);  // the lane's head within the group
+  const int fl = lane & 15;              // the lane's feature within the slice
+  const bool feature = warp < fw && g < G && fl < nf;
   const bool dwarp = warp == fw && lane < G;
   pdl_wait_prior();
   // copy group 0, by every thread: the group's weight rows (contiguous [h][P])
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
     cp_async_wait<0>();
   }
   __syncthreads();  // the weights are visible to every thread
-  const float* w = mla_w + (warp < fw ? g : (lane < G ? lane : 0)) * wld;
+  const float* w = mla_w + (warp < fw ? (g < G ? g : 0) : (lane < G ? lane : 0)) * wld;
   float acc = 0.0f;  // a feature chain, or a denominator's weight sum
   if (warp < fw) {
     for (int st = 0; st < nst; ++st) {
@@ -300,12 +305,12 @@ __global__ void __launch_bounds__(4 * kMlaSlice + 32) mla_output_kernel(MlaArgs 
   __syncthreads();
   if (warp < fw) {
     const int f = f0 + fl;
-    const float den = s_den[g];
+    const float den = s_den[g < G ? g : 0];
     if (den > 0.0f) acc = __fdiv_rn(acc, den);
     // inverse RoPE: sin negated; the pair partner is the neighbouring lane
     // (nope_dim and the slice start are even)
     const float partner = __shfl_xor_sync(0xffffffffu, acc, 1);
-    if (fl < nf) {
+    if (g < G && fl < nf) {
       if (f >= a.nope_dim) {
         const int i = (f - a.nope_dim) >> 1;
         const float c = a.rope_cos[i], sn = -a.rope_sin[i];
@@ -332,7 +337,7 @@ bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output) {
                                   (size_t)kMlaScoreTile * kMlaScoreHeads);
   if (*smem_scores > kBudget) return false;
   for (int stages : {12, 8, 4})
-    for (int g : {4, 2, 1}) {
+    for (int g : {16, 8, 4, 2, 1}) {
       if (H % g) continue;
       const size_t bytes =
           sizeof(float) * (size_t)g * ((((size_t)P + 3) & ~(size_t)3) + 4) + stages * kMlaStageBytes;
@@ -386,7 +391,7 @@ cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t sm
   e = cudaLaunchKernelEx(&cfg, mla_weights_kernel, a);
   if (e != cudaSuccess) return e;
   cfg.gridDim = dim3((a.head_dim + kMlaSlice - 1) / kMlaSlice, a.heads / a.head_group);
-  cfg.blockDim = dim3(2 * 32 * a.head_group + 32);
+  cfg.blockDim = dim3(32 * ((a.head_group + 1) / 2) + 32);
   cfg.dynamicSmemBytes = smem_output;
   switch (a.stages) {
     case 12: return launch_mla_output<12>(cfg, a);
