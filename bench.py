@@ -1230,6 +1230,10 @@ def run_lm_head(args):
 # before each kernel, so the output kernel's key rows count as DRAM there; in
 # the timed pipeline they are L2 hits.
 MLA_TRAFFIC = 5_612_288
+# cycles per step of a dependent FP32 addition chain (acc = acc + x * y with the
+# products independent), measured on this pool's B200 with one thread timing a
+# 2^20-step chain by clock64: 4.44 (4.56 for bare additions)
+FADD_CHAIN_CYCLES = 4.44
 METRIC_MLA = "MLA attention-core calls/s (one decode token, one DeepSeek-V4 layer, 64 heads)"
 MLA_HEADS, MLA_HD, MLA_NOPE, MLA_POS, MLA_COMP = 64, 512, 448, 4095, 1024
 WORKLOAD_MLA = ("MLA attention core of DeepSeek-V4-Flash (64 heads x 512 = 448 nope + 64 rope), "
@@ -1341,7 +1345,7 @@ def run_mla(args):
     achieved = alg / (ms_step * 1e-3) / 1e9
     clocks = clk.summary()
     sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-    chain_us = (MLA_HD + rows) * 4 / sm_mhz
+    chain_us = (MLA_HD + rows) * FADD_CHAIN_CYCLES / sm_mhz
     res = None
     if rank == 0:
         res = {
@@ -1360,7 +1364,8 @@ def run_mla(args):
                          "note": "latency-bound: the reference's in-order sums are "
                                  f"dependent chains of {MLA_HD} (scores) and {rows} "
                                  "(weighted sum) additions; chain_floor_us = those "
-                                 "additions at 4 cycles each and the sampled SM clock"},
+                                 "additions at the measured 4.44 cycles each and the "
+                                 "sampled SM clock"},
             "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "calls/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
                     "d2h_bytes_per_step": out.numel() * 4,
@@ -1501,7 +1506,7 @@ def run_mhc(args):
     achieved = alg / (ms_step * 1e-3) / 1e9
     clocks = clk.summary()
     sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-    chain_us = hc_dim * 4 / sm_mhz
+    chain_us = hc_dim * FADD_CHAIN_CYCLES / sm_mhz
     res_line = None
     if rank == 0:
         res_line = {
@@ -1521,7 +1526,8 @@ def run_mhc(args):
                          "note": "latency-bound: the sum of squares and each fn-row dot are "
                                  f"chains of {hc_dim} dependent additions in the "
                                  "reference's order; chain_floor_us = one such chain at "
-                                 "4 cycles an addition and the sampled SM clock"},
+                                 "the measured 4.44 cycles an addition and the sampled "
+                                 "SM clock"},
             "e2e": {"value": round(world * T * 1e3 / e2e_ms, 2), "unit": "token-calls/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": x.numel() * 4,
                     "d2h_bytes_per_step": out.numel() * 4,

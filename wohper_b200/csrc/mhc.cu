@@ -13,7 +13,7 @@
 // (no fused multiply-add), and its exp is the host libm's expf (libm_expf).
 //
 // The sum of squares and the fn-row dots are dependent chains of hc_dim
-// additions (16384 for V4: about 33 us at 4 cycles an add).  hc_dots_kernel
+// additions (16384 for V4: about 37 us at 4.4 cycles an add).  hc_dots_kernel
 // runs each chain in a CTA of its own (25 CTAs per token for V4); the split
 // kernel then runs the Sinkhorn (or the head gates) and the pooled output;
 // hc_post is elementwise.
