@@ -368,7 +368,7 @@ struct wh_moe_plan {
 
 extern "C" {
 
-int wh_version(void) { return 100; }
+int wh_version(void) { return 200; }
 
 const char* wh_last_error_detail(void) { return g_detail.c_str(); }
 
