@@ -54,7 +54,7 @@ UP_TRAFFIC = 63_314_688
 STEP_TRAFFIC = None
 STEP_TRAFFIC_SOURCE = "not captured yet"
 # grouped up GEMM: DRAM bytes read per algorithmic byte read in the ncu capture of the
-# grouped16 case (161,668,608 / 159,088,640; profiles/grouped_gemm_grouped16.md); the
+# grouped16 case (161,668,608 / 159,088,640 bytes, bench.py --ncu-case grouped16); the
 # config-3 launch is too large to capture, its traffic is scaled by the units processed
 GROUPED_UP_TRAFFIC_RATIO = 161_668_608 / 159_088_640
 METRIC = "decode tokens/s (one-token FP4 MoE FFN, config 2)"
@@ -221,6 +221,19 @@ def cpu_run(steps: int, warmup: int, seed: int = 900, budget_s: float | None = N
             break
     dt = time.perf_counter() - t0
     return done / dt, done, O.threads()
+
+
+def config2_dict(world: int, fp8_shared: bool, step_bytes: int) -> dict:
+    """The config-2 workload description, the same on both arms."""
+    return {
+        "workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID, "inter": INTER,
+        "batch": 1,
+        "shared_expert": ("fp8 e4m3 x ue8m0-128x128 (DeepSeek-V4's layout), on the FP8 "
+                          "GEMV after the routed experts" if fp8_shared else "fp4"),
+        "l2": "flushed between steps (256 MiB memset outside the timed events)",
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "bytes_per_step": step_bytes,
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -404,15 +417,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "fp4-e2m1 x fp8-e4m3 (act-quant) products, f32 accumulate",
             "data": "synthetic (seeded random-init weights and N(0,1) tokens)",
-            "config": {
-                "workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID, "inter": INTER,
-                "batch": 1,
-                "shared_expert": ("fp8 e4m3 x ue8m0-128x128 (DeepSeek-V4's layout), on the FP8 "
-                                  "GEMV after the routed experts" if fp8_shared else "fp4"),
-                "l2": "flushed between steps (256 MiB memset outside the timed events)",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                "bytes_per_step": step_bytes,
-            },
+            "config": config2_dict(world, fp8_shared, step_bytes),
             "step_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
             "phases_ms": {"router": round(router_ms, 5), "moe_up": round(up_ms, 5),
                           "moe_down": round(down_ms, 5)},
@@ -481,13 +486,222 @@ def run_reference(args):
         "ms_per_step": round(1e3 / v, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp4-e2m1 x fp8-e4m3 (act-quant) products, f32 accumulate",
         "data": "synthetic (seeded random-init weights and N(0,1) tokens)",
-        "config": {"workload": WORKLOAD, "experts": E, "topk": TOPK, "hidden": HID,
-                   "inter": INTER, "batch": 1, "shared_expert": "fp4"},
+        "config": config2_dict(world, False, STEP_BYTES),
         "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{n} tokens, one per step"},
         "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+
+
+# ---------------------------------------------------------------------------
+# config 1: one FP8 block-scaled GEMV, W [4096 x 4096] E4M3 + UE8M0 per 128x128
+# ---------------------------------------------------------------------------
+R1 = C1 = 4096
+FP8_BYTES = R1 * C1 + (R1 // 128) * (C1 // 128) + 4 * C1 + 4 * R1   # 16,811,008 per call
+FP8_COPIES = 16          # distinct weight matrices: 269 MB, over twice the 126 MB L2
+# DRAM bytes (read + write) of one fp8_gemv_rowgroup_kernel launch at 4096 x 4096 from
+# an ncu capture (bench.py --ncu-case fp8)
+FP8_TRAFFIC = 16_831_232
+METRIC1 = "FP8 GEMV HBM GB/s (config 1: 4096x4096 E4M3, UE8M0 per 128x128, f32 x)"
+WORKLOAD1 = ("config 1: gemv_fp8_e4m3_ue8m0_tensorwise, W [4096 x 4096] E4M3 of N(0,0.05), "
+             "UE8M0 block scales 2^[-8,-2] per 128x128, x f32 N(0,1), f32 accumulate in the "
+             "reference's 16-chain order; one GEMV per step over 16 distinct weight copies "
+             "in rotation, back to back as a decode step's projections run")
+
+
+def config1_dict(world: int) -> dict:
+    return {"workload": WORKLOAD1, "rows": R1, "cols": C1, "batch": 1,
+            "weight_copies": FP8_COPIES,
+            "l2": f"inputs larger than L2: {FP8_COPIES} distinct weight copies "
+                  f"({FP8_COPIES * R1 * C1 >> 20} MiB) in rotation",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "bytes_per_step": FP8_BYTES}
+
+
+def config1_cpu(budget_s: float, threads_all: bool):
+    """The reference's tensorwise FP8 GEMV (oracle restatement) on host cores:
+    (GB/s of the same algorithmic bytes, calls, threads)."""
+    import oracle as O
+    from tests import helpers as H
+
+    if threads_all:
+        O.set_threads(os.cpu_count() or 1)
+    w, sc = H.fp8_weight(11, R1, C1)
+    x = H.activations(12, 1, C1).reshape(-1)
+    O.fp8_gemv(w, sc, x, R1, C1, R1 // 128, C1 // 128)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        st, _ = O.fp8_gemv(w, sc, x, R1, C1, R1 // 128, C1 // 128)
+        assert st == O.OK
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return FP8_BYTES * n / dt / 1e9, n, O.threads()
+
+
+def run_config1(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    import oracle as O
+    import wohper_b200 as W
+    from tests import helpers as H
+
+    dev = torch.device("cuda", local)
+    ctx = W.Context(local)
+    w0, s0 = H.fp8_weight(11 + rank, R1, C1)
+    x0 = H.activations(12 + rank, 1, C1).reshape(-1)
+    # distinct copies (the same bytes at distinct addresses: every call reads
+    # its weights from HBM, never from L2)
+    wd = [torch.from_numpy(w0).to(dev) for _ in range(FP8_COPIES)]
+    sd = torch.from_numpy(s0).to(dev)
+    x = torch.from_numpy(x0).to(dev)
+    ys = torch.empty(FP8_COPIES, R1, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def call(i, xin=x, yout=None):
+        W.gemv_fp8_e4m3_ue8m0_tensorwise(ctx, wd[i % FP8_COPIES], sd, xin,
+                                         ys[i % FP8_COPIES] if yout is None else yout)
+
+    for i in range(max(args.warmup, FP8_COPIES)):
+        call(i)
+    ctx.sync()
+    # parity spot check of the timed path: bit-exact with the reference order
+    st, want = O.fp8_gemv(w0, s0, x0, R1, C1, R1 // 128, C1 // 128)
+    parity = bool(st == O.OK and np.array_equal(ys[0].cpu().numpy().view(np.uint32),
+                                                 want.view(np.uint32)))
+    # ---- K calls back to back, captured once as a CUDA graph ---------------
+    K = args.steps
+    timing = "cuda graph of the K calls (PDL between them)"
+    graph = None
+    try:
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(K):
+                    call(i)
+        stream.wait_stream(cap)
+        torch.cuda.synchronize()
+        for _ in range(max(1, args.warmup // K)):
+            graph.replay()
+        torch.cuda.synchronize()
+    except Exception as exc:
+        graph = None
+        timing = f"direct calls (graph capture failed: {type(exc).__name__})"
+        torch.cuda.synchronize()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(K):
+                call(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ctx.sync()
+    ms_step = all_max(world, e0.elapsed_time(e1)) / K
+    del graph
+    # ---- one isolated call (L2 flushed before it), for comparison ----------
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    iso = []
+    for i in range(8):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        call(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        iso.append(a.elapsed_time(b))
+    iso_ms = statistics.median(iso)
+    # ---- end to end: pinned host x in, host y out, every call -------------
+    xh = torch.from_numpy(H.activations(13 + rank, K, C1)).pin_memory()
+    yh = torch.empty(K, R1).pin_memory()
+    xd = torch.empty(C1, device=dev)
+    yd = torch.empty(R1, device=dev)
+    for i in range(args.warmup):
+        xd.copy_(xh[i], non_blocking=True)
+        call(i, xd, yd)
+        yh[i].copy_(yd, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(K):
+        xd.copy_(xh[i], non_blocking=True)
+        call(i, xd, yd)
+        yh[i].copy_(yd, non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = all_max(world, a.elapsed_time(b)) / K
+    ctx.sync()
+    peak, peak_kind = peaks()
+    res = None
+    if rank == 0:
+        gbs = FP8_BYTES / (ms_step * 1e-3) / 1e9
+        res = {
+            "metric": METRIC1, "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 weights x f32 x, f32 accumulate",
+            "data": "synthetic (seeded E4M3 weights, N(0,1) x)",
+            "config": config1_dict(world),
+            "calls_per_s": round(world / (ms_step * 1e-3), 1),
+            "isolated_call_ms": round(iso_ms, 5),
+            "isolated_call_gbs": round(FP8_BYTES / (iso_ms * 1e-3) / 1e9, 1),
+            "roofline": {"kernel": "fp8_gemv_rowgroup_kernel (one GEMV per launch)",
+                         "bound": "hbm", "achieved": round(gbs, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                         "algorithmic_bytes": FP8_BYTES, "traffic": FP8_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read+write of one launch "
+                                           "(bench.py --ncu-case fp8, the same shape)"},
+            "e2e": {"value": round(FP8_BYTES / (e2e_ms * 1e-3) / 1e9 * world, 1), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 6), "h2d_bytes_per_step": 4 * C1,
+                    "d2h_bytes_per_step": 4 * R1,
+                    "path": "pinned host x -> H2D -> wh_fp8_gemv (C ABI) -> D2H pinned host y"},
+            "parity_bit_exact_vs_oracle": parity,
+            "gpu_launches": K, "timing": timing, "clocks": clk.summary(),
+        }
+    ctx.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, n, cores = config1_cpu(10.0, False)
+        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": cores,
+                               "kind": "port",
+                               "sample": f"{n} calls of the same GEMV (one weight matrix), C++ "
+                                         "restatement of the reference's AVX2 kernel, "
+                                         "reference threading (nproc-2 threads)"}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res
+
+
+def run_reference_config1(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    v, n, cores = config1_cpu(max(5.0, 0.2 * args.steps), True)
+    return {"impl": "reference", "metric": METRIC1, "value": round(v, 3), "unit": "GB/s",
+            "n_gpus": world, "steps": n, "warmup": args.warmup,
+            "ms_per_step": round(FP8_BYTES / (v * 1e9) * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 weights x f32 x, f32 accumulate",
+            "data": "synthetic (seeded E4M3 weights, N(0,1) x)", "config": config1_dict(world),
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} calls"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
 
 
 # ---------------------------------------------------------------------------
@@ -1086,7 +1300,7 @@ WORKLOAD_LM = ("lm_head top-k: every logit of the BF16 lm_head of DeepSeek-V3/V4
                "(129280 x 4096, 1.06 GB) in the reference's dot_bf16_row order, then the "
                "top-k push_topk_candidate keeps, sorted; one hidden vector per step")
 # DRAM bytes / algorithmic bytes of lm_logits_kernel from the ncu capture of the lmhead case
-# (32768 rows: 268,467,200 read + 3,915,264 written / 268,582,912; profiles/lm_logits_lmhead.md),
+# (32768 rows: 268,467,200 read + 3,915,264 written / 268,582,912; bench.py --ncu-case lmhead),
 # scaled to the full launch by rows
 LM_TRAFFIC_RATIO = 272_382_464 / 268_582_912
 
@@ -1652,9 +1866,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
-                    help="2: one-token decode FFN (default); 3: 2048-token batched FFN; "
-                         "4: expert-parallel layer over the ranks")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+                    help="1: one FP8 GEMV 4096x4096; 2: one-token decode FFN (default); "
+                         "3: 2048-token batched FFN; 4: expert-parallel layer over the ranks")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="config 4: rows over NVLink peer stores (p2p) or NCCL all-to-all")
     ap.add_argument("--workload", default="moe", choices=["moe", "expert-load", "lm-head", "mla", "mhc"],
@@ -1687,6 +1901,8 @@ def main():
         res = run_mla(args)
     elif args.workload == "mhc":
         res = run_mhc(args)
+    elif args.config == 1:
+        res = run_config1(args) if args.impl == "ours" else run_reference_config1(args)
     elif args.config == 3 and args.impl == "ours":
         res = run_config3(args)
     elif args.config == 4 and args.impl == "ours":

@@ -3,7 +3,7 @@
  * Wohper (engine/zc_infer_core).  Every entry point here replaces one Rust
  * function of the reference's kernel layer; the comment above each cites the
  * reference interface it stands in for (path:line inside the reference
- * project).  A Rust FFI crate binds these symbols one to one (INTEGRATION.md).
+ * project).  A Rust FFI crate binds these symbols one to one.
  *
  * Conventions
  *  - All data pointers are DEVICE pointers owned by the caller (weights are
@@ -174,7 +174,8 @@ wh_status wh_fp4_expert_forward(wh_ctx* ctx, const wh_fp4_expert* expert, const 
  * with hidden + 2 * intermediate > 65536 return WH_ERR_SCRATCH_TOO_SMALL.
  * Nothing in it needs to start at zero.  The first call on each device looks
  * the array up (cudaGetSymbolAddress) and should happen before any stream
- * capture.  The array is shared by every caller on a device: calls that
+ * capture; after cudaDeviceReset the next call is a first call again (the
+ * array is looked up anew in the new context).  The array is shared by every caller on a device: calls that
  * overlap in time there (other streams, threads or contexts) race; calls in
  * order on one stream are safe.  Computes the reference-order exact path;
  * device-side errors are reported by wh_ctx_sync like every other call. */
@@ -260,6 +261,25 @@ void wh_moe_plan_destroy(wh_moe_plan* plan);
 
 /* Device scratch bytes wh_moe_ffn needs for `tokens` tokens. */
 size_t wh_moe_scratch_bytes(const wh_moe_plan* plan, int tokens);
+
+/* Where one intermediate array of the tensor-core (grouped) path lies inside
+ * the scratch of a wh_moe_ffn call of `tokens` tokens: byte offset from the
+ * scratch pointer and size.  For tests and debugging (the act-quantised SwiGLU
+ * hidden of every routed row is WH_MOE_FIELD_HQ / _HSF); it has no
+ * counterpart in the reference.  Rows of an expert are contiguous from
+ * offsets[e]; the row of (token t, route k) is offsets[ids[t][k]] +
+ * slot[t][k], the shared expert's row of token t is offsets[num_experts] + t.
+ * Calls that do not take the grouped path return WH_ERR_UNSUPPORTED. */
+#define WH_MOE_FIELD_SLOT 1      /* int32 [tokens][topk] */
+#define WH_MOE_FIELD_OFFSETS 2   /* int32 [experts (+1 shared) + 1] */
+#define WH_MOE_FIELD_COMBINE_W 3 /* f32 [tokens][topk]: w / sum(w) */
+#define WH_MOE_FIELD_XQ 4        /* u8 [rows][hidden]: E4M3 act-quantised token */
+#define WH_MOE_FIELD_XSF 5       /* u8 [rows][hidden/32]: UE8M0 */
+#define WH_MOE_FIELD_HQ 6        /* u8 [rows][inter]: E4M3 act-quantised hidden */
+#define WH_MOE_FIELD_HSF 7       /* u8 [rows][inter/32]: UE8M0 */
+#define WH_MOE_FIELD_YROWS 8     /* f32 [rows][hidden]: each row's expert output */
+wh_status wh_moe_scratch_field(const wh_moe_plan* plan, int tokens, int field, size_t* offset,
+                               size_t* bytes);
 
 /* One MoE FFN step for `tokens` tokens (x, y: [tokens][hidden] f32).
  * Replaces, per token, routing (see wh_router_topk) followed by

@@ -385,3 +385,16 @@ def moe_batched(experts_arr, num_experts, ids, weights, shared_fp4, x):
     st = lib().orc_moe_batched(experts_arr, num_experts, _p(ids), _p(weights), T, K, sh4, _p(x),
                                x.shape[1], _p(y))
     return st, y
+
+
+def fp4_expert_hidden(expert: Fp4Expert, x):
+    """(status, h): the act-quantised SwiGLU hidden the reference's expert
+    forward feeds to w2 (src/deepseek_v4.rs:586-596) -- the first `inter`
+    floats of its scratch once deepseek_v4_fp4_expert_forward_scalar returns."""
+    x = _c(x, np.float32)
+    inter = expert.w1.rows
+    y = np.zeros(expert.w2.rows, np.float32)
+    scratch = np.zeros(2 * inter, np.float32)
+    st = lib().orc_fp4_expert_forward(C.byref(expert), _p(x), x.size, _p(y), y.size, _p(scratch),
+                                      2 * inter)
+    return st, scratch[:inter].copy()

@@ -264,7 +264,8 @@ def build_numpy_tool(reference: Path) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="path of the reference checkout (the Wohper repository root)")
     args = ap.parse_args()
     (HERE / "kats.json").write_text(json.dumps(build_kats(), indent=1) + "\n")
     ref = Path(args.reference)

@@ -99,7 +99,8 @@ def write_safetensors(path: Path, items: dict):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="path of the reference checkout (the Wohper repository root)")
     args = ap.parse_args()
     tools = Path(args.reference) / "tools"
     sys.path.insert(0, str(tools))

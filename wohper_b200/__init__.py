@@ -55,13 +55,17 @@ STATUS_NAMES = {
 }
 ROUTER_RAW_LOGITS = 0
 ROUTER_SQRT_SOFTPLUS = 1
+# wh_moe_scratch_field fields (include/wohper_b200.h)
+MOE_FIELD_SLOT, MOE_FIELD_OFFSETS, MOE_FIELD_COMBINE_W = 1, 2, 3
+MOE_FIELD_XQ, MOE_FIELD_XSF, MOE_FIELD_HQ, MOE_FIELD_HSF, MOE_FIELD_YROWS = 4, 5, 6, 7, 8
 
 # Every symbol include/wohper_b200.h declares (checked by tests/test_capi.py).
 EXPORTS = (
     "wh_version", "wh_ctx_create", "wh_ctx_destroy", "wh_ctx_sync", "wh_last_error_detail",
     "wh_fp8_gemv", "wh_act_quant_fp8", "wh_fp4_matvec", "wh_fp4_expert_scratch_len",
     "wh_fp4_expert_forward", "wh_router_topk", "wh_moe_plan_create", "wh_moe_plan_destroy",
-    "wh_moe_scratch_bytes", "wh_moe_ffn", "wh_debug_act_quant_table", "wh_debug_e4m3_round",
+    "wh_moe_scratch_bytes", "wh_moe_scratch_field", "wh_moe_ffn", "wh_debug_act_quant_table",
+    "wh_debug_e4m3_round",
     "wh_ctx_set_profiling", "wh_ctx_phase_times", "wh_debug_e4m3_round_n",
     "wh_fp4_expert_forward_noalloc", "wh_ep_row_bytes", "wh_ep_scratch_bytes", "wh_ep_dispatch",
     "wh_ep_expert_ffn", "wh_ep_combine", "wh_ep_window_bytes", "wh_ep_window_create",
@@ -165,6 +169,7 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_moe_plan_destroy": (None, [vp]),
         "wh_moe_plan_set_fused_decode": (st, [vp, i]),
         "wh_moe_scratch_bytes": (sz, [vp, i]),
+        "wh_moe_scratch_field": (st, [vp, i, i, C.POINTER(sz), C.POINTER(sz)]),
         "wh_moe_ffn": (st, [vp, vp, vp, i, vp, vp, vp, vp, vp, sz, vp]),
         "wh_debug_act_quant_table": (None, [vp]),
         "wh_debug_e4m3_round": (f, [f]),
@@ -607,6 +612,21 @@ class MoeLayer:
                                 _ptr(ids), _ptr(weights), _ptr(self.scratch), self.scratch.numel(),
                                 _stream(stream)))
         return y
+
+    def scratch_field(self, tokens: int, field: int, dtype, shape):
+        """A view of one intermediate array of the last grouped (tensor-core)
+        call of `tokens` tokens (MOE_FIELD_*), read from the layer's scratch."""
+        import torch
+
+        off, n = C.c_size_t(), C.c_size_t()
+        _check(lib().wh_moe_scratch_field(self.plan, tokens, field, C.byref(off), C.byref(n)))
+        es = torch.empty((), dtype=dtype).element_size()
+        count = 1
+        for d in shape:
+            count *= d
+        if count * es > n.value:
+            raise ValueError(f"field {field}: {count * es} bytes asked, {n.value} there")
+        return self.scratch[off.value:off.value + count * es].view(dtype).view(*shape)
 
     def set_fused_decode(self, on: bool = True) -> None:
         """One-token calls as one persistent kernel (on) or as three kernels (default)."""

@@ -1191,6 +1191,34 @@ size_t moe_path_scratch_bytes(const wh_moe_plan* p, int tokens) {
                                 : moe_scratch_layout(p, tokens, nullptr).bytes;
 }
 
+wh_status wh_moe_scratch_field(const wh_moe_plan* p, int tokens, int field, size_t* offset,
+                               size_t* bytes) {
+  if (!p || !offset || !bytes) return fail(WH_ERR_INVALID_POINTER, "null plan/out");
+  if (tokens <= 0) return fail(WH_ERR_EMPTY_SHAPE, "tokens");
+  if (!use_grouped(p, tokens)) return fail(WH_ERR_UNSUPPORTED, "the call does not take the grouped path");
+  // lay the scratch out at a stand-in base address and report offsets from it
+  uint8_t* base = reinterpret_cast<uint8_t*>(uintptr_t(1) << 40);
+  const GroupedScratch g = grouped_scratch_layout(p, tokens, base);
+  const auto& d = p->d;
+  const size_t T = tokens, k = d.topk, R = g.rows, ne = d.num_experts + (d.shared ? 1 : 0);
+  const void* q = nullptr;
+  size_t n = 0;
+  switch (field) {
+    case WH_MOE_FIELD_SLOT: q = g.slot; n = sizeof(int) * T * k; break;
+    case WH_MOE_FIELD_OFFSETS: q = g.offsets; n = sizeof(int) * (ne + 1); break;
+    case WH_MOE_FIELD_COMBINE_W: q = g.combine_w; n = sizeof(float) * T * k; break;
+    case WH_MOE_FIELD_XQ: q = g.xq; n = R * d.hidden; break;
+    case WH_MOE_FIELD_XSF: q = g.xsf; n = R * (d.hidden / 32); break;
+    case WH_MOE_FIELD_HQ: q = g.hq; n = R * d.inter; break;
+    case WH_MOE_FIELD_HSF: q = g.hsf; n = R * (d.inter / 32); break;
+    case WH_MOE_FIELD_YROWS: q = g.yrows; n = sizeof(float) * R * d.hidden; break;
+    default: return fail(WH_ERR_UNSUPPORTED, "unknown scratch field");
+  }
+  *offset = size_t(static_cast<const uint8_t*>(q) - base);
+  *bytes = n;
+  return WH_OK;
+}
+
 size_t wh_moe_scratch_bytes(const wh_moe_plan* p, int tokens) {
   if (!p || tokens <= 0) return 0;
   size_t n = align256(moe_path_scratch_bytes(p, tokens)) +

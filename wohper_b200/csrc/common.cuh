@@ -120,6 +120,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
   return true;
 }
 
+// Producer drain before it leaves the kernel: a bounded wait that gives up at
+// once when a wait of this launch sequence has already timed out, so a failed
+// kernel returns after one timeout instead of one per ring stage.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t phase, uint32_t* status) {
+  if (status && (*(volatile uint32_t*)status & WH_DEV_TIMEOUT)) return false;
+  return mbar_wait(bar, phase, status);
+}
+
 // ---------------------------------------------------------------------------
 // system-scope flags between ranks (bounded waits, never a trap)
 // ---------------------------------------------------------------------------

@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
       }
       // no copy may be in flight when this warp leaves
       for (int i = max(0, g - nstages); i < g; ++i)
-        mbar_wait(&full[i % nstages], (i / nstages) & 1, a.status);
+        if (!mbar_drain(&full[i % nstages], (i / nstages) & 1, a.status)) break;
     }
     return;
   }
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(kRgThreads)
         }
       }
       for (int i = max(0, g - nstages); i < g; ++i)
-        mbar_wait(&full[i % nstages], (i / nstages) & 1, a.status);
+        if (!mbar_drain(&full[i % nstages], (i / nstages) & 1, a.status)) break;
     }
     return;
   }

@@ -142,10 +142,28 @@ __device__ __forceinline__ uint32_t pick4(const uint4& v, int k) {
 __device__ __forceinline__ uint8_t e4m3_byte(float q) {
   return (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
 }
-// two values -> E4M3 bytes, round to nearest even, saturated to +-448
+// two values -> E4M3 bytes, round to nearest even, saturated to +-448 (exact
+// for values already on the E4M3 grid)
 __device__ __forceinline__ uint32_t e4m3x2_rn(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// The reference's act-quant rounding of t = v / scale (src/compute.rs:2504-2545):
+// clamp to +-448 (a NaN stays NaN, as f32::clamp keeps it), then the nearest
+// E4M3 grid value with ties to the lower entry; returned as the E4M3 byte.
+// A NaN maps to the reference's lut[0] = -480, which has no E4M3 encoding
+// other than 0xFF (NaN to the tensor core); the layer's output is then
+// non-finite and the call reports NonFiniteOutput.
+__device__ __forceinline__ float aq_clamp448(float t) {
+  return t < -448.0f ? -448.0f : (t > 448.0f ? 448.0f : t);
+}
+__device__ __forceinline__ uint32_t e4m3x2_ref(float lo, float hi) {
+  const float a = e4m3_nearest_ties_lower(aq_clamp448(lo));
+  const float b = e4m3_nearest_ties_lower(aq_clamp448(hi));
+  uint32_t r = e4m3x2_rn(a, b);
+  if (a == -480.0f) r |= 0xFFu;
+  if (b == -480.0f) r |= 0xFF00u;
   return r;
 }
 
@@ -229,7 +247,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       }
       // no copy may be in flight when the CTA exits
       for (uint32_t i = g > kGStages ? g - kGStages : 0; i < g; ++i)
-        mbar_wait(&raw_full[i % kGStages], (i / kGStages) & 1, a.status);
+        if (!mbar_drain(&raw_full[i % kGStages], (i / kGStages) & 1, a.status)) break;
     }
   } else if (warp == kGWork + 1) {
     // ---------------- MMA issuer ----------------
@@ -356,10 +374,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
           float h[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            // SwiGLU with the reference clamps (src/deepseek_v4.rs:589-593)
+            // SwiGLU with the reference clamps and its silu, x / (1 + expf(-x)),
+            // with the host libm's expf (src/deepseek_v4.rs:551-554,589-593)
             const float gte = fminf(__uint_as_float(v1[j]), 10.0f);
-            const float upv = fminf(fmaxf(__uint_as_float(v3[j]), -10.0f), 10.0f);
-            h[j] = __fdividef(gte, 1.0f + __expf(-gte)) * upv;
+            float upv = __uint_as_float(v3[j]);
+            upv = upv < -10.0f ? -10.0f : upv;
+            upv = upv > 10.0f ? 10.0f : upv;
+            h[j] = __fmul_rn(silu_ref(gte), upv);
           }
           // act quant of h per token over the 64 features of warps 2p, 2p+1
           float mine = 0.0f;
@@ -391,7 +412,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             const int k0 = __shfl_sync(0xffffffffu, kj, j);
             const int k1 = __shfl_sync(0xffffffffu, kj, j + 1);
             // h / 2^k == h * 2^-k exactly
-            const uint32_t b2 = e4m3x2_rn(__fmul_rn(h[j], exp2i(-k0)), __fmul_rn(h[j + 1], exp2i(-k1)));
+            const uint32_t b2 = e4m3x2_ref(__fmul_rn(h[j], exp2i(-k0)), __fmul_rn(h[j + 1], exp2i(-k1)));
             const long long row = un.z + n0 + j;
             if (n0 + j < un.w) a.hq[row * a.M + feat] = (uint8_t)(b2 & 0xff);
             if (n0 + j + 1 < un.w) a.hq[(row + 1) * a.M + feat] = (uint8_t)(b2 >> 8);

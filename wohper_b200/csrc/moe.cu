@@ -568,8 +568,8 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
       }
       // leave no copy in flight if the consumers stopped early
       for (int k = max(0, i - kUpStages); k < i; ++k)
-        mbar_wait(&full[k % kUpStages], (k / kUpStages) & 1, a.status);
-      mbar_wait(xbar, 0, a.status);
+        if (!mbar_drain(&full[k % kUpStages], (k / kUpStages) & 1, a.status)) break;
+      mbar_drain(xbar, 0, a.status);
     }
     return;
   }
@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(kDownThreads) moe_down_kernel(MoeArgs a, const
         }
       }
       for (int i = max(0, nbox - kDownStages); i < nbox; ++i)
-        mbar_wait(&full[i % kDownStages], (i / kDownStages) & 1, a.status);
+        if (!mbar_drain(&full[i % kDownStages], (i / kDownStages) & 1, a.status)) break;
     }
     return;
   }

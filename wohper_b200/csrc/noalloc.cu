@@ -12,10 +12,15 @@
 // the array has to start at zero or be cleared between calls.  Larger experts
 // are rejected with WH_ERR_SCRATCH_TOO_SMALL before anything is launched.
 //
-// Set-up: the array's device address is looked up once per device, with that
-// device current, by cudaGetSymbolAddress (which may load the module on that
-// device); host code passes only that looked-up pointer to the kernels.  Make
-// the first call on each device before any stream capture begins.
+// Set-up: the array's device address is looked up once per device context,
+// with that device current, by cudaGetSymbolAddress (which may load the
+// module on that device); host code passes only that looked-up pointer to the
+// kernels.  Make the first call on each device before any stream capture
+// begins.  The lookup is keyed by the driver's context id (cuCtxGetId, never
+// reused): after cudaDeviceReset the primary context is created anew, the
+// module is loaded again and the array may move, so the next call looks it up
+// again instead of launching on the old address.  That call is again a first
+// call and belongs before any stream capture.
 //
 // The array is one per device and process: calls that overlap in time on one
 // device (two streams, two threads, two contexts) race on it.  Calls issued in
@@ -36,17 +41,49 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {};
+unsigned long long g_noalloc_ctx_id[kMaxDevices] = {};
 
-// Device address of g_expert_scratch on the current device, looked up once.
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the current driver context (unique for the life of the process).
+wh_status current_ctx_id(unsigned long long* id) {
+  static PfnCtxGetCurrent get_current = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PfnCtxGetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PfnCtxGetId>(p);
+  });
+  if (!get_current || !get_id) return fail(WH_ERR_CUDA, "cuCtxGetCurrent/cuCtxGetId unavailable");
+  CUcontext cx = nullptr;
+  if (get_current(&cx) != CUDA_SUCCESS || !cx) return fail(WH_ERR_CUDA, "no current CUDA context");
+  if (get_id(cx, id) != CUDA_SUCCESS) return fail(WH_ERR_CUDA, "cuCtxGetId failed");
+  return WH_OK;
+}
+
+// Device address of g_expert_scratch in the current context of `device`,
+// looked up once per context.
 wh_status noalloc_scratch(int device, float** out) {
   if (device < 0 || device >= kMaxDevices) return fail(WH_ERR_UNSUPPORTED, "device ordinal >= 64");
+  unsigned long long id = 0;
+  wh_status st = current_ctx_id(&id);
+  if (st != WH_OK) return st;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[device]) {
+  if (!g_noalloc_ptr[device] || g_noalloc_ctx_id[device] != id) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_expert_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(expert scratch)");
     if (!p || !aligned(p, 256)) return fail(WH_ERR_CUDA, "expert scratch address not 256-aligned");
     g_noalloc_ptr[device] = static_cast<float*>(p);
+    g_noalloc_ctx_id[device] = id;
   }
   *out = g_noalloc_ptr[device];
   return WH_OK;
