@@ -456,6 +456,15 @@ def run_ours(args):
         }
     layer.close()
     ctx.close()
+    del stack
+    torch.cuda.empty_cache()
+    if not args.no_ep:
+        # the path that shards: config 4's expert-parallel layer on the same
+        # ranks, so that a 1 -> N scaling run records its curve
+        ep = ep_measure(args, world, rank, local, "p2p")
+        if rank == 0:
+            result["ep"] = ep
+            result["gpu_launches"] += 11 * args.steps
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, n, cores = cpu_run(steps=24, warmup=1, budget_s=20.0)
         result["cpu_baseline"] = {
@@ -913,20 +922,18 @@ def config4_cpu(T_sample: int):
     return T_sample / dt, O.threads()
 
 
-def run_config4(args):
+def ep_measure(args, world: int, rank: int, local: int, transport: str = "p2p"):
+    """Config 4 on this process group: T4 tokens per step split over the ranks,
+    the 256 experts sharded contiguously.  Returns (rank 0) a dict with the
+    step time (max over ranks), the per-phase medians over the timed steps
+    and the per-rank roofline; None on the other ranks."""
     import torch
     import torch.distributed as dist
 
-    world, rank, local = dist_setup(args.gpus)
     import wohper_b200 as W
     from tests import helpers as H
     from wohper_b200.ep import DeviceOps, EpMoeLayer
 
-    if world == 1 and not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29631")
-        dist.init_process_group("nccl", rank=0, world_size=1,
-                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     ctx = W.Context(local)
     El = E // world
@@ -940,7 +947,7 @@ def run_config4(args):
 
     Tl = T4 // world
     layer = EpMoeLayer(ctx, [wexp(e) for e in range(El)], wexp(El), world,
-                       transport=args.ep_transport, max_tokens=Tl)
+                       transport=transport, max_tokens=Tl)
     ids_all, w_all = config4_routes(4000)
     lo = rank * Tl
     x = torch.from_numpy(H.activations(4200 + rank, Tl, HID)).to(dev)
@@ -965,72 +972,137 @@ def run_config4(args):
             ev[k][1].record(stream)
         torch.cuda.synchronize()
     barrier(world)
+    ctx.sync()
     ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
-    # phase split of one step (events between the calls and collectives)
+    # phase split: events between the calls on every timed-length pass, the
+    # median of each phase over the steps, then the max over ranks
     flat = ids.reshape(-1).to(torch.int64) // El
     per_dest = torch.bincount(flat, minlength=world).tolist()
-    if args.ep_transport == "p2p":
-        pe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        flush.zero_()
-        layer.forward_p2p(x, ids, wts, marks=lambda i: pe[i].record(stream))
-        torch.cuda.synchronize()
+    if transport == "p2p":
+        names = ["dispatch_and_row_stores", "expert_ffn_and_result_stores", "wait_and_combine"]
+        samples = []
+        for k in range(args.steps):
+            pe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            flush.zero_()
+            layer.forward_p2p(x, ids, wts, marks=lambda i: pe[i].record(stream))
+            torch.cuda.synchronize()
+            samples.append([pe[i].elapsed_time(pe[i + 1]) for i in range(3)])
         ctx.sync()
-        ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(3)]
-        phases = {"dispatch_and_row_stores": round(ph[0], 4),
-                  "expert_ffn_and_result_stores": round(ph[1], 4),
-                  "wait_and_combine": round(ph[2], 4)}
+        med = np.median(np.array(samples), axis=0)
+        ph = [all_max(world, float(v)) for v in med]
     else:
+        names = ["dispatch", "all_to_all_rows", "expert_ffn", "all_to_all_results", "combine"]
         ops = DeviceOps(layer)
-        pe = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        flush.zero_()
-        pe[0].record(stream)
-        send, cnt, pos = ops.dispatch(x, ids)
-        rc = torch.empty_like(cnt)
-        dist.all_to_all_single(rc, cnt)
-        both = ops.to_list(ops.cat([cnt.view(world, El).sum(1), rc.view(world, El).sum(1)]))
-        per_dest, per_src = both[:world], both[world:]
-        R = sum(per_src)
-        recv = ops.empty_rows(R)
-        pe[1].record(stream)
-        dist.all_to_all_single(recv, send, output_split_sizes=per_src, input_split_sizes=per_dest)
-        pe[2].record(stream)
-        y_rows = ops.expert_ffn(recv, rc, R, x)
-        pe[3].record(stream)
-        y_back = ops.empty_results(send.shape[0])
-        dist.all_to_all_single(y_back, y_rows[:R], output_split_sizes=per_dest,
-                               input_split_sizes=per_src)
-        pe[4].record(stream)
-        ops.combine(ids, wts, pos, y_back, y_rows[R:])
-        pe[5].record(stream)
-        torch.cuda.synchronize()
+        samples = []
+        for k in range(args.steps):
+            pe = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            flush.zero_()
+            pe[0].record(stream)
+            send, cnt, pos = ops.dispatch(x, ids)
+            rc = torch.empty_like(cnt)
+            dist.all_to_all_single(rc, cnt)
+            both = ops.to_list(ops.cat([cnt.view(world, El).sum(1), rc.view(world, El).sum(1)]))
+            pdst, psrc = both[:world], both[world:]
+            R = sum(psrc)
+            recv = ops.empty_rows(R)
+            pe[1].record(stream)
+            dist.all_to_all_single(recv, send, output_split_sizes=psrc, input_split_sizes=pdst)
+            pe[2].record(stream)
+            y_rows = ops.expert_ffn(recv, rc, R, x)
+            pe[3].record(stream)
+            y_back = ops.empty_results(send.shape[0])
+            dist.all_to_all_single(y_back, y_rows[:R], output_split_sizes=pdst,
+                                   input_split_sizes=psrc)
+            pe[4].record(stream)
+            ops.combine(ids, wts, pos, y_back, y_rows[R:])
+            pe[5].record(stream)
+            torch.cuda.synchronize()
+            samples.append([pe[i].elapsed_time(pe[i + 1]) for i in range(5)])
         ctx.sync()
-        ph = [all_max(world, pe[i].elapsed_time(pe[i + 1])) for i in range(5)]
-        phases = {"dispatch": round(ph[0], 4), "all_to_all_rows": round(ph[1], 4),
-                  "expert_ffn": round(ph[2], 4), "all_to_all_results": round(ph[3], 4),
-                  "combine": round(ph[4], 4)}
+        med = np.median(np.array(samples), axis=0)
+        ph = [all_max(world, float(v)) for v in med]
+    phases = {n: round(v, 4) for n, v in zip(names, ph)}
     rb = layer.row_bytes
     sent_remote = sum(n for d, n in enumerate(per_dest) if d != rank)
+    # per-rank roofline: the rank's local experts' weights once, its rows in
+    # and results out; FLOPs of the routed rows it receives (T4*topk/world on
+    # average) and of the shared expert over its own tokens
+    flops_rank = (T4 * TOPK / world + Tl) * 2 * 3 * HID * INTER
+    bytes_rank = (El + 1) * EXPERT_BYTES
+    link_bytes = (T4 * TOPK / world) * (world - 1) / world * (rb + 4 * HID)
+    hbm, _ = peaks()
+    tflops_peak = 2 * bf16_peak()
+    t_tensor = flops_rank / (tflops_peak * 1e12)
+    t_hbm = bytes_rank / (hbm * 1e9)
+    t_link = link_bytes / (770e9) if world > 1 else 0.0
+    bound = max(("tensor", t_tensor), ("hbm", t_hbm), ("nvlink", t_link), key=lambda p: p[1])
     res = None
     if rank == 0:
         res = {
-            "metric": METRIC4, "value": round(T4 / (ms_step * 1e-3), 1), "unit": "tokens/s",
+            "tokens_per_s": round(T4 / (ms_step * 1e-3), 1), "ms_per_step": round(ms_step, 5),
+            "n_gpus": world, "tokens": T4, "tokens_per_rank": Tl, "experts_per_rank": El,
+            "transport": transport, "dispatch_row_bytes": int(rb),
+            "phases_ms_median_over_steps_max_over_ranks": phases,
+            "rank0_remote_rows_sent": sent_remote,
+            "roofline_per_rank": {
+                "bound": bound[0], "target_ms": round(bound[1] * 1e3, 4),
+                "frac": round(bound[1] * 1e3 / ms_step, 4),
+                "tensor_tflops_achieved": round(flops_rank / (ms_step * 1e-3) / 1e12, 1),
+                "tensor_peak_tflops": tflops_peak,
+                "tensor_peak_kind": "2 x measured bf16 dense (B200's fp8 kind::f8f6f4 rate is "
+                                    "twice its bf16 rate)",
+                "flops_per_rank": flops_rank, "hbm_bytes_per_rank": bytes_rank,
+                "nvlink_bytes_per_rank": int(link_bytes), "nvlink_gbs_per_direction": 770.0},
+            "gpu_launches_per_step": 11,
+            "clocks": clk.summary(),
+        }
+    layer.close()
+    ctx.close()
+    return res
+
+
+def bf16_peak() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
+def run_config4(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup(args.gpus)
+    if world == 1 and not dist.is_initialized() and args.ep_transport == "nccl":
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29631")
+        dist.init_process_group("nccl", rank=0, world_size=1,
+                                device_id=torch.device("cuda", local))
+    m = ep_measure(args, world, rank, local, args.ep_transport)
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC4, "value": m["tokens_per_s"], "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": m["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None,
             "dtype": "fp4-e2m1 (as e4m3) x fp8-e4m3, ue8m0 block scales, f32 accumulate",
             "data": "synthetic (seeded random-init weights, N(0,1) tokens, uniform routes)",
             "config": {"workload": WORKLOAD4, "experts": E, "topk": TOPK, "hidden": HID,
-                       "inter": INTER, "tokens": T4, "tokens_per_rank": Tl,
-                       "experts_per_rank": El, "dispatch_row_bytes": int(rb),
+                       "inter": INTER, "tokens": T4, "tokens_per_rank": m["tokens_per_rank"],
+                       "experts_per_rank": m["experts_per_rank"],
+                       "dispatch_row_bytes": m["dispatch_row_bytes"],
                        "l2": "flushed between steps (256 MiB memset outside the timed events)",
                        "parallelism": f"expert parallel x{world}"},
             "transport": args.ep_transport,
-            "phases_ms_max_over_ranks": phases,
-            "rank0_remote_rows_sent": sent_remote,
+            "phases_ms_median_over_steps_max_over_ranks":
+                m["phases_ms_median_over_steps_max_over_ranks"],
+            "rank0_remote_rows_sent": m["rank0_remote_rows_sent"],
+            "roofline_per_rank": m["roofline_per_rank"],
             # count, scan, pack | totals, units, permute, pack_local, map_tail, up,
             # down | combine (the NCCL transport adds the collectives' kernels)
             "gpu_launches": 11 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": m["clocks"],
         }
         if not args.no_cpu_baseline:
             v, th = config4_cpu(16)
@@ -1038,9 +1110,8 @@ def run_config4(args):
                                    "kind": "port",
                                    "sample": "16 tokens of the workload through the C++ "
                                              "restatement's batched path, one host"}
-    layer.close()
-    ctx.close()
-    dist.destroy_process_group()
+    if dist.is_initialized():
+        dist.destroy_process_group()
     return res
 
 
@@ -1866,6 +1937,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="config 2: skip the nested config-4 expert-parallel measurement")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="1: one FP8 GEMV 4096x4096; 2: one-token decode FFN (default); "
                          "3: 2048-token batched FFN; 4: expert-parallel layer over the ranks")

@@ -381,6 +381,18 @@ wh_status wh_ep_p2p_expert_ffn(wh_ctx* ctx, wh_ep_window* window, const float* x
 wh_status wh_ep_p2p_combine(wh_ctx* ctx, wh_ep_window* window, const int32_t* ids,
                             const float* weights, const int32_t* pos, int tokens,
                             const float* y_shared, float* y, wh_stream_t stream);
+/* The whole expert-parallel MoE layer on a connected window in one call:
+ * wh_ep_p2p_dispatch -> wh_ep_p2p_expert_ffn -> wh_ep_p2p_combine, with the
+ * route positions and the shared expert's output kept in the window's
+ * rank-private memory.  x, y: [tokens][hidden] f32 of this rank's tokens
+ * (tokens <= the window's max_tokens); ids, weights: [tokens][topk] routes
+ * (global expert ids).  Every rank calls it once per step, in the same order;
+ * the step splits the reference's batched MoE (accumulate_expert_for_positions
+ * + finish, src/compute.rs:1779-1870) over the ranks, which the reference,
+ * running on one host, has no counterpart for. */
+wh_status wh_ep_moe_layer(wh_ctx* ctx, wh_ep_window* window, const float* x, int tokens,
+                          const int32_t* ids, const float* weights, float* y,
+                          wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* MLA attention (DeepSeek-V4 decode)                                          */
@@ -411,6 +423,59 @@ wh_status wh_mla_attention(wh_ctx* ctx, const float* q, int heads, int head_dim,
                            const float* keys, int key_stride, int token_pos, int window,
                            const float* compressed, int compressed_count, const float* sink,
                            const float* inv_freqs, float* out, wh_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* DeepSeek-V4 attention block: norm and the MLA projection path               */
+/* ------------------------------------------------------------------------ */
+/* Replaces apply_weighted_rms_norm (src/compute.rs:3077-3115) or, with
+ * weight_bf16 NULL, rms_norm_in_place (src/compute.rs:7110-7122) for
+ * `segments` vectors of n floats each (n <= 4096; in and out may be the same):
+ * mean of squares summed in index order, inv = 1/sqrt(ms + 1e-6),
+ * out = (x * inv) * weight.  Bit-exact. */
+wh_status wh_rms_norm(wh_ctx* ctx, const float* in, float* out, int segments, int n,
+                      const uint16_t* weight_bf16, wh_stream_t stream);
+
+/* The reference's grouped low-rank projection wo_a (src/compute.rs:4244-4258:
+ * gemv_fp8_e4m3_ue8m0_rows per group): row r of [row_start, row_end) reads
+ * the input x + (r / group_rows) * group_offset (+ b * ldx for input b), with
+ * the optional fused act quant applied to each group's input alone.  Bit-exact
+ * as wh_fp8_gemv; y[b * ldy + r - row_start]. */
+wh_status wh_fp8_gemv_grouped(wh_ctx* ctx, const uint8_t* weight, const uint8_t* scale, int rows,
+                              int cols, int scale_rows, int scale_cols, int row_start,
+                              int row_end, const float* x, int batch, int ldx, int group_rows,
+                              long long group_offset, float* y, int ldy, int act_quant_block,
+                              wh_stream_t stream);
+
+/* One layer's MLA attention weights (DeepSeek-V4-Flash: hidden 4096, 64 heads
+ * of 512 = 448 nope + 64 rope, q_lora_rank 1024, 8 output groups of rank 1024,
+ * sliding window 128).  FP8 E4M3 matrices with UE8M0 128x128 scales. */
+typedef struct wh_v4_attn {
+  int hidden, heads, head_dim, nope_dim, q_lora_rank, o_groups, o_lora_rank, window;
+  wh_fp8_matrix wq_a;   /* [q_lora_rank][hidden] */
+  wh_fp8_matrix wq_b;   /* [heads * head_dim][q_lora_rank] */
+  wh_fp8_matrix wkv;    /* [head_dim][hidden] */
+  wh_fp8_matrix wo_a;   /* [o_groups * o_lora_rank][heads * head_dim / o_groups] */
+  wh_fp8_matrix wo_b;   /* [hidden][o_groups * o_lora_rank] */
+  const uint16_t* q_norm;  /* bf16 [q_lora_rank] (q_a_layernorm), NULL: unweighted */
+  const uint16_t* kv_norm; /* bf16 [head_dim] (kv_a_layernorm), NULL: unweighted */
+  const float* sink;       /* [heads] attention sink, nullable */
+} wh_v4_attn;
+/* Floats of scratch wh_v4_attention needs. */
+size_t wh_v4_attention_scratch_len(const wh_v4_attn* layer);
+/* Replaces compute_deepseek_v4_mla_attention (src/compute.rs:3924-4293) for
+ * one token, bit-exact: hidden [hidden] holds the normed attention input on
+ * entry and the attention output on return.  q path wq_a -> q_norm -> act
+ * quant -> wq_b -> per-head RMS -> RoPE; kv path wkv -> kv_norm -> RoPE of
+ * the rope dims -> act quant of the nope dims, stored into kv_cache row
+ * token_pos (row stride kv_stride); the attention core of wh_mla_attention
+ * over the window and the compressed rows (produced by the caller's
+ * compressor); act quant -> grouped wo_a -> act quant -> wo_b.  inv_freqs:
+ * HOST array, the layer's rope_inv_freqs.  The MLA workspace is context-owned:
+ * calls on one context are serialised by the caller. */
+wh_status wh_v4_attention(wh_ctx* ctx, const wh_v4_attn* layer, int token_pos, float* hidden,
+                          float* kv_cache, int kv_stride, const float* compressed,
+                          int compressed_count, const float* inv_freqs, float* scratch,
+                          size_t scratch_len, wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* mHC hyper-connections (DeepSeek-V4)                                         */

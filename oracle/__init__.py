@@ -106,6 +106,10 @@ def lib() -> C.CDLL:
         L.orc_rope_inv_freqs.restype = None
         L.orc_mla_attention.argtypes = [vp, sz, sz, sz, vp, sz, sz, sz, vp, sz, vp, vp, vp]
         L.orc_mla_attention.restype = None
+        L.orc_rms_norm.argtypes = [vp, sz, vp, vp]
+        L.orc_rms_norm.restype = None
+        L.orc_v4_attention.argtypes = [C.c_void_p, sz, vp, vp, sz, vp, sz, vp]
+        L.orc_v4_attention.restype = i
         L.orc_hc_split_sinkhorn.argtypes = [vp, sz, vp, sz, vp, sz, sz, sz, f, vp, vp, vp]
         L.orc_hc_split_sinkhorn.restype = i
         L.orc_hc_pre.argtypes = [vp, sz, sz, vp, sz, vp, vp, sz, sz, sz, f, vp, vp, vp]
@@ -398,3 +402,34 @@ def fp4_expert_hidden(expert: Fp4Expert, x):
     st = lib().orc_fp4_expert_forward(C.byref(expert), _p(x), x.size, _p(y), y.size, _p(scratch),
                                       2 * inter)
     return st, scratch[:inter].copy()
+
+
+def rms_norm(x, weight_bf16=None):
+    """apply_weighted_rms_norm / rms_norm_in_place of each row of x."""
+    x = _c(x, np.float32)
+    w = None if weight_bf16 is None else _c(weight_bf16, np.uint16)
+    rows = x.reshape(-1, x.shape[-1])
+    out = np.zeros_like(rows)
+    for i in range(rows.shape[0]):
+        lib().orc_rms_norm(_p(rows[i]), rows.shape[1], _p(w), _p(out[i]))
+    return out.reshape(x.shape)
+
+
+class V4Attn(C.Structure):
+    _fields_ = [(n, C.c_size_t) for n in ("hidden", "heads", "head_dim", "nope_dim",
+                                          "q_lora_rank", "o_groups", "o_lora_rank", "window")] + [
+        ("wq_a", Fp8Matrix), ("wq_b", Fp8Matrix), ("wkv", Fp8Matrix), ("wo_a", Fp8Matrix),
+        ("wo_b", Fp8Matrix), ("q_norm", C.c_void_p), ("kv_norm", C.c_void_p),
+        ("sink", C.c_void_p)]
+
+
+def v4_attention(layer: V4Attn, token_pos, hidden, kv_cache, compressed, inv_freqs):
+    """compute_deepseek_v4_mla_attention for one token: (status, out [hidden]);
+    kv_cache [positions, stride] (numpy, row token_pos is written)."""
+    h = np.array(hidden, np.float32, copy=True)
+    comp = None if compressed is None else _c(compressed, np.float32)
+    fr = _c(inv_freqs, np.float32)
+    st = lib().orc_v4_attention(C.byref(layer), token_pos, _p(h), _p(kv_cache),
+                                kv_cache.shape[1], _p(comp), 0 if comp is None else comp.shape[0],
+                                _p(fr))
+    return st, h

@@ -1207,4 +1207,66 @@ int orc_moe_batched(const orc_fp4_expert* experts, size_t num_experts, const int
   return ORC_OK;
 }
 
+
+static inline float bf16_value(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// apply_weighted_rms_norm (src/compute.rs:3077-3115) / rms_norm_in_place
+// (src/compute.rs:7110-7122): the mean of squares summed in index order
+// (Iterator::sum), eps 1e-6, then (x * inv_rms) * weight.
+void orc_rms_norm(const float* in, size_t n, const uint16_t* weight_bf16, float* out) {
+  if (n == 0) return;
+  float sum = 0.0f;
+  for (size_t i = 0; i < n; ++i) sum += in[i] * in[i];
+  const float mean_square = sum / (float)n;
+  const float inv_rms = 1.0f / sqrtf(mean_square + 1.0e-6f);
+  for (size_t i = 0; i < n; ++i)
+    out[i] = weight_bf16 ? in[i] * inv_rms * bf16_value(weight_bf16[i]) : in[i] * inv_rms;
+}
+
+// compute_deepseek_v4_mla_attention (src/compute.rs:3924-4293), the compressor's
+// rows given: q path (:3994-4040), kv path (:4041-4075), the attention core
+// (orc_mla_attention, :4080-4185), the grouped output projection (:4230-4293).
+int orc_v4_attention(const orc_v4_attn* L, size_t token_pos, float* hidden, float* kv_cache,
+                     size_t kv_stride, const float* compressed, size_t compressed_count,
+                     const float* inv_freqs) {
+  const size_t hd = L->head_dim, nope = L->nope_dim, heads = L->heads, hidden_n = L->hidden;
+  const size_t q_full = heads * hd, groups = L->o_groups, o_lora = L->o_lora_rank;
+  if (groups == 0 || o_lora == 0 || q_full % groups != 0) return ORC_ERR_INVALID_SHAPE;
+  const size_t group_in = q_full / groups, o_mid_len = groups * o_lora;
+  std::vector<float> x_fp8(hidden, hidden + hidden_n), q_lora(L->q_lora_rank), q(q_full),
+      kv(hd), attn(q_full), o_mid(o_mid_len);
+  act_quant(x_fp8.data(), x_fp8.size(), 64);
+  int st = fp8_gemv_full(L->wq_a, x_fp8.data(), q_lora.data());
+  if (st != ORC_OK) return st;
+  orc_rms_norm(q_lora.data(), q_lora.size(), L->q_norm, q_lora.data());
+  act_quant(q_lora.data(), q_lora.size(), 64);
+  if ((st = fp8_gemv_full(L->wq_b, q_lora.data(), q.data())) != ORC_OK) return st;
+  for (size_t h = 0; h < heads; ++h) orc_rms_norm(&q[h * hd], hd, nullptr, &q[h * hd]);
+  for (size_t h = 0; h < heads; ++h)
+    rope_pairs(&q[h * hd + nope], token_pos, inv_freqs, (hd - nope) / 2, false);
+  if ((st = fp8_gemv_full(L->wkv, x_fp8.data(), kv.data())) != ORC_OK) return st;
+  orc_rms_norm(kv.data(), hd, L->kv_norm, kv.data());
+  rope_pairs(&kv[nope], token_pos, inv_freqs, (hd - nope) / 2, false);
+  act_quant(kv.data(), nope, 64);
+  std::copy(kv.begin(), kv.end(), kv_cache + token_pos * kv_stride);
+  orc_mla_attention(q.data(), heads, hd, nope, kv_cache, kv_stride, token_pos, L->window,
+                    compressed, compressed_count, L->sink, inv_freqs, attn.data());
+  act_quant(attn.data(), attn.size(), 64);
+  for (size_t g = 0; g < groups; ++g) {
+    const orc_fp8_matrix& m = L->wo_a;
+    st = orc_fp8_gemv_rows(m.weight, m.rows * m.cols, m.rows, m.cols, m.scale,
+                           m.scale_rows * m.scale_cols, m.scale_rows, m.scale_cols, g * o_lora,
+                           (g + 1) * o_lora, &attn[g * group_in], group_in, &o_mid[g * o_lora],
+                           o_lora);
+    if (st != ORC_OK) return st;
+  }
+  act_quant(o_mid.data(), o_mid.size(), 64);
+  return fp8_gemv_full(L->wo_b, o_mid.data(), hidden);
+}
+
 }  // extern "C"

@@ -80,3 +80,20 @@ def test_ep_two_ranks():
                        env=env, cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     assert "ep world=2" in r.stdout
+
+
+def test_ep_all_gpus_config4_shape():
+    """BASELINE config 4 at its own shape on every visible GPU (4 or 8): 256
+    experts sharded contiguously, 8192 tokens; both transports equal the
+    world-1 layer and each other, and a token sample matches the CPU oracle."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 or more GPUs")
+    n = 8 if torch.cuda.device_count() >= 8 else 4
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        f"--nproc-per-node={n}", "--master-addr=127.0.0.1",
+                        f"--master-port={_port()}", str(ROOT / "tests" / "ep_worker.py"), "v4"],
+                       env=env, cwd=ROOT, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    assert f"ep world={n} v4 shape" in r.stdout
+    print(r.stdout[-2500:])

@@ -70,7 +70,8 @@ EXPORTS = (
     "wh_fp4_expert_forward_noalloc", "wh_ep_row_bytes", "wh_ep_scratch_bytes", "wh_ep_dispatch",
     "wh_ep_expert_ffn", "wh_ep_combine", "wh_ep_window_bytes", "wh_ep_window_create",
     "wh_ep_window_connect", "wh_ep_window_destroy", "wh_ep_p2p_dispatch",
-    "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine", "wh_moe_plan_set_fused_decode",
+    "wh_ep_p2p_expert_ffn", "wh_ep_p2p_combine", "wh_ep_moe_layer",
+    "wh_moe_plan_set_fused_decode",
     "wh_zcblk_parse", "wh_zcblk_tensor_at", "wh_zcblk_tensor_dim", "wh_zcblk_find_suffix",
     "wh_zcblk_fp4_expert", "wh_fp4_expert_device_bytes", "wh_fp4_expert_upload",
     "wh_model_open", "wh_model_close", "wh_model_get_header", "wh_model_layer_count",
@@ -79,7 +80,8 @@ EXPORTS = (
     "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
     "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward", "wh_rope_inv_freqs",
     "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf", "wh_hc_pre",
-    "wh_hc_post", "wh_hc_head",
+    "wh_hc_post", "wh_hc_head", "wh_rms_norm", "wh_fp8_gemv_grouped",
+    "wh_v4_attention_scratch_len", "wh_v4_attention",
 )
 
 
@@ -164,11 +166,17 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_ep_p2p_dispatch": (st, [vp, vp, vp, i, vp, vp, vp]),
         "wh_ep_p2p_expert_ffn": (st, [vp, vp, vp, i, vp, vp]),
         "wh_ep_p2p_combine": (st, [vp, vp, vp, vp, vp, i, vp, vp, vp]),
+        "wh_ep_moe_layer": (st, [vp, vp, vp, i, vp, vp, vp, vp]),
         "wh_router_topk": (st, [vp, vp, i, i, vp, i, i, i, vp, f, vp, vp, vp, vp, vp]),
         "wh_moe_plan_create": (st, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
         "wh_moe_plan_destroy": (None, [vp]),
         "wh_moe_plan_set_fused_decode": (st, [vp, i]),
         "wh_moe_scratch_bytes": (sz, [vp, i]),
+        "wh_rms_norm": (st, [vp, vp, vp, i, i, vp, vp]),
+        "wh_fp8_gemv_grouped": (st, [vp, vp, vp, i, i, i, i, i, i, vp, i, i, i, C.c_longlong, vp,
+                                     i, i, vp]),
+        "wh_v4_attention_scratch_len": (sz, [vp]),
+        "wh_v4_attention": (st, [vp, vp, i, vp, vp, i, vp, i, vp, vp, sz, vp]),
         "wh_moe_scratch_field": (st, [vp, i, i, C.POINTER(sz), C.POINTER(sz)]),
         "wh_moe_ffn": (st, [vp, vp, vp, i, vp, vp, vp, vp, vp, sz, vp]),
         "wh_debug_act_quant_table": (None, [vp]),
@@ -559,6 +567,104 @@ def hc_head(ctx: Context, fn, scale: float, base, x, hc: int, hidden: int,
     _check(lib().wh_hc_head(ctx.handle, _ptr(fn), float(scale), _ptr(base), _ptr(x), tokens,
                             hc, hidden, eps, _ptr(out), _stream(stream)))
     return out
+
+
+# --------------------------------------------------------------------------
+# DeepSeek-V4 attention block (src/compute.rs:3077-3115, 3924-4293)
+# --------------------------------------------------------------------------
+def rms_norm(ctx: Context, x, weight_bf16=None, out=None, stream=None):
+    """apply_weighted_rms_norm (weight: bf16 bits [n]) or rms_norm_in_place
+    (weight None) of every row of x [..., n] f32 on the device."""
+    import torch
+
+    n = x.shape[-1]
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib().wh_rms_norm(ctx.handle, _ptr(x), _ptr(out), x.numel() // n, n,
+                             _ptr(weight_bf16), _stream(stream)))
+    return out
+
+
+def gemv_fp8_e4m3_ue8m0_grouped(ctx: Context, weight, scale, x, group_rows: int,
+                                group_offset: int, row_start: int = 0, row_end=None, out=None,
+                                act_quant_block: int = 0, stream=None):
+    """The reference's grouped wo_a (gemv_fp8_e4m3_ue8m0_rows per group): row r
+    reads x[(r // group_rows) * group_offset:][:cols]."""
+    import torch
+
+    rows, cols = weight.shape
+    srows, scols = scale.shape
+    row_end = rows if row_end is None else row_end
+    if out is None:
+        out = torch.empty(row_end - row_start, device=x.device, dtype=torch.float32)
+    _check(lib().wh_fp8_gemv_grouped(ctx.handle, _ptr(weight), _ptr(scale), rows, cols, srows,
+                                     scols, row_start, row_end, _ptr(x), 1, x.numel(),
+                                     group_rows, group_offset, _ptr(out), out.numel(),
+                                     act_quant_block, _stream(stream)))
+    return out
+
+
+class V4AttnSpec(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "heads", "head_dim", "nope_dim", "q_lora_rank",
+                                       "o_groups", "o_lora_rank", "window")] + [
+        ("wq_a", Fp8MatrixSpec), ("wq_b", Fp8MatrixSpec), ("wkv", Fp8MatrixSpec),
+        ("wo_a", Fp8MatrixSpec), ("wo_b", Fp8MatrixSpec), ("q_norm", C.c_void_p),
+        ("kv_norm", C.c_void_p), ("sink", C.c_void_p)]
+
+
+@dataclass
+class V4Attention:
+    """One layer's MLA attention weights (device tensors): Fp8Matrix projections,
+    bf16-bit norms (or None) and the attention sink (or None)."""
+    wq_a: "Fp8Matrix"
+    wq_b: "Fp8Matrix"
+    wkv: "Fp8Matrix"
+    wo_a: "Fp8Matrix"
+    wo_b: "Fp8Matrix"
+    q_norm: object = None
+    kv_norm: object = None
+    sink: object = None
+    hidden: int = 4096
+    heads: int = 64
+    head_dim: int = 512
+    nope_dim: int = 448
+    q_lora_rank: int = 1024
+    o_groups: int = 8
+    o_lora_rank: int = 1024
+    window: int = DEEPSEEK_V4_SLIDING_WINDOW
+
+    def spec(self) -> V4AttnSpec:
+        return V4AttnSpec(self.hidden, self.heads, self.head_dim, self.nope_dim,
+                          self.q_lora_rank, self.o_groups, self.o_lora_rank, self.window,
+                          self.wq_a.spec(), self.wq_b.spec(), self.wkv.spec(), self.wo_a.spec(),
+                          self.wo_b.spec(), _ptr(self.q_norm), _ptr(self.kv_norm),
+                          _ptr(self.sink))
+
+
+def v4_attention_scratch_len(layer: V4Attention) -> int:
+    s = layer.spec()
+    return int(lib().wh_v4_attention_scratch_len(C.byref(s)))
+
+
+def v4_attention(ctx: Context, layer: V4Attention, token_pos: int, hidden, kv_cache, inv_freqs,
+                 compressed=None, scratch=None, stream=None):
+    """compute_deepseek_v4_mla_attention for one token on the device, bit-exact:
+    hidden [hidden] f32 (normed input) is overwritten by the attention output;
+    kv_cache [positions, stride] f32 gets row token_pos."""
+    import numpy as np
+    import torch
+
+    s = layer.spec()
+    n = int(lib().wh_v4_attention_scratch_len(C.byref(s)))
+    if scratch is None:
+        scratch = torch.empty(n, dtype=torch.float32, device=hidden.device)
+    fr = np.ascontiguousarray(inv_freqs, dtype=np.float32)
+    cc = 0 if compressed is None else compressed.shape[0]
+    _check(lib().wh_v4_attention(ctx.handle, C.byref(s), token_pos, _ptr(hidden), _ptr(kv_cache),
+                                 kv_cache.stride(0), _ptr(compressed), cc,
+                                 fr.ctypes.data if fr.size else None, _ptr(scratch),
+                                 scratch.numel(), _stream(stream)))
+    return hidden
 
 
 class MoeLayer:

@@ -462,10 +462,12 @@ wh_status wh_act_quant_fp8(wh_ctx* c, float* v, size_t n, int block, wh_stream_t
 
 namespace {
 // wh_fp8_gemv with an optional addend (laid out like y): y = gemv + addend
+// x_group_rows > 0: row r reads the input at x + (r / x_group_rows) * x_group_off
 wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows,
                         int cols, int scale_rows, int scale_cols, int row_start, int row_end,
                         const float* x, int batch, int ldx, float* y, int ldy,
-                        int act_quant_block, const float* addend, wh_stream_t stream) {
+                        int act_quant_block, const float* addend, wh_stream_t stream,
+                        int x_group_rows = 0, long long x_group_off = 0) {
   if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
   // src/compute.rs:6256-6289 validation order
   if (rows <= 0 || cols <= 0 || scale_rows <= 0 || scale_cols <= 0 || rows % scale_rows != 0 ||
@@ -496,16 +498,25 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
   a.act_quant_block = act_quant_block;
   a.status = c->status;
   a.addend = addend;
+  a.x_group_rows = x_group_rows;
+  a.x_group_off = x_group_off;
 
-  const bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
-                    ldx % 4 == 0 && fp8_gemv_smem_bytes(1, cols) <= 200 * 1024;
+  const bool fast0 = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
+                     ldx % 4 == 0 && fp8_gemv_smem_bytes(1, cols) <= 200 * 1024 &&
+                     x_group_off % 4 == 0;
+  const int nrows = row_end - row_start;
+  int tb = batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8;
+  while (tb > 1 && fp8_gemv_smem_bytes(tb, cols) > 200 * 1024) tb /= 2;
+  const int tiles = (batch + tb - 1) / tb;
+  int per = std::max(1, c->num_sms / tiles);
+  int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
+  if (x_group_rows > 0) {
+    // every CTA's rows must lie in one group: a box height dividing the group
+    // and the start row
+    while (box_rows > 1 && (x_group_rows % box_rows != 0 || row_start % box_rows != 0)) --box_rows;
+  }
+  const bool fast = fast0;
   if (fast) {
-    const int nrows = row_end - row_start;
-    int tb = batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8;
-    while (tb > 1 && fp8_gemv_smem_bytes(tb, cols) > 200 * 1024) tb /= 2;
-    const int tiles = (batch + tb - 1) / tb;
-    int per = std::max(1, c->num_sms / tiles);
-    int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
     a.box_rows = box_rows;
     auto key = std::make_tuple((const void*)weight, rows, cols, box_rows);
     auto it = c->fp8_maps.find(key);
@@ -528,10 +539,14 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
       }
       return WH_OK;
     }
-    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, false));
+    // one input: programmatic dependent launch, so that back-to-back GEMVs
+    // overlap one's weight stream with the previous one's tail
+    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, batch == 1 && c->pdl()));
     return WH_OK;
   }
   // generic path
+  if (act_quant_block > 0 && x_group_rows > 0)
+    return fail(WH_ERR_UNSUPPORTED, "grouped FP8 GEMV with act quant needs the fast path's shapes");
   if (act_quant_block > 0) {
     wh_status st = c->ensure_work(sizeof(float) * (size_t)batch * cols);
     if (st != WH_OK) return st;
@@ -597,6 +612,21 @@ wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, in
                       wh_stream_t stream) {
   return fp8_gemv_impl(c, weight, scale, rows, cols, scale_rows, scale_cols, row_start, row_end,
                        x, batch, ldx, y, ldy, act_quant_block, nullptr, stream);
+}
+
+wh_status wh_fp8_gemv_grouped(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows,
+                              int cols, int scale_rows, int scale_cols, int row_start,
+                              int row_end, const float* x, int batch, int ldx, int group_rows,
+                              long long group_offset, float* y, int ldy, int act_quant_block,
+                              wh_stream_t stream) {
+  if (group_rows < 1 || group_offset < 0 || rows % group_rows != 0)
+    return fail(WH_ERR_INVALID_SHAPE, "DeepSeek FP8 grouped rows");
+  // the reference quantises each group's input alone: blocks must not straddle groups
+  if (act_quant_block > 0 && (cols % act_quant_block != 0 || group_offset % act_quant_block != 0))
+    return fail(WH_ERR_INVALID_SHAPE, "act quant blocks straddle the groups' inputs");
+  return fp8_gemv_impl(c, weight, scale, rows, cols, scale_rows, scale_cols, row_start, row_end,
+                       x, batch, ldx, y, ldy, act_quant_block, nullptr, stream, group_rows,
+                       group_offset);
 }
 
 size_t wh_fp8_expert_scratch_len(size_t hidden, size_t intermediate) {
@@ -1688,6 +1718,8 @@ struct wh_ep_window {
   EpPeer* peers = nullptr;   // [world]
   float** yback_peers = nullptr;        // [world] peer d's result rows
   uint64_t** res_flag_peers = nullptr;  // [world] &peer d's res_flag[rank]
+  int32_t* pos = nullptr;    // [max_tokens * topk] result row of each route (wh_ep_moe_layer)
+  float* y_shared = nullptr; // [max_tokens][hidden] shared-expert output (wh_ep_moe_layer)
   CUtensorMap bup{}, bdown{};
   std::vector<void*> opened;
   uint64_t epoch = 0;
@@ -1764,7 +1796,9 @@ wh_status wh_ep_window_create(wh_ctx* c, const wh_moe_plan* p, int world, int ra
   const size_t sc_bytes =
       ep_scratch_layout(p, world, max_tokens, world * w->cap, nullptr).bytes;
   const size_t tab = align256(sc_bytes) + 2 * align256(sizeof(int) * nseg) + 256 +
-                     align256(sizeof(EpPeer) * world) + 2 * align256(sizeof(void*) * world);
+                     align256(sizeof(EpPeer) * world) + 2 * align256(sizeof(void*) * world) +
+                     align256(sizeof(int32_t) * (size_t)w->cap) +
+                     align256(sizeof(float) * (size_t)max_tokens * d.hidden);
   cudaError_t e = cudaMalloc(&w->base, w->bytes);
   if (e == cudaSuccess) e = cudaMemset(w->base, 0, w->bytes);
   if (e == cudaSuccess) e = cudaMalloc(&w->local, tab);
@@ -1790,6 +1824,10 @@ wh_status wh_ep_window_create(wh_ctx* c, const wh_moe_plan* p, int world, int ra
   w->yback_peers = reinterpret_cast<float**>(w->local + o);
   o += align256(sizeof(void*) * world);
   w->res_flag_peers = reinterpret_cast<uint64_t**>(w->local + o);
+  o += align256(sizeof(void*) * world);
+  w->pos = reinterpret_cast<int32_t*>(w->local + o);
+  o += align256(sizeof(int32_t) * (size_t)w->cap);
+  w->y_shared = reinterpret_cast<float*>(w->local + o);
   // B operand maps over the fixed sorted-row and h buffers
   const int rows = world * w->cap + max_tokens;
   if ((st = make_u8_map_strided(&w->bup, w->sc.sorted, rows, d.hidden, w->row_bytes, kGN)) !=
@@ -1988,6 +2026,17 @@ wh_status wh_ep_p2p_combine(wh_ctx* c, wh_ep_window* w, const int32_t* ids, cons
       c->status, stream));
   w->stage = 0;
   return WH_OK;
+}
+
+wh_status wh_ep_moe_layer(wh_ctx* c, wh_ep_window* w, const float* x, int tokens,
+                          const int32_t* ids, const float* weights, float* y,
+                          wh_stream_t stream) {
+  if (!c || !w) return fail(WH_ERR_INVALID_POINTER, "null ctx/window");
+  if (tokens > w->max_tokens) return fail(WH_ERR_INVALID_SHAPE, "tokens > the window's max_tokens");
+  wh_status st;
+  if ((st = wh_ep_p2p_dispatch(c, w, x, tokens, ids, w->pos, stream)) != WH_OK) return st;
+  if ((st = wh_ep_p2p_expert_ffn(c, w, x, tokens, w->y_shared, stream)) != WH_OK) return st;
+  return wh_ep_p2p_combine(c, w, ids, weights, w->pos, tokens, w->y_shared, y, stream);
 }
 
 }  // extern "C"

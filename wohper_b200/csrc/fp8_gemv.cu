@@ -30,6 +30,12 @@
 
 namespace wh {
 
+// The input of the rows from `row0` on (grouped mode: the group row0 lies in).
+__device__ __forceinline__ const float* fp8_x_rows(const Fp8GemvArgs& a, int row0) {
+  return a.x_group_rows ? a.x + (long long)(row0 / a.x_group_rows) * a.x_group_off : a.x;
+}
+
+
 __constant__ ActQuantTable c_aq;
 
 cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
@@ -146,7 +152,8 @@ __global__ void fp8_gemv_generic_kernel(Fp8GemvArgs a) {
     int r = a.row_start + int(i % (a.row_end - a.row_start));
     const uint8_t* w = a.weight + (long long)r * a.cols;
     const uint8_t* s = a.scale + (long long)(r / row_group) * a.scale_cols;
-    float acc = fp8_row_dot_exact(w, s, a.scale_cols, col_group, a.x + (long long)b * a.ldx);
+    float acc = fp8_row_dot_exact(w, s, a.scale_cols, col_group,
+                                  fp8_x_rows(a, r) + (long long)b * a.ldx);
     if (!isfinite(acc)) flag(a.status, WH_DEV_NONFINITE);
     const long long o = (long long)b * a.ldy + (r - a.row_start);
     a.y[o] = a.addend ? __fadd_rn(acc, a.addend[o]) : acc;
@@ -225,7 +232,8 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
   // x and the scale rows: every load in flight before the first store (one
   // memory latency instead of one per pass)
   for (int b = 0; b < tb; ++b) {
-    const float4* src = reinterpret_cast<const float4*>(a.x + (long long)(tile * TB + b) * a.ldx);
+    const float4* src =
+        reinterpret_cast<const float4*>(fp8_x_rows(a, row0) + (long long)(tile * TB + b) * a.ldx);
     float4* dst = reinterpret_cast<float4*>(xs + b * a.cols);
     const int n4 = a.cols / 4;
     for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * nthr) {
@@ -382,7 +390,8 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
 // so the chain runs under the weight stream; then the pairwise 8-lane sum.
 // Same arithmetic as fp8_gemv_tma_kernel.
 // ---------------------------------------------------------------------------
-constexpr int kRgConsumers = 16;  // phase-1 warps
+constexpr int kRgConsumers = 8;   // phase-1 warps
+constexpr int kRgRing = 12;       // weight stages in flight per CTA
 constexpr int kRgChain = 8;       // chain warps: 32 rows x 8 chains
 constexpr int kRgMaxGroups = 64;  // cols <= 8192
 constexpr int kRgThreads = 32 * (kRgConsumers + kRgChain + 1);
@@ -394,7 +403,7 @@ static int fp8_rg_stages(int cols) {
                    (long long)ngroups * 32 * 8 * 4 - (2 * kFp8MaxStages + kRgMaxGroups) * 8 -
                    (32LL * ngroups + 16);
   int ns = (int)std::max(0LL, room / kFp8StageBytes);
-  return std::min({ns, kFp8MaxStages, ngroups});
+  return std::min({ns, kRgRing, ngroups});
 }
 
 size_t fp8_gemv_rg_smem_bytes(int cols) {
@@ -423,6 +432,9 @@ __global__ void __launch_bounds__(kRgThreads)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int box_rows = a.box_rows;
   const int row0 = a.row_start + blockIdx.x * box_rows;
+  // the next kernel in the stream may start now: it streams its own weights
+  // while this one finishes (it waits for this grid before reading results)
+  pdl_launch_dependents();
 
   // one barrier per thread: a single thread initialising them one after the
   // other delays the first TMA issue by about a microsecond
@@ -487,6 +499,7 @@ __global__ void __launch_bounds__(kRgThreads)
     const float s2 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
     const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
     const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));
+    pdl_wait_prior();  // the addend may come from the previous kernel
     if (j == 0 && active && ok) {
       float tot = __fadd_rn(s8, 0.0f);
       if (!isfinite(tot)) {
@@ -504,7 +517,7 @@ __global__ void __launch_bounds__(kRgThreads)
   // x: when no act-quant block straddles a 128-column group, each warp stages
   // (and act-quantises) only the groups it computes, so phase 1 starts without
   // a CTA-wide barrier and the x loads overlap the weight stream
-  const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  const float4* x4 = reinterpret_cast<const float4*>(fp8_x_rows(a, row0));
   float4* xs4 = reinterpret_cast<float4*>(xs);
   const bool own_x = a.act_quant_block == 0 || 128 % a.act_quant_block == 0;
   if (own_x) {

@@ -148,6 +148,10 @@ struct Fp8GemvArgs {
   int box_rows;         // rows per CTA (fast path)
   uint32_t* status;
   const float* addend;  // nullable, laid out like y: y = gemv + addend (after the finite check)
+  // grouped input (the reference's grouped wo_a): row r reads x + (r / x_group_rows) *
+  // x_group_off (+ b * ldx); 0 = every row reads x
+  int x_group_rows;
+  long long x_group_off;
 };
 
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);

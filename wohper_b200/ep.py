@@ -195,14 +195,20 @@ class EpMoeLayer:
         return self.forward_p2p(x, ids, weights)
 
     def forward_p2p(self, x, ids, weights, marks=None):
-        """The peer-transport step; `marks(i)` (optional) is called before the
-        first call and after each of the three (event records for phase times)."""
+        """The peer-transport step: one wh_ep_moe_layer call, or, when
+        `marks(i)` is given, its three calls with marks(i) called before the
+        first and after each (event records for phase times)."""
         import torch
 
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
         L, s, h = lib(), _stream(None), self.ctx.handle
+        if marks is None:
+            y = torch.empty(T, self.hidden, dtype=torch.float32, device=self.device)
+            _check(L.wh_ep_moe_layer(h, self.window, _ptr(x), T, _ptr(ids), _ptr(weights),
+                                     _ptr(y), s))
+            return y
         pos = torch.empty(T * self.topk, dtype=torch.int32, device=self.device)
         ysh = torch.empty(T, self.hidden, dtype=torch.float32, device=self.device)
         y = torch.empty(T, self.hidden, dtype=torch.float32, device=self.device)
