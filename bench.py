@@ -714,6 +714,206 @@ def run_reference_config1(args):
 
 
 # ---------------------------------------------------------------------------
+# config 5: the full synthetic-weight DeepSeek-V4 decode step (43 layers)
+# ---------------------------------------------------------------------------
+V4_LAYERS = 43
+V4_VOCAB = 129280
+V4_POS = 4095
+V4_ATTN_BYTES = sum(r * c + (-(-r // 128)) * (-(-c // 128)) for r, c in
+                    ((1024, 4096), (32768, 1024), (512, 4096), (8192, 4096), (4096, 8192)))
+METRIC5 = "decode tokens/s (config 5: full synthetic 43-layer DeepSeek-V4 decode step)"
+
+
+def config5_dict(world: int, batch: int, layers: int) -> dict:
+    return {"workload": f"config 5: {layers} DeepSeek-V4-Flash-shape layers (mHC hc=4, MLA 64 "
+                        "heads x 512 with q/kv low-rank FP8 projections, 256 routed FP4 "
+                        "experts top-6 sqrt-softplus + shared), pooled head, bf16 lm_head "
+                        f"129280 x 4096 top-1; KV cache filled to {V4_POS + 1} positions "
+                        "(window 128 + compressed rows 512 / 32 by layer ratio)",
+            "layers": layers, "batch": batch, "token_pos": V4_POS, "experts": E, "topk": TOPK,
+            "hidden": HID, "inter": INTER,
+            "l2": "inputs larger than L2 (about 8.6 GB of weights read per step)",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+
+def run_config5(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    import wohper_b200 as W
+    from tests import helpers as H
+    from wohper_b200.v4model import V4Decoder
+
+    dev = torch.device("cuda", local)
+    ctx = W.Context(local)
+    B, NL = args.batch, args.layers
+    t0 = time.time()
+    layers, raws = [], []
+    for li in range(NL):
+        L, raw = H.v4_layer(W, ctx, li, E, seed=600 + li, max_tokens=B, router_mode=1,
+                            device=dev)
+        layers.append(L)
+        raws.append(raw)
+    g = torch.Generator(device=dev)
+    g.manual_seed(700 + rank)
+    kv = [[torch.randn(V4_POS + 1, 512, generator=g, device=dev) for _ in range(NL)]
+          for _ in range(B)]
+    comp = [[(torch.randn(n, 512, generator=g, device=dev) if n else None)
+             for n in (H.v4_compressed_count(li, V4_POS) for li in range(NL))] for _ in range(B)]
+    head = H.torch_hc_params(701, 4, HID, head=True, device=dev)
+    final_norm = H.torch_bf16_norm(702, HID, device=dev)
+    lm = (torch.randn(V4_VOCAB, HID, generator=g, device=dev) * 0.02).to(torch.bfloat16).view(
+        torch.int16)
+    build_s = time.time() - t0
+    dec = V4Decoder(ctx, layers, head, final_norm, lm, kv, comp, batch=B, top_k=1)
+    positions = [V4_POS] * B
+    n_tok = args.warmup + args.steps
+    xs = torch.randn(n_tok, B, 4 * HID, generator=g, device=dev)
+    x = torch.empty(B, 4 * HID, device=dev)
+    stream = torch.cuda.current_stream()
+    x.copy_(xs[0])
+    dec.step(x, positions)  # sizes the workspaces outside the capture
+    torch.cuda.synchronize()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            dec.step(x, positions)
+    stream.wait_stream(cap)
+    torch.cuda.synchronize()
+    for i in range(args.warmup):
+        x.copy_(xs[i])
+        graph.replay()
+    torch.cuda.synchronize()
+    ctx.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            x.copy_(xs[args.warmup + k])
+            ev[k][0].record(stream)
+            graph.replay()
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ctx.sync()
+    ms_step = all_max(world, sum(a.elapsed_time(b) for a, b in ev)) / args.steps
+    # graph output equals a direct step on the same input (bit for bit)
+    x.copy_(xs[0])
+    graph.replay()
+    tg = dec.tokens.clone()
+    xg = x.clone()
+    x.copy_(xs[0])
+    dec.step(x, positions)
+    torch.cuda.synchronize()
+    graph_ok = bool(torch.equal(tg, dec.tokens) and torch.equal(xg, x))
+    # ---- end to end: the residual stream from pinned host memory, the token ids back
+    xh = torch.randn(n_tok, B, 4 * HID, generator=torch.Generator().manual_seed(703)).pin_memory()
+    th = torch.empty(args.steps, B, dtype=torch.int32).pin_memory()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for k in range(args.steps):
+        x.copy_(xh[k], non_blocking=True)
+        graph.replay()
+        th[k].copy_(dec.tokens[:, 0], non_blocking=True)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = all_max(world, a0.elapsed_time(a1)) / args.steps
+    # ---- the two halves of a layer, timed alone over all layers (graphs) ----
+    def part_ms(fn):
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            fn()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gp, stream=cap):
+                fn()
+        torch.cuda.synchronize()
+        gp.replay()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(3):
+            gp.replay()
+        b1.record(stream)
+        torch.cuda.synchronize()
+        return b0.elapsed_time(b1) / 3
+
+    yb = torch.randn(B, HID, generator=g, device=dev)
+
+    def attn_only():
+        for li, L in enumerate(layers):
+            for b in range(B):
+                W.v4_attention(ctx, L.attn, V4_POS, yb[b], kv[b][li], dec.freqs[li],
+                               comp[b][li], dec.attn_scratch)
+
+    def moe_only():
+        for L in layers:
+            L.moe.forward(yb, dec.y2)
+
+    def mhc_only():
+        for L in layers:
+            W.hc_pre(ctx, *L.hc_attn, x, 4, HID, out=(dec.y, dec.post, dec.comb))
+            W.hc_post(ctx, dec.y, dec.resid, dec.post, dec.comb, 4, HID, out=dec.x2)
+            W.hc_pre(ctx, *L.hc_ffn, x, 4, HID, out=(dec.y, dec.post, dec.comb))
+            W.hc_post(ctx, dec.y, dec.resid, dec.post, dec.comb, 4, HID, out=dec.x2)
+
+    parts = {"attention_all_layers": round(part_ms(attn_only), 4),
+             "moe_all_layers": round(part_ms(moe_only), 4),
+             "mhc_all_layers": round(part_ms(mhc_only), 4)}
+    ctx.sync()
+    res = None
+    if rank == 0:
+        # HBM bytes one step reads: attention weights, the experts each token
+        # selects (a union at batch > 1: counted as min(batch * 6, 256) + shared),
+        # the router, the mHC parameters, the KV rows the attention reads, the lm_head
+        experts_read = min(B * TOPK, E) + 1
+        kv_rows = sum(min(V4_POS + 1, 128) + H.v4_compressed_count(li, V4_POS)
+                      for li in range(NL)) * B
+        step_bytes = (NL * (V4_ATTN_BYTES + experts_read * EXPERT_BYTES + ROUTER_BYTES
+                            + 2 * 24 * 4 * HID * 4)
+                      + kv_rows * 512 * 4 + V4_VOCAB * HID * 2)
+        peak, peak_kind = peaks()
+        gbs = step_bytes / (ms_step * 1e-3) / 1e9
+        res = {
+            "metric": METRIC5, "value": round(B * world / (ms_step * 1e-3), 3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp8/fp4 weights x act-quantised fp8 activations, f32 accumulate, "
+                     "bit-exact reference order",
+            "data": "synthetic (seeded random-init weights, N(0,1) KV cache and residual stream)",
+            "config": config5_dict(world, B, NL),
+            "hbm_bytes_per_step": int(step_bytes),
+            "roofline": {"kernel": "the whole decode step", "bound": "hbm",
+                         "achieved": round(gbs, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(gbs / peak, 4),
+                         "algorithmic_bytes": int(step_bytes), "traffic": None},
+            "parts_ms": parts,
+            "e2e": {"value": round(B * world / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": B * 4 * HID * 4,
+                    "d2h_bytes_per_step": B * 4,
+                    "path": "pinned host residual stream -> the captured step (C ABI kernels) "
+                            "-> top-1 token ids to pinned host"},
+            "graph_output_matches_direct_step": graph_ok,
+            "build_s": round(build_s, 1),
+            "gpu_launches": None, "timing": "cuda graph of one step, replayed",
+            "clocks": clk.summary(),
+        }
+    del graph
+    for L in layers:
+        L.moe.close()
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # config 3: batched (prefill) MoE FFN on the tensor cores
 # ---------------------------------------------------------------------------
 T3 = 2048
@@ -1939,7 +2139,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true",
                     help="config 2: skip the nested config-4 expert-parallel measurement")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+    ap.add_argument("--batch", type=int, default=1, help="config 5: sequences per step")
+    ap.add_argument("--layers", type=int, default=V4_LAYERS, help="config 5: layers")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="1: one FP8 GEMV 4096x4096; 2: one-token decode FFN (default); "
                          "3: 2048-token batched FFN; 4: expert-parallel layer over the ranks")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
@@ -1974,6 +2176,8 @@ def main():
         res = run_mla(args)
     elif args.workload == "mhc":
         res = run_mhc(args)
+    elif args.config == 5 and args.impl == "ours":
+        res = run_config5(args)
     elif args.config == 1:
         res = run_config1(args) if args.impl == "ours" else run_reference_config1(args)
     elif args.config == 3 and args.impl == "ours":

@@ -103,3 +103,110 @@ def zipf_routing(seed: int, gate_bits: np.ndarray, x: np.ndarray, s: float = 1.1
     g[:, 0] = bf16_bits(prior)
     x[:, 0] = 1.0
     return g, x
+
+
+# ---------------------------------------------------------------------------
+# DeepSeek-V4 decode layers with seeded synthetic weights, generated on the
+# device (the attention projections as E4M3 of N(0, 0.05) with UE8M0 scales
+# 2^[-8,-2], norms 1 + N(0, 0.1) in bf16, mHC parameters N(0, 0.02) / fixed
+# scales, the MoE as torch_fp4_experts + an N(0, 0.02) bf16 router)
+# ---------------------------------------------------------------------------
+V4_SHAPES = {"wq_a": (1024, 4096), "wq_b": (32768, 1024), "wkv": (512, 4096),
+             "wo_a": (8192, 4096), "wo_b": (4096, 8192)}
+
+
+def _torch_gen(seed: int, device):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def torch_fp8_matrix(seed: int, rows: int, cols: int, device="cuda"):
+    import torch
+
+    g = _torch_gen(seed, device)
+    w = (torch.randn(rows, cols, generator=g, device=device) * 0.05).to(torch.float8_e4m3fn)
+    s = torch.randint(119, 126, (-(-rows // 128), -(-cols // 128)), dtype=torch.uint8,
+                      generator=g, device=device)
+    return w.view(torch.uint8), s
+
+
+def torch_bf16_norm(seed: int, n: int, device="cuda"):
+    import torch
+
+    g = _torch_gen(seed, device)
+    return (1.0 + 0.1 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16).view(
+        torch.int16)
+
+
+def torch_hc_params(seed: int, hc: int, hidden: int, head: bool = False, device="cuda"):
+    """(fn, scale, base): hc_pre's [(2+hc)*hc, hc*hidden] / [3] / [(2+hc)*hc], or
+    with head=True hc_head's [hc, hc*hidden] / float / [hc]."""
+    import torch
+
+    g = _torch_gen(seed, device)
+    mix = hc if head else (2 + hc) * hc
+    fn = torch.randn(mix, hc * hidden, generator=g, device=device) * 0.02
+    base = torch.randn(mix, generator=g, device=device) * 0.1
+    if head:
+        return fn, 0.5, base
+    return fn, torch.tensor([0.5, 0.5, 0.5], device=device), base
+
+
+def v4_layer(W, ctx, index: int, experts: int, seed: int, max_tokens: int = 1,
+             router_mode: int = 0, device="cuda"):
+    """One DeepSeek-V4-Flash-shape decode layer (hidden 4096, 64 heads of 512,
+    q_lora 1024, 8 output groups, `experts` FP4 experts 4096 -> 2048 + shared,
+    top-6).  Returns (V4LayerWeights, raw) with raw the device tensors."""
+    import torch
+
+    from wohper_b200.v4model import V4LayerWeights
+
+    raw = {}
+    mats = {}
+    for i, (name, (r, c)) in enumerate(V4_SHAPES.items()):
+        w, s = torch_fp8_matrix(seed * 100 + i, r, c, device)
+        raw[name] = (w, s)
+        mats[name] = W.Fp8Matrix(w, s)
+    raw["q_norm"] = torch_bf16_norm(seed * 100 + 10, 1024, device)
+    raw["kv_norm"] = torch_bf16_norm(seed * 100 + 11, 512, device)
+    raw["sink"] = torch.randn(64, generator=_torch_gen(seed * 100 + 12, device), device=device)
+    attn = W.V4Attention(**mats, q_norm=raw["q_norm"], kv_norm=raw["kv_norm"], sink=raw["sink"])
+    raw["attn_norm"] = torch_bf16_norm(seed * 100 + 13, 4096, device)
+    raw["ffn_norm"] = torch_bf16_norm(seed * 100 + 14, 4096, device)
+    raw["hc_attn"] = torch_hc_params(seed * 100 + 15, 4, 4096, device=device)
+    raw["hc_ffn"] = torch_hc_params(seed * 100 + 16, 4, 4096, device=device)
+    stack = torch_fp4_experts(seed * 100 + 17, experts + 1, 4096, 2048, device=device)
+    raw["stack"] = stack
+    gate = torch.from_numpy(router_gate(seed * 100 + 18, experts, 4096).view(np.int16)).to(device)
+    raw["gate"] = gate
+    bias = None
+    if router_mode == 1:
+        bias = torch.randn(experts, generator=_torch_gen(seed * 100 + 19, device),
+                           device=device) * 0.01
+    raw["gate_bias"] = bias
+
+    def wexp(e):
+        w1, s1, w3, s3, w2, s2 = expert_views(stack, e)
+        return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, 2048, 4096, 128),
+                                     W.Fp4Matvec(w3, s3, 2048, 4096, 128),
+                                     W.Fp4Matvec(w2, s2, 4096, 2048, 64))
+
+    moe = W.MoeLayer(ctx, [wexp(e) for e in range(experts)], wexp(experts), gate, topk=6,
+                     router_mode=router_mode, route_scale=1.5 if router_mode == 1 else 1.0,
+                     gate_bias=bias, max_tokens=max_tokens)
+    layer = V4LayerWeights(index, attn, raw["attn_norm"], raw["ffn_norm"], raw["hc_attn"],
+                           raw["hc_ffn"], moe)
+    return layer, raw
+
+
+def v4_compressed_count(layer_index: int, token_pos: int) -> int:
+    """Compressed rows visible at token_pos (src/compute.rs:3716-3719: at most
+    (pos + 1) / ratio, capped at 512)."""
+    from wohper_b200 import DEEPSEEK_V4_COMPRESS_RATIOS
+
+    ratio = DEEPSEEK_V4_COMPRESS_RATIOS[layer_index] if layer_index < len(
+        DEEPSEEK_V4_COMPRESS_RATIOS) else 0
+    return 0 if ratio == 0 else min((token_pos + 1) // ratio, 512)
