@@ -845,9 +845,8 @@ def run_config5(args):
 
     def attn_only():
         for li, L in enumerate(layers):
-            for b in range(B):
-                W.v4_attention(ctx, L.attn, V4_POS, yb[b], kv[b][li], dec.freqs[li],
-                               comp[b][li], dec.attn_scratch)
+            W.v4_attention(ctx, L.attn, positions, yb, [kv[b][li] for b in range(B)],
+                           dec.freqs[li], [comp[b][li] for b in range(B)], dec.attn_scratch)
 
     def moe_only():
         for L in layers:

@@ -460,22 +460,29 @@ typedef struct wh_v4_attn {
   const uint16_t* kv_norm; /* bf16 [head_dim] (kv_a_layernorm), NULL: unweighted */
   const float* sink;       /* [heads] attention sink, nullable */
 } wh_v4_attn;
-/* Floats of scratch wh_v4_attention needs. */
-size_t wh_v4_attention_scratch_len(const wh_v4_attn* layer);
+/* Floats of scratch wh_v4_attention needs for `tokens` tokens. */
+size_t wh_v4_attention_scratch_len(const wh_v4_attn* layer, int tokens);
 /* Replaces compute_deepseek_v4_mla_attention (src/compute.rs:3924-4293) for
- * one token, bit-exact: hidden [hidden] holds the normed attention input on
- * entry and the attention output on return.  q path wq_a -> q_norm -> act
- * quant -> wq_b -> per-head RMS -> RoPE; kv path wkv -> kv_norm -> RoPE of
- * the rope dims -> act quant of the nope dims, stored into kv_cache row
- * token_pos (row stride kv_stride); the attention core of wh_mla_attention
- * over the window and the compressed rows (produced by the caller's
- * compressor); act quant -> grouped wo_a -> act quant -> wo_b.  inv_freqs:
- * HOST array, the layer's rope_inv_freqs.  The MLA workspace is context-owned:
- * calls on one context are serialised by the caller. */
-wh_status wh_v4_attention(wh_ctx* ctx, const wh_v4_attn* layer, int token_pos, float* hidden,
-                          float* kv_cache, int kv_stride, const float* compressed,
-                          int compressed_count, const float* inv_freqs, float* scratch,
-                          size_t scratch_len, wh_stream_t stream);
+ * `tokens` decode tokens (1..32, each of its own sequence), bit-exact per
+ * token: hidden [tokens][hidden] holds the normed attention inputs on entry
+ * and the attention outputs on return.  q path wq_a -> q_norm -> act quant ->
+ * wq_b -> per-head RMS -> RoPE; kv path wkv -> kv_norm -> RoPE of the rope
+ * dims -> act quant of the nope dims, stored into row token_pos[t] of token
+ * t's KV cache kv_caches[t] (row stride kv_stride); the attention core of
+ * wh_mla_attention over the window and the compressed rows compressed[t]
+ * [compressed_count[t]][head_dim] (produced by the caller's compressor; both
+ * arrays nullable when there are none); act quant -> grouped wo_a -> act
+ * quant -> wo_b.  The projections run once over all tokens (their weights
+ * are read once, as in the reference's batched pass, src/compute.rs:4307).
+ * token_pos, kv_caches, compressed, compressed_count and inv_freqs (the
+ * layer's rope_inv_freqs) are HOST arrays; the pointers in them are device
+ * pointers.  The MLA workspace is context-owned: calls on one context are
+ * serialised by the caller. */
+wh_status wh_v4_attention(wh_ctx* ctx, const wh_v4_attn* layer, int tokens, const int* token_pos,
+                          float* hidden, float* const* kv_caches, int kv_stride,
+                          const float* const* compressed, const int* compressed_count,
+                          const float* inv_freqs, float* scratch, size_t scratch_len,
+                          wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* mHC hyper-connections (DeepSeek-V4)                                         */

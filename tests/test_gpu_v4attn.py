@@ -112,3 +112,25 @@ def test_v4_attention_projection_path_bit_exact(ctx, W, layer_index, token_pos, 
     got = hid.cpu().numpy()
     assert np.all(np.isfinite(got))
     assert np.array_equal(bits(got), bits(want))
+
+
+def test_v4_attention_batch_of_tokens_bit_exact(ctx, W):
+    # three sequences, two at the same position (one norm launch covers both)
+    layer, spec, keep = _v4_layer(W, 340)
+    theta, yarn = W.deepseek_rope_for_layer(2)
+    fr = W.rope_inv_freqs(64, theta, yarn)
+    pos = [500, 500, 260]
+    kvs = [H.activations(341 + t, p + 4, 512) for t, p in enumerate(pos)]
+    comps = [H.activations(345 + t, H.v4_compressed_count(2, p), 512) for t, p in enumerate(pos)]
+    x = O.rms_norm(H.activations(349, 3, 4096), norm_weight(350, 4096))
+    kv_d = [torch.from_numpy(k).cuda() for k in kvs]
+    hid = torch.from_numpy(x).cuda()
+    W.v4_attention(ctx, layer, pos, hid, kv_d, fr, [torch.from_numpy(c).cuda() for c in comps])
+    ctx.sync()
+    got = hid.cpu().numpy()
+    for t, p in enumerate(pos):
+        kv_h = kvs[t].copy()
+        st, want = O.v4_attention(spec, p, x[t], kv_h, comps[t], fr)
+        assert st == O.OK
+        assert np.array_equal(bits(kv_d[t].cpu().numpy()[p]), bits(kv_h[p])), t
+        assert np.array_equal(bits(got[t]), bits(want)), t

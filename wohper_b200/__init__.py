@@ -175,8 +175,8 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_rms_norm": (st, [vp, vp, vp, i, i, vp, vp]),
         "wh_fp8_gemv_grouped": (st, [vp, vp, vp, i, i, i, i, i, i, vp, i, i, i, C.c_longlong, vp,
                                      i, i, vp]),
-        "wh_v4_attention_scratch_len": (sz, [vp]),
-        "wh_v4_attention": (st, [vp, vp, i, vp, vp, i, vp, i, vp, vp, sz, vp]),
+        "wh_v4_attention_scratch_len": (sz, [vp, i]),
+        "wh_v4_attention": (st, [vp, vp, i, vp, vp, vp, i, vp, vp, vp, vp, sz, vp]),
         "wh_moe_scratch_field": (st, [vp, i, i, C.POINTER(sz), C.POINTER(sz)]),
         "wh_moe_ffn": (st, [vp, vp, vp, i, vp, vp, vp, vp, vp, sz, vp]),
         "wh_debug_act_quant_table": (None, [vp]),
@@ -641,27 +641,38 @@ class V4Attention:
                           _ptr(self.sink))
 
 
-def v4_attention_scratch_len(layer: V4Attention) -> int:
+def v4_attention_scratch_len(layer: V4Attention, tokens: int = 1) -> int:
     s = layer.spec()
-    return int(lib().wh_v4_attention_scratch_len(C.byref(s)))
+    return int(lib().wh_v4_attention_scratch_len(C.byref(s), tokens))
 
 
-def v4_attention(ctx: Context, layer: V4Attention, token_pos: int, hidden, kv_cache, inv_freqs,
+def v4_attention(ctx: Context, layer: V4Attention, token_pos, hidden, kv_caches, inv_freqs,
                  compressed=None, scratch=None, stream=None):
-    """compute_deepseek_v4_mla_attention for one token on the device, bit-exact:
-    hidden [hidden] f32 (normed input) is overwritten by the attention output;
-    kv_cache [positions, stride] f32 gets row token_pos."""
+    """compute_deepseek_v4_mla_attention on the device, bit-exact, for one
+    token (token_pos an int, hidden [hidden], kv_caches one [positions, stride]
+    tensor, compressed one tensor or None) or for a batch (token_pos a list,
+    hidden [tokens, hidden], kv_caches / compressed lists, one per token).
+    hidden is overwritten by the attention outputs; each token's KV cache gets
+    its row token_pos."""
     import numpy as np
     import torch
 
+    single = isinstance(token_pos, int)
+    pos = [token_pos] if single else list(token_pos)
+    kvs = [kv_caches] if single else list(kv_caches)
+    comps = [compressed] if single else list(compressed or [None] * len(pos))
+    T = len(pos)
     s = layer.spec()
-    n = int(lib().wh_v4_attention_scratch_len(C.byref(s)))
-    if scratch is None:
+    n = int(lib().wh_v4_attention_scratch_len(C.byref(s), T))
+    if scratch is None or scratch.numel() < n:
         scratch = torch.empty(n, dtype=torch.float32, device=hidden.device)
     fr = np.ascontiguousarray(inv_freqs, dtype=np.float32)
-    cc = 0 if compressed is None else compressed.shape[0]
-    _check(lib().wh_v4_attention(ctx.handle, C.byref(s), token_pos, _ptr(hidden), _ptr(kv_cache),
-                                 kv_cache.stride(0), _ptr(compressed), cc,
+    pos_a = (C.c_int * T)(*pos)
+    kv_a = (C.c_void_p * T)(*[_ptr(k) for k in kvs])
+    cp_a = (C.c_void_p * T)(*[_ptr(c) for c in comps])
+    cc_a = (C.c_int * T)(*[0 if c is None else c.shape[0] for c in comps])
+    _check(lib().wh_v4_attention(ctx.handle, C.byref(s), T, pos_a, _ptr(hidden), kv_a,
+                                 kvs[0].stride(0), cp_a, cc_a,
                                  fr.ctypes.data if fr.size else None, _ptr(scratch),
                                  scratch.numel(), _stream(stream)))
     return hidden

@@ -83,7 +83,7 @@ class V4Decoder:
         self.post = torch.empty(B, hc, device=dev)
         self.comb = torch.empty(B, hc, hc, device=dev)
         self.pooled = torch.empty(B, hidden, device=dev)
-        n = max(v4_attention_scratch_len(L.attn) for L in self.layers)
+        n = max(v4_attention_scratch_len(L.attn, B) for L in self.layers)
         self.attn_scratch = torch.empty(n, device=dev)
         self.freqs = [rope_inv_freqs(L.attn.head_dim - L.attn.nope_dim,
                                      *deepseek_rope_for_layer(L.index)) for L in self.layers]
@@ -108,10 +108,9 @@ class V4Decoder:
             hc_pre(c, fn, scale, base, x, hc, H, DEEPSEEK_V4_HC_SINKHORN_ITERS,
                    DEEPSEEK_V4_HC_EPS, out=(self.y, self.post, self.comb))
             rms_norm(c, self.y, L.attn_norm, out=self.y)
-            for b in range(self.batch):
-                comp = self.comp[b][li]
-                v4_attention(c, L.attn, positions[b], self.y[b], self.kv[b][li], self.freqs[li],
-                             comp, self.attn_scratch)
+            v4_attention(c, L.attn, list(positions), self.y,
+                         [self.kv[b][li] for b in range(self.batch)], self.freqs[li],
+                         [self.comp[b][li] for b in range(self.batch)], self.attn_scratch)
             hc_post(c, self.y, self.resid, self.post, self.comb, hc, H, out=x)
             # --- ffn hc_pre + norm (phase 1), MoE + hc_post (phase 2) ---
             self.resid.copy_(x)
