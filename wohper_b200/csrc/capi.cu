@@ -8,6 +8,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <memory>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -604,6 +605,100 @@ wh_status fp8_expert_check(const wh_fp8_expert& e, size_t hidden) {
 }
 }  // namespace
 
+// The MLA attention core for `ntok` tokens in one set of launches (grid z =
+// token): each token's own q, cache rows, position, compressed rows and out.
+struct MlaToken {
+  const float* q;
+  const float* keys;
+  int token_pos;
+  const float* compressed;
+  int compressed_count;
+  float* out;
+};
+
+wh_status mla_attention_tokens(wh_ctx* c, int heads, int head_dim, int nope_dim, int key_stride,
+                               int window, const float* sink, const float* inv_freqs,
+                               const MlaToken* toks, int ntok, wh_stream_t stream) {
+  if (heads < 1 || head_dim < 1 || nope_dim < 0 || nope_dim > head_dim ||
+      (head_dim - nope_dim) % 2 != 0 || key_stride < head_dim || window < 1 || ntok < 1)
+    return fail(WH_ERR_INVALID_SHAPE, "MLA attention shape");
+  if (ntok > kMlaMaxTok) return fail(WH_ERR_UNSUPPORTED, "more than 32 tokens per call");
+  const int pairs = (head_dim - nope_dim) / 2;
+  if (pairs > 64 || (ntok > 1 && pairs > 64)) return fail(WH_ERR_UNSUPPORTED, "rope dim > 128");
+  if (pairs > 0 && nope_dim % 2 != 0) return fail(WH_ERR_UNSUPPORTED, "odd nope_dim");
+  if (pairs > 0 && !inv_freqs) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  for (int t = 0; t < ntok; ++t) {
+    const MlaToken& k = toks[t];
+    if (k.token_pos < 0 || k.compressed_count < 0)
+      return fail(WH_ERR_INVALID_SHAPE, "MLA attention shape");
+    if (!k.q || !k.keys || !k.out || (k.compressed_count > 0 && !k.compressed))
+      return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  }
+  auto batch = std::make_unique<MlaBatch<kMlaMaxTok>>();
+  auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  int widest = 0, pmax = -1;
+  size_t work = 0;
+  std::vector<size_t> woff(ntok);
+  for (int t = 0; t < ntok; ++t) {
+    const MlaToken& k = toks[t];
+    MlaArgs& a = batch->t[t];
+    a.q = k.q;
+    a.keys = k.keys;
+    a.compressed = k.compressed;
+    a.sink = sink;
+    a.out = k.out;
+    a.heads = heads;
+    a.head_dim = head_dim;
+    a.nope_dim = nope_dim;
+    a.key_stride = key_stride;
+    const int context = k.token_pos + 1;
+    a.window_start = context > window ? context - window : 0;  // saturating_sub
+    a.window_len = context - a.window_start;
+    a.compressed_count = k.compressed_count;
+    a.vec4 = head_dim % 4 == 0 && key_stride % 4 == 0 && al16(k.q) && al16(k.keys) &&
+             (k.compressed_count == 0 || al16(k.compressed));
+    a.scale = powf((float)head_dim, -0.5f);  // (head_dim as f32).powf(-0.5)
+    const float pos = (float)k.token_pos;
+    for (int i = 0; i < pairs; ++i) {
+      const float angle = pos * inv_freqs[i];
+      a.rope_sin[i] = sinf(angle);
+      a.rope_cos[i] = cosf(angle);
+    }
+    const int P = a.window_len + a.compressed_count;
+    if (P > pmax) {
+      pmax = P;
+      widest = t;
+    }
+    woff[t] = work;
+    work += align256(mla_scratch_bytes(heads, P));
+  }
+  size_t smem_scores = 0, smem_output = 0;
+  if (!mla_plan(batch->t[widest], &smem_scores, &smem_output))
+    return fail(WH_ERR_UNSUPPORTED, "heads, head_dim or visible rows do not fit shared memory");
+  cudaSetDevice(c->device);
+  if (wh_status st = c->ensure_mla_work(work)) return st;
+  for (int t = 0; t < ntok; ++t) {
+    MlaArgs& a = batch->t[t];
+    a.smem_ld = batch->t[widest].smem_ld;
+    a.head_group = batch->t[widest].head_group;
+    a.stages = batch->t[widest].stages;
+    const int P = a.window_len + a.compressed_count;
+    a.scores = reinterpret_cast<float*>(static_cast<uint8_t*>(c->mla_work) + woff[t]);
+    a.weights = a.scores + (size_t)P * heads;
+    a.tile_max = a.weights + (size_t)P * heads;
+    a.head_max = a.tile_max + mla_tile_count(P) * heads;
+  }
+  if (ntok == 1) {
+    MlaBatch<1> one;
+    one.t[0] = batch->t[0];
+    WH_CUDA(launch_mla_attention<1>(one, 1, smem_scores, smem_output, (cudaStream_t)stream));
+  } else {
+    WH_CUDA(launch_mla_attention<kMlaMaxTok>(*batch, ntok, smem_scores, smem_output,
+                                             (cudaStream_t)stream));
+  }
+  return WH_OK;
+}
+
 extern "C" {
 
 wh_status wh_fp8_gemv(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, int rows, int cols,
@@ -833,51 +928,9 @@ wh_status wh_mla_attention(wh_ctx* c, const float* q, int heads, int head_dim, i
                            const float* compressed, int compressed_count, const float* sink,
                            const float* inv_freqs, float* out, wh_stream_t stream) {
   if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
-  if (heads < 1 || head_dim < 1 || nope_dim < 0 || nope_dim > head_dim ||
-      (head_dim - nope_dim) % 2 != 0 || key_stride < head_dim || token_pos < 0 || window < 1 ||
-      compressed_count < 0)
-    return fail(WH_ERR_INVALID_SHAPE, "MLA attention shape");
-  const int pairs = (head_dim - nope_dim) / 2;
-  if (pairs > 64) return fail(WH_ERR_UNSUPPORTED, "rope dim > 128");
-  if (pairs > 0 && nope_dim % 2 != 0) return fail(WH_ERR_UNSUPPORTED, "odd nope_dim");
-  if (!q || !keys || !out || (compressed_count > 0 && !compressed) || (pairs > 0 && !inv_freqs))
-    return fail(WH_ERR_INVALID_POINTER, "null pointer");
-  MlaArgs a{};
-  a.q = q;
-  a.keys = keys;
-  a.compressed = compressed;
-  a.sink = sink;
-  a.out = out;
-  a.heads = heads;
-  a.head_dim = head_dim;
-  a.nope_dim = nope_dim;
-  a.key_stride = key_stride;
-  const int context = token_pos + 1;
-  a.window_start = context > window ? context - window : 0;  // saturating_sub
-  a.window_len = context - a.window_start;
-  a.compressed_count = compressed_count;
-  size_t smem_scores = 0, smem_output = 0;
-  if (!mla_plan(a, &smem_scores, &smem_output))
-    return fail(WH_ERR_UNSUPPORTED, "heads, head_dim or visible rows do not fit shared memory");
-  auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  a.vec4 = head_dim % 4 == 0 && key_stride % 4 == 0 && al16(q) && al16(keys) &&
-           (compressed_count == 0 || al16(compressed));
-  a.scale = powf((float)head_dim, -0.5f);  // (head_dim as f32).powf(-0.5)
-  cudaSetDevice(c->device);
-  const int positions = a.window_len + compressed_count;
-  if (wh_status st = c->ensure_mla_work(mla_scratch_bytes(heads, positions))) return st;
-  a.scores = (float*)c->mla_work;
-  a.weights = a.scores + (size_t)positions * heads;
-  a.tile_max = a.weights + (size_t)positions * heads;
-  a.head_max = a.tile_max + mla_tile_count(positions) * heads;
-  const float pos = (float)token_pos;
-  for (int i = 0; i < pairs; ++i) {
-    const float angle = pos * inv_freqs[i];
-    a.rope_sin[i] = sinf(angle);
-    a.rope_cos[i] = cosf(angle);
-  }
-  WH_CUDA(launch_mla_attention(a, smem_scores, smem_output, (cudaStream_t)stream));
-  return WH_OK;
+  MlaToken t{q, keys, token_pos, compressed, compressed_count, out};
+  return mla_attention_tokens(c, heads, head_dim, nope_dim, key_stride, window, sink, inv_freqs,
+                              &t, 1, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -106,11 +106,21 @@ struct MlaArgs {
   float scale;
   float rope_cos[64], rope_sin[64];  // per rope pair at the token's position
 };
+// The launches take the arguments of up to N tokens; token z of the grid's z
+// dimension reads t[z] (its own q, cache, compressed rows, window and rope).
+constexpr int kMlaMaxTok = 32;
+template <int N>
+struct MlaBatch {
+  MlaArgs t[N];
+};
 bool mla_plan(MlaArgs& a, size_t* smem_scores, size_t* smem_output);
 size_t mla_scratch_bytes(int heads, int positions);
 size_t mla_tile_count(int positions);
-cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t smem_output,
-                                 cudaStream_t s);
+// every token's plan fields (smem_ld, head_group, stages) must be equal;
+// smem sizes and grids are those of the token with the most positions
+template <int N>
+cudaError_t launch_mla_attention(const MlaBatch<N>& b, int tokens, size_t smem_scores,
+                                 size_t smem_output, cudaStream_t s);
 
 // ---------------- BF16 lm_head top-k ----------------
 struct LmHeadArgs {

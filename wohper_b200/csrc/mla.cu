@@ -42,6 +42,7 @@
 // staging copies are cp.async, so all of a CTA's loads are in flight at once.
 #include "common.cuh"
 #include "kernels.cuh"
+#include <algorithm>
 
 namespace wh {
 
@@ -75,11 +76,15 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a) {
+template <int N>
+__global__ void __launch_bounds__(kMlaScoreThreads)
+    mla_scores_kernel(const __grid_constant__ MlaBatch<N> b) {
+  const MlaArgs& a = b.t[blockIdx.z];
   extern __shared__ __align__(16) float mla_s[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = a.heads, D = a.head_dim, ld = a.smem_ld;
   const int P = a.window_len + a.compressed_count;
+  if ((int)blockIdx.x * kMlaScoreTile >= P) return;  // beyond this token's positions
   const int p0 = blockIdx.x * kMlaScoreTile, np = min(kMlaScoreTile, P - p0);
   const int hb = blockIdx.y * kMlaScoreHeads, nh = min(kMlaScoreHeads, H - hb);
   float* q_s = mla_s;                              // [kMlaScoreHeads][ld]
@@ -156,11 +161,15 @@ __global__ void __launch_bounds__(kMlaScoreThreads) mla_scores_kernel(MlaArgs a)
 
 // w[h][p] = exp(s_p - max_h) for a chunk of positions of one head; the head's
 // max over the tile maxima.
-__global__ void __launch_bounds__(kMlaWeightThreads) mla_weights_kernel(MlaArgs a) {
+template <int N>
+__global__ void __launch_bounds__(kMlaWeightThreads)
+    mla_weights_kernel(const __grid_constant__ MlaBatch<N> b) {
+  const MlaArgs& a = b.t[blockIdx.z];
   __shared__ float s_red[kMlaWeightThreads / 32];
   const int tid = threadIdx.x, h = blockIdx.y;
   const int H = a.heads;
   const int P = a.window_len + a.compressed_count;
+  if ((int)blockIdx.x * kMlaWeightThreads >= P) return;  // beyond this token's positions
   const int ntiles = (P + kMlaScoreTile - 1) / kMlaScoreTile;
   pdl_wait_prior();
   float m = -INFINITY;
@@ -204,8 +213,10 @@ __device__ __forceinline__ void mla_issue_rows(const MlaArgs& a, float* slot, in
   }
 }
 
-template <int kStages>
-__global__ void __launch_bounds__(kMlaMaxGroup * kMlaSlice + 32) mla_output_kernel(MlaArgs a) {
+template <int kStages, int N>
+__global__ void __launch_bounds__(kMlaMaxGroup * kMlaSlice + 32)
+    mla_output_kernel(const __grid_constant__ MlaBatch<N> b) {
+  const MlaArgs& a = b.t[blockIdx.z];
   extern __shared__ __align__(16) float mla_w[];  // [group][P] weights | key ring
   __shared__ float s_den[kMlaMaxGroup];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -360,17 +371,20 @@ size_t mla_tile_count(int positions) {
   return (size_t)(positions + kMlaScoreTile - 1) / kMlaScoreTile;
 }
 
-template <int S>
-static cudaError_t launch_mla_output(const cudaLaunchConfig_t& cfg, const MlaArgs& a) {
-  cudaError_t e = ensure_smem(mla_output_kernel<S>, cfg.dynamicSmemBytes);
+template <int S, int N>
+static cudaError_t launch_mla_output(const cudaLaunchConfig_t& cfg, const MlaBatch<N>& b) {
+  cudaError_t e = ensure_smem(mla_output_kernel<S, N>, cfg.dynamicSmemBytes);
   if (e != cudaSuccess) return e;
-  return cudaLaunchKernelEx(&cfg, mla_output_kernel<S>, a);
+  return cudaLaunchKernelEx(&cfg, mla_output_kernel<S, N>, b);
 }
 
-cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t smem_output,
-                                 cudaStream_t s) {
-  const int P = a.window_len + a.compressed_count;
-  cudaError_t e = ensure_smem(mla_scores_kernel, smem_scores);
+template <int N>
+cudaError_t launch_mla_attention(const MlaBatch<N>& b, int tokens, size_t smem_scores,
+                                 size_t smem_output, cudaStream_t s) {
+  int P = 0;
+  for (int t = 0; t < tokens; ++t) P = std::max(P, b.t[t].window_len + b.t[t].compressed_count);
+  const MlaArgs& a = b.t[0];
+  cudaError_t e = ensure_smem(mla_scores_kernel<N>, smem_scores);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -380,24 +394,28 @@ cudaError_t launch_mla_attention(const MlaArgs& a, size_t smem_scores, size_t sm
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3((P + kMlaScoreTile - 1) / kMlaScoreTile,
-                     (a.heads + kMlaScoreHeads - 1) / kMlaScoreHeads);
+                     (a.heads + kMlaScoreHeads - 1) / kMlaScoreHeads, tokens);
   cfg.blockDim = dim3(kMlaScoreThreads);
   cfg.dynamicSmemBytes = smem_scores;
-  e = cudaLaunchKernelEx(&cfg, mla_scores_kernel, a);
+  e = cudaLaunchKernelEx(&cfg, mla_scores_kernel<N>, b);
   if (e != cudaSuccess) return e;
-  cfg.gridDim = dim3((P + kMlaWeightThreads - 1) / kMlaWeightThreads, a.heads);
+  cfg.gridDim = dim3((P + kMlaWeightThreads - 1) / kMlaWeightThreads, a.heads, tokens);
   cfg.blockDim = dim3(kMlaWeightThreads);
   cfg.dynamicSmemBytes = 0;
-  e = cudaLaunchKernelEx(&cfg, mla_weights_kernel, a);
+  e = cudaLaunchKernelEx(&cfg, mla_weights_kernel<N>, b);
   if (e != cudaSuccess) return e;
-  cfg.gridDim = dim3((a.head_dim + kMlaSlice - 1) / kMlaSlice, a.heads / a.head_group);
+  cfg.gridDim = dim3((a.head_dim + kMlaSlice - 1) / kMlaSlice, a.heads / a.head_group, tokens);
   cfg.blockDim = dim3(32 * ((a.head_group + 1) / 2) + 32);
   cfg.dynamicSmemBytes = smem_output;
   switch (a.stages) {
-    case 12: return launch_mla_output<12>(cfg, a);
-    case 8: return launch_mla_output<8>(cfg, a);
-    default: return launch_mla_output<4>(cfg, a);
+    case 12: return launch_mla_output<12, N>(cfg, b);
+    case 8: return launch_mla_output<8, N>(cfg, b);
+    default: return launch_mla_output<4, N>(cfg, b);
   }
 }
+template cudaError_t launch_mla_attention<1>(const MlaBatch<1>&, int, size_t, size_t,
+                                             cudaStream_t);
+template cudaError_t launch_mla_attention<kMlaMaxTok>(const MlaBatch<kMlaMaxTok>&, int, size_t,
+                                                      size_t, cudaStream_t);
 
 }  // namespace wh

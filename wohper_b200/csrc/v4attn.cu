@@ -284,14 +284,16 @@ wh_status wh_v4_attention(wh_ctx* c, const wh_v4_attn* L, int tokens, const int*
     WH_CUDA(wh::launch_norm(nh, s));
     WH_CUDA(wh::launch_norm(nk, s));
   }
-  // attention core, per token
+  // attention core, every token in one set of launches
+  MlaToken mt[wh::kNormMaxTok];
   for (int t = 0; t < tokens; ++t) {
     const int cc = compressed_count ? compressed_count[t] : 0;
-    if ((st = wh_mla_attention(c, q + (size_t)t * ld_q, heads, hd, nope, kv_caches[t], kv_stride,
-                               token_pos[t], L->window, cc > 0 ? compressed[t] : nullptr, cc,
-                               L->sink, inv_freqs, attn + (size_t)t * ld_q, stream)) != WH_OK)
-      return st;
+    mt[t] = MlaToken{q + (size_t)t * ld_q, kv_caches[t], token_pos[t],
+                     cc > 0 ? compressed[t] : nullptr, cc, attn + (size_t)t * ld_q};
   }
+  if ((st = mla_attention_tokens(c, heads, hd, nope, kv_stride, L->window, L->sink, inv_freqs, mt,
+                                 tokens, stream)) != WH_OK)
+    return st;
   // grouped low-rank output projection (src/compute.rs:4244-4293)
   if ((st = wh_fp8_gemv_grouped(c, L->wo_a.weight, L->wo_a.scale, L->wo_a.rows, L->wo_a.cols,
                                 L->wo_a.scale_rows, L->wo_a.scale_cols, 0, o_mid, attn, tokens,
