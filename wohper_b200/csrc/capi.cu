@@ -502,22 +502,26 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
   a.x_group_rows = x_group_rows;
   a.x_group_off = x_group_off;
 
-  const bool fast0 = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
-                     ldx % 4 == 0 && fp8_gemv_smem_bytes(1, cols) <= 200 * 1024 &&
-                     x_group_off % 4 == 0;
-  const int nrows = row_end - row_start;
-  int tb = batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8;
-  while (tb > 1 && fp8_gemv_smem_bytes(tb, cols) > 200 * 1024) tb /= 2;
-  const int tiles = (batch + tb - 1) / tb;
-  int per = std::max(1, c->num_sms / tiles);
-  int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
-  if (x_group_rows > 0) {
-    // every CTA's rows must lie in one group: a box height dividing the group
-    // and the start row
-    while (box_rows > 1 && (x_group_rows % box_rows != 0 || row_start % box_rows != 0)) --box_rows;
-  }
-  const bool fast = fast0;
+  // the columns one input spans (grouped: every group's slice)
+  const long long xspan =
+      x_group_rows > 0 ? (long long)(rows / x_group_rows - 1) * x_group_off + cols : cols;
+  const bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
+                    ldx % 4 == 0 && x_group_off % 4 == 0 && cols <= 8192 &&
+                    (batch == 1 ? fp8_gemv_rg_smem_bytes(cols) <= 200 * 1024
+                                : act_quant_block == 0 ||
+                                      (xspan % act_quant_block == 0 &&
+                                       cols % act_quant_block == 0));
   if (fast) {
+    const int nrows = row_end - row_start;
+    const int tiles = batch == 1 ? 1 : (batch + 15) / 16;
+    int per = std::max(1, c->num_sms / tiles);
+    int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
+    if (x_group_rows > 0) {
+      // every CTA's rows must lie in one group: a box height dividing the group
+      // and the start row
+      while (box_rows > 1 && (x_group_rows % box_rows != 0 || row_start % box_rows != 0))
+        --box_rows;
+    }
     a.box_rows = box_rows;
     auto key = std::make_tuple((const void*)weight, rows, cols, box_rows);
     auto it = c->fp8_maps.find(key);
@@ -527,22 +531,23 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
       if (st != WH_OK) return st;
       it = c->fp8_maps.emplace(key, m).first;
     }
-    // the launcher picks TB from batch; keep it consistent with the smem check
-    if (tb != (batch < 8 ? (batch < 4 ? (batch < 2 ? 1 : 2) : 4) : 8)) {
-      // large cols: run the batch in slices the shared memory can hold
-      for (int b0 = 0; b0 < batch; b0 += tb) {
-        Fp8GemvArgs s = a;
-        s.x = x + (size_t)b0 * ldx;
-        s.y = y + (size_t)b0 * ldy;
-        s.addend = addend ? addend + (size_t)b0 * ldy : nullptr;
-        s.batch = std::min(tb, batch - b0);
-        WH_CUDA(launch_fp8_gemv(&it->second, s, c->num_sms, stream, false));
-      }
-      return WH_OK;
+    if (batch > 1 && act_quant_block > 0) {
+      // the batched kernel streams its inputs: quantise each input's span
+      // beforehand (blocks never straddle inputs or groups)
+      wh_status st = c->ensure_work(sizeof(float) * (size_t)batch * xspan);
+      if (st != WH_OK) return st;
+      float* xw = static_cast<float*>(c->work);
+      WH_CUDA(cudaMemcpy2DAsync(xw, sizeof(float) * xspan, x, sizeof(float) * ldx,
+                                sizeof(float) * xspan, batch, cudaMemcpyDeviceToDevice, stream));
+      WH_CUDA(launch_act_quant(xw, (long long)batch * xspan, act_quant_block, c->status,
+                               c->num_sms, stream));
+      a.x = xw;
+      a.ldx = (int)xspan;
+      a.act_quant_block = 0;
     }
-    // one input: programmatic dependent launch, so that back-to-back GEMVs
-    // overlap one's weight stream with the previous one's tail
-    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, batch == 1 && c->pdl()));
+    // programmatic dependent launch, so that back-to-back GEMVs overlap one's
+    // weight stream with the previous one's tail
+    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, c->pdl()));
     return WH_OK;
   }
   // generic path

@@ -168,170 +168,115 @@ constexpr int kFp8StageBytes = 32 * 128;  // up to 32 rows x 128 B, 1024-aligned
 constexpr int kFp8MaxStages = 48;
 constexpr size_t kFp8SmemBudget = 200 * 1024;
 
-// stages that fit next to tb x cols floats of input
-static int fp8_stages(int tb, int cols, int ngroups) {
-  long long room = (long long)kFp8SmemBudget - 1024 - (long long)tb * cols * 4 -
-                   2 * kFp8MaxStages * 8 - (32LL * (cols / 128) + 16);
-  int ns = (int)std::max(0LL, room / kFp8StageBytes);
-  return std::min({ns, kFp8MaxStages, ngroups});
+
+// ---------------------------------------------------------------------------
+// Batched path (2..N inputs): the inputs stream with the weights.  Each ring
+// stage holds one 128-column group: the weight box [32 rows][128 B] (TMA) and
+// the group's 128 columns of each of the tile's TB inputs (one 512-byte bulk
+// copy per input), so nothing is staged before the first group and a CTA
+// holds 4 stages.  Lane mapping as fp8_gemv_tma_kernel (8 lanes per row, lane
+// q the chains 2(q&3), 2(q&3)+1 of g0 or g1); the row's weights of a group
+// are decoded once and applied to the TB inputs.  Inputs are act-quantised
+// beforehand when the call asks for it.
+// ---------------------------------------------------------------------------
+constexpr int kFbStages = 4;
+constexpr int kFbTB = 16;                           // inputs per CTA
+constexpr int kFbStageBytes = 4096 + kFbTB * 512;   // weight box + x tile
+constexpr int kFbThreads = 32 * (8 + 1);            // 8 consumer warps + producer
+
+size_t fp8_gemv_batch_smem_bytes(int scale_cols) {
+  return 1024 + (size_t)kFbStages * kFbStageBytes + 2 * kFbStages * 8 + 32 * (size_t)scale_cols +
+         64;
 }
 
-template <int TB>
-__global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap,
-                                                           Fp8GemvArgs a, int nstages) {
+__global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
+    const __grid_constant__ CUtensorMap wmap, Fp8GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
-  uint64_t* empty = full + kFp8MaxStages;
-  float* xs = reinterpret_cast<float*>(empty + kFp8MaxStages);  // TB x cols
-  uint8_t* scale_s = reinterpret_cast<uint8_t*>(xs + TB * a.cols);  // CTA's scale rows
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kFbStages * kFbStageBytes);
+  uint64_t* empty = full + kFbStages;
+  uint8_t* scale_s = reinterpret_cast<uint8_t*>(empty + kFbStages);  // CTA's scale rows
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nconsumer = (blockDim.x >> 5) - 1;  // last warp is the producer
-  const int box_rows = a.box_rows;
+  const int box_rows = a.box_rows;  // <= 32
   const int row0 = a.row_start + blockIdx.x * box_rows;
-  const int ngroups = a.scale_cols;  // col_group == 128
-  const int tile = blockIdx.y;       // input tile
-  const int tb = min(TB, a.batch - tile * TB);
+  const int ngroups = a.scale_cols;
+  const int tile = blockIdx.y;
+  const int tb = min(kFbTB, a.batch - tile * kFbTB);
+  const float* xbase = fp8_x_rows(a, row0) + (long long)tile * kFbTB * a.ldx;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < nstages; ++s) {
+    for (int s = 0; s < kFbStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], nconsumer);
+      mbar_init(&empty[s], 8);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == nconsumer) {
-    // ---------------- producer: weights do not depend on earlier kernels ----
+  if (warp == 8) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
-      int g = 0, s = 0;
-      uint32_t phase = 0;  // phase of the empty barrier the next refill waits for
+      pdl_wait_prior();  // the inputs may come from the previous kernel
+      int g = 0;
       for (; g < ngroups; ++g) {
-        if (g >= nstages && !mbar_wait(&empty[s], phase, a.status)) break;
-        mbar_arrive_expect_tx(&full[s], box_rows * 128);
-        tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
-        if (++s == nstages) {
-          s = 0;
-          if (g >= nstages) phase ^= 1u;
-        }
+        const int s = g % kFbStages;
+        if (g >= kFbStages && !mbar_wait(&empty[s], ((g / kFbStages) - 1) & 1, a.status)) break;
+        uint8_t* st = stages + s * kFbStageBytes;
+        mbar_arrive_expect_tx(&full[s], box_rows * 128 + tb * 512);
+        tma_load_2d(st, &wmap, &full[s], g * 128, row0);
+        for (int b = 0; b < tb; ++b)
+          bulk_load(st + 4096 + b * 512, xbase + (long long)b * a.ldx + g * 128, 512, &full[s]);
       }
-      // no copy may be in flight when this warp leaves
-      for (int i = max(0, g - nstages); i < g; ++i)
-        if (!mbar_drain(&full[i % nstages], (i / nstages) & 1, a.status)) break;
+      for (int i = max(0, g - kFbStages); i < g; ++i)
+        if (!mbar_drain(&full[i % kFbStages], (i / kFbStages) & 1, a.status)) break;
     }
     return;
   }
 
-  // ---------------- consumers ----------------
-  pdl_wait_prior();  // x may be produced by the previous kernel in the stream
-  const int nthr = nconsumer * 32;
-  // x and the scale rows: every load in flight before the first store (one
-  // memory latency instead of one per pass)
-  for (int b = 0; b < tb; ++b) {
-    const float4* src =
-        reinterpret_cast<const float4*>(fp8_x_rows(a, row0) + (long long)(tile * TB + b) * a.ldx);
-    float4* dst = reinterpret_cast<float4*>(xs + b * a.cols);
-    const int n4 = a.cols / 4;
-    for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * nthr) {
-      float4 v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (i0 + k * nthr < n4) v[k] = __ldg(src + i0 + k * nthr);
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (i0 + k * nthr < n4) dst[i0 + k * nthr] = v[k];
-    }
-  }
-  // the UE8M0 scale rows this CTA's rows use (<= 32), so the group loop never
-  // waits on a global load
   const int row_group = a.rows / a.scale_rows;
   const int last_row = min(row0 + box_rows, a.row_end) - 1;
   const int srow0 = row0 / row_group;
   const int nsrows = last_row / row_group - srow0 + 1;
-  for (int i = threadIdx.x; i < nsrows * a.scale_cols; i += nthr)
+  for (int i = threadIdx.x; i < nsrows * a.scale_cols; i += 256)
     scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
-  asm volatile("bar.sync 1, %0;" ::"r"(nthr));
-  if (a.act_quant_block > 0) {
-    for (int b = 0; b < tb; ++b)
-      act_quant_smem_warp(xs + b * a.cols, a.cols, a.act_quant_block, warp, nconsumer, lane, &c_aq);
-    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
-  }
+  asm volatile("bar.sync 1, 256;" ::: "memory");
 
-  // 8 lanes per row; lane q holds the reference's chains j = 2(q & 3) and
-  // 2(q & 3) + 1 of g0 (q < 4: columns 16c + 2q, +1) or of g1 (q >= 4: columns
-  // 16c + 8 + 2(q - 4), +1), c = 0..7 in order.  Lanes q and q ^ 4 add g0_j and
-  // g1_j; acc_j = fma(g0_j + g1_j, scale, acc_j) as the reference.
   const int rloc = warp * 4 + (lane >> 3);  // row within the box
   const int q = lane & 7;
   const int row = row0 + rloc;
   const bool active = rloc < box_rows && row < a.row_end;
-  const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
   const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
+  // the lane's two columns within each 16-column chunk
+  const int cofs = (q < 4 ? 0 : 8) + 2 * (q & 3);
 
-  float2 acc[TB];
+  float2 acc[kFbTB];
 #pragma unroll
-  for (int b = 0; b < TB; ++b) acc[b] = make_float2(0.0f, 0.0f);
-
-  // Software pipeline: the weights (and, for one input, x) of group g + 1
-  // are loaded from shared memory while group g is decoded and accumulated.
+  for (int b = 0; b < kFbTB; ++b) acc[b] = make_float2(0.0f, 0.0f);
   bool ok = true;
-  uint32_t wv[8], wn[8];
-  float2 xc[8], xn[8];  // x of the current / next group (TB == 1 only)
-  auto load_group = [&](int slot, int g, uint32_t (&w)[8], float2 (&x)[8]) {
-    const uint8_t* base = stages + slot * kFp8StageBytes + rloc * 128 + 2 * q;
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      w[c] = *reinterpret_cast<const uint16_t*>(base + 16 * (c ^ (rloc & 7)));
-    if (TB == 1) {
-      const float* xg = xs + g * 128 + 2 * q;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const float2*>(xg + 16 * c);
+  for (int g = 0; g < ngroups; ++g) {
+    const int s = g % kFbStages;
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (g / kFbStages) & 1, a.status))) {
+      ok = false;
+      break;
     }
-  };
-  int s = 0;
-  uint32_t phase = 0;
-  if (ngroups > 0) {
-    ok = mbar_wait(&full[0], 0, a.status);
-    if (ok) load_group(0, 0, wv, xc);
-  }
-  for (int g = 0; ok && g < ngroups; ++g) {
-    int sn = s + 1;
-    uint32_t pn = phase;
-    if (sn == nstages) {
-      sn = 0;
-      pn ^= 1u;
-    }
-    if (g + 1 < ngroups) {
-      if (!mbar_wait(&full[sn], pn, a.status)) {
-        ok = false;
-        break;
-      }
-      load_group(sn, g + 1, wn, xn);
-    }
-    const float scale = decode_ue8m0(srow_s[g]);
+    const uint8_t* st = stages + s * kFbStageBytes;
     float2 wf[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) wf[c] = h2_to_f2(e4m3x2_to_f16x2(wv[c]));
+    for (int c = 0; c < 8; ++c)
+        wf[c] = h2_to_f2(e4m3x2_to_f16x2(
+          *reinterpret_cast<const uint16_t*>(st + rloc * 128 + 16 * (c ^ (rloc & 7)) + cofs)));
+    const float scale = decode_ue8m0(srow_s[g]);
     const float2 sc = make_float2(scale, scale);
+    const float* xt = reinterpret_cast<const float*>(st + 4096) + cofs;
 #pragma unroll
-    for (int b = 0; b < TB; ++b) {
+    for (int b = 0; b < kFbTB; ++b) {
       if (b < tb) {
-        float2 xv[8];
-        if (TB == 1) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) xv[c] = xc[c];
-        } else {
-          const float* xg = xs + b * a.cols + g * 128 + 2 * q;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) xv[c] = *reinterpret_cast<const float2*>(xg + 16 * c);
-        }
         float2 pj = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) pj = ffma2(wf[c], xv[c], pj);
+        for (int c = 0; c < 8; ++c)
+          pj = ffma2(wf[c], *reinterpret_cast<const float2*>(xt + b * 128 + 16 * c), pj);
         // P_j = g0_j + g1_j: lanes q and q ^ 4 hold g0 / g1 of the same j
         float2 o;
         o.x = __shfl_xor_sync(0xffffffffu, pj.x, 4);
@@ -339,20 +284,13 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
         acc[b] = ffma2(fadd2(pj, o), sc, acc[b]);
       }
     }
-    // release the slot only after the loaded words have been consumed
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    s = sn;
-    phase = pn;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      wv[c] = wn[c];
-      xc[c] = xn[c];
-    }
   }
   if (!ok) return;
+  const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
 #pragma unroll
-  for (int b = 0; b < TB; ++b) {
+  for (int b = 0; b < kFbTB; ++b) {
     if (b < tb) {
       // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
       const float s2 = __fadd_rn(acc[b].x, acc[b].y);
@@ -360,11 +298,11 @@ __global__ void __launch_bounds__(288) fp8_gemv_tma_kernel(const __grid_constant
       const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 2));
       if (q == 0 && active) {
         float tot = __fadd_rn(s8, 0.0f);
-        const int bi = tile * TB + b;
+        const int bi = tile * kFbTB + b;
         if (!isfinite(tot)) {
           // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
-          const float* xb = xs + b * a.cols;
-          tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xb);
+          tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128,
+                                  xbase + (long long)b * a.ldx);
           if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
         }
         const long long o = (long long)bi * a.ldy + (row - a.row_start);
@@ -602,12 +540,6 @@ __global__ void __launch_bounds__(kRgThreads)
 
 static size_t fp8_scale_smem(int cols) { return size_t(32) * (cols / 128) + 16; }
 
-size_t fp8_gemv_smem_bytes(int tb, int cols) {
-  const int ns = fp8_stages(tb, cols, 1 << 20);
-  if (ns < 4) return size_t(1) << 30;  // does not fit: caller takes the generic path
-  return 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
-         size_t(tb) * cols * sizeof(float) + fp8_scale_smem(cols);
-}
 
 cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
                             cudaStream_t stream, bool pdl) {
@@ -635,27 +567,13 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
     if (e != cudaSuccess) return e;
     return cudaLaunchKernelEx(&cfg, fp8_gemv_rowgroup_kernel, *wmap, a, ns);
   }
-  const int tb = a.batch < 8 ? (a.batch < 4 ? (a.batch < 2 ? 1 : 2) : 4) : 8;
-  const int nconsumer = (a.box_rows + 3) / 4;  // 4 rows per consumer warp
-  const int ns = fp8_stages(tb, a.cols, a.scale_cols);
-  cfg.blockDim = dim3(32 * (nconsumer + 1));
-  cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + tb - 1) / tb);
-  cfg.dynamicSmemBytes = 1024 + size_t(ns) * kFp8StageBytes + 2 * kFp8MaxStages * sizeof(uint64_t) +
-                         size_t(tb) * a.cols * sizeof(float) + fp8_scale_smem(a.cols);
-  cudaError_t e;
-#define WH_LAUNCH_TB(T)                                                                     \
-  case T:                                                                                   \
-    e = ensure_smem(fp8_gemv_tma_kernel<T>, cfg.dynamicSmemBytes);                          \
-    if (e != cudaSuccess) return e;                                                         \
-    return cudaLaunchKernelEx(&cfg, fp8_gemv_tma_kernel<T>, *wmap, a, ns);
-  switch (tb) {
-    WH_LAUNCH_TB(1)
-    WH_LAUNCH_TB(2)
-    WH_LAUNCH_TB(4)
-    WH_LAUNCH_TB(8)
-  }
-#undef WH_LAUNCH_TB
-  return cudaErrorInvalidValue;
+  // 2..N inputs: the streaming batched kernel, kFbTB inputs per CTA
+  cfg.blockDim = dim3(kFbThreads);
+  cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + kFbTB - 1) / kFbTB);
+  cfg.dynamicSmemBytes = fp8_gemv_batch_smem_bytes(a.scale_cols);
+  cudaError_t e = ensure_smem(fp8_gemv_batch_kernel, cfg.dynamicSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, fp8_gemv_batch_kernel, *wmap, a);
 }
 
 cudaError_t launch_act_quant(float* v, long long n, int block, uint32_t* status, int num_sms,

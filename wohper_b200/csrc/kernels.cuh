@@ -166,7 +166,6 @@ struct Fp8GemvArgs {
 
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);
 const ActQuantTable* act_quant_table_device();
-size_t fp8_gemv_smem_bytes(int tb, int cols);
 // wmap == nullptr selects the generic kernel.
 cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
                             cudaStream_t stream, bool pdl);
