@@ -174,21 +174,15 @@ struct DevExpertSet {
   Fp4ExpertDev* experts = nullptr;  // device [n]
   CUtensorMap* gmaps = nullptr;     // device [n][3], grouped-GEMM boxes (nullable)
   CUtensorMap* dmaps = nullptr;     // device [n], w2 boxes [8 rows][128 B] (decode kernel)
-  CUtensorMap* umaps = nullptr;     // device [n][2], w1/w3 boxes [8 rows][128 B] (moe_up)
   int n = 0;
 };
 
 wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) {
-  std::vector<CUtensorMap> maps(size_t(n) * 3), dmaps(n), umaps(size_t(n) * 2);
+  std::vector<CUtensorMap> maps(size_t(n) * 3), dmaps(n);
   std::vector<Fp4ExpertDev> ex(n);
   for (int i = 0; i < n; ++i) {
     const wh_fp4_expert& e = list[i];
     wh_status st;
-    if ((st = make_u8_map(&umaps[i * 2 + 0], e.w1.packed_weight, e.w1.rows, e.w1.cols / 2,
-                          kMoeUpWarpRows)) ||
-        (st = make_u8_map(&umaps[i * 2 + 1], e.w3.packed_weight, e.w3.rows, e.w3.cols / 2,
-                          kMoeUpWarpRows)))
-      return st;
     if ((st = make_u8_map(&dmaps[i], e.w2.packed_weight, e.w2.rows, e.w2.cols / 2,
                           kDecDownRows)))
       return st;
@@ -206,9 +200,6 @@ wh_status build_expert_set(const wh_fp4_expert* list, int n, DevExpertSet* out) 
   }
   WH_CUDA(cudaMalloc(&out->maps, maps.size() * sizeof(CUtensorMap)));
   WH_CUDA(cudaMalloc(&out->dmaps, dmaps.size() * sizeof(CUtensorMap)));
-  WH_CUDA(cudaMalloc(&out->umaps, umaps.size() * sizeof(CUtensorMap)));
-  WH_CUDA(cudaMemcpy(out->umaps, umaps.data(), umaps.size() * sizeof(CUtensorMap),
-                     cudaMemcpyHostToDevice));
   WH_CUDA(cudaMalloc(&out->experts, ex.size() * sizeof(Fp4ExpertDev)));
   WH_CUDA(cudaMemcpy(out->maps, maps.data(), maps.size() * sizeof(CUtensorMap),
                      cudaMemcpyHostToDevice));
@@ -224,7 +215,6 @@ void free_expert_set(DevExpertSet& s) {
   if (s.experts) cudaFree(s.experts);
   if (s.gmaps) cudaFree(s.gmaps);
   if (s.dmaps) cudaFree(s.dmaps);
-  if (s.umaps) cudaFree(s.umaps);
   s = DevExpertSet{};
 }
 
@@ -369,7 +359,6 @@ struct wh_moe_plan {
   DevExpertSet set;  // routed experts, then the shared expert
   uint32_t* counters = nullptr;      // router: [max_tokens]
   uint32_t* blk_counters = nullptr;  // moe_up: [max_tokens][slots][inter/64]
-  uint32_t* down_counters = nullptr;  // moe_down: [max_tokens][hidden/16]
   bool grouped = false;              // tensor-core path available (desc.exact == 0)
   uint32_t* dec_sync = nullptr;      // decode kernel's grid counters [4] (zero at rest)
   int decode_ok = -1;                // one-token persistent kernel: -1 not checked yet
@@ -824,7 +813,6 @@ wh_status wh_fp4_expert_forward(wh_ctx* c, const wh_fp4_expert* e, const float* 
     float* hqm = reinterpret_cast<float*>(base + o_hqm);
     MoeArgs a{};
     a.maps = it->second.maps;
-    a.umaps = it->second.umaps;
     a.experts = it->second.experts;
     a.num_experts = 0;
     a.has_shared = 1;
@@ -1160,9 +1148,6 @@ wh_status wh_moe_plan_create(wh_ctx* c, const wh_moe_desc* d, wh_moe_plan** out)
   if (e == cudaSuccess) e = cudaMemset(p->counters, 0, sizeof(uint32_t) * d->max_tokens);
   if (e == cudaSuccess) e = cudaMalloc(&p->blk_counters, sizeof(uint32_t) * nblk);
   if (e == cudaSuccess) e = cudaMemset(p->blk_counters, 0, sizeof(uint32_t) * nblk);
-  const size_t ndown = (size_t)d->max_tokens * (d->hidden / kMoeDownRows);
-  if (e == cudaSuccess) e = cudaMalloc(&p->down_counters, sizeof(uint32_t) * ndown);
-  if (e == cudaSuccess) e = cudaMemset(p->down_counters, 0, sizeof(uint32_t) * ndown);
   if (e == cudaSuccess) e = cudaMalloc(&p->dec_sync, sizeof(uint32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(p->dec_sync, 0, sizeof(uint32_t) * 4);
   if (e != cudaSuccess) {
@@ -1179,7 +1164,6 @@ void wh_moe_plan_destroy(wh_moe_plan* p) {
   free_expert_set(p->set);
   if (p->counters) cudaFree(p->counters);
   if (p->blk_counters) cudaFree(p->blk_counters);
-  if (p->down_counters) cudaFree(p->down_counters);
   if (p->dec_sync) cudaFree(p->dec_sync);
   delete p;
 }
@@ -1201,7 +1185,6 @@ struct MoeScratch {
   float* h;
   __half* hq;
   float* hq_mult;
-  float* yk;  // [T][slots][hidden] per-slot down rows for the combine
   size_t bytes;
 };
 MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
@@ -1223,7 +1206,6 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
   s.h = reinterpret_cast<float*>(take(4 * (size_t)T * S * d.inter));
   s.hq = reinterpret_cast<__half*>(take(2 * (size_t)T * S * d.inter));
   s.hq_mult = reinterpret_cast<float*>(take(sizeof(float) * T * S * (d.inter / 64)));
-  s.yk = reinterpret_cast<float*>(take(sizeof(float) * (size_t)T * S * d.hidden));
   s.bytes = off;
   return s;
 }
@@ -1495,9 +1477,6 @@ static wh_status moe_ffn_routed(wh_ctx* c, const wh_moe_plan* p, const float* x,
   if ((pst = c->prof_mark(stream)) != WH_OK) return pst;
   MoeArgs a{};
   a.maps = p->set.maps;
-  a.umaps = p->set.umaps;
-  a.yk = s.yk;
-  a.down_counters = p->down_counters;
   a.experts = p->set.experts;
   a.num_experts = d.num_experts;
   a.has_shared = d.shared ? 1 : 0;

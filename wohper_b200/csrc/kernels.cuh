@@ -209,7 +209,6 @@ struct RouterArgs {
 // kernels size their shared-memory stages and transaction counts from them.
 constexpr int kMoeUpRows = 32;
 constexpr int kMoeDownRows = 16;
-constexpr int kMoeUpWarpRows = 8;  // moe_up: rows of w1 and of w3 per one-warp CTA (umaps)
 struct Fp4ExpertDev {
   const uint8_t* w1_scale;  // [inter][hidden/32]
   const uint8_t* w3_scale;
@@ -235,9 +234,6 @@ struct MoeArgs {
   float* expert_out;           // nullable [tokens][slots][hidden] (per-expert outputs)
   int combine;                 // 1: routed combine + shared; 0: write expert_out only
   uint32_t* status;
-  const CUtensorMap* umaps;    // [num_experts + has_shared][2] w1, w3 boxes [8 rows][128 B]
-  float* yk;                   // combine: scratch [tokens][slots][hidden] of per-slot rows
-  uint32_t* down_counters;     // combine: zeroed [tokens][hidden/16] arrival counters
 };
 cudaError_t launch_moe_up(const MoeArgs& a, int num_sms, cudaStream_t stream, bool pdl);
 cudaError_t launch_moe_down(const MoeArgs& a, int num_sms, cudaStream_t stream, bool pdl);

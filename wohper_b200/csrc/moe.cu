@@ -462,70 +462,24 @@ __device__ __forceinline__ float hsum8(const float a[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// moe_up: grid (inter/8, slots, tokens) of one consumer warp + one TMA
-// producer warp.  The consumer computes 8 rows of w1 (lanes 0-15) and the same
-// 8 rows of w3 (lanes 16-31), two lanes per row (each lane four of the row's
-// eight FMA chains, in the reference's order), then SwiGLU; the last of the 8
-// CTAs of each 64-row act-quant block quantises it (atomic arrival counter, no
-// waiting).  One warp per CTA spreads the 1792 warp-units of a one-token call
-// evenly over the SMs (12 or 13 per SM on 148 SMs); with four-warp CTAs an
-// SM held 3 or 4 CTAs, a third more work on the loaded SMs.  The token x and
-// its block multipliers are read through L1 (every CTA of an SM reads the same
-// 8 KB), so a CTA's shared memory is its weight ring and scale rows only.
+// moe_up: grid (inter/32, slots, tokens).  Warps 0-1 compute the 32 w1 (gate)
+// rows, warps 2-3 the same w3 (up) rows, two lanes per row (each lane four of
+// the row's eight FMA chains); warp 4 streams both with TMA.  Four consumer
+// warps per CTA spread the FMA work evenly over an SM's four schedulers.  The
+// SwiGLU hidden of the 32 rows goes to global memory; the second CTA of each
+// 64-row act-quant block to finish quantises the block (atomic arrival
+// counter, no waiting).
 // ---------------------------------------------------------------------------
-constexpr int kUpStages = 6;
-constexpr int kUpRows = kMoeUpWarpRows;       // 8
-constexpr int kUpBox = kUpRows * 128;         // 1 KB
+constexpr int kUpConsumers = 4;
+constexpr int kUpThreads = (kUpConsumers + 1) * 32;
+constexpr int kUpStages = 4;
+constexpr int kUpRows = kMoeUpRows;
+constexpr int kUpBox = kUpRows * 128;         // 4 KB
 constexpr int kUpStageBytes = 2 * kUpBox;     // w1 box + w3 box
-constexpr int kUpThreads = 64;
 
 size_t moe_up_smem_bytes(int hidden) {
-  return 1024 + kUpStages * kUpStageBytes + 2 * kUpStages * 8 + 16 + 2 * kUpRows * (hidden / 32) +
-         64;
-}
-
-// fp4_box_accumulate_half with the input read from global memory (through
-// L1; written by the previous kernel, read after its completion)
-__device__ __forceinline__ void fp4_box_accumulate_half_g(const uint4 (&wb)[8], const __half* xs,
-                                                          const float* xm, int box,
-                                                          uint2 sb, int hf, float acc[4]) {
-  const uint32_t sbw[2] = {sb.x, sb.y};
-  const int sh = 16 * hf;
-  const uint2* xp = reinterpret_cast<const uint2*>(xs) + hf;
-  uint2 xv[2][4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) xv[0][c] = xp[8 * (box * 8) + 2 * c];
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    const int G = box * 8 + g;
-    if (g + 1 < 8) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) xv[(g + 1) & 1][c] = xp[8 * (G + 1) + 2 * c];
-    }
-    const uint32_t ws[4] = {wb[g].x, wb[g].y, wb[g].z, wb[g].w};
-    float gacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t hw = ws[c] >> sh;
-      const uint32_t w0 = fp4x2_to_f16x2_ref(hw);
-      const uint32_t w1 = fp4x2_to_f16x2_ref(hw >> 8);
-      const uint2 xc = xv[g & 1][c];
-      gacc[0] = fma_f16lo(w0, xc.x, gacc[0]);
-      gacc[1] = fma_f16hi(w0, xc.x, gacc[1]);
-      gacc[2] = fma_f16lo(w1, xc.y, gacc[2]);
-      gacc[3] = fma_f16hi(w1, xc.y, gacc[3]);
-    }
-    const float m = xm[G >> 1];
-    const float s8 = __fmul_rn(decode_ue8m0((sbw[g >> 2] >> (8 * (g & 3))) & 0xff), 0.125f);
-    const float2 mm = make_float2(m, m), ss = make_float2(s8, s8);
-#pragma unroll
-    for (int j = 0; j < 4; j += 2) {
-      const float2 r = ffma2(fmul2(make_float2(gacc[j], gacc[j + 1]), mm), ss,
-                             make_float2(acc[j], acc[j + 1]));
-      acc[j] = r.x;
-      acc[j + 1] = r.y;
-    }
-  }
+  return 1024 + kUpStages * kUpStageBytes + 2 * kUpStages * 8 + 16 + hidden * 2 +
+         (hidden / 64) * 4 + 128 + 2 * kUpRows * (hidden / 32) + 64;
 }
 
 __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __half* __restrict__ xq,
@@ -536,22 +490,24 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kUpStages * kUpStageBytes);
   uint64_t* empty = full + kUpStages;
-  uint64_t* sbar = empty + kUpStages;
-  uint8_t* ssm = reinterpret_cast<uint8_t*>(sbar + 2);  // [2][8 rows][hidden/32] scales
+  uint64_t* xbar = empty + kUpStages;
+  __half* xs = reinterpret_cast<__half*>(xbar + 2);
+  float* xm = reinterpret_cast<float*>(xs + a.hidden);
+  float* gsh = xm + a.hidden / 64;  // [32] gate values handed to the up warp
+  uint8_t* ssm = reinterpret_cast<uint8_t*>(gsh + 32);  // [2][32 rows][hidden/32] scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.z, slot = blockIdx.y;
   const int row0 = blockIdx.x * kUpRows;
   const int nslots = a.topk + a.has_shared;
   const int nbox = a.hidden / 256;  // 128 B = 256 columns per box
-  const int scols = a.hidden / 32;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUpStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kUpConsumers);
     }
-    mbar_init(sbar, 1);
+    mbar_init(xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -565,50 +521,75 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
   }
   const bool valid_expert = expert >= 0 && expert < a.num_experts + a.has_shared;
 
-  if (warp == 1) {
+  if (warp == kUpConsumers) {
     if (lane == 0 && valid_expert) {
-      const CUtensorMap* m1 = a.umaps + expert * 2 + 0;
-      const CUtensorMap* m3 = a.umaps + expert * 2 + 1;
+      const CUtensorMap* m1 = a.maps + expert * 3 + 0;
+      const CUtensorMap* m3 = a.maps + expert * 3 + 1;
       prefetch_tensormap(m1);
       prefetch_tensormap(m3);
-      const Fp4ExpertDev& ex = a.experts[expert];
-      // this CTA's scale rows ([8 rows][hidden/32] per matrix, contiguous)
-      mbar_arrive_expect_tx(sbar, 2 * kUpRows * scols);
-      bulk_load(ssm, ex.w1_scale + (long long)row0 * scols, kUpRows * scols, sbar);
-      bulk_load(ssm + kUpRows * scols, ex.w3_scale + (long long)row0 * scols, kUpRows * scols,
-                sbar);
-      int i = 0;
-      for (; i < nbox; ++i) {
+      auto issue = [&](int i) {
         const int s = i % kUpStages;
-        if (i >= kUpStages && !mbar_wait(&empty[s], ((i / kUpStages) - 1) & 1, a.status)) break;
         mbar_arrive_expect_tx(&full[s], kUpStageBytes);
         tma_load_2d(stages + s * kUpStageBytes, m1, &full[s], i * 128, row0);
         tma_load_2d(stages + s * kUpStageBytes + kUpBox, m3, &full[s], i * 128, row0);
+      };
+      const int scols = a.hidden / 32;
+      const Fp4ExpertDev& ex = a.experts[expert];
+      // x and its multipliers (produced by the router) and this CTA's scale
+      // rows ([32 rows][hidden/32] per matrix, contiguous) on one barrier
+      mbar_arrive_expect_tx(xbar, a.hidden * 2 + (a.hidden / 64) * 4 + 2 * kUpRows * scols);
+      auto load_scales = [&]() {
+        bulk_load(ssm, ex.w1_scale + (long long)row0 * scols, kUpRows * scols, xbar);
+        bulk_load(ssm + kUpRows * scols, ex.w3_scale + (long long)row0 * scols, kUpRows * scols,
+                  xbar);
+      };
+      auto load_x = [&]() {
+        bulk_load(xs, xq + (long long)t * a.hidden, a.hidden * 2, xbar);
+        bulk_load(xm, xq_mult + (long long)t * (a.hidden / 64), (a.hidden / 64) * 4, xbar);
+      };
+      int i = 0;
+      if (slot >= a.topk) {
+        // shared expert: weights and scales do not depend on the router, so
+        // they stream while it runs; x once it has completed
+        load_scales();
+        for (; i < nbox && i < kUpStages; ++i) issue(i);  // first pass needs no free slot
+        pdl_wait_prior();
+        load_x();
+      } else {
+        // routed (the router has completed): the small inputs go ahead of the
+        // ring so that they do not queue behind 32 KB of weights
+        load_x();
+        load_scales();
+        for (; i < nbox && i < kUpStages; ++i) issue(i);
       }
-      // leave no copy in flight if the consumer stopped early
+      for (; i < nbox; ++i) {
+        if (!mbar_wait(&empty[i % kUpStages], ((i / kUpStages) - 1) & 1, a.status)) break;
+        issue(i);
+      }
+      // leave no copy in flight if the consumers stopped early
       for (int k = max(0, i - kUpStages); k < i; ++k)
         if (!mbar_drain(&full[k % kUpStages], (k / kUpStages) & 1, a.status)) break;
-      mbar_drain(sbar, 0, a.status);
+      mbar_drain(xbar, 0, a.status);
     }
     return;
   }
   if (!valid_expert) {
-    if (lane == 0) flag(a.status, WH_DEV_BADARG);
+    if (threadIdx.x == 0) flag(a.status, WH_DEV_BADARG);
     return;
   }
-  // x and its multipliers come from the router: wait for it in every slot (the
-  // routed slots already did); the next kernel reads the router's ids before
-  // its own wait, so it is released only now
+  // the next kernel reads the router's ids before its own wait: only release it
+  // once the router has completed (shared-slot CTAs have not waited yet)
   if (slot >= a.topk) pdl_wait_prior();
   pdl_launch_dependents();
-  bool ok = __all_sync(0xffffffffu, mbar_wait(sbar, 0, a.status));
+  // a failed (timed-out) wait skips the work but still reaches the named
+  // barrier below, so the partner warp is never stranded
+  bool ok = __all_sync(0xffffffffu, mbar_wait(xbar, 0, a.status));
 
-  const int mat = lane >> 4;          // 0: w1, 1: w3
-  const int rl = (lane & 15) >> 1;    // row within the CTA's 8
-  const int hf = lane & 1;            // chain half
+  const int mat = warp >> 1;                      // 0: w1, 1: w3
+  const int rl = (warp & 1) * 16 + (lane >> 1);   // row within the CTA's 32
+  const int hf = lane & 1;                        // chain half
   const int row = row0 + rl;
-  const __half* xs = xq + (long long)t * a.hidden;
-  const float* xm = xq_mult + (long long)t * (a.hidden / 64);
+  const int scols = a.hidden / 32;
   const uint8_t* srow = ssm + (mat * kUpRows + rl) * scols;
   float acc[4];
 #pragma unroll
@@ -617,6 +598,7 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
   for (int i = 0; ok && i < nbox; ++i) {
     const int s = i % kUpStages;
     const uint2 sb = *reinterpret_cast<const uint2*>(srow + i * 8);
+    // warp-uniform: the lane pairs exchange partial sums with shuffles
     if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kUpStages) & 1, a.status))) {
       ok = false;
       break;
@@ -624,37 +606,39 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
     const uint8_t* base = stages + s * kUpStageBytes + mat * kUpBox + rl * 128;
     uint4 wb[8];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ rl));
-    fp4_box_accumulate_half_g(wb, xs, xm, i, sb, hf, acc);
-    // release the slot only after every lane has consumed its loads
+    for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (rl & 7)));
+    fp4_box_accumulate_half(wb, xs, xm, i, sb, hf, acc);
+    // release the slot only after every lane has consumed its loads: an
+    // arrive issued while shared-memory loads are still outstanding lets the
+    // next TMA overwrite the slot under them (seen with several CTAs per SM)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!ok) return;
   const float v = __fadd_rn(hsum8_pair(acc), 0.0f);
   if (!isfinite(v)) flag(a.status, WH_DEV_NONFINITE);
-  // the gate of row rl (lane 2 rl) to its up lane (16 + 2 rl)
-  const float gate = __shfl_sync(0xffffffffu, v, lane & 15);
+  if (mat == 0 && hf == 0) gsh[rl] = v;
+  const int ok_all = bar_and(1, kUpConsumers * 32, ok);
+  if (mat == 0 || !ok_all) return;
+
+  // SwiGLU with the reference clamps (src/deepseek_v4.rs:556-596)
+  const float gated = fminf(gsh[rl], 10.0f);
+  float upped = v;
+  upped = upped < -10.0f ? -10.0f : upped;
+  upped = upped > 10.0f ? 10.0f : upped;
+  const float hv = __fmul_rn(silu_ref(gated), upped);
   const long long hb = ((long long)t * nslots + slot) * a.inter;
-  if (mat == 1 && hf == 0) {
-    // SwiGLU with the reference clamps (src/deepseek_v4.rs:556-596)
-    const float gated = fminf(gate, 10.0f);
-    float upped = v;
-    upped = upped < -10.0f ? -10.0f : upped;
-    upped = upped > 10.0f ? 10.0f : upped;
-    a.h[hb + row] = __fmul_rn(silu_ref(gated), upped);
-  }
-  // act quant over the 64-row block (src/deepseek_v4.rs:595): the last of its
-  // 8 CTAs quantises it.  Every lane fences its store before lane 0 publishes
-  // the arrival.
+  if (hf == 0) a.h[hb + row] = hv;
+  // act quant over the 64-row block (src/deepseek_v4.rs:595): the later of the
+  // two 32-row CTAs quantises the whole block.  Every thread fences its store
+  // before warp 2's lane 0 publishes the arrival.
   __threadfence();
-  __syncwarp();
-  constexpr uint32_t kArrivals = 64 / kUpRows;
+  bar_and(2, 64, 1);
+  if (warp != 2) return;
   uint32_t prev = 0;
   const long long blk = hb / 64 + row0 / 64;
   if (lane == 0) prev = atomicAdd(&a.blk_counters[blk], 1u);
   prev = __shfl_sync(0xffffffffu, prev, 0);
-  if (prev != kArrivals - 1) return;
+  if (prev == 0) return;
   __threadfence();
   const int b0 = (row0 / 64) * 64;
   const float h0 = __ldcg(a.h + hb + b0 + lane), h1 = __ldcg(a.h + hb + b0 + 32 + lane);
@@ -671,20 +655,22 @@ __global__ void __launch_bounds__(kUpThreads) moe_up_kernel(MoeArgs a, const __h
 }
 
 // ---------------------------------------------------------------------------
-// moe_down: grid (hidden/16, slots, tokens) of one consumer warp (16 rows of
-// the slot's w2, two lanes per row) + one TMA producer warp.  With combine,
-// each CTA stores its slot's rows to yk and the last of the row block's slots
-// to arrive (atomic counter) adds them in route order with the shared expert
-// (src/compute.rs:1872-2030), as the 8-warp CTA did in shared memory.
+// moe_down: grid (hidden/16, tokens); 8 consumer warps (warp k = slot k, 16 rows,
+// two lanes per row) + a TMA producer warp
 // ---------------------------------------------------------------------------
+constexpr int kDownConsumers = 8;
+constexpr int kDownThreads = (kDownConsumers + 1) * 32;
 constexpr int kDownStages = 4;
-constexpr int kDownRows = kMoeDownRows;                // 16
+constexpr int kDownRows = kMoeDownRows;
+constexpr int kDownSlots = 8;
 constexpr int kDownBox = kDownRows * 128;              // 2 KB
-constexpr int kDownThreads = 64;
+constexpr int kDownStageBytes = kDownSlots * kDownBox;  // 16 KB
 
 size_t moe_down_smem_bytes(int inter, int slots) {
   (void)slots;
-  return 1024 + kDownStages * kDownBox + 2 * kDownStages * 8 + 16 + kDownRows * (inter / 32) + 64;
+  return 1024 + kDownStages * kDownStageBytes + 2 * kDownStages * 8 + 16 +
+         kDownSlots * (inter * 2 + 16) + kDownSlots * (inter / 64) * 4 +
+         kDownSlots * kDownRows * 4 + kDownSlots * kDownRows * (inter / 32) + 64;
 }
 
 __global__ void __launch_bounds__(kDownThreads) moe_down_kernel(MoeArgs a, const __half* __restrict__ hq,
@@ -692,119 +678,146 @@ __global__ void __launch_bounds__(kDownThreads) moe_down_kernel(MoeArgs a, const
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kDownStages * kDownBox);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kDownStages * kDownStageBytes);
   uint64_t* empty = full + kDownStages;
-  uint64_t* sbar = empty + kDownStages;
-  uint8_t* ssm = reinterpret_cast<uint8_t*>(sbar + 2);  // [16 rows][inter/32]
+  uint64_t* xbar = empty + kDownStages;
+  const int hstride = a.inter * 2 + 16;  // bytes per slot (padded: slots of a warp hit other banks)
+  uint8_t* hs = reinterpret_cast<uint8_t*>(xbar + 2);
+  float* hm = reinterpret_cast<float*>(hs + kDownSlots * hstride);
+  float* ys = hm + kDownSlots * (a.inter / 64);
+  uint8_t* ssm = reinterpret_cast<uint8_t*>(ys + kDownSlots * kDownRows);  // [slot][16][inter/32]
+  __shared__ int slot_expert[kDownSlots];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.z, slot = blockIdx.y;
+  const int t = blockIdx.y;
   const int row0 = blockIdx.x * kDownRows;
   const int nslots = a.topk + a.has_shared;
   const int nbox = a.inter / 256;
-  const int scols = a.inter / 32;
 
-  // the slot's expert: the router's ids (written two kernels back)
-  int e = slot < a.topk ? a.ids[(long long)t * a.topk + slot] : a.num_experts;
-  const bool active = e >= 0 && e < a.num_experts + a.has_shared;
+  if (threadIdx.x < kDownSlots) {
+    int e = -1;
+    if (threadIdx.x < a.topk)
+      e = a.ids[(long long)t * a.topk + threadIdx.x];  // written by the router, 2 kernels back
+    else if (threadIdx.x < nslots)
+      e = a.num_experts;
+    if (e < -1 || e >= a.num_experts + a.has_shared) e = -1;
+    slot_expert[threadIdx.x] = e;
+  }
+  uint64_t* sbar = xbar + 1;  // the slots' w2 scale rows
   if (threadIdx.x == 0) {
     for (int s = 0; s < kDownStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kDownConsumers);
     }
+    mbar_init(xbar, 1);
     mbar_init(sbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == 1) {
-    if (lane == 0 && active) {
-      const CUtensorMap* m2 = a.maps + e * 3 + 2;
-      prefetch_tensormap(m2);
-      // the scale rows depend only on the router's ids: staged before the wait
-      mbar_arrive_expect_tx(sbar, kDownRows * scols);
-      bulk_load(ssm, a.experts[e].w2_scale + (long long)row0 * scols, kDownRows * scols, sbar);
-      int i = 0;
-      for (; i < nbox; ++i) {
+  if (warp == kDownConsumers) {
+    if (lane == 0) {
+      int nvalid = 0;
+      for (int k = 0; k < nslots; ++k) nvalid += slot_expert[k] >= 0;
+      for (int i = 0; i < nbox; ++i) {
         const int s = i % kDownStages;
-        if (i >= kDownStages && !mbar_wait(&empty[s], ((i / kDownStages) - 1) & 1, a.status))
-          break;
-        mbar_arrive_expect_tx(&full[s], kDownBox);
-        tma_load_2d(stages + s * kDownBox, m2, &full[s], i * 128, row0);
+        if (i >= kDownStages && !mbar_wait(&empty[s], ((i / kDownStages) - 1) & 1, a.status)) break;
+        mbar_arrive_expect_tx(&full[s], nvalid * kDownBox);
+        for (int k = 0; k < nslots; ++k) {
+          const int e = slot_expert[k];
+          if (e >= 0)
+            tma_load_2d(stages + s * kDownStageBytes + k * kDownBox, a.maps + e * 3 + 2, &full[s],
+                        i * 128, row0);
+        }
       }
-      for (int k = max(0, i - kDownStages); k < i; ++k)
-        if (!mbar_drain(&full[k % kDownStages], (k / kDownStages) & 1, a.status)) break;
-      mbar_drain(sbar, 0, a.status);
+      for (int i = max(0, nbox - kDownStages); i < nbox; ++i)
+        if (!mbar_drain(&full[i % kDownStages], (i / kDownStages) & 1, a.status)) break;
     }
     return;
   }
+
+  // the w2 scale rows depend only on the router's ids: stage them before the
+  // wait for moe_up (this CTA's 16 rows of each slot's w2 scales are contiguous)
+  const int scols = a.inter / 32;
+  if (threadIdx.x == 0) {
+    int nvalid = 0;
+    for (int k = 0; k < nslots; ++k) nvalid += slot_expert[k] >= 0;
+    mbar_arrive_expect_tx(sbar, nvalid * kDownRows * scols);
+    for (int k = 0; k < nslots; ++k) {
+      const int e = slot_expert[k];
+      if (e >= 0)
+        bulk_load(ssm + k * kDownRows * scols, a.experts[e].w2_scale + (long long)row0 * scols,
+                  kDownRows * scols, sbar);
+    }
+  }
   pdl_wait_prior();  // hq from moe_up
   pdl_launch_dependents();
-  bool ok = true;
-  float yv = 0.0f;
-  const int r = lane >> 1, hf = lane & 1;
+  // stage hq of every slot (bulk copies, one barrier)
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(xbar, nslots * (a.inter * 2 + (a.inter / 64) * 4));
+    for (int k = 0; k < nslots; ++k) {
+      bulk_load(hs + k * hstride, hq + ((long long)t * nslots + k) * a.inter, a.inter * 2, xbar);
+      bulk_load(hm + k * (a.inter / 64), hq_mult + ((long long)t * nslots + k) * (a.inter / 64),
+                (a.inter / 64) * 4, xbar);
+    }
+  }
+  bool ok = __all_sync(0xffffffffu, mbar_wait(sbar, 0, a.status) && mbar_wait(xbar, 0, a.status));
+
+  const int slot = warp;
+  const int r = lane >> 1;
+  const int hf = lane & 1;
   const int row = row0 + r;
-  if (active) {
-    ok = __all_sync(0xffffffffu, mbar_wait(sbar, 0, a.status));
-    const uint8_t* srow = ssm + r * scols;
-    const __half* hs = hq + ((long long)t * nslots + slot) * a.inter;
-    const float* hm = hq_mult + ((long long)t * nslots + slot) * (a.inter / 64);
-    float acc[4];
+  const int e = slot < nslots ? slot_expert[slot] : -1;
+  const bool active = e >= 0;
+  const uint8_t* srow = ssm + ((active ? slot : 0) * kDownRows + r) * scols;
+  const __half* hslot = reinterpret_cast<const __half*>(hs + (active ? slot : 0) * hstride);
+  const float* hmul = hm + (active ? slot : 0) * (a.inter / 64);
+  float acc[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
-    for (int i = 0; ok && i < nbox; ++i) {
-      const int s = i % kDownStages;
-      const uint2 sb = *reinterpret_cast<const uint2*>(srow + i * 8);
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kDownStages) & 1, a.status))) {
-        ok = false;
-        break;
-      }
-      const uint8_t* base = stages + s * kDownBox + r * 128;
-      uint4 wb[8];
+  for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
+  for (int i = 0; ok && i < nbox; ++i) {
+    const int s = i % kDownStages;
+    uint2 sb = make_uint2(0, 0);
+    if (active) sb = *reinterpret_cast<const uint2*>(srow + i * 8);
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kDownStages) & 1, a.status))) {
+      ok = false;
+      break;
+    }
+    uint4 wb[8];
+    if (active) {
+      const uint8_t* base = stages + s * kDownStageBytes + slot * kDownBox + r * 128;
 #pragma unroll
       for (int g = 0; g < 8; ++g) wb[g] = *reinterpret_cast<const uint4*>(base + 16 * (g ^ (r & 7)));
-      fp4_box_accumulate_half_g(wb, hs, hm, i, sb, hf, acc);
-      __syncwarp();  // slot released after its data has been consumed
-      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (!ok) return;
-    yv = __fadd_rn(hsum8_pair(acc), 0.0f);
+    if (active) fp4_box_accumulate_half(wb, hslot, hmul, i, sb, hf, acc);
+    __syncwarp();  // slot released after its data has been consumed
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (ok && active) {  // warp-uniform
+    const float yv = __fadd_rn(hsum8_pair(acc), 0.0f);
     if (!isfinite(yv)) flag(a.status, WH_DEV_NONFINITE);
-    if (hf == 0 && a.expert_out)
-      a.expert_out[((long long)t * nslots + slot) * a.hidden + row] = yv;
+    if (hf == 0) {
+      ys[slot * kDownRows + r] = yv;
+      if (a.expert_out)
+        a.expert_out[((long long)t * nslots + slot) * a.hidden + row] = yv;
+    }
   }
-  if (!a.combine) return;
-  if (hf == 0) a.yk[((long long)t * nslots + slot) * a.hidden + row] = yv;
-  // the last slot of the row block to arrive combines (each lane fences its
-  // store before lane 0 publishes the arrival)
-  __threadfence();
-  __syncwarp();
-  uint32_t prev = 0;
-  const long long cblk = (long long)t * (a.hidden / kDownRows) + blockIdx.x;
-  if (lane == 0) prev = atomicAdd(&a.down_counters[cblk], 1u);
-  prev = __shfl_sync(0xffffffffu, prev, 0);
-  if (prev != (uint32_t)nslots - 1) return;
-  __threadfence();
-  if (lane == 0) a.down_counters[cblk] = 0;  // ready for the next call
-  if (lane >= kDownRows) return;
-  const int rr = row0 + lane;
-  const float* ys = a.yk + (long long)t * nslots * a.hidden + rr;
-  const float* cw = a.combine_w + (long long)t * a.topk;
-  // a slot whose expert id was invalid stored 0 (its weight still counts, as
-  // the three-kernel path did)
-  float routed = 0.0f;
-  if (a.topk == 1) {
-    routed = __ldcg(ys);  // one expert: unweighted (src/compute.rs:1960-1966)
-  } else {
-    for (int k = 0; k < a.topk; ++k)
-      routed = __fadd_rn(routed, __fmul_rn(__ldcg(ys + (long long)k * a.hidden), cw[k]));
+  const int ok_all = bar_and(1, kDownConsumers * 32, ok);
+  if (ok_all && a.combine && threadIdx.x < kDownRows) {
+    const int rr = threadIdx.x;
+    const float* cw = a.combine_w + (long long)t * a.topk;
+    float routed = 0.0f;
+    if (a.topk == 1) {
+      routed = ys[0 * kDownRows + rr];  // one expert: unweighted (src/compute.rs:1960-1966)
+    } else {
+      for (int k = 0; k < a.topk; ++k)
+        routed = __fadd_rn(routed, __fmul_rn(ys[k * kDownRows + rr], cw[k]));
+    }
+    float out = routed;
+    if (a.has_shared) out = a.topk > 0 ? __fadd_rn(ys[a.topk * kDownRows + rr], routed)
+                                       : ys[a.topk * kDownRows + rr];
+    a.y[(long long)t * a.hidden + row0 + rr] = out;
   }
-  float out = routed;
-  if (a.has_shared) {
-    const float sh = __ldcg(ys + (long long)a.topk * a.hidden);
-    out = a.topk > 0 ? __fadd_rn(sh, routed) : sh;
-  }
-  a.y[(long long)t * a.hidden + rr] = out;
 }
 
 // ---------------------------------------------------------------------------
@@ -1071,7 +1084,7 @@ cudaError_t launch_moe_down_ex(const MoeArgs& a, const __half* hq, const float* 
   const size_t smem = moe_down_smem_bytes(a.inter, a.topk + a.has_shared);
   cudaError_t e = ensure_smem(moe_down_kernel, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(a.hidden / kDownRows, a.topk + a.has_shared, a.tokens);
+  dim3 grid(a.hidden / kDownRows, a.tokens);
   cudaLaunchConfig_t cfg = pdl_cfg(grid, dim3(kDownThreads), smem, s, attr, pdl);
   return cudaLaunchKernelEx(&cfg, moe_down_kernel, a, hq, hq_mult);
 }
