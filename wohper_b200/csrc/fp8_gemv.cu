@@ -330,9 +330,8 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
 // ---------------------------------------------------------------------------
 constexpr int kRgConsumers = 8;   // phase-1 warps
 constexpr int kRgRing = 12;       // weight stages in flight per CTA
-constexpr int kRgChain = 8;       // chain warps: 32 rows x 8 chains
 constexpr int kRgMaxGroups = 64;  // cols <= 8192
-constexpr int kRgThreads = 32 * (kRgConsumers + kRgChain + 1);
+constexpr int kRgThreads = 32 * (kRgConsumers + 1);
 
 static int fp8_rg_stages(int cols) {
   const int ngroups = cols / 128;
@@ -361,8 +360,7 @@ __global__ void __launch_bounds__(kRgThreads)
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
   uint64_t* empty = full + kFp8MaxStages;
-  uint64_t* pready = empty + kFp8MaxStages;                       // [kRgMaxGroups]
-  float* xs = reinterpret_cast<float*>(pready + kRgMaxGroups);    // cols
+  float* xs = reinterpret_cast<float*>(empty + kFp8MaxStages + kRgMaxGroups);  // cols
   const int ngroups = a.scale_cols;                               // col_group == 128
   float* ps = xs + a.cols;                                        // [ngroups][32][8]
   uint8_t* scale_s = reinterpret_cast<uint8_t*>(ps + ngroups * 32 * 8);
@@ -382,13 +380,11 @@ __global__ void __launch_bounds__(kRgThreads)
     if (t < nstages) mbar_init(&full[t], 1);
     else if (t < 2 * kFp8MaxStages && t - kFp8MaxStages < nstages && ring)
       mbar_init(&empty[t - kFp8MaxStages], 1);  // one warp consumes each group
-    else if (t >= 2 * kFp8MaxStages && t - 2 * kFp8MaxStages < ngroups)
-      mbar_init(&pready[t - 2 * kFp8MaxStages], 1);
-    if (t < 2 * kFp8MaxStages + kRgMaxGroups) fence_barrier_init();
+    if (t < 2 * kFp8MaxStages) fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kRgConsumers + kRgChain) {
+  if (warp == kRgConsumers) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
       int g = 0, s = 0;
@@ -413,44 +409,9 @@ __global__ void __launch_bounds__(kRgThreads)
   const int last_row = min(row0 + box_rows, a.row_end) - 1;
   const int srow0 = row0 / row_group;
   const int nsrows = last_row / row_group - srow0 + 1;
-  if (warp >= kRgConsumers) {
-    // ---- chain warps: acc_j over the groups as their P_j land ----
-    const int t = threadIdx.x - nthr;  // 0 .. 255
-    for (int i = t; i < nsrows * a.scale_cols; i += 32 * kRgChain)
-      scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
-    asm volatile("bar.sync 2, %0;" ::"r"(32 * kRgChain));
-    const int rr = t >> 3, j = t & 7;
-    const int row = row0 + rr;
-    const bool active = rr < box_rows && row < a.row_end;
-    const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
-    const float* pj = ps + rr * 8 + j;
-    float acc = 0.0f;
-    bool ok = true;
-    for (int g = 0; g < ngroups; ++g) {
-      if (!mbar_wait(&pready[g], 0, a.status)) {
-        ok = false;
-        break;
-      }
-      acc = fmaf(pj[g * 256], decode_ue8m0(srow_s[g]), acc);
-    }
-    // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
-    const float s2 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-    const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
-    const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));
-    pdl_wait_prior();  // the addend may come from the previous kernel
-    if (j == 0 && active && ok) {
-      float tot = __fadd_rn(s8, 0.0f);
-      if (!isfinite(tot)) {
-        // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
-        const uint8_t* srow = a.scale + (long long)(row / row_group) * a.scale_cols;
-        tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs);
-        if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
-      }
-      a.y[row - a.row_start] = a.addend ? __fadd_rn(tot, a.addend[row - a.row_start]) : tot;
-    }
-    pdl_launch_dependents();
-    return;
-  }
+  // the UE8M0 scale rows of the box (used by the chains at the end)
+  for (int i = threadIdx.x; i < nsrows * a.scale_cols; i += nthr)
+    scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
   pdl_wait_prior();
   // x: when no act-quant block straddles a 128-column group, each warp stages
   // (and act-quantises) only the groups it computes, so phase 1 starts without
@@ -526,16 +487,39 @@ __global__ void __launch_bounds__(kRgThreads)
       pd[0] = make_float4(p0.x, p0.y, p1.x, p1.y);
       pd[1] = make_float4(p2.x, p2.y, p3.x, p3.y);
     }
-    // the P_j stores of the warp before the arrival (which releases them to
-    // the chain warps); after a timed-out wait the arrivals still come, so no
-    // chain thread waits on a group that will never be computed
+    // release the slot after the warp's weight loads (after a timed-out wait
+    // the arrivals still come, so the producer never waits on a dead slot)
     __syncwarp();
-    if (lane == 0) {
-      if (ngroups > nstages) mbar_arrive(&empty[s]);
-      mbar_arrive(&pready[g]);
-    }
+    if (lane == 0 && ngroups > nstages) mbar_arrive(&empty[s]);
   }
-  pdl_launch_dependents();
+  // ---- the chains: acc_j = fma(P_j, scale_g, acc_j) over the groups in
+  // order, one consumer thread per (row, j), once every P_j is stored ----
+  const int ok_all = bar_and(1, nthr, ok);
+  const int t = threadIdx.x;
+  const int rr = t >> 3, j = t & 7;
+  const int row = row0 + rr;
+  const bool active = rr < box_rows && row < a.row_end;
+  const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
+  const float* pj = ps + rr * 8 + j;
+  float acc = 0.0f;
+  if (active && ok_all) {
+#pragma unroll 4
+    for (int g = 0; g < ngroups; ++g) acc = fmaf(pj[g * 256], decode_ue8m0(srow_s[g]), acc);
+  }
+  // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
+  const float s2 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+  const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
+  const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));
+  if (j == 0 && active && ok_all) {
+    float tot = __fadd_rn(s8, 0.0f);
+    if (!isfinite(tot)) {
+      // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
+      const uint8_t* srow = a.scale + (long long)(row / row_group) * a.scale_cols;
+      tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs);
+      if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
+    }
+    a.y[row - a.row_start] = a.addend ? __fadd_rn(tot, a.addend[row - a.row_start]) : tot;
+  }
 }
 
 static size_t fp8_scale_smem(int cols) { return size_t(32) * (cols / 128) + 16; }
