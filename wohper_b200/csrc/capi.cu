@@ -505,12 +505,12 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
   // the columns one input spans (grouped: every group's slice)
   const long long xspan =
       x_group_rows > 0 ? (long long)(rows / x_group_rows - 1) * x_group_off + cols : cols;
-  const bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
-                    ldx % 4 == 0 && x_group_off % 4 == 0 && cols <= 8192 &&
-                    (batch == 1 ? fp8_gemv_rg_smem_bytes(cols) <= 200 * 1024
-                                : act_quant_block == 0 ||
-                                      (xspan % act_quant_block == 0 &&
-                                       cols % act_quant_block == 0));
+  // act quant ahead of the kernel: blocks never straddle inputs or groups
+  const bool pre_aq_ok =
+      act_quant_block == 0 || (xspan % act_quant_block == 0 && cols % act_quant_block == 0);
+  bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
+              ldx % 4 == 0 && x_group_off % 4 == 0 && cols <= 8192;
+  bool in_kernel_aq = false;  // the one-input kernel quantises x itself
   if (fast) {
     const int nrows = row_end - row_start;
     const int tiles = batch == 1 ? 1 : (batch + 15) / 16;
@@ -523,6 +523,11 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
         --box_rows;
     }
     a.box_rows = box_rows;
+    in_kernel_aq = fp8_gemv_rowgroup_fits(a, c->num_sms);
+    if (act_quant_block > 0 && !in_kernel_aq && !pre_aq_ok) fast = false;
+  }
+  if (fast) {
+    const int box_rows = a.box_rows;
     auto key = std::make_tuple((const void*)weight, rows, cols, box_rows);
     auto it = c->fp8_maps.find(key);
     if (it == c->fp8_maps.end()) {
@@ -531,7 +536,7 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
       if (st != WH_OK) return st;
       it = c->fp8_maps.emplace(key, m).first;
     }
-    if (batch > 1 && act_quant_block > 0) {
+    if (act_quant_block > 0 && !in_kernel_aq) {
       // the batched kernel streams its inputs: quantise each input's span
       // beforehand (blocks never straddle inputs or groups)
       wh_status st = c->ensure_work(sizeof(float) * (size_t)batch * xspan);

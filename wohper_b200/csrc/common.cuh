@@ -122,8 +122,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
 
 // Producer drain before it leaves the kernel: a bounded wait that gives up at
 // once when a wait of this launch sequence has already timed out, so a failed
-// kernel returns after one timeout instead of one per ring stage.
+// kernel returns after one timeout instead of one per ring stage.  A copy that
+// has landed (the normal case: its consumer waited for it) returns without
+// reading the status word; that read goes to L2 and, once per ring stage,
+// would hold the CTA -- and the next kernel's dependency wait -- by
+// microseconds.
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t phase, uint32_t* status) {
+  if (mbar_try_wait(bar, phase)) return true;
   if (status && (*(volatile uint32_t*)status & WH_DEV_TIMEOUT)) return false;
   return mbar_wait(bar, phase, status);
 }
@@ -306,13 +311,16 @@ struct ActQuantTable {
   uint32_t thr[256];
 };
 
-__device__ __forceinline__ int ceil_log2f_ref(float q, const ActQuantTable* t) {
+__device__ __forceinline__ int ceil_log2f_thr(float q, const uint32_t* thr) {
   uint32_t u = __float_as_uint(q);
   uint32_t E = (u >> 23) & 0xFF;
   uint32_t m = u & 0x7FFFFF;
   int k = int(E) - 127;
-  if (m == 0 || m < t->thr[E]) return k;
+  if (m == 0 || m < thr[E]) return k;
   return k + 1;
+}
+__device__ __forceinline__ int ceil_log2f_ref(float q, const ActQuantTable* t) {
+  return ceil_log2f_thr(q, t->thr);
 }
 
 // scale = 2^k as float for k in the normal range (k >= -126 always holds here:
@@ -320,6 +328,28 @@ __device__ __forceinline__ int ceil_log2f_ref(float q, const ActQuantTable* t) {
 __device__ __forceinline__ float exp2i(int k) {
   if (k > 127) return __int_as_float(0x7f800000);
   return __uint_as_float(uint32_t(k + 127) << 23);
+}
+
+// The block scale 2^k of an act-quant block with the given amax, and 2^-k.
+// v / 2^k equals v * 2^-k bit for bit: both round the same real quotient
+// once, and 2^-k is a normal float for every k reachable (the 1e-4 amax floor
+// gives k >= -22, a finite amax k <= 120).  amax = inf gives k = 128, scale
+// inf and 2^-k = 0: v * 0 is the +-0 (NaN for +-inf) that v / inf is.
+struct AqScale {
+  float scale, inv;
+};
+__device__ __forceinline__ AqScale aq_block_scale(float amax, const uint32_t* thr) {
+  amax = fmaxf(amax, 1.0e-4f);
+  const int k = ceil_log2f_thr(__fdiv_rn(amax, 448.0f), thr);
+  return {exp2i(k), k > 126 ? 0.0f : exp2i(-k)};
+}
+__host__ __device__ __forceinline__ float e4m3_nearest_ties_lower(float t);
+// Quant-dequant of one value: nearest E4M3 of clamp(v / scale, +-448) times scale.
+__device__ __forceinline__ float aq_value(float v, AqScale s) {
+  float t = __fmul_rn(v, s.inv);
+  t = t < -448.0f ? -448.0f : t;
+  t = t > 448.0f ? 448.0f : t;
+  return __fmul_rn(e4m3_nearest_ties_lower(t), s.scale);
 }
 
 // Nearest E4M3 grid value of t (|t| <= 448 or NaN) with ties to the lower

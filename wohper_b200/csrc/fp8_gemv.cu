@@ -10,13 +10,14 @@
 // it is batch-invariant like the reference's rows_multi.
 //
 // Layout / data movement (fast path, col_group == 128):
-//   * one CTA per block of <= 32 rows (block size chosen so the grid covers
-//     the SMs once); a producer warp streams [rows x 128 B] boxes of W with TMA
-//     (SWIZZLE_128B) through an 8-stage mbarrier ring; the swizzle makes the
+//   * one CTA per box of <= 32 rows (box height chosen so the grid covers the
+//     SMs once); a producer warp streams [rows x 128 B] boxes of W with TMA
+//     (SWIZZLE_128B) through an mbarrier ring; the swizzle makes the
 //     consumers' row-per-lane reads bank-conflict free;
-//   * 4 lanes per row, each owning 4 of the 16 chains (4 bytes per 16-byte
-//     chunk), so a warp covers 8 rows; x sits in shared memory (optionally
-//     act-quantised in the prologue) and is read as broadcast float4s;
+//   * one input: fp8_gemv_rowgroup_kernel, a lane per row and a warp per
+//     column group, x staged (and act-quantised) in shared memory;
+//   * 2..N inputs: fp8_gemv_batch_kernel, the inputs streamed with the
+//     weights, 8 lanes per row, the decoded weights applied to 16 inputs;
 //   * E4M3 -> f16x2 by the hardware converter, f16 -> f32, fma.rn.f32x2.
 //     0x7F/0xFF (the reference's +-480, NaN for the hardware) make the row
 //     non-finite; such rows are recomputed with the exact bit decoder.
@@ -53,8 +54,14 @@ cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
   return e;
 }
 
+// the same thresholds in global memory, for kernels that stage them in shared
+// memory with one coalesced load (a constant-bank read with 256 distinct
+// indices per warp would serialise)
+__device__ ActQuantTable g_aq;
+
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s) {
   cudaMemcpyToSymbolAsync(c_aq, &t, sizeof(t), 0, cudaMemcpyHostToDevice, s);
+  cudaMemcpyToSymbolAsync(g_aq, &t, sizeof(t), 0, cudaMemcpyHostToDevice, s);
 }
 const ActQuantTable* act_quant_table_device() {
   void* p = nullptr;
@@ -71,15 +78,8 @@ __device__ void act_quant_smem_warp(float* v, int n, int block, int warp, int nw
     float amax = 0.0f;
     for (int i = b0 + lane; i < b1; i += 32) amax = fmaxf(amax, fabsf(v[i]));
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    amax = fmaxf(amax, 1.0e-4f);
-    float q = __fdiv_rn(amax, 448.0f);
-    float scale = exp2i(ceil_log2f_ref(q, tab));
-    for (int i = b0 + lane; i < b1; i += 32) {
-      float t = __fdiv_rn(v[i], scale);
-      t = t < -448.0f ? -448.0f : t;
-      t = t > 448.0f ? 448.0f : t;
-      v[i] = __fmul_rn(e4m3_nearest_ties_lower(t), scale);
-    }
+    const AqScale sc = aq_block_scale(amax, tab->thr);
+    for (int i = b0 + lane; i < b1; i += 32) v[i] = aq_value(v[i], sc);
   }
 }
 
@@ -94,22 +94,19 @@ __global__ void act_quant_kernel(float* v, long long n, int block, uint32_t* sta
     float amax = 0.0f;
     for (long long i = b0 + lane; i < b1; i += 32) amax = fmaxf(amax, fabsf(v[i]));
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    amax = fmaxf(amax, 1.0e-4f);
-    float scale = exp2i(ceil_log2f_ref(__fdiv_rn(amax, 448.0f), &c_aq));
-    for (long long i = b0 + lane; i < b1; i += 32) {
-      float t = __fdiv_rn(v[i], scale);
-      t = t < -448.0f ? -448.0f : t;
-      t = t > 448.0f ? 448.0f : t;
-      v[i] = __fmul_rn(e4m3_nearest_ties_lower(t), scale);
-    }
+    const AqScale sc = aq_block_scale(amax, c_aq.thr);
+    for (long long i = b0 + lane; i < b1; i += 32) v[i] = aq_value(v[i], sc);
   }
   pdl_launch_dependents();
 }
 
 // Exact scalar restatement of fp8_ue8m0_dot_row_avx2 for one (row, input),
 // used by the generic kernel and for the rare non-finite recompute.
+// x_pad: floats of padding after every 8 groups of x (the one-input kernel's
+// shared-memory layout), 0 for a plain vector.
 __device__ float fp8_row_dot_exact(const uint8_t* __restrict__ w, const uint8_t* __restrict__ srow,
-                                   int scale_cols, int col_group, const float* __restrict__ x) {
+                                   int scale_cols, int col_group, const float* __restrict__ x,
+                                   int x_pad = 0) {
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
@@ -118,7 +115,7 @@ __device__ float fp8_row_dot_exact(const uint8_t* __restrict__ w, const uint8_t*
   for (int g = 0; g < scale_cols; ++g) {
     float scale = decode_ue8m0(srow[g]);
     const uint8_t* bytes = w + (long long)g * col_group;
-    const float* cols = x + (long long)g * col_group;
+    const float* cols = x + (long long)g * col_group + (g >> 3) * x_pad;
     float g0[8], g1[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) g0[j] = g1[j] = 0.0f;
@@ -164,8 +161,6 @@ __global__ void fp8_gemv_generic_kernel(Fp8GemvArgs a) {
 // ---------------------------------------------------------------------------
 // Fast path
 // ---------------------------------------------------------------------------
-constexpr int kFp8StageBytes = 32 * 128;  // up to 32 rows x 128 B, 1024-aligned
-constexpr int kFp8MaxStages = 48;
 constexpr size_t kFp8SmemBudget = 200 * 1024;
 
 
@@ -174,8 +169,8 @@ constexpr size_t kFp8SmemBudget = 200 * 1024;
 // stage holds one 128-column group: the weight box [32 rows][128 B] (TMA) and
 // the group's 128 columns of each of the tile's TB inputs (one 512-byte bulk
 // copy per input), so nothing is staged before the first group and a CTA
-// holds 4 stages.  Lane mapping as fp8_gemv_tma_kernel (8 lanes per row, lane
-// q the chains 2(q&3), 2(q&3)+1 of g0 or g1); the row's weights of a group
+// holds 4 stages.  8 lanes per row, lane q holding the chains 2(q&3),
+// 2(q&3)+1 of g0 (q < 4) or g1 (q >= 4); the row's weights of a group
 // are decoded once and applied to the TB inputs.  Inputs are act-quantised
 // beforehand when the call asks for it.
 // ---------------------------------------------------------------------------
@@ -205,6 +200,9 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
   const int tile = blockIdx.y;
   const int tb = min(kFbTB, a.batch - tile * kFbTB);
   const float* xbase = fp8_x_rows(a, row0) + (long long)tile * kFbTB * a.ldx;
+  // the next kernel may start its weight stream now (it waits for this grid
+  // before reading y)
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFbStages; ++s) {
@@ -218,14 +216,22 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
   if (warp == 8) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
+      // the first stages' weights do not depend on the previous kernel
+      const int pre = min(ngroups, kFbStages);
+      for (int g = 0; g < pre; ++g) {
+        mbar_arrive_expect_tx(&full[g], box_rows * 128 + tb * 512);
+        tma_load_2d(stages + g * kFbStageBytes, &wmap, &full[g], g * 128, row0);
+      }
       pdl_wait_prior();  // the inputs may come from the previous kernel
       int g = 0;
       for (; g < ngroups; ++g) {
         const int s = g % kFbStages;
-        if (g >= kFbStages && !mbar_wait(&empty[s], ((g / kFbStages) - 1) & 1, a.status)) break;
         uint8_t* st = stages + s * kFbStageBytes;
-        mbar_arrive_expect_tx(&full[s], box_rows * 128 + tb * 512);
-        tma_load_2d(st, &wmap, &full[s], g * 128, row0);
+        if (g >= pre) {
+          if (!mbar_wait(&empty[s], ((g / kFbStages) - 1) & 1, a.status)) break;
+          mbar_arrive_expect_tx(&full[s], box_rows * 128 + tb * 512);
+          tma_load_2d(st, &wmap, &full[s], g * 128, row0);
+        }
         for (int b = 0; b < tb; ++b)
           bulk_load(st + 4096 + b * 512, xbase + (long long)b * a.ldx + g * 128, 512, &full[s]);
       }
@@ -310,63 +316,130 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
       }
     }
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
-// One-input fast path: lane = row, warp = column group.
+// One-input fast path: lanes = rows, warps = column groups.
 //
 // The reference's g0/g1 chains restart at every 128-column group, so a
 // (row, group) pair is an independent unit of 16 chains x 8 FMAs; only
 // acc_j = fma(P_j, scale_g, acc_j) runs across the groups.  Phase 1 gives each
-// lane one row of the tile and each warp a column group: the lane runs all 16
-// chains of its (row, group) with the group's x read as shared-memory
-// broadcasts and its weight row read as 16-byte words (bank-conflict free
-// under the 128-byte swizzle), and stores P_j = g0_j + g1_j.  Eight chain
-// warps give each (row, j) a thread that runs the acc_j chain over the groups
-// in order, each group as soon as its P_j are stored (one mbarrier per group),
-// so the chain runs under the weight stream; then the pairwise 8-lane sum.
-// Same arithmetic as fp8_gemv_tma_kernel.
+// warp every 8th column group and each lane one (row, group) pair of the
+// CTA's box of rows: the lane runs all 16 chains with the group's x read as
+// shared-memory broadcasts and its weight row read as 16-byte words
+// (bank-conflict free under the 128-byte swizzle), and stores
+// P_j = g0_j + g1_j.  A box of R <= 16 rows puts 32/R groups side by side in
+// the warp (R rounded up to a power of two), so short boxes keep the lanes
+// busy.  After a barrier each (row, j) thread runs its acc_j chain over the
+// groups in order, then the pairwise 8-lane sum.
+//
+// Each group has its own full barrier, so a consumer waits for exactly its
+// group's copy whatever order the copies land in (ring slots are reused by
+// groups that other warps consume).
+//
+// At decode sizes latency, not arithmetic, bounds this kernel, so:
+//   * a ring slot is the box rounded up to 1 KiB (the 128-byte swizzle repeats
+//     every 1 KiB), so a short box keeps more groups in flight.  The ring is
+//     sized for two CTAs per SM when that leaves at least 8 slots (the next
+//     kernel's CTAs then issue their weight loads while this one finishes),
+//     else one CTA per SM takes a deeper ring;
+//   * weights, scales and the act-quant thresholds do not depend on the
+//     previous kernel: they are requested before the programmatic-dependency
+//     wait, x after it;
+//   * x is act-quantised in registers as it is loaded: a block of 4L values
+//     spans L lanes of the warp, and a warp quantises 4 groups at once.
+// Shared-memory x is padded by 4 floats after every 8 groups, so the groups a
+// quarter-warp reads side by side (8 apart) sit in different banks.
 // ---------------------------------------------------------------------------
 constexpr int kRgConsumers = 8;   // phase-1 warps
-constexpr int kRgRing = 12;       // weight stages in flight per CTA
 constexpr int kRgMaxGroups = 64;  // cols <= 8192
+constexpr int kRgXBatch = 4;      // x float4s a lane loads at once
 constexpr int kRgThreads = 32 * (kRgConsumers + 1);
+constexpr long long kRgTwoPerSm = 112 * 1024;  // dynamic smem per CTA with two CTAs per SM
+constexpr int kRgMinRing = 8;
+constexpr int kRgMaxRing = 64;
+constexpr int kRgXPad = 4;
 
-static int fp8_rg_stages(int cols) {
-  const int ngroups = cols / 128;
-  if (ngroups > kRgMaxGroups) return 0;
-  long long room = (long long)kFp8SmemBudget - 1024 - (long long)cols * 4 -
-                   (long long)ngroups * 32 * 8 * 4 - (2 * kFp8MaxStages + kRgMaxGroups) * 8 -
-                   (32LL * ngroups + 16);
-  int ns = (int)std::max(0LL, room / kFp8StageBytes);
-  return std::min({ns, kRgRing, ngroups});
+__host__ __device__ constexpr int fp8_rg_slot(int box_rows) {
+  return ((box_rows * 128 + 1023) / 1024) * 1024;
+}
+__host__ __device__ constexpr int fp8_rg_xs_len(int ngroups) {
+  return ngroups * 128 + ((ngroups + 7) / 8) * kRgXPad;
+}
+__host__ __device__ constexpr int fp8_rg_lane_rows(int box_rows) {  // power of two >= box_rows
+  return box_rows <= 1 ? 1 : box_rows <= 2 ? 2 : box_rows <= 4 ? 4 : box_rows <= 8 ? 8
+       : box_rows <= 16 ? 16 : 32;
 }
 
-size_t fp8_gemv_rg_smem_bytes(int cols) {
-  const int ns = fp8_rg_stages(cols);
-  if (ns < 4) return size_t(1) << 30;
-  const int ngroups = cols / 128;
-  return 1024 + size_t(ns) * kFp8StageBytes +
-         (2 * kFp8MaxStages + kRgMaxGroups) * sizeof(uint64_t) + size_t(cols) * sizeof(float) +
-         size_t(ngroups) * 32 * 8 * sizeof(float) + size_t(32) * ngroups + 16;
+// bytes besides the ring: alignment pad, barriers, x, P, thresholds, scale rows
+static long long fp8_rg_fixed(int ngroups, int box_rows) {
+  return 1024 + 2LL * kRgMaxGroups * 8 + 4LL * fp8_rg_xs_len(ngroups) +
+         4LL * ngroups * box_rows * 8 + 256 * 4 + 32LL * ngroups + 16;
 }
 
-__global__ void __launch_bounds__(kRgThreads)
+struct RgPlan {
+  int ns;  // ring slots
+  size_t smem;
+};
+
+static bool fp8_rg_plan(const Fp8GemvArgs& a, RgPlan* p) {
+  const int ngroups = a.scale_cols, box = a.box_rows, aqb = a.act_quant_block;
+  if (a.batch != 1 || a.ldx < a.cols || ngroups < 1 || ngroups > kRgMaxGroups ||
+      a.cols != ngroups * 128 || box < 1 || box > 32)
+    return false;
+  if (aqb != 0 && (aqb < 4 || 128 % aqb != 0)) return false;  // quantised in registers
+  const long long fixed = fp8_rg_fixed(ngroups, box);
+  const int slot = fp8_rg_slot(box);
+  // A warp waits for its 32/R side-by-side groups together before it frees
+  // their slots, so the ring must hold one such pass of every warp: with
+  // fewer slots a pass could wait for a copy that only a later pass frees.
+  const int need = std::min(ngroups, kRgConsumers * (32 / fp8_rg_lane_rows(box)));
+  const int two = (int)std::max(0LL, (kRgTwoPerSm - fixed) / slot);
+  int ns = std::min(two, ngroups);
+  if (two < std::max(need, std::min(ngroups, kRgMinRing)))
+    ns = std::min((int)std::max(0LL, ((long long)kFp8SmemBudget - fixed) / slot), ngroups);
+  ns = std::min(ns, kRgMaxRing);
+  if (ns < std::max(need, std::min(ngroups, 4))) return false;
+  p->ns = ns;
+  p->smem = (size_t)(fixed + (long long)ns * slot);
+  return true;
+}
+
+bool fp8_gemv_rowgroup_fits(const Fp8GemvArgs& a, int) {
+  RgPlan p;
+  return fp8_rg_plan(a, &p);
+}
+
+// Act quant-dequant of the float4 `v` a lane holds, in blocks of 4 * lanes
+// values over aligned groups of `lanes` lanes (lanes a power of two <= 32).
+__device__ __forceinline__ float4 act_quant_lanes(float4 v, int lanes, const uint32_t* thr) {
+  // max|v| ignoring NaN (as the reference's f32::max): a NaN operand of fmaxf
+  // yields the other one, and the 1e-4 floor comes after
+  float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  for (int o = lanes >> 1; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const AqScale sc = aq_block_scale(m, thr);
+  return make_float4(aq_value(v.x, sc), aq_value(v.y, sc), aq_value(v.z, sc), aq_value(v.w, sc));
+}
+
+// R: the box height rounded up to a power of two (lanes per group)
+template <int R>
+__global__ void __launch_bounds__(kRgThreads, 4)
     fp8_gemv_rowgroup_kernel(const __grid_constant__ CUtensorMap wmap, Fp8GemvArgs a,
                              int nstages) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
+  const int box_rows = a.box_rows;
+  const int slot = fp8_rg_slot(box_rows);
+  const int ngroups = a.scale_cols;  // col_group == 128
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * kFp8StageBytes);
-  uint64_t* empty = full + kFp8MaxStages;
-  float* xs = reinterpret_cast<float*>(empty + kFp8MaxStages + kRgMaxGroups);  // cols
-  const int ngroups = a.scale_cols;                               // col_group == 128
-  float* ps = xs + a.cols;                                        // [ngroups][32][8]
-  uint8_t* scale_s = reinterpret_cast<uint8_t*>(ps + ngroups * 32 * 8);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nstages * slot);  // [group]
+  uint64_t* empty = full + kRgMaxGroups;                                 // [ring slot]
+  float* xs = reinterpret_cast<float*>(empty + kRgMaxGroups);            // padded x
+  float* ps = xs + fp8_rg_xs_len(ngroups);                               // [group][row][8]
+  uint32_t* thr_s = reinterpret_cast<uint32_t*>(ps + ngroups * box_rows * 8);  // 256
+  uint8_t* scale_s = reinterpret_cast<uint8_t*>(thr_s + 256);  // the box's scale rows
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int box_rows = a.box_rows;
   const int row0 = a.row_start + blockIdx.x * box_rows;
   // the next kernel in the stream may start now: it streams its own weights
   // while this one finishes (it waits for this grid before reading results)
@@ -376,97 +449,98 @@ __global__ void __launch_bounds__(kRgThreads)
   // other delays the first TMA issue by about a microsecond
   {
     const int t = threadIdx.x;
-    const bool ring = ngroups > nstages;  // empty barriers only when slots are reused
-    if (t < nstages) mbar_init(&full[t], 1);
-    else if (t < 2 * kFp8MaxStages && t - kFp8MaxStages < nstages && ring)
-      mbar_init(&empty[t - kFp8MaxStages], 1);  // one warp consumes each group
-    if (t < 2 * kFp8MaxStages) fence_barrier_init();
+    if (t < ngroups) mbar_init(&full[t], 1);
+    else if (t >= kRgMaxGroups && t - kRgMaxGroups < nstages)
+      mbar_init(&empty[t - kRgMaxGroups], 1);  // the lane group that read the slot
+    if (t < 2 * kRgMaxGroups) fence_barrier_init();
   }
   __syncthreads();
 
   if (warp == kRgConsumers) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
+      // slot and phase advance without a division: the producer's turn
+      // between a freed slot and the next copy is on the stream's critical path
       int g = 0, s = 0;
       uint32_t phase = 0;
       for (; g < ngroups; ++g) {
         if (g >= nstages && !mbar_wait(&empty[s], phase, a.status)) break;
-        mbar_arrive_expect_tx(&full[s], box_rows * 128);
-        tma_load_2d(stages + s * kFp8StageBytes, &wmap, &full[s], g * 128, row0);
+        mbar_arrive_expect_tx(&full[g], box_rows * 128);
+        tma_load_2d(stages + s * slot, &wmap, &full[g], g * 128, row0);
         if (++s == nstages) {
           s = 0;
           if (g >= nstages) phase ^= 1u;
         }
       }
+      // the copies still in flight land before the CTA leaves
       for (int i = max(0, g - nstages); i < g; ++i)
-        if (!mbar_drain(&full[i % nstages], (i / nstages) & 1, a.status)) break;
+        if (!mbar_drain(&full[i], 0, a.status)) break;
     }
     return;
   }
 
   constexpr int nthr = kRgConsumers * 32;
+  const int t = threadIdx.x;
+  const int aqb = a.act_quant_block;
   const int row_group = a.rows / a.scale_rows;
-  const int last_row = min(row0 + box_rows, a.row_end) - 1;
   const int srow0 = row0 / row_group;
-  const int nsrows = last_row / row_group - srow0 + 1;
-  // the UE8M0 scale rows of the box (used by the chains at the end)
-  for (int i = threadIdx.x; i < nsrows * a.scale_cols; i += nthr)
-    scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
-  pdl_wait_prior();
-  // x: when no act-quant block straddles a 128-column group, each warp stages
-  // (and act-quantises) only the groups it computes, so phase 1 starts without
-  // a CTA-wide barrier and the x loads overlap the weight stream
-  const float4* x4 = reinterpret_cast<const float4*>(fp8_x_rows(a, row0));
-  float4* xs4 = reinterpret_cast<float4*>(xs);
-  const bool own_x = a.act_quant_block == 0 || 128 % a.act_quant_block == 0;
-  if (own_x) {
-    for (int g0 = warp; g0 < ngroups; g0 += 4 * kRgConsumers) {
-      float4 v[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (g0 + k * kRgConsumers < ngroups) v[k] = __ldg(x4 + (g0 + k * kRgConsumers) * 32 + lane);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (g0 + k * kRgConsumers < ngroups) xs4[(g0 + k * kRgConsumers) * 32 + lane] = v[k];
-    }
-  } else {
-    const int n4 = a.cols / 4;
-    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * nthr) {
-      float4 v[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (i0 + k * nthr < n4) v[k] = __ldg(x4 + i0 + k * nthr);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (i0 + k * nthr < n4) xs4[i0 + k * nthr] = v[k];
-    }
+  // constant inputs first: the act-quant thresholds (one per thread) and the
+  // UE8M0 scale rows of the box (read by the chains)
+  const uint32_t thr_v = aqb > 0 ? __ldg(&g_aq.thr[t]) : 0u;
+  {
+    const int nsr = (min(row0 + box_rows, a.row_end) - 1) / row_group - srow0 + 1;
+    for (int i = t; i < nsr * ngroups; i += nthr)
+      scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
   }
-  if (own_x) {
-    __syncwarp();
-    if (a.act_quant_block > 0) {
-      for (int g = warp; g < ngroups; g += kRgConsumers)
-        act_quant_smem_warp(xs + g * 128, 128, a.act_quant_block, 0, 1, lane, &c_aq);
-      __syncwarp();
+  pdl_wait_prior();
+
+  // ---- x: each warp stages (and act-quantises) only the groups it computes ----
+  const int jw = (ngroups - warp + kRgConsumers - 1) / kRgConsumers;  // this warp's groups
+  {
+    const float4* x4 = reinterpret_cast<const float4*>(fp8_x_rows(a, row0));
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    for (int j0 = 0; j0 < kRgMaxGroups / kRgConsumers; j0 += kRgXBatch) {
+      if (j0 > 0 && j0 >= jw) break;  // the first batch runs in every warp (barrier)
+      float4 v[kRgXBatch];
+#pragma unroll
+      for (int u = 0; u < kRgXBatch; ++u)
+        if (j0 + u < jw) v[u] = __ldg(x4 + (warp + kRgConsumers * (j0 + u)) * 32 + lane);
+      if (j0 == 0 && aqb > 0) {
+        thr_s[t] = thr_v;
+        asm volatile("bar.sync 2, %0;" ::"r"(nthr) : "memory");
+      }
+#pragma unroll
+      for (int u = 0; u < kRgXBatch; ++u) {
+        const int g = warp + kRgConsumers * (j0 + u);
+        if (j0 + u < jw) {
+          if (aqb > 0) v[u] = act_quant_lanes(v[u], aqb / 4, thr_s);
+          xs4[(g * 128 + (g >> 3) * kRgXPad) / 4 + lane] = v[u];
+        }
+      }
     }
-  } else {
-    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
-    act_quant_smem_warp(xs, a.cols, a.act_quant_block, warp, kRgConsumers, lane, &c_aq);
-    asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+    __syncwarp();
   }
 
-  // ---- phase 1: P_j of (row = lane, group) ----
+  // ---- phase 1: P_j of (row r, group g) ----
+  constexpr int gpw = 32 / R;  // groups side by side in a warp
+  const int r = lane & (R - 1), q = lane / R;
   bool ok = true;
-  const int r = lane;
-  const bool has_row = r < box_rows;
-  for (int g = warp; g < ngroups; g += kRgConsumers) {
+  for (int j0 = 0; j0 < jw; j0 += gpw) {
+    const int j = j0 + q;
+    const bool has_g = j < jw;
+    const int g = warp + kRgConsumers * j;
     const int s = g % nstages;
-    ok = ok && mbar_wait(&full[s], (uint32_t)((g / nstages) & 1), a.status);
-    if (ok && has_row) {
-      const uint8_t* wrow = stages + s * kFp8StageBytes + r * 128;
-      const float4* xg = reinterpret_cast<const float4*>(xs + g * 128);
+    bool landed = false;
+    if (has_g) {
+      ok = ok && mbar_wait(&full[g], 0, a.status);
+      landed = ok;
+    }
+    if (landed && r < box_rows) {
+      const uint8_t* wrow = stages + s * slot + r * 128;
+      const float4* xg = reinterpret_cast<const float4*>(xs + g * 128 + (g >> 3) * kRgXPad);
       float2 g0[4], g1[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) g0[k] = g1[k] = make_float2(0.0f, 0.0f);
+      for (int u = 0; u < 4; ++u) g0[u] = g1[u] = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 w = *reinterpret_cast<const uint4*>(wrow + 16 * (c ^ (r & 7)));
@@ -481,49 +555,48 @@ __global__ void __launch_bounds__(kRgThreads)
         g1[2] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.w)), make_float2(x3.x, x3.y), g1[2]);
         g1[3] = ffma2(h2_to_f2(e4m3x2_to_f16x2(w.w >> 16)), make_float2(x3.z, x3.w), g1[3]);
       }
-      float4* pd = reinterpret_cast<float4*>(ps + (g * 32 + r) * 8);
+      float4* pd = reinterpret_cast<float4*>(ps + (g * box_rows + r) * 8);
       const float2 p0 = fadd2(g0[0], g1[0]), p1 = fadd2(g0[1], g1[1]);
       const float2 p2 = fadd2(g0[2], g1[2]), p3 = fadd2(g0[3], g1[3]);
       pd[0] = make_float4(p0.x, p0.y, p1.x, p1.y);
       pd[1] = make_float4(p2.x, p2.y, p3.x, p3.y);
     }
-    // release the slot after the warp's weight loads (after a timed-out wait
-    // the arrivals still come, so the producer never waits on a dead slot)
+    // release the slot once the group's lanes have read it (after a timed-out
+    // wait the arrivals still come, so the producer never waits on a dead slot)
     __syncwarp();
-    if (lane == 0 && ngroups > nstages) mbar_arrive(&empty[s]);
+    if (has_g && r == 0) mbar_arrive(&empty[s]);
   }
+
   // ---- the chains: acc_j = fma(P_j, scale_g, acc_j) over the groups in
   // order, one consumer thread per (row, j), once every P_j is stored ----
   const int ok_all = bar_and(1, nthr, ok);
-  const int t = threadIdx.x;
-  const int rr = t >> 3, j = t & 7;
+  const int rr = t >> 3, j8 = t & 7;
   const int row = row0 + rr;
   const bool active = rr < box_rows && row < a.row_end;
-  const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
-  const float* pj = ps + rr * 8 + j;
+  const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * ngroups;
+  const float* pj = ps + rr * 8 + j8;
+  const int pstride = box_rows * 8;
   float acc = 0.0f;
   if (active && ok_all) {
 #pragma unroll 4
-    for (int g = 0; g < ngroups; ++g) acc = fmaf(pj[g * 256], decode_ue8m0(srow_s[g]), acc);
+    for (int g = 0; g < ngroups; ++g) acc = fmaf(pj[g * pstride], decode_ue8m0(srow_s[g]), acc);
   }
   // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
   const float s2 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
   const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
   const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));
-  if (j == 0 && active && ok_all) {
+  if (j8 == 0 && active && ok_all) {
     float tot = __fadd_rn(s8, 0.0f);
     if (!isfinite(tot)) {
       // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
       const uint8_t* srow = a.scale + (long long)(row / row_group) * a.scale_cols;
-      tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs);
+      tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128, xs,
+                              kRgXPad);
       if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
     }
     a.y[row - a.row_start] = a.addend ? __fadd_rn(tot, a.addend[row - a.row_start]) : tot;
   }
 }
-
-static size_t fp8_scale_smem(int cols) { return size_t(32) * (cols / 128) + 16; }
-
 
 cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
                             cudaStream_t stream, bool pdl) {
@@ -542,14 +615,23 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
     return cudaLaunchKernelEx(&cfg, fp8_gemv_generic_kernel, a);
   }
   const int nrows = a.row_end - a.row_start;
-  if (a.batch == 1 && a.ldx >= a.cols && fp8_gemv_rg_smem_bytes(a.cols) <= kFp8SmemBudget + 1024) {
-    const int ns = fp8_rg_stages(a.cols);
+  RgPlan p;
+  if (fp8_rg_plan(a, &p)) {
     cfg.blockDim = dim3(kRgThreads);
     cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows);
-    cfg.dynamicSmemBytes = fp8_gemv_rg_smem_bytes(a.cols);
-    cudaError_t e = ensure_smem(fp8_gemv_rowgroup_kernel, cfg.dynamicSmemBytes);
+    cfg.dynamicSmemBytes = p.smem;
+    auto* kern = fp8_gemv_rowgroup_kernel<32>;
+    switch (fp8_rg_lane_rows(a.box_rows)) {
+      case 1:
+      case 2:
+      case 4: kern = fp8_gemv_rowgroup_kernel<4>; break;
+      case 8: kern = fp8_gemv_rowgroup_kernel<8>; break;
+      case 16: kern = fp8_gemv_rowgroup_kernel<16>; break;
+      default: break;
+    }
+    cudaError_t e = ensure_smem(kern, cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return e;
-    return cudaLaunchKernelEx(&cfg, fp8_gemv_rowgroup_kernel, *wmap, a, ns);
+    return cudaLaunchKernelEx(&cfg, kern, *wmap, a, p.ns);
   }
   // 2..N inputs: the streaming batched kernel, kFbTB inputs per CTA
   cfg.blockDim = dim3(kFbThreads);

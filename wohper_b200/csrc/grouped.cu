@@ -127,13 +127,6 @@ __device__ __forceinline__ void convert_tiles(const uint8_t* raw, int raw_stride
     }
 }
 
-// ceil(log2f(q)) through the act-quant threshold table (shared-memory copy)
-__device__ __forceinline__ int ceil_log2f_thr(float q, const uint32_t* thr) {
-  const uint32_t u = __float_as_uint(q);
-  const uint32_t E = (u >> 23) & 0xFF, m = u & 0x7FFFFF;
-  const int k = int(E) - 127;
-  return (m == 0 || m < thr[E]) ? k : k + 1;
-}
 // word k of a 16-byte group without local memory
 __device__ __forceinline__ uint32_t pick4(const uint4& v, int k) {
   return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;

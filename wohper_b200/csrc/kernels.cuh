@@ -166,6 +166,8 @@ struct Fp8GemvArgs {
 
 void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);
 const ActQuantTable* act_quant_table_device();
+// true when the one-input kernel takes the call (it then act-quantises x itself)
+bool fp8_gemv_rowgroup_fits(const Fp8GemvArgs& a, int num_sms);
 // wmap == nullptr selects the generic kernel.
 cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
                             cudaStream_t stream, bool pdl);
