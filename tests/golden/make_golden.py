@@ -259,7 +259,62 @@ def build_numpy_tool(reference: Path) -> dict:
             vecs.append({"block": block, "x": [int(v) for v in x.view(np.uint32)],
                          "y": [int(v) for v in y.astype(np.float32).view(np.uint32)]})
     out["act_quant"] = vecs
+    out.update(build_numpy_tool_matvecs(tool))
     return out
+
+
+def build_numpy_tool_matvecs(tool) -> dict:
+    """The tool's own FP8 matvec (fp8_matvec, over a core file it reads),
+    FP4 matvec (fp4_matvec_from_records) and FP4 expert forward
+    (fp4_expert_forward) on the seeded inputs of numpy_tool_inputs.py.  The
+    tool act-quantises each input in blocks of 128 and sums each 128-column
+    block with BLAS; the oracle test feeds the oracle the same act-quantised
+    input and compares within a tolerance that absorbs the summation order."""
+    import tempfile
+
+    sys.path.insert(0, str(HERE))
+    import numpy_tool_inputs as NI  # noqa: E402
+
+    def u32(a) -> list:
+        return [int(v) for v in np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)]
+
+    res: dict = {}
+    # FP8: the tool reads the weight rows and the scale grid from a core file
+    w, s, x = NI.fp8_matvec_case()
+    rows, cols = w.shape
+    with tempfile.TemporaryDirectory() as d:
+        core = Path(d) / "core.bin"
+        core.write_bytes(w.tobytes() + s.tobytes())
+        tensors = {
+            "m.weight": {"shape": [rows, cols], "absolute_data_offset": 0, "data_bytes": w.size},
+            "m.scale": {"shape": list(s.shape), "absolute_data_offset": w.size,
+                        "data_bytes": s.size},
+        }
+        y, _ = tool.fp8_matvec(core, tensors, "m.weight", x)
+    res["fp8_matvec"] = {"seed": 8101, "rows": rows, "cols": cols, "act_quant_block": 128,
+                         "y": u32(y)}
+
+    def records(mats: dict) -> dict:
+        rec = {}
+        for name, (packed, scale) in mats.items():
+            rec[f"{name}.weight"] = {"shape": list(packed.shape),
+                                     "payload": memoryview(packed.tobytes())}
+            rec[f"{name}.scale"] = {"shape": list(scale.shape),
+                                    "payload": memoryview(scale.tobytes())}
+        return rec
+
+    packed, s4, x4 = NI.fp4_matvec_case()
+    rows4, cols4 = packed.shape[0], packed.shape[1] * 2
+    y4 = tool.fp4_matvec_from_records(records({"e.w1": (packed, s4)}), ".w1.weight",
+                                      (rows4, cols4), x4)
+    res["fp4_matvec"] = {"seed": 4101, "rows": rows4, "cols": cols4, "group": 32,
+                         "act_quant_block": 128, "y": u32(y4)}
+
+    m1, m3, m2, xe = NI.fp4_expert_case()
+    ye = tool.fp4_expert_forward(records({"e.w1": m1, "e.w3": m3, "e.w2": m2}), xe)
+    res["fp4_expert"] = {"seed": 4201, "hidden": 4096, "inter": 2048, "group": 32,
+                         "act_quant_block": 128, "swiglu_limit": 10.0, "y": u32(ye)}
+    return res
 
 
 def main() -> None:

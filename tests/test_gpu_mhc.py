@@ -71,7 +71,7 @@ def _check_pre_post(W, ctx, hc, hidden, T, seed, x=None, iters=20):
     return y
 
 
-@pytest.mark.parametrize("T", [1, 3, 16])
+@pytest.mark.parametrize("T", [1, 3, 16, 40])
 def test_hc_pre_post_v4_shape_bit_exact(ctx, W, T):
     _check_pre_post(W, ctx, 4, 4096, T, 10 + T)
 
@@ -90,7 +90,7 @@ def test_hc_pre_nan_input(ctx, W):
     _check_pre_post(W, ctx, hc, hidden, 1, 7, x=x)
 
 
-@pytest.mark.parametrize("hc,hidden,T", [(4, 4096, 2), (3, 11, 1)])
+@pytest.mark.parametrize("hc,hidden,T", [(4, 4096, 2), (3, 11, 1), (4, 256, 33)])
 def test_hc_head_bit_exact(ctx, W, hc, hidden, T):
     fn, _, base = _params(21, hc, hidden, rows=hc)
     x = np.random.default_rng(22).standard_normal((T, hc * hidden)).astype(np.float32)

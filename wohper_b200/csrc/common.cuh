@@ -193,7 +193,7 @@ __device__ __forceinline__ int bar_and(int id, int nthreads, int pred) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA / bulk copies (no .multicast::cluster anywhere in this project)
+// TMA / bulk copies (plain loads only: no cluster-multicast form anywhere here)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
