@@ -108,21 +108,21 @@ __device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* p, uint32_t v) 
 // min of the expert id among the lanes holding it), which is the order of the
 // reference's stable descending sort.  Ordered sums (the reference adds left
 // to right) gather their terms with independent shuffles first.
-template <int PER>
+// ld(sc): loads the logits of experts i*32 + lane (i < PER) into sc, all in
+// flight together; entries past the last expert are cleared below.
+template <int PER, class Ld>
 __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int t, int lane,
-                                                        bool dry = false) {
+                                                        bool dry, Ld ld) {
   constexpr unsigned kFull = 0xffffffffu;
-  const float* L = a.logits + (long long)t * a.experts;
   const bool biased = a.mode == 1 && a.bias != nullptr;
   float sc[PER];
   int32_t key[PER];
   uint32_t avail = 0;  // bit i: candidate i exists and is not selected yet
-  // every load first, so that they are in flight together
+  ld(sc);
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    const int ex = i * 32 + lane;
-    const bool in = ex < a.experts;
-    sc[i] = in ? __ldcg(L + ex) : 0.0f;
+    const bool in = i * 32 + lane < a.experts;
+    if (!in) sc[i] = 0.0f;
     avail |= uint32_t(in) << i;
   }
   if (a.mode == 1) {
@@ -238,6 +238,17 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
   if (lane == 0) a.counters[t] = 0;  // ready for the next call
 }
 
+// Candidate logits of token t from global memory: every load is issued before
+// the first is used (indices clamped to the last expert; the top-k clears the
+// entries past it).
+template <int PER>
+__device__ __forceinline__ void router_load_global(const RouterArgs& a, int t, int lane,
+                                                   float (&sc)[PER]) {
+  const float* L = a.logits + (long long)t * a.experts;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) sc[i] = __ldcg(L + min(i * 32 + lane, a.experts - 1));
+}
+
 // The top-k runs once per token, in one warp of the last CTA, usually on code
 // that is in no cache (the weights streamed since the last call evict it).
 // A third warp of every CTA runs it once "dry" (no stores; logits of an
@@ -245,12 +256,13 @@ __device__ __forceinline__ void router_topk_and_weights(const RouterArgs& a, int
 // compute the logits, so that the last CTA's real pass fetches its
 // instructions on chip (not inlined: both passes run the same code).
 __device__ __noinline__ void router_topk_any(const RouterArgs& a, int t, int lane, bool dry) {
-  if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane, dry);
-  else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane, dry);
-  else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane, dry);
-  else if (a.experts <= 256) router_topk_and_weights<8>(a, t, lane, dry);
-  else if (a.experts <= 512) router_topk_and_weights<16>(a, t, lane, dry);
-  else router_topk_and_weights<32>(a, t, lane, dry);
+  auto ld = [&](auto& sc) { router_load_global(a, t, lane, sc); };
+  if (a.experts <= 32) router_topk_and_weights<1>(a, t, lane, dry, ld);
+  else if (a.experts <= 64) router_topk_and_weights<2>(a, t, lane, dry, ld);
+  else if (a.experts <= 128) router_topk_and_weights<4>(a, t, lane, dry, ld);
+  else if (a.experts <= 256) router_topk_and_weights<8>(a, t, lane, dry, ld);
+  else if (a.experts <= 512) router_topk_and_weights<16>(a, t, lane, dry, ld);
+  else router_topk_and_weights<32>(a, t, lane, dry, ld);
 }
 
 // kSmem: rows and x staged in shared memory (hidden % 8 == 0, 16-byte aligned
@@ -1029,7 +1041,9 @@ template <int PER>
 __global__ void __launch_bounds__(128) router_topk_kernel(RouterArgs a) {
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= a.tokens) return;  // warp-uniform
-  router_topk_and_weights<PER>(a, t, threadIdx.x & 31);
+  const int lane = threadIdx.x & 31;
+  router_topk_and_weights<PER>(a, t, lane, false,
+                               [&](auto& sc) { router_load_global(a, t, lane, sc); });
 }
 
 cudaError_t launch_router_batched(const RouterArgs& a, cudaStream_t s) {
