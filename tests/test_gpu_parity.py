@@ -123,6 +123,23 @@ def test_fp8_gemv_rows_multi_act_quant_bit_exact(ctx, W, batch):
     np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(want))
 
 
+@pytest.mark.parametrize("rows,cols,batch", [(32768, 1024, 32), (1024, 4096, 17), (4096, 8192, 2),
+                                             (640, 512, 40), (256, 128, 5)])
+def test_fp8_gemv_batched_shapes_bit_exact(ctx, W, rows, cols, batch):
+    # the batched kernel (16 inputs x 32 rows per CTA, ragged input tiles) and,
+    # at 128 columns, the generic kernel; rows with 0x7F/0xFF bytes take the
+    # exact recompute
+    w, s = _fp8_case(rows * 7 + batch, rows, cols)
+    w[3, 5] = 0x7F
+    w[rows - 1, cols - 1] = 0xFF
+    xs = H.activations(rows + batch, batch, cols)
+    st, want = O.fp8_gemv_multi(w, s, xs, rows, cols, rows // 128, cols // 128)
+    assert st == O.OK
+    y = W.gemv_fp8_e4m3_ue8m0_rows_multi(ctx, dev(w), dev(s), dev(xs), 0, rows)
+    ctx.sync()
+    np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(want))
+
+
 def test_fp8_gemv_nan_bytes_decode_as_480(ctx, W):
     # 0x7F / 0xFF decode to +-480 in the reference (no NaN): rows holding them
     # take the exact recompute path

@@ -142,6 +142,25 @@ wh_status make_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_
   return WH_OK;
 }
 
+// f32 matrix [height][width], rows ld floats apart: box [16 rows][136 floats],
+// no swizzle (the batched FP8 GEMV's input tiles; 136 = a 128-column group
+// plus 8 floats that pad each row of the tile onto other banks).  Returns
+// false, recording nothing, when the driver refuses the map (the caller then
+// runs the generic kernel).
+bool make_f32_xmap(CUtensorMap* map, const float* base, uint64_t width, uint64_t height,
+                   uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {width, height};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {136, 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // validate_fp4_matvec (src/deepseek_v4.rs:434-462)
 wh_status validate_fp4(const wh_fp4_matvec_spec& s, size_t input_len, size_t output_len) {
   if (s.rows == 0 || s.cols == 0 || s.scale_cols == 0) return fail(WH_ERR_EMPTY_SHAPE, "empty shape");
@@ -281,6 +300,8 @@ struct wh_ctx {
   void* work = nullptr;  // generic-path workspace
   size_t work_bytes = 0;
   std::map<std::tuple<const void*, int, int, int>, CUtensorMap> fp8_maps;
+  // batched FP8 GEMV inputs: (x, width, batch, ldx) -> map of box [16][136] f32
+  std::map<std::tuple<const void*, long long, int, int>, CUtensorMap> fp8_xmaps;
   std::map<std::tuple<const void*, const void*, const void*, size_t, size_t>, DevExpertSet> experts;
   bool profile = false;
   std::vector<cudaEvent_t> ev;  // 2 per phase
@@ -511,20 +532,49 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
   bool fast = cols / scale_cols == 128 && aligned(weight, 16) && aligned(x, 16) &&
               ldx % 4 == 0 && x_group_off % 4 == 0 && cols <= 8192;
   bool in_kernel_aq = false;  // the one-input kernel quantises x itself
-  if (fast) {
-    const int nrows = row_end - row_start;
-    const int tiles = batch == 1 ? 1 : (batch + 15) / 16;
-    int per = std::max(1, c->num_sms / tiles);
-    int box_rows = std::min(32, std::max(1, (nrows + per - 1) / per));
-    if (x_group_rows > 0) {
-      // every CTA's rows must lie in one group: a box height dividing the group
-      // and the start row
+  // every CTA's rows must lie in one group: a box height dividing the group
+  // and the start row
+  auto fit_groups = [&](int box_rows) {
+    if (x_group_rows > 0)
       while (box_rows > 1 && (x_group_rows % box_rows != 0 || row_start % box_rows != 0))
         --box_rows;
+    return box_rows;
+  };
+  const CUtensorMap* xmap = nullptr;
+  if (fast) {
+    // one input: boxes of ceil(rows / SMs) rows, one per SM; the batched
+    // kernel: boxes of 32 rows
+    const int nrows = row_end - row_start;
+    const int per = std::max(1, c->num_sms);
+    a.box_rows = fit_groups(std::min(32, std::max(1, (nrows + per - 1) / per)));
+    in_kernel_aq = batch == 1 && fp8_gemv_rowgroup_fits(a, c->num_sms);
+    if (!in_kernel_aq) {
+      a.box_rows = fit_groups(32);
+      if (act_quant_block > 0 && !pre_aq_ok) fast = false;
     }
-    a.box_rows = box_rows;
-    in_kernel_aq = fp8_gemv_rowgroup_fits(a, c->num_sms);
-    if (act_quant_block > 0 && !in_kernel_aq && !pre_aq_ok) fast = false;
+  }
+  if (fast && !in_kernel_aq) {
+    // the batched kernel's input tiles: x itself, or the act-quantised copy of
+    // each input's span in the workspace
+    const float* xsrc = x;
+    int xld = ldx;
+    if (act_quant_block > 0) {
+      wh_status st = c->ensure_work(sizeof(float) * (size_t)batch * xspan);
+      if (st != WH_OK) return st;
+      xsrc = static_cast<const float*>(c->work);
+      xld = (int)xspan;
+    }
+    auto xkey = std::make_tuple((const void*)xsrc, xspan, batch, xld);
+    auto xit = c->fp8_xmaps.find(xkey);
+    if (xit == c->fp8_xmaps.end()) {
+      CUtensorMap m;
+      if (xspan >= 136 && make_f32_xmap(&m, xsrc, xspan, batch, xld))
+        xit = c->fp8_xmaps.emplace(xkey, m).first;
+    }
+    if (xit == c->fp8_xmaps.end())
+      fast = false;  // no input map for this shape: the generic kernel
+    else
+      xmap = &xit->second;
   }
   if (fast) {
     const int box_rows = a.box_rows;
@@ -552,7 +602,7 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
     }
     // programmatic dependent launch, so that back-to-back GEMVs overlap one's
     // weight stream with the previous one's tail
-    WH_CUDA(launch_fp8_gemv(&it->second, a, c->num_sms, stream, c->pdl()));
+    WH_CUDA(launch_fp8_gemv(&it->second, xmap, a, c->num_sms, stream, c->pdl()));
     return WH_OK;
   }
   // generic path
@@ -579,7 +629,7 @@ wh_status fp8_gemv_impl(wh_ctx* c, const uint8_t* weight, const uint8_t* scale, 
     a.ldx = cols;
     a.act_quant_block = 0;
   }
-  WH_CUDA(launch_fp8_gemv(nullptr, a, c->num_sms, stream, false));
+  WH_CUDA(launch_fp8_gemv(nullptr, nullptr, a, c->num_sms, stream, false));
   return WH_OK;
 }
 

@@ -165,18 +165,25 @@ constexpr size_t kFp8SmemBudget = 200 * 1024;
 
 
 // ---------------------------------------------------------------------------
-// Batched path (2..N inputs): the inputs stream with the weights.  Each ring
-// stage holds one 128-column group: the weight box [32 rows][128 B] (TMA) and
-// the group's 128 columns of each of the tile's TB inputs (one 512-byte bulk
-// copy per input), so nothing is staged before the first group and a CTA
-// holds 4 stages.  8 lanes per row, lane q holding the chains 2(q&3),
-// 2(q&3)+1 of g0 (q < 4) or g1 (q >= 4); the row's weights of a group
-// are decoded once and applied to the TB inputs.  Inputs are act-quantised
-// beforehand when the call asks for it.
+// Batched path (2..N inputs): a CTA takes a box of up to 32 rows and a tile of
+// 16 inputs; per 128-column group one ring stage holds the weight box
+// [rows][128 B] (TMA, 128-byte swizzle) and the x tile [16 inputs][136 floats]
+// (TMA from a [batch][cols] map: the 8 floats past the group pad every input
+// row onto other banks, and are never read).
+//
+// A group of 4 lanes (a quad) owns 2 rows x 4 inputs; lane q of the quad holds
+// the chains 2q and 2q+1 of both halves (g0: columns 16c + 2q, +1; g1:
+// 16c + 8 + 2q, +1) as f32 pairs, so P_j = g0_j + g1_j is local and the
+// reference's acc_j = fma(P_j, scale, acc_j) follows once per group.  Each
+// weight pair is decoded once and used for 4 inputs; each x pair is read once
+// and used for 2 rows.  The pairwise 8-lane sum of the end is two shuffles
+// inside the quad.  Inputs are act-quantised beforehand when the call asks.
 // ---------------------------------------------------------------------------
 constexpr int kFbStages = 4;
 constexpr int kFbTB = 16;                           // inputs per CTA
-constexpr int kFbStageBytes = 4096 + kFbTB * 512;   // weight box + x tile
+constexpr int kFbXStride = 136;                     // floats per input row of a stage
+constexpr int kFbXBytes = kFbTB * kFbXStride * 4;   // 8704
+constexpr int kFbStageBytes = 13 * 1024;            // weight box (4 KB) + x tile, 1 KiB multiple
 constexpr int kFbThreads = 32 * (8 + 1);            // 8 consumer warps + producer
 
 size_t fp8_gemv_batch_smem_bytes(int scale_cols) {
@@ -184,22 +191,23 @@ size_t fp8_gemv_batch_smem_bytes(int scale_cols) {
          64;
 }
 
-__global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
-    const __grid_constant__ CUtensorMap wmap, Fp8GemvArgs a) {
+__global__ void __launch_bounds__(kFbThreads, 2) fp8_gemv_batch_kernel(
+    const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+    Fp8GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kFbStages * kFbStageBytes);
   uint64_t* empty = full + kFbStages;
-  uint8_t* scale_s = reinterpret_cast<uint8_t*>(empty + kFbStages);  // CTA's scale rows
+  uint8_t* scale_s = reinterpret_cast<uint8_t*>(empty + kFbStages);  // the box's scale rows
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int box_rows = a.box_rows;  // <= 32
-  const int row0 = a.row_start + blockIdx.x * box_rows;
+  const int tile = blockIdx.x;      // inputs [16 tile, 16 tile + 16): neighbours share weights
+  const int row0 = a.row_start + blockIdx.y * box_rows;
   const int ngroups = a.scale_cols;
-  const int tile = blockIdx.y;
-  const int tb = min(kFbTB, a.batch - tile * kFbTB);
-  const float* xbase = fp8_x_rows(a, row0) + (long long)tile * kFbTB * a.ldx;
+  // grouped mode: the box's rows read their group's slice of every input
+  const int xcol0 = a.x_group_rows ? (int)((row0 / a.x_group_rows) * a.x_group_off) : 0;
   // the next kernel may start its weight stream now (it waits for this grid
   // before reading y)
   pdl_launch_dependents();
@@ -216,24 +224,30 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
   if (warp == 8) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
+      prefetch_tensormap(&xmap);
+      const uint32_t stage_tx = box_rows * 128 + kFbXBytes;
       // the first stages' weights do not depend on the previous kernel
       const int pre = min(ngroups, kFbStages);
       for (int g = 0; g < pre; ++g) {
-        mbar_arrive_expect_tx(&full[g], box_rows * 128 + tb * 512);
+        mbar_arrive_expect_tx(&full[g], stage_tx);
         tma_load_2d(stages + g * kFbStageBytes, &wmap, &full[g], g * 128, row0);
       }
       pdl_wait_prior();  // the inputs may come from the previous kernel
-      int g = 0;
+      for (int g = 0; g < pre; ++g)
+        tma_load_2d(stages + g * kFbStageBytes + 4096, &xmap, &full[g], xcol0 + g * 128,
+                    tile * kFbTB);
+      int g = pre, s = 0;
+      uint32_t phase = 0;
       for (; g < ngroups; ++g) {
-        const int s = g % kFbStages;
+        if (!mbar_wait(&empty[s], phase, a.status)) break;  // slot of group g - kFbStages
         uint8_t* st = stages + s * kFbStageBytes;
-        if (g >= pre) {
-          if (!mbar_wait(&empty[s], ((g / kFbStages) - 1) & 1, a.status)) break;
-          mbar_arrive_expect_tx(&full[s], box_rows * 128 + tb * 512);
-          tma_load_2d(st, &wmap, &full[s], g * 128, row0);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        tma_load_2d(st, &wmap, &full[s], g * 128, row0);
+        tma_load_2d(st + 4096, &xmap, &full[s], xcol0 + g * 128, tile * kFbTB);
+        if (++s == kFbStages) {
+          s = 0;
+          phase ^= 1u;
         }
-        for (int b = 0; b < tb; ++b)
-          bulk_load(st + 4096 + b * 512, xbase + (long long)b * a.ldx + g * 128, 512, &full[s]);
       }
       for (int i = max(0, g - kFbStages); i < g; ++i)
         if (!mbar_drain(&full[i % kFbStages], (i / kFbStages) & 1, a.status)) break;
@@ -249,66 +263,99 @@ __global__ void __launch_bounds__(kFbThreads) fp8_gemv_batch_kernel(
     scale_s[i] = a.scale[(long long)srow0 * a.scale_cols + i];
   asm volatile("bar.sync 1, 256;" ::: "memory");
 
-  const int rloc = warp * 4 + (lane >> 3);  // row within the box
-  const int q = lane & 7;
-  const int row = row0 + rloc;
-  const bool active = rloc < box_rows && row < a.row_end;
-  const uint8_t* srow_s = scale_s + ((active ? row : row0) / row_group - srow0) * a.scale_cols;
-  // the lane's two columns within each 16-column chunk
-  const int cofs = (q < 4 ? 0 : 8) + 2 * (q & 3);
-
-  float2 acc[kFbTB];
+  const int quad = lane >> 2, q = lane & 3;
+  const int rl0 = warp * 4 + (quad >> 2) * 2;  // the quad's two rows within the box
+  const int ig = quad & 3;                      // its inputs: ig + 4m, m = 0..3
+  const uint8_t* srow_s[2];
+  bool rvalid[2];
 #pragma unroll
-  for (int b = 0; b < kFbTB; ++b) acc[b] = make_float2(0.0f, 0.0f);
+  for (int k = 0; k < 2; ++k) {
+    const int row = row0 + rl0 + k;
+    rvalid[k] = rl0 + k < box_rows && row < a.row_end;
+    srow_s[k] = scale_s + ((rvalid[k] ? row : row0) / row_group - srow0) * a.scale_cols;
+  }
+  const int tb = min(kFbTB, a.batch - tile * kFbTB);
+
+  float2 acc[2][4];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int m = 0; m < 4; ++m) acc[k][m] = make_float2(0.0f, 0.0f);
   bool ok = true;
+  int s = 0;
+  uint32_t phase = 0;
   for (int g = 0; g < ngroups; ++g) {
-    const int s = g % kFbStages;
-    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (g / kFbStages) & 1, a.status))) {
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], phase, a.status))) {
       ok = false;
       break;
     }
-    const uint8_t* st = stages + s * kFbStageBytes;
-    float2 wf[8];
+    const uint8_t* wst = stages + s * kFbStageBytes;
+    const float* xst = reinterpret_cast<const float*>(wst + 4096) + ig * kFbXStride + 2 * q;
+    float2 g0[2][4], g1[2][4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-        wf[c] = h2_to_f2(e4m3x2_to_f16x2(
-          *reinterpret_cast<const uint16_t*>(st + rloc * 128 + 16 * (c ^ (rloc & 7)) + cofs)));
-    const float scale = decode_ue8m0(srow_s[g]);
-    const float2 sc = make_float2(scale, scale);
-    const float* xt = reinterpret_cast<const float*>(st + 4096) + cofs;
+    for (int k = 0; k < 2; ++k)
 #pragma unroll
-    for (int b = 0; b < kFbTB; ++b) {
-      if (b < tb) {
-        float2 pj = make_float2(0.0f, 0.0f);
+      for (int m = 0; m < 4; ++m) g0[k][m] = g1[k][m] = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          pj = ffma2(wf[c], *reinterpret_cast<const float2*>(xt + b * 128 + 16 * c), pj);
-        // P_j = g0_j + g1_j: lanes q and q ^ 4 hold g0 / g1 of the same j
-        float2 o;
-        o.x = __shfl_xor_sync(0xffffffffu, pj.x, 4);
-        o.y = __shfl_xor_sync(0xffffffffu, pj.y, 4);
-        acc[b] = ffma2(fadd2(pj, o), sc, acc[b]);
+    for (int c = 0; c < 8; ++c) {
+      float2 w0[2], w1[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int r = rl0 + k;
+        const uint4 ch = *reinterpret_cast<const uint4*>(wst + r * 128 + 16 * (c ^ (r & 7)));
+        // bytes 2q, 2q+1 (g0) and 8 + 2q, 9 + 2q (g1) of the 16-column chunk
+        const uint32_t lo = (q >> 1) ? ch.y : ch.x, hi = (q >> 1) ? ch.w : ch.z;
+        const int sh = 16 * (q & 1);
+        w0[k] = h2_to_f2(e4m3x2_to_f16x2(lo >> sh));
+        w1[k] = h2_to_f2(e4m3x2_to_f16x2(hi >> sh));
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float* xp = xst + 4 * m * kFbXStride + 16 * c;
+        const float2 x0 = *reinterpret_cast<const float2*>(xp);
+        const float2 x1 = *reinterpret_cast<const float2*>(xp + 8);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          g0[k][m] = ffma2(w0[k], x0, g0[k][m]);
+          g1[k][m] = ffma2(w1[k], x1, g1[k][m]);
+        }
       }
     }
+    // release the slot after the warp's reads of it
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float sc = decode_ue8m0(srow_s[k][g]);
+      const float2 sc2 = make_float2(sc, sc);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) acc[k][m] = ffma2(fadd2(g0[k][m], g1[k][m]), sc2, acc[k][m]);
+    }
+    if (++s == kFbStages) {
+      s = 0;
+      phase ^= 1u;
+    }
   }
   if (!ok) return;
-  const uint8_t* srow = a.scale + (long long)((active ? row : a.row_start) / row_group) * a.scale_cols;
 #pragma unroll
-  for (int b = 0; b < kFbTB; ++b) {
-    if (b < tb) {
-      // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7))
-      const float s2 = __fadd_rn(acc[b].x, acc[b].y);
+  for (int k = 0; k < 2; ++k) {
+    const int row = row0 + rl0 + k;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      // hsum256: ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7)); lane q holds
+      // a_2q, a_2q+1
+      const float s2 = __fadd_rn(acc[k][m].x, acc[k][m].y);
       const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
       const float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 2));
-      if (q == 0 && active) {
+      const int b = ig + 4 * m;
+      if (q == 0 && rvalid[k] && b < tb) {
         float tot = __fadd_rn(s8, 0.0f);
         const int bi = tile * kFbTB + b;
         if (!isfinite(tot)) {
           // 0x7F/0xFF bytes (or a genuine overflow): exact recompute
+          const uint8_t* srow = a.scale + (long long)(row / row_group) * a.scale_cols;
           tot = fp8_row_dot_exact(a.weight + (long long)row * a.cols, srow, a.scale_cols, 128,
-                                  xbase + (long long)b * a.ldx);
+                                  fp8_x_rows(a, row) + (long long)bi * a.ldx);
           if (!isfinite(tot)) flag(a.status, WH_DEV_NONFINITE);
         }
         const long long o = (long long)bi * a.ldy + (row - a.row_start);
@@ -598,8 +645,8 @@ __global__ void __launch_bounds__(kRgThreads, 4)
   }
 }
 
-cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
-                            cudaStream_t stream, bool pdl) {
+cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const CUtensorMap* xmap,
+                            const Fp8GemvArgs& a, int num_sms, cudaStream_t stream, bool pdl) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -633,13 +680,16 @@ cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int n
     if (e != cudaSuccess) return e;
     return cudaLaunchKernelEx(&cfg, kern, *wmap, a, p.ns);
   }
-  // 2..N inputs: the streaming batched kernel, kFbTB inputs per CTA
+  // 2..N inputs: the batched kernel, 16 inputs x one row box per CTA; the
+  // input tiles of a row box are neighbours in launch order (they read the
+  // same weights)
+  if (xmap == nullptr) return cudaErrorInvalidValue;
   cfg.blockDim = dim3(kFbThreads);
-  cfg.gridDim = dim3((nrows + a.box_rows - 1) / a.box_rows, (a.batch + kFbTB - 1) / kFbTB);
+  cfg.gridDim = dim3((a.batch + kFbTB - 1) / kFbTB, (nrows + a.box_rows - 1) / a.box_rows);
   cfg.dynamicSmemBytes = fp8_gemv_batch_smem_bytes(a.scale_cols);
   cudaError_t e = ensure_smem(fp8_gemv_batch_kernel, cfg.dynamicSmemBytes);
   if (e != cudaSuccess) return e;
-  return cudaLaunchKernelEx(&cfg, fp8_gemv_batch_kernel, *wmap, a);
+  return cudaLaunchKernelEx(&cfg, fp8_gemv_batch_kernel, *wmap, *xmap, a);
 }
 
 cudaError_t launch_act_quant(float* v, long long n, int block, uint32_t* status, int num_sms,

@@ -168,9 +168,11 @@ void set_act_quant_table(const ActQuantTable& t, cudaStream_t s);
 const ActQuantTable* act_quant_table_device();
 // true when the one-input kernel takes the call (it then act-quantises x itself)
 bool fp8_gemv_rowgroup_fits(const Fp8GemvArgs& a, int num_sms);
-// wmap == nullptr selects the generic kernel.
-cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const Fp8GemvArgs& a, int num_sms,
-                            cudaStream_t stream, bool pdl);
+// wmap == nullptr selects the generic kernel; the batched kernel (2..N
+// inputs, or one input the one-input kernel does not take) needs xmap: x as
+// f32 [batch][ldx] with box [16 inputs][136 floats], no swizzle.
+cudaError_t launch_fp8_gemv(const CUtensorMap* wmap, const CUtensorMap* xmap,
+                            const Fp8GemvArgs& a, int num_sms, cudaStream_t stream, bool pdl);
 cudaError_t launch_act_quant(float* v, long long n, int block, uint32_t* status, int num_sms,
                              cudaStream_t stream);
 
