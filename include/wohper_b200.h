@@ -532,6 +532,20 @@ wh_status wh_lm_head_topk(wh_ctx* ctx, const uint16_t* weight, long long rows, i
                           uint32_t row_base, const float* x, size_t x_len, int top_k,
                           uint32_t* out_tokens, float* out_logits, float* logits, void* scratch,
                           size_t scratch_bytes, wh_stream_t stream);
+/* Device scratch bytes wh_lm_head_topk_batch needs for `tokens` inputs. */
+size_t wh_lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens);
+/* wh_lm_head_topk for `tokens` inputs at once, as the reference's batched
+ * decode scores each position (score_bf16_lm_head_topk per token of
+ * run_positions_batch, src/server/generation.rs:2330): input t is
+ * x + t * ldx; its result goes to out_tokens / out_logits + t * top_k and, when
+ * logits is given, its logits to logits + t * rows.  Each token's result equals
+ * wh_lm_head_topk's bit for bit; the weight is streamed once per tile of up to
+ * 8 tokens instead of once per token.  Same limits as wh_lm_head_topk. */
+wh_status wh_lm_head_topk_batch(wh_ctx* ctx, const uint16_t* weight, long long rows, int cols,
+                                uint32_t row_base, const float* x, int tokens, int ldx,
+                                int top_k, uint32_t* out_tokens, float* out_logits,
+                                float* logits, void* scratch, size_t scratch_bytes,
+                                wh_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* ZCBLK01 tensor blocks (host memory; no device work)                        */

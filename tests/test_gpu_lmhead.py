@@ -142,3 +142,59 @@ def test_lm_head_candidate_overflow_takes_the_replay(ctx, W):
     x[3] = abs(float(x[3])) + 1.0
     tg, vg = _check(W, ctx, w, x, 5)
     assert tg.tolist() == [7000, 1, 2, 3, 4]
+
+
+def _check_batch(W, ctx, w, xs, k, row_base=0):
+    """The several-token call against the single-token call, token by token:
+    the same tokens, logits and per-row logits, bit for bit."""
+    rows = w.shape[0]
+    T = xs.shape[0]
+    logits = torch.empty(T, rows, device="cuda")
+    tb, vb = W.lm_head_topk_score_batch(ctx, w, xs, k, row_base=row_base, logits=logits)
+    ctx.sync()
+    tb, vb, lb = tb.cpu().numpy().astype(np.uint32), vb.cpu().numpy(), logits.cpu().numpy()
+    for t in range(T):
+        ts, vs, ls = _run(W, ctx, w, xs[t], k, row_base)
+        _same(lb[t], ls)
+        np.testing.assert_array_equal(tb[t], ts)
+        _same(vb[t], vs)
+    return tb, vb
+
+
+@pytest.mark.parametrize("T", [3, 9, 32])
+def test_lm_head_batch_deepseek_vocab_matches_per_token(ctx, W, T):
+    w = _weight(21, 129280, 4096)
+    g = torch.Generator(device="cuda").manual_seed(22 + T)
+    xs = torch.randn(T, 4096, device="cuda", generator=g)
+    _check_batch(W, ctx, w, xs, 50)
+    # one token against the oracle as well
+    tb, vb = _check_batch(W, ctx, w, xs[:1], 8)
+    n, to, vo, lo = O.lm_head_topk(w.cpu().numpy().view(np.uint16), xs[0].cpu().numpy(), 8)
+    np.testing.assert_array_equal(tb[0], to)
+    _same(vb[0], vo)
+
+
+def test_lm_head_batch_tiles_strides_ties_and_nans(ctx, W):
+    # 8192 and 16384 columns take 4- and 2-token tiles; a strided input; an
+    # 8-column tail; duplicate rows (ties) and a NaN row and a NaN input
+    for cols, T in ((8192, 7), (16384, 5), (4104, 11)):
+        w = _weight(30 + T, 3000, cols)
+        buf = torch.randn(T, cols + 12, device="cuda")
+        xs = buf[:, :cols]
+        w[17] = w[2900]
+        w[400] = w[2900]
+        w[1234, 5] = 0x7FC0
+        xs[T - 1, 3] = float("nan")
+        tb, _ = _check_batch(W, ctx, w, xs, 6, row_base=777)
+        assert all(1234 + 777 not in tb[t].tolist() for t in range(T - 1))
+
+
+def test_lm_head_batch_argument_errors(ctx, W):
+    w = _weight(40, 64, 256)
+    with pytest.raises(W.WohperError) as e:
+        W.lm_head_topk_score_batch(ctx, w, torch.randn(0, 256, device="cuda"), 4)
+    assert e.value.kind == "EmptyShape"
+    with pytest.raises(W.WohperError) as e:
+        W.lm_head_topk_score_batch(ctx, w, torch.randn(2, 256, device="cuda"), 4,
+                                   scratch=torch.empty(64, dtype=torch.uint8, device="cuda"))
+    assert e.value.kind == "ScratchTooSmall"

@@ -81,7 +81,8 @@ EXPORTS = (
     "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward", "wh_rope_inv_freqs",
     "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf", "wh_hc_pre",
     "wh_hc_post", "wh_hc_head", "wh_rms_norm", "wh_fp8_gemv_grouped",
-    "wh_v4_attention_scratch_len", "wh_v4_attention",
+    "wh_v4_attention_scratch_len", "wh_v4_attention", "wh_lm_head_batch_scratch_bytes",
+    "wh_lm_head_topk_batch",
 )
 
 
@@ -197,6 +198,9 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
                                        vp]),
         "wh_lm_head_topk": (st, [vp, vp, C.c_longlong, i, C.c_uint32, vp, sz, i, vp, vp, vp, vp,
                                  sz, vp]),
+        "wh_lm_head_batch_scratch_bytes": (sz, [C.c_longlong, i, i]),
+        "wh_lm_head_topk_batch": (st, [vp, vp, C.c_longlong, i, C.c_uint32, vp, i, i, i, vp, vp,
+                                       vp, vp, sz, vp]),
         "wh_zcblk_parse": (st, [vp, sz, vp]),
         "wh_zcblk_tensor_at": (st, [vp, sz, C.c_uint32, vp]),
         "wh_zcblk_tensor_dim": (st, [vp, sz, vp, C.c_uint32, vp]),
@@ -461,6 +465,31 @@ def lm_head_topk_score(ctx: Context, weight_bf16, x, top_k: int, row_base: int =
                                  x.numel(), k, _ptr(toks), _ptr(vals), _ptr(logits),
                                  _ptr(scratch), scratch.numel(), _stream(stream)))
     return toks[:n], vals[:n]
+
+
+def lm_head_topk_score_batch(ctx: Context, weight_bf16, x, top_k: int, row_base: int = 0,
+                             logits=None, scratch=None, stream=None):
+    """lm_head_topk_score for every row of x [tokens, cols] at once (the
+    weight streams once per tile of up to 8 tokens).  Returns (tokens int32
+    [T, min(top_k, rows)], logits f32 [T, min(top_k, rows)]); row t equals
+    lm_head_topk_score(x[t]) bit for bit."""
+    import torch
+
+    rows, cols = weight_bf16.shape
+    T = x.shape[0]
+    k = max(int(top_k), 1)
+    n = min(k, rows)
+    dev = weight_bf16.device
+    toks = torch.empty(T, k, dtype=torch.int32, device=dev)
+    vals = torch.empty(T, k, dtype=torch.float32, device=dev)
+    if scratch is None:
+        scratch = torch.empty(lib().wh_lm_head_batch_scratch_bytes(rows, k, T),
+                              dtype=torch.uint8, device=dev)
+    _check(lib().wh_lm_head_topk_batch(ctx.handle, _ptr(weight_bf16), rows, cols, row_base,
+                                       _ptr(x), T, x.stride(0), k, _ptr(toks), _ptr(vals),
+                                       _ptr(logits), _ptr(scratch), scratch.numel(),
+                                       _stream(stream)))
+    return toks[:, :n], vals[:, :n]
 
 
 # DeepSeek-V4's attention constants (src/compute.rs DEEPSEEK_V4_YARN,

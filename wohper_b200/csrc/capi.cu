@@ -1116,6 +1116,8 @@ wh_status wh_lm_head_topk(wh_ctx* c, const uint16_t* weight, long long rows, int
   a.cand = reinterpret_cast<uint64_t*>(carve(8192 * 8));
   a.out_tokens = out_tokens;
   a.out_logits = out_logits;
+  a.tokens = 1;
+  a.ldx = cols;
   cudaStream_t s = (cudaStream_t)stream;
   WH_CUDA(cudaMemsetAsync(a.flags, 0, 16 + 4096 * 4, s));
   wh_status st;
@@ -1125,6 +1127,62 @@ wh_status wh_lm_head_topk(wh_ctx* c, const uint16_t* weight, long long rows, int
     WH_CUDA(launch_lm_head_stage(a, stage, c->pdl(), s));
     if ((st = c->prof_mark(s)) != WH_OK) return st;
   }
+  return WH_OK;
+}
+
+size_t wh_lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens) {
+  return tokens < 1 ? 0 : lm_head_batch_scratch_bytes(rows, top_k, tokens);
+}
+
+wh_status wh_lm_head_topk_batch(wh_ctx* c, const uint16_t* weight, long long rows, int cols,
+                                uint32_t row_base, const float* x, int tokens, int ldx,
+                                int top_k, uint32_t* out_tokens, float* out_logits,
+                                float* logits, void* scratch, size_t scratch_bytes,
+                                wh_stream_t stream) {
+  if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
+  top_k = top_k < 1 ? 1 : top_k;  // top_k.max(1) (src/compute.rs:2777)
+  if (tokens < 1) return fail(WH_ERR_EMPTY_SHAPE, "LM-head batch has no tokens");
+  if (tokens > 65535) return fail(WH_ERR_UNSUPPORTED, "LM-head batch takes at most 65535 tokens");
+  if (!scratch || scratch_bytes == 0) return fail(WH_ERR_SCRATCH_TOO_SMALL, "scratch is empty");
+  if (cols <= 0 || rows < 0) return fail(WH_ERR_INVALID_SHAPE, "LM-head shape");
+  if (ldx < cols) return fail(WH_ERR_INVALID_SHAPE, "LM-head input too small");
+  if (rows == 0) return fail(WH_ERR_INVALID_SHAPE, "LM-head has no rows");
+  if (!weight || !x || !out_tokens || !out_logits) return fail(WH_ERR_INVALID_POINTER, "null pointer");
+  if (!lm_head_supported(rows, cols, top_k) || cols % 8 != 0 || !aligned(weight, 16))
+    return fail(WH_ERR_UNSUPPORTED,
+                "lm_head top-k needs cols % 8 == 0, cols <= 16384, a 16-byte aligned weight "
+                "and top_k <= 511");
+  if (scratch_bytes < lm_head_batch_scratch_bytes(rows, top_k, tokens))
+    return fail(WH_ERR_SCRATCH_TOO_SMALL, "lm_head batch scratch too small");
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  auto carve = [&](size_t bytes) {
+    uint8_t* q = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+    p = q + bytes;
+    return q;
+  };
+  LmHeadArgs a{};
+  a.weight = weight;
+  a.x = x;
+  a.rows = rows;
+  a.cols = cols;
+  a.top_k = top_k;
+  a.row_base = row_base;
+  a.tokens = tokens;
+  a.ldx = ldx;
+  float* lg = reinterpret_cast<float*>(carve(size_t(tokens) * rows * 4));
+  a.logits = logits ? logits : lg;
+  // per token: flags, pass counter, candidate count, -, histogram; one memset
+  const size_t words = size_t(tokens) * kLmTokWords;
+  a.flags = reinterpret_cast<uint32_t*>(carve(words * 4));
+  a.counter = a.flags + 1;
+  a.cand_count = a.flags + 2;
+  a.hist = reinterpret_cast<int*>(a.flags + 4);
+  a.cand = reinterpret_cast<uint64_t*>(carve(size_t(tokens) * 8192 * 8));
+  a.out_tokens = out_tokens;
+  a.out_logits = out_logits;
+  cudaStream_t s = (cudaStream_t)stream;
+  WH_CUDA(cudaMemsetAsync(a.flags, 0, words * 4, s));
+  WH_CUDA(launch_lm_head_batch(a, c->pdl(), s));
   return WH_OK;
 }
 

@@ -138,8 +138,16 @@ struct LmHeadArgs {
   uint64_t* cand;        // [8192] candidate keys
   uint32_t* out_tokens;
   float* out_logits;
+  // several tokens in one call: token t reads x + t * ldx and owns
+  // logits + t * rows, the words flags + t * kLmTokWords (flags, counter,
+  // candidate count, -, histogram), cand + t * 8192 and out_* + t * top_k
+  int tokens;  // 1 for the one-token call
+  int ldx;
 };
+constexpr int kLmTokWords = 4 + 4096;
 size_t lm_head_scratch_bytes(long long rows, int top_k);
+size_t lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens);
+cudaError_t launch_lm_head_batch(const LmHeadArgs& a, bool pdl, cudaStream_t s);
 bool lm_head_supported(long long rows, int cols, int top_k);
 cudaError_t launch_lm_head_stage(const LmHeadArgs& a, int stage, bool pdl, cudaStream_t s);
 

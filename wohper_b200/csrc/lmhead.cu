@@ -31,6 +31,8 @@ namespace wh {
 constexpr int kLmRowsPerWarp = 16;
 constexpr int kLmWarps = 8;
 constexpr int kLmMaxK = 511;
+constexpr int kLmSelCap = 8192;
+constexpr int kLmBins = 4096;
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 v;
@@ -129,6 +131,118 @@ __global__ void __launch_bounds__(32 * kLmWarps) lm_logits_kernel(LmHeadArgs a) 
   pdl_launch_dependents();
 }
 
+// Logits of TB tokens per weight pass (several-token call): the same row
+// passes, lanes and chain order as lm_logits_kernel, with the tile's inputs
+// in shared memory and TB accumulator sets per lane, so the weights stream
+// once per tile of tokens instead of once per token.  Grid y = token tiles;
+// each tile hands out its passes from the counter of its first token.
+template <int TB>
+constexpr int lm_batch_threads() { return TB >= 8 ? 256 : 512; }  // 8 tokens: registers
+template <int TB>
+__global__ void __launch_bounds__(lm_batch_threads<TB>(), 1) lm_logits_batch_kernel(LmHeadArgs a) {
+  extern __shared__ __align__(16) float lm_xt[];  // [TB][cols]
+  const int t0 = blockIdx.y * TB;
+  const int nt = min(TB, a.tokens - t0);
+  pdl_wait_prior();
+  for (int i = threadIdx.x; i < TB * a.cols; i += blockDim.x) {
+    const int tt = i / a.cols, col = i - tt * a.cols;
+    lm_xt[i] = tt < nt ? a.x[(long long)(t0 + tt) * a.ldx + col] : 0.0f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int half = lane & 1;
+  const int chunks = a.cols / 16;
+  uint32_t* counter = a.flags + (long long)t0 * kLmTokWords + 1;
+  const long long passes = (a.rows + kLmRowsPerWarp - 1) / kLmRowsPerWarp;
+  for (;;) {
+    long long pass = 0;
+    if (lane == 0) pass = (long long)atomicAdd(counter, 1u);
+    pass = __shfl_sync(0xffffffffu, pass, 0);
+    if (pass >= passes) break;
+    const long long row = pass * kLmRowsPerWarp + (lane >> 1);
+    const bool active = row < a.rows;
+    const long long rr = active ? row : a.rows - 1;  // every lane joins the shuffles
+    const uint16_t* wrow = a.weight + rr * a.cols;
+    const uint8_t* wp = reinterpret_cast<const uint8_t*>(wrow) + 16 * half;
+    float2 acc[TB][4];
+#pragma unroll
+    for (int tt = 0; tt < TB; ++tt)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[tt][k] = make_float2(0.0f, 0.0f);
+    auto step = [&](const uint4 w, int c) {
+      const float2 w0 = make_float2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u));
+      const float2 w1 = make_float2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+      const float2 w2 = make_float2(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xffff0000u));
+      const float2 w3 = make_float2(__uint_as_float(w.w << 16), __uint_as_float(w.w & 0xffff0000u));
+#pragma unroll
+      for (int tt = 0; tt < TB; ++tt) {
+        const float* xp = lm_xt + tt * a.cols + 8 * half + 16 * c;
+        const float4 xa = *reinterpret_cast<const float4*>(xp);
+        const float4 xb = *reinterpret_cast<const float4*>(xp + 4);
+        acc[tt][0] = ffma2(w0, make_float2(xa.x, xa.y), acc[tt][0]);
+        acc[tt][1] = ffma2(w1, make_float2(xa.z, xa.w), acc[tt][1]);
+        acc[tt][2] = ffma2(w2, make_float2(xb.x, xb.y), acc[tt][2]);
+        acc[tt][3] = ffma2(w3, make_float2(xb.z, xb.w), acc[tt][3]);
+      }
+    };
+    int c = 0;
+    for (; c + 4 <= chunks; c += 4) {
+      uint4 w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = ld_stream_v4(wp + 32 * (c + k));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) step(w[k], c + k);
+    }
+    for (; c < chunks; ++c) step(ld_stream_v4(wp + 32 * c), c);
+#pragma unroll
+    for (int tt = 0; tt < TB; ++tt) {
+      // P_j = acc0_j + acc1_j, then ((P0 + P1) + (P2 + P3)) + ((P4 + P5) + (P6 + P7))
+      float p[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        p[2 * k] = __fadd_rn(acc[tt][k].x, __shfl_xor_sync(0xffffffffu, acc[tt][k].x, 1));
+        p[2 * k + 1] = __fadd_rn(acc[tt][k].y, __shfl_xor_sync(0xffffffffu, acc[tt][k].y, 1));
+      }
+      int bin = -1;
+      if (half == 0 && active && tt < nt) {
+        const float h = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
+                                  __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+        const float* xt = lm_xt + tt * a.cols;
+        float tail = 0.0f;
+        for (int i = chunks * 16; i < a.cols; ++i)
+          tail = __fadd_rn(tail, __fmul_rn(__uint_as_float(uint32_t(wrow[i]) << 16), xt[i]));
+        const float v = __fadd_rn(h, tail);
+        const long long t = t0 + tt;
+        a.logits[t * a.rows + row] = v;
+        if (isnan(v)) atomicOr(a.flags + t * kLmTokWords, 1u);
+        bin = int(total_ukey(v) >> 20);
+      }
+      const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && lane == __ffs(peers) - 1)
+        atomicAdd(reinterpret_cast<int*>(a.flags + (long long)(t0 + tt) * kLmTokWords + 4) + bin,
+                  __popc(peers));
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// The arguments of token t of a several-token call (t = 0: the call itself).
+__device__ __forceinline__ LmHeadArgs lm_token(const LmHeadArgs& a0, int t) {
+  LmHeadArgs a = a0;
+  if (t > 0) {
+    a.x = a0.x + (long long)t * a0.ldx;
+    a.logits = a0.logits + (long long)t * a0.rows;
+    a.flags = a0.flags + (long long)t * kLmTokWords;
+    a.counter = a.flags + 1;
+    a.cand_count = a.flags + 2;
+    a.hist = reinterpret_cast<int*>(a.flags + 4);
+    a.cand = a0.cand + (long long)t * kLmSelCap;
+    a.out_tokens = a0.out_tokens + (long long)t * a0.top_k;
+    a.out_logits = a0.out_logits + (long long)t * a0.top_k;
+  }
+  return a;
+}
+
 // in-place ascending bitonic sort of n (a power of two) keys in shared memory
 __device__ void bitonic_sort(uint64_t* k, int n) {
   for (int size = 2; size <= n; size <<= 1) {
@@ -211,11 +325,10 @@ __device__ void lm_replay(const LmHeadArgs& a, uint32_t* best_row, float* best_v
 // The rows whose logit lies in the histogram bin that leaves at least k+1
 // rows at or above it, or in a higher bin: about k+1 plus the few that share
 // the boundary bin.  Every CTA finds the bin from the histogram itself.
-constexpr int kLmSelCap = 8192;
-constexpr int kLmBins = 4096;
 constexpr int kLmCollectRows = 8 * 1024;  // rows per collect CTA
 
-__global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
+__global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a0) {
+  const LmHeadArgs a = lm_token(a0, blockIdx.y);
   __shared__ int s_bin;
   __shared__ int hist[kLmBins];
   const int tid = threadIdx.x, lane = tid & 31;
@@ -269,7 +382,8 @@ __global__ void __launch_bounds__(1024) lm_collect_kernel(LmHeadArgs a) {
 // the (k+1)-th (IEEE comparison) and no logit is NaN, the reference's result
 // is exactly the sorted top k; ties, NaNs or more candidates than fit take the
 // exact replay of push_topk_candidate.
-__global__ void __launch_bounds__(256) lm_select_kernel(LmHeadArgs a) {
+__global__ void __launch_bounds__(256) lm_select_kernel(LmHeadArgs a0) {
+  const LmHeadArgs a = lm_token(a0, blockIdx.x);
   extern __shared__ __align__(16) uint64_t lm_sel[];  // cand[kLmSelCap] | replay state
   __shared__ int s_n;
   uint64_t* cand = lm_sel;
@@ -369,6 +483,63 @@ cudaError_t launch_lm_head_stage(const LmHeadArgs& a, int stage, bool pdl, cudaS
       e = ensure_smem(lm_select_kernel, cfg.dynamicSmemBytes);
       return e != cudaSuccess ? e : cudaLaunchKernelEx(&cfg, lm_select_kernel, a);
   }
+}
+
+size_t lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens) {
+  (void)top_k;
+  return 1024 + size_t(tokens) * (size_t(rows) * 4 + size_t(kLmTokWords) * 4 +
+                                  size_t(kLmSelCap) * 8);
+}
+
+// Tokens per weight pass: as many as fit (with x) in 192 KB of shared memory.
+static int lm_batch_tile(int cols) {
+  const size_t bytes = size_t(cols) * 4;
+  return bytes * 8 <= 192 * 1024 ? 8 : bytes * 4 <= 192 * 1024 ? 4 : bytes * 2 <= 192 * 1024 ? 2 : 1;
+}
+
+template <int TB>
+static cudaError_t launch_lm_logits_batch(const LmHeadArgs& a, cudaLaunchConfig_t cfg) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long passes = (a.rows + kLmRowsPerWarp - 1) / kLmRowsPerWarp;
+  const int tiles = (a.tokens + TB - 1) / TB;
+  const long long per_tile = std::max<long long>(1, sms / tiles);
+  cfg.blockDim = dim3(lm_batch_threads<TB>());
+  cfg.gridDim = dim3(unsigned(std::min<long long>(per_tile, (passes + 15) / 16)), tiles);
+  cfg.dynamicSmemBytes = size_t(TB) * a.cols * 4;
+  cudaError_t e = ensure_smem(lm_logits_batch_kernel<TB>, cfg.dynamicSmemBytes);
+  return e != cudaSuccess ? e : cudaLaunchKernelEx(&cfg, lm_logits_batch_kernel<TB>, a);
+}
+
+// Several tokens: the logits of every token (weights streamed once per tile of
+// tokens), then the candidates and the selection of every token, one grid each.
+cudaError_t launch_lm_head_batch(const LmHeadArgs& a, bool pdl, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
+  cudaError_t e;
+  switch (lm_batch_tile(a.cols)) {
+    case 8: e = launch_lm_logits_batch<8>(a, cfg); break;
+    case 4: e = launch_lm_logits_batch<4>(a, cfg); break;
+    case 2: e = launch_lm_logits_batch<2>(a, cfg); break;
+    default: e = launch_lm_logits_batch<1>(a, cfg); break;
+  }
+  if (e != cudaSuccess) return e;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.blockDim = dim3(1024);
+  cfg.gridDim = dim3(unsigned((a.rows + kLmCollectRows - 1) / kLmCollectRows), a.tokens);
+  cfg.dynamicSmemBytes = 0;
+  if ((e = cudaLaunchKernelEx(&cfg, lm_collect_kernel, a)) != cudaSuccess) return e;
+  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(a.tokens);
+  cfg.dynamicSmemBytes = size_t(kLmSelCap) * 8 + 2 * (kLmMaxK + 1) * 4;
+  if ((e = ensure_smem(lm_select_kernel, cfg.dynamicSmemBytes)) != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, lm_select_kernel, a);
 }
 
 }  // namespace wh

@@ -16,7 +16,7 @@ src/compute.rs:1644-1700):
     x = hc_post(y, residual, post, comb)
 
 and after the last layer the pooled head (hc_head_pool, final norm) and the
-lm_head top-k (wh_lm_head_topk).  Every kernel is the bit-exact one, so the
+lm_head top-k of every sequence (wh_lm_head_topk_batch).  Every kernel is the bit-exact one, so the
 step equals the oracle's composition of the same functions.
 
 The step takes `batch` sequences, each at its own position with its own
@@ -32,7 +32,7 @@ from typing import List, Optional, Sequence
 
 from . import (DEEPSEEK_V4_HC_EPS, DEEPSEEK_V4_HC_SINKHORN_ITERS, Context, MoeLayer,
                V4Attention, deepseek_rope_for_layer, hc_head, hc_post, hc_pre,
-               lm_head_topk_score, rms_norm, rope_inv_freqs, v4_attention,
+               lm_head_topk_score_batch, rms_norm, rope_inv_freqs, v4_attention,
                v4_attention_scratch_len)
 
 
@@ -91,9 +91,8 @@ class V4Decoder:
         self.logits = torch.empty(B, max(top_k, 1), device=dev)
         from . import lib
 
-        self.lm_scratch = torch.empty(lib().wh_lm_head_scratch_bytes(lm_head.shape[0],
-                                                                      max(top_k, 1)),
-                                      dtype=torch.uint8, device=dev)
+        self.lm_scratch = torch.empty(lib().wh_lm_head_batch_scratch_bytes(
+            lm_head.shape[0], max(top_k, 1), B), dtype=torch.uint8, device=dev)
 
     def step(self, x, positions: Sequence[int]):
         """One decode position per sequence: x [batch, hc*hidden] is the
@@ -123,9 +122,10 @@ class V4Decoder:
         fn, scale, base = self.head
         hc_head(c, fn, scale, base, x, hc, H, DEEPSEEK_V4_HC_EPS, out=self.pooled)
         rms_norm(c, self.pooled, self.final_norm, out=self.pooled)
-        for b in range(self.batch):
-            t, v = lm_head_topk_score(c, self.lm_head, self.pooled[b], self.top_k,
-                                      scratch=self.lm_scratch)
-            self.tokens[b, :t.numel()].copy_(t)
-            self.logits[b, :v.numel()].copy_(v)
+        # every sequence's lm_head top-k in one call: the 129280 x 4096 weight
+        # streams once per tile of 8 sequences, not once per sequence
+        t, v = lm_head_topk_score_batch(c, self.lm_head, self.pooled, self.top_k,
+                                        scratch=self.lm_scratch)
+        self.tokens[:, :t.shape[1]].copy_(t)
+        self.logits[:, :v.shape[1]].copy_(v)
         return self.tokens, self.logits
