@@ -119,6 +119,34 @@ def test_grouped_v4_shape(ctx, W):
         layer.close()
 
 
+@pytest.mark.parametrize("T", [32, 64])
+def test_grouped_batched_decode_small_tiles(ctx, W, T):
+    # batched decode: at most 4 routes per expert on average, so the 16-token
+    # tiles run with the batched (ascending expert id) combine
+    E, Hd, I = 128, 1024, 512
+    stack = H.torch_fp4_experts(85 + T, E + 1, Hd, I)
+    gate = H.router_gate(86, E, Hd)
+    x = H.activations(87 + T, T, Hd)
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
+    try:
+        _check(ctx, W, layer, stack, gate, x, E, Hd, I)
+    finally:
+        layer.close()
+
+
+def test_grouped_v4_batch32_decode(ctx, W):
+    # the decode step's batch-32 MoE: 256 V4-shape experts + shared, 32 tokens
+    E, Hd, I, T = 256, 4096, 2048, 32
+    stack = H.torch_fp4_experts(88, E + 1, Hd, I)
+    gate = H.router_gate(89, E, Hd)
+    x = H.activations(90, T, Hd)
+    layer = _layer(W, ctx, stack, gate, E, Hd, I, T)
+    try:
+        _check(ctx, W, layer, stack, gate, x, E, Hd, I, sample=list(range(0, T, 4)))
+    finally:
+        layer.close()
+
+
 def test_grouped_config3_shape(ctx, W):
     """BASELINE config 3 at its own shape: 256 experts + shared, 4096 -> 2048 ->
     4096, 2048 tokens with Zipf(1.1)-skewed routing (12,288 routed rows, uneven

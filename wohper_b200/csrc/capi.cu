@@ -1324,8 +1324,15 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
 }
 }  // namespace
 
-// decode-sized calls: 16-token tiles and the single-token (route-order) combine
-int grouped_tile_n(int tokens) { return tokens < kGroupedMinTokens ? kGNSmall : kGN; }
+// 16-token tiles while the routed experts average at most 4 rows (decode-sized
+// calls and batched decode: each expert's weights stream and convert once per
+// tile, and a 128-token tile would carry mostly empty columns); 128-token
+// tiles beyond that.
+int grouped_tile_n(const wh_moe_plan* p, int tokens) {
+  return (tokens < kGroupedMinTokens || (long long)tokens * p->d.topk <= 4LL * p->d.num_experts)
+             ? kGNSmall
+             : kGN;
+}
 
 struct GroupedScratch {
   float* logits;
@@ -1350,7 +1357,7 @@ GroupedScratch grouped_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base
   const auto& d = p->d;
   const int ne = d.num_experts + (d.shared ? 1 : 0);
   const int R = T * d.topk + (d.shared ? T : 0);
-  const size_t tiles = size_t(R) / grouped_tile_n(T) + 1 + ne;  // >= sum of ceil(rows/tile)
+  const size_t tiles = size_t(R) / grouped_tile_n(p, T) + 1 + ne;  // >= sum of ceil(rows/tile)
   GroupedScratch s{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1469,7 +1476,7 @@ wh_status moe_ffn_grouped(wh_ctx* c, const wh_moe_plan* p, const float* x, int t
   pa.n_units = g.n_units;
   pa.mt_up = d.inter / 128;
   pa.mt_down = d.hidden / 128;
-  pa.tile_n = grouped_tile_n(tokens);
+  pa.tile_n = grouped_tile_n(p, tokens);
   pa.route_order = tokens < kGroupedMinTokens;
   pa.status = c->status;
   CUtensorMap bup, bdown;

@@ -491,10 +491,13 @@ size_t lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens) {
                                   size_t(kLmSelCap) * 8);
 }
 
-// Tokens per weight pass: as many as fit (with x) in 192 KB of shared memory.
-static int lm_batch_tile(int cols) {
+// Tokens per weight pass: as many as fit (with x) in 192 KB of shared memory,
+// and no more than the call's token count rounded up to a power of two.
+static int lm_batch_tile(int cols, int tokens) {
   const size_t bytes = size_t(cols) * 4;
-  return bytes * 8 <= 192 * 1024 ? 8 : bytes * 4 <= 192 * 1024 ? 4 : bytes * 2 <= 192 * 1024 ? 2 : 1;
+  int tb = bytes * 8 <= 192 * 1024 ? 8 : bytes * 4 <= 192 * 1024 ? 4 : bytes * 2 <= 192 * 1024 ? 2 : 1;
+  while (tb > 1 && tb / 2 >= tokens) tb /= 2;
+  return tb;
 }
 
 template <int TB>
@@ -515,6 +518,11 @@ static cudaError_t launch_lm_logits_batch(const LmHeadArgs& a, cudaLaunchConfig_
 // Several tokens: the logits of every token (weights streamed once per tile of
 // tokens), then the candidates and the selection of every token, one grid each.
 cudaError_t launch_lm_head_batch(const LmHeadArgs& a, bool pdl, cudaStream_t s) {
+  if (a.tokens == 1) {  // token 0's words are the single call's layout
+    cudaError_t e = cudaSuccess;
+    for (int stage = 0; stage < 3 && e == cudaSuccess; ++stage) e = launch_lm_head_stage(a, stage, pdl, s);
+    return e;
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -523,7 +531,7 @@ cudaError_t launch_lm_head_batch(const LmHeadArgs& a, bool pdl, cudaStream_t s) 
   cfg.attrs = attr;
   cfg.numAttrs = 0;
   cudaError_t e;
-  switch (lm_batch_tile(a.cols)) {
+  switch (lm_batch_tile(a.cols, a.tokens)) {
     case 8: e = launch_lm_logits_batch<8>(a, cfg); break;
     case 4: e = launch_lm_logits_batch<4>(a, cfg); break;
     case 2: e = launch_lm_logits_batch<2>(a, cfg); break;
