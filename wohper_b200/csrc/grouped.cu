@@ -37,8 +37,21 @@ constexpr int kGNSmall = 16;    // tokens per tile for decode-sized batches
 template <int kN>
 struct GStages { static constexpr int value = kN <= 16 ? 8 : 4; };
 constexpr int kGConv = 2;       // converted-A ring depth
-constexpr int kGWork = 16;      // converter + epilogue warps
-constexpr int kGThreads = (kGWork + 2) * 32;  // + TMA producer warp + MMA warp
+constexpr int kGWork = 16;      // converter + epilogue warps (128-token tiles)
+// Warp roles.  128-token tiles: 16 warps convert and then run the unit's
+// epilogue, one TMEM accumulator.  16-token tiles: the epilogue (SwiGLU with
+// the exact expf, act quant, stores) takes about a third of a unit and is
+// latency-bound, so 4 warps (TMEM lane quadrants 0-3) run it alone on one of two
+// accumulators while 8 converter warps and the MMA go on with the next unit.
+// Then come the TMA producer warp and the MMA warp.
+template <int kN>
+struct GWarps {
+  static constexpr bool split = kN <= 16;
+  static constexpr int epi = split ? 4 : 0;     // epilogue-only warps
+  static constexpr int conv = split ? 8 : kGWork;  // converter warps
+  static constexpr int acc_bufs = split ? 2 : 1;
+  static constexpr int threads = (epi + conv + 2) * 32;
+};
 constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
 constexpr int kGConvA = 128 * 128;  // E4M3 A tile
 
@@ -80,7 +93,7 @@ struct GroupedSmem {
   static constexpr int kSfStage = (kUp ? 3 : 2) * 512;
   static constexpr size_t kBytes = 1024 + size_t(kGStages) * kRawStage +
                                    size_t(kGConv) * kConvStage + size_t(kGConv) * kSfStage +
-                                   (2 * kGStages + 2 * kGConv + 3 + kGWork / 2) * 8 + 16 +
+                                   (2 * kGStages + 2 * kGConv + 5 + kGWork / 2) * 8 + 16 +
                                    2 * kGWork * 16 * 4;
 };
 
@@ -97,26 +110,26 @@ __device__ __forceinline__ uint2 fp4x8_to_e4m3x8(uint32_t w) {
 }
 
 // FP4 tiles [128 rows][64 B] -> E4M3 [128 rows][128 B] with 128-byte
-// swizzle; 32 * kGWork threads, 512 / (32 * kGWork) 16-byte chunks of each
+// swizzle; 32 * kWork threads, 512 / (32 * kWork) 16-byte chunks of each
 // of the kMats tiles per thread.  Every load is issued before the first
 // conversion.
-template <int kMats>
+template <int kMats, int kWork>
 __device__ __forceinline__ void convert_tiles(const uint8_t* raw, int raw_stride, uint8_t* dst,
                                               int dst_stride, int tid) {
-  constexpr int kPer = 512 / (32 * kGWork);
+  constexpr int kPer = 512 / (32 * kWork);
   uint4 v[kMats][kPer];
 #pragma unroll
   for (int m = 0; m < kMats; ++m)
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int i = tid + 32 * kGWork * j;
+      const int i = tid + 32 * kWork * j;
       v[m][j] = *reinterpret_cast<const uint4*>(raw + m * raw_stride + (i >> 2) * 64 + (i & 3) * 16);
     }
 #pragma unroll
   for (int m = 0; m < kMats; ++m)
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int i = tid + 32 * kGWork * j;
+      const int i = tid + 32 * kWork * j;
       const int r = i >> 2, ch = i & 3;
       const uint2 a = fp4x8_to_e4m3x8(v[m][j].x), b = fp4x8_to_e4m3x8(v[m][j].y);
       const uint2 c = fp4x8_to_e4m3x8(v[m][j].z), d = fp4x8_to_e4m3x8(v[m][j].w);
@@ -161,11 +174,15 @@ __device__ __forceinline__ uint32_t e4m3x2_ref(float lo, float hi) {
 }
 
 template <bool kUp, int kN>
-__global__ void __launch_bounds__(kGThreads, 1)
+__global__ void __launch_bounds__(GWarps<kN>::threads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap bmap, GroupedArgs a) {
   using L = GroupedSmem<kUp, kN>;
   constexpr int kGB = L::kGB;
   constexpr int kGStages = L::kGStages;
+  using WR = GWarps<kN>;
+  constexpr int kEpiW = WR::epi, kConvW = WR::conv, kAccBufs = WR::acc_bufs;
+  constexpr int kProducer = kEpiW + kConvW, kMmaWarp = kProducer + 1;
+  constexpr int kEpiWarps = WR::split ? kEpiW : kConvW;  // warps that run epilogues
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* raw = smem;                                        // [stages][B | A1 | A3]
@@ -175,9 +192,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint64_t* raw_empty = raw_full + kGStages;
   uint64_t* conv_full = raw_empty + kGStages;
   uint64_t* conv_empty = conv_full + kGConv;
-  uint64_t* acc_full = conv_empty + kGConv;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* mma_done = acc_empty + 1;
+  uint64_t* acc_full = conv_empty + kGConv;  // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* mma_done = acc_empty + 2;
   uint64_t* pair_bar = mma_done + 1;  // [kGWork/2]: warps 2p, 2p+1 (act-quant amax exchange)
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(pair_bar + kGWork / 2);
   float* amax_s = reinterpret_cast<float*>(tmem_base_s + 4);  // [2 parity][8 warps][16]
@@ -186,19 +203,21 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ktiles = a.K / 128;
   constexpr int kMats = kUp ? 2 : 1;
-  for (int i = tid; i < 256; i += kGThreads) aq_thr[i] = c_aq.thr[i];
+  for (int i = tid; i < 256; i += WR::threads) aq_thr[i] = c_aq.thr[i];
 
   if (tid == 0) {
     for (int s = 0; s < kGStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kGWork + 1);
+      mbar_init(&raw_empty[s], kConvW + 1);
     }
     for (int c = 0; c < kGConv; ++c) {
-      mbar_init(&conv_full[c], kGWork);
+      mbar_init(&conv_full[c], kConvW);
       mbar_init(&conv_empty[c], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kGWork);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
     mbar_init(mma_done, 1);
     for (int p = 0; p < kGWork / 2; ++p) mbar_init(&pair_bar[p], 64);
     fence_barrier_init();
@@ -213,7 +232,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const uint32_t tmem = *tmem_base_s;
   const int n_units = *a.n_units;
 
-  if (warp == kGWork) {
+  if (warp == kProducer) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       bool ok = true;
@@ -242,14 +261,17 @@ __global__ void __launch_bounds__(kGThreads, 1)
       for (uint32_t i = g > kGStages ? g - kGStages : 0; i < g; ++i)
         if (!mbar_drain(&raw_full[i % kGStages], (i / kGStages) & 1, a.status)) break;
     }
-  } else if (warp == kGWork + 1) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
       uint32_t g = 0, gc = 0, nu = 0;
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
-        if (nu > 0 && !mbar_wait(acc_empty, (nu - 1) & 1, a.status)) break;
+        const uint32_t ab = nu % kAccBufs;
+        if (nu >= kAccBufs && !mbar_wait(&acc_empty[ab], ((nu / kAccBufs) - 1) & 1, a.status))
+          break;
         tc::fence_after_sync();
+        const uint32_t tacc = tmem + ab * 2 * kN;
         for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
           const int s = g % kGStages, c = gc % kGConv;
           if (!mbar_wait(&conv_full[c], (gc / kGConv) & 1, a.status) ||
@@ -258,7 +280,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             break;
           }
           tc::fence_after_sync();
-          const uint32_t tsf = tmem + 2 * kN + 16 * c;
+          const uint32_t tsf = tmem + kAccBufs * 2 * kN + 16 * c;
           const uint8_t* sf = sfs + c * L::kSfStage;
           tc::cp_sf_block(tsf, tc::desc_sf_block(smem_u32(sf)));
           if (kUp) tc::cp_sf_block(tsf + 4, tc::desc_sf_block(smem_u32(sf + 512)));
@@ -271,89 +293,33 @@ __global__ void __launch_bounds__(kGThreads, 1)
             const uint32_t acc = (kt | k) != 0;
             const uint32_t id = tc::idesc_mxf8(kN, k, k);
             const uint64_t db = tc::desc_sw128(smem_u32(bt + 32 * k));
-            tc::mma_mxf8(tmem, tc::desc_sw128(smem_u32(ct + 32 * k)), db, id,
+            tc::mma_mxf8(tacc, tc::desc_sw128(smem_u32(ct + 32 * k)), db, id,
                          tsf | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
             if (kUp)
-              tc::mma_mxf8(tmem + kN, tc::desc_sw128(smem_u32(ct + kGConvA + 32 * k)), db, id,
+              tc::mma_mxf8(tacc + kN, tc::desc_sw128(smem_u32(ct + kGConvA + 32 * k)), db, id,
                            (tsf + 4) | (uint32_t(k) << 30), tsfb | (uint32_t(k) << 30), acc);
           }
           tc::commit(&conv_empty[c]);
           tc::commit(&raw_empty[s]);
         }
-        if (ok) tc::commit(acc_full);
+        if (ok) tc::commit(&acc_full[ab]);
       }
       // every MMA and scale copy has finished before TMEM is released
       tc::commit(mma_done);
       mbar_wait(mma_done, 0, a.status);
     }
   } else {
-    // ------- converters + epilogue: warp w reads TMEM lanes 32*(w%4).., -------
-    // ------- columns [64*(w/4), +64) of the accumulators                  -------
-    bool ok = true;
-    uint32_t g = 0, gc = 0, nu = 0, chunk = 0;
-    // scale factors: threads 0-127 stage SFA1 (+ SFB) of row tid, threads
-    // 128-255 stage SFA3 of row tid-128, the others none
-    const int r = tid & 127;
-    const bool second = tid >= 128;
-    const bool stages_sf = tid < 256;
-    const int sfk = a.K / 32;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
-      const int4 un = a.units[u];
-      const Fp4ExpertDev& ex = a.experts[un.x];
-      const uint8_t* sfa = (second ? ex.w3_scale : (kUp ? ex.w1_scale : ex.w2_scale)) +
-                           (long long)(un.y * 128 + r) * sfk;
-      const bool need_a = stages_sf && (!second || kUp);
-      const bool brow_ok = un.z + r < a.rows_total;
-      const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * a.bsf_stride;
-      // scale bytes of 4 K tiles per 16-byte load, one group ahead
-      auto sf_group = [&](int kt0, uint4& qa, uint4& qb) {
-        qa = need_a ? __ldg(reinterpret_cast<const uint4*>(sfa + kt0 * 4)) : make_uint4(0, 0, 0, 0);
-        qb = (!second && stages_sf && brow_ok) ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
-                                  : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
-      };
-      uint4 ca, cb, na, nb;
-      sf_group(0, na, nb);
-      for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
-        const int s = g % kGStages, c = gc % kGConv;
-        if ((kt & 3) == 0) {
-          ca = na;
-          cb = nb;
-          if (kt + 4 < ktiles) sf_group(kt + 4, na, nb);
-        }
-        if (!mbar_wait(&raw_full[s], (g / kGStages) & 1, a.status) ||
-            (gc >= kGConv && !mbar_wait(&conv_empty[c], ((gc / kGConv) - 1) & 1, a.status))) {
-          ok = false;
-          break;
-        }
-        const uint8_t* st = raw + s * L::kRawStage;
-        uint8_t* ct = conv + c * L::kConvStage;
-        convert_tiles<kMats>(st + kGB, kGRawA, ct, kGConvA, tid);
-        uint8_t* sf = sfs + c * L::kSfStage;
-        const int atom = (r & 31) * 16 + (r >> 5) * 4;
-        if (!stages_sf) {
-        } else if (!second) {
-          *reinterpret_cast<uint32_t*>(sf + atom) = pick4(ca, kt & 3);
-          *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = pick4(cb, kt & 3);
-        } else if (kUp) {
-          *reinterpret_cast<uint32_t*>(sf + 512 + atom) = pick4(ca, kt & 3);
-        }
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&conv_full[c]);
-          mbar_arrive(&raw_empty[s]);
-        }
-      }
-      // ---------------- epilogue ----------------
-      if (ok) ok = mbar_wait(acc_full, nu & 1, a.status);
-      if (!ok) break;
-      tc::fence_after_sync();
+    // ------- epilogue: warp w reads TMEM lanes 32*(w%4).. and, with 16 -------
+    // ------- epilogue warps, columns [kN/4*(w/4), +kN/4) of the tile    -------
+    uint32_t chunk = 0;  // act-quant exchange parity
+    auto epilogue = [&](const int4& un, uint32_t tacc) -> bool {
+      bool ok = true;
       const int q4 = warp & 3;
       const int feat = un.y * 128 + q4 * 32 + lane;
-      const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-      // columns of this warp: the tile split over the kGWork/4 groups of 4
+      const uint32_t trow = tacc + ((uint32_t)(q4 * 32) << 16);
+      // columns of this warp: the tile split over the kEpiWarps/4 groups of 4
       // warps in 16-column chunks (the small tile's single chunk goes to warps 0-3)
-      constexpr int kGroups = kGWork / 4;
+      constexpr int kGroups = kEpiWarps / 4;
       constexpr int kCols = kN / kGroups >= 16 ? kN / kGroups : 16;
       const int col0 = (warp >> 2) * kCols;
       for (int n0 = col0; n0 < col0 + kCols && n0 < kN; n0 += 16) {
@@ -428,9 +394,93 @@ __global__ void __launch_bounds__(kGThreads, 1)
             }
         }
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      return ok;
+    };
+    if constexpr (WR::split) {
+      if (warp < kEpiW) {
+        // ---------------- epilogue warps ----------------
+        bool ok = true;
+        uint32_t nu = 0;
+        for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
+          const uint32_t ab = nu % kAccBufs;
+          if (!mbar_wait(&acc_full[ab], (nu / kAccBufs) & 1, a.status)) break;
+          tc::fence_after_sync();
+          ok = epilogue(a.units[u], tmem + ab * 2 * kN);
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        }
+      }
+    }
+    if (WR::split ? warp >= kEpiW : true) {
+      // ---------------- converters (128-token tiles: then the epilogue) ----------------
+      const int ctid = tid - 32 * kEpiW;
+      bool ok = true;
+      uint32_t g = 0, gc = 0, nu = 0;
+      // scale factors: converter threads 0-127 stage SFA1 (+ SFB) of row ctid,
+      // threads 128-255 stage SFA3 of row ctid-128, the others none
+      const int r = ctid & 127;
+      const bool second = ctid >= 128;
+      const bool stages_sf = ctid < 256;
+      const int sfk = a.K / 32;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
+        const int4 un = a.units[u];
+        const Fp4ExpertDev& ex = a.experts[un.x];
+        const uint8_t* sfa = (second ? ex.w3_scale : (kUp ? ex.w1_scale : ex.w2_scale)) +
+                             (long long)(un.y * 128 + r) * sfk;
+        const bool need_a = stages_sf && (!second || kUp);
+        const bool brow_ok = un.z + r < a.rows_total;
+        const uint8_t* sfb = a.bsf + (long long)(brow_ok ? un.z + r : 0) * a.bsf_stride;
+        // scale bytes of 4 K tiles per 16-byte load, one group ahead
+        auto sf_group = [&](int kt0, uint4& qa, uint4& qb) {
+          qa = need_a ? __ldg(reinterpret_cast<const uint4*>(sfa + kt0 * 4)) : make_uint4(0, 0, 0, 0);
+          qb = (!second && stages_sf && brow_ok) ? __ldg(reinterpret_cast<const uint4*>(sfb + kt0 * 4))
+                                    : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+        };
+        uint4 ca, cb, na, nb;
+        sf_group(0, na, nb);
+        for (int kt = 0; kt < ktiles; ++kt, ++g, ++gc) {
+          const int s = g % kGStages, c = gc % kGConv;
+          if ((kt & 3) == 0) {
+            ca = na;
+            cb = nb;
+            if (kt + 4 < ktiles) sf_group(kt + 4, na, nb);
+          }
+          if (!mbar_wait(&raw_full[s], (g / kGStages) & 1, a.status) ||
+              (gc >= kGConv && !mbar_wait(&conv_empty[c], ((gc / kGConv) - 1) & 1, a.status))) {
+            ok = false;
+            break;
+          }
+          const uint8_t* st = raw + s * L::kRawStage;
+          uint8_t* ct = conv + c * L::kConvStage;
+          convert_tiles<kMats, kConvW>(st + kGB, kGRawA, ct, kGConvA, ctid);
+          uint8_t* sf = sfs + c * L::kSfStage;
+          const int atom = (r & 31) * 16 + (r >> 5) * 4;
+          if (!stages_sf) {
+          } else if (!second) {
+            *reinterpret_cast<uint32_t*>(sf + atom) = pick4(ca, kt & 3);
+            *reinterpret_cast<uint32_t*>(sf + (kUp ? 1024 : 512) + atom) = pick4(cb, kt & 3);
+          } else if (kUp) {
+            *reinterpret_cast<uint32_t*>(sf + 512 + atom) = pick4(ca, kt & 3);
+          }
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&conv_full[c]);
+            mbar_arrive(&raw_empty[s]);
+          }
+        }
+        if constexpr (!WR::split) {
+          // ---------------- epilogue ----------------
+          if (ok) ok = mbar_wait(&acc_full[0], nu & 1, a.status);
+          if (!ok) break;
+          tc::fence_after_sync();
+          ok = epilogue(un, tmem);
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[0]);
+        }
+      }
     }
   }
   tc::fence_before_sync();
@@ -640,7 +690,7 @@ cudaError_t launch_grouped_t(const CUtensorMap& bmap, const GroupedArgs& a, int 
   const size_t smem = GroupedSmem<kUp, kN>::kBytes;
   cudaError_t e = ensure_smem(grouped_gemm_kernel<kUp, kN>, smem);
   if (e != cudaSuccess) return e;
-  grouped_gemm_kernel<kUp, kN><<<num_sms, kGThreads, smem, s>>>(bmap, a);
+  grouped_gemm_kernel<kUp, kN><<<num_sms, GWarps<kN>::threads, smem, s>>>(bmap, a);
   return cudaGetLastError();
 }
 
