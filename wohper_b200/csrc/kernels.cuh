@@ -28,6 +28,10 @@ struct ExpfTable {
   const float* vals;
   const uint32_t* bucket;  // [2^20 + 1]: first key index of each (bits >> 12) bucket
   int n;
+  // relative distance from a rounding midpoint within which x is looked up: a
+  // power of two at least twice the farthest host difference measured, and at
+  // least the 2^-44 band the table holds in full
+  double near;
 };
 constexpr int kExpfBucketShift = 12;
 constexpr uint32_t kExpfBuckets = 1u << (32 - kExpfBucketShift);
@@ -40,9 +44,9 @@ __device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
   const uint32_t cb = __float_as_uint(c);
   const double dc = (double)c;
   const double other = (double)__uint_as_float(yd > dc ? cb + 1u : cb - 1u);
-  if (fabs(yd - 0.5 * (dc + other)) <= yd * 0x1p-30) {
-    // near a rounding midpoint (about 0.6 % of inputs): x's bucket bounds, then
-    // a binary search over the bucket's few keys
+  if (fabs(yd - 0.5 * (dc + other)) <= yd * t.near) {
+    // near a rounding midpoint (about 0.14 % of inputs with glibc 2.39's
+    // 2^-32): x's bucket bounds, then a binary search over the bucket's few keys
     const uint32_t xb = __float_as_uint(x);
     const uint32_t b = xb >> kExpfBucketShift;
     int lo = (int)__ldg(t.bucket + b), hi = (int)__ldg(t.bucket + b + 1);

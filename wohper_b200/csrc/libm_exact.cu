@@ -15,11 +15,14 @@
 // within 2^-44 of a midpoint (there a one-ulp difference between the host's and
 // the device's double exp could flip the rounding).  The table is installed
 // once per device in constant memory (c_expf).  On the device, ref_expf rounds
-// exp((double)x) once and looks x up only when the result is within 2^-30 of a
-// midpoint, about 0.6 % of inputs: one load of x's bucket bounds (2^20 buckets
-// by the top 20 bits of x), then a binary search over that bucket's keys (65
-// at most for glibc 2.39, a few cache lines).  Outside (-104, 89) both sides
-// saturate to 0 or inf.  Every exp of the reference's arithmetic on this path
+// exp((double)x) once and looks x up only when the result is close to a
+// midpoint: one load of x's bucket bounds (2^20 buckets by the top 20 bits of
+// x), then a binary search over that bucket's keys (65 at most for glibc 2.39,
+// a few cache lines).  "Close" is a band measured with the table: the smallest
+// power of two at least twice the farthest relative distance from a midpoint
+// of any input where the two differ (2^-33.2 for glibc 2.39, so 2^-32: about
+// 0.14 % of inputs are looked up), and never below the 2^-44 band.  Outside
+// (-104, 89) both sides saturate to 0 or inf.  Every exp of the reference's arithmetic on this path
 // (SiLU, the router's softplus and softmax, the MLA softmax) goes through
 // libm_expf.
 #include <algorithm>
@@ -40,6 +43,7 @@ struct ExpfHostTable {
   std::vector<float> vals;     // the host expf(x)
   std::vector<uint32_t> bucket;  // first key index per (bits >> 12) bucket, plus n
   bool model_ok = true;          // every difference lies inside the device gate
+  double near = 0x1p-30;         // the device's lookup band (ExpfTable::near)
 };
 
 inline float bits_to_float(uint32_t u) {
@@ -54,7 +58,7 @@ inline uint32_t float_to_bits(float f) {
 }
 
 void scan_expf_range(uint32_t lo, uint32_t hi, std::vector<uint32_t>& keys,
-                     std::vector<float>& vals, bool& ok) {
+                     std::vector<float>& vals, bool& ok, double& far) {
   for (uint32_t u = lo; u < hi; ++u) {
     const float x = bits_to_float(u);
     const float g = expf(x);
@@ -69,6 +73,7 @@ void scan_expf_range(uint32_t lo, uint32_t hi, std::vector<uint32_t>& keys,
       keys.push_back(u);
       vals.push_back(g);
       if (differs && !(dist <= yd * 0x1p-30)) ok = false;
+      if (differs) far = std::max(far, dist / yd);
     }
   }
 }
@@ -89,6 +94,7 @@ const ExpfHostTable& expf_host_table() {
     std::vector<std::vector<uint32_t>> ck(chunks.size());
     std::vector<std::vector<float>> cv(chunks.size());
     std::vector<char> cok(chunks.size(), 1);
+    std::vector<double> cfar(chunks.size(), 0.0);
     std::atomic<size_t> next{0};
     unsigned nt = std::max(1u, std::thread::hardware_concurrency());
     std::vector<std::thread> pool;
@@ -96,7 +102,7 @@ const ExpfHostTable& expf_host_table() {
       pool.emplace_back([&] {
         for (size_t i = next++; i < chunks.size(); i = next++) {
           bool ok = true;
-          scan_expf_range(chunks[i].first, chunks[i].second, ck[i], cv[i], ok);
+          scan_expf_range(chunks[i].first, chunks[i].second, ck[i], cv[i], ok, cfar[i]);
           cok[i] = ok;
         }
       });
@@ -106,6 +112,12 @@ const ExpfHostTable& expf_host_table() {
       table.vals.insert(table.vals.end(), cv[i].begin(), cv[i].end());
       if (!cok[i]) table.model_ok = false;
     }
+    // the lookup band: the smallest power of two >= twice the farthest
+    // difference (the device's double exp may sit an ulp of a double away from
+    // the host's), between 2^-44 (the band the table holds in full) and 2^-30
+    const double far = *std::max_element(cfar.begin(), cfar.end());
+    table.near = 0x1p-44;
+    while (table.near < 2.0 * far && table.near < 0x1p-30) table.near *= 2.0;
     table.bucket.resize((size_t)kExpfBuckets + 1);
     size_t k = 0;
     for (uint64_t b = 0; b <= kExpfBuckets; ++b) {
@@ -133,6 +145,8 @@ bool expf_bucket_host(const uint32_t** bucket) {
   return expf_host_table().model_ok;
 }
 
+double expf_near_host() { return expf_host_table().near; }
+
 bool install_expf_table(cudaError_t* err) {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
@@ -153,7 +167,7 @@ bool install_expf_table(cudaError_t* err) {
   void* mem = nullptr;
   if ((*err = cudaMalloc(&mem, kb + vb + bb)) != cudaSuccess) return true;
   const ExpfTable t{(const uint32_t*)mem, (const float*)((char*)mem + kb),
-                    (const uint32_t*)((char*)mem + kb + vb), n};
+                    (const uint32_t*)((char*)mem + kb + vb), n, expf_near_host()};
   if ((*err = cudaMemcpy(mem, keys, kb, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (*err = cudaMemcpy((char*)mem + kb, vals, vb, cudaMemcpyHostToDevice)) != cudaSuccess ||
       (*err = cudaMemcpy((char*)mem + kb + vb, bucket, bb, cudaMemcpyHostToDevice)) !=
