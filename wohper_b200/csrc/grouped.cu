@@ -30,26 +30,31 @@ namespace wh {
 constexpr int kGroupedMinTokens = 32;
 // K (hidden and inter) must be a multiple of 512: scale bytes are read 16 at a
 // time (4 K tiles of 128)
-constexpr int kGN = 128;        // tokens per tile (MMA N) of batches
+// tokens per tile (MMA N) of batches: 112, not 128, so that two accumulator
+// sets of both up matrices (2 x 2 x 112 columns) and the scale columns fit in
+// TMEM's 512 columns
+constexpr int kGN = 112;
 constexpr int kGNSmall = 16;    // tokens per tile for decode-sized batches
 // TMA ring depth (raw FP4 A + E4M3 B per K tile): deeper for the small tile,
-// whose stages are smaller
-template <int kN>
-struct GStages { static constexpr int value = kN <= 16 ? 8 : 4; };
-constexpr int kGConv = 2;       // converted-A ring depth
-constexpr int kGWork = 16;      // converter + epilogue warps (128-token tiles)
-// Warp roles.  128-token tiles: 16 warps convert and then run the unit's
-// epilogue, one TMEM accumulator.  16-token tiles: the epilogue (SwiGLU with
-// the exact expf, act quant, stores) takes about a third of a unit and is
-// latency-bound, so 4 warps (TMEM lane quadrants 0-3) run it alone on one of two
-// accumulators while 8 converter warps and the MMA go on with the next unit.
-// Then come the TMA producer warp and the MMA warp.
+// whose stages are smaller.  A third converted-A slot (at the cost of TMA
+// stages where shared memory is short) changed the 32-token layer by 1 % and
+// config 3 by less than its noise.
+template <bool kUp, int kN>
+struct GRing {
+  static constexpr int stages = kN <= 16 ? 8 : 4;
+  static constexpr int conv = 2;  // converted-A ring depth
+};
+constexpr int kGWork = 16;      // act-quant exchange slots (barrier pairs, amax rows)
+// Warp roles: epilogue-only warps (SwiGLU with the exact expf, act quant,
+// stores; latency-bound, a third of a unit's time or more) on one of two TMEM
+// accumulator sets, while 8 converter warps and the MMA go on with the next
+// unit; then the TMA producer warp and the MMA warp.  Epilogue warp w reads TMEM
+// lane quadrant w % 4; 16-token tiles take 4, the larger tiles 8 (two column
+// halves).
 template <int kN>
 struct GWarps {
-  static constexpr bool split = kN <= 16;
-  static constexpr int epi = split ? 4 : 0;     // epilogue-only warps
-  static constexpr int conv = split ? 8 : kGWork;  // converter warps
-  static constexpr int acc_bufs = split ? 2 : 1;
+  static constexpr int epi = kN <= 16 ? 4 : 8;
+  static constexpr int conv = 8;
   static constexpr int threads = (epi + conv + 2) * 32;
 };
 constexpr int kGRawA = 128 * 64;    // FP4 A tile: 128 rows x 128 K
@@ -86,7 +91,8 @@ struct GroupedArgs {
 
 template <bool kUp, int kN>
 struct GroupedSmem {
-  static constexpr int kGStages = GStages<kN>::value;
+  static constexpr int kGStages = GRing<kUp, kN>::stages;
+  static constexpr int kGConv = GRing<kUp, kN>::conv;
   static constexpr int kGB = kN * 128;  // E4M3 B tile (1024-byte multiple)
   static constexpr int kRawStage = kGB + (kUp ? 2 : 1) * kGRawA;
   static constexpr int kConvStage = (kUp ? 2 : 1) * kGConvA;
@@ -95,6 +101,8 @@ struct GroupedSmem {
                                    size_t(kGConv) * kConvStage + size_t(kGConv) * kSfStage +
                                    (2 * kGStages + 2 * kGConv + 5 + kGWork / 2) * 8 + 16 +
                                    2 * kGWork * 16 * 4;
+  static_assert(kBytes <= 232448, "grouped GEMM shared memory over 227 KB");
+  static_assert(2 * 2 * kN + 16 * kGConv <= 512, "two accumulator sets and the scales exceed TMEM");
 };
 
 // 8 FP4 codes (one 32-bit word, code i in bits 4i..4i+3) -> 8 E4M3 bytes of
@@ -179,10 +187,11 @@ __global__ void __launch_bounds__(GWarps<kN>::threads, 1)
   using L = GroupedSmem<kUp, kN>;
   constexpr int kGB = L::kGB;
   constexpr int kGStages = L::kGStages;
+  constexpr int kGConv = L::kGConv;
   using WR = GWarps<kN>;
-  constexpr int kEpiW = WR::epi, kConvW = WR::conv, kAccBufs = WR::acc_bufs;
+  constexpr int kEpiW = WR::epi, kConvW = WR::conv, kAccBufs = 2;
   constexpr int kProducer = kEpiW + kConvW, kMmaWarp = kProducer + 1;
-  constexpr int kEpiWarps = WR::split ? kEpiW : kConvW;  // warps that run epilogues
+  constexpr int kEpiWarps = kEpiW;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* raw = smem;                                        // [stages][B | A1 | A3]
@@ -309,8 +318,8 @@ __global__ void __launch_bounds__(GWarps<kN>::threads, 1)
       mbar_wait(mma_done, 0, a.status);
     }
   } else {
-    // ------- epilogue: warp w reads TMEM lanes 32*(w%4).. and, with 16 -------
-    // ------- epilogue warps, columns [kN/4*(w/4), +kN/4) of the tile    -------
+    // ------- epilogue: warp w reads TMEM lanes 32*(w%4).. and columns -------
+    // ------- [kCols*(w/4), +kCols) of the tile                         -------
     uint32_t chunk = 0;  // act-quant exchange parity
     auto epilogue = [&](const int4& un, uint32_t tacc) -> bool {
       bool ok = true;
@@ -320,7 +329,7 @@ __global__ void __launch_bounds__(GWarps<kN>::threads, 1)
       // columns of this warp: the tile split over the kEpiWarps/4 groups of 4
       // warps in 16-column chunks (the small tile's single chunk goes to warps 0-3)
       constexpr int kGroups = kEpiWarps / 4;
-      constexpr int kCols = kN / kGroups >= 16 ? kN / kGroups : 16;
+      constexpr int kCols = (kN / 16 + kGroups - 1) / kGroups * 16;  // whole 16-column chunks
       const int col0 = (warp >> 2) * kCols;
       for (int n0 = col0; n0 < col0 + kCols && n0 < kN; n0 += 16) {
         if (n0 >= un.w) break;  // every remaining column is past the expert's rows
@@ -396,24 +405,21 @@ __global__ void __launch_bounds__(GWarps<kN>::threads, 1)
       }
       return ok;
     };
-    if constexpr (WR::split) {
-      if (warp < kEpiW) {
-        // ---------------- epilogue warps ----------------
-        bool ok = true;
-        uint32_t nu = 0;
-        for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
-          const uint32_t ab = nu % kAccBufs;
-          if (!mbar_wait(&acc_full[ab], (nu / kAccBufs) & 1, a.status)) break;
-          tc::fence_after_sync();
-          ok = epilogue(a.units[u], tmem + ab * 2 * kN);
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[ab]);
-        }
+    if (warp < kEpiW) {
+      // ---------------- epilogue warps ----------------
+      bool ok = true;
+      uint32_t nu = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++nu) {
+        const uint32_t ab = nu % kAccBufs;
+        if (!mbar_wait(&acc_full[ab], (nu / kAccBufs) & 1, a.status)) break;
+        tc::fence_after_sync();
+        ok = epilogue(a.units[u], tmem + ab * 2 * kN);
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[ab]);
       }
-    }
-    if (WR::split ? warp >= kEpiW : true) {
-      // ---------------- converters (128-token tiles: then the epilogue) ----------------
+    } else {
+      // ---------------- converters ----------------
       const int ctid = tid - 32 * kEpiW;
       bool ok = true;
       uint32_t g = 0, gc = 0, nu = 0;
@@ -469,16 +475,6 @@ __global__ void __launch_bounds__(GWarps<kN>::threads, 1)
             mbar_arrive(&conv_full[c]);
             mbar_arrive(&raw_empty[s]);
           }
-        }
-        if constexpr (!WR::split) {
-          // ---------------- epilogue ----------------
-          if (ok) ok = mbar_wait(&acc_full[0], nu & 1, a.status);
-          if (!ok) break;
-          tc::fence_after_sync();
-          ok = epilogue(un, tmem);
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[0]);
         }
       }
     }
