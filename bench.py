@@ -2048,6 +2048,9 @@ def run_ncu_case(args):
            logits + candidates + selection per step.
     mla:   the MLA attention core at the bench's shape (10 MB of cache rows).
     mhc:   hc_pre + hc_post of one token at the bench's shape.
+    moe-batch: one wh_moe_ffn layer of 256 V4-shape experts + shared with
+           --batch tokens (softmax routing): the batched-decode grouped path
+           (32 tokens: 16-token tiles) or, from 171 tokens, 112-token tiles.
     L2 is flushed (256 MiB memset) before every step."""
     import torch
 
@@ -2086,6 +2089,24 @@ def run_ncu_case(args):
         for _ in range(n):
             flush.zero_()
             W.gemv_fp8_e4m3_ue8m0_tensorwise(ctx, wd, sd, x)
+    elif args.ncu_case == "moe-batch":
+        ne, T = E, args.batch
+        stack = H.torch_fp4_experts(88, ne + 1, HID, INTER)
+        gate = H.router_gate(89, ne, HID)
+
+        def wexp(e):
+            w1, s1, w3, s3, w2, s2 = H.expert_views(stack, e)
+            return W.DeepSeekV4Fp4Expert(W.Fp4Matvec(w1, s1, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w3, s3, INTER, HID, HID // 32),
+                                         W.Fp4Matvec(w2, s2, HID, INTER, INTER // 32))
+
+        layer = W.MoeLayer(ctx, [wexp(e) for e in range(ne)], wexp(ne),
+                           torch.from_numpy(gate.view(np.int16)).cuda(), topk=TOPK, max_tokens=T)
+        x = torch.from_numpy(H.activations(90, T, HID)).cuda()
+        for _ in range(n):
+            flush.zero_()
+            layer.forward(x)
+        layer.close()
     elif args.ncu_case == "grouped16":
         ne, T = 16, 256
         stack = H.torch_fp4_experts(5, ne + 1, HID, INTER)
@@ -2160,7 +2181,8 @@ def main():
     ap.add_argument("--shared", default="fp4", choices=["fp4", "fp8"],
                     help="config 2: the shared expert's format (fp4, as BASELINE's config 2; "
                          "fp8: DeepSeek-V4's FP8 shared expert)")
-    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "lmhead", "mla", "mhc"],
+    ap.add_argument("--ncu-case", choices=["fp8", "moe16", "grouped16", "moe-batch", "lmhead", "mla",
+                                           "mhc"],
                     help="run a small workload for an ncu capture instead of the bench")
     args = ap.parse_args()
     if args.ncu_case:

@@ -1046,9 +1046,103 @@ __global__ void __launch_bounds__(128) router_topk_kernel(RouterArgs a) {
                                [&](auto& sc) { router_load_global(a, t, lane, sc); });
 }
 
+// Router logits of a decode batch (up to 128 tokens): the 32 x 32 tiles above
+// give such a batch only experts/32 x tokens/32 CTAs (8 for 256 experts and 32
+// tokens), each walking the whole hidden dimension.  Here a warp owns 16
+// experts x TB tokens with two lanes per expert row, the lanes holding chains
+// 8h + j over columns 16c + 8h + j -- the same 16 chains in the same order as
+// the tile kernel's, summed the same way -- and the grid has experts/64 x
+// tokens/TB CTAs of four warps.  The gate rows are read through L2 (2 MB for
+// 256 x 4096), 16 chunks in flight per lane.
+constexpr int kRsWarps = 4;
+constexpr int kRsDepth = 16;
+template <int TB>
+__global__ void __launch_bounds__(32 * kRsWarps) router_logits_small_kernel(RouterArgs a) {
+  extern __shared__ __align__(16) float rs_x[];  // [TB][hidden]
+  const int t0 = blockIdx.y * TB;
+  const int nt = min(TB, a.tokens - t0);
+  for (int i = threadIdx.x * 4; i < TB * a.hidden; i += blockDim.x * 4) {
+    const int tt = i / a.hidden, col = i - tt * a.hidden;
+    *reinterpret_cast<float4*>(rs_x + i) =
+        tt < nt ? __ldg(reinterpret_cast<const float4*>(a.x + (long long)(t0 + tt) * a.hidden + col))
+                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane & 1;
+  const int e = (blockIdx.x * kRsWarps + warp) * 16 + (lane >> 1);
+  const bool active = e < a.experts;
+  const uint8_t* wp = reinterpret_cast<const uint8_t*>(a.gate + (long long)(active ? e : a.experts - 1) *
+                                                                    a.hidden) + 16 * half;
+  const int chunks = a.hidden / 16;
+  float2 acc[TB][4];
+#pragma unroll
+  for (int tt = 0; tt < TB; ++tt)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[tt][k] = make_float2(0.0f, 0.0f);
+  auto step = [&](const uint4 w, int c) {
+    const float2 w0 = make_float2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u));
+    const float2 w1 = make_float2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+    const float2 w2 = make_float2(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xffff0000u));
+    const float2 w3 = make_float2(__uint_as_float(w.w << 16), __uint_as_float(w.w & 0xffff0000u));
+#pragma unroll
+    for (int tt = 0; tt < TB; ++tt) {
+      const float* xp = rs_x + tt * a.hidden + 8 * half + 16 * c;
+      const float4 xa = *reinterpret_cast<const float4*>(xp);
+      const float4 xb = *reinterpret_cast<const float4*>(xp + 4);
+      acc[tt][0] = ffma2(w0, make_float2(xa.x, xa.y), acc[tt][0]);
+      acc[tt][1] = ffma2(w1, make_float2(xa.z, xa.w), acc[tt][1]);
+      acc[tt][2] = ffma2(w2, make_float2(xb.x, xb.y), acc[tt][2]);
+      acc[tt][3] = ffma2(w3, make_float2(xb.z, xb.w), acc[tt][3]);
+    }
+  };
+  int c = 0;
+  for (; c + kRsDepth <= chunks; c += kRsDepth) {
+    uint4 w[kRsDepth];
+#pragma unroll
+    for (int k = 0; k < kRsDepth; ++k) w[k] = __ldg(reinterpret_cast<const uint4*>(wp + 32 * (c + k)));
+#pragma unroll
+    for (int k = 0; k < kRsDepth; ++k) step(w[k], c + k);
+  }
+  for (; c < chunks; ++c) step(__ldg(reinterpret_cast<const uint4*>(wp + 32 * c)), c);
+#pragma unroll
+  for (int tt = 0; tt < TB; ++tt) {
+    // v_j = chain j + chain 8 + j (the partner lane), then
+    // ((v0 + v1) + (v2 + v3)) + ((v4 + v5) + (v6 + v7)), then the empty column tail
+    float p[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      p[2 * k] = __fadd_rn(acc[tt][k].x, __shfl_xor_sync(0xffffffffu, acc[tt][k].x, 1));
+      p[2 * k + 1] = __fadd_rn(acc[tt][k].y, __shfl_xor_sync(0xffffffffu, acc[tt][k].y, 1));
+    }
+    if (half == 0 && active && tt < nt) {
+      const float h = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
+                                __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+      a.logits[(long long)(t0 + tt) * a.experts + e] = __fadd_rn(h, 0.0f);
+    }
+  }
+}
+
+template <int TB>
+static cudaError_t launch_router_small(const RouterArgs& a, cudaStream_t s) {
+  const size_t smem = size_t(TB) * a.hidden * 4;
+  cudaError_t e = ensure_smem(router_logits_small_kernel<TB>, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((a.experts + 16 * kRsWarps - 1) / (16 * kRsWarps), (a.tokens + TB - 1) / TB);
+  router_logits_small_kernel<TB><<<grid, 32 * kRsWarps, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_router_batched(const RouterArgs& a, cudaStream_t s) {
-  dim3 grid((a.experts + kRbTile - 1) / kRbTile, (a.tokens + kRbTile - 1) / kRbTile);
-  router_logits_batched_kernel<<<grid, 256, 0, s>>>(a);
+  if (a.tokens <= 32 && a.hidden % 16 == 0) {
+    cudaError_t e = launch_router_small<2>(a, s);
+    if (e != cudaSuccess) return e;
+  } else if (a.tokens <= 128 && a.hidden % 16 == 0) {
+    cudaError_t e = launch_router_small<4>(a, s);
+    if (e != cudaSuccess) return e;
+  } else {
+    dim3 grid((a.experts + kRbTile - 1) / kRbTile, (a.tokens + kRbTile - 1) / kRbTile);
+    router_logits_batched_kernel<<<grid, 256, 0, s>>>(a);
+  }
   const int blocks = (a.tokens + 3) / 4;
   if (a.experts <= 32) router_topk_kernel<1><<<blocks, 128, 0, s>>>(a);
   else if (a.experts <= 64) router_topk_kernel<2><<<blocks, 128, 0, s>>>(a);
