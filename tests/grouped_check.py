@@ -16,7 +16,8 @@ oracle, counts the flips, and requires
     D = sum_k |c_k| |W2_k| |h_k|            (per output element),
 
 i.e. once the flips' exact effect is taken out, the rest is within the
-survey's normalised-error bound tol = 2e-6 (|y - y_hat| / sum|w x|).  It also
+grouped path's normalised-error bound tol = 2e-6 (|y - y_hat| / sum|w x|), the
+bound for a tensor-core accumulation order over K up to 4096.  It also
 reports the normalised error of the raw outputs and the flip count.
 """
 from __future__ import annotations
