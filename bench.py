@@ -859,6 +859,19 @@ def run_config5(args):
             W.hc_pre(ctx, *L.hc_ffn, x, 4, HID, out=(dec.y, dec.post, dec.comb))
             W.hc_post(ctx, dec.y, dec.resid, dec.post, dec.comb, 4, HID, out=dec.x2)
 
+    # this library's kernels in one replay of the step graph (CUPTI through the
+    # torch profiler, after the timed region)
+    launches_per_step = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            graph.replay()
+            torch.cuda.synchronize()
+        launches_per_step = sum(1 for ev in prof.events()
+                                if ev.device_type.name == "CUDA" and ev.name.startswith(("wh::", "void wh::")))
+    except Exception:  # the profiler is unavailable: the line says null
+        launches_per_step = None
     parts = {"attention_all_layers": round(part_ms(attn_only), 4),
              "moe_all_layers": round(part_ms(moe_only), 4),
              "mhc_all_layers": round(part_ms(mhc_only), 4)}
@@ -898,7 +911,9 @@ def run_config5(args):
                             "-> top-1 token ids to pinned host"},
             "graph_output_matches_direct_step": graph_ok,
             "build_s": round(build_s, 1),
-            "gpu_launches": None, "timing": "cuda graph of one step, replayed",
+            "gpu_launches": (launches_per_step * args.steps if launches_per_step else None),
+            "gpu_launches_per_step": launches_per_step,
+            "timing": "cuda graph of one step, replayed",
             "clocks": clk.summary(),
         }
     del graph
