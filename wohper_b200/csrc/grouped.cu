@@ -36,13 +36,13 @@ constexpr int kGroupedMinTokens = 32;
 constexpr int kGN = 112;
 constexpr int kGNSmall = 16;    // tokens per tile for decode-sized batches
 // TMA ring depth (raw FP4 A + E4M3 B per K tile): deeper for the small tile,
-// whose stages are smaller.  A third converted-A slot (at the cost of TMA
-// stages where shared memory is short) changed the 32-token layer by 1 % and
-// config 3 by less than its noise.
+// whose stages are smaller.  The 16-token up GEMM trades two TMA stages for a
+// third converted-A slot (its converters wait less on the MMA); for the
+// 112-token tiles a third slot measured no better.
 template <bool kUp, int kN>
 struct GRing {
-  static constexpr int stages = kN <= 16 ? 8 : 4;
-  static constexpr int conv = 2;  // converted-A ring depth
+  static constexpr int stages = kN <= 16 ? (kUp ? 6 : 8) : 4;
+  static constexpr int conv = kN <= 16 && kUp ? 3 : 2;  // converted-A ring depth
 };
 constexpr int kGWork = 16;      // act-quant exchange slots (barrier pairs, amax rows)
 // Warp roles: epilogue-only warps (SwiGLU with the exact expf, act quant,

@@ -1052,8 +1052,9 @@ __global__ void __launch_bounds__(128) router_topk_kernel(RouterArgs a) {
 // experts x TB tokens with two lanes per expert row, the lanes holding chains
 // 8h + j over columns 16c + 8h + j -- the same 16 chains in the same order as
 // the tile kernel's, summed the same way -- and the grid has experts/64 x
-// tokens/TB CTAs of four warps.  The gate rows are read through L2 (2 MB for
-// 256 x 4096), 16 chunks in flight per lane.
+// tokens/TB CTAs of four warps (TB = 1 up to 32 tokens, 4 up to 128).  The
+// gate rows are read through L2 (2 MB for 256 x 4096), 16 chunks in flight per
+// lane.
 constexpr int kRsWarps = 4;
 constexpr int kRsDepth = 16;
 template <int TB>
@@ -1134,7 +1135,7 @@ static cudaError_t launch_router_small(const RouterArgs& a, cudaStream_t s) {
 
 cudaError_t launch_router_batched(const RouterArgs& a, cudaStream_t s) {
   if (a.tokens <= 32 && a.hidden % 16 == 0) {
-    cudaError_t e = launch_router_small<2>(a, s);
+    cudaError_t e = launch_router_small<1>(a, s);
     if (e != cudaSuccess) return e;
   } else if (a.tokens <= 128 && a.hidden % 16 == 0) {
     cudaError_t e = launch_router_small<4>(a, s);
