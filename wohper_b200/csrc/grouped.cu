@@ -24,9 +24,10 @@
 
 namespace wh {
 
-// Below this many tokens a call is decode-sized: 16-token tiles and the
-// single-token (route-order) combine; from here on 128-token tiles and the
-// batched (ascending expert id) combine.
+// Below this many tokens a call is decode-sized and takes the single-token
+// (route-order) combine; from here on the batched (ascending expert id)
+// combine.  The tile size is chosen apart from it (grouped_tile_n): 16 tokens
+// while the routed experts average at most 4 rows, kGN beyond.
 constexpr int kGroupedMinTokens = 32;
 // K (hidden and inter) must be a multiple of 512: scale bytes are read 16 at a
 // time (4 K tiles of 128)
