@@ -1326,8 +1326,8 @@ MoeScratch moe_scratch_layout(const wh_moe_plan* p, int T, uint8_t* base) {
 
 // 16-token tiles while the routed experts average at most 4 rows (decode-sized
 // calls and batched decode: each expert's weights stream and convert once per
-// tile, and a 128-token tile would carry mostly empty columns); 128-token
-// tiles beyond that.
+// tile, and a batch tile would carry mostly empty columns); kGN-token tiles
+// beyond that.
 int grouped_tile_n(const wh_moe_plan* p, int tokens) {
   return (tokens < kGroupedMinTokens || (long long)tokens * p->d.topk <= 4LL * p->d.num_experts)
              ? kGNSmall
