@@ -706,6 +706,11 @@ void wh_debug_e4m3_round_n(const float* in, float* out, size_t n); /* host array
  * Returns the number of entries, negated if some difference fell outside the
  * device's midpoint gate (wh_ctx_create then fails with Unsupported). */
 int wh_debug_expf_table(const uint32_t** keys, const float** vals);
+/* The band the device's exp looks inputs up in: a result within this relative
+ * distance of a float rounding midpoint is looked up in the table above.  It is
+ * measured with the table: the smallest power of two at least twice the
+ * farthest distance of any host difference, in [2^-44, 2^-30]. */
+double wh_debug_expf_near(void);
 /* y[i] = the host libm's expf(x[i]), evaluated on the device (device arrays). */
 wh_status wh_debug_ref_expf(wh_ctx* ctx, const float* x, float* y, size_t n,
                             wh_stream_t stream);

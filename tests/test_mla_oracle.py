@@ -101,6 +101,25 @@ def _expf_table():
     return n, keys, vals
 
 
+def test_expf_lookup_band_covers_every_host_difference():
+    # the device looks x up only when exp(x) lies within the band of a float
+    # rounding midpoint; every input where the host expf differs from the
+    # once-rounded double exp must lie well inside it
+    n, keys, vals = _expf_table()
+    near = W.lib().wh_debug_expf_near()
+    assert 2.0 ** -44 <= near <= 2.0 ** -30
+    assert np.log2(near) == np.round(np.log2(near))  # a power of two
+    x = keys.view(np.float32)
+    yd = np.exp(x.astype(np.float64))
+    c = yd.astype(np.float32)
+    differs = c.view(np.uint32) != vals.view(np.uint32)
+    other = np.where(yd > c.astype(np.float64), np.nextafter(c, np.float32(np.inf)),
+                     np.nextafter(c, np.float32(-np.inf))).astype(np.float64)
+    dist = np.abs(yd - 0.5 * (c.astype(np.float64) + other)) / yd
+    assert differs.any()
+    assert dist[differs].max() <= near / 2
+
+
 def test_expf_table_is_sorted_and_holds_the_host_expf():
     # the device's exp is the once-rounded double exp except at these inputs,
     # where it returns the host libm's expf (the value Rust's f32::exp gives)

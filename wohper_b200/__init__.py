@@ -79,7 +79,7 @@ EXPORTS = (
     "wh_expert_loader_create", "wh_expert_loader_destroy", "wh_expert_arena_bytes",
     "wh_expert_loader_load", "wh_lm_head_scratch_bytes", "wh_lm_head_topk",
     "wh_fp8_expert_scratch_len", "wh_fp8_expert_forward", "wh_rope_inv_freqs",
-    "wh_mla_attention", "wh_debug_expf_table", "wh_debug_ref_expf", "wh_hc_pre",
+    "wh_mla_attention", "wh_debug_expf_table", "wh_debug_expf_near", "wh_debug_ref_expf", "wh_hc_pre",
     "wh_hc_post", "wh_hc_head", "wh_rms_norm", "wh_fp8_gemv_grouped",
     "wh_v4_attention_scratch_len", "wh_v4_attention", "wh_lm_head_batch_scratch_bytes",
     "wh_lm_head_topk_batch",
@@ -188,6 +188,7 @@ def lib(build_if_missing: bool = True) -> C.CDLL:
         "wh_lm_head_scratch_bytes": (sz, [C.c_longlong, i]),
         "wh_rope_inv_freqs": (None, [i, f, f, f, f, C.c_uint64, vp]),
         "wh_debug_expf_table": (i, [C.POINTER(vp), C.POINTER(vp)]),
+        "wh_debug_expf_near": (C.c_double, []),
         "wh_debug_ref_expf": (st, [vp, vp, vp, sz, vp]),
         "wh_hc_pre": (st, [vp, vp, vp, vp, vp, i, i, i, i, f, vp, vp, vp, vp]),
         "wh_hc_post": (st, [vp, vp, vp, vp, vp, i, i, i, vp, vp]),

@@ -1659,6 +1659,8 @@ int wh_debug_expf_table(const uint32_t** keys, const float** vals) {
   return ok ? n : -n;
 }
 
+double wh_debug_expf_near(void) { return expf_near_host(); }
+
 wh_status wh_debug_ref_expf(wh_ctx* c, const float* x, float* y, size_t n, wh_stream_t stream) {
   if (!c) return fail(WH_ERR_INVALID_POINTER, "ctx is null");
   if (n > 0 && (!x || !y)) return fail(WH_ERR_INVALID_POINTER, "null pointer");

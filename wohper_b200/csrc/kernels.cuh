@@ -37,6 +37,7 @@ constexpr int kExpfBucketShift = 12;
 constexpr uint32_t kExpfBuckets = 1u << (32 - kExpfBucketShift);
 bool expf_table_host(const uint32_t** keys, const float** vals, int* n);
 bool expf_bucket_host(const uint32_t** bucket);
+double expf_near_host();
 
 __device__ __forceinline__ float ref_expf(float x, const ExpfTable& t) {
   const double yd = exp((double)x);
