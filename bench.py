@@ -736,6 +736,173 @@ def config5_dict(world: int, batch: int, layers: int) -> dict:
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
 
 
+def config5_cpu(batch: int, seed: int = 880, vocab_sample: int = 16384, layer_index: int = 2,
+                reps: int = 1):
+    """The reference's decode step on this host's cores, sampled (oracle = the
+    reference's CPU kernels restated, composed as run_model_for_one_token does).
+
+    One V4-Flash-shape layer -- hc_pre, attention norm, the MLA attention with
+    its FP8 projections, hc_post, hc_pre, FFN norm, the sqrt-softplus router
+    and the 6 routed + shared FP4 experts, hc_post -- runs for `batch`
+    sequences at position 4095, then the pooled head, the final norm and the
+    lm_head top-1 over `vocab_sample` vocabulary rows.  Host-generated weights
+    of the config-5 shapes (generation untimed), `reps` timed passes.  Returns
+    ([estimated step seconds = 43 x the layer + the head scaled to the full
+    vocabulary, one per pass], threads)."""
+    import oracle as O
+    import wohper_b200 as Wp  # host-side rope constants only
+    from tests import helpers as H
+
+    O.set_threads(os.cpu_count() or 1)
+    keep: list = []
+    m = {}
+    for i, (name, (r, c)) in enumerate(H.V4_SHAPES.items()):
+        w, sc = H.fp8_weight(seed * 100 + i, r, c)
+        keep += [w, sc]
+        m[name] = O.fp8_matrix(w, sc, r, c, sc.shape[0], sc.shape[1], keep)
+    g = H.rng(seed)
+    qn = H.bf16_bits(1.0 + 0.1 * g.standard_normal(1024).astype(np.float32))
+    kn = H.bf16_bits(1.0 + 0.1 * g.standard_normal(512).astype(np.float32))
+    sink = g.standard_normal(64).astype(np.float32)
+    keep += [qn, kn, sink]
+    spec = O.V4Attn(HID, 64, 512, 448, 1024, 8, 1024, 128, m["wq_a"], m["wq_b"], m["wkv"],
+                    m["wo_a"], m["wo_b"], qn.ctypes.data, kn.ctypes.data, sink.ctypes.data)
+    attn_norm = H.bf16_bits(1.0 + 0.1 * g.standard_normal(HID).astype(np.float32))
+    ffn_norm = H.bf16_bits(1.0 + 0.1 * g.standard_normal(HID).astype(np.float32))
+    hc = 4
+
+    def hc_params(mix):
+        return ((0.02 * g.standard_normal((mix, hc * HID))).astype(np.float32),
+                np.array([0.5, 0.5, 0.5], np.float32),
+                (0.1 * g.standard_normal(mix)).astype(np.float32))
+
+    hc_attn, hc_ffn = hc_params((2 + hc) * hc), hc_params((2 + hc) * hc)
+    head_fn = (0.02 * g.standard_normal((hc, hc * HID))).astype(np.float32)
+    head_base = (0.1 * g.standard_normal(hc)).astype(np.float32)
+    final_norm = H.bf16_bits(1.0 + 0.1 * g.standard_normal(HID).astype(np.float32))
+    gate = H.router_gate(seed * 100 + 18, E, HID)
+    bias = (0.01 * g.standard_normal(E)).astype(np.float32)
+    model = HostModel(seed)
+    fr = Wp.rope_inv_freqs(64, *Wp.deepseek_rope_for_layer(layer_index))
+    n_comp = H.v4_compressed_count(layer_index, V4_POS)
+    kv = [(g.standard_normal((V4_POS + 1, 512))).astype(np.float32) for _ in range(batch)]
+    comp = [(g.standard_normal((n_comp, 512))).astype(np.float32) if n_comp else None
+            for _ in range(batch)]
+    xs0 = [(g.standard_normal(hc * HID)).astype(np.float32) for _ in range(batch)]
+    lm = H.bf16_bits((0.02 * g.standard_normal((vocab_sample, HID))).astype(np.float32))
+    # the experts the sampled tokens route to, generated before the timed region
+    arr = (O.Fp4Expert * (E + 1))()
+    arr[E] = model.expert(E)
+
+    def check(st):
+        if st != O.OK:
+            raise RuntimeError(f"oracle status {st} in the config-5 CPU sample")
+
+    steps = []
+    for _ in range(reps):
+        t_layer = 0.0
+        pooled_all = []
+        for b in range(batch):
+            xs = xs0[b]
+            t0 = time.perf_counter()
+            st, y, post, cm = O.hc_pre(*hc_attn, xs, hc, HID)
+            check(st)
+            y = O.rms_norm(y, attn_norm)
+            st, y = O.v4_attention(spec, V4_POS, y, kv[b], comp[b], fr)
+            check(st)
+            xs = O.hc_post(y, xs, post, cm, hc, HID)
+            st, y, post, cm = O.hc_pre(*hc_ffn, xs, hc, HID)
+            check(st)
+            y = O.rms_norm(y, ffn_norm)
+            _, ids, w, _ = O.router(gate, y, TOPK, mode=1, bias=bias, route_scale=1.5)
+            t_route = time.perf_counter() - t0
+            for e in ids:
+                arr[int(e)] = model.expert(int(e))  # generated untimed
+            t1 = time.perf_counter()
+            st, y = O.moe_combine_token(arr, ids, w, arr[E], y)
+            check(st)
+            xs = O.hc_post(y, xs, post, cm, hc, HID)
+            t_layer += t_route + time.perf_counter() - t1
+            pooled_all.append(xs)
+        t0 = time.perf_counter()
+        for xs in pooled_all:
+            pooled = O.hc_head(head_fn, 0.5, head_base, xs, hc, HID)
+            pooled = O.rms_norm(pooled, final_norm)
+            O.lm_head_topk(lm, pooled, 1)
+        t_head = (time.perf_counter() - t0) * V4_VOCAB / vocab_sample
+        steps.append(V4_LAYERS * t_layer + t_head)
+    return steps, O.threads()
+
+
+def run_reference_config5(args):
+    """--config 5 --impl reference: the sampled CPU decode step (config5_cpu),
+    one sample per step, on config 5's metric and unit."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    B = args.batch
+    times, threads = config5_cpu(B, reps=args.warmup + args.steps)
+    times = times[args.warmup:]
+    step_s = sum(times) / len(times)
+    v = B / step_s
+    sample = (f"one layer (index 2, compressed rows at position 4095) and the head for {B} "
+              f"sequence(s) through the oracle's composition, the lm_head over 16384 of "
+              f"{V4_VOCAB} rows; the step estimated as {V4_LAYERS} x the layer + the head "
+              f"scaled to the full vocabulary")
+    return {
+        "impl": "reference", "metric": METRIC5, "value": round(v, 4), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8/fp4 weights x act-quantised fp8 activations, f32 accumulate",
+        "data": "synthetic (seeded random-init weights, N(0,1) KV cache and residual stream)",
+        "config": config5_dict(world, B, args.layers),
+        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference_moe_batch(args, config: int):
+    """--config 3/4 --impl reference: the oracle's batched MoE (exact router +
+    expert-major path for config 3, the given uniform routes for config 4) on a
+    16-token sample per step, all host threads, on the config's metric."""
+    import oracle as O
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    O.set_threads(os.cpu_count() or 1)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        if config == 3:
+            v, th = config3_cpu(16, 1000, threads_all=True)
+        else:
+            v, th = config4_cpu(16)
+        if i >= args.warmup:
+            vals.append(v)
+    v = sum(vals) / len(vals)
+    metric, workload, tokens = (METRIC3, WORKLOAD3, T3) if config == 3 else (METRIC4, WORKLOAD4, T4)
+    return {
+        "impl": "reference", "metric": metric, "value": round(v, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(16 / v * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if config == 3 else "strong", "vs_baseline": None,
+        "dtype": "fp4-e2m1 x fp8-e4m3 (act-quant) products, f32 accumulate",
+        "data": "synthetic (seeded random-init weights, N(0,1) tokens)",
+        "config": {"workload": workload, "experts": E, "topk": TOPK, "hidden": HID,
+                   "inter": INTER, "tokens": tokens},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": th, "kind": "port",
+                         "sample": "16 tokens of the workload per step through the C++ "
+                                   "restatement's batched MoE path"},
+        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
 def run_config5(args):
     import torch
 
@@ -2212,14 +2379,14 @@ def main():
         res = run_mla(args)
     elif args.workload == "mhc":
         res = run_mhc(args)
-    elif args.config == 5 and args.impl == "ours":
-        res = run_config5(args)
+    elif args.config == 5:
+        res = run_config5(args) if args.impl == "ours" else run_reference_config5(args)
     elif args.config == 1:
         res = run_config1(args) if args.impl == "ours" else run_reference_config1(args)
-    elif args.config == 3 and args.impl == "ours":
-        res = run_config3(args)
-    elif args.config == 4 and args.impl == "ours":
-        res = run_config4(args)
+    elif args.config == 3:
+        res = run_config3(args) if args.impl == "ours" else run_reference_moe_batch(args, 3)
+    elif args.config == 4:
+        res = run_config4(args) if args.impl == "ours" else run_reference_moe_batch(args, 4)
     else:
         res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
