@@ -1083,6 +1083,18 @@ def run_config5(args):
             "timing": "cuda graph of one step, replayed",
             "clocks": clk.summary(),
         }
+        if world == 1 and not args.no_cpu_baseline:
+            # the sampled CPU step of the reference arm (config5_cpu), once
+            try:
+                times, threads = config5_cpu(B)
+                v = B / times[0]
+                res["cpu_baseline"] = {
+                    "value": round(v, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                    "sample": f"one layer and the head for {B} sequence(s) through the oracle's "
+                              f"composition, the lm_head over 16384 rows; the step estimated as "
+                              f"{V4_LAYERS} x the layer + the head scaled to {V4_VOCAB} rows"}
+            except Exception as e:  # the line stands without it
+                res["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     del graph
     for L in layers:
         L.moe.close()
