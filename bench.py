@@ -885,7 +885,7 @@ def run_reference_moe_batch(args, config: int):
         if i >= args.warmup:
             vals.append(v)
     v = sum(vals) / len(vals)
-    metric, workload, tokens = (METRIC3, WORKLOAD3, T3) if config == 3 else (METRIC4, WORKLOAD4, T4)
+    metric, workload, tokens = (METRIC3, workload3(), T3) if config == 3 else (METRIC4, WORKLOAD4, T4)
     return {
         "impl": "reference", "metric": metric, "value": round(v, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -1113,6 +1113,12 @@ T3 = 2048
 METRIC3 = "prefill tokens/s (batched FP4 MoE FFN, config 3)"
 WORKLOAD3 = ("config 3: 2048 tokens through the FP4 MoE FFN, 256 experts + shared, "
              "4096->2048->4096, Zipf(1.1)-skewed top-6 routing, grouped block-scaled GEMMs")
+
+
+def workload3() -> str:
+    """WORKLOAD3, or with --tokens the same workload at another token count (the
+    compute-bound point of the grouped GEMMs is 16384 tokens)."""
+    return WORKLOAD3 if T3 == 2048 else WORKLOAD3.replace("2048 tokens", f"{T3} tokens", 1)
 W13_BYTES = 2 * (PACKED_W13 + SCALES_W13)   # w1 + w3 of one expert
 W2_BYTES = PACKED_W2 + SCALES_W2
 
@@ -1238,7 +1244,7 @@ def run_config3(args):
             "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp4-e2m1 (as e4m3) x fp8-e4m3, ue8m0 block scales, f32 accumulate",
             "data": "synthetic (seeded random-init weights, N(0,1) tokens, Zipf prior on routing)",
-            "config": {"workload": WORKLOAD3, "experts": E, "topk": TOPK, "hidden": HID,
+            "config": {"workload": workload3(), "experts": E, "topk": TOPK, "hidden": HID,
                        "inter": INTER, "tokens": T3, "experts_used": used,
                        "max_expert_rows": int(counts.max()), "rows": R,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)",
@@ -1252,7 +1258,15 @@ def run_config3(args):
                          "algorithmic_bytes": int(up_bytes),
                          "traffic": int(up_bytes * GROUPED_UP_TRAFFIC_RATIO),
                          "traffic_note": "scaled from the ncu capture of the grouped16 case",
-                         "tensor_tflops": round(up_flops / (up_ms * 1e-3) / 1e12, 1)},
+                         "tensor_tflops": round(up_flops / (up_ms * 1e-3) / 1e12, 1),
+                         # the MMA is kind::mxf8f6f4 on E4M3 operands (the reference's FP4
+                         # code 1 has no E2M1 encoding), so its dense peak is the FP8 rate,
+                         # twice the measured bf16 GEMM; the nominal FP4 rate is twice that
+                         "tensor_peak_tflops": round(2 * bf16_peak(), 1),
+                         "tensor_peak_kind": "2 x measured bf16 dense (the fp8 kind::f8f6f4 rate)",
+                         "tensor_frac": round(up_flops / (up_ms * 1e-3) / 1e12 / (2 * bf16_peak()), 4),
+                         "tensor_frac_of_nominal_fp4": round(
+                             up_flops / (up_ms * 1e-3) / 1e12 / 9000.0, 4)},
             "step_tflops": round(step_flops / (ms_step * 1e-3) / 1e12, 1),
             "e2e": {"value": round(world * T3 / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": T3 * HID * 4,
@@ -2354,6 +2368,8 @@ def main():
     ap.add_argument("--no-ep", action="store_true",
                     help="config 2: skip the nested config-4 expert-parallel measurement")
     ap.add_argument("--batch", type=int, default=1, help="config 5: sequences per step")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="config 3: tokens per step (default 2048; 16384 is the compute-bound point)")
     ap.add_argument("--layers", type=int, default=V4_LAYERS, help="config 5: layers")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="1: one FP8 GEMV 4096x4096; 2: one-token decode FFN (default); "
@@ -2383,6 +2399,9 @@ def main():
         run_ncu_case(args)
         return
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.tokens > 0:
+        global T3
+        T3 = args.tokens
     if args.workload == "expert-load":
         res = run_expert_load(args)
     elif args.workload == "lm-head":
