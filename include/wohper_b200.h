@@ -540,7 +540,8 @@ size_t wh_lm_head_batch_scratch_bytes(long long rows, int top_k, int tokens);
  * x + t * ldx; its result goes to out_tokens / out_logits + t * top_k and, when
  * logits is given, its logits to logits + t * rows.  Each token's result equals
  * wh_lm_head_topk's bit for bit; the weight is streamed once per tile of up to
- * 8 tokens instead of once per token.  Same limits as wh_lm_head_topk. */
+ * 8 tokens instead of once per token.  Same limits as wh_lm_head_topk, and
+ * 1 <= tokens <= 65535, ldx >= cols. */
 wh_status wh_lm_head_topk_batch(wh_ctx* ctx, const uint16_t* weight, long long rows, int cols,
                                 uint32_t row_base, const float* x, int tokens, int ldx,
                                 int top_k, uint32_t* out_tokens, float* out_logits,
